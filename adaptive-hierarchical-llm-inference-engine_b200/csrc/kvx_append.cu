@@ -1,0 +1,79 @@
+// kvx_append.cu -- paged append: scatter each sequence's new K/V rows into
+// slot pos % page_tokens of physical page block_table[s][pos / page_tokens].
+// Replaces KVManager::save_page (cache/kv_cache.cpp:111-127) on the append
+// path of InferenceController::appendKVPage (runtime/inference.cpp:50-54).
+//
+// One thread per 16-byte vector of a (sequence, K|V, head) row: consecutive
+// threads write consecutive bytes of a row (coalesced), rows land wherever
+// the block table points.  Pure copy, bit-exact.
+#include "kvx_common.cuh"
+
+namespace kvx {
+namespace {
+
+__global__ void __launch_bounds__(256)
+append_kernel(uint8_t *pool, const uint8_t *new_k, const uint8_t *new_v,
+              const int32_t *block_table, const int32_t *positions, int32_t *error_flag,
+              int batch, int hkv, int max_pages, int num_pages, int page_tokens,
+              int row_vecs /* 16-byte vectors per row */) {
+    const long long total = (long long)batch * 2 * hkv * row_vecs;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int v = (int)(i % row_vecs);
+        long long r = i / row_vecs;            // row = ((s * 2) + kv) * hkv + h
+        const int h = (int)(r % hkv);
+        r /= hkv;
+        const int kv = (int)(r % 2);
+        const int s = (int)(r / 2);
+        const int pos = positions[s];
+        const int lp = pos / page_tokens;
+        if (pos < 0 || lp >= max_pages) {
+            if (error_flag && v == 0) atomicOr(error_flag, 2);
+            continue;
+        }
+        const int phys = block_table[(size_t)s * max_pages + lp];
+        if (phys < 0 || phys >= num_pages) {
+            if (error_flag && v == 0) atomicOr(error_flag, 2);
+            continue;
+        }
+        const int slot = pos % page_tokens;
+        const size_t row_bytes = (size_t)row_vecs * 16;
+        const size_t dst = ((((size_t)phys * 2 + kv) * hkv + h) * page_tokens + slot) * row_bytes;
+        const size_t src = ((size_t)s * hkv + h) * row_bytes;
+        const uint4 val = *reinterpret_cast<const uint4 *>((kv ? new_v : new_k) + src + v * 16);
+        *reinterpret_cast<uint4 *>(pool + dst + v * 16) = val;
+    }
+}
+
+}  // namespace
+}  // namespace kvx
+
+using namespace kvx;
+
+extern "C" KVX_API int kvx_append(const kvx_paged *kv, const int32_t *block_table,
+                                  int32_t max_pages, const int32_t *positions, int32_t batch,
+                                  const void *new_k, const void *new_v, int32_t *error_flag,
+                                  void *stream) {
+    if (!kv || !kv->pool || !block_table || !positions || !new_k || !new_v) return KVX_EINVAL;
+    if (batch < 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || kv->page_tokens <= 0 ||
+        kv->head_dim <= 0 || kv->num_pages <= 0)
+        return KVX_EINVAL;
+    if (kv->dtype != KVX_F32 && kv->dtype != KVX_F16) return KVX_EUNSUPPORTED;
+    const int esize = kv->dtype == KVX_F32 ? 4 : 2;
+    const size_t row_bytes = (size_t)kv->head_dim * esize;
+    if (row_bytes % 16) return KVX_EUNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(kv->pool) | reinterpret_cast<uintptr_t>(new_k) |
+         reinterpret_cast<uintptr_t>(new_v)) & 15)
+        return KVX_EINVAL;
+    if (batch == 0) return KVX_OK;
+    const int row_vecs = (int)(row_bytes / 16);
+    const long long total = (long long)batch * 2 * kv->num_kv_heads * row_vecs;
+    const int threads = 256;
+    long long blocks = (total + threads - 1) / threads;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    append_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint8_t *>(kv->pool), static_cast<const uint8_t *>(new_k),
+        static_cast<const uint8_t *>(new_v), block_table, positions, error_flag, batch,
+        kv->num_kv_heads, max_pages, kv->num_pages, kv->page_tokens, row_vecs);
+    return launch_status();
+}

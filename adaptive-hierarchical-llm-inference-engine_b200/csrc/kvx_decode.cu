@@ -1,0 +1,588 @@
+// kvx_decode.cu -- paged GQA decode attention for sm_100a.
+//
+// Semantics: TensorOps::attention (runtime/tensor_ops.cpp:179-219) for one
+// query row per (sequence, q-head), scale 1/sqrt(head_dim), over the tokens
+// of the sequence gathered through its block table; q-head h reads kv-head
+// h / (num_q_heads / num_kv_heads).
+//
+// Design (memory bound: every K/V byte is read once per step):
+//  * grid = (head_group x split, kv_head, sequence).  A split is a chunk of
+//    `chunk` consecutive logical pages; one CTA of 4 warps owns it and its
+//    warps take the chunk's pages round-robin.
+//  * Each warp streams its pages through a private 2-stage shared-memory
+//    ring: lane 0 issues two bulk copies (cp.async.bulk, the TMA engine; K
+//    block + V block of one (page, head), 4 KiB each at fp16) that complete
+//    on an mbarrier; all lanes wait with a bounded poll.  No register
+//    staging, one instruction per 4 KiB.
+//  * Q.K: lane (grp = lane/8, sub = lane%8) owns 16 dims (two 16-byte
+//    vectors per row); the 8 lanes of a group read one 128-byte segment of a
+//    row per instruction (bank-conflict free) and reduce with 3 shuffles.
+//    Softmax is online in the log2 domain (q pre-scaled by scale*log2 e).
+//  * P.V: lane owns 4 output dims; one row per instruction, conflict free.
+//  * Warps merge through shared memory; a split writes (m, l, o) partials
+//    and kvx_combine_kernel folds the splits (flash-decoding), or the CTA
+//    writes the final row directly when the sequence has a single split.
+//  * int8 pages: the (page, head) block's {scale, zeroPoint} rides in the
+//    same bulk transfer; dequantisation is folded algebraically:
+//    q.(zp + c*s) = zp*sum(q) + s*(q.c), p.(zp + c*s) = zp*sum(p) + (p*s).c.
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include <cstdio>
+#include <cstdlib>
+
+#include "kvx_common.cuh"
+
+namespace kvx {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxHeadsPerCta = 4;
+
+struct DecodeParams {
+    const uint8_t *pool;
+    const float *stats;
+    const int32_t *block_table;
+    const int32_t *seq_lens;
+    const void *q;
+    void *out;
+    float *part_o;   // [batch][hq][max_splits][128]
+    float *part_ml;  // [batch][hq][max_splits][2]
+    int32_t *error_flag;
+    int num_pages, hkv, hq, max_pages, max_splits, chunk, group, nhg;
+    float scale_log2;
+};
+
+template <typename KVT> struct KvTraits;
+// kVec: elements per 16-byte vector; kStages: ring depth per warp (fp32
+// pages are 32 KiB per stage, so one stage keeps a CTA inside 227 KB).
+template <> struct KvTraits<float> {
+    static constexpr int kVec = 4;
+    static constexpr bool kI8 = false;
+    static constexpr int kStages = 1;
+};
+template <> struct KvTraits<__half> {
+    static constexpr int kVec = 8;
+    static constexpr bool kI8 = false;
+    static constexpr int kStages = 2;
+};
+template <> struct KvTraits<int8_t> {
+    static constexpr int kVec = 16;
+    static constexpr bool kI8 = true;
+    static constexpr int kStages = 3;
+};
+
+// 16 bytes of K/V elements -> kVec floats (int8: code + 128, exact).
+template <typename KVT> __device__ __forceinline__ void unpack16(const uint4 &w, float *f);
+template <> __device__ __forceinline__ void unpack16<float>(const uint4 &w, float *f) {
+    f[0] = __uint_as_float(w.x);
+    f[1] = __uint_as_float(w.y);
+    f[2] = __uint_as_float(w.z);
+    f[3] = __uint_as_float(w.w);
+}
+template <> __device__ __forceinline__ void unpack16<__half>(const uint4 &w, float *f) {
+    float2 a = h2_to_f2(w.x), b = h2_to_f2(w.y), c = h2_to_f2(w.z), d = h2_to_f2(w.w);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+    f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+// int8 code c (two's complement byte) -> float(c + 128): flip the sign bit
+// to get the unsigned byte, place it in the mantissa of 2^23 and subtract.
+__device__ __forceinline__ void unpack_u8x4(uint32_t w, float *f) {
+    uint32_t u = w ^ 0x80808080u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        f[i] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | i)) - 8388608.0f;
+}
+template <> __device__ __forceinline__ void unpack16<int8_t>(const uint4 &w, float *f) {
+    unpack_u8x4(w.x, f);
+    unpack_u8x4(w.y, f + 4);
+    unpack_u8x4(w.z, f + 8);
+    unpack_u8x4(w.w, f + 12);
+}
+
+// 4 consecutive elements of a V row -> floats.
+template <typename KVT> __device__ __forceinline__ void load_v4(const KVT *row, int lane, float *f);
+template <> __device__ __forceinline__ void load_v4<float>(const float *row, int lane, float *f) {
+    float4 v = *reinterpret_cast<const float4 *>(row + 4 * lane);
+    f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+}
+template <> __device__ __forceinline__ void load_v4<__half>(const __half *row, int lane, float *f) {
+    uint2 v = *reinterpret_cast<const uint2 *>(row + 4 * lane);
+    float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+template <> __device__ __forceinline__ void load_v4<int8_t>(const int8_t *row, int lane, float *f) {
+    unpack_u8x4(*reinterpret_cast<const uint32_t *>(row + 4 * lane), f);
+}
+
+template <typename KVT> __host__ __device__ constexpr int block_bytes() { return kPageTokens * kHeadDim * (int)sizeof(KVT); }
+template <typename KVT> __host__ __device__ constexpr int stage_bytes() {
+    return 2 * block_bytes<KVT>() + (KvTraits<KVT>::kI8 ? 32 : 0);
+}
+template <typename KVT> __host__ __device__ constexpr int smem_bytes() {
+    constexpr int kStages = KvTraits<KVT>::kStages;
+    return kWarps * kStages * stage_bytes<KVT>() + kWarps * kStages * 8 +
+           kWarps * kMaxHeadsPerCta * kPageTokens * 4 + 2 * kWarps * kMaxHeadsPerCta * 4;
+}
+
+template <typename KVT, typename QT, int G>
+__global__ void __launch_bounds__(kThreads)
+paged_decode_kernel(const DecodeParams p) {
+    using TR = KvTraits<KVT>;
+    constexpr int kVec = TR::kVec;
+    constexpr int kNv = 16 / kVec;                // 16-byte vectors per lane per K row
+    constexpr int kBlk = block_bytes<KVT>();
+    constexpr int kStage = stage_bytes<KVT>();
+    constexpr int kRowBytes = kHeadDim * (int)sizeof(KVT);
+    constexpr int kStages = TR::kStages;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane >> 3, sub = lane & 7;
+    const int hg = blockIdx.x % p.nhg, split = blockIdx.x / p.nhg;
+    const int kvh = blockIdx.y, s = blockIdx.z;
+    const int T = p.seq_lens[s];
+    const int npages = (T + kPageTokens - 1) / kPageTokens;
+    const int p0 = split * p.chunk;
+    if (p0 >= npages) return;  // whole CTA: this split is past the sequence
+    const int p1 = min(p0 + p.chunk, npages);
+    const int nsplit = (npages + p.chunk - 1) / p.chunk;
+    const int h0 = kvh * p.group + hg * G;  // first q-head of this CTA
+    const int nh = min(G, p.group - hg * G);
+
+    uint8_t *wbuf = smem + warp * kStages * kStage;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWarps * kStages * kStage) + warp * kStages;
+    float *sp = reinterpret_cast<float *>(smem + kWarps * kStages * kStage + kWarps * kStages * 8) +
+                warp * kMaxHeadsPerCta * kPageTokens;
+    float *s_m = reinterpret_cast<float *>(smem + kWarps * kStages * kStage + kWarps * kStages * 8 +
+                                           kWarps * kMaxHeadsPerCta * kPageTokens * 4);
+    float *s_l = s_m + kWarps * kMaxHeadsPerCta;
+
+    if (lane == 0) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    const int n_my = (p1 - p0 - warp + kWarps - 1) / kWarps;  // pages of this warp
+    const int32_t *bt = p.block_table + (size_t)s * p.max_pages;
+
+    auto issue = [&](int i, int st) {
+        const int lp = p0 + warp + kWarps * i;
+        const int phys = bt[lp];
+        uint64_t *bar = &bars[st];
+        if (phys < 0 || phys >= p.num_pages) {
+            if (p.error_flag) atomicOr(p.error_flag, 2);
+            mbar_arrive_expect_tx(bar, 0);  // completes the phase with no data
+            return;
+        }
+        const size_t kb = ((size_t)phys * 2) * p.hkv + kvh;
+        const size_t vb = kb + p.hkv;
+        uint8_t *dst = wbuf + st * kStage;
+        mbar_arrive_expect_tx(bar, kStage);
+        bulk_g2s(dst, p.pool + kb * kBlk, kBlk, bar);
+        bulk_g2s(dst + kBlk, p.pool + vb * kBlk, kBlk, bar);
+        if constexpr (TR::kI8) {
+            bulk_g2s(dst + 2 * kBlk, p.stats + kb * 4, 16, bar);
+            bulk_g2s(dst + 2 * kBlk + 16, p.stats + vb * 4, 16, bar);
+        }
+    };
+
+    if (lane == 0)
+        for (int i = 0; i < min(kStages, n_my); ++i) issue(i, i);
+
+    // q for this lane's dims, pre-scaled into the log2 domain.
+    float qv[G][16];
+    float qsum[G];
+    {
+        const QT *qb = reinterpret_cast<const QT *>(p.q) + ((size_t)s * p.hq + h0) * kHeadDim;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            qsum[g] = 0.f;
+#pragma unroll
+            for (int j = 0; j < kNv; ++j)
+#pragma unroll
+                for (int e = 0; e < kVec; ++e) {
+                    const int d = (sub + 8 * j) * kVec + e;
+                    float v = g < nh ? io_traits<QT>::load(qb + g * kHeadDim + d) * p.scale_log2 : 0.f;
+                    qv[g][j * kVec + e] = v;
+                    qsum[g] += v;
+                }
+            if constexpr (TR::kI8) {
+                qsum[g] += __shfl_xor_sync(0xffffffffu, qsum[g], 1);
+                qsum[g] += __shfl_xor_sync(0xffffffffu, qsum[g], 2);
+                qsum[g] += __shfl_xor_sync(0xffffffffu, qsum[g], 4);
+            }
+        }
+    }
+
+    float m[G], l[G], acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -CUDART_INF_F;
+        l[g] = 0.f;
+        acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+    }
+
+    bool ok = true;
+    int done = 0;
+    for (int i = 0; i < n_my; ++i) {
+        const int st = i % kStages;
+        const uint32_t par = (i / kStages) & 1;
+        if (!mbar_wait_bounded(&bars[st], par, p.error_flag)) {
+            ok = false;
+            break;
+        }
+        done = i + 1;
+        const int lp = p0 + warp + kWarps * i;
+        const int phys = bt[lp];
+        if (phys >= 0 && phys < p.num_pages) {
+            const uint8_t *kbuf = wbuf + st * kStage;
+            const KVT *Vs = reinterpret_cast<const KVT *>(kbuf + kBlk);
+            float kscale = 1.f, kzp = 0.f, vscale = 1.f, vzp = 0.f;
+            if constexpr (TR::kI8) {
+                const float4 ks = *reinterpret_cast<const float4 *>(kbuf + 2 * kBlk);
+                const float4 vs = *reinterpret_cast<const float4 *>(kbuf + 2 * kBlk + 16);
+                kscale = ks.z; kzp = ks.w; vscale = vs.z; vzp = vs.w;
+            }
+            // ---- scores for rows grp, grp+4, grp+8, grp+12 ----
+            float sc[4][G];
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+                const int r = grp + 4 * r4;
+                float kf[16];
+#pragma unroll
+                for (int j = 0; j < kNv; ++j) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(kbuf + r * kRowBytes + (sub + 8 * j) * 16);
+                    unpack16<KVT>(w, kf + j * kVec);
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) a = fmaf(qv[g][e], kf[e], a);
+                    sc[r4][g] = a;
+                }
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4)
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        sc[r4][g] += __shfl_xor_sync(0xffffffffu, sc[r4][g], off);
+            const int tok0 = lp * kPageTokens;
+            float mx[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) mx[g] = -CUDART_INF_F;
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+                const bool valid = tok0 + grp + 4 * r4 < T;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float v = sc[r4][g];
+                    if constexpr (TR::kI8) v = fmaf(kscale, v, kzp * qsum[g]);
+                    v = valid ? v : -CUDART_INF_F;
+                    sc[r4][g] = v;
+                    mx[g] = fmaxf(mx[g], v);
+                }
+            }
+            float alpha[G], psum[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], 8));
+                mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], 16));
+                const float mn = fmaxf(m[g], mx[g]);
+                alpha[g] = exp2f(m[g] - mn);
+                m[g] = mn;
+                psum[g] = 0.f;
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4) {
+                    const float e = exp2f(sc[r4][g] - mn);
+                    sc[r4][g] = e;
+                    psum[g] += e;
+                }
+                l[g] = l[g] * alpha[g] + psum[g];
+            }
+            if (sub == 0) {
+#pragma unroll
+                for (int r4 = 0; r4 < 4; ++r4)
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        sp[g * kPageTokens + grp + 4 * r4] = sc[r4][g] * (TR::kI8 ? vscale : 1.f);
+            }
+            __syncwarp();
+            // ---- P.V ----
+            float pz[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                acc[g][0] *= alpha[g]; acc[g][1] *= alpha[g];
+                acc[g][2] *= alpha[g]; acc[g][3] *= alpha[g];
+                pz[g] = 0.f;
+            }
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+                float pt[G][4];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 v = *reinterpret_cast<const float4 *>(sp + g * kPageTokens + 4 * t4);
+                    pt[g][0] = v.x; pt[g][1] = v.y; pt[g][2] = v.z; pt[g][3] = v.w;
+                }
+#pragma unroll
+                for (int tt = 0; tt < 4; ++tt) {
+                    float vf[4];
+                    load_v4<KVT>(Vs + (4 * t4 + tt) * kHeadDim, lane, vf);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        acc[g][0] = fmaf(pt[g][tt], vf[0], acc[g][0]);
+                        acc[g][1] = fmaf(pt[g][tt], vf[1], acc[g][1]);
+                        acc[g][2] = fmaf(pt[g][tt], vf[2], acc[g][2]);
+                        acc[g][3] = fmaf(pt[g][tt], vf[3], acc[g][3]);
+                    }
+                }
+            }
+            if constexpr (TR::kI8) {
+                // zp * sum_t p_t, added to every dim (p without the scale factor)
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float zp_add = vzp * psum[g];
+                    // psum is this lane group's 4 rows; total over the 4 groups
+                    float z = zp_add + __shfl_xor_sync(0xffffffffu, zp_add, 8);
+                    z += __shfl_xor_sync(0xffffffffu, z, 16);
+                    pz[g] = z;
+                    acc[g][0] += pz[g]; acc[g][1] += pz[g]; acc[g][2] += pz[g]; acc[g][3] += pz[g];
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kStages < n_my) {
+            fence_proxy_async_smem();
+            issue(i + kStages, st);
+        }
+    }
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    if (!ok) {
+        // Drain copies this warp may still have in flight; the CTA then
+        // leaves this split unwritten (error_flag is set).
+        for (int i = done; i < min(done + kStages, n_my); ++i)
+            (void)mbar_wait_bounded(&bars[i % kStages], (i / kStages) & 1, nullptr);
+        if (lane == 0) s_fail = 1;
+    }
+    __syncthreads();
+    if (s_fail) return;
+
+    // ---- merge the warps of the CTA ----
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        l[g] += __shfl_xor_sync(0xffffffffu, l[g], 8);
+        l[g] += __shfl_xor_sync(0xffffffffu, l[g], 16);
+    }
+    // each warp parks its accumulator in its own (now idle) stage buffer
+    float *wacc = reinterpret_cast<float *>(wbuf);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+        *reinterpret_cast<float4 *>(wacc + g * kHeadDim + 4 * lane) =
+            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            s_m[warp * kMaxHeadsPerCta + g] = m[g];
+            s_l[warp * kMaxHeadsPerCta + g] = l[g];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kThreads) {
+        const int g = idx / kHeadDim, d = idx % kHeadDim;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w * kMaxHeadsPerCta + g]);
+        float O = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float mw = s_m[w * kMaxHeadsPerCta + g];
+            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
+            O += sw * reinterpret_cast<const float *>(smem + w * kStages * kStage)[g * kHeadDim + d];
+            L += sw * s_l[w * kMaxHeadsPerCta + g];
+        }
+        const int h = h0 + g;
+        if (nsplit == 1) {
+            QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
+            io_traits<QT>::store(o + d, O / L);
+        } else {
+            const size_t pi = ((size_t)s * p.hq + h) * p.max_splits + split;
+            p.part_o[pi * kHeadDim + d] = O;
+            if (d == 0) {
+                p.part_ml[pi * 2] = M;
+                p.part_ml[pi * 2 + 1] = L;
+            }
+        }
+    }
+}
+
+// Fold the split partials of sequences with more than one split; write zero
+// rows for empty sequences.  One warp per (sequence, q-head).
+template <typename QT>
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x * 4 + warp;
+    const int s = blockIdx.y;
+    if (h >= p.hq) return;
+    const int T = p.seq_lens[s];
+    const int npages = (T + kPageTokens - 1) / kPageTokens;
+    const int nsplit = (npages + p.chunk - 1) / p.chunk;
+    QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
+    if (nsplit == 1) return;
+    if (nsplit == 0) {
+        for (int d = lane; d < kHeadDim; d += 32) io_traits<QT>::store(o + d, 0.f);
+        return;
+    }
+    const size_t base = ((size_t)s * p.hq + h) * p.max_splits;
+    float M = -CUDART_INF_F;
+    for (int c = lane; c < nsplit; c += 32) M = fmaxf(M, p.part_ml[(base + c) * 2]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < nsplit; ++c) {
+        const float mc = p.part_ml[(base + c) * 2];
+        const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
+        L += w * p.part_ml[(base + c) * 2 + 1];
+        const float4 v = *reinterpret_cast<const float4 *>(p.part_o + (base + c) * kHeadDim + 4 * lane);
+        O[0] += w * v.x; O[1] += w * v.y; O[2] += w * v.z; O[3] += w * v.w;
+    }
+    const float inv = 1.f / L;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) io_traits<QT>::store(o + 4 * lane + j, O[j] * inv);
+}
+
+constexpr int kMinChunk = 4;
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
+    if (const char *e = getenv("KVX_DECODE_CHUNK")) {
+        int c = atoi(e);
+        if (c >= kMinChunk) return c;
+    }
+    // aim at ~4 waves of 3 resident CTAs per SM, counting half of max_pages
+    // as the mean sequence length
+    const long long work = (long long)batch * hkv * nhg * max_pages;
+    const long long target = (long long)sm_count() * 3 * 4;
+    long long c = (work / 2 + target - 1) / target;
+    if (c < kMinChunk) c = kMinChunk;
+    if (c > 64) c = 64;
+    return (int)((c + kWarps - 1) / kWarps * kWarps);
+}
+
+template <typename KVT, typename QT, int G>
+int launch(DecodeParams &p, int batch, cudaStream_t st) {
+    auto kern = paged_decode_kernel<KVT, QT, G>;
+    constexpr int smem = smem_bytes<KVT>();
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return KVX_ECUDA;
+        attr_set = true;
+    }
+    dim3 grid(p.nhg * p.max_splits, p.hkv, batch);
+    kern<<<grid, kThreads, smem, st>>>(p);
+    int rc = launch_status();
+    if (rc) return rc;
+    // the combine pass also writes the zero rows of empty sequences
+    dim3 cg((p.hq + 3) / 4, batch);
+    combine_kernel<QT><<<cg, 128, 0, st>>>(p);
+    return launch_status();
+}
+
+template <typename KVT, typename QT>
+int dispatch_g(DecodeParams &p, int batch, cudaStream_t st, int G) {
+    switch (G) {
+    case 1: return launch<KVT, QT, 1>(p, batch, st);
+    case 2: return launch<KVT, QT, 2>(p, batch, st);
+    case 3: return launch<KVT, QT, 3>(p, batch, st);
+    case 4: return launch<KVT, QT, 4>(p, batch, st);
+    default: return KVX_EUNSUPPORTED;
+    }
+}
+
+template <typename QT>
+int dispatch_kv(DecodeParams &p, int dtype, int batch, cudaStream_t st, int G) {
+    switch (dtype) {
+    case KVX_F32: return dispatch_g<float, QT>(p, batch, st, G);
+    case KVX_F16: return dispatch_g<__half, QT>(p, batch, st, G);
+    case KVX_I8: return dispatch_g<int8_t, QT>(p, batch, st, G);
+    default: return KVX_EINVAL;
+    }
+}
+
+size_t max_splits_for(int max_pages) { return (size_t)(max_pages + kMinChunk - 1) / kMinChunk; }
+
+}  // namespace
+}  // namespace kvx
+
+using namespace kvx;
+
+extern "C" KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads,
+                                                     int32_t max_pages, int32_t page_tokens) {
+    if (batch <= 0 || num_q_heads <= 0 || max_pages <= 0 || page_tokens != kPageTokens) return 0;
+    const size_t splits = max_splits_for(max_pages);
+    return (size_t)batch * num_q_heads * splits * (kHeadDim + 2) * sizeof(float);
+}
+
+extern "C" KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                                  const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                                  const void *q, void *out, int32_t io_dtype, float sm_scale,
+                                  void *workspace, size_t workspace_bytes, int32_t *error_flag,
+                                  void *stream) {
+    if (!kv || !kv->pool || !block_table || !seq_lens || !q || !out) return KVX_EINVAL;
+    if (batch <= 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || num_q_heads <= 0) return KVX_EINVAL;
+    if (num_q_heads % kv->num_kv_heads != 0) return KVX_EINVAL;
+    if (kv->head_dim != kHeadDim || kv->page_tokens != kPageTokens) return KVX_EUNSUPPORTED;
+    if (kv->dtype == KVX_I8 && !kv->stats) return KVX_EINVAL;
+    if (io_dtype != KVX_F32 && io_dtype != KVX_F16) return KVX_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(kv->pool) & 15) ||
+        (kv->stats && (reinterpret_cast<uintptr_t>(kv->stats) & 15)))
+        return KVX_EINVAL;
+    const size_t need = kvx_decode_workspace_bytes(batch, num_q_heads, max_pages, kv->page_tokens);
+    if (!workspace || workspace_bytes < need) return KVX_ENOSPC;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return KVX_EINVAL;
+
+    DecodeParams p{};
+    p.pool = static_cast<const uint8_t *>(kv->pool);
+    p.stats = kv->stats;
+    p.block_table = block_table;
+    p.seq_lens = seq_lens;
+    p.q = q;
+    p.out = out;
+    p.error_flag = error_flag;
+    p.num_pages = kv->num_pages;
+    p.hkv = kv->num_kv_heads;
+    p.hq = num_q_heads;
+    p.max_pages = max_pages;
+    p.group = num_q_heads / kv->num_kv_heads;
+    if (p.group > 4 * kMaxHeadsPerCta) return KVX_EUNSUPPORTED;
+    p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+    const int G = (p.group + p.nhg - 1) / p.nhg;
+    p.chunk = choose_chunk(batch, p.hkv, p.nhg, max_pages);
+    p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
+    const size_t splits_cap = max_splits_for(max_pages);
+    p.part_o = static_cast<float *>(workspace);
+    p.part_ml = p.part_o + (size_t)batch * num_q_heads * splits_cap * kHeadDim;
+    // the partial arrays are indexed with max_splits (<= splits_cap) as stride
+    const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)kHeadDim);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return io_dtype == KVX_F32 ? dispatch_kv<float>(p, kv->dtype, batch, st, G)
+                               : dispatch_kv<__half>(p, kv->dtype, batch, st, G);
+}

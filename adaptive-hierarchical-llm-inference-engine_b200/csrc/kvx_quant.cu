@@ -1,0 +1,319 @@
+// kvx_quant.cu -- the reference's KV codecs as vectorised sm_100a kernels.
+//
+//  * int8 per-block quantisation, bit-exact with KVCompressionEngine::
+//    compressToINT8 / decompressINT8
+//    (native-engine/cpp/KVCompressionEngine.cpp:83-122).  One warp per block
+//    (2048 elements = one (page, K|V, head) block at 16 x 128), 16-byte
+//    loads, the block held in registers between the min/max pass and the
+//    quantise pass, 16-byte code stores.
+//  * the truncating fp32<->fp16 converter of the disk tier, bit-exact with
+//    float_to_half / half_to_float (compression/kv_compress.cpp:6-46).
+//
+// Bit-exactness notes.  The reference is plain x86-64 SSE fp32 without FMA,
+// so every step here uses the explicitly rounded intrinsics (__fsub_rn,
+// __fdiv_rn, __fmul_rn, __fadd_rn) that the compiler cannot contract.
+//  - min/max: the reference keeps the FIRST element that compares smallest
+//    (largest) in index order; only +0/-0 compare equal with different bits,
+//    so the reduction carries (value, index) and breaks ties on the index.
+//    A NaN first element makes min and max NaN; later NaNs are never taken.
+//  - (int32_t)std::round(x): roundf, then x86 cvttss2si, which yields
+//    INT32_MIN for NaN and out-of-range values (clamped to code -128).
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include "kvx_common.cuh"
+
+namespace kvx {
+namespace {
+
+__device__ __forceinline__ int32_t cvt_trunc_i32_x86(float r) {
+    if (!(r >= -2147483648.0f && r < 2147483648.0f)) return INT32_MIN;
+    return (int32_t)r;
+}
+
+__device__ __forceinline__ int8_t quant_one(float x, float mn, float scale) {
+    const float normalized = __fdiv_rn(__fsub_rn(x, mn), scale);
+    int32_t q = cvt_trunc_i32_x86(roundf(normalized));
+    q = q < 0 ? 0 : (q > 255 ? 255 : q);
+    return (int8_t)(q - 128);
+}
+
+// (value, index) candidates in index order; strict comparisons keep the
+// first occurrence, exactly as std::min / std::max over a forward loop.
+struct MinMax {
+    float mn, mx;
+    int imn, imx;
+};
+
+__device__ __forceinline__ void mm_take(MinMax &a, float v, int i) {
+    if (v != v) return;  // NaN never replaces (first element handled apart)
+    if (v < a.mn || (v == a.mn && i < a.imn)) { a.mn = v; a.imn = i; }
+    if (a.mx < v || (v == a.mx && i < a.imx)) { a.mx = v; a.imx = i; }
+}
+
+__device__ __forceinline__ MinMax mm_warp_reduce(MinMax a) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const float mn = __shfl_xor_sync(0xffffffffu, a.mn, off);
+        const int imn = __shfl_xor_sync(0xffffffffu, a.imn, off);
+        const float mx = __shfl_xor_sync(0xffffffffu, a.mx, off);
+        const int imx = __shfl_xor_sync(0xffffffffu, a.imx, off);
+        if (mn < a.mn || (mn == a.mn && imn < a.imn)) { a.mn = mn; a.imn = imn; }
+        if (a.mx < mx || (mx == a.mx && imx < a.imx)) { a.mx = mx; a.imx = imx; }
+    }
+    return a;
+}
+
+template <typename T> __device__ __forceinline__ float ld_elem(const T *p, size_t i);
+template <> __device__ __forceinline__ float ld_elem<float>(const float *p, size_t i) { return p[i]; }
+template <> __device__ __forceinline__ float ld_elem<__half>(const __half *p, size_t i) {
+    return __half2float(p[i]);
+}
+
+// Finish stats from the reduced min/max; writes stats[4] from lane 0.
+__device__ __forceinline__ void finish_stats(MinMax r, float first, float *stats, int lane,
+                                             float &mn, float &scale) {
+    if (first != first) {  // NaN first element: the reference keeps NaN
+        r.mn = first;
+        r.mx = first;
+    }
+    mn = r.mn;
+    float sc = __fdiv_rn(__fsub_rn(r.mx, r.mn), 255.0f);
+    if (sc == 0.0f) sc = 1.0f;
+    scale = sc;
+    if (lane == 0) *reinterpret_cast<float4 *>(stats) = make_float4(r.mn, r.mx, sc, r.mn);
+}
+
+// Fast path: 2048-element blocks, 16-byte vectors, block kept in registers.
+template <typename T>
+__global__ void __launch_bounds__(256)
+compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
+                     float *__restrict__ stats, size_t num_blocks) {
+    constexpr int kBlock = 2048;
+    constexpr int kPerVec = 16 / sizeof(T);             // elements per 16-byte load
+    constexpr int kVecs = kBlock / kPerVec / 32;        // loads per lane
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
+         b += warps) {
+        const T *in = src + b * kBlock;
+        uint4 w[kVecs];
+#pragma unroll
+        for (int j = 0; j < kVecs; ++j)
+            w[j] = __ldcs(reinterpret_cast<const uint4 *>(in) + j * 32 + lane);
+        MinMax a{CUDART_INF_F, -CUDART_INF_F, 1 << 30, 1 << 30};
+        float f[kPerVec];
+#pragma unroll
+        for (int j = 0; j < kVecs; ++j) {
+            const T *e = reinterpret_cast<const T *>(&w[j]);
+#pragma unroll
+            for (int k = 0; k < kPerVec; ++k) f[k] = ld_elem<T>(e, k);
+            const int base = (j * 32 + lane) * kPerVec;
+#pragma unroll
+            for (int k = 0; k < kPerVec; ++k) mm_take(a, f[k], base + k);
+        }
+        // +-inf initial values: if every element is NaN or the block is all
+        // +inf / -inf, the index stays 1<<30 and the value is the sentinel;
+        // restore the reference's in[0]-seeded result in that case.
+        const float first = ld_elem<T>(in, 0);
+        a = mm_warp_reduce(a);
+        if (a.imn == (1 << 30)) a.mn = first;
+        if (a.imx == (1 << 30)) a.mx = first;
+        float mn, scale;
+        finish_stats(a, first, stats + 4 * b, lane, mn, scale);
+        int8_t *out = codes + b * kBlock;
+#pragma unroll
+        for (int j = 0; j < kVecs; ++j) {
+            const T *e = reinterpret_cast<const T *>(&w[j]);
+            if constexpr (kPerVec == 8) {
+                uint2 packed;
+                int8_t *c = reinterpret_cast<int8_t *>(&packed);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) c[k] = quant_one(ld_elem<T>(e, k), mn, scale);
+                __stcs(reinterpret_cast<uint2 *>(out) + j * 32 + lane, packed);
+            } else {
+                uint32_t packed;
+                int8_t *c = reinterpret_cast<int8_t *>(&packed);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) c[k] = quant_one(ld_elem<T>(e, k), mn, scale);
+                __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, packed);
+            }
+        }
+    }
+}
+
+// Generic path: any block size, one warp per block, two passes over global.
+template <typename T>
+__global__ void __launch_bounds__(256)
+compress_generic_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
+                        float *__restrict__ stats, size_t num_blocks, int block_elems) {
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
+         b += warps) {
+        const T *in = src + b * (size_t)block_elems;
+        MinMax a{CUDART_INF_F, -CUDART_INF_F, 1 << 30, 1 << 30};
+        for (int i = lane; i < block_elems; i += 32) mm_take(a, ld_elem<T>(in, i), i);
+        const float first = ld_elem<T>(in, 0);
+        a = mm_warp_reduce(a);
+        if (a.imn == (1 << 30)) a.mn = first;
+        if (a.imx == (1 << 30)) a.mx = first;
+        float mn, scale;
+        finish_stats(a, first, stats + 4 * b, lane, mn, scale);
+        int8_t *out = codes + b * (size_t)block_elems;
+        for (int i = lane; i < block_elems; i += 32) out[i] = quant_one(ld_elem<T>(in, i), mn, scale);
+    }
+}
+
+__device__ __forceinline__ float dequant_one(int8_t c, float zp, float scale) {
+    return __fadd_rn(zp, __fmul_rn((float)((int32_t)c + 128), scale));
+}
+
+// One thread per 4 codes; block_elems % 4 == 0.
+template <typename T>
+__global__ void __launch_bounds__(256)
+decompress_kernel(const int8_t *__restrict__ codes, const float *__restrict__ stats,
+                  T *__restrict__ dst, size_t num_blocks, int block_elems) {
+    const size_t quads = num_blocks * (size_t)(block_elems / 4);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t e0 = i * 4;
+        const size_t b = e0 / block_elems;
+        const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
+        const uint32_t w = __ldcs(reinterpret_cast<const uint32_t *>(codes) + i);
+        const int8_t *c = reinterpret_cast<const int8_t *>(&w);
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = dequant_one(c[k], st.w, st.z);
+        if constexpr (sizeof(T) == 4) {
+            __stcs(reinterpret_cast<float4 *>(dst) + i, make_float4(v[0], v[1], v[2], v[3]));
+        } else {
+            __half2 a = __floats2half2_rn(v[0], v[1]), bb = __floats2half2_rn(v[2], v[3]);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t *>(&a);
+            u.y = *reinterpret_cast<uint32_t *>(&bb);
+            __stcs(reinterpret_cast<uint2 *>(dst) + i, u);
+        }
+    }
+}
+
+// ---- compression/kv_compress.cpp:6-46 ------------------------------------
+__device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t mant = x & 0x007FFFFFu;
+    const int32_t e = (int32_t)((x >> 23) & 0xFFu) - 127;
+    if (e > 15) return (uint16_t)(sign | 0x7C00u);
+    if (e > -15) return (uint16_t)(sign | ((uint32_t)(e + 15) << 10) | (mant >> 13));
+    return (uint16_t)sign;
+}
+
+__device__ __forceinline__ float f16_trunc_to_f32(uint16_t h) {
+    const uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    const uint32_t e = ((uint32_t)h & 0x7C00u) >> 10;
+    const uint32_t mant = (uint32_t)h & 0x03FFu;
+    uint32_t x;
+    if (e == 0) x = sign;
+    else if (e == 0x1F) x = sign | 0x7F800000u | (mant << 13);
+    else x = sign | ((e - 15 + 127) << 23) | (mant << 13);
+    return __uint_as_float(x);
+}
+
+__global__ void __launch_bounds__(256)
+encode_trunc_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, size_t n) {
+    const size_t quads = n / 4;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(src) + i);
+        uint2 o;
+        o.x = (uint32_t)f32_to_f16_trunc(v.x) | ((uint32_t)f32_to_f16_trunc(v.y) << 16);
+        o.y = (uint32_t)f32_to_f16_trunc(v.z) | ((uint32_t)f32_to_f16_trunc(v.w) << 16);
+        __stcs(reinterpret_cast<uint2 *>(dst) + i, o);
+    }
+    for (size_t i = quads * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = f32_to_f16_trunc(src[i]);
+}
+
+__global__ void __launch_bounds__(256)
+decode_trunc_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, size_t n) {
+    const size_t quads = n / 4;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src) + i);
+        __stcs(reinterpret_cast<float4 *>(dst) + i,
+               make_float4(f16_trunc_to_f32((uint16_t)v.x), f16_trunc_to_f32((uint16_t)(v.x >> 16)),
+                           f16_trunc_to_f32((uint16_t)v.y), f16_trunc_to_f32((uint16_t)(v.y >> 16))));
+    }
+    for (size_t i = quads * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = f16_trunc_to_f32(src[i]);
+}
+
+unsigned grid_for(size_t work, int per_block) {
+    size_t b = (work + per_block - 1) / per_block;
+    const size_t cap = 148ull * 16;  // persistent-ish: 16 CTAs per SM, grid-stride beyond
+    if (b > cap) b = cap;
+    return (unsigned)(b ? b : 1);
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace kvx
+
+using namespace kvx;
+
+extern "C" KVX_API int kvx_compress_int8(const void *src, int32_t src_dtype, int8_t *codes,
+                                         float *stats, size_t num_blocks, int32_t block_elems,
+                                         void *stream) {
+    if (!src || !codes || !stats || block_elems <= 0) return KVX_EINVAL;
+    if (src_dtype != KVX_F16 && src_dtype != KVX_F32) return KVX_EINVAL;
+    if (!aligned16(stats)) return KVX_EINVAL;
+    if (num_blocks == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(num_blocks, 8);
+    const bool fast = block_elems == 2048 && aligned16(src) && aligned16(codes);
+    if (src_dtype == KVX_F16) {
+        if (fast)
+            compress_2048_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks);
+        else
+            compress_generic_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks, block_elems);
+    } else {
+        if (fast)
+            compress_2048_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks);
+        else
+            compress_generic_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks, block_elems);
+    }
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *stats, void *dst,
+                                           int32_t dst_dtype, size_t num_blocks,
+                                           int32_t block_elems, void *stream) {
+    if (!codes || !stats || !dst || block_elems <= 0) return KVX_EINVAL;
+    if (dst_dtype != KVX_F16 && dst_dtype != KVX_F32) return KVX_EINVAL;
+    if (block_elems % 4 || !aligned16(stats) || (reinterpret_cast<uintptr_t>(codes) & 3) ||
+        !aligned16(dst))
+        return KVX_EINVAL;
+    if (num_blocks == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(num_blocks * (size_t)(block_elems / 4), 256);
+    if (dst_dtype == KVX_F32)
+        decompress_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+    else
+        decompress_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_f32_to_f16_trunc(const float *src, uint16_t *dst, size_t n, void *stream) {
+    if (!src || !dst || !aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7)) return KVX_EINVAL;
+    if (n == 0) return KVX_OK;
+    encode_trunc_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n);
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, size_t n, void *stream) {
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 7) || !aligned16(dst)) return KVX_EINVAL;
+    if (n == 0) return KVX_OK;
+    decode_trunc_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n);
+    return launch_status();
+}

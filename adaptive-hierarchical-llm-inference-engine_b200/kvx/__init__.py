@@ -1,0 +1,202 @@
+"""Python front end of libadaptive_engine.so (ctypes over the C ABI in
+include/kvx.h and include/adaptive_engine.h).
+
+Tensors are torch CUDA tensors; only their data pointers and the current
+CUDA stream cross the ABI.  There is no fallback: importing this module on a
+machine where the library cannot be loaded raises, and every call whose
+status is not KVX_OK raises KvxError.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(PKG, "libadaptive_engine.so")
+
+KVX_F32, KVX_F16, KVX_I8 = 0, 1, 2
+HEAD_DIM, PAGE_TOKENS = 128, 16
+
+STATUS = {0: "ok", -1: "invalid argument", -2: "object pinned", -3: "CUDA error",
+          -4: "unsupported geometry or dtype", -5: "bounded device wait expired",
+          -6: "workspace or pool too small", -7: "no sm_100 device"}
+
+
+class KvxError(RuntimeError):
+    def __init__(self, fn, status):
+        super().__init__(f"{fn}: {STATUS.get(status, status)} ({status})")
+        self.status = status
+
+
+def build() -> str:
+    """Compile the library in-tree (nvcc, sm_100a)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", PKG, "-j8"], check=True)
+    return LIB_PATH
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `make -C {PKG}`")
+    return C.CDLL(LIB_PATH)
+
+
+lib = _load()
+
+
+class KvPaged(C.Structure):
+    _fields_ = [("pool", C.c_void_p), ("stats", C.c_void_p), ("dtype", C.c_int32),
+                ("num_pages", C.c_int32), ("num_kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("page_tokens", C.c_int32)]
+
+
+_vp, _i32, _sz, _f32 = C.c_void_p, C.c_int32, C.c_size_t, C.c_float
+lib.kvx_version.restype = C.c_char_p
+lib.kvx_status_string.restype = C.c_char_p
+lib.kvx_status_string.argtypes = [C.c_int]
+lib.kvx_device_check.restype = C.c_int
+lib.kvx_append.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp]
+lib.kvx_decode_workspace_bytes.restype = _sz
+lib.kvx_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32]
+lib.kvx_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32, _f32,
+                           _vp, _sz, _vp, _vp]
+lib.kvx_compress_int8.argtypes = [_vp, _i32, _vp, _vp, _sz, _i32, _vp]
+lib.kvx_decompress_int8.argtypes = [_vp, _vp, _vp, _i32, _sz, _i32, _vp]
+lib.kvx_f32_to_f16_trunc.argtypes = [_vp, _vp, _sz, _vp]
+lib.kvx_f16_trunc_to_f32.argtypes = [_vp, _vp, _sz, _vp]
+lib.kvx_lru_select.argtypes = [_vp, _sz, _vp, _vp]
+lib.kvx_migrate_frames.argtypes = [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _sz, _i32, _i32, _vp, _vp]
+for _fn in ("kvx_append", "kvx_decode", "kvx_compress_int8", "kvx_decompress_int8",
+            "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
+            "kvx_migrate_frames"):
+    getattr(lib, _fn).restype = C.c_int
+
+
+def _check(fn, rc):
+    if rc != 0:
+        raise KvxError(fn, rc)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _stream(stream):
+    if stream is not None:
+        return C.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    return C.c_void_p(_torch().cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t):
+    torch = _torch()
+    return {torch.float32: KVX_F32, torch.float16: KVX_F16, torch.int8: KVX_I8}[t.dtype]
+
+
+def paged(pool, stats=None) -> KvPaged:
+    """Describe one layer's pool tensor [pages][2][hkv][16][128]."""
+    assert pool.is_cuda and pool.is_contiguous() and pool.dim() == 5
+    pages, two, hkv, pt, dim = pool.shape
+    assert two == 2
+    return KvPaged(pool.data_ptr(), 0 if stats is None else stats.data_ptr(), _dtype_code(pool),
+                   pages, hkv, dim, pt)
+
+
+def append(pool, block_table, positions, new_k, new_v, error_flag=None, stream=None):
+    kv = paged(pool)
+    rc = lib.kvx_append(C.byref(kv), _ptr(block_table), block_table.shape[1], _ptr(positions),
+                        positions.shape[0], _ptr(new_k), _ptr(new_v), _ptr(error_flag),
+                        _stream(stream))
+    _check("kvx_append", rc)
+
+
+def decode_workspace_bytes(batch, num_q_heads, max_pages):
+    return lib.kvx_decode_workspace_bytes(batch, num_q_heads, max_pages, PAGE_TOKENS)
+
+
+def decode(pool, block_table, seq_lens, q, out=None, stats=None, workspace=None,
+           error_flag=None, sm_scale=0.0, stream=None):
+    """Paged GQA decode.  q: [batch][hq][128] fp32/fp16 CUDA tensor."""
+    torch = _torch()
+    kv = paged(pool, stats)
+    batch, hq, _ = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    need = decode_workspace_bytes(batch, hq, block_table.shape[1])
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    rc = lib.kvx_decode(C.byref(kv), _ptr(block_table), block_table.shape[1], _ptr(seq_lens),
+                        batch, hq, _ptr(q), _ptr(out), _dtype_code(q), sm_scale,
+                        _ptr(workspace), workspace.numel() * workspace.element_size(),
+                        _ptr(error_flag), _stream(stream))
+    _check("kvx_decode", rc)
+    return out
+
+
+def compress_int8(src, block_elems=PAGE_TOKENS * HEAD_DIM, codes=None, stats=None, stream=None):
+    torch = _torch()
+    n = src.numel()
+    nb = n // block_elems
+    if codes is None:
+        codes = torch.empty(n, dtype=torch.int8, device=src.device)
+    if stats is None:
+        stats = torch.empty((nb, 4), dtype=torch.float32, device=src.device)
+    rc = lib.kvx_compress_int8(_ptr(src), _dtype_code(src), _ptr(codes), _ptr(stats), nb,
+                               block_elems, _stream(stream))
+    _check("kvx_compress_int8", rc)
+    return codes, stats
+
+
+def decompress_int8(codes, stats, dtype=None, block_elems=PAGE_TOKENS * HEAD_DIM, out=None,
+                    stream=None):
+    torch = _torch()
+    dtype = dtype or torch.float32
+    if out is None:
+        out = torch.empty(codes.numel(), dtype=dtype, device=codes.device)
+    rc = lib.kvx_decompress_int8(_ptr(codes), _ptr(stats), _ptr(out), _dtype_code(out),
+                                 codes.numel() // block_elems, block_elems, _stream(stream))
+    _check("kvx_decompress_int8", rc)
+    return out
+
+
+def f32_to_f16_trunc(x, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(x.numel(), dtype=torch.int16, device=x.device)
+    _check("kvx_f32_to_f16_trunc", lib.kvx_f32_to_f16_trunc(_ptr(x), _ptr(out), x.numel(),
+                                                            _stream(stream)))
+    return out
+
+
+def f16_trunc_to_f32(h, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(h.numel(), dtype=torch.float32, device=h.device)
+    _check("kvx_f16_trunc_to_f32", lib.kvx_f16_trunc_to_f32(_ptr(h), _ptr(out), h.numel(),
+                                                            _stream(stream)))
+    return out
+
+
+def lru_select(stamps, victim=None, stream=None):
+    torch = _torch()
+    if victim is None:
+        victim = torch.empty(1, dtype=torch.int32, device=stamps.device)
+    _check("kvx_lru_select", lib.kvx_lru_select(_ptr(stamps), stamps.numel(), _ptr(victim),
+                                                _stream(stream)))
+    return victim
+
+
+def migrate_frames(dev_base, dev_capacity, host_base, host_capacity, dev_frames, host_frames,
+                   frame_bytes, direction, ctas=0, error_flag=None, stream=None):
+    """dev_base/host_base: raw addresses (int) or tensors; frames: int32 CUDA tensors."""
+    def addr(x):
+        return C.c_void_p(x if isinstance(x, int) else x.data_ptr())
+    rc = lib.kvx_migrate_frames(addr(dev_base), dev_capacity, addr(host_base), host_capacity,
+                                _ptr(dev_frames), _ptr(host_frames), dev_frames.numel(),
+                                frame_bytes, direction, ctas, _ptr(error_flag), _stream(stream))
+    _check("kvx_migrate_frames", rc)

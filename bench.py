@@ -1,0 +1,398 @@
+"""Benchmark: batched fragmented paged decode (the KV-cache hot path).
+
+Workload (one step): for each of 28 layers of Llama-3.2-3B KV geometry
+(8 KV heads x 128, fp16, 24 q-heads, GQA group 3) and batch 32 with context
+lengths U[512, 8192] (seeded) and randomly permuted physical pages, append
+one token per sequence into its page, then run paged GQA decode attention
+over the whole context.  Metric: KV bytes read by decode per second (GB/s),
+whole job.  With --gpus N the KV heads are sharded over N ranks (each rank
+owns 8/N heads and the matching q-heads) and the attention outputs are
+all-gathered over NCCL each layer; total work is fixed (strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "adaptive-hierarchical-llm-inference-engine_b200")
+for _p in (PKG, os.path.join(ROOT, "tests"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import kvgen  # noqa: E402
+
+METRIC = "paged-decode KV GB/s"
+LAYERS, HKV, HQ, DIM, PT, BATCH = 28, 8, 24, 128, 16, 32
+CTX_LO, CTX_HI, SEED = 512, 8192, 20241201
+WORKLOAD = "batched fragmented decode: Llama-3.2-3B KV (28L, 8kv x128, 24q), fp16, B32, ctx U[512,8192], permuted pages"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def workload_lens():
+    return kvgen.randint(SEED, BATCH, CTX_LO, CTX_HI).astype(np.int64)
+
+
+# --------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import kvx
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    assert HKV % world == 0, "KV heads must divide evenly over the GPUs"
+    hkv, hq = HKV // world, HQ // world
+    steps, warm = args.steps, args.warmup
+    total_steps = steps + warm
+
+    lens0 = workload_lens()
+    bt_np, num_pages = kvgen.paged_layout(lens0, PT, total_steps, SEED + 1)
+    max_pages = bt_np.shape[1]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 17 * rank)
+    pools = [torch.randn((num_pages, 2, hkv, PT, DIM), generator=g, device="cuda",
+                         dtype=torch.float16) for _ in range(LAYERS)]
+    bt = torch.from_numpy(bt_np).cuda()
+    q = torch.randn((LAYERS, BATCH, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nk = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nv = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    out = torch.empty((LAYERS, BATCH, hq, DIM), device="cuda", dtype=torch.float16)
+    gathered = torch.empty((LAYERS, world, BATCH, hq, DIM), device="cuda", dtype=torch.float16) \
+        if world > 1 else None
+    ws_bytes = kvx.decode_workspace_bytes(BATCH, hq, max_pages)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = torch.from_numpy(lens0.astype(np.int32)).cuda()
+    lens1 = pos + 1
+    comm = torch.cuda.Stream() if world > 1 else None
+    main = torch.cuda.current_stream()
+    layer_done = [torch.cuda.Event() for _ in range(LAYERS)]
+
+    def step(ev=None):
+        for l in range(LAYERS):
+            kvx.append(pools[l], bt, pos, nk[l], nv[l], error_flag=err)
+            if ev is not None:
+                ev[l][0].record()
+            kvx.decode(pools[l], bt, lens1, q[l], out=out[l], workspace=ws, error_flag=err)
+            if ev is not None:
+                ev[l][1].record()
+            if world > 1:
+                layer_done[l].record()
+                with torch.cuda.stream(comm):
+                    comm.wait_event(layer_done[l])
+                    dist.all_gather_into_tensor(gathered[l], out[l])
+        pos.add_(1)
+        lens1.add_(1)
+        if world > 1:
+            main.wait_stream(comm)
+
+    def kv_bytes(lens_after):  # algorithmic K+V bytes decode reads for one layer
+        return int(lens_after.sum()) * 2 * hkv * DIM * 2
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(LAYERS)] for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    t0.record()
+    for k in range(steps):
+        step([(a, b) for (a, b) in ev[k]])
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    dec_ms = [a.elapsed_time(b) for row in ev for (a, b) in row]
+    assert err.item() == 0, f"device error flag {err.item()}"
+
+    lens_timed = [lens0 + warm + k + 1 for k in range(steps)]
+    rank_bytes = sum(kv_bytes(L) * LAYERS for L in lens_timed)
+    t_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max = t.item()
+    total_bytes = rank_bytes * world
+    value = total_bytes / (t_max / 1e3) / 1e9
+
+    # roofline of the decode kernel: algorithmic bytes per launch / mean launch time
+    mean_layer_bytes = rank_bytes / (steps * LAYERS)
+    qo_bytes = 2 * BATCH * hq * DIM * 2 + BATCH * max_pages * 4 + BATCH * 4
+    mean_dec_ms = sum(dec_ms) / len(dec_ms)
+    achieved = (mean_layer_bytes + qo_bytes) / (mean_dec_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(t_max / steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic (seeded N(0,1) K/V/Q, seeded context lengths and page permutation)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "batch": BATCH, "kv_heads": HKV,
+                   "q_heads": HQ, "head_dim": DIM, "page_tokens": PT,
+                   "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": "inputs larger than L2 (KV pool ~17 GB)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_kind": peak_kind, "kernel": "paged_decode_kernel (+combine)",
+                     "mean_launch_us": round(mean_dec_ms * 1e3, 2)},
+        "gpu_launches": steps * LAYERS * 3,
+        "clocks": clk,
+    }
+    if not args.no_e2e:
+        result["e2e"] = run_e2e(args, pools, bt, lens0, warm + steps, hq, hkv, ws, err, world)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(sample_layers=1)
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, pools, bt, lens0, start_step, hq, hkv, ws, err, world):
+    """Same step through the C ABI with host buffers: every step copies its
+    q / new K / new V for all layers from pinned host memory and reads the
+    attention outputs back, inside the timed region."""
+    import torch
+
+    import kvx
+    steps = max(4, min(args.steps, 16))
+    h_q = torch.randn((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
+    h_k = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
+    h_v = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
+    h_o = torch.empty((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
+    d_q, d_k, d_v = (torch.empty_like(h, device="cuda") for h in (h_q, h_k, h_v))
+    d_o = torch.empty_like(h_o, device="cuda")
+    # replay the positions of the last `steps` device-resident steps (the
+    # pool has room for exactly warmup+steps appended tokens per sequence)
+    pos = torch.from_numpy((lens0 + start_step - steps).astype(np.int32)).cuda()
+    lens1 = pos + 1
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    nbytes = 0
+    for k in range(steps):
+        d_q.copy_(h_q, non_blocking=True)
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        for l in range(LAYERS):
+            kvx.append(pools[l], bt, pos, d_k[l], d_v[l], error_flag=err)
+            kvx.decode(pools[l], bt, lens1, d_q[l], out=d_o[l], workspace=ws, error_flag=err)
+        h_o.copy_(d_o, non_blocking=True)
+        nbytes += int((lens0 + start_step - steps + k + 1).sum()) * 2 * hkv * DIM * 2 * LAYERS
+        pos.add_(1)
+        lens1.add_(1)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return {"value": round(nbytes * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2),
+            "d2h_bytes_per_step": int(h_o.numel() * 2), "steps": steps,
+            "path": "kvx C ABI (ctypes) with pinned host buffers"}
+
+
+# --------------------------------------------------------------------------
+def cpu_baseline(sample_layers=1):
+    """The reference's own CPU code (oracle/_ref/libkvref.so, built from the
+    reference sources) on this host's cores: one layer of the step (append
+    one token per sequence with KVManager::save_page, then single-query
+    attention per (sequence, q-head) composed from TensorOps matmul/softmax),
+    fanned over all host threads.  Falls back to the C restatement (port)."""
+    threads = os.cpu_count() or 1
+    lens = workload_lens() + 1
+    kind = "reference"
+    try:
+        from oracle import Reference
+        R = Reference()
+    except Exception:
+        R, kind = None, "port"
+    total_s = 0.0
+    total_bytes = 0
+    rng = np.random.default_rng(SEED)
+    tmax = int(lens.max())
+    Kall = rng.standard_normal((HKV, tmax, DIM), dtype=np.float32)
+    Vall = rng.standard_normal((HKV, tmax, DIM), dtype=np.float32)
+    for layer in range(sample_layers):
+        for s in range(BATCH):
+            T = int(lens[s])
+            K = np.ascontiguousarray(Kall[:, :T])
+            V = np.ascontiguousarray(Vall[:, :T])
+            q = rng.standard_normal((HQ, DIM), dtype=np.float32)
+            out = np.empty((HQ, DIM), np.float32)
+            if R is not None:
+                # one call per sequence: HQ units over HKV kv-heads (unit u -> kv u % HKV
+                # is the helper's mapping; reorder q so unit u reads kv-head u // G)
+                qq = np.ascontiguousarray(q.reshape(HKV, HQ // HKV, DIM).transpose(1, 0, 2).reshape(HQ, DIM))
+                dt = R.L.kvref_time_decode(qq, np.ascontiguousarray(K), np.ascontiguousarray(V), HKV, HQ, T, DIM,
+                                           threads, out)
+            else:
+                from oracle import Oracle
+                o = Oracle()
+                t0 = time.perf_counter()
+                for h in range(HQ):
+                    o.attention_row(q[h], K[h // (HQ // HKV)], V[h // (HQ // HKV)])
+                dt = time.perf_counter() - t0
+            total_s += dt
+            total_bytes += T * 2 * HKV * DIM * 2
+    append_s = 0.0
+    if R is not None:
+        with tempfile.TemporaryDirectory(dir="/dev/shm" if os.path.isdir("/dev/shm") else None) as d:
+            cwd = os.getcwd()
+            os.chdir(d)
+            try:
+                rows = kvgen.normal(77, (BATCH, HKV * DIM))
+                append_s = R.L.kvref_time_append(rows, BATCH, HKV, DIM, PT, b"pages")
+            finally:
+                os.chdir(cwd)
+    value = total_bytes / (total_s + append_s) / 1e9
+    return {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{sample_layers} of {LAYERS} layers of one step: {BATCH} appends via KVManager::save_page "
+                      f"+ {BATCH}x{HQ} single-query attentions (TensorOps matmul/softmax), {threads} threads",
+            "seconds": round(total_s + append_s, 3)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(1))
+    wall = time.perf_counter() - t0
+    v = statistics.median([x["value"] for x in vals])
+    base = vals[-1]
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "sample": base["sample"]},
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": base["cores"], "kind": base["kind"],
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

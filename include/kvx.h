@@ -1,0 +1,152 @@
+/*
+ * kvx.h -- C ABI of the B200 (sm_100a) KV-cache kernels.
+ *
+ * Plain C: device pointers, sizes and a cudaStream_t passed as void*.  Every
+ * entry point returns KVX_OK (0) or a negative kvx_status and never throws.
+ * All work is enqueued on the given stream (NULL = legacy default stream);
+ * nothing here synchronises the host unless its comment says so.
+ *
+ * Page pool layout (one layer):
+ *     pool[num_pages][2 (0=K, 1=V)][num_kv_heads][page_tokens][head_dim]
+ * so one (page, K|V, head) block of page_tokens x head_dim elements is
+ * contiguous (4 KiB at fp16, 16 x 128).  For int8 pools a parallel array
+ *     stats[num_pages][2][num_kv_heads][4] = {minVal, maxVal, scale, zeroPoint}
+ * holds the reference's QuantizationStats of each block.
+ *
+ * Each entry point names the reference interface it replaces (paths
+ * relative to the reference project root).
+ */
+#ifndef KVX_H
+#define KVX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define KVX_API __declspec(dllexport)
+#else
+#define KVX_API __attribute__((visibility("default")))
+#endif
+
+enum kvx_status {
+    KVX_OK = 0,
+    KVX_EINVAL = -1,       /* bad argument, id or geometry (the reference's -1) */
+    KVX_EBUSY = -2,        /* object pinned / in use (the reference's -2) */
+    KVX_ECUDA = -3,        /* a CUDA runtime call or launch failed */
+    KVX_EUNSUPPORTED = -4, /* geometry/dtype this build has no kernel for */
+    KVX_ETIMEOUT = -5,     /* a bounded device wait expired (see error_flag) */
+    KVX_ENOSPC = -6,       /* workspace / pool too small */
+    KVX_ENODEV = -7        /* no sm_100 device current */
+};
+
+enum kvx_dtype { KVX_F32 = 0, KVX_F16 = 1, KVX_I8 = 2 };
+
+/* One layer of the paged cache. */
+typedef struct kvx_paged {
+    void *pool;           /* see layout above */
+    const float *stats;   /* KVX_I8 only, else NULL */
+    int32_t dtype;        /* enum kvx_dtype */
+    int32_t num_pages;
+    int32_t num_kv_heads;
+    int32_t head_dim;     /* 128 */
+    int32_t page_tokens;  /* 16 */
+} kvx_paged;
+
+KVX_API const char *kvx_version(void);
+KVX_API const char *kvx_status_string(int status);
+/* KVX_OK when the current device is compute capability 10.x (the only
+ * target this library carries code for), else KVX_ENODEV. */
+KVX_API int kvx_device_check(void);
+
+/* Paged append.  Replaces KVManager::save_page (cache/kv_cache.cpp:111-127)
+ * as called by InferenceController::appendKVPage (runtime/inference.cpp:50-54):
+ * for each sequence s the token at position positions[s] is stored in
+ * physical page block_table[s*max_pages + pos/page_tokens], slot
+ * pos % page_tokens.  new_k/new_v: [batch][num_kv_heads][head_dim] in the
+ * pool's dtype (KVX_F32 or KVX_F16).  Bit-exact copy.  A position or page
+ * id out of range skips that row and sets bit 1 of *error_flag (device
+ * int32, may be NULL). */
+KVX_API int kvx_append(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                       const int32_t *positions, int32_t batch, const void *new_k,
+                       const void *new_v, int32_t *error_flag, void *stream);
+
+/* Bytes of scratch kvx_decode needs (split-K partial results). */
+KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t max_pages,
+                                          int32_t page_tokens);
+
+/* Paged GQA decode attention.  Replaces the naive attention of
+ * runtime/gpu/cuda_executor.cu:246-311 and native-engine/cuda/attention.cu:18-157
+ * with the semantics of TensorOps::attention (runtime/tensor_ops.cpp:179-219):
+ * for sequence s and q-head h (kv-head h / (num_q_heads/num_kv_heads)),
+ * out = softmax(q.K^T * sm_scale) V over tokens [0, seq_lens[s]), gathered
+ * through the block table.  sm_scale <= 0 means 1/sqrt(head_dim).
+ * q/out: [batch][num_q_heads][head_dim] in io_dtype (KVX_F32 or KVX_F16).
+ * seq_lens[s] == 0 gives a zero row.  error_flag (device int, may be NULL)
+ * gets bit 0 set if a bounded wait for page data expired.  workspace:
+ * kvx_decode_workspace_bytes() bytes of device memory, no initialisation. */
+KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                       const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                       const void *q, void *out, int32_t io_dtype, float sm_scale,
+                       void *workspace, size_t workspace_bytes, int32_t *error_flag,
+                       void *stream);
+
+/* Per-block int8 quantisation.  Replaces KVCompressionEngine::compressToINT8
+ * (native-engine/cpp/KVCompressionEngine.cpp:83-113), one reference call per
+ * block of block_elems elements: min/max, scale=(max-min)/255 (0 -> 1),
+ * zeroPoint=min, code = clamp(round((x-min)/scale), 0, 255) - 128.
+ * src: num_blocks*block_elems elements of src_dtype (KVX_F16 widened
+ * exactly, or KVX_F32).  stats: [num_blocks][4] = {min, max, scale, zeroPoint}.
+ * Bit-exact with the reference. */
+KVX_API int kvx_compress_int8(const void *src, int32_t src_dtype, int8_t *codes, float *stats,
+                              size_t num_blocks, int32_t block_elems, void *stream);
+
+/* Inverse.  Replaces KVCompressionEngine::decompressINT8
+ * (native-engine/cpp/KVCompressionEngine.cpp:115-122): zeroPoint +
+ * (code+128)*scale in fp32 (no FMA).  dst_dtype KVX_F32 (bit-exact) or
+ * KVX_F16 (that value rounded to nearest). */
+KVX_API int kvx_decompress_int8(const int8_t *codes, const float *stats, void *dst,
+                                int32_t dst_dtype, size_t num_blocks, int32_t block_elems,
+                                void *stream);
+
+/* Truncating fp32 -> fp16 of the disk tier.  Replaces float32_to_float16
+ * (compression/kv_compress.cpp:6-25,48-53).  Bit-exact. */
+KVX_API int kvx_f32_to_f16_trunc(const float *src, uint16_t *dst, size_t n, void *stream);
+/* Inverse, subnormals to zero.  Replaces float16_to_float32
+ * (compression/kv_compress.cpp:27-46,55-60).  Bit-exact. */
+KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, size_t n, void *stream);
+
+/* LRU victim.  Replaces LRUEvictionPolicy::selectPageToEvict
+ * (native-engine/cpp/AdvancedEvictionPolicy.cpp:9-23) and KVCacheGPU::findLRUPage
+ * (native-engine/cpp/KVCacheGPU.cpp:54-66): the index of the smallest stamp,
+ * the lowest index on ties, UINT64_MAX stamps never chosen; -1 if none.
+ * Writes the index to *victim (device int32).  No workspace. */
+KVX_API int kvx_lru_select(const uint64_t *stamps, size_t n, int32_t *victim, void *stream);
+
+/* Page-frame migration between the device pool and a host frame arena
+ * (pinned, mapped with cudaHostAlloc(..., cudaHostAllocMapped) or registered).
+ * Replaces KVCacheGPU::transferToHost / transferToGPU
+ * (native-engine/cpp/KVCacheGPU.cpp:68-120) and the simulated copies of
+ * lw_moveKvToRam / lw_moveKvToGpu (native-engine/llama_wrapper/llama_wrapper.cpp:220-341).
+ * Frame i of the transfer moves frame_bytes between
+ *   device  dev_base + dev_frames[i]  * frame_bytes
+ *   host    host_base + host_frames[i] * frame_bytes
+ * direction 0: device -> host (evict), 1: host -> device (fetch).
+ * frame_bytes must be a multiple of 16 and both bases 16-byte aligned.
+ * dev_frames/host_frames are device-readable int32 arrays; a frame id
+ * outside [0, dev_capacity) / [0, host_capacity) skips that frame and sets
+ * bit 1 of *error_flag (may be NULL).  `ctas` bounds the SMs the copy
+ * occupies (0 = default 16), so it can run on a side stream beside decode. */
+KVX_API int kvx_migrate_frames(void *dev_base, int32_t dev_capacity, void *host_base,
+                               int32_t host_capacity, const int32_t *dev_frames,
+                               const int32_t *host_frames, int32_t num_frames,
+                               size_t frame_bytes, int32_t direction, int32_t ctas,
+                               int32_t *error_flag, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

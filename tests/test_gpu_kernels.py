@@ -1,0 +1,275 @@
+"""GPU parity: every kernel of libadaptive_engine.so against the oracle.
+
+Integer / byte / index results (append, int8 codes + stats, fp16 truncation
+codec, LRU victims, frame migration) must be bit-exact.  Attention outputs
+must satisfy |gpu - ref| <= ATOL + RTOL * |ref| with the tolerance the
+reference comparison is specified at: RTOL = 1e-3, ATOL = 1e-2.
+"""
+import numpy as np
+import pytest
+
+import kvgen
+from conftest import golden
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 1e-2
+
+
+@pytest.fixture(scope="module")
+def kvx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import kvx as k
+    assert k.lib.kvx_device_check() == 0, "not an sm_100 device"
+    return k
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def assert_close(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = np.abs(got - want) - (ATOL + RTOL * np.abs(want))
+    assert err.max() <= 0, f"max excess {err.max():.3e}, max abs err {np.abs(got - want).max():.3e}"
+
+
+# ---------------------------------------------------------------- append ---
+
+@pytest.mark.parametrize("np_dtype", [np.float32, np.float16])
+def test_append_bitexact(kvx, oracle, np_dtype):
+    lens = np.array([0, 5, 15, 16, 17, 100, 255, 300], np.int64)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 1, seed=77)
+    hkv = 8
+    pool = kvgen.normal(78, (num_pages, 2, hkv, 16, 128)).astype(np_dtype)
+    nk = kvgen.normal(79, (lens.size, hkv, 128)).astype(np_dtype)
+    nv = kvgen.normal(80, (lens.size, hkv, 128)).astype(np_dtype)
+    pos = lens.astype(np.int32)
+    g_pool = dev(pool)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kvx.append(g_pool, dev(bt), dev(pos), dev(nk), dev(nv), error_flag=err)
+    oracle.append(pool, bt, pos, nk, nv, 16)
+    assert np.array_equal(g_pool.cpu().numpy().view(np.uint8), pool.view(np.uint8))
+    assert err.item() == 0
+
+
+def test_append_out_of_range_is_reported_not_written(kvx):
+    bt = np.array([[0, 1]], np.int32)
+    pool = torch.zeros((2, 2, 1, 16, 128), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ones = torch.ones((1, 1, 128), dtype=torch.float16, device="cuda")
+    kvx.append(pool, dev(bt), dev(np.array([32], np.int32)), ones, ones, error_flag=err)
+    torch.cuda.synchronize()
+    assert err.item() & 2
+    assert pool.abs().sum().item() == 0
+
+
+# ---------------------------------------------------------------- decode ---
+
+def fill_pool_gpu(kvx, g, dtype_np):
+    """Append every token of the golden case through the GPU append kernel."""
+    B = len(g["seq_lens"])
+    tmax = int(g["seq_lens"].max())
+    hkv, hq, dim, seed = int(g["hkv"]), int(g["hq"]), int(g["dim"]), int(g["seed"])
+    K = kvgen.normal(seed + 1, (B, tmax, hkv, dim)).astype(dtype_np)
+    V = kvgen.normal(seed + 2, (B, tmax, hkv, dim)).astype(dtype_np)
+    Q = kvgen.normal(seed + 3, (B, hq, dim)).astype(np.float32)
+    pool = torch.zeros((int(g["num_pages"]), 2, hkv, 16, dim),
+                       dtype=torch.float32 if dtype_np == np.float32 else torch.float16,
+                       device="cuda")
+    bt = dev(g["block_table"])
+    lens = g["seq_lens"]
+    Kd, Vd = dev(K), dev(V)
+    for t in range(tmax):
+        rows = np.nonzero(lens > t)[0]
+        r = torch.from_numpy(rows).cuda()
+        kvx.append(pool, bt[r].contiguous(), dev(np.full(rows.size, t, np.int32)),
+                   Kd[r, t].contiguous(), Vd[r, t].contiguous())
+    return pool, K, V, Q
+
+
+@pytest.mark.parametrize("name,dtype", [("paged_cfg1.npz", np.float32),
+                                        ("paged_fp16.npz", np.float16),
+                                        ("paged_gqa8.npz", np.float16)])
+def test_decode_matches_reference_golden(kvx, oracle, name, dtype):
+    g = golden(name)
+    pool, K, V, Q = fill_pool_gpu(kvx, g, dtype)
+    # cache contents: bit-exact with the oracle's paged append of the same tokens
+    ref_pool = np.zeros(tuple(pool.shape), dtype)
+    lens = g["seq_lens"]
+    for t in range(int(lens.max())):
+        rows = np.nonzero(lens > t)[0]
+        oracle.append(ref_pool, g["block_table"][rows], np.full(rows.size, t, np.int32),
+                      K[rows, t], V[rows, t], 16)
+    assert np.array_equal(pool.cpu().numpy().view(np.uint8), ref_pool.view(np.uint8))
+    for io in (torch.float32, torch.float16):
+        q = dev(Q).to(io)
+        out = kvx.decode(pool, dev(g["block_table"]), dev(g["seq_lens"]), q)
+        torch.cuda.synchronize()
+        want = g["out"] if io == torch.float32 else g["out"].astype(np.float16).astype(np.float32)
+        assert_close(out.float().cpu().numpy(), want)
+
+
+def test_decode_empty_and_single_token(kvx, oracle):
+    lens = np.array([0, 1, 0, 2], np.int64)
+    bt, num_pages = kvgen.paged_layout(np.maximum(lens, 1), 16, 0, seed=5)
+    pool = kvgen.normal(6, (num_pages, 2, 2, 16, 128)).astype(np.float16)
+    q = kvgen.normal(7, (4, 6, 128))
+    out = kvx.decode(dev(pool), dev(bt), dev(lens.astype(np.int32)), dev(q)).cpu().numpy()
+    ref = oracle.paged_decode(pool, bt, lens.astype(np.int32), q)
+    assert np.all(out[0] == 0) and np.all(out[2] == 0)
+    assert_close(out, ref)
+
+
+def config2_layer(seed=2024, batch=32, lo=512, hi=8192):
+    """One layer of the batched fragmented decode workload: fp16 K/V N(0,1),
+    context lengths U[lo, hi], physical pages a seeded permutation."""
+    lens = kvgen.randint(seed, batch, lo, hi)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed + 1)
+    pool = kvgen.normal(seed + 2, (num_pages, 2, 8, 16, 128)).astype(np.float16)
+    q = kvgen.normal(seed + 3, (batch, 24, 128))
+    return lens.astype(np.int32), bt, pool, q
+
+
+def test_decode_config2_layer_against_oracle(kvx, oracle):
+    lens, bt, pool, q = config2_layer()
+    out = kvx.decode(dev(pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
+    ref = oracle.paged_decode(pool, bt, lens, q)
+    assert_close(out, ref)
+
+
+@pytest.mark.parametrize("chunk", ["4", "8", "64"])
+def test_decode_split_invariance(kvx, monkeypatch, chunk):
+    """Size-independent property: the result does not depend on how the
+    context is split across CTAs (flash-decoding combine)."""
+    lens, bt, pool, q = config2_layer(seed=99, batch=8, lo=1, hi=3000)
+    base = kvx.decode(dev(pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
+    monkeypatch.setenv("KVX_DECODE_CHUNK", chunk)
+    other = kvx.decode(dev(pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
+    assert np.abs(base - other).max() < 1e-4
+
+
+def test_decode_gqa_grouping_matches_mha_expansion(kvx):
+    """Property: GQA with group G equals MHA on a pool whose kv heads are
+    repeated G times."""
+    lens = np.array([40, 333], np.int32)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=11)
+    pool = kvgen.normal(12, (num_pages, 2, 2, 16, 128)).astype(np.float16)
+    q = kvgen.normal(13, (2, 6, 128))
+    gqa = kvx.decode(dev(pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
+    mha_pool = np.repeat(pool, 3, axis=2)
+    mha = kvx.decode(dev(mha_pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
+    assert np.abs(gqa - mha).max() < 1e-5
+
+
+# ------------------------------------------------------------------ int8 ---
+
+def test_compress_int8_golden_cases(kvx):
+    g = golden("int8.npz")
+    off = 0
+    for i, n in enumerate(g["lens"]):
+        data = dev(g["data"][off:off + n])
+        codes, stats = kvx.compress_int8(data, block_elems=int(n))
+        torch.cuda.synchronize()
+        assert np.array_equal(codes.cpu().numpy(), g["codes"][off:off + n]), g["names"][i]
+        assert np.array_equal(stats.cpu().numpy().view(np.uint32).ravel(),
+                              g["stats"][i].view(np.uint32)), g["names"][i]
+        if n % 4 == 0:
+            dec = kvx.decompress_int8(codes, stats, block_elems=int(n)).cpu().numpy()
+            assert np.array_equal(dec.view(np.uint32), g["dec"][off:off + n].view(np.uint32))
+        off += n
+
+
+@pytest.mark.parametrize("np_dtype", [np.float16, np.float32])
+def test_compress_int8_pages_bitexact(kvx, oracle, np_dtype):
+    nb = 3000
+    data = kvgen.normal(31, (nb, 2048))
+    data[kvgen.uniform(32, data.size).reshape(data.shape) < 0.01] *= 20
+    data[5, :] = 0.0
+    data[6, ::2] = -0.0
+    data[7, :] = 1.5
+    data = data.astype(np_dtype)
+    codes, stats = kvx.compress_int8(dev(data))
+    rc, rs = oracle.compress_int8_blocks(data, 2048)
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    dec = kvx.decompress_int8(codes, stats).cpu().numpy()
+    assert np.array_equal(dec.view(np.uint32), oracle.decompress_int8_blocks(rc, rs, 2048).view(np.uint32))
+
+
+def test_compress_roundtrip_error_bound(kvx):
+    """Property at scale: |x - dequant(quant(x))| <= scale/2 (+1 ulp) per block."""
+    nb = 65536  # 128 Mi elements = 256 MiB fp16, larger than L2
+    x = torch.randn((nb, 2048), dtype=torch.float16, device="cuda")
+    codes, stats = kvx.compress_int8(x)
+    back = kvx.decompress_int8(codes, stats).view(nb, 2048)
+    err = (back - x.float()).abs().amax(dim=1)
+    assert bool((err <= stats[:, 2] * 0.5001 + 1e-6).all())
+
+
+def test_int8_decode_matches_reference_golden(kvx, oracle):
+    g = golden("int8_decode.npz")
+    seed, pt, dim, hkv = int(g["seed"]), int(g["pt"]), int(g["dim"]), int(g["hkv"])
+    num_pages = int(g["num_pages"])
+    pool = kvgen.normal(seed + 1, (num_pages, 2, hkv, pt, dim)).astype(np.float16)
+    mask = kvgen.uniform(seed + 5, pool.size).reshape(pool.shape) < 0.01
+    pool = (pool.astype(np.float32) * np.where(mask, 20.0, 1.0)).astype(np.float16)
+    Q = kvgen.normal(seed + 3, (len(g["seq_lens"]), int(g["hq"]), dim))
+    codes, stats = kvx.compress_int8(dev(pool))
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), g["stats"].view(np.uint32))
+    cpool = codes.view(num_pages, 2, hkv, pt, dim)
+    out = kvx.decode(cpool, dev(g["block_table"]), dev(g["seq_lens"]), dev(Q), stats=stats)
+    assert_close(out.cpu().numpy(), g["out"])
+
+
+# ------------------------------------------------------- fp16 trunc codec ---
+
+def test_f16_trunc_codec_bitexact(kvx):
+    g = golden("kv_compress.npz")
+    enc = kvx.f32_to_f16_trunc(dev(g["x"])).cpu().numpy().view(np.uint16)
+    assert np.array_equal(enc, g["enc"])
+    allh = dev(np.arange(65536, dtype=np.uint16).view(np.int16))
+    dec = kvx.f16_trunc_to_f32(allh).cpu().numpy().view(np.uint32)
+    assert np.array_equal(dec, g["dec_bits"])
+
+
+# ------------------------------------------------------------- eviction ---
+
+def test_lru_select_matches_reference(kvx, oracle):
+    g = golden("lru.npz")
+    for st, n, want in zip(g["select_stamps"], g["select_n"], g["select_out"]):
+        v = kvx.lru_select(dev(st[:n].copy())).item()
+        assert v == want
+    big = kvgen.randint(55, 1_000_001, 0, 5000).astype(np.uint64)
+    big[::7] = np.iinfo(np.uint64).max
+    assert kvx.lru_select(dev(big)).item() == oracle.lru_select(big)
+    allmax = np.full(10, np.iinfo(np.uint64).max, np.uint64)
+    assert kvx.lru_select(dev(allmax)).item() == -1
+
+
+# ------------------------------------------------------------- migration ---
+
+def test_migrate_frames_roundtrip(kvx):
+    frame = 64 * 1024
+    nf_dev, nf_host = 64, 96
+    devbuf = torch.randint(-128, 127, (nf_dev * frame,), dtype=torch.int8, device="cuda")
+    host = torch.zeros(nf_host * frame, dtype=torch.int8).pin_memory()
+    dsel = kvgen.permutation(3, nf_dev)[:40].astype(np.int32)
+    hsel = kvgen.permutation(4, nf_host)[:40].astype(np.int32)
+    kvx.migrate_frames(devbuf, nf_dev, host, nf_host, dev(dsel), dev(hsel), frame, 0, ctas=8)
+    torch.cuda.synchronize()
+    d = devbuf.cpu().numpy().reshape(nf_dev, frame)
+    h = host.numpy().reshape(nf_host, frame)
+    assert np.array_equal(h[hsel], d[dsel])
+    back = torch.zeros_like(devbuf)
+    kvx.migrate_frames(back, nf_dev, host, nf_host, dev(dsel), dev(hsel), frame, 1, ctas=8)
+    torch.cuda.synchronize()
+    assert np.array_equal(back.cpu().numpy().reshape(nf_dev, frame)[dsel], d[dsel])
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kvx.migrate_frames(back, nf_dev, host, nf_host, dev(np.array([nf_dev], np.int32)),
+                       dev(np.array([0], np.int32)), frame, 1, error_flag=err)
+    torch.cuda.synchronize()
+    assert err.item() & 2
