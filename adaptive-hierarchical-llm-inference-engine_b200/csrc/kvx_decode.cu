@@ -19,9 +19,15 @@
 //    row per instruction (bank-conflict free) and reduce with 3 shuffles.
 //    Softmax is online in the log2 domain (q pre-scaled by scale*log2 e).
 //  * P.V: lane owns 4 output dims; one row per instruction, conflict free.
-//  * Warps merge through shared memory; a split writes (m, l, o) partials
-//    and kvx_combine_kernel folds the splits (flash-decoding), or the CTA
-//    writes the final row directly when the sequence has a single split.
+//  * Warps merge through shared memory.  A sequence with one split writes
+//    its rows directly; otherwise every split writes (m, l, o) partials and
+//    takes a ticket on a per-(sequence, kv-head, head-group) counter; the
+//    last CTA to arrive folds the splits (flash-decoding combine) and resets
+//    the counter to zero, so no second launch is needed.
+//  * Fused append (kvx_append_decode): the token at positions[s] is written
+//    into its page by one CTA, and every CTA that reads that page patches
+//    the row into its shared-memory copy, so readers never depend on the
+//    write landing first.
 //  * int8 pages: the (page, head) block's {scale, zeroPoint} rides in the
 //    same bulk transfer; dequantisation is folded algebraically:
 //    q.(zp + c*s) = zp*sum(q) + s*(q.c), p.(zp + c*s) = zp*sum(p) + (p*s).c.
@@ -32,6 +38,7 @@
 #include <cstdlib>
 
 #include "kvx_common.cuh"
+#include "kvx_decode_params.cuh"
 
 namespace kvx {
 namespace {
@@ -40,19 +47,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxHeadsPerCta = 4;
 
-struct DecodeParams {
-    const uint8_t *pool;
-    const float *stats;
-    const int32_t *block_table;
-    const int32_t *seq_lens;
-    const void *q;
-    void *out;
-    float *part_o;   // [batch][hq][max_splits][128]
-    float *part_ml;  // [batch][hq][max_splits][2]
-    int32_t *error_flag;
-    int num_pages, hkv, hq, max_pages, max_splits, chunk, group, nhg;
-    float scale_log2;
-};
+
 
 template <typename KVT> struct KvTraits;
 // kVec: elements per 16-byte vector; kStages: ring depth per warp (fp32
@@ -142,14 +137,27 @@ paged_decode_kernel(const DecodeParams p) {
     const int grp = lane >> 3, sub = lane & 7;
     const int hg = blockIdx.x % p.nhg, split = blockIdx.x / p.nhg;
     const int kvh = blockIdx.y, s = blockIdx.z;
-    const int T = p.seq_lens[s];
+    const bool fused = p.positions != nullptr;
+    int T = fused ? p.positions[s] + 1 : max(p.seq_lens[s], 0);
+    if (fused && T <= 0) T = 0;
+    if (T > p.max_pages * kPageTokens) {  // context longer than the block table row
+        if (p.error_flag && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+            atomicOr(p.error_flag, 4);
+        T = p.max_pages * kPageTokens;
+    }
     const int npages = (T + kPageTokens - 1) / kPageTokens;
     const int p0 = split * p.chunk;
-    if (p0 >= npages) return;  // whole CTA: this split is past the sequence
-    const int p1 = min(p0 + p.chunk, npages);
-    const int nsplit = (npages + p.chunk - 1) / p.chunk;
     const int h0 = kvh * p.group + hg * G;  // first q-head of this CTA
     const int nh = min(G, p.group - hg * G);
+    if (p0 >= npages) {  // whole CTA: this split is past the sequence
+        if (npages == 0 && split == 0) {  // empty context: zero rows (no attention)
+            QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0) * kHeadDim;
+            for (int i = threadIdx.x; i < nh * kHeadDim; i += kThreads) io_traits<QT>::store(o + i, 0.f);
+        }
+        return;
+    }
+    const int p1 = min(p0 + p.chunk, npages);
+    const int nsplit = (npages + p.chunk - 1) / p.chunk;
 
     uint8_t *wbuf = smem + warp * kStages * kStage;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWarps * kStages * kStage) + warp * kStages;
@@ -164,6 +172,28 @@ paged_decode_kernel(const DecodeParams p) {
         fence_barrier_init();
     }
     __syncwarp();
+
+    constexpr int kRowVecs = kRowBytes / 16;
+    // page / slot of the appended token (none when its position is out of range)
+    const bool append_ok = fused && p.positions[s] >= 0 && p.positions[s] < p.max_pages * kPageTokens;
+    const int lp_new = append_ok ? p.positions[s] / kPageTokens : -1;
+    const int slot_new = append_ok ? p.positions[s] % kPageTokens : 0;
+    if constexpr (!TR::kI8) {
+        if (fused && hg == 0 && lp_new >= p0 && lp_new < p1 && warp == 0) {
+            const int phys = p.block_table[(size_t)s * p.max_pages + lp_new];
+            if (phys >= 0 && phys < p.num_pages) {
+                for (int v = lane; v < 2 * kRowVecs; v += 32) {
+                    const int kv = v / kRowVecs, e = v % kRowVecs;
+                    const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * kRowBytes;
+                    uint8_t *dst = const_cast<uint8_t *>(p.pool) +
+                                   ((((size_t)phys * 2 + kv) * p.hkv + kvh) * kPageTokens + slot_new) * kRowBytes;
+                    reinterpret_cast<uint4 *>(dst)[e] = reinterpret_cast<const uint4 *>(src)[e];
+                }
+            } else if (p.error_flag && lane == 0) {
+                atomicOr(p.error_flag, 2);
+            }
+        }
+    }
 
     const int n_my = (p1 - p0 - warp + kWarps - 1) / kWarps;  // pages of this warp
     const int32_t *bt = p.block_table + (size_t)s * p.max_pages;
@@ -239,6 +269,18 @@ paged_decode_kernel(const DecodeParams p) {
         const int phys = bt[lp];
         if (phys >= 0 && phys < p.num_pages) {
             const uint8_t *kbuf = wbuf + st * kStage;
+            if constexpr (!TR::kI8) {
+                if (lp == lp_new) {  // fused append: patch the new row into smem
+                    uint8_t *kb = wbuf + st * kStage;
+                    for (int v = lane; v < 2 * kRowVecs; v += 32) {
+                        const int kv = v / kRowVecs, e = v % kRowVecs;
+                        const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * kRowBytes;
+                        reinterpret_cast<uint4 *>(kb + kv * kBlk + slot_new * kRowBytes)[e] =
+                            reinterpret_cast<const uint4 *>(src)[e];
+                    }
+                    __syncwarp();
+                }
+            }
             const KVT *Vs = reinterpret_cast<const KVT *>(kbuf + kBlk);
             float kscale = 1.f, kzp = 0.f, vscale = 1.f, vzp = 0.f;
             if constexpr (TR::kI8) {
@@ -372,7 +414,13 @@ paged_decode_kernel(const DecodeParams p) {
         if (lane == 0) s_fail = 1;
     }
     __syncthreads();
-    if (s_fail) return;
+    if (s_fail) {
+        if (nsplit > 1 && threadIdx.x == 0) {
+            int *ctr = p.counters + ((size_t)s * p.hkv + kvh) * p.nhg + hg;
+            if (atomicAdd(ctr, 1) == nsplit - 1) atomicExch(ctr, 0);
+        }
+        return;
+    }
 
     // ---- merge the warps of the CTA ----
 #pragma unroll
@@ -420,41 +468,38 @@ paged_decode_kernel(const DecodeParams p) {
             }
         }
     }
-}
-
-// Fold the split partials of sequences with more than one split; write zero
-// rows for empty sequences.  One warp per (sequence, q-head).
-template <typename QT>
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x * 4 + warp;
-    const int s = blockIdx.y;
-    if (h >= p.hq) return;
-    const int T = p.seq_lens[s];
-    const int npages = (T + kPageTokens - 1) / kPageTokens;
-    const int nsplit = (npages + p.chunk - 1) / p.chunk;
-    QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
     if (nsplit == 1) return;
-    if (nsplit == 0) {
-        for (int d = lane; d < kHeadDim; d += 32) io_traits<QT>::store(o + d, 0.f);
-        return;
+
+    // ---- split combine by the last CTA of this (sequence, kv-head, head-group)
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();  // release this CTA's partials (ordered after the barrier)
+        int *ctr = p.counters + ((size_t)s * p.hkv + kvh) * p.nhg + hg;
+        const int ticket = atomicAdd(ctr, 1);
+        s_last = ticket == nsplit - 1;
+        if (s_last) {
+            atomicExch(ctr, 0);  // every split has arrived: reset for the next launch
+            __threadfence();     // acquire the other splits' partials
+        }
     }
-    const size_t base = ((size_t)s * p.hq + h) * p.max_splits;
-    float M = -CUDART_INF_F;
-    for (int c = lane; c < nsplit; c += 32) M = fmaxf(M, p.part_ml[(base + c) * 2]);
-#pragma unroll
-    for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < nsplit; ++c) {
-        const float mc = p.part_ml[(base + c) * 2];
-        const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
-        L += w * p.part_ml[(base + c) * 2 + 1];
-        const float4 v = *reinterpret_cast<const float4 *>(p.part_o + (base + c) * kHeadDim + 4 * lane);
-        O[0] += w * v.x; O[1] += w * v.y; O[2] += w * v.z; O[3] += w * v.w;
+    __syncthreads();
+    if (!s_last) return;
+    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kThreads) {
+        const int g = idx / kHeadDim, d = idx % kHeadDim;
+        const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
+        float M = -CUDART_INF_F;
+        for (int c = 0; c < nsplit; ++c) M = fmaxf(M, __ldcg(p.part_ml + (base + c) * 2));
+        float O = 0.f, L = 0.f;
+        for (int c = 0; c < nsplit; ++c) {
+            const float mc = __ldcg(p.part_ml + (base + c) * 2);
+            const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
+            L += w * __ldcg(p.part_ml + (base + c) * 2 + 1);
+            O += w * __ldcg(p.part_o + (base + c) * kHeadDim + d);
+        }
+        QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim;
+        io_traits<QT>::store(o + d, O / L);
     }
-    const float inv = 1.f / L;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) io_traits<QT>::store(o + 4 * lane + j, O[j] * inv);
 }
 
 constexpr int kMinChunk = 4;
@@ -497,11 +542,6 @@ int launch(DecodeParams &p, int batch, cudaStream_t st) {
     }
     dim3 grid(p.nhg * p.max_splits, p.hkv, batch);
     kern<<<grid, kThreads, smem, st>>>(p);
-    int rc = launch_status();
-    if (rc) return rc;
-    // the combine pass also writes the zero rows of empty sequences
-    dim3 cg((p.hq + 3) / 4, batch);
-    combine_kernel<QT><<<cg, 128, 0, st>>>(p);
     return launch_status();
 }
 
@@ -528,34 +568,33 @@ int dispatch_kv(DecodeParams &p, int dtype, int batch, cudaStream_t st, int G) {
 
 size_t max_splits_for(int max_pages) { return (size_t)(max_pages + kMinChunk - 1) / kMinChunk; }
 
-}  // namespace
-}  // namespace kvx
-
-using namespace kvx;
-
-extern "C" KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads,
-                                                     int32_t max_pages, int32_t page_tokens) {
-    if (batch <= 0 || num_q_heads <= 0 || max_pages <= 0 || page_tokens != kPageTokens) return 0;
+size_t workspace_bytes(int batch, int hq, int max_pages) {
     const size_t splits = max_splits_for(max_pages);
-    return (size_t)batch * num_q_heads * splits * (kHeadDim + 2) * sizeof(float);
+    size_t b = (size_t)batch * hq * splits * (kHeadDim + 2) * sizeof(float);
+    b += (size_t)batch * hq * sizeof(int32_t);  // split arrival counters
+    return (b + 15) / 16 * 16;
 }
 
-extern "C" KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
-                                  const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
-                                  const void *q, void *out, int32_t io_dtype, float sm_scale,
-                                  void *workspace, size_t workspace_bytes, int32_t *error_flag,
-                                  void *stream) {
-    if (!kv || !kv->pool || !block_table || !seq_lens || !q || !out) return KVX_EINVAL;
+int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+               const int32_t *seq_lens, const int32_t *positions, const void *new_k,
+               const void *new_v, int32_t batch, int32_t num_q_heads, const void *q, void *out,
+               int32_t io_dtype, float sm_scale, void *workspace, size_t workspace_bytes_,
+               int32_t *error_flag, void *stream) {
+    if (!kv || !kv->pool || !block_table || !q || !out) return KVX_EINVAL;
+    if (!seq_lens && !positions) return KVX_EINVAL;
     if (batch <= 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || num_q_heads <= 0) return KVX_EINVAL;
     if (num_q_heads % kv->num_kv_heads != 0) return KVX_EINVAL;
     if (kv->head_dim != kHeadDim || kv->page_tokens != kPageTokens) return KVX_EUNSUPPORTED;
     if (kv->dtype == KVX_I8 && !kv->stats) return KVX_EINVAL;
+    if (positions && kv->dtype == KVX_I8) return KVX_EUNSUPPORTED;
+    if (positions && (!new_k || !new_v)) return KVX_EINVAL;
     if (io_dtype != KVX_F32 && io_dtype != KVX_F16) return KVX_EINVAL;
     if ((reinterpret_cast<uintptr_t>(kv->pool) & 15) ||
-        (kv->stats && (reinterpret_cast<uintptr_t>(kv->stats) & 15)))
+        (kv->stats && (reinterpret_cast<uintptr_t>(kv->stats) & 15)) ||
+        (reinterpret_cast<uintptr_t>(new_k) & 15) || (reinterpret_cast<uintptr_t>(new_v) & 15))
         return KVX_EINVAL;
-    const size_t need = kvx_decode_workspace_bytes(batch, num_q_heads, max_pages, kv->page_tokens);
-    if (!workspace || workspace_bytes < need) return KVX_ENOSPC;
+    const size_t need = workspace_bytes(batch, num_q_heads, max_pages);
+    if (!workspace || workspace_bytes_ < need) return KVX_ENOSPC;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return KVX_EINVAL;
 
     DecodeParams p{};
@@ -563,6 +602,9 @@ extern "C" KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_tabl
     p.stats = kv->stats;
     p.block_table = block_table;
     p.seq_lens = seq_lens;
+    p.positions = positions;
+    p.new_k = static_cast<const uint8_t *>(new_k);
+    p.new_v = static_cast<const uint8_t *>(new_v);
     p.q = q;
     p.out = out;
     p.error_flag = error_flag;
@@ -572,17 +614,73 @@ extern "C" KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_tabl
     p.max_pages = max_pages;
     p.group = num_q_heads / kv->num_kv_heads;
     if (p.group > 4 * kMaxHeadsPerCta) return KVX_EUNSUPPORTED;
-    p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+    // fp16 pools take the tensor-core kernel (all q-heads of a kv-head in
+    // one CTA); fp32 / int8 pools the SIMT kernel (head groups of <= 4).
+    const char *force_simt = getenv("KVX_DECODE_SIMT");
+    const bool tc = kv->dtype == KVX_F16 && p.group <= 16 && !(force_simt && force_simt[0] == '1');
+    p.nhg = tc ? 1 : (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
     const int G = (p.group + p.nhg - 1) / p.nhg;
     p.chunk = choose_chunk(batch, p.hkv, p.nhg, max_pages);
     p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
     const size_t splits_cap = max_splits_for(max_pages);
     p.part_o = static_cast<float *>(workspace);
     p.part_ml = p.part_o + (size_t)batch * num_q_heads * splits_cap * kHeadDim;
-    // the partial arrays are indexed with max_splits (<= splits_cap) as stride
+    p.counters = reinterpret_cast<int32_t *>(p.part_ml + (size_t)batch * num_q_heads * splits_cap * 2);
     const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)kHeadDim);
     p.scale_log2 = scale * 1.4426950408889634f;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (tc) {
+        const int rc = launch_decode_tc(p, io_dtype, batch, st);
+        if (rc != KVX_EUNSUPPORTED) return rc;
+        p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;  // no tensor map: SIMT kernel
+        p.chunk = choose_chunk(batch, p.hkv, p.nhg, max_pages);
+        p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
+        return io_dtype == KVX_F32 ? dispatch_kv<float>(p, kv->dtype, batch, st, (p.group + p.nhg - 1) / p.nhg)
+                                   : dispatch_kv<__half>(p, kv->dtype, batch, st, (p.group + p.nhg - 1) / p.nhg);
+    }
     return io_dtype == KVX_F32 ? dispatch_kv<float>(p, kv->dtype, batch, st, G)
                                : dispatch_kv<__half>(p, kv->dtype, batch, st, G);
+}
+
+}  // namespace
+}  // namespace kvx
+
+using namespace kvx;
+
+extern "C" KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads,
+                                                     int32_t max_pages, int32_t page_tokens) {
+    if (batch <= 0 || num_q_heads <= 0 || max_pages <= 0 || page_tokens != kPageTokens) return 0;
+    return workspace_bytes(batch, num_q_heads, max_pages);
+}
+
+extern "C" KVX_API int kvx_decode_workspace_init(void *workspace, size_t workspace_bytes_,
+                                                 void *stream) {
+    if (!workspace) return KVX_EINVAL;
+    return cudaMemsetAsync(workspace, 0, workspace_bytes_, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? KVX_OK
+               : KVX_ECUDA;
+}
+
+extern "C" KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                                  const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                                  const void *q, void *out, int32_t io_dtype, float sm_scale,
+                                  void *workspace, size_t workspace_bytes_, int32_t *error_flag,
+                                  void *stream) {
+    if (!seq_lens) return KVX_EINVAL;
+    return run_decode(kv, block_table, max_pages, seq_lens, nullptr, nullptr, nullptr, batch,
+                      num_q_heads, q, out, io_dtype, sm_scale, workspace, workspace_bytes_,
+                      error_flag, stream);
+}
+
+extern "C" KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *block_table,
+                                         int32_t max_pages, const int32_t *positions, int32_t batch,
+                                         const void *new_k, const void *new_v, int32_t num_q_heads,
+                                         const void *q, void *out, int32_t io_dtype, float sm_scale,
+                                         void *workspace, size_t workspace_bytes_,
+                                         int32_t *error_flag, void *stream) {
+    if (!positions) return KVX_EINVAL;
+    return run_decode(kv, block_table, max_pages, nullptr, positions, new_k, new_v, batch,
+                      num_q_heads, q, out, io_dtype, sm_scale, workspace, workspace_bytes_,
+                      error_flag, stream);
 }

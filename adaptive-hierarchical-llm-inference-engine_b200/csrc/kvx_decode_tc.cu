@@ -1,0 +1,499 @@
+// kvx_decode_tc.cu -- tensor-core paged GQA decode for fp16 pools (sm_100a).
+//
+// Same contract and CTA decomposition as the SIMT kernel in kvx_decode.cu
+// (grid = split x kv-head x sequence, 4 warps per CTA, pages round-robin
+// over warps, flash-decoding partials folded by the last CTA), with the math
+// moved to the tensor cores so the kernel is bound by HBM, not by issue:
+//
+//  * staging: per (page, head) the K and V blocks (16 tokens x 128 dims) are
+//    fetched as four 2 KiB TMA tensor tiles (cp.async.bulk.tensor.2d, box
+//    64 dims x 16 tokens, 128-byte swizzle) into a per-warp 2-stage ring,
+//    completing on an mbarrier (bounded wait).  The swizzle makes every
+//    ldmatrix below bank-conflict free although page rows are 256 B apart.
+//  * S = Q K^T: mma.sync m16n8k16 (fp16 in, fp32 accumulate) with the GQA
+//    group as M (q-heads, padded to 16), tokens as N (two n-tiles per page)
+//    and head_dim as K (8 k-steps).  Q lives in registers as A fragments.
+//  * online softmax on the S fragments in the log2 domain (fp32).
+//  * O += P V: the S accumulators, rounded to fp16, are the A fragments of
+//    the next mma (no shared-memory round trip); V is read with
+//    ldmatrix.trans; O is 16 n-tiles of fp32 accumulators per warp.
+//
+// Instruction count per (page, head): 8 + 8 ldmatrix.x4, 32 mma, ~40 for
+// softmax and rescale -- against ~1100 for the SIMT kernel.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include <mutex>
+
+#include "kvx_decode_params.cuh"
+
+namespace kvx {
+namespace {
+
+constexpr int kTcWarps = 4;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kTcStages = 2;
+constexpr int kBox = 2048;          // 16 tokens x 64 dims x fp16, 128B-swizzled
+constexpr int kTcStage = 4 * kBox;  // K dims 0-63 | K dims 64-127 | V 0-63 | V 64-127
+constexpr int kTcSmem = 1024 /* alignment slack */ + kTcWarps * kTcStages * kTcStage +
+                        kTcWarps * kTcStages * 8 + 2 * kTcWarps * 16 * 4 + 16;
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int x, int y,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                          uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Same mma when only rows 0-7 of the tile matter (GQA group <= 8): the
+// accumulator rows 8-15 enter as zero and their results are discarded, so
+// they occupy no long-lived registers.
+__device__ __forceinline__ void mma16816_lo(float &c0, float &c1, const uint32_t (&a)[4], uint32_t b0,
+                                            uint32_t b1) {
+    float d2, d3;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%11,%12,%12};"
+        : "=f"(c0), "=f"(c1), "=f"(d2), "=f"(d3)
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f));
+    (void)d2;
+    (void)d3;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of `row` inside a 128B-swizzled
+// box whose rows are 128 bytes: the TMA unit XORs the chunk index with the
+// row index modulo 8.
+__device__ __forceinline__ uint32_t swz(int row, int c) {
+    return (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4));
+}
+
+template <typename QT, bool kBig>
+__global__ void __launch_bounds__(kTcThreads, 3)
+tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates
+    const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
+    const bool fused = p.positions != nullptr;
+    int T = fused ? p.positions[s] + 1 : max(p.seq_lens[s], 0);
+    if (fused && T <= 0) T = 0;
+    if (T > p.max_pages * kPageTokens) {
+        if (p.error_flag && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+            atomicOr(p.error_flag, 4);
+        T = p.max_pages * kPageTokens;
+    }
+    const int npages = (T + kPageTokens - 1) / kPageTokens;
+    const int p0 = split * p.chunk;
+    const int h0 = kvh * p.group;
+    const int nh = p.group;
+    if (p0 >= npages) {
+        if (npages == 0 && split == 0) {
+            QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0) * kHeadDim;
+            for (int i = threadIdx.x; i < nh * kHeadDim; i += kTcThreads) io_traits<QT>::store(o + i, 0.f);
+        }
+        return;
+    }
+    const int p1 = min(p0 + p.chunk, npages);
+    const int nsplit = (npages + p.chunk - 1) / p.chunk;
+
+    uint8_t *wbuf = smem + warp * kTcStages * kTcStage;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcWarps * kTcStages * kTcStage) + warp * kTcStages;
+    float *s_m = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8);
+    float *s_l = s_m + kTcWarps * 16;
+    int *s_flag = reinterpret_cast<int *>(s_l + kTcWarps * 16);
+
+    if (lane == 0) {
+        for (int i = 0; i < kTcStages; ++i) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    // fused append: one CTA writes the new token's rows into the pool
+    const bool append_ok = fused && p.positions[s] >= 0 && p.positions[s] < p.max_pages * kPageTokens;
+    const int lp_new = append_ok ? p.positions[s] / kPageTokens : -1;
+    const int slot_new = append_ok ? p.positions[s] % kPageTokens : 0;
+    if (append_ok && lp_new >= p0 && lp_new < p1 && warp == 0) {
+        const int phys = p.block_table[(size_t)s * p.max_pages + lp_new];
+        if (phys >= 0 && phys < p.num_pages) {
+            const int kv = lane >> 4, e = lane & 15;  // 2 rows x 16 vectors of 16 B
+            const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;
+            uint8_t *dst = const_cast<uint8_t *>(p.pool) +
+                           ((((size_t)phys * 2 + kv) * p.hkv + kvh) * kPageTokens + slot_new) * 256;
+            reinterpret_cast<uint4 *>(dst)[e] = reinterpret_cast<const uint4 *>(src)[e];
+        } else if (p.error_flag && lane == 0) {
+            atomicOr(p.error_flag, 2);
+        }
+    }
+
+    const int n_my = (p1 - p0 - warp + kTcWarps - 1) / kTcWarps;
+    const int32_t *bt = p.block_table + (size_t)s * p.max_pages;
+    const uint32_t wbase = smem_addr(wbuf);
+
+    auto issue = [&](int i, int st) {
+        const int lp = p0 + warp + kTcWarps * i;
+        const int phys = bt[lp];
+        uint64_t *bar = &bars[st];
+        if (phys < 0 || phys >= p.num_pages) {
+            if (p.error_flag) atomicOr(p.error_flag, 2);
+            mbar_arrive_expect_tx(bar, 0);
+            return;
+        }
+        const int yk = (((phys * 2) * p.hkv) + kvh) * kPageTokens;
+        const int yv = yk + p.hkv * kPageTokens;
+        const uint32_t dst = wbase + st * kTcStage;
+        const uint32_t b = smem_addr(bar);
+        mbar_arrive_expect_tx(bar, kTcStage);
+        tma_load_2d(dst, &tm, 0, yk, b);
+        tma_load_2d(dst + kBox, &tm, 64, yk, b);
+        tma_load_2d(dst + 2 * kBox, &tm, 0, yv, b);
+        tma_load_2d(dst + 3 * kBox, &tm, 64, yv, b);
+    };
+    if (lane == 0)
+        for (int i = 0; i < min(kTcStages, n_my); ++i) issue(i, i);
+
+    // Q as m16n8k16 A fragments: rows = q-heads of this kv-head (zero padded),
+    // k = head_dim in 8 steps of 16.
+    uint32_t qa[8][4];
+    {
+        const QT *qb = reinterpret_cast<const QT *>(p.q) + ((size_t)s * p.hq + h0) * kHeadDim;
+        const bool r0 = gq < nh, r1 = kBig && gq + 8 < nh;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const int c0 = 16 * kk + 2 * tq;
+            auto ld = [&](bool ok, int row, int col) -> float {
+                return ok ? io_traits<QT>::load(qb + row * kHeadDim + col) : 0.f;
+            };
+            qa[kk][0] = pack_h2(ld(r0, gq, c0), ld(r0, gq, c0 + 1));
+            qa[kk][1] = pack_h2(ld(r1, gq + 8, c0), ld(r1, gq + 8, c0 + 1));
+            qa[kk][2] = pack_h2(ld(r0, gq, c0 + 8), ld(r0, gq, c0 + 9));
+            qa[kk][3] = pack_h2(ld(r1, gq + 8, c0 + 8), ld(r1, gq + 8, c0 + 9));
+        }
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+
+    // per-lane ldmatrix row coordinates
+    const int lrow = lane & 7, lmat = lane >> 3;
+
+    bool ok = true;
+    int done = 0;
+    for (int i = 0; i < n_my; ++i) {
+        const int st = i % kTcStages;
+        const uint32_t par = (i / kTcStages) & 1;
+        if (!mbar_wait_bounded(&bars[st], par, p.error_flag)) {
+            ok = false;
+            break;
+        }
+        done = i + 1;
+        const int lp = p0 + warp + kTcWarps * i;
+        const int phys = bt[lp];
+        const uint32_t sbase = wbase + st * kTcStage;
+        if (phys >= 0 && phys < p.num_pages) {
+            if (lp == lp_new) {  // fused append: patch the new rows into the staged tiles
+                const int kv = lane >> 4, c = lane & 15;
+                const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;
+                uint8_t *tile = wbuf + st * kTcStage + kv * 2 * kBox + (c >> 3) * kBox;
+                *reinterpret_cast<uint4 *>(tile + swz(slot_new, c & 7)) =
+                    reinterpret_cast<const uint4 *>(src)[c];
+                __syncwarp();
+            }
+            // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
+            float sc[2][4];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+                for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = chunks 4kp..4kp+3
+                    const int chunk = 4 * kp + lmat;
+                    const uint32_t addr = sbase + (chunk >> 3) * kBox + swz(8 * j + lrow, chunk & 7);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(addr, b0, b1, b2, b3);
+                    if constexpr (kBig) {
+                        mma16816(sc[j], qa[2 * kp], b0, b1);
+                        mma16816(sc[j], qa[2 * kp + 1], b2, b3);
+                    } else {
+                        mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp], b0, b1);
+                        mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp + 1], b2, b3);
+                    }
+                }
+            }
+            // ---- online softmax (log2 domain)
+            const int tok = lp * kPageTokens + 2 * tq;
+            float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const bool valid = tok + 8 * j + e < T;
+                    sc[j][e] = valid ? sc[j][e] * p.scale_log2 : -CUDART_INF_F;
+                    mx0 = fmaxf(mx0, sc[j][e]);
+                    if constexpr (kBig) {
+                        sc[j][2 + e] = valid ? sc[j][2 + e] * p.scale_log2 : -CUDART_INF_F;
+                        mx1 = fmaxf(mx1, sc[j][2 + e]);
+                    }
+                }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            const float mn0 = fmaxf(m0, mx0);
+            const float a0 = exp2f(m0 - mn0);
+            m0 = mn0;
+            float a1 = 1.f;
+            if constexpr (kBig) {
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+                const float mn1 = fmaxf(m1, mx1);
+                a1 = exp2f(m1 - mn1);
+                m1 = mn1;
+            }
+            float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    sc[j][e] = exp2f(sc[j][e] - m0);
+                    ps0 += sc[j][e];
+                    if constexpr (kBig) {
+                        sc[j][2 + e] = exp2f(sc[j][2 + e] - m1);
+                        ps1 += sc[j][2 + e];
+                    }
+                }
+            l0 = l0 * a0 + ps0;
+            if constexpr (kBig) l1 = l1 * a1 + ps1;
+            uint32_t pa[4];
+            pa[0] = pack_h2(sc[0][0], sc[0][1]);
+            pa[2] = pack_h2(sc[1][0], sc[1][1]);
+            if constexpr (kBig) {
+                pa[1] = pack_h2(sc[0][2], sc[0][3]);
+                pa[3] = pack_h2(sc[1][2], sc[1][3]);
+            } else {
+                pa[1] = pa[3] = 0u;
+            }
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+                o[n][0] *= a0;
+                o[n][1] *= a0;
+                if constexpr (kBig) {
+                    o[n][2] *= a1;
+                    o[n][3] *= a1;
+                }
+            }
+            // ---- O += P V
+#pragma unroll
+            for (int np = 0; np < 8; ++np) {
+                const int chunk = 2 * np + (lmat >> 1);
+                const int vrow = (lmat & 1) * 8 + lrow;
+                const uint32_t addr = sbase + 2 * kBox + (chunk >> 3) * kBox + swz(vrow, chunk & 7);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(addr, b0, b1, b2, b3);
+                if constexpr (kBig) {
+                    mma16816(o[2 * np], pa, b0, b1);
+                    mma16816(o[2 * np + 1], pa, b2, b3);
+                } else {
+                    mma16816_lo(o[2 * np][0], o[2 * np][1], pa, b0, b1);
+                    mma16816_lo(o[2 * np + 1][0], o[2 * np + 1][1], pa, b2, b3);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + kTcStages < n_my) {
+            fence_proxy_async_smem();
+            issue(i + kTcStages, st);
+        }
+    }
+
+    if (threadIdx.x == 0) s_flag[0] = 0;
+    __syncthreads();
+    if (!ok) {
+        for (int i = done; i < min(done + kTcStages, n_my); ++i)
+            (void)mbar_wait_bounded(&bars[i % kTcStages], (i / kTcStages) & 1, nullptr);
+        if (lane == 0) s_flag[0] = 1;
+    }
+    __syncthreads();
+    if (s_flag[0]) {
+        if (nsplit > 1 && threadIdx.x == 0) {
+            int *ctr = p.counters + (size_t)s * p.hkv + kvh;
+            if (atomicAdd(ctr, 1) == nsplit - 1) atomicExch(ctr, 0);
+        }
+        return;
+    }
+
+    // ---- merge the 4 warps: each parks O (fp32 [16 rows][128]) in its stage 0
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    if constexpr (kBig) {
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    }
+    float *wacc = reinterpret_cast<float *>(wbuf);
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        *reinterpret_cast<float2 *>(wacc + gq * kHeadDim + 8 * n + 2 * tq) = make_float2(o[n][0], o[n][1]);
+        if constexpr (kBig)
+            *reinterpret_cast<float2 *>(wacc + (gq + 8) * kHeadDim + 8 * n + 2 * tq) =
+                make_float2(o[n][2], o[n][3]);
+    }
+    if (tq == 0) {
+        s_m[warp * 16 + gq] = m0;
+        s_l[warp * 16 + gq] = l0;
+        s_m[warp * 16 + gq + 8] = kBig ? m1 : -CUDART_INF_F;
+        s_l[warp * 16 + gq + 8] = kBig ? l1 : 0.f;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kTcThreads) {
+        const int g = idx / kHeadDim, d = idx % kHeadDim;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, s_m[w * 16 + g]);
+        float O = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) {
+            const float mw = s_m[w * 16 + g];
+            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
+            O += sw * reinterpret_cast<const float *>(smem + w * kTcStages * kTcStage)[g * kHeadDim + d];
+            L += sw * s_l[w * 16 + g];
+        }
+        const int h = h0 + g;
+        if (nsplit == 1) {
+            QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
+            io_traits<QT>::store(out + d, O / L);
+        } else {
+            const size_t pi = ((size_t)s * p.hq + h) * p.max_splits + split;
+            p.part_o[pi * kHeadDim + d] = O;
+            if (d == 0) {
+                p.part_ml[pi * 2] = M;
+                p.part_ml[pi * 2 + 1] = L;
+            }
+        }
+    }
+    if (nsplit == 1) return;
+
+    // ---- last CTA of (sequence, kv-head) folds the splits
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();  // release this CTA's partials (ordered after the barrier)
+        int *ctr = p.counters + (size_t)s * p.hkv + kvh;
+        const int ticket = atomicAdd(ctr, 1);
+        const int last = ticket == nsplit - 1;
+        if (last) {
+            atomicExch(ctr, 0);
+            __threadfence();  // acquire the other splits' partials
+        }
+        s_flag[1] = last;
+    }
+    __syncthreads();
+    if (!s_flag[1]) return;
+    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kTcThreads) {
+        const int g = idx / kHeadDim, d = idx % kHeadDim;
+        const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
+        float M = -CUDART_INF_F;
+        for (int c = 0; c < nsplit; ++c) M = fmaxf(M, __ldcg(p.part_ml + (base + c) * 2));
+        float O = 0.f, L = 0.f;
+        for (int c = 0; c < nsplit; ++c) {
+            const float mc = __ldcg(p.part_ml + (base + c) * 2);
+            const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
+            L += w * __ldcg(p.part_ml + (base + c) * 2 + 1);
+            O += w * __ldcg(p.part_o + (base + c) * kHeadDim + d);
+        }
+        QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim;
+        io_traits<QT>::store(out + d, O / L);
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// 2D view of the pool: rows of 128 fp16 (one token of one (page, K|V, head)
+// block), box = 64 dims x 16 tokens, 128-byte swizzle.
+bool make_pool_map(CUtensorMap *tm, const void *pool, long long rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || rows <= 0 || rows > (1ll << 31)) return false;
+    cuuint64_t gdim[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)kHeadDim * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)kPageTokens};
+    cuuint32_t estride[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(pool), gdim, gstride, box,
+              estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename QT, bool kBig>
+int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorMap &tm) {
+    auto kern = tc_decode_kernel<QT, kBig>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+            return KVX_ECUDA;
+        attr_set = true;
+    }
+    dim3 grid(p.max_splits, p.hkv, batch);
+    kern<<<grid, kTcThreads, kTcSmem, st>>>(p, tm);
+    return launch_status();
+}
+
+}  // namespace
+
+int launch_decode_tc(DecodeParams &p, int io_dtype, int batch, cudaStream_t st) {
+    if (p.group > 16) return KVX_EUNSUPPORTED;
+    CUtensorMap tm;
+    const long long rows = (long long)p.num_pages * 2 * p.hkv * kPageTokens;
+    if (!make_pool_map(&tm, p.pool, rows)) return KVX_EUNSUPPORTED;
+    const bool big = p.group > 8;
+    if (io_dtype == KVX_F32)
+        return big ? launch_tc<float, true>(p, batch, st, tm) : launch_tc<float, false>(p, batch, st, tm);
+    return big ? launch_tc<__half, true>(p, batch, st, tm) : launch_tc<__half, false>(p, batch, st, tm);
+}
+
+}  // namespace kvx

@@ -31,6 +31,17 @@ __device__ __forceinline__ int32_t cvt_trunc_i32_x86(float r) {
     return (int32_t)r;
 }
 
+// x86 SSE NaN rules for a binary op r = a op b: a NaN operand is returned
+// quieted (the first one if both are NaN); an invalid operation on non-NaN
+// operands (0*inf, inf-inf, 0/0) returns the default NaN 0xFFC00000.  The
+// GPU returns the canonical 0x7FFFFFFF instead, so NaN results are rebuilt.
+__device__ __forceinline__ float x86_nan(float r, float a, float b) {
+    if (r == r) return r;
+    if (a != a) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (b != b) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xFFC00000u);
+}
+
 __device__ __forceinline__ int8_t quant_one(float x, float mn, float scale) {
     const float normalized = __fdiv_rn(__fsub_rn(x, mn), scale);
     int32_t q = cvt_trunc_i32_x86(roundf(normalized));
@@ -66,7 +77,12 @@ __device__ __forceinline__ MinMax mm_warp_reduce(MinMax a) {
 
 template <typename T> __device__ __forceinline__ float ld_elem(const T *p, size_t i);
 template <> __device__ __forceinline__ float ld_elem<float>(const float *p, size_t i) { return p[i]; }
+// fp16 -> fp32 widening, exact; NaNs keep their payload with the quiet bit
+// set (as x86 F16C / gcc's _Float16 conversion does).
 template <> __device__ __forceinline__ float ld_elem<__half>(const __half *p, size_t i) {
+    const uint16_t h = __half_as_ushort(p[i]);
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu))
+        return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7FC00000u | ((uint32_t)(h & 0x3FFu) << 13));
     return __half2float(p[i]);
 }
 
@@ -78,7 +94,8 @@ __device__ __forceinline__ void finish_stats(MinMax r, float first, float *stats
         r.mx = first;
     }
     mn = r.mn;
-    float sc = __fdiv_rn(__fsub_rn(r.mx, r.mn), 255.0f);
+    const float range = x86_nan(__fsub_rn(r.mx, r.mn), r.mx, r.mn);
+    float sc = x86_nan(__fdiv_rn(range, 255.0f), range, 255.0f);
     if (sc == 0.0f) sc = 1.0f;
     scale = sc;
     if (lane == 0) *reinterpret_cast<float4 *>(stats) = make_float4(r.mn, r.mx, sc, r.mn);
@@ -166,7 +183,9 @@ compress_generic_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
 }
 
 __device__ __forceinline__ float dequant_one(int8_t c, float zp, float scale) {
-    return __fadd_rn(zp, __fmul_rn((float)((int32_t)c + 128), scale));
+    const float q = (float)((int32_t)c + 128);
+    const float m = x86_nan(__fmul_rn(q, scale), q, scale);
+    return x86_nan(__fadd_rn(zp, m), zp, m);
 }
 
 // One thread per 4 codes; block_elems % 4 == 0.

@@ -61,13 +61,16 @@ lib.kvx_decode_workspace_bytes.restype = _sz
 lib.kvx_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32]
 lib.kvx_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32, _f32,
                            _vp, _sz, _vp, _vp]
+lib.kvx_append_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
+                                  _vp, _i32, _f32, _vp, _sz, _vp, _vp]
+lib.kvx_decode_workspace_init.argtypes = [_vp, _sz, _vp]
 lib.kvx_compress_int8.argtypes = [_vp, _i32, _vp, _vp, _sz, _i32, _vp]
 lib.kvx_decompress_int8.argtypes = [_vp, _vp, _vp, _i32, _sz, _i32, _vp]
 lib.kvx_f32_to_f16_trunc.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_f16_trunc_to_f32.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_lru_select.argtypes = [_vp, _sz, _vp, _vp]
 lib.kvx_migrate_frames.argtypes = [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _sz, _i32, _i32, _vp, _vp]
-for _fn in ("kvx_append", "kvx_decode", "kvx_compress_int8", "kvx_decompress_int8",
+for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
             "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
             "kvx_migrate_frames"):
     getattr(lib, _fn).restype = C.c_int
@@ -119,6 +122,13 @@ def decode_workspace_bytes(batch, num_q_heads, max_pages):
     return lib.kvx_decode_workspace_bytes(batch, num_q_heads, max_pages, PAGE_TOKENS)
 
 
+def decode_workspace(batch, num_q_heads, max_pages, device="cuda"):
+    """A zero-filled decode workspace (the split counters start at zero)."""
+    torch = _torch()
+    return torch.zeros(max(decode_workspace_bytes(batch, num_q_heads, max_pages), 16),
+                       dtype=torch.uint8, device=device)
+
+
 def decode(pool, block_table, seq_lens, q, out=None, stats=None, workspace=None,
            error_flag=None, sm_scale=0.0, stream=None):
     """Paged GQA decode.  q: [batch][hq][128] fp32/fp16 CUDA tensor."""
@@ -127,14 +137,32 @@ def decode(pool, block_table, seq_lens, q, out=None, stats=None, workspace=None,
     batch, hq, _ = q.shape
     if out is None:
         out = torch.empty_like(q)
-    need = decode_workspace_bytes(batch, hq, block_table.shape[1])
     if workspace is None:
-        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+        workspace = decode_workspace(batch, hq, block_table.shape[1], q.device)
     rc = lib.kvx_decode(C.byref(kv), _ptr(block_table), block_table.shape[1], _ptr(seq_lens),
                         batch, hq, _ptr(q), _ptr(out), _dtype_code(q), sm_scale,
                         _ptr(workspace), workspace.numel() * workspace.element_size(),
                         _ptr(error_flag), _stream(stream))
     _check("kvx_decode", rc)
+    return out
+
+
+def append_decode(pool, block_table, positions, new_k, new_v, q, out=None, workspace=None,
+                  error_flag=None, sm_scale=0.0, stream=None):
+    """Append the token at `positions` and decode over positions+1 tokens, one launch."""
+    torch = _torch()
+    kv = paged(pool)
+    batch, hq, _ = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        workspace = decode_workspace(batch, hq, block_table.shape[1], q.device)
+    rc = lib.kvx_append_decode(C.byref(kv), _ptr(block_table), block_table.shape[1],
+                               _ptr(positions), batch, _ptr(new_k), _ptr(new_v), hq, _ptr(q),
+                               _ptr(out), _dtype_code(q), sm_scale, _ptr(workspace),
+                               workspace.numel() * workspace.element_size(), _ptr(error_flag),
+                               _stream(stream))
+    _check("kvx_append_decode", rc)
     return out
 
 

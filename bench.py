@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers per step (profiling of a smaller case; the metric is defined at 28)")
     return ap.parse_args()
 
 
@@ -145,21 +147,19 @@ def run_ours(args):
     out = torch.empty((LAYERS, BATCH, hq, DIM), device="cuda", dtype=torch.float16)
     gathered = torch.empty((LAYERS, world, BATCH, hq, DIM), device="cuda", dtype=torch.float16) \
         if world > 1 else None
-    ws_bytes = kvx.decode_workspace_bytes(BATCH, hq, max_pages)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = kvx.decode_workspace(BATCH, hq, max_pages)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     pos = torch.from_numpy(lens0.astype(np.int32)).cuda()
-    lens1 = pos + 1
     comm = torch.cuda.Stream() if world > 1 else None
     main = torch.cuda.current_stream()
     layer_done = [torch.cuda.Event() for _ in range(LAYERS)]
 
     def step(ev=None):
         for l in range(LAYERS):
-            kvx.append(pools[l], bt, pos, nk[l], nv[l], error_flag=err)
             if ev is not None:
                 ev[l][0].record()
-            kvx.decode(pools[l], bt, lens1, q[l], out=out[l], workspace=ws, error_flag=err)
+            kvx.append_decode(pools[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
+                              error_flag=err)
             if ev is not None:
                 ev[l][1].record()
             if world > 1:
@@ -168,7 +168,6 @@ def run_ours(args):
                     comm.wait_event(layer_done[l])
                     dist.all_gather_into_tensor(gathered[l], out[l])
         pos.add_(1)
-        lens1.add_(1)
         if world > 1:
             main.wait_stream(comm)
 
@@ -235,9 +234,9 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (KV pool ~17 GB)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_kind": peak_kind, "kernel": "paged_decode_kernel (+combine)",
+                     "peak_kind": peak_kind, "kernel": "paged_decode_kernel (append + decode + split combine fused)",
                      "mean_launch_us": round(mean_dec_ms * 1e3, 2)},
-        "gpu_launches": steps * LAYERS * 3,
+        "gpu_launches": steps * LAYERS,
         "clocks": clk,
     }
     if not args.no_e2e:
@@ -270,7 +269,6 @@ def run_e2e(args, pools, bt, lens0, start_step, hq, hkv, ws, err, world):
     # replay the positions of the last `steps` device-resident steps (the
     # pool has room for exactly warmup+steps appended tokens per sequence)
     pos = torch.from_numpy((lens0 + start_step - steps).astype(np.int32)).cuda()
-    lens1 = pos + 1
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     t0.record()
@@ -280,12 +278,11 @@ def run_e2e(args, pools, bt, lens0, start_step, hq, hkv, ws, err, world):
         d_k.copy_(h_k, non_blocking=True)
         d_v.copy_(h_v, non_blocking=True)
         for l in range(LAYERS):
-            kvx.append(pools[l], bt, pos, d_k[l], d_v[l], error_flag=err)
-            kvx.decode(pools[l], bt, lens1, d_q[l], out=d_o[l], workspace=ws, error_flag=err)
+            kvx.append_decode(pools[l], bt, pos, d_k[l], d_v[l], d_q[l], out=d_o[l], workspace=ws,
+                              error_flag=err)
         h_o.copy_(d_o, non_blocking=True)
         nbytes += int((lens0 + start_step - steps + k + 1).sum()) * 2 * hkv * DIM * 2 * LAYERS
         pos.add_(1)
-        lens1.add_(1)
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
@@ -387,7 +384,9 @@ def run_reference(args):
 
 
 def main():
+    global LAYERS
     args = parse()
+    LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:

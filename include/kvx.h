@@ -74,9 +74,13 @@ KVX_API int kvx_append(const kvx_paged *kv, const int32_t *block_table, int32_t 
                        const int32_t *positions, int32_t batch, const void *new_k,
                        const void *new_v, int32_t *error_flag, void *stream);
 
-/* Bytes of scratch kvx_decode needs (split-K partial results). */
+/* Bytes of scratch kvx_decode / kvx_append_decode need: split-K partial
+ * results plus one arrival counter per (sequence, q-head). */
 KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t max_pages,
                                           int32_t page_tokens);
+/* Zero-fill a decode workspace (cudaMemsetAsync).  Required once before its
+ * first use; every decode launch leaves the counters at zero again. */
+KVX_API int kvx_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream);
 
 /* Paged GQA decode attention.  Replaces the naive attention of
  * runtime/gpu/cuda_executor.cu:246-311 and native-engine/cuda/attention.cu:18-157
@@ -86,13 +90,28 @@ KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, in
  * through the block table.  sm_scale <= 0 means 1/sqrt(head_dim).
  * q/out: [batch][num_q_heads][head_dim] in io_dtype (KVX_F32 or KVX_F16).
  * seq_lens[s] == 0 gives a zero row.  error_flag (device int, may be NULL)
- * gets bit 0 set if a bounded wait for page data expired.  workspace:
- * kvx_decode_workspace_bytes() bytes of device memory, no initialisation. */
+ * gets bit 0 set if a bounded wait for page data expired, bit 1 for a page
+ * id outside the pool (that page is skipped) and bit 2 for a context longer
+ * than max_pages*page_tokens (clamped).  workspace:
+ * kvx_decode_workspace_bytes() bytes of device memory, zero-filled once by
+ * kvx_decode_workspace_init; launches that share a workspace must be
+ * ordered (same stream), as they share its counters. */
 KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
                        const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
                        const void *q, void *out, int32_t io_dtype, float sm_scale,
                        void *workspace, size_t workspace_bytes, int32_t *error_flag,
                        void *stream);
+
+/* Fused append + decode: kvx_append of the token at positions[s] followed by
+ * kvx_decode over seq_lens[s] = positions[s] + 1, in one launch.  Replaces
+ * the save_page-then-attention sequence of InferenceController::appendKVPage
+ * (runtime/inference.cpp:50-54) + TensorOps::attention
+ * (runtime/tensor_ops.cpp:179-219).  fp16 / fp32 pools only. */
+KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                              const int32_t *positions, int32_t batch, const void *new_k,
+                              const void *new_v, int32_t num_q_heads, const void *q, void *out,
+                              int32_t io_dtype, float sm_scale, void *workspace,
+                              size_t workspace_bytes, int32_t *error_flag, void *stream);
 
 /* Per-block int8 quantisation.  Replaces KVCompressionEngine::compressToINT8
  * (native-engine/cpp/KVCompressionEngine.cpp:83-113), one reference call per

@@ -24,7 +24,8 @@ def declared_symbols():
 
 def test_header_declares_entry_points():
     names = declared_symbols()
-    for n in ("kvx_append", "kvx_decode", "kvx_compress_int8", "kvx_decompress_int8",
+    for n in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init",
+              "kvx_compress_int8", "kvx_decompress_int8",
               "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
               "kvx_migrate_frames", "kvx_decode_workspace_bytes"):
         assert n in names
@@ -45,8 +46,10 @@ def test_version_and_status_strings():
 
 def test_workspace_size_formula():
     import kvx
-    # split-K partials: batch * hq * ceil(max_pages/4) * (128 + 2) floats
-    assert kvx.decode_workspace_bytes(32, 24, 544) == 32 * 24 * 136 * 130 * 4
+    # split-K partials: batch * hq * ceil(max_pages/4) * (128 + 2) floats,
+    # then one int32 arrival counter per (sequence, q-head), 16-byte padded
+    assert kvx.decode_workspace_bytes(32, 24, 544) == 32 * 24 * 136 * 130 * 4 + 32 * 24 * 4
+    assert kvx.decode_workspace_bytes(1, 3, 4) % 16 == 0
     assert kvx.decode_workspace_bytes(0, 24, 544) == 0
 
 

@@ -152,6 +152,66 @@ def test_decode_split_invariance(kvx, monkeypatch, chunk):
     assert np.abs(base - other).max() < 1e-4
 
 
+@pytest.mark.parametrize("np_dtype", [np.float16, np.float32])
+def test_append_decode_fused_matches_append_then_decode(kvx, oracle, np_dtype):
+    lens = kvgen.randint(41, 12, 0, 900)
+    lens[0], lens[1], lens[2] = 0, 15, 16  # first token, page end, page start
+    bt, num_pages = kvgen.paged_layout(lens, 16, 1, seed=42)
+    pool = kvgen.normal(43, (num_pages, 2, 8, 16, 128)).astype(np_dtype)
+    nk = kvgen.normal(44, (lens.size, 8, 128)).astype(np_dtype)
+    nv = kvgen.normal(45, (lens.size, 8, 128)).astype(np_dtype)
+    q = kvgen.normal(46, (lens.size, 24, 128))
+    pos = lens.astype(np.int32)
+    g_pool = dev(pool)
+    ws = kvx.decode_workspace(lens.size, 24, bt.shape[1])
+    for rep in range(2):  # second call reuses the workspace: counters must be back at zero
+        out = kvx.append_decode(g_pool, dev(bt), dev(pos), dev(nk), dev(nv), dev(q), workspace=ws)
+        torch.cuda.synchronize()
+    ref_pool = pool.copy()
+    oracle.append(ref_pool, bt, pos, nk, nv, 16)
+    assert np.array_equal(g_pool.cpu().numpy().view(np.uint8), ref_pool.view(np.uint8))
+    ref = oracle.paged_decode(ref_pool, bt, pos + 1, q)
+    assert_close(out.cpu().numpy(), ref)
+    assert int(ws[-lens.size * 24 * 4:].view(torch.int32).abs().sum().item()) == 0
+
+
+def test_compress_int8_fp16_nan_and_inf_blocks(kvx, oracle):
+    data = kvgen.normal(61, (6, 2048)).astype(np.float16)
+    bits = data.view(np.uint16)
+    bits[0, 0] = 0x7E00          # quiet NaN first
+    bits[1, 0] = 0x7C01          # signaling NaN first (payload kept, quieted)
+    bits[2, 100] = 0xFE00        # NaN later (ignored)
+    bits[3, 0] = 0x7C00          # +inf first
+    bits[4, 7] = 0xFC00          # -inf inside
+    bits[5, :] = 0x0000
+    bits[5, 3] = 0x8000          # -0 after +0: min/max keep the first zero
+    codes, stats = kvx.compress_int8(dev(data))
+    rc, rs = oracle.compress_int8_blocks(data, 2048)
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    dec = kvx.decompress_int8(codes, stats).cpu().numpy()
+    assert np.array_equal(dec.view(np.uint32), oracle.decompress_int8_blocks(rc, rs, 2048).view(np.uint32))
+
+
+@pytest.mark.parametrize("hkv,hq", [(8, 8), (8, 24), (2, 16), (1, 16), (4, 8)])
+def test_decode_tensor_core_path_matches_oracle(kvx, oracle, monkeypatch, hkv, hq):
+    """fp16 pools run on the tensor-core kernel (GQA group as the mma M
+    dimension, up to 16); the SIMT kernel must agree with it and both with
+    the oracle."""
+    lens = kvgen.randint(70 + hq, 6, 1, 1500)
+    lens[0] = 1
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=71)
+    pool = kvgen.normal(72, (num_pages, 2, hkv, 16, 128)).astype(np.float16)
+    q = kvgen.normal(73, (lens.size, hq, 128))
+    args = (dev(pool), dev(bt), dev(lens.astype(np.int32)), dev(q))
+    tc = kvx.decode(*args).cpu().numpy()
+    monkeypatch.setenv("KVX_DECODE_SIMT", "1")
+    simt = kvx.decode(*args).cpu().numpy()
+    ref = oracle.paged_decode(pool, bt, lens.astype(np.int32), q)
+    assert_close(tc, ref)
+    assert_close(simt, ref)
+
+
 def test_decode_gqa_grouping_matches_mha_expansion(kvx):
     """Property: GQA with group G equals MHA on a pool whose kv heads are
     repeated G times."""
