@@ -85,6 +85,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return false;
 }
 
+// Arrival ticket with release + acquire semantics at GPU scope: the
+// caller's (and, through a preceding warp/CTA barrier, its peers') prior
+// writes are visible to whoever later acquires this counter, and the
+// caller sees everything released to it before.  Cheaper than a
+// sequentially consistent fence (__threadfence).
+__device__ __forceinline__ int atomic_add_acq_rel(int *p, int v) {
+    int r;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(r) : "l"(p), "r"(v) : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
     __half2 h = *reinterpret_cast<__half2 *>(&v);
     return __half22float2(h);

@@ -34,6 +34,7 @@
 #include <cuda_fp16.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 
@@ -473,15 +474,11 @@ paged_decode_kernel(const DecodeParams p) {
     // ---- split combine by the last CTA of this (sequence, kv-head, head-group)
     __shared__ int s_last;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();  // release this CTA's partials (ordered after the barrier)
+    if (threadIdx.x == 0) {  // release this CTA's partials, acquire the others if last
         int *ctr = p.counters + ((size_t)s * p.hkv + kvh) * p.nhg + hg;
-        const int ticket = atomicAdd(ctr, 1);
+        const int ticket = atomic_add_acq_rel(ctr, 1);
         s_last = ticket == nsplit - 1;
-        if (s_last) {
-            atomicExch(ctr, 0);  // every split has arrived: reset for the next launch
-            __threadfence();     // acquire the other splits' partials
-        }
+        if (s_last) atomicExch(ctr, 0);  // every split has arrived: reset for the next launch
     }
     __syncthreads();
     if (!s_last) return;

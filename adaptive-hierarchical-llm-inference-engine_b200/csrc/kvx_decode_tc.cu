@@ -98,6 +98,112 @@ __device__ __forceinline__ uint32_t swz(int row, int c) {
     return (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4));
 }
 
+// One staged (page, head) tile pair: S = Q K^T (two n-tiles of 8 tokens),
+// online softmax in the log2 domain, O += P V.  `sbase` is the shared
+// address of the stage (K lo | K hi | V lo | V hi, 128B-swizzled); `tok`
+// the absolute index of token 2*tq of the page; tokens >= T are masked.
+template <bool kBig>
+__device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][4], float (&o)[16][4],
+                                        float &m0, float &m1, float &l0, float &l1, int tok, int T,
+                                        float scale_log2, int lane) {
+    const int tq = lane & 3, lrow = lane & 7, lmat = lane >> 3;
+    // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = chunks 4kp..4kp+3
+            const int chunk = 4 * kp + lmat;
+            const uint32_t addr = sbase + (chunk >> 3) * kBox + swz(8 * j + lrow, chunk & 7);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(addr, b0, b1, b2, b3);
+            if constexpr (kBig) {
+                mma16816(sc[j], qa[2 * kp], b0, b1);
+                mma16816(sc[j], qa[2 * kp + 1], b2, b3);
+            } else {
+                mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp], b0, b1);
+                mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp + 1], b2, b3);
+            }
+        }
+    }
+    // ---- online softmax (log2 domain)
+    float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const bool valid = tok + 8 * j + e < T;
+            sc[j][e] = valid ? sc[j][e] * scale_log2 : -CUDART_INF_F;
+            mx0 = fmaxf(mx0, sc[j][e]);
+            if constexpr (kBig) {
+                sc[j][2 + e] = valid ? sc[j][2 + e] * scale_log2 : -CUDART_INF_F;
+                mx1 = fmaxf(mx1, sc[j][2 + e]);
+            }
+        }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    const float mn0 = fmaxf(m0, mx0);
+    const float a0 = exp2f(m0 - mn0);
+    m0 = mn0;
+    float a1 = 1.f;
+    if constexpr (kBig) {
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn1 = fmaxf(m1, mx1);
+        a1 = exp2f(m1 - mn1);
+        m1 = mn1;
+    }
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            sc[j][e] = exp2f(sc[j][e] - m0);
+            ps0 += sc[j][e];
+            if constexpr (kBig) {
+                sc[j][2 + e] = exp2f(sc[j][2 + e] - m1);
+                ps1 += sc[j][2 + e];
+            }
+        }
+    l0 = l0 * a0 + ps0;
+    if constexpr (kBig) l1 = l1 * a1 + ps1;
+    uint32_t pa[4];
+    pa[0] = pack_h2(sc[0][0], sc[0][1]);
+    pa[2] = pack_h2(sc[1][0], sc[1][1]);
+    if constexpr (kBig) {
+        pa[1] = pack_h2(sc[0][2], sc[0][3]);
+        pa[3] = pack_h2(sc[1][2], sc[1][3]);
+    } else {
+        pa[1] = pa[3] = 0u;
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        o[n][0] *= a0;
+        o[n][1] *= a0;
+        if constexpr (kBig) {
+            o[n][2] *= a1;
+            o[n][3] *= a1;
+        }
+    }
+    // ---- O += P V
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+        const int chunk = 2 * np + (lmat >> 1);
+        const int vrow = (lmat & 1) * 8 + lrow;
+        const uint32_t addr = sbase + 2 * kBox + (chunk >> 3) * kBox + swz(vrow, chunk & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+        if constexpr (kBig) {
+            mma16816(o[2 * np], pa, b0, b1);
+            mma16816(o[2 * np + 1], pa, b2, b3);
+        } else {
+            mma16816_lo(o[2 * np][0], o[2 * np][1], pa, b0, b1);
+            mma16816_lo(o[2 * np + 1][0], o[2 * np + 1][1], pa, b2, b3);
+        }
+    }
+}
+
 template <typename QT, bool kBig>
 __global__ void __launch_bounds__(kTcThreads, 3)
 tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
@@ -208,9 +314,6 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
 
-    // per-lane ldmatrix row coordinates
-    const int lrow = lane & 7, lmat = lane >> 3;
-
     bool ok = true;
     int done = 0;
     for (int i = 0; i < n_my; ++i) {
@@ -233,102 +336,8 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
                     reinterpret_cast<const uint4 *>(src)[c];
                 __syncwarp();
             }
-            // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
-            float sc[2][4];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-#pragma unroll
-                for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = chunks 4kp..4kp+3
-                    const int chunk = 4 * kp + lmat;
-                    const uint32_t addr = sbase + (chunk >> 3) * kBox + swz(8 * j + lrow, chunk & 7);
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(addr, b0, b1, b2, b3);
-                    if constexpr (kBig) {
-                        mma16816(sc[j], qa[2 * kp], b0, b1);
-                        mma16816(sc[j], qa[2 * kp + 1], b2, b3);
-                    } else {
-                        mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp], b0, b1);
-                        mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp + 1], b2, b3);
-                    }
-                }
-            }
-            // ---- online softmax (log2 domain)
-            const int tok = lp * kPageTokens + 2 * tq;
-            float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const bool valid = tok + 8 * j + e < T;
-                    sc[j][e] = valid ? sc[j][e] * p.scale_log2 : -CUDART_INF_F;
-                    mx0 = fmaxf(mx0, sc[j][e]);
-                    if constexpr (kBig) {
-                        sc[j][2 + e] = valid ? sc[j][2 + e] * p.scale_log2 : -CUDART_INF_F;
-                        mx1 = fmaxf(mx1, sc[j][2 + e]);
-                    }
-                }
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-            const float mn0 = fmaxf(m0, mx0);
-            const float a0 = exp2f(m0 - mn0);
-            m0 = mn0;
-            float a1 = 1.f;
-            if constexpr (kBig) {
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-                const float mn1 = fmaxf(m1, mx1);
-                a1 = exp2f(m1 - mn1);
-                m1 = mn1;
-            }
-            float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    sc[j][e] = exp2f(sc[j][e] - m0);
-                    ps0 += sc[j][e];
-                    if constexpr (kBig) {
-                        sc[j][2 + e] = exp2f(sc[j][2 + e] - m1);
-                        ps1 += sc[j][2 + e];
-                    }
-                }
-            l0 = l0 * a0 + ps0;
-            if constexpr (kBig) l1 = l1 * a1 + ps1;
-            uint32_t pa[4];
-            pa[0] = pack_h2(sc[0][0], sc[0][1]);
-            pa[2] = pack_h2(sc[1][0], sc[1][1]);
-            if constexpr (kBig) {
-                pa[1] = pack_h2(sc[0][2], sc[0][3]);
-                pa[3] = pack_h2(sc[1][2], sc[1][3]);
-            } else {
-                pa[1] = pa[3] = 0u;
-            }
-#pragma unroll
-            for (int n = 0; n < 16; ++n) {
-                o[n][0] *= a0;
-                o[n][1] *= a0;
-                if constexpr (kBig) {
-                    o[n][2] *= a1;
-                    o[n][3] *= a1;
-                }
-            }
-            // ---- O += P V
-#pragma unroll
-            for (int np = 0; np < 8; ++np) {
-                const int chunk = 2 * np + (lmat >> 1);
-                const int vrow = (lmat & 1) * 8 + lrow;
-                const uint32_t addr = sbase + 2 * kBox + (chunk >> 3) * kBox + swz(vrow, chunk & 7);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(addr, b0, b1, b2, b3);
-                if constexpr (kBig) {
-                    mma16816(o[2 * np], pa, b0, b1);
-                    mma16816(o[2 * np + 1], pa, b2, b3);
-                } else {
-                    mma16816_lo(o[2 * np][0], o[2 * np][1], pa, b0, b1);
-                    mma16816_lo(o[2 * np + 1][0], o[2 * np + 1][1], pa, b2, b3);
-                }
-            }
+            tc_page<kBig>(sbase, qa, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
+                          p.scale_log2, lane);
         }
         __syncwarp();
         if (lane == 0 && i + kTcStages < n_my) {
@@ -405,15 +414,11 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
 
     // ---- last CTA of (sequence, kv-head) folds the splits
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();  // release this CTA's partials (ordered after the barrier)
+    if (threadIdx.x == 0) {  // release this CTA's partials, acquire the others if last
         int *ctr = p.counters + (size_t)s * p.hkv + kvh;
-        const int ticket = atomicAdd(ctr, 1);
+        const int ticket = atomic_add_acq_rel(ctr, 1);
         const int last = ticket == nsplit - 1;
-        if (last) {
-            atomicExch(ctr, 0);
-            __threadfence();  // acquire the other splits' partials
-        }
+        if (last) atomicExch(ctr, 0);
         s_flag[1] = last;
     }
     __syncthreads();

@@ -95,7 +95,8 @@ KVX_API int kvx_decode_workspace_init(void *workspace, size_t workspace_bytes, v
  * than max_pages*page_tokens (clamped).  workspace:
  * kvx_decode_workspace_bytes() bytes of device memory, zero-filled once by
  * kvx_decode_workspace_init; launches that share a workspace must be
- * ordered (same stream), as they share its counters. */
+ * ordered (same stream), as they share its counters.  After a launch that
+ * set bit 0 of error_flag, zero-fill the workspace again before reuse. */
 KVX_API int kvx_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
                        const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
                        const void *q, void *out, int32_t io_dtype, float sm_scale,

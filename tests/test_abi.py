@@ -46,9 +46,10 @@ def test_version_and_status_strings():
 
 def test_workspace_size_formula():
     import kvx
-    # split-K partials: batch * hq * ceil(max_pages/4) * (128 + 2) floats,
-    # then one int32 arrival counter per (sequence, q-head), 16-byte padded
-    assert kvx.decode_workspace_bytes(32, 24, 544) == 32 * 24 * 136 * 130 * 4 + 32 * 24 * 4
+    # partials: batch * hq * ceil(max_pages/4) rows of (128 + 2) floats, then
+    # one int32 arrival counter per (sequence, q-head), rounded up to 16 bytes
+    want = 32 * 24 * 136 * 130 * 4 + 32 * 24 * 4
+    assert kvx.decode_workspace_bytes(32, 24, 544) == (want + 15) // 16 * 16
     assert kvx.decode_workspace_bytes(1, 3, 4) % 16 == 0
     assert kvx.decode_workspace_bytes(0, 24, 544) == 0
 

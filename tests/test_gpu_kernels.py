@@ -152,6 +152,25 @@ def test_decode_split_invariance(kvx, monkeypatch, chunk):
     assert np.abs(base - other).max() < 1e-4
 
 
+def test_decode_many_ragged_sequences(kvx, oracle):
+    """Many short, empty and long sequences in one launch; the workspace is
+    reused, so the split counters must be back at zero after each launch."""
+    lens = kvgen.randint(81, 300, 0, 2000)
+    lens[::17] = 0
+    lens[5] = 16
+    lens[6] = 1
+    bt, num_pages = kvgen.paged_layout(np.maximum(lens, 1), 16, 0, seed=82)
+    pool = kvgen.normal(83, (num_pages, 2, 8, 16, 128)).astype(np.float16)
+    q = kvgen.normal(84, (lens.size, 24, 128))
+    ws = kvx.decode_workspace(lens.size, 24, bt.shape[1])
+    for _ in range(2):  # counters must come back to zero between launches
+        out = kvx.decode(dev(pool), dev(bt), dev(lens.astype(np.int32)), dev(q), workspace=ws)
+    out = out.cpu().numpy()
+    ref = oracle.paged_decode(pool, bt, lens.astype(np.int32), q)
+    assert_close(out, ref)
+    assert np.all(out[lens == 0] == 0)
+
+
 @pytest.mark.parametrize("np_dtype", [np.float16, np.float32])
 def test_append_decode_fused_matches_append_then_decode(kvx, oracle, np_dtype):
     lens = kvgen.randint(41, 12, 0, 900)
@@ -222,7 +241,9 @@ def test_decode_gqa_grouping_matches_mha_expansion(kvx):
     gqa = kvx.decode(dev(pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
     mha_pool = np.repeat(pool, 3, axis=2)
     mha = kvx.decode(dev(mha_pool), dev(bt), dev(lens), dev(q)).cpu().numpy()
-    assert np.abs(gqa - mha).max() < 1e-5
+    # the pools differ in size, so the work is split differently: fp32
+    # summation order differs, nothing else
+    assert np.abs(gqa - mha).max() < 2e-4
 
 
 # ------------------------------------------------------------------ int8 ---
