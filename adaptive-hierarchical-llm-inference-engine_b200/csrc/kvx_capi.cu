@@ -16,6 +16,7 @@ extern "C" KVX_API const char *kvx_status_string(int status) {
     case KVX_ETIMEOUT: return "bounded device wait expired";
     case KVX_ENOSPC: return "workspace or pool too small";
     case KVX_ENODEV: return "no sm_100 device";
+    case KVX_ETOOBIG: return "request exceeds the static scratch of kvx_decode_noalloc";
     default: return "unknown status";
     }
 }

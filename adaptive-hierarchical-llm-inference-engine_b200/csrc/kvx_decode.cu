@@ -37,6 +37,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "kvx_common.cuh"
 #include "kvx_decode_params.cuh"
@@ -576,7 +577,7 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
                const int32_t *seq_lens, const int32_t *positions, const void *new_k,
                const void *new_v, int32_t batch, int32_t num_q_heads, const void *q, void *out,
                int32_t io_dtype, float sm_scale, void *workspace, size_t workspace_bytes_,
-               int32_t *error_flag, void *stream) {
+               int32_t *error_flag, void *stream, int min_chunk = 0) {
     if (!kv || !kv->pool || !block_table || !q || !out) return KVX_EINVAL;
     if (!seq_lens && !positions) return KVX_EINVAL;
     if (batch <= 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || num_q_heads <= 0) return KVX_EINVAL;
@@ -590,7 +591,14 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
         (kv->stats && (reinterpret_cast<uintptr_t>(kv->stats) & 15)) ||
         (reinterpret_cast<uintptr_t>(new_k) & 15) || (reinterpret_cast<uintptr_t>(new_v) & 15))
         return KVX_EINVAL;
-    const size_t need = workspace_bytes(batch, num_q_heads, max_pages);
+    // min_chunk > 0 (fixed-size scratch): splits are capped at
+    // ceil(max_pages / min_chunk) and the arrays are laid out for that cap
+    const int min_chunk_r = min_chunk > 0 ? (min_chunk + kWarps - 1) / kWarps * kWarps : 0;
+    const size_t need = min_chunk_r > 0
+                            ? (size_t)batch * num_q_heads *
+                                  ((size_t)(max_pages + min_chunk_r - 1) / min_chunk_r * (kHeadDim + 2) + 1) *
+                                  sizeof(float)
+                            : workspace_bytes(batch, num_q_heads, max_pages);
     if (!workspace || workspace_bytes_ < need) return KVX_ENOSPC;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return KVX_EINVAL;
 
@@ -617,9 +625,10 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     const bool tc = kv->dtype == KVX_F16 && p.group <= 16 && !(force_simt && force_simt[0] == '1');
     p.nhg = tc ? 1 : (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
     const int G = (p.group + p.nhg - 1) / p.nhg;
-    p.chunk = choose_chunk(batch, p.hkv, p.nhg, max_pages);
+    p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages), min_chunk_r);
     p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
-    const size_t splits_cap = max_splits_for(max_pages);
+    const size_t splits_cap = min_chunk_r > 0 ? (size_t)(max_pages + min_chunk_r - 1) / min_chunk_r
+                                              : max_splits_for(max_pages);
     p.part_o = static_cast<float *>(workspace);
     p.part_ml = p.part_o + (size_t)batch * num_q_heads * splits_cap * kHeadDim;
     p.counters = reinterpret_cast<int32_t *>(p.part_ml + (size_t)batch * num_q_heads * splits_cap * 2);
@@ -630,7 +639,7 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
         const int rc = launch_decode_tc(p, io_dtype, batch, st);
         if (rc != KVX_EUNSUPPORTED) return rc;
         p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;  // no tensor map: SIMT kernel
-        p.chunk = choose_chunk(batch, p.hkv, p.nhg, max_pages);
+        p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages), min_chunk_r);
         p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
         return io_dtype == KVX_F32 ? dispatch_kv<float>(p, kv->dtype, batch, st, (p.group + p.nhg - 1) / p.nhg)
                                    : dispatch_kv<__half>(p, kv->dtype, batch, st, (p.group + p.nhg - 1) / p.nhg);
@@ -680,4 +689,74 @@ extern "C" KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *blo
     return run_decode(kv, block_table, max_pages, nullptr, positions, new_k, new_v, batch,
                       num_q_heads, q, out, io_dtype, sm_scale, workspace, workspace_bytes_,
                       error_flag, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Decode that allocates nothing.
+//
+// Some callers of this library cannot allocate device memory at the moment
+// they decode: a JVM scheduler thread reaching the engine through JNI holds
+// only the buffers it was handed, an engine whose KV pool is capped to a
+// fixed byte budget must not grow, and code running under another
+// framework's allocator (or inside its stream capture) may not call
+// cudaMalloc / cudaFree behind that allocator's back.  kvx_decode_noalloc
+// serves them: its split-K scratch is a file-scope device array of
+// kNoAllocScratchBytes that every GPU loading this library holds until the
+// process exits.  The array is shared by all calls on a device and keeps the
+// last call's contents; the arrival counters that must start at zero are
+// cleared on the caller's stream before every launch, so calls that overlap
+// on the GPU (different streams, no ordering) race on the array.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+constexpr int kNoAllocMaxDevices = 64;
+void *g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device with cudaGetSymbolAddress (with that device current).
+int noalloc_scratch(void **addr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return KVX_ECUDA;
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return KVX_EUNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return KVX_ECUDA;
+        g_noalloc_addr[dev] = ptr;
+    }
+    *addr = g_noalloc_addr[dev];
+    return KVX_OK;
+}
+}  // namespace
+
+extern "C" KVX_API size_t kvx_decode_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" KVX_API int kvx_decode_noalloc(const kvx_paged *kv, const int32_t *block_table,
+                                          int32_t max_pages, const int32_t *seq_lens, int32_t batch,
+                                          int32_t num_q_heads, const void *q, void *out,
+                                          int32_t io_dtype, float sm_scale, int32_t *error_flag,
+                                          void *stream) {
+    if (!seq_lens || batch <= 0 || num_q_heads <= 0 || max_pages <= 0) return KVX_EINVAL;
+    // smallest layout: one split per (sequence, q-head) + its counter
+    const size_t rows = (size_t)batch * num_q_heads;
+    const size_t per_split = rows * (kHeadDim + 2) * sizeof(float);
+    if (rows * sizeof(int32_t) + per_split > kNoAllocScratchBytes) return KVX_ETOOBIG;
+    const size_t fit = (kNoAllocScratchBytes - rows * sizeof(int32_t)) / per_split;  // >= 1
+    // chunk so that ceil(max_pages / chunk) <= fit, a multiple of the 4 warps
+    int min_chunk = (int)((max_pages + fit - 1) / fit);
+    min_chunk = (min_chunk + kWarps - 1) / kWarps * kWarps;
+    while ((size_t)((max_pages + min_chunk - 1) / min_chunk) > fit) min_chunk += kWarps;
+    void *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc != KVX_OK) return rc;
+    const size_t splits_cap = (size_t)(max_pages + min_chunk - 1) / min_chunk;
+    int32_t *counters = reinterpret_cast<int32_t *>(static_cast<float *>(scratch) + rows * splits_cap * (kHeadDim + 2));
+    if (cudaMemsetAsync(counters, 0, rows * sizeof(int32_t), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return KVX_ECUDA;
+    return run_decode(kv, block_table, max_pages, seq_lens, nullptr, nullptr, nullptr, batch,
+                      num_q_heads, q, out, io_dtype, sm_scale, scratch, kNoAllocScratchBytes,
+                      error_flag, stream, min_chunk);
 }

@@ -20,7 +20,8 @@ HEAD_DIM, PAGE_TOKENS = 128, 16
 
 STATUS = {0: "ok", -1: "invalid argument", -2: "object pinned", -3: "CUDA error",
           -4: "unsupported geometry or dtype", -5: "bounded device wait expired",
-          -6: "workspace or pool too small", -7: "no sm_100 device"}
+          -6: "workspace or pool too small", -7: "no sm_100 device",
+          -8: "request exceeds the static scratch of kvx_decode_noalloc"}
 
 
 class KvxError(RuntimeError):
@@ -64,6 +65,10 @@ lib.kvx_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, 
 lib.kvx_append_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
                                   _vp, _i32, _f32, _vp, _sz, _vp, _vp]
 lib.kvx_decode_workspace_init.argtypes = [_vp, _sz, _vp]
+lib.kvx_decode_noalloc.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32,
+                                   _f32, _vp, _vp]
+lib.kvx_decode_noalloc.restype = C.c_int
+lib.kvx_decode_noalloc_scratch_bytes.restype = _sz
 lib.kvx_compress_int8.argtypes = [_vp, _i32, _vp, _vp, _sz, _i32, _vp]
 lib.kvx_decompress_int8.argtypes = [_vp, _vp, _vp, _i32, _sz, _i32, _vp]
 lib.kvx_f32_to_f16_trunc.argtypes = [_vp, _vp, _sz, _vp]

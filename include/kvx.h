@@ -40,7 +40,8 @@ enum kvx_status {
     KVX_EUNSUPPORTED = -4, /* geometry/dtype this build has no kernel for */
     KVX_ETIMEOUT = -5,     /* a bounded device wait expired (see error_flag) */
     KVX_ENOSPC = -6,       /* workspace / pool too small */
-    KVX_ENODEV = -7        /* no sm_100 device current */
+    KVX_ENODEV = -7,       /* no sm_100 device current */
+    KVX_ETOOBIG = -8       /* request exceeds kvx_decode_noalloc's static scratch */
 };
 
 enum kvx_dtype { KVX_F32 = 0, KVX_F16 = 1, KVX_I8 = 2 };
@@ -113,6 +114,25 @@ KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *block_table, i
                               const void *new_v, int32_t num_q_heads, const void *q, void *out,
                               int32_t io_dtype, float sm_scale, void *workspace,
                               size_t workspace_bytes, int32_t *error_flag, void *stream);
+
+/* kvx_decode without any allocation, for callers that cannot allocate
+ * device memory when they decode: a JNI / FFI caller holding only the
+ * buffers it was given, an engine whose KV memory is capped at a fixed
+ * budget, or code living under another framework's allocator or stream
+ * capture.  No counterpart in the reference.  Same arguments and result as
+ * kvx_decode minus the workspace: the split-K scratch is a static device
+ * array of kvx_decode_noalloc_scratch_bytes() (8 MiB) that each GPU loading
+ * this library holds until exit.  The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress), so make it before any
+ * stream capture.  All calls on a device share the array: calls that
+ * overlap on the GPU race, so order them on one stream.  A batch whose
+ * batch*num_q_heads rows do not fit even at one split per row returns
+ * KVX_ETOOBIG.  Calls no cudaMalloc / cudaFree. */
+KVX_API size_t kvx_decode_noalloc_scratch_bytes(void);
+KVX_API int kvx_decode_noalloc(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                               const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                               const void *q, void *out, int32_t io_dtype, float sm_scale,
+                               int32_t *error_flag, void *stream);
 
 /* Per-block int8 quantisation.  Replaces KVCompressionEngine::compressToINT8
  * (native-engine/cpp/KVCompressionEngine.cpp:83-113), one reference call per
