@@ -1,0 +1,609 @@
+// engine.cpp -- tier moves, LRU slab eviction and the decode step of the
+// KV-cache engine (see engine.h).  All device work goes through the kvx C
+// ABI (include/kvx.h); this file only does bookkeeping and copies.
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+namespace kvx_engine {
+namespace {
+
+int env_int(const char *name, int dflt) {
+    const char *v = getenv(name);
+    if (!v || !*v) return dflt;
+    char *end = nullptr;
+    long x = strtol(v, &end, 10);
+    return (end && *end == 0 && x > 0 && x < (1 << 30)) ? (int)x : dflt;
+}
+
+double now_ms() {
+    using namespace std::chrono;
+    return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
+}
+
+uint64_t splitmix(uint64_t &x) {
+    uint64_t z = (x += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+}  // namespace
+
+Engine &Engine::instance() {
+    static Engine *e = new Engine();  // lives until exit; never destroyed mid-call
+    return *e;
+}
+
+Engine::~Engine() { release_all(); }
+
+void Engine::default_config(adaptive_engine_config *cfg) const {
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->layers = env_int("ADAPTIVELLM_KV_LAYERS", 28);
+    cfg->kv_heads = 8;
+    cfg->q_heads = 24;
+    cfg->head_dim = 128;
+    cfg->page_tokens = 16;
+    cfg->max_batch = env_int("ADAPTIVELLM_KV_BATCH", 32);
+    cfg->pages_per_layer = env_int("ADAPTIVELLM_KV_PAGES", 256);
+    cfg->gpu_layer_slots = std::min(env_int("ADAPTIVELLM_KV_GPU_LAYERS", cfg->layers), cfg->layers);
+    const char *dev = getenv("ADAPTIVELLM_DEVICE");
+    cfg->device = dev ? atoi(dev) : 0;
+    const char *dir = getenv("ADAPTIVELLM_KV_OFFLOAD_DIR");
+    snprintf(cfg->offload_dir, sizeof(cfg->offload_dir), "%s", dir && *dir ? dir : "/tmp");
+}
+
+int Engine::configure(const adaptive_engine_config &cfg) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (started_) return KVX_EBUSY;
+    if (cfg.layers <= 0 || cfg.kv_heads <= 0 || cfg.q_heads <= 0 || cfg.q_heads % cfg.kv_heads ||
+        cfg.head_dim != 128 || cfg.page_tokens != 16 || cfg.max_batch <= 0 || cfg.pages_per_layer <= 0 ||
+        cfg.gpu_layer_slots <= 0 || cfg.gpu_layer_slots > cfg.layers)
+        return KVX_EINVAL;
+    cfg_ = cfg;
+    cfg_.offload_dir[sizeof(cfg_.offload_dir) - 1] = 0;
+    configured_ = true;
+    return KVX_OK;
+}
+
+bool Engine::started() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return started_;
+}
+
+void Engine::start() {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (started_) return;
+    if (!configured_) default_config(&cfg_);
+    if (cudaSetDevice(cfg_.device) != cudaSuccess || kvx_device_check() != KVX_OK) {
+        fprintf(stderr, "[adaptive_engine] start(): no sm_100 device %d\n", cfg_.device);
+        return;
+    }
+    slab_bytes_ = (size_t)cfg_.pages_per_layer * 2 * cfg_.kv_heads * 16 * 128 * sizeof(uint16_t);
+    blocks_per_slab_ = (size_t)cfg_.pages_per_layer * 2 * cfg_.kv_heads;
+    bool ok = cudaMalloc(&arena_, slab_bytes_ * cfg_.gpu_layer_slots) == cudaSuccess &&
+              cudaMemset(arena_, 0, slab_bytes_ * cfg_.gpu_layer_slots) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&compute_, cudaStreamNonBlocking) == cudaSuccess &&
+         cudaStreamCreateWithFlags(&copy_, cudaStreamNonBlocking) == cudaSuccess;
+    const size_t qn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.q_heads * 128;
+    const size_t kn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.kv_heads * 128;
+    ok = ok && cudaMalloc(&d_q_, qn * 2) == cudaSuccess && cudaMalloc(&d_out_, qn * 2) == cudaSuccess &&
+         cudaMalloc(&d_k_, kn * 2) == cudaSuccess && cudaMalloc(&d_v_, kn * 2) == cudaSuccess &&
+         cudaMalloc(&d_pos_, cfg_.max_batch * sizeof(int32_t)) == cudaSuccess &&
+         cudaMalloc(&d_err_, sizeof(int32_t)) == cudaSuccess && cudaMemset(d_err_, 0, 4) == cudaSuccess &&
+         cudaHostAlloc(&h_pos_, cfg_.max_batch * sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    ev_in_.assign(cfg_.layers, nullptr);
+    ev_out_.assign(cfg_.layers, nullptr);
+    for (int l = 0; ok && l < cfg_.layers; ++l)
+        ok = cudaEventCreateWithFlags(&ev_in_[l], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&ev_out_[l], cudaEventDisableTiming) == cudaSuccess;
+    device_bytes_ = (long long)(slab_bytes_ * cfg_.gpu_layer_slots + 2 * qn * 2 + 2 * kn * 2);
+    layers_.assign(cfg_.layers, Layer{});
+    free_slabs_.clear();
+    for (int i = cfg_.gpu_layer_slots - 1; i >= 0; --i) free_slabs_.push_back(i);
+    for (int l = 0; ok && l < cfg_.layers; ++l) {
+        if (l < cfg_.gpu_layer_slots) {
+            layers_[l].tier = kGpu;
+            layers_[l].slab = free_slabs_.back();
+            free_slabs_.pop_back();
+        } else {  // beyond the device budget: starts in RAM, zero-filled
+            layers_[l].tier = kRam;
+            ok = ensure_host(l) == KVX_OK;
+            if (ok) memset(layers_[l].host, 0, slab_bytes_);
+        }
+    }
+    free_pages_.clear();
+    for (int pg = cfg_.pages_per_layer - 1; pg >= 0; --pg) free_pages_.push_back(pg);
+    batch_ = 0;
+    max_pages_ = 0;
+    clock_ = 0;
+    current_layer_ = 0;
+    if (!ok) {
+        fprintf(stderr, "[adaptive_engine] start(): device allocation failed\n");
+        release_all();
+        return;
+    }
+    started_ = true;
+}
+
+void Engine::release_all() {
+    if (compute_) cudaStreamSynchronize(compute_);
+    if (copy_) cudaStreamSynchronize(copy_);
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        Layer &L = layers_[l];
+        if (L.host) cudaFreeHost(L.host);
+        if (L.codes) cudaFree(L.codes);
+        if (L.stats) cudaFree(L.stats);
+        if (L.tier == kOffloaded) remove(offload_path((int)l).c_str());
+        L = Layer{};
+    }
+    layers_.clear();
+    for (auto &e : ev_in_) if (e) cudaEventDestroy(e);
+    for (auto &e : ev_out_) if (e) cudaEventDestroy(e);
+    ev_in_.clear();
+    ev_out_.clear();
+    auto free_dev = [](auto *&p) {
+        if (p) cudaFree((void *)p);
+        p = nullptr;
+    };
+    free_dev(arena_);
+    free_dev(d_q_);
+    free_dev(d_k_);
+    free_dev(d_v_);
+    free_dev(d_out_);
+    free_dev(d_table_);
+    free_dev(d_pos_);
+    free_dev(d_err_);
+    if (d_ws_) cudaFree(d_ws_);
+    d_ws_ = nullptr;
+    if (h_pos_) cudaFreeHost(h_pos_);
+    h_pos_ = nullptr;
+    if (compute_) cudaStreamDestroy(compute_);
+    if (copy_) cudaStreamDestroy(copy_);
+    compute_ = copy_ = nullptr;
+    free_slabs_.clear();
+    device_bytes_ = 0;
+    batch_ = 0;
+}
+
+void Engine::stop() {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!started_) return;
+    release_all();
+    started_ = false;
+}
+
+bool Engine::valid(long layer) const {
+    return started_ && layer >= 0 && layer < (long)layers_.size();
+}
+
+long Engine::ms_since(double t0) const {
+    const double ms = now_ms() - t0;
+    return std::max(1l, (long)std::ceil(ms));  // work was done: at least 1 ms, as callers test > 0
+}
+
+std::string Engine::offload_path(int l) const {
+    return std::string(cfg_.offload_dir) + "/adaptive_kv_layer_" + std::to_string(l) + ".bin";
+}
+
+int Engine::ensure_host(int l) {
+    if (layers_[l].host) return KVX_OK;
+    return cudaHostAlloc(&layers_[l].host, slab_bytes_, cudaHostAllocPortable) == cudaSuccess
+               ? KVX_OK
+               : KVX_ENOSPC;
+}
+
+// A free device slab for layer `for_layer`, evicting the least recently used
+// GPU-resident layer to RAM when none is free (KVCacheGPU::transferToGPU's
+// evict-then-retry, native-engine/cpp/KVCacheGPU.cpp:68-109).  The victim is
+// the smallest last_used stamp, the lowest layer index on ties
+// (KVCacheGPU::findLRUPage, KVCacheGPU.cpp:54-66); pinned layers are skipped.
+int Engine::alloc_slab(int for_layer) {
+    if (!free_slabs_.empty()) {
+        const int s = free_slabs_.back();
+        free_slabs_.pop_back();
+        return s;
+    }
+    int victim = -1;
+    uint64_t best = UINT64_MAX;
+    bool any_pinned = false;
+    for (int l = 0; l < (int)layers_.size(); ++l) {
+        const Layer &L = layers_[l];
+        if (l == for_layer || L.tier != kGpu) continue;
+        if (L.refcount > 0) {
+            any_pinned = true;
+            continue;
+        }
+        if (L.last_used < best) {
+            best = L.last_used;
+            victim = l;
+        }
+    }
+    if (victim < 0) return any_pinned ? -2 : -1;
+    if (to_ram_locked(victim) < 0) return -1;
+    const int s = free_slabs_.back();
+    free_slabs_.pop_back();
+    return s;
+}
+
+int Engine::to_ram_locked(int l) {
+    Layer &L = layers_[l];
+    if (L.tier == kRam) return 0;
+    cudaStreamSynchronize(compute_);
+    if (ensure_host(l) != KVX_OK) return KVX_ENOSPC;
+    if (L.tier == kOffloaded) {
+        FILE *f = fopen(offload_path(l).c_str(), "rb");
+        const bool ok = f && fread(L.host, 1, slab_bytes_, f) == slab_bytes_;
+        if (f) fclose(f);
+        if (!ok) return KVX_EINVAL;
+        remove(offload_path(l).c_str());
+        L.tier = kRam;
+        return 1;
+    }
+    if (L.tier == kCompressed) {  // decompress into a slab first
+        const int rc = to_gpu_locked(l);
+        if (rc < 0) return rc;
+    }
+    if (cudaMemcpyAsync(L.host, arena_ + (size_t)L.slab * slab_bytes_, slab_bytes_,
+                        cudaMemcpyDeviceToHost, copy_) != cudaSuccess ||
+        cudaStreamSynchronize(copy_) != cudaSuccess)
+        return KVX_ECUDA;
+    free_slabs_.push_back(L.slab);
+    L.slab = -1;
+    L.tier = kRam;
+    return 1;
+}
+
+int Engine::to_gpu_locked(int l) {
+    Layer &L = layers_[l];
+    L.last_used = ++clock_;
+    if (L.tier == kGpu) return 0;
+    const int s = alloc_slab(l);
+    if (s == -2) return KVX_EBUSY;
+    if (s < 0) return KVX_ENOSPC;
+    uint8_t *dst = arena_ + (size_t)s * slab_bytes_;
+    int rc = KVX_OK;
+    if (L.tier == kCompressed) {
+        rc = kvx_decompress_int8(L.codes, L.stats, dst, KVX_F16, blocks_per_slab_, 2048, copy_);
+    } else {
+        if (L.tier == kOffloaded) {
+            if (ensure_host(l) != KVX_OK) rc = KVX_ENOSPC;
+            FILE *f = rc ? nullptr : fopen(offload_path(l).c_str(), "rb");
+            if (!rc && !(f && fread(L.host, 1, slab_bytes_, f) == slab_bytes_)) rc = KVX_EINVAL;
+            if (f) fclose(f);
+        }
+        if (!rc && cudaMemcpyAsync(dst, L.host, slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess)
+            rc = KVX_ECUDA;
+    }
+    if (!rc && cudaStreamSynchronize(copy_) != cudaSuccess) rc = KVX_ECUDA;
+    if (rc) {
+        free_slabs_.push_back(s);
+        return rc;
+    }
+    if (L.tier == kCompressed) {
+        cudaFree(L.codes);
+        cudaFree(L.stats);
+        L.codes = nullptr;
+        L.stats = nullptr;
+        device_bytes_ -= (long long)(slab_bytes_ / 2 + blocks_per_slab_ * 16);
+    } else if (L.tier == kOffloaded) {
+        remove(offload_path(l).c_str());
+    }
+    L.slab = s;
+    L.tier = kGpu;
+    return 1;
+}
+
+int Engine::compress_locked(int l) {
+    Layer &L = layers_[l];
+    if (L.tier == kCompressed) return 0;
+    if (L.tier != kGpu) {
+        const int rc = to_gpu_locked(l);
+        if (rc < 0) return rc;
+    }
+    cudaStreamSynchronize(compute_);
+    if (cudaMalloc(&L.codes, slab_bytes_ / 2) != cudaSuccess) {
+        L.codes = nullptr;
+        return KVX_ENOSPC;
+    }
+    if (cudaMalloc(&L.stats, blocks_per_slab_ * 16) != cudaSuccess) {
+        cudaFree(L.codes);
+        L.codes = nullptr;
+        L.stats = nullptr;
+        return KVX_ENOSPC;
+    }
+    int rc = kvx_compress_int8(arena_ + (size_t)L.slab * slab_bytes_, KVX_F16, L.codes, L.stats,
+                               blocks_per_slab_, 2048, copy_);
+    if (!rc && cudaStreamSynchronize(copy_) != cudaSuccess) rc = KVX_ECUDA;
+    if (rc) {
+        cudaFree(L.codes);
+        cudaFree(L.stats);
+        L.codes = nullptr;
+        L.stats = nullptr;
+        return rc;
+    }
+    device_bytes_ += (long long)(slab_bytes_ / 2 + blocks_per_slab_ * 16);
+    free_slabs_.push_back(L.slab);
+    L.slab = -1;
+    L.tier = kCompressed;
+    return 1;
+}
+
+int Engine::offload_locked(int l) {
+    Layer &L = layers_[l];
+    if (L.tier == kOffloaded) return 0;
+    if (L.tier != kRam) {
+        const int rc = to_ram_locked(l);
+        if (rc < 0) return rc;
+    }
+    FILE *f = fopen(offload_path(l).c_str(), "wb");
+    const bool ok = f && fwrite(L.host, 1, slab_bytes_, f) == slab_bytes_;
+    if (f) fclose(f);
+    if (!ok) return KVX_EINVAL;
+    cudaFreeHost(L.host);
+    L.host = nullptr;
+    L.tier = kOffloaded;
+    return 1;
+}
+
+// ---- NativeEngineApi operations ------------------------------------------
+
+long Engine::move_to_ram(long layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    if (layers_[layer].refcount > 0 && layers_[layer].tier != kRam) return -2;
+    const int rc = to_ram_locked((int)layer);
+    return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
+}
+
+long Engine::move_to_gpu(long layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    const int rc = to_gpu_locked((int)layer);
+    return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
+}
+
+long Engine::compress(long layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    if (layers_[layer].refcount > 0 && layers_[layer].tier != kCompressed) return -2;
+    const int rc = compress_locked((int)layer);
+    return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
+}
+
+long Engine::offload(long layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    if (layers_[layer].refcount > 0 && layers_[layer].tier != kOffloaded) return -2;
+    const int rc = offload_locked((int)layer);
+    if (rc > 0) layers_[layer].cached = false;
+    return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
+}
+
+// Layer-cache bitmap with pins (llama_wrapper.cpp:171-219), tied to KV
+// residency: a cached layer has its KV on the device.
+long Engine::prefetch_layer(int layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    Layer &L = layers_[layer];
+    if (L.cached) return 0;
+    const int rc = to_gpu_locked(layer);
+    if (rc < 0) return rc == KVX_EBUSY ? -2 : -1;
+    L.cached = true;
+    return ms_since(t0);
+}
+
+long Engine::evict_layer(int layer) {
+    const double t0 = now_ms();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    Layer &L = layers_[layer];
+    if (!L.cached) return 0;
+    if (L.refcount > 0) return -2;
+    const int rc = to_ram_locked(layer);
+    if (rc < 0) return -1;
+    L.cached = false;
+    return ms_since(t0);
+}
+
+long Engine::keep_layer(int layer) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    Layer &L = layers_[layer];
+    if (!L.cached) {
+        const int rc = to_gpu_locked(layer);
+        if (rc < 0) return rc == KVX_EBUSY ? -2 : -1;
+        L.cached = true;
+    }
+    return ++L.refcount;
+}
+
+void Engine::release_layer(int layer) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer)) return;
+    if (layers_[layer].refcount > 0) --layers_[layer].refcount;
+}
+
+int Engine::current_layer() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return current_layer_;
+}
+
+long Engine::gpu_memory() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return (long)device_bytes_;
+}
+
+int Engine::kv_pages() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return started_ ? (int)layers_.size() : (configured_ ? cfg_.layers : 0);
+}
+
+int Engine::cached_layers() {
+    std::lock_guard<std::mutex> lk(mu_);
+    int n = 0;
+    for (const Layer &L : layers_) n += L.cached ? 1 : 0;
+    return n;
+}
+
+int Engine::layer_view(int layer, kvx_paged *view) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!view || !valid(layer) || layers_[layer].tier != kGpu) return KVX_EINVAL;
+    view->pool = arena_ + (size_t)layers_[layer].slab * slab_bytes_;
+    view->stats = nullptr;
+    view->dtype = KVX_F16;
+    view->num_pages = cfg_.pages_per_layer;
+    view->num_kv_heads = cfg_.kv_heads;
+    view->head_dim = 128;
+    view->page_tokens = 16;
+    return KVX_OK;
+}
+
+int Engine::layer_tier(int layer) {
+    std::lock_guard<std::mutex> lk(mu_);
+    return valid(layer) ? (int)layers_[layer].tier : -1;
+}
+
+long long Engine::device_bytes() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return device_bytes_;
+}
+
+int32_t Engine::seq_len(int s) {
+    std::lock_guard<std::mutex> lk(mu_);
+    return (s >= 0 && s < batch_) ? lens_[s] : -1;
+}
+
+int Engine::copy_layer(int layer, void *ptr, bool load) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!ptr || !valid(layer)) return KVX_EINVAL;
+    const int rc = to_gpu_locked(layer);
+    if (rc < 0) return rc;
+    cudaStreamSynchronize(compute_);
+    uint8_t *slab = arena_ + (size_t)layers_[layer].slab * slab_bytes_;
+    const cudaError_t e = load ? cudaMemcpy(slab, ptr, slab_bytes_, cudaMemcpyDefault)
+                               : cudaMemcpy(ptr, slab, slab_bytes_, cudaMemcpyDefault);
+    return e == cudaSuccess ? KVX_OK : KVX_ECUDA;
+}
+
+int32_t Engine::block_table(int32_t *dst) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (dst) std::copy(table_.begin(), table_.end(), dst);
+    return max_pages_;
+}
+
+// ---- sequences and the decode step ---------------------------------------
+
+int Engine::set_sequences(int batch, const int32_t *lens, int reserve_tokens, uint64_t seed) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!started_ || batch <= 0 || batch > cfg_.max_batch || !lens || reserve_tokens < 0) return KVX_EINVAL;
+    cudaStreamSynchronize(compute_);
+    // every physical page back into the free list, then hand them out
+    std::vector<int32_t> order(cfg_.pages_per_layer);
+    for (int i = 0; i < cfg_.pages_per_layer; ++i) order[i] = i;
+    if (seed) {  // Fisher-Yates with splitmix64: fragmented page tables
+        uint64_t st = seed;
+        for (int i = cfg_.pages_per_layer - 1; i > 0; --i) std::swap(order[i], order[splitmix(st) % (uint64_t)(i + 1)]);
+    }
+    int max_pages = 1;
+    long long need = 0;
+    for (int s = 0; s < batch; ++s) {
+        if (lens[s] < 0) return KVX_EINVAL;
+        const int np = (lens[s] + reserve_tokens + 15) / 16;
+        max_pages = std::max(max_pages, np);
+        need += np;
+    }
+    if (need > cfg_.pages_per_layer) return KVX_ENOSPC;
+    table_.assign((size_t)batch * max_pages, -1);
+    size_t next = 0;
+    for (int s = 0; s < batch; ++s) {
+        const int np = (lens[s] + reserve_tokens + 15) / 16;
+        for (int j = 0; j < np; ++j) table_[(size_t)s * max_pages + j] = order[next++];
+    }
+    free_pages_.assign(order.begin() + next, order.end());
+    if (d_table_) cudaFree(d_table_);
+    d_table_ = nullptr;
+    if (d_ws_) cudaFree(d_ws_);
+    d_ws_ = nullptr;
+    ws_bytes_ = kvx_decode_workspace_bytes(batch, cfg_.q_heads, max_pages, 16);
+    if (cudaMalloc(&d_table_, table_.size() * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&d_ws_, ws_bytes_) != cudaSuccess ||
+        cudaMemcpy(d_table_, table_.data(), table_.size() * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess ||
+        kvx_decode_workspace_init(d_ws_, ws_bytes_, nullptr) != KVX_OK || cudaDeviceSynchronize() != cudaSuccess) {
+        batch_ = 0;
+        return KVX_ECUDA;
+    }
+    lens_.assign(lens, lens + batch);
+    batch_ = batch;
+    max_pages_ = max_pages;
+    return KVX_OK;
+}
+
+int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!started_ || batch_ == 0 || !q || !k || !v || !out) return KVX_EINVAL;
+    for (int s = 0; s < batch_; ++s)  // every sequence needs a page for its next token
+        if (lens_[s] / 16 >= max_pages_ || table_[(size_t)s * max_pages_ + lens_[s] / 16] < 0)
+            return KVX_ENOSPC;
+    const int L = cfg_.layers, B = batch_, hq = cfg_.q_heads, hkv = cfg_.kv_heads;
+    const size_t qrow = (size_t)B * hq * 128, krow = (size_t)B * hkv * 128;  // elements per layer
+    const size_t qstride = (size_t)cfg_.max_batch * hq * 128, kstride = (size_t)cfg_.max_batch * hkv * 128;
+    memcpy(h_pos_, lens_.data(), B * sizeof(int32_t));
+    if (cudaMemcpyAsync(d_pos_, h_pos_, B * sizeof(int32_t), cudaMemcpyHostToDevice, compute_) != cudaSuccess)
+        return KVX_ECUDA;
+    for (int l = 0; l < L; ++l) {  // inputs of every layer, one event per layer
+        if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
+            cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
+            cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
+            cudaEventRecord(ev_in_[l], copy_))
+            return KVX_ECUDA;
+    }
+    int rc = KVX_OK;
+    for (int l = 0; l < L && rc == KVX_OK; ++l) {
+        if (layers_[l].tier != kGpu) {  // tiered: bring the layer back (may evict the LRU layer)
+            const int r = to_gpu_locked(l);
+            if (r < 0) {
+                rc = r;
+                break;
+            }
+        }
+        layers_[l].last_used = ++clock_;
+        kvx_paged view{arena_ + (size_t)layers_[l].slab * slab_bytes_, nullptr, KVX_F16,
+                       cfg_.pages_per_layer, hkv, 128, 16};
+        if (cudaStreamWaitEvent(compute_, ev_in_[l], 0) != cudaSuccess) {
+            rc = KVX_ECUDA;
+            break;
+        }
+        rc = kvx_append_decode(&view, d_table_, max_pages_, d_pos_, B, d_k_ + l * kstride,
+                               d_v_ + l * kstride, hq, d_q_ + l * qstride, d_out_ + l * qstride,
+                               KVX_F16, 0.f, d_ws_, ws_bytes_, d_err_, compute_);
+        if (rc) break;
+        if (cudaEventRecord(ev_out_[l], compute_) || cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
+            cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
+            rc = KVX_ECUDA;
+        current_layer_ = l;
+    }
+    int32_t err = 0;
+    if (cudaStreamSynchronize(compute_) != cudaSuccess || cudaStreamSynchronize(copy_) != cudaSuccess ||
+        cudaMemcpy(&err, d_err_, sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return KVX_ECUDA;
+    if (rc) return rc;
+    if (err) {
+        cudaMemset(d_err_, 0, sizeof(int32_t));
+        return (err & 1) ? KVX_ETIMEOUT : KVX_EINVAL;
+    }
+    for (int s = 0; s < B; ++s) ++lens_[s];
+    return KVX_OK;
+}
+
+}  // namespace kvx_engine

@@ -1,0 +1,134 @@
+/*
+ * adaptive_engine.h -- the C ABI the reference's Java/JNI stack binds
+ * (dlopen of libadaptive_engine.so, then adaptive_engine_get_api()), backed
+ * by the B200 KV-cache engine.
+ *
+ * NativeEngineApi keeps the exact layout and calling convention of
+ * native-engine/llama_wrapper/llama_wrapper.cpp:26-40 (duplicated in
+ * src/main/cpp/adaptive_scheduler.cpp:106-120 and
+ * native-engine/shim/adaptive_engine_shim.cpp:13-27): 13 function pointers
+ * in this order.  As in the reference, a "kvPageId" is a layer index.  The
+ * KV operations do real work here:
+ *   moveKvToRam(l)  copy layer l's KV pool to pinned host memory, release
+ *                   its device slab                      (llama_wrapper.cpp:220-280)
+ *   moveKvToGpu(l)  bring layer l back into a device slab (from RAM, the
+ *                   int8 form or the file tier), evicting the least recently
+ *                   used resident layer when no slab is free (llama_wrapper.cpp:281-341,
+ *                   eviction as native-engine/cpp/KVCacheGPU.cpp:68-109)
+ *   compressKv(l)   int8-quantise layer l per (page, K|V, head) block with
+ *                   the reference's KVCompressionEngine scheme, release the
+ *                   fp16 slab                            (llama_wrapper.cpp:342-406)
+ *   offloadKv(l)    write layer l to the file tier, release device and host
+ *                   memory                               (llama_wrapper.cpp:407-433)
+ * Return convention (llama_wrapper.cpp:187-433): the four KV operations
+ * return the milliseconds spent, rounded up and at least 1 on success (also
+ * when the layer already was in the requested tier, as the reference's
+ * always report their latency); prefetchLayer / evictLayer return 0 when
+ * the layer already was cached / evicted (llama_wrapper.cpp:176,192); -1
+ * means an invalid id, a stopped engine or an allocation failure, -2 that a
+ * pinned layer would have to leave the device.
+ */
+#ifndef ADAPTIVE_ENGINE_H
+#define ADAPTIVE_ENGINE_H
+
+#include <stdint.h>
+
+#include "kvx.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define ADAPTIVE_ENGINE_EXPORT __declspec(dllexport)
+#else
+#define ADAPTIVE_ENGINE_EXPORT __attribute__((visibility("default")))
+#endif
+
+typedef struct NativeEngineApi {
+    void (*start)();
+    void (*stop)();
+    long (*prefetchLayer)(int layerId);
+    long (*evictLayer)(int layerId);
+    long (*keepLayer)(int layerId);
+    long (*moveKvToRam)(long kvPageId);
+    long (*moveKvToGpu)(long kvPageId);
+    long (*compressKv)(long kvPageId);
+    long (*offloadKv)(long kvPageId);
+    int (*getCurrentLayer)();
+    long (*getGpuMemory)();
+    int (*getKvPages)();
+    int (*getCachedLayers)();
+} NativeEngineApi;
+
+/* native-engine/llama_wrapper/llama_wrapper.cpp:742-744 */
+ADAPTIVE_ENGINE_EXPORT NativeEngineApi *adaptive_engine_get_api(void);
+/* native-engine/llama_wrapper/llama_wrapper.cpp:733-740: drop one pin. */
+ADAPTIVE_ENGINE_EXPORT void adaptive_engine_test_release_layer(int layerId);
+
+/* ---- additive engine interface (the reference has no device engine) ---- */
+
+/* Geometry and budgets.  Defaults: Llama-3.2-3B KV (28 layers, 8 KV heads,
+ * 24 q-heads, head_dim 128), 16-token pages, 32 sequences, 256 pages per
+ * layer, every layer given a device slab, offload files under /tmp.
+ * Environment overrides read by start(): ADAPTIVELLM_KV_LAYERS,
+ * ADAPTIVELLM_KV_PAGES, ADAPTIVELLM_KV_BATCH, ADAPTIVELLM_KV_GPU_LAYERS,
+ * ADAPTIVELLM_KV_OFFLOAD_DIR, ADAPTIVELLM_DEVICE. */
+typedef struct adaptive_engine_config {
+    int32_t layers;
+    int32_t kv_heads;
+    int32_t q_heads;
+    int32_t head_dim;         /* 128 */
+    int32_t page_tokens;      /* 16 */
+    int32_t max_batch;        /* sequence slots */
+    int32_t pages_per_layer;  /* physical pages of one layer's pool */
+    int32_t gpu_layer_slots;  /* device slabs (< layers: layers compete, LRU) */
+    int32_t device;
+    char offload_dir[256];
+} adaptive_engine_config;
+
+/* Fill *cfg with the defaults (environment applied). */
+ADAPTIVE_ENGINE_EXPORT void adaptive_engine_default_config(adaptive_engine_config *cfg);
+/* Set the geometry used by the next start().  KVX_EBUSY while started. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_configure(const adaptive_engine_config *cfg);
+/* Layer l's device pool as a kvx_paged view (KVX_EINVAL if the layer has
+ * no fp16 device slab right now).  The view stays valid until the layer
+ * moves. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_layer_view(int layer, kvx_paged *view);
+/* Start `batch` sequences with context lengths lens[0..batch) (host array):
+ * pages for the contexts plus `reserve_tokens` future tokens are taken from
+ * the pool's free list -- in order, or in a seeded random order when
+ * seed != 0 (fragmented page tables).  Page contents are left as they are
+ * (the caller fills them, e.g. through adaptive_engine_layer_view). */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_sequences(int32_t batch, const int32_t *lens,
+                                                         int32_t reserve_tokens, uint64_t seed);
+/* One decode step through host buffers for every layer: copy q
+ * [layers][batch][q_heads][head_dim], new K and V [layers][batch][kv_heads]
+ * [head_dim] (fp16 bits) to the device, append the token and run paged GQA
+ * decode per layer, copy the attention output [layers][batch][q_heads]
+ * [head_dim] back.  Copies overlap the layers' kernels (side stream, one
+ * event per layer).  Returns a kvx_status. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_decode_step(const uint16_t *q, const uint16_t *k,
+                                                       const uint16_t *v, uint16_t *out);
+/* Copy layer l's whole fp16 pool (slab_bytes = pages_per_layer * 2 *
+ * kv_heads * 16 * 128 * 2 bytes) from `src` / to `dst`, host or device
+ * memory (cudaMemcpyDefault); the layer is brought to the GPU first.  For
+ * restoring / checkpointing a layer's KV.  Return a kvx_status. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_load_layer(int layer, const void *src);
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_read_layer(int layer, void *dst);
+/* The block table of the current sequences: returns max_pages (the row
+ * length) and, when dst != NULL, copies batch * max_pages int32 physical
+ * page ids (-1 = unassigned). */
+ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_block_table(int32_t *dst);
+/* Current context length of sequence s (-1 if none). */
+ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_seq_len(int32_t s);
+/* Tier of layer l: 0 GPU, 1 RAM, 2 COMPRESSED (int8 on device),
+ * 3 OFFLOADED (file), -1 invalid. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_layer_tier(int layer);
+/* Bytes of device memory the engine holds. */
+ADAPTIVE_ENGINE_EXPORT long long adaptive_engine_device_bytes(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,155 @@
+"""The engine's tiers and decode step, checked bit for bit where the data is
+only moved and against the oracle where it is computed.
+
+- GPU -> RAM -> GPU and GPU -> file -> GPU preserve every byte.
+- GPU -> int8 -> GPU equals the oracle's KVCompressionEngine round trip
+  (compressToINT8 / decompressINT8, native-engine/cpp/KVCompressionEngine.cpp:83-122)
+  rounded to fp16.
+- With fewer device slabs than layers, the layer evicted by each move to the
+  GPU is the least recently used one, lowest index on ties
+  (KVCacheGPU::findLRUPage, native-engine/cpp/KVCacheGPU.cpp:54-66).
+- adaptive_engine_decode_step (host buffers in and out) equals the oracle's
+  append + paged GQA decode, and leaves the pool as the oracle's append.
+"""
+import numpy as np
+import pytest
+
+import kvgen
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 1e-2
+LAYERS, PAGES, HKV, HQ = 4, 32, 8, 24
+
+
+@pytest.fixture()
+def engine(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import kvx.engine as E
+    api = E.api()
+    api.stop()
+    yield E, api, tmp_path
+    api.stop()
+
+
+def start(E, api, tmp_path, slots=LAYERS, batch=4):
+    E.configure(layers=LAYERS, pages_per_layer=PAGES, max_batch=batch, gpu_layer_slots=slots,
+                offload_dir=str(tmp_path))
+    api.start()
+    assert api.getKvPages() == LAYERS
+
+
+def slab(seed):
+    return kvgen.normal(seed, (PAGES, 2, HKV, 16, 128)).astype(np.float16)
+
+
+def test_tier_round_trips_preserve_bytes(engine):
+    E, api, tmp = engine
+    start(E, api, tmp)
+    data = [slab(100 + l) for l in range(LAYERS)]
+    for l in range(LAYERS):
+        E.load_layer(l, data[l])
+    assert api.moveKvToRam(0) > 0 and E.tier(0) == "RAM"
+    assert api.offloadKv(1) > 0 and E.tier(1) == "OFFLOADED"
+    assert api.moveKvToRam(1) > 0 and E.tier(1) == "RAM"
+    assert api.offloadKv(2) > 0 and E.tier(2) == "OFFLOADED"
+    for l in range(3):
+        assert api.moveKvToGpu(l) > 0 and E.tier(l) == "GPU"
+        back = np.empty_like(data[l])
+        E.read_layer(l, back)
+        assert np.array_equal(back.view(np.uint16), data[l].view(np.uint16)), l
+
+
+def test_compress_tier_matches_reference_codec(engine, oracle):
+    E, api, tmp = engine
+    start(E, api, tmp)
+    x = slab(7)
+    x.reshape(-1)[::997] *= np.float16(20)
+    E.load_layer(3, x)
+    assert api.compressKv(3) > 0 and E.tier(3) == "COMPRESSED"
+    assert api.moveKvToGpu(3) > 0 and E.tier(3) == "GPU"
+    back = np.empty_like(x)
+    E.read_layer(3, back)
+    codes, stats = oracle.compress_int8_blocks(x, 2048)
+    want = oracle.decompress_int8_blocks(codes, stats, 2048).astype(np.float16).reshape(x.shape)
+    assert np.array_equal(back.view(np.uint16), want.view(np.uint16))
+
+
+def test_lru_eviction_under_device_budget(engine):
+    E, api, tmp = engine
+    start(E, api, tmp, slots=2)
+    # layers 0,1 start on the device (stamps 0), 2,3 in RAM
+    stamp = {0: 0, 1: 0}
+    clock = 0
+    rng = np.random.default_rng(5)
+    for step in range(40):
+        l = int(rng.integers(0, LAYERS))
+        resident = {k for k in range(LAYERS) if E.tier(k) == "GPU"}
+        assert resident == set(stamp), step
+        want_victim = None
+        if l not in stamp and len(stamp) == 2:
+            want_victim = min(sorted(stamp), key=lambda k: stamp[k])  # min stamp, lowest index
+        clock += 1
+        assert api.moveKvToGpu(l) > 0
+        if want_victim is not None:
+            assert E.tier(want_victim) == "RAM", step
+            del stamp[want_victim]
+        stamp[l] = clock
+    assert api.keepLayer(0) >= 1  # pinned layers are never victims
+    for l in (1, 2, 3, 1, 2, 3):
+        assert api.moveKvToGpu(l) > 0
+        assert E.tier(0) == "GPU"
+    for _ in range(3):
+        E.lib.adaptive_engine_test_release_layer(0)
+
+
+def test_decode_step_through_host_buffers(engine, oracle):
+    E, api, tmp = engine
+    start(E, api, tmp, batch=4)
+    lens = np.array([0, 15, 40, 100], np.int32)
+    E.set_sequences(lens, reserve_tokens=20, seed=11)
+    bt = E.block_table(len(lens))
+    pools = [slab(300 + l) for l in range(LAYERS)]
+    for l in range(LAYERS):
+        E.load_layer(l, pools[l])
+    q = kvgen.normal(1, (LAYERS, 4, HQ, 128)).astype(np.float16)
+    k = kvgen.normal(2, (LAYERS, 4, HKV, 128)).astype(np.float16)
+    v = kvgen.normal(3, (LAYERS, 4, HKV, 128)).astype(np.float16)
+    out = np.zeros_like(q)
+    for step in range(2):
+        E.decode_step(q, k, v, out)
+        for l in range(LAYERS):
+            oracle.append(pools[l], bt, lens, k[l], v[l], 16)
+            ref = oracle.paged_decode(pools[l], bt, lens + 1, q[l].astype(np.float32))
+            got = out[l].astype(np.float32)
+            excess = np.abs(got - ref) - (ATOL + RTOL * np.abs(ref))
+            assert excess.max() <= 0, (step, l, excess.max())
+            back = np.empty_like(pools[l])
+            E.read_layer(l, back)
+            assert np.array_equal(back.view(np.uint16), pools[l].view(np.uint16)), (step, l)
+        lens = lens + 1
+        assert [E.lib.adaptive_engine_seq_len(s) for s in range(4)] == list(lens)
+
+
+def test_decode_step_with_layers_in_other_tiers(engine, oracle):
+    E, api, tmp = engine
+    start(E, api, tmp, slots=2, batch=2)
+    lens = np.array([33, 64], np.int32)
+    E.set_sequences(lens, reserve_tokens=4, seed=0)
+    bt = E.block_table(2)
+    pools = [slab(500 + l) for l in range(LAYERS)]
+    for l in range(LAYERS):
+        E.load_layer(l, pools[l])
+    assert api.offloadKv(1) > 0
+    q = kvgen.normal(4, (LAYERS, 2, HQ, 128)).astype(np.float16)
+    k = kvgen.normal(5, (LAYERS, 2, HKV, 128)).astype(np.float16)
+    v = kvgen.normal(6, (LAYERS, 2, HKV, 128)).astype(np.float16)
+    out = np.zeros_like(q)
+    E.decode_step(q, k, v, out)  # brings every layer through the two device slabs
+    for l in range(LAYERS):
+        oracle.append(pools[l], bt, lens, k[l], v[l], 16)
+        ref = oracle.paged_decode(pools[l], bt, lens + 1, q[l].astype(np.float32))
+        excess = np.abs(out[l].astype(np.float32) - ref) - (ATOL + RTOL * np.abs(ref))
+        assert excess.max() <= 0, l
