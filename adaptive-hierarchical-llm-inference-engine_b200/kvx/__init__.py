@@ -107,7 +107,10 @@ def _dtype_code(t):
 
 
 def paged(pool, stats=None) -> KvPaged:
-    """Describe one layer's pool tensor [pages][2][hkv][16][128]."""
+    """Describe one layer's pool: a CUDA tensor [pages][2][hkv][16][128], or
+    an existing KvPaged view (e.g. from kvx.engine.layer_view)."""
+    if isinstance(pool, KvPaged):
+        return pool
     assert pool.is_cuda and pool.is_contiguous() and pool.dim() == 5
     pages, two, hkv, pt, dim = pool.shape
     assert two == 2

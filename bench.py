@@ -119,6 +119,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import kvx
+    import kvx.engine as E
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -133,13 +134,24 @@ def run_ours(args):
     steps, warm = args.steps, args.warmup
     total_steps = steps + warm
 
+    # the engine owns the paged KV cache: one fp16 pool per layer, this
+    # rank's KV heads, sequences with seeded lengths and permuted pages
     lens0 = workload_lens()
-    bt_np, num_pages = kvgen.paged_layout(lens0, PT, total_steps, SEED + 1)
+    reserve = max(total_steps, 24)  # the e2e pass appends up to 17 more tokens
+    need_pages = int(((lens0 + reserve + PT - 1) // PT).sum())
+    E.configure(layers=LAYERS, kv_heads=hkv, q_heads=hq, max_batch=BATCH,
+                pages_per_layer=need_pages, gpu_layer_slots=LAYERS, device=local)
+    api = E.api()
+    api.start()
+    E.set_sequences(lens0.astype(np.int32), reserve_tokens=reserve, seed=SEED + 1)
+    bt_np = E.block_table(BATCH)
     max_pages = bt_np.shape[1]
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED + 17 * rank)
-    pools = [torch.randn((num_pages, 2, hkv, PT, DIM), generator=g, device="cuda",
-                         dtype=torch.float16) for _ in range(LAYERS)]
+    for l in range(LAYERS):  # N(0,1) fp16 context, generated on the device
+        E.load_layer(l, torch.randn((need_pages, 2, hkv, PT, DIM), generator=g, device="cuda",
+                                    dtype=torch.float16))
+    views = [E.layer_view(l) for l in range(LAYERS)]
     bt = torch.from_numpy(bt_np).cuda()
     q = torch.randn((LAYERS, BATCH, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
     nk = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
@@ -158,7 +170,7 @@ def run_ours(args):
         for l in range(LAYERS):
             if ev is not None:
                 ev[l][0].record()
-            kvx.append_decode(pools[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
+            kvx.append_decode(views[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
                               error_flag=err)
             if ev is not None:
                 ev[l][1].record()
@@ -189,7 +201,7 @@ def run_ours(args):
     time.sleep(0.3)
     t0.record()
     for k in range(steps):
-        step([(a, b) for (a, b) in ev[k]])
+        step(ev[k])
     t1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -211,7 +223,7 @@ def run_ours(args):
 
     # roofline of the decode kernel: algorithmic bytes per launch / mean launch time
     mean_layer_bytes = rank_bytes / (steps * LAYERS)
-    qo_bytes = 2 * BATCH * hq * DIM * 2 + BATCH * max_pages * 4 + BATCH * 4
+    qo_bytes = 2 * BATCH * hq * DIM * 2 + BATCH * max_pages * 4 + BATCH * 4 + 2 * BATCH * hkv * DIM * 2
     mean_dec_ms = sum(dec_ms) / len(dec_ms)
     achieved = (mean_layer_bytes + qo_bytes) / (mean_dec_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
@@ -234,13 +246,13 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (KV pool ~17 GB)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_kind": peak_kind, "kernel": "paged_decode_kernel (append + decode + split combine fused)",
+                     "peak_kind": peak_kind, "kernel": "tc_decode_kernel (append + decode + split combine fused)",
                      "mean_launch_us": round(mean_dec_ms * 1e3, 2)},
         "gpu_launches": steps * LAYERS,
         "clocks": clk,
     }
     if not args.no_e2e:
-        result["e2e"] = run_e2e(args, pools, bt, lens0, warm + steps, hq, hkv, ws, err, world)
+        result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -248,53 +260,40 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(sample_layers=1)
         print(json.dumps(result), flush=True)
+    api.stop()
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_e2e(args, pools, bt, lens0, start_step, hq, hkv, ws, err, world):
-    """Same step through the C ABI with host buffers: every step copies its
-    q / new K / new V for all layers from pinned host memory and reads the
-    attention outputs back, inside the timed region."""
+def run_e2e(args, E, lens0, hq, hkv, world):
+    """The same step through the engine's public C ABI with host buffers:
+    adaptive_engine_decode_step copies every layer's q / new K / new V from
+    pinned host memory, runs append + decode per layer and copies the
+    attention outputs back, all inside the timed region (wall clock around
+    the blocking call; the call returns when the outputs are on the host)."""
     import torch
-
-    import kvx
     steps = max(4, min(args.steps, 16))
     h_q = torch.randn((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
     h_k = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
     h_v = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
     h_o = torch.empty((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
-    d_q, d_k, d_v = (torch.empty_like(h, device="cuda") for h in (h_q, h_k, h_v))
-    d_o = torch.empty_like(h_o, device="cuda")
-    # replay the positions of the last `steps` device-resident steps (the
-    # pool has room for exactly warmup+steps appended tokens per sequence)
-    pos = torch.from_numpy((lens0 + start_step - steps).astype(np.int32)).cuda()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    E.decode_step(h_q, h_k, h_v, h_o)  # warm-up: the engine's sequences start at lens0
     torch.cuda.synchronize()
-    t0.record()
     nbytes = 0
+    t0 = time.perf_counter()
     for k in range(steps):
-        d_q.copy_(h_q, non_blocking=True)
-        d_k.copy_(h_k, non_blocking=True)
-        d_v.copy_(h_v, non_blocking=True)
-        for l in range(LAYERS):
-            kvx.append_decode(pools[l], bt, pos, d_k[l], d_v[l], d_q[l], out=d_o[l], workspace=ws,
-                              error_flag=err)
-        h_o.copy_(d_o, non_blocking=True)
-        nbytes += int((lens0 + start_step - steps + k + 1).sum()) * 2 * hkv * DIM * 2 * LAYERS
-        pos.add_(1)
-    t1.record()
-    torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
+        E.decode_step(h_q, h_k, h_v, h_o)
+        nbytes += int((lens0 + 2 + k).sum()) * 2 * hkv * DIM * 2 * LAYERS
+    secs = time.perf_counter() - t0
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([ms], device="cuda")
+        t = torch.tensor([secs], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    return {"value": round(nbytes * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+        secs = t.item()
+    return {"value": round(nbytes * world / secs / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2),
             "d2h_bytes_per_step": int(h_o.numel() * 2), "steps": steps,
-            "path": "kvx C ABI (ctypes) with pinned host buffers"}
+            "path": "adaptive_engine_decode_step (C ABI) with pinned host buffers"}
 
 
 # --------------------------------------------------------------------------
