@@ -238,9 +238,11 @@ __device__ __forceinline__ float f16_trunc_to_f32(uint16_t h) {
     return __uint_as_float(x);
 }
 
+// `vec`: both arrays 16 / 8-byte aligned, so four elements move per access;
+// otherwise every element is handled on its own.
 __global__ void __launch_bounds__(256)
-encode_trunc_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, size_t n) {
-    const size_t quads = n / 4;
+encode_trunc_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, size_t n, bool vec) {
+    const size_t quads = vec ? n / 4 : 0;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
         const float4 v = __ldcs(reinterpret_cast<const float4 *>(src) + i);
@@ -254,8 +256,8 @@ encode_trunc_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, s
 }
 
 __global__ void __launch_bounds__(256)
-decode_trunc_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, size_t n) {
-    const size_t quads = n / 4;
+decode_trunc_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, size_t n, bool vec) {
+    const size_t quads = vec ? n / 4 : 0;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
         const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src) + i);
@@ -324,15 +326,21 @@ extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *sta
 }
 
 extern "C" KVX_API int kvx_f32_to_f16_trunc(const float *src, uint16_t *dst, size_t n, void *stream) {
-    if (!src || !dst || !aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7)) return KVX_EINVAL;
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(dst) & 1))
+        return KVX_EINVAL;
     if (n == 0) return KVX_OK;
-    encode_trunc_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n);
+    const bool vec = aligned16(src) && !(reinterpret_cast<uintptr_t>(dst) & 7);
+    encode_trunc_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, dst, n, vec);
     return launch_status();
 }
 
 extern "C" KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, size_t n, void *stream) {
-    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 7) || !aligned16(dst)) return KVX_EINVAL;
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 1) || (reinterpret_cast<uintptr_t>(dst) & 3))
+        return KVX_EINVAL;
     if (n == 0) return KVX_OK;
-    decode_trunc_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, n);
+    const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
+    decode_trunc_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, dst, n, vec);
     return launch_status();
 }

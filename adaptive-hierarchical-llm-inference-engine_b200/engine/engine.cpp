@@ -92,7 +92,9 @@ void Engine::start() {
          cudaStreamCreateWithFlags(&copy_, cudaStreamNonBlocking) == cudaSuccess;
     const size_t qn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.q_heads * 128;
     const size_t kn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.kv_heads * 128;
-    ok = ok && cudaMalloc(&d_q_, qn * 2) == cudaSuccess && cudaMalloc(&d_out_, qn * 2) == cudaSuccess &&
+    // q / out also carry one layer of fp32 rows for decode_layer_f32
+    const size_t qbytes = std::max(qn * 2, (size_t)cfg_.max_batch * cfg_.q_heads * 128 * 4);
+    ok = ok && cudaMalloc(&d_q_, qbytes) == cudaSuccess && cudaMalloc(&d_out_, qbytes) == cudaSuccess &&
          cudaMalloc(&d_k_, kn * 2) == cudaSuccess && cudaMalloc(&d_v_, kn * 2) == cudaSuccess &&
          cudaMalloc(&d_pos_, cfg_.max_batch * sizeof(int32_t)) == cudaSuccess &&
          cudaMalloc(&d_err_, sizeof(int32_t)) == cudaSuccess && cudaMemset(d_err_, 0, 4) == cudaSuccess &&
@@ -604,6 +606,60 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     }
     for (int s = 0; s < B; ++s) ++lens_[s];
     return KVX_OK;
+}
+
+int Engine::decode_layer_f32(int layer, const float *q, const float *k, const float *v, float *out) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!valid(layer) || batch_ == 0 || !q || !k || !v || !out) return KVX_EINVAL;
+    for (int s = 0; s < batch_; ++s)
+        if (lens_[s] / 16 >= max_pages_ || table_[(size_t)s * max_pages_ + lens_[s] / 16] < 0)
+            return KVX_ENOSPC;
+    const int B = batch_, hq = cfg_.q_heads, hkv = cfg_.kv_heads;
+    const size_t qn = (size_t)B * hq * 128, kn = (size_t)B * hkv * 128;
+    std::vector<_Float16> k16(kn), v16(kn);  // round to nearest, as the pool stores it
+    for (size_t i = 0; i < kn; ++i) {
+        k16[i] = (_Float16)k[i];
+        v16[i] = (_Float16)v[i];
+    }
+    if (layers_[layer].tier != kGpu) {
+        const int r = to_gpu_locked(layer);
+        if (r < 0) return r;
+    }
+    layers_[layer].last_used = ++clock_;
+    // fp32 q / out share the step buffers' space (the fp16 step buffers hold
+    // twice the elements needed here)
+    float *dq = reinterpret_cast<float *>(d_q_), *dout = reinterpret_cast<float *>(d_out_);
+    memcpy(h_pos_, lens_.data(), B * sizeof(int32_t));
+    int rc = KVX_OK;
+    if (cudaMemcpyAsync(d_pos_, h_pos_, B * 4, cudaMemcpyHostToDevice, compute_) ||
+        cudaMemcpyAsync(dq, q, qn * 4, cudaMemcpyHostToDevice, compute_) ||
+        cudaMemcpyAsync(d_k_, k16.data(), kn * 2, cudaMemcpyHostToDevice, compute_) ||
+        cudaMemcpyAsync(d_v_, v16.data(), kn * 2, cudaMemcpyHostToDevice, compute_))
+        return KVX_ECUDA;
+    kvx_paged view{arena_ + (size_t)layers_[layer].slab * slab_bytes_, nullptr, KVX_F16,
+                   cfg_.pages_per_layer, hkv, 128, 16};
+    rc = kvx_append_decode(&view, d_table_, max_pages_, d_pos_, B, d_k_, d_v_, hq, dq, dout, KVX_F32, 0.f,
+                           d_ws_, ws_bytes_, d_err_, compute_);
+    if (rc) return rc;
+    int32_t err = 0;
+    if (cudaMemcpyAsync(out, dout, qn * 4, cudaMemcpyDeviceToHost, compute_) ||
+        cudaMemcpyAsync(&err, d_err_, 4, cudaMemcpyDeviceToHost, compute_) ||
+        cudaStreamSynchronize(compute_))
+        return KVX_ECUDA;
+    if (err) {
+        cudaMemset(d_err_, 0, 4);
+        return (err & 1) ? KVX_ETIMEOUT : KVX_EINVAL;
+    }
+    current_layer_ = layer;
+    if (layer == cfg_.layers - 1)
+        for (int s = 0; s < B; ++s) ++lens_[s];
+    return KVX_OK;
+}
+
+void Engine::config(adaptive_engine_config *cfg) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (started_ || configured_) *cfg = cfg_;
+    else default_config(cfg);
 }
 
 }  // namespace kvx_engine

@@ -64,6 +64,11 @@ public:
     int layer_tier(int layer);
     int set_sequences(int batch, const int32_t *lens, int reserve_tokens, uint64_t seed);
     int decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out);
+    // One layer of a step with fp32 host data: q [B][q_heads][128], new
+    // K/V [B][kv_heads][128] (rounded to the pool's fp16), out fp32.  The
+    // last layer advances the sequences.
+    int decode_layer_f32(int layer, const float *q, const float *k, const float *v, float *out);
+    void config(adaptive_engine_config *cfg);
     int32_t seq_len(int s);
     int copy_layer(int layer, void *ptr, bool load);
     int32_t block_table(int32_t *dst);

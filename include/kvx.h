@@ -153,11 +153,27 @@ KVX_API int kvx_decompress_int8(const int8_t *codes, const float *stats, void *d
                                 void *stream);
 
 /* Truncating fp32 -> fp16 of the disk tier.  Replaces float32_to_float16
- * (compression/kv_compress.cpp:6-25,48-53).  Bit-exact. */
+ * (compression/kv_compress.cpp:6-25,48-53).  Bit-exact.  Any naturally
+ * aligned arrays (4 elements per access when 16 / 8-byte aligned). */
 KVX_API int kvx_f32_to_f16_trunc(const float *src, uint16_t *dst, size_t n, void *stream);
 /* Inverse, subnormals to zero.  Replaces float16_to_float32
  * (compression/kv_compress.cpp:27-46,55-60).  Bit-exact. */
 KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, size_t n, void *stream);
+
+/* Row softmax of a dense [rows][cols] fp32 matrix (device pointers).
+ * Replaces the reference's softmax_row_kernel / cuda_softmax
+ * (runtime/gpu/cuda_executor.cu:149-184,224-244) with TensorOps::softmax
+ * semantics (runtime/tensor_ops.cpp:155-177, sum==0 -> 1e-6). */
+KVX_API int kvx_softmax_rows(const float *in, float *out, int64_t rows, int64_t cols, void *stream);
+
+/* Dense attention: out[i] = softmax(Q[i] . K^T * scale) V for seq_q query
+ * rows over seq_k keys, fp32 [rows][dim] device arrays, dim <= 1024,
+ * scale <= 0 -> 1/sqrt(dim).  Replaces the reference's cuda_attention
+ * (runtime/gpu/cuda_executor.cu:246-311) with the semantics of
+ * TensorOps::attention (runtime/tensor_ops.cpp:179-219). */
+KVX_API int kvx_attention_dense(const float *Q, const float *K, const float *V, float *out,
+                                int64_t seq_q, int64_t seq_k, int32_t dim, float scale,
+                                void *stream);
 
 /* LRU victim.  Replaces LRUEvictionPolicy::selectPageToEvict
  * (native-engine/cpp/AdvancedEvictionPolicy.cpp:9-23) and KVCacheGPU::findLRUPage

@@ -315,6 +315,11 @@ def test_f16_trunc_codec_bitexact(kvx):
     allh = dev(np.arange(65536, dtype=np.uint16).view(np.int16))
     dec = kvx.f16_trunc_to_f32(allh).cpu().numpy().view(np.uint32)
     assert np.array_equal(dec, g["dec_bits"])
+    # misaligned views take the element-wise path, same bits
+    enc_odd = kvx.f32_to_f16_trunc(dev(g["x"])[1:]).cpu().numpy().view(np.uint16)
+    assert np.array_equal(enc_odd, g["enc"][1:])
+    dec_odd = kvx.f16_trunc_to_f32(allh[3:]).cpu().numpy().view(np.uint32)
+    assert np.array_equal(dec_odd, g["dec_bits"][3:])
 
 
 # ------------------------------------------------------------- eviction ---
