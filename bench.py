@@ -157,8 +157,8 @@ def run_ours(args):
     nk = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
     nv = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
     out = torch.empty((LAYERS, BATCH, hq, DIM), device="cuda", dtype=torch.float16)
-    gathered = torch.empty((LAYERS, world, BATCH, hq, DIM), device="cuda", dtype=torch.float16) \
-        if world > 1 else None
+    gathered = torch.empty((LAYERS, world * BATCH, hq, DIM), device="cuda", dtype=torch.float16) \
+        if world > 1 else None  # per layer: [world][B][hq/world][D] -> kvx.shard.gathered_to_heads
     ws = kvx.decode_workspace(BATCH, hq, max_pages)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     pos = torch.from_numpy(lens0.astype(np.int32)).cuda()
