@@ -9,6 +9,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <dlfcn.h>
+
+#include <nccl.h>
 
 namespace kvx_engine {
 namespace {
@@ -33,7 +36,67 @@ uint64_t splitmix(uint64_t &x) {
     return z ^ (z >> 31);
 }
 
+// NCCL through dlopen: binds to the libnccl.so.2 the process already loaded
+// (torch's), else the system one; no link-time dependency.
+struct Nccl {
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    bool ok = false;
+};
+
+const Nccl &nccl() {
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return;
+        n.get_unique_id = reinterpret_cast<decltype(n.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        n.comm_init_rank = reinterpret_cast<decltype(n.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
+        n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        n.ok = n.get_unique_id && n.comm_init_rank && n.all_gather && n.comm_destroy;
+    });
+    return n;
+}
+
 }  // namespace
+
+int nccl_unique_id(void *id128) {
+    const Nccl &n = nccl();
+    if (!n.ok) return KVX_EUNSUPPORTED;
+    ncclUniqueId id;
+    if (n.get_unique_id(&id) != ncclSuccess) return KVX_ECUDA;
+    memcpy(id128, &id, sizeof(id));
+    return KVX_OK;
+}
+
+int Engine::set_comm(int rank, int world, const void *id128) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!started_ || world < 1 || rank < 0 || rank >= world || !id128) return KVX_EINVAL;
+    const Nccl &n = nccl();
+    if (!n.ok) return KVX_EUNSUPPORTED;
+    if (comm_) return KVX_EBUSY;
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof(id));
+    ncclComm_t c = nullptr;
+    if (n.comm_init_rank(&c, world, id, rank) != ncclSuccess) return KVX_ECUDA;
+    const size_t gbytes = (size_t)cfg_.layers * world * cfg_.max_batch * cfg_.q_heads * 128 * 2;
+    if (cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&d_gather_, gbytes) != cudaSuccess) {
+        n.comm_destroy(c);
+        return KVX_ECUDA;
+    }
+    ev_gath_.assign(cfg_.layers, nullptr);
+    for (auto &e : ev_gath_) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    device_bytes_ += (long long)gbytes;
+    comm_ = c;
+    world_ = world;
+    rank_ = rank;
+    return KVX_OK;
+}
 
 Engine &Engine::instance() {
     static Engine *e = new Engine();  // lives until exit; never destroyed mid-call
@@ -136,6 +199,17 @@ void Engine::start() {
 void Engine::release_all() {
     if (compute_) cudaStreamSynchronize(compute_);
     if (copy_) cudaStreamSynchronize(copy_);
+    if (comm_stream_) cudaStreamSynchronize(comm_stream_);
+    if (comm_) nccl().comm_destroy(static_cast<ncclComm_t>(comm_));
+    comm_ = nullptr;
+    world_ = 1;
+    rank_ = 0;
+    for (auto &e : ev_gath_) if (e) cudaEventDestroy(e);
+    ev_gath_.clear();
+    if (d_gather_) cudaFree(d_gather_);
+    d_gather_ = nullptr;
+    if (comm_stream_) cudaStreamDestroy(comm_stream_);
+    comm_stream_ = nullptr;
     for (size_t l = 0; l < layers_.size(); ++l) {
         Layer &L = layers_[l];
         if (L.host) cudaFreeHost(L.host);
@@ -590,13 +664,25 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                                d_v_ + l * kstride, hq, d_q_ + l * qstride, d_out_ + l * qstride,
                                KVX_F16, 0.f, d_ws_, ws_bytes_, d_err_, compute_);
         if (rc) break;
-        if (cudaEventRecord(ev_out_[l], compute_) || cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
-            cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
+        if (cudaEventRecord(ev_out_[l], compute_)) {
             rc = KVX_ECUDA;
+        } else if (comm_) {  // all-gather this layer's rows over NCCL, then read them back
+            uint16_t *g = d_gather_ + (size_t)l * world_ * qrow;
+            if (cudaStreamWaitEvent(comm_stream_, ev_out_[l], 0) ||
+                nccl().all_gather(d_out_ + l * qstride, g, qrow, ncclFloat16, static_cast<ncclComm_t>(comm_),
+                                  comm_stream_) != ncclSuccess ||
+                cudaEventRecord(ev_gath_[l], comm_stream_) || cudaStreamWaitEvent(copy_, ev_gath_[l], 0) ||
+                cudaMemcpyAsync(out + l * world_ * qrow, g, world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                rc = KVX_ECUDA;
+        } else if (cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
+                   cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_)) {
+            rc = KVX_ECUDA;
+        }
         current_layer_ = l;
     }
     int32_t err = 0;
     if (cudaStreamSynchronize(compute_) != cudaSuccess || cudaStreamSynchronize(copy_) != cudaSuccess ||
+        (comm_stream_ && cudaStreamSynchronize(comm_stream_) != cudaSuccess) ||
         cudaMemcpy(&err, d_err_, sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
         return KVX_ECUDA;
     if (rc) return rc;

@@ -71,6 +71,7 @@ public:
     void config(adaptive_engine_config *cfg);
     int32_t seq_len(int s);
     int copy_layer(int layer, void *ptr, bool load);
+    int set_comm(int rank, int world, const void *id128);
     int32_t block_table(int32_t *dst);
     long long device_bytes();
 
@@ -114,6 +115,15 @@ private:
     size_t ws_bytes_ = 0;
     uint16_t *d_q_ = nullptr, *d_k_ = nullptr, *d_v_ = nullptr, *d_out_ = nullptr;
     long long device_bytes_ = 0;
+    // NCCL all-gather of the attention outputs (multi-GPU)
+    void *comm_ = nullptr;  // ncclComm_t
+    int world_ = 1, rank_ = 0;
+    cudaStream_t comm_stream_ = nullptr;
+    uint16_t *d_gather_ = nullptr;
+    std::vector<cudaEvent_t> ev_gath_;
 };
+
+// NCCL entry points, resolved at run time.
+int nccl_unique_id(void *id128);
 
 }  // namespace kvx_engine

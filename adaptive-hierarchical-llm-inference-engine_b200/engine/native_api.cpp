@@ -71,6 +71,14 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_read_layer(int layer, void *dst) {
     return Engine::instance().copy_layer(layer, dst, false);
 }
 
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_nccl_unique_id(void *id128) {
+    return id128 ? kvx_engine::nccl_unique_id(id128) : KVX_EINVAL;
+}
+
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const void *id128) {
+    return Engine::instance().set_comm(rank, world, id128);
+}
+
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_block_table(int32_t *dst) {
     return Engine::instance().block_table(dst);
 }

@@ -52,6 +52,10 @@ lib.adaptive_engine_read_layer.argtypes = [C.c_int, C.c_void_p]
 lib.adaptive_engine_read_layer.restype = C.c_int
 lib.adaptive_engine_block_table.argtypes = [C.c_void_p]
 lib.adaptive_engine_block_table.restype = C.c_int32
+lib.adaptive_engine_nccl_unique_id.argtypes = [C.c_void_p]
+lib.adaptive_engine_nccl_unique_id.restype = C.c_int
+lib.adaptive_engine_set_comm.argtypes = [C.c_int, C.c_int, C.c_void_p]
+lib.adaptive_engine_set_comm.restype = C.c_int
 
 TIERS = {0: "GPU", 1: "RAM", 2: "COMPRESSED", 3: "OFFLOADED"}
 
@@ -125,3 +129,18 @@ def block_table(batch: int) -> np.ndarray:
     out = np.empty((batch, max(mp, 1)), np.int32)
     lib.adaptive_engine_block_table(out.ctypes.data)
     return out
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_char * 128)()
+    rc = lib.adaptive_engine_nccl_unique_id(buf)
+    if rc != 0:
+        raise KvxError("adaptive_engine_nccl_unique_id", rc)
+    return bytes(buf)
+
+
+def set_comm(rank: int, world: int, uid: bytes):
+    buf = (C.c_char * 128).from_buffer_copy(uid)
+    rc = lib.adaptive_engine_set_comm(rank, world, buf)
+    if rc != 0:
+        raise KvxError("adaptive_engine_set_comm", rc)

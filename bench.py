@@ -6,8 +6,9 @@ lengths U[512, 8192] (seeded) and randomly permuted physical pages, append
 one token per sequence into its page, then run paged GQA decode attention
 over the whole context.  Metric: KV bytes read by decode per second (GB/s),
 whole job.  With --gpus N the KV heads are sharded over N ranks (each rank
-owns 8/N heads and the matching q-heads) and the attention outputs are
-all-gathered over NCCL each layer; total work is fixed (strong scaling).
+owns 8/N heads and the matching q-heads, for all sequences) and the
+attention outputs are all-gathered over NCCL each layer; the batch grows to
+32*N sequences so every GPU reads the same bytes per step (weak scaling).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -109,8 +110,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def workload_lens():
-    return kvgen.randint(SEED, BATCH, CTX_LO, CTX_HI).astype(np.int64)
+def workload_lens(batch=BATCH):
+    # the first 32 values of the stream are the same for every batch size
+    return kvgen.randint(SEED, batch, CTX_LO, CTX_HI).astype(np.int64)
 
 
 # --------------------------------------------------------------------------
@@ -131,20 +133,21 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     assert HKV % world == 0, "KV heads must divide evenly over the GPUs"
     hkv, hq = HKV // world, HQ // world
+    B = BATCH * world
     steps, warm = args.steps, args.warmup
     total_steps = steps + warm
 
     # the engine owns the paged KV cache: one fp16 pool per layer, this
     # rank's KV heads, sequences with seeded lengths and permuted pages
-    lens0 = workload_lens()
+    lens0 = workload_lens(B)
     reserve = max(total_steps, 24)  # the e2e pass appends up to 17 more tokens
     need_pages = int(((lens0 + reserve + PT - 1) // PT).sum())
-    E.configure(layers=LAYERS, kv_heads=hkv, q_heads=hq, max_batch=BATCH,
+    E.configure(layers=LAYERS, kv_heads=hkv, q_heads=hq, max_batch=B,
                 pages_per_layer=need_pages, gpu_layer_slots=LAYERS, device=local)
     api = E.api()
     api.start()
     E.set_sequences(lens0.astype(np.int32), reserve_tokens=reserve, seed=SEED + 1)
-    bt_np = E.block_table(BATCH)
+    bt_np = E.block_table(B)
     max_pages = bt_np.shape[1]
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED + 17 * rank)
@@ -153,13 +156,13 @@ def run_ours(args):
                                     dtype=torch.float16))
     views = [E.layer_view(l) for l in range(LAYERS)]
     bt = torch.from_numpy(bt_np).cuda()
-    q = torch.randn((LAYERS, BATCH, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
-    nk = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
-    nv = torch.randn((LAYERS, BATCH, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
-    out = torch.empty((LAYERS, BATCH, hq, DIM), device="cuda", dtype=torch.float16)
-    gathered = torch.empty((LAYERS, world * BATCH, hq, DIM), device="cuda", dtype=torch.float16) \
+    q = torch.randn((LAYERS, B, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nk = torch.randn((LAYERS, B, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nv = torch.randn((LAYERS, B, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    out = torch.empty((LAYERS, B, hq, DIM), device="cuda", dtype=torch.float16)
+    gathered = torch.empty((LAYERS, world * B, hq, DIM), device="cuda", dtype=torch.float16) \
         if world > 1 else None  # per layer: [world][B][hq/world][D] -> kvx.shard.gathered_to_heads
-    ws = kvx.decode_workspace(BATCH, hq, max_pages)
+    ws = kvx.decode_workspace(B, hq, max_pages)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     pos = torch.from_numpy(lens0.astype(np.int32)).cuda()
     comm = torch.cuda.Stream() if world > 1 else None
@@ -223,7 +226,7 @@ def run_ours(args):
 
     # roofline of the decode kernel: algorithmic bytes per launch / mean launch time
     mean_layer_bytes = rank_bytes / (steps * LAYERS)
-    qo_bytes = 2 * BATCH * hq * DIM * 2 + BATCH * max_pages * 4 + BATCH * 4 + 2 * BATCH * hkv * DIM * 2
+    qo_bytes = 2 * B * hq * DIM * 2 + B * max_pages * 4 + B * 4 + 2 * B * hkv * DIM * 2
     mean_dec_ms = sum(dec_ms) / len(dec_ms)
     achieved = (mean_layer_bytes + qo_bytes) / (mean_dec_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
@@ -238,9 +241,10 @@ def run_ours(args):
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(t_max / steps, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (seeded N(0,1) K/V/Q, seeded context lengths and page permutation)",
-        "config": {"workload": WORKLOAD, "layers": LAYERS, "batch": BATCH, "kv_heads": HKV,
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "batch": B, "batch_per_gpu_equiv": BATCH,
+                   "kv_heads": HKV,
                    "q_heads": HQ, "head_dim": DIM, "page_tokens": PT,
                    "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
                    "l2": "inputs larger than L2 (KV pool ~17 GB)"},
@@ -252,7 +256,7 @@ def run_ours(args):
         "clocks": clk,
     }
     if not args.no_e2e:
-        result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world)
+        result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -265,20 +269,28 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_e2e(args, E, lens0, hq, hkv, world):
+def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
     """The same step through the engine's public C ABI with host buffers:
     adaptive_engine_decode_step copies every layer's q / new K / new V from
-    pinned host memory, runs append + decode per layer and copies the
-    attention outputs back, all inside the timed region (wall clock around
-    the blocking call; the call returns when the outputs are on the host)."""
+    pinned host memory, runs append + decode per layer, all-gathers the
+    layer's attention output over NCCL when there are several GPUs, and
+    copies the (gathered) outputs back, all inside the timed region (wall
+    clock around the blocking call, max over ranks)."""
     import torch
+    if world > 1:
+        import torch.distributed as dist
+        uid = [E.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        E.set_comm(rank, world, uid[0])
     steps = max(4, min(args.steps, 16))
-    h_q = torch.randn((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
-    h_k = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
-    h_v = torch.randn((LAYERS, BATCH, hkv, DIM), dtype=torch.float16).pin_memory()
-    h_o = torch.empty((LAYERS, BATCH, hq, DIM), dtype=torch.float16).pin_memory()
+    h_q = torch.randn((LAYERS, B, hq, DIM), dtype=torch.float16).pin_memory()
+    h_k = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
+    h_v = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
+    h_o = torch.empty((LAYERS, world, B, hq, DIM), dtype=torch.float16).pin_memory()
     E.decode_step(h_q, h_k, h_v, h_o)  # warm-up: the engine's sequences start at lens0
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     nbytes = 0
     t0 = time.perf_counter()
     for k in range(steps):
@@ -286,14 +298,14 @@ def run_e2e(args, E, lens0, hq, hkv, world):
         nbytes += int((lens0 + 2 + k).sum()) * 2 * hkv * DIM * 2 * LAYERS
     secs = time.perf_counter() - t0
     if world > 1:
-        import torch.distributed as dist
         t = torch.tensor([secs], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         secs = t.item()
     return {"value": round(nbytes * world / secs / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2),
             "d2h_bytes_per_step": int(h_o.numel() * 2), "steps": steps,
-            "path": "adaptive_engine_decode_step (C ABI) with pinned host buffers"}
+            "path": "adaptive_engine_decode_step (C ABI) with pinned host buffers" +
+                    (", NCCL all-gather of outputs in the engine" if world > 1 else "")}
 
 
 # --------------------------------------------------------------------------

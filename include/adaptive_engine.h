@@ -120,6 +120,16 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_read_layer(int layer, void *dst);
  * length) and, when dst != NULL, copies batch * max_pages int32 physical
  * page ids (-1 = unassigned). */
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_block_table(int32_t *dst);
+/* Multi-GPU: one process per GPU, each engine holding its KV-head shard
+ * (kv_heads / q_heads of the config are the local counts).  Rank 0 makes a
+ * 128-byte NCCL unique id, every rank passes it to set_comm after start();
+ * from then on adaptive_engine_decode_step all-gathers each layer's
+ * attention output over NCCL (NVLink) and `out` receives
+ * [layers][world][batch][q_heads][head_dim].  NCCL is loaded at run time
+ * (dlopen of libnccl.so.2, binding to the copy the process already has).
+ * Return kvx_status (KVX_EUNSUPPORTED if NCCL cannot be loaded). */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_nccl_unique_id(void *id128);
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const void *id128);
 /* Current context length of sequence s (-1 if none). */
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_seq_len(int32_t s);
 /* Tier of layer l: 0 GPU, 1 RAM, 2 COMPRESSED (int8 on device),
