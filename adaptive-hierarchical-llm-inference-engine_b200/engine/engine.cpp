@@ -627,7 +627,7 @@ int Engine::set_sequences(int batch, const int32_t *lens, int reserve_tokens, ui
 
 int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out) {
     std::lock_guard<std::mutex> lk(mu_);
-    if (!started_ || batch_ == 0 || !q || !k || !v || !out) return KVX_EINVAL;
+    if (!started_ || batch_ == 0 || !q || !k || !v) return KVX_EINVAL;
     for (int s = 0; s < batch_; ++s)  // every sequence needs a page for its next token
         if (lens_[s] / 16 >= max_pages_ || table_[(size_t)s * max_pages_ + lens_[s] / 16] < 0)
             return KVX_ENOSPC;
@@ -671,11 +671,14 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
             if (cudaStreamWaitEvent(comm_stream_, ev_out_[l], 0) ||
                 nccl().all_gather(d_out_ + l * qstride, g, qrow, ncclFloat16, static_cast<ncclComm_t>(comm_),
                                   comm_stream_) != ncclSuccess ||
-                cudaEventRecord(ev_gath_[l], comm_stream_) || cudaStreamWaitEvent(copy_, ev_gath_[l], 0) ||
-                cudaMemcpyAsync(out + l * world_ * qrow, g, world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                cudaEventRecord(ev_gath_[l], comm_stream_) ||
+                (out && (cudaStreamWaitEvent(copy_, ev_gath_[l], 0) ||
+                         cudaMemcpyAsync(out + l * world_ * qrow, g, world_ * qrow * 2, cudaMemcpyDeviceToHost,
+                                         copy_))))
                 rc = KVX_ECUDA;
-        } else if (cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
-                   cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_)) {
+        } else if (out && (cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
+                           cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost,
+                                           copy_))) {
             rc = KVX_ECUDA;
         }
         current_layer_ = l;

@@ -96,8 +96,11 @@ def set_sequences(lens, reserve_tokens=0, seed=0):
 
 
 def decode_step(q, k, v, out):
-    """q/k/v/out: host buffers (numpy fp16 or pinned torch CPU tensors)."""
+    """q/k/v/out: host buffers (numpy fp16 or pinned torch CPU tensors); out
+    may be None (no read-back)."""
     def ptr(a):
+        if a is None:
+            return None
         return a.ctypes.data if isinstance(a, np.ndarray) else a.data_ptr()
     rc = lib.adaptive_engine_decode_step(ptr(q), ptr(k), ptr(v), ptr(out))
     if rc != 0:

@@ -106,7 +106,8 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_sequences(int32_t batch, const in
  * [layers][batch][q_heads][head_dim], new K and V [layers][batch][kv_heads]
  * [head_dim] (fp16 bits) to the device, append the token and run paged GQA
  * decode per layer, copy the attention output [layers][batch][q_heads]
- * [head_dim] back.  Copies overlap the layers' kernels (side stream, one
+ * [head_dim] back (skipped when out is NULL, e.g. on all but one rank of a
+ * multi-GPU job).  Copies overlap the layers' kernels (side stream, one
  * event per layer).  Returns a kvx_status. */
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_decode_step(const uint16_t *q, const uint16_t *k,
                                                        const uint16_t *v, uint16_t *out);
