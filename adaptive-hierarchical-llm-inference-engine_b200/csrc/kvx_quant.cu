@@ -101,7 +101,31 @@ __device__ __forceinline__ void finish_stats(MinMax r, float first, float *stats
     if (lane == 0) *reinterpret_cast<float4 *>(stats) = make_float4(r.mn, r.mx, sc, r.mn);
 }
 
+// Plain widening for the shortcut (a NaN only has to stay NaN there).
+template <typename T> __device__ __forceinline__ float ld_raw(const T *p, int i);
+template <> __device__ __forceinline__ float ld_raw<float>(const float *p, int i) { return p[i]; }
+template <> __device__ __forceinline__ float ld_raw<__half>(const __half *p, int i) { return __half2float(p[i]); }
+
+// Distance from a half-integer below which the reciprocal shortcut defers to
+// the exact division.  For a finite block every quotient is <= 255 * (1 +
+// 2^-23); t = RN(RN(x - mn) * RN(1/scale)) is then within 255 * 2^-23 <
+// 3.1e-5 of (x - mn) / scale and RN((x - mn) / scale) within 2^-17 < 7.7e-6
+// of it, so when |t - rint(t)| <= 0.5 - 4e-5 both round to rint(t).
+constexpr float kTieLimit = 0.5f - 4.0e-5f;
+constexpr float kTwo23 = 8388608.0f;  // t + 2^23: rint(t) in the low mantissa bits
+
+__device__ __forceinline__ float max_nan(float a, float b) {  // NaN wins
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 // Fast path: 2048-element blocks, 16-byte vectors, block kept in registers.
+// min / max first by value alone (fp16 pairs for fp16 input), NaN-skipping;
+// only when a result is +-0 -- the one tie whose bits differ -- does a
+// second pass pick the first such element in index order.  Codes come from
+// the reciprocal shortcut above; a lane holding a near-tie or a NaN then
+// rewrites those codes with the exact division (quant_one).
 template <typename T>
 __global__ void __launch_bounds__(256)
 compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
@@ -118,43 +142,92 @@ compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
 #pragma unroll
         for (int j = 0; j < kVecs; ++j)
             w[j] = __ldcs(reinterpret_cast<const uint4 *>(in) + j * 32 + lane);
-        MinMax a{CUDART_INF_F, -CUDART_INF_F, 1 << 30, 1 << 30};
-        float f[kPerVec];
+        float mn, mx;
+        if constexpr (sizeof(T) == 2) {
+            __half2 lo = reinterpret_cast<const __half2 *>(&w[0])[0], hi = lo;
 #pragma unroll
-        for (int j = 0; j < kVecs; ++j) {
-            const T *e = reinterpret_cast<const T *>(&w[j]);
+            for (int j = 0; j < kVecs; ++j) {
+                const __half2 *h = reinterpret_cast<const __half2 *>(&w[j]);
 #pragma unroll
-            for (int k = 0; k < kPerVec; ++k) f[k] = ld_elem<T>(e, k);
-            const int base = (j * 32 + lane) * kPerVec;
-#pragma unroll
-            for (int k = 0; k < kPerVec; ++k) mm_take(a, f[k], base + k);
-        }
-        // +-inf initial values: if every element is NaN or the block is all
-        // +inf / -inf, the index stays 1<<30 and the value is the sentinel;
-        // restore the reference's in[0]-seeded result in that case.
-        const float first = ld_elem<T>(in, 0);
-        a = mm_warp_reduce(a);
-        if (a.imn == (1 << 30)) a.mn = first;
-        if (a.imx == (1 << 30)) a.mx = first;
-        float mn, scale;
-        finish_stats(a, first, stats + 4 * b, lane, mn, scale);
-        int8_t *out = codes + b * kBlock;
-#pragma unroll
-        for (int j = 0; j < kVecs; ++j) {
-            const T *e = reinterpret_cast<const T *>(&w[j]);
-            if constexpr (kPerVec == 8) {
-                uint2 packed;
-                int8_t *c = reinterpret_cast<int8_t *>(&packed);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) c[k] = quant_one(ld_elem<T>(e, k), mn, scale);
-                __stcs(reinterpret_cast<uint2 *>(out) + j * 32 + lane, packed);
-            } else {
-                uint32_t packed;
-                int8_t *c = reinterpret_cast<int8_t *>(&packed);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) c[k] = quant_one(ld_elem<T>(e, k), mn, scale);
-                __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, packed);
+                for (int k = 0; k < 4; ++k) {
+                    lo = __hmin2(lo, h[k]);
+                    hi = __hmax2(hi, h[k]);
+                }
             }
+            mn = fminf(__low2float(lo), __high2float(lo));
+            mx = fmaxf(__low2float(hi), __high2float(hi));
+        } else {
+            mn = CUDART_INF_F;
+            mx = -CUDART_INF_F;
+#pragma unroll
+            for (int j = 0; j < kVecs; ++j) {
+                const float *e = reinterpret_cast<const float *>(&w[j]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    mn = fminf(mn, e[k]);
+                    mx = fmaxf(mx, e[k]);
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        }
+        const float first = ld_elem<T>(in, 0);
+        MinMax a{mn, mx, 0, 0};
+        if (mn != mn) {  // every element NaN: the reference keeps in[0]
+            a.mn = a.mx = first;
+        } else if (mn == 0.f || mx == 0.f) {  // +-0 ties: first in index order
+            MinMax z{CUDART_INF_F, -CUDART_INF_F, 1 << 30, 1 << 30};
+#pragma unroll 1
+            for (int i = lane; i < kBlock; i += 32) mm_take(z, ld_elem<T>(in, i), i);
+            a = mm_warp_reduce(z);
+        }
+        float mnv, scale;
+        finish_stats(a, first, stats + 4 * b, lane, mnv, scale);
+        const float rcp = __frcp_rn(scale);
+        int8_t *out = codes + b * kBlock;
+        if (isfinite(scale) && isfinite(rcp)) {  // warp-uniform; mn, mx finite too
+            float worst = 0.f;
+#pragma unroll
+            for (int j = 0; j < kVecs; ++j) {
+                const T *e = reinterpret_cast<const T *>(&w[j]);
+                uint32_t word[kPerVec / 4];
+#pragma unroll
+                for (int k4 = 0; k4 < kPerVec / 4; ++k4) {
+                    uint32_t u[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float t = __fmul_rn(__fsub_rn(ld_raw<T>(e, 4 * k4 + k), mnv), rcp);
+                        const float s = __fadd_rn(t, kTwo23);
+                        worst = max_nan(worst, fabsf(__fsub_rn(t, __fsub_rn(s, kTwo23))));
+                        u[k] = __float_as_uint(s);
+                    }
+                    word[k4] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
+                                           0x5410) ^ 0x80808080u;
+                }
+                if constexpr (kPerVec == 8)
+                    __stcs(reinterpret_cast<uint2 *>(out) + j * 32 + lane, make_uint2(word[0], word[1]));
+                else
+                    __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0]);
+            }
+            if (!(worst <= kTieLimit)) {  // rare: near-ties or NaN in this lane
+#pragma unroll 1
+                for (int j = 0; j < kVecs; ++j) {
+                    const int base = (j * 32 + lane) * kPerVec;
+#pragma unroll 1
+                    for (int k = 0; k < kPerVec; ++k) {
+                        const float x = ld_elem<T>(in, base + k);
+                        const float t = __fmul_rn(__fsub_rn(x, mnv), rcp);
+                        if (!(fabsf(__fsub_rn(t, rintf(t))) <= kTieLimit))
+                            out[base + k] = quant_one(x, mnv, scale);
+                    }
+                }
+            }
+        } else {  // inf / NaN range or denormal scale: exact division throughout
+#pragma unroll 1
+            for (int i = lane; i < kBlock; i += 32) out[i] = quant_one(ld_elem<T>(in, i), mnv, scale);
         }
     }
 }
@@ -186,6 +259,50 @@ __device__ __forceinline__ float dequant_one(int8_t c, float zp, float scale) {
     const float q = (float)((int32_t)c + 128);
     const float m = x86_nan(__fmul_rn(q, scale), q, scale);
     return x86_nan(__fadd_rn(zp, m), zp, m);
+}
+
+// Warp per 2048-element block: stats read once, 16 codes per lane-load,
+// NaN rebuild only for blocks whose scale or zero point is not finite.
+template <typename T>
+__global__ void __launch_bounds__(256)
+decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict__ stats,
+                       T *__restrict__ dst, size_t num_blocks) {
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
+         b += warps) {
+        const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
+        const float scale = st.z, zp = st.w;
+        const bool finite = isfinite(scale) && isfinite(zp);
+        const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 2048);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // 4 x 16 codes per lane
+            const uint4 w = __ldcs(src + j * 32 + lane);
+            const int8_t *c = reinterpret_cast<const int8_t *>(&w);
+            float v[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float q = (float)((int32_t)c[k] + 128);
+                v[k] = finite ? __fadd_rn(zp, __fmul_rn(q, scale)) : dequant_one(c[k], zp, scale);
+            }
+            const size_t e0 = (size_t)b * 2048 + (size_t)(j * 32 + lane) * 16;
+            if constexpr (sizeof(T) == 4) {
+                float4 *o = reinterpret_cast<float4 *>(dst + e0);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) __stcs(o + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+            } else {
+                uint4 o[2];
+                uint32_t *u = reinterpret_cast<uint32_t *>(o);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+                    u[k] = *reinterpret_cast<uint32_t *>(&h);
+                }
+                __stcs(reinterpret_cast<uint4 *>(dst + e0), o[0]);
+                __stcs(reinterpret_cast<uint4 *>(dst + e0) + 1, o[1]);
+            }
+        }
+    }
 }
 
 // One thread per 4 codes; block_elems % 4 == 0.
@@ -317,6 +434,14 @@ extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *sta
         return KVX_EINVAL;
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (block_elems == 2048 && aligned16(codes)) {
+        const unsigned grid = grid_for(num_blocks, 8);
+        if (dst_dtype == KVX_F32)
+            decompress_2048_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+        else
+            decompress_2048_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+        return launch_status();
+    }
     const unsigned grid = grid_for(num_blocks * (size_t)(block_elems / 4), 256);
     if (dst_dtype == KVX_F32)
         decompress_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);

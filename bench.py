@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 5],
+                    help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     return ap.parse_args()
 
 
@@ -396,12 +398,225 @@ def run_reference(args):
     }), flush=True)
 
 
+# --------------------------------------------------------------------------
+def _events_time(fn, iters, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters  # ms
+
+
+def run_config1(args):
+    """One layer of Llama-3.2-3B attention geometry (24 q / 8 kv heads x 128),
+    fp32, batch 1: 1024 tokens appended one at a time into 16-token pages
+    (sequential physical pages), then one decode for a fresh query."""
+    import torch
+    import kvx
+    T = 1024
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)
+    pool = torch.zeros((T // PT, 2, HKV, PT, DIM), device="cuda", dtype=torch.float32)
+    bt = torch.arange(T // PT, dtype=torch.int32, device="cuda").view(1, -1)
+    rows = torch.randn((T, 2, 1, HKV, DIM), generator=g, device="cuda", dtype=torch.float32)
+    pos = [torch.tensor([t], dtype=torch.int32, device="cuda") for t in range(T)]
+    q = torch.randn((1, HQ, DIM), generator=g, device="cuda", dtype=torch.float32)
+    lens = torch.tensor([T], dtype=torch.int32, device="cuda")
+    ws = kvx.decode_workspace(1, HQ, T // PT)
+
+    def appends():
+        for t in range(T):
+            kvx.append(pool, bt, pos[t], rows[t, 0], rows[t, 1])
+    ms_app = _events_time(appends, 5, 1)
+    ms_dec = _events_time(lambda: kvx.decode(pool, bt, lens, q, workspace=ws), 200)
+    kv_bytes = T * 2 * HKV * DIM * 4
+    print(json.dumps({"config": 1, "workload": "1 layer, 24q/8kv x128, fp32, B1, 1024 tokens appended one by one, then decode",
+                      "append_tokens_per_s": round(T / (ms_app / 1e3), 1),
+                      "append_us_per_token": round(ms_app * 1e3 / T, 2),
+                      "decode_us": round(ms_dec * 1e3, 2),
+                      "decode_GBps": round(kv_bytes / (ms_dec / 1e3) / 1e9, 1),
+                      "note": "latency-bound: one launch per token, 8 MiB of K/V per decode"}), flush=True)
+
+
+def run_config3(args):
+    """compressKv round trip: 1,048,576 pages of 16 tokens x 8 KV heads x 128
+    fp16 (N(0,1), 1% of elements x20), quantised per (page, head) block with
+    the reference's int8 scheme, dequantised, then decode (batch 32, context
+    4096, 24 q-heads) reading the int8 pages with fused dequantisation."""
+    import torch
+    import kvx
+    peak, peak_kind = peaks()
+    pages = 1 << 20
+    blocks = pages * HKV  # one (page, head) block of 2048 elements
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 3)
+    x = torch.empty((blocks, PT * DIM), device="cuda", dtype=torch.float16)
+    for c in range(0, blocks, 1 << 20):  # fill in chunks (bounded temporaries)
+        part = torch.randn((min(1 << 20, blocks - c), PT * DIM), generator=g, device="cuda")
+        mask = torch.rand(part.shape, generator=g, device="cuda") < 0.01
+        part[mask] *= 20.0
+        x[c:c + part.shape[0]] = part.half()
+        del part, mask
+    codes = torch.empty((blocks, PT * DIM), device="cuda", dtype=torch.int8)
+    stats = torch.empty((blocks, 4), device="cuda", dtype=torch.float32)
+    back = torch.empty_like(x)
+    ms_c = _events_time(lambda: kvx.compress_int8(x, codes=codes, stats=stats), 5)
+    ms_d = _events_time(lambda: kvx.decompress_int8(codes, stats, dtype=torch.float16, out=back), 5)
+    err = True  # |x - dequant(quant(x))| <= scale/2 per block (fp32 dequant), in chunks
+    for c in range(0, blocks, 1 << 20):
+        part = kvx.decompress_int8(codes[c:c + (1 << 20)], stats[c:c + (1 << 20)]).view(-1, PT * DIM)
+        e = (part - x[c:c + (1 << 20)].float()).abs().amax(dim=1)
+        err = err and bool((e <= stats[c:c + (1 << 20), 2] * 0.5001 + 1e-6).all().item())
+        del part, e
+    n = x.numel()
+    c_bytes = n * 2 + n + blocks * 16
+    d_bytes = n + blocks * 16 + n * 2
+    del back
+    # decode over int8 pages: batch 32, context 4096, one layer, 24 q-heads
+    B, T = 32, 4096
+    npg = T // PT
+    lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
+    # the 1,048,576 K-or-V pages pair up into 524,288 (K, V) pages of the pool layout
+    kv_pages = pages // 2
+    pool = codes.view(kv_pages, 2, HKV, PT, DIM)
+    pstats = stats.view(kv_pages, 2, HKV, 4)
+    bt = torch.randperm(kv_pages, generator=g, device="cuda")[: B * npg].to(torch.int32).view(B, npg).contiguous()
+    q = torch.randn((B, HQ, DIM), generator=g, device="cuda", dtype=torch.float16)
+    ws = kvx.decode_workspace(B, HQ, npg)
+    ms_q = _events_time(lambda: kvx.decode(pool, bt, lens, q, stats=pstats, workspace=ws), 20)
+    q_bytes = B * T * 2 * HKV * DIM * 1 + B * npg * 2 * HKV * 16
+    cpu = cpu_compress_baseline()
+    print(json.dumps({
+        "config": 3, "workload": "1,048,576 pages x 16 tok x 8 heads x 128 fp16, 1% outliers x20; int8 per (page, head)",
+        "compress": {"GBps": round(c_bytes / (ms_c / 1e3) / 1e9, 1), "ms": round(ms_c, 3),
+                     "frac_of_peak": round(c_bytes / (ms_c / 1e3) / 1e9 / peak, 3)},
+        "decompress": {"GBps": round(d_bytes / (ms_d / 1e3) / 1e9, 1), "ms": round(ms_d, 3),
+                       "frac_of_peak": round(d_bytes / (ms_d / 1e3) / 1e9 / peak, 3)},
+        "roundtrip_error_within_scale_half": bool(err),
+        "int8_decode": {"GBps": round(q_bytes / (ms_q / 1e3) / 1e9, 1), "us": round(ms_q * 1e3, 1),
+                        "batch": B, "context": T, "frac_of_peak": round(q_bytes / (ms_q / 1e3) / 1e9 / peak, 3)},
+        "peak": peak, "peak_kind": peak_kind, "cpu_baseline": cpu}), flush=True)
+
+
+def cpu_compress_baseline(blocks=16384):
+    """KVCompressionEngine INT8 (oracle/_ref, the reference's code) per
+    2048-element block over all host threads, on a sample of blocks."""
+    try:
+        from oracle import Reference
+        R = Reference()
+    except Exception as e:
+        return {"unavailable": str(e)[:120]}
+    threads = os.cpu_count() or 1
+    x = np.random.default_rng(SEED).standard_normal((blocks, 2048), dtype=np.float32)
+    codes = np.empty((blocks, 2048), np.int8)
+    stats = np.empty((blocks, 4), np.float32)
+    secs = R.L.kvref_time_compress(x, codes, stats, blocks, 2048, threads)
+    # same byte accounting as the GPU (fp16 in: the reference takes fp32)
+    gbps = blocks * (2048 * 2 + 2048 + 16) / secs / 1e9
+    return {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"{blocks} blocks of 2048 through KVCompressionEngine::compress(INT8)"}
+
+
+def run_config5(args):
+    """Llama-3-70B KV geometry (80 layers, 64 q-heads, 8 KV heads x 128,
+    GQA group 8, fp16), batch 64, 32,768-token contexts, 16-token pages
+    randomly permuted; KV heads sharded over the GPUs with an NCCL
+    all-gather of each layer's output.  The full cache (687 GB) fits only
+    on 8 GPUs; with fewer, each GPU holds its shard of as many layers as fit
+    in ~150 GB and the result is reported per layer and projected to 80."""
+    import torch
+    import torch.distributed as dist
+    import kvx
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    L_FULL, HQ5, HKV5, B5, T5 = 80, 64, 8, 64, 32768
+    hkv, hq = HKV5 // world, HQ5 // world
+    npg = T5 // PT
+    pages = B5 * npg + B5  # room for one more page per sequence
+    layer_bytes = pages * 2 * hkv * PT * DIM * 2
+    L = min(L_FULL, int(150e9 // layer_bytes))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 5)
+    pools = [torch.empty((pages, 2, hkv, PT, DIM), device="cuda", dtype=torch.float16).normal_(generator=g)
+             for _ in range(L)]
+    perm = torch.randperm(pages, generator=torch.Generator().manual_seed(SEED + 6)).to(torch.int32)
+    bt = perm[: B5 * (npg + 1)].view(B5, npg + 1).cuda()
+    pos = torch.full((B5,), T5 - 1, dtype=torch.int32, device="cuda")  # appends token T-1: context T
+    q = torch.randn((B5, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nk = torch.randn((B5, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    out = torch.empty((L, B5, hq, DIM), device="cuda", dtype=torch.float16)
+    gathered = torch.empty((L, world * B5, hq, DIM), device="cuda", dtype=torch.float16) if world > 1 else None
+    ws = kvx.decode_workspace(B5, hq, npg + 1)
+    comm = torch.cuda.Stream() if world > 1 else None
+    done = [torch.cuda.Event() for _ in range(L)]
+
+    def step():
+        for l in range(L):
+            kvx.append_decode(pools[l], bt, pos, nk, nk, q, out=out[l], workspace=ws)
+            if world > 1:
+                done[l].record()
+                with torch.cuda.stream(comm):
+                    comm.wait_event(done[l])
+                    dist.all_gather_into_tensor(gathered[l], out[l])
+        if world > 1:
+            torch.cuda.current_stream().wait_stream(comm)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = max(2, min(args.steps, 5))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    kv = B5 * T5 * 2 * hkv * DIM * 2 * L  # bytes one rank reads per step
+    peak, peak_kind = peaks()
+    res = {"config": 5, "workload": "Llama-3-70B KV (80L, 64q/8kv x128, G8), fp16, B64, ctx 32768, permuted pages",
+           "n_gpus": world, "layers_resident": L, "ms_per_step": round(ms, 3),
+           "ms_per_layer": round(ms / L, 4), "projected_80_layer_step_ms": round(ms / L * L_FULL, 2),
+           "value": round(kv * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "per_gpu_frac_of_peak": round(kv / (ms / 1e3) / 1e9 / peak, 3), "peak": peak, "peak_kind": peak_kind,
+           "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else "")}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     global LAYERS
     args = parse()
     LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 1:
+        run_config1(args)
+    elif args.config == 3:
+        run_config3(args)
+    elif args.config == 5:
+        run_config5(args)
     else:
         run_ours(args)
 

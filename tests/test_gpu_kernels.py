@@ -281,6 +281,33 @@ def test_compress_int8_pages_bitexact(kvx, oracle, np_dtype):
     assert np.array_equal(dec.view(np.uint32), oracle.decompress_int8_blocks(rc, rs, 2048).view(np.uint32))
 
 
+@pytest.mark.parametrize("np_dtype", [np.float16, np.float32])
+def test_compress_int8_half_ties_bitexact(kvx, oracle, np_dtype):
+    """Quotients (x - min) / scale on and next to k + 1/2, where a
+    reciprocal-multiply could round differently from the division."""
+    rows = []
+    k = np.arange(2048) % 255
+    rows.append(np.where(k == 0, 0.0, k + 0.5))                   # scale 1: exact ties
+    rows[-1][1] = 255.0
+    for span in (1.0, 3.0, 0.1, 7.0, 1e-3, 6e4):
+        t = (np.arange(2048) % 256 + 0.5) / 255.0 * span         # ties for a non-dyadic scale
+        t[0], t[1] = 0.0, span
+        rows.append(t)
+        for ulps in (-2, -1, 1, 2):
+            r = t.astype(np_dtype)
+            bits = r.view(np.uint16 if np_dtype == np.float16 else np.uint32).copy()
+            bits[2:] = bits[2:] + ulps * (bits[2:] > 0)
+            rows.append(bits.view(np_dtype).astype(np.float64))
+    data = np.stack(rows).astype(np_dtype)
+    codes, stats = kvx.compress_int8(dev(data))
+    rc, rs = oracle.compress_int8_blocks(data, 2048)
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    dec16 = kvx.decompress_int8(codes, stats, dtype=torch.float16).cpu().numpy()
+    want = oracle.decompress_int8_blocks(rc, rs, 2048).astype(np.float16)
+    assert np.array_equal(dec16.view(np.uint16), want.view(np.uint16))
+
+
 def test_compress_roundtrip_error_bound(kvx):
     """Property at scale: |x - dequant(quant(x))| <= scale/2 (+1 ulp) per block."""
     nb = 65536  # 128 Mi elements = 256 MiB fp16, larger than L2
