@@ -513,14 +513,16 @@ int sm_count() {
     return n;
 }
 
-int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
+int choose_chunk(int batch, int hkv, int nhg, int max_pages, int page_scale = 1) {
     if (const char *e = getenv("KVX_DECODE_CHUNK")) {
         int c = atoi(e);
         if (c >= kMinChunk) return c;
     }
     // aim at ~4 waves of 3 resident CTAs per SM, counting half of max_pages
-    // as the mean sequence length
-    const long long work = (long long)batch * hkv * nhg * max_pages;
+    // as the mean sequence length; page_scale > 1 for pages that carry less
+    // data each (int8: a warp's fixed per-page cost is the same for half
+    // the bytes, so a CTA takes more of them)
+    const long long work = (long long)batch * hkv * nhg * max_pages * page_scale;
     const long long target = (long long)sm_count() * 3 * 4;
     long long c = (work / 2 + target - 1) / target;
     if (c < kMinChunk) c = kMinChunk;
@@ -619,13 +621,15 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     p.max_pages = max_pages;
     p.group = num_q_heads / kv->num_kv_heads;
     if (p.group > 4 * kMaxHeadsPerCta) return KVX_EUNSUPPORTED;
-    // fp16 pools take the tensor-core kernel (all q-heads of a kv-head in
-    // one CTA); fp32 / int8 pools the SIMT kernel (head groups of <= 4).
+    // fp16 and int8 pools take the tensor-core kernel (all q-heads of a
+    // kv-head in one CTA); fp32 pools the SIMT kernel (head groups of <= 4).
     const char *force_simt = getenv("KVX_DECODE_SIMT");
-    const bool tc = kv->dtype == KVX_F16 && p.group <= 16 && !(force_simt && force_simt[0] == '1');
+    const bool tc = (kv->dtype == KVX_F16 || kv->dtype == KVX_I8) && p.group <= 16 &&
+                    !(force_simt && force_simt[0] == '1');
     p.nhg = tc ? 1 : (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
     const int G = (p.group + p.nhg - 1) / p.nhg;
-    p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages), min_chunk_r);
+    p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages, tc && kv->dtype == KVX_I8 ? 3 : 1),
+                       min_chunk_r);
     p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
     const size_t splits_cap = min_chunk_r > 0 ? (size_t)(max_pages + min_chunk_r - 1) / min_chunk_r
                                               : max_splits_for(max_pages);
@@ -636,7 +640,7 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     p.scale_log2 = scale * 1.4426950408889634f;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (tc) {
-        const int rc = launch_decode_tc(p, io_dtype, batch, st);
+        const int rc = launch_decode_tc(p, kv->dtype, io_dtype, batch, st);
         if (rc != KVX_EUNSUPPORTED) return rc;
         p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;  // no tensor map: SIMT kernel
         p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages), min_chunk_r);

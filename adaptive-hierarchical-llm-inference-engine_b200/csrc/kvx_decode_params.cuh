@@ -23,8 +23,8 @@ struct DecodeParams {
     float scale_log2;
 };
 
-// Tensor-core path for fp16 pools (kvx_decode_tc.cu).  Returns a kvx_status;
-// KVX_EUNSUPPORTED when the geometry has no tensor-core kernel.
-int launch_decode_tc(DecodeParams &p, int io_dtype, int batch, cudaStream_t st);
+// Tensor-core path for fp16 and int8 pools (kvx_decode_tc.cu).  Returns a
+// kvx_status; KVX_EUNSUPPORTED when the geometry has no tensor-core kernel.
+int launch_decode_tc(DecodeParams &p, int kv_dtype, int io_dtype, int batch, cudaStream_t st);
 
 }  // namespace kvx

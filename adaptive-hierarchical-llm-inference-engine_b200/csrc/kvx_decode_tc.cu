@@ -20,6 +20,24 @@
 //
 // Instruction count per (page, head): 8 + 8 ldmatrix.x4, 32 mma, ~40 for
 // softmax and rescale -- against ~1100 for the SIMT kernel.
+//
+// int8 pools (codes of the reference's KVCompressionEngine scheme, one
+// {min, max, scale, zero_point} per (page, K|V, head) block) run the same
+// kernel with kI8: a stage is the two 2 KiB code blocks (TMA box 128 x 16
+// bytes, 128-byte swizzle) plus both 16-byte stats rows (bulk copies), four
+// stages per warp.  Codes become fp16 in registers: x = c ^ 0x80 is the
+// unsigned code u = c + 128, and the bytes {u, 0x64} are the fp16 1024 + u
+// (byte permutes, no conversion instruction).  With k = zp + scale * u:
+//   q.k = scale * (q . (1024 + u)) + (zp - 1024 * scale) * sum(q)
+// per page, so the mma runs on 1024 + u directly; for V the softmax weights
+// are multiplied by the page's scale before rounding to fp16 (P' = p * sv)
+// and the zero point enters through one scalar per row,
+//   sum_t p_t v_t = P' . (1024 + u) + sum_t (zp * p_t - 1024 * P'_t),
+// with P'_t the rounded values the mma used, so the 1024 terms cancel.
+// The head dimension is permuted to make every fragment a contiguous run of
+// codes: for QK, k-step kc of lane (g, r) takes bytes 32r + 4kc .. +3 of its
+// token row (Q loaded in the same order); for PV, lane (g, r) reads bytes
+// 16g .. 16g + 15 of four token rows and n-tile jn column g is dim 16g + jn.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <math_constants.h>
@@ -33,11 +51,20 @@ namespace {
 
 constexpr int kTcWarps = 4;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kTcStages = 2;
-constexpr int kBox = 2048;          // 16 tokens x 64 dims x fp16, 128B-swizzled
-constexpr int kTcStage = 4 * kBox;  // K dims 0-63 | K dims 64-127 | V 0-63 | V 64-127
-constexpr int kTcSmem = 1024 /* alignment slack */ + kTcWarps * kTcStages * kTcStage +
-                        kTcWarps * kTcStages * 8 + 2 * kTcWarps * 16 * 4 + 16;
+constexpr int kBox = 2048;          // 16 tokens x 64 dims x fp16 (or 128 int8), 128B-swizzled
+constexpr int kQloBytes = 8 * 32 * 16;  // q lo A fragments, 8 k-steps x 32 lanes x 4 regs (group > 8)
+constexpr int kBtCache = 64;            // block-table entries staged per warp
+
+// Per-warp staging ring.  fp16: 2 stages of K dims 0-63 | K 64-127 | V 0-63 |
+// V 64-127.  int8: 4 stages of K codes | V codes, stats rows kept apart.
+template <bool kI8> struct TcCfg {
+    static constexpr int kStages = kI8 ? 4 : 2;
+    static constexpr int kStage = kI8 ? 2 * kBox : 4 * kBox;
+    static constexpr int kRing = kStages * kStage;  // >= 16 KiB: parks O at the end
+    static constexpr int kStatBytes = kI8 ? kTcWarps * kStages * 32 : 0;
+    static constexpr int kSmem = 1024 /* alignment slack */ + kTcWarps * kRing + kTcWarps * kStages * 8 +
+                                 kStatBytes + 2 * kTcWarps * 16 * 4 + 16 + kQloBytes + kTcWarps * kBtCache * 4;
+};
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int x, int y,
                                             uint32_t bar) {
@@ -86,6 +113,12 @@ __device__ __forceinline__ void mma16816_lo(float &c0, float &c1, const uint32_t
     (void)d3;
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
@@ -102,29 +135,49 @@ __device__ __forceinline__ uint32_t swz(int row, int c) {
 // online softmax in the log2 domain, O += P V.  `sbase` is the shared
 // address of the stage (K lo | K hi | V lo | V hi, 128B-swizzled); `tok`
 // the absolute index of token 2*tq of the page; tokens >= T are masked.
+//
+// q enters as fp16 hi + lo (q - hi rounded again), so that scores keep
+// fp32-like accuracy against keys with outlier channels: with a GQA group
+// <= 8 the lo parts are rows 8-15 of the A tile (padding otherwise) and S
+// adds rows g and g + 8; with a larger group the lo fragments come from
+// shared memory (`qlo`, CTA-wide) and take a second mma per k-step.
 template <bool kBig>
-__device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][4], float (&o)[16][4],
-                                        float &m0, float &m1, float &l0, float &l1, int tok, int T,
-                                        float scale_log2, int lane) {
+__device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][4], uint32_t qlo,
+                                        float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
+                                        int tok, int T, float scale_log2, int lane) {
     const int tq = lane & 3, lrow = lane & 7, lmat = lane >> 3;
     // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
     float sc[2][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
-        for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = chunks 4kp..4kp+3
+    for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = chunks 4kp..4kp+3
+        uint32_t l0a[4], l1a[4];
+        if constexpr (kBig) {
+            const uint4 x = lds128(qlo + ((2 * kp) * 32 + lane) * 16);
+            const uint4 y = lds128(qlo + ((2 * kp + 1) * 32 + lane) * 16);
+            l0a[0] = x.x, l0a[1] = x.y, l0a[2] = x.z, l0a[3] = x.w;
+            l1a[0] = y.x, l1a[1] = y.y, l1a[2] = y.z, l1a[3] = y.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
             const int chunk = 4 * kp + lmat;
             const uint32_t addr = sbase + (chunk >> 3) * kBox + swz(8 * j + lrow, chunk & 7);
             uint32_t b0, b1, b2, b3;
             ldsm_x4(addr, b0, b1, b2, b3);
+            mma16816(sc[j], qa[2 * kp], b0, b1);
+            mma16816(sc[j], qa[2 * kp + 1], b2, b3);
             if constexpr (kBig) {
-                mma16816(sc[j], qa[2 * kp], b0, b1);
-                mma16816(sc[j], qa[2 * kp + 1], b2, b3);
-            } else {
-                mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp], b0, b1);
-                mma16816_lo(sc[j][0], sc[j][1], qa[2 * kp + 1], b2, b3);
+                mma16816(sc[j], l0a, b0, b1);
+                mma16816(sc[j], l1a, b2, b3);
             }
+        }
+    }
+    if constexpr (!kBig) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            sc[j][0] += sc[j][2];
+            sc[j][1] += sc[j][3];
         }
     }
     // ---- online softmax (log2 domain)
@@ -177,13 +230,15 @@ __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][
     } else {
         pa[1] = pa[3] = 0u;
     }
+    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-        o[n][0] *= a0;
-        o[n][1] *= a0;
-        if constexpr (kBig) {
-            o[n][2] *= a1;
-            o[n][3] *= a1;
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= a0;
+            o[n][1] *= a0;
+            if constexpr (kBig) {
+                o[n][2] *= a1;
+                o[n][3] *= a1;
+            }
         }
     }
     // ---- O += P V
@@ -204,16 +259,182 @@ __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][
     }
 }
 
-template <typename QT, bool kBig>
+// fp16 pair {1024 + byte lo, 1024 + byte hi} of two bytes of x.
+__device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t x, uint32_t sel) { return __byte_perm(x, 0x64u, sel); }
+
+// One staged int8 (page, head): K codes at kbase, V codes at kbase + kBox
+// (128-byte rows, 128B-swizzled); sk / sv = {min, max, scale, zero_point};
+// qs0 / qs1 = sum of the q fed to the mma for rows g / g + 8; z0 / z1 the
+// zero-point scalars of rows g / g + 8 (partial over this lane's tokens).
+//
+// The weights multiply v - zp = scale * u, which in a block with outliers
+// can be far larger than v itself, so one fp16 rounding of P' would cost up
+// to 2^-11 of the block's range.  P' is therefore carried as fp16 hi + lo,
+// like q: with a GQA group <= 8 the lo parts ride in rows 8-15 of the m16
+// tile, which are padding otherwise (S and O add rows g and g + 8); with a
+// larger group the lo parts take a second mma into the same accumulators
+// (q lo fragments from shared memory, `qlo`).
+template <bool kBig>
+__device__ __forceinline__ void tc_page_i8(uint32_t kbase, float4 sk, float4 sv, const uint32_t (&qa)[8][4],
+                                           uint32_t qlo, float qs0, float qs1, float (&o)[16][4], float &m0,
+                                           float &m1, float &l0, float &l1, float &z0, float &z1, int tok,
+                                           int T, float scale_log2, int lane) {
+    const int g = lane >> 2, r = lane & 3;
+    // ---- S = scale * Q (1024 + u) + (zp - 1024 scale) sum(q)
+    float sc[2][4];
+    uint32_t w[2][8];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+        const uint4 a = lds128(kbase + swz(8 * j + g, 2 * r));
+        const uint4 b = lds128(kbase + swz(8 * j + g, 2 * r + 1));
+        w[j][0] = a.x, w[j][1] = a.y, w[j][2] = a.z, w[j][3] = a.w;
+        w[j][4] = b.x, w[j][5] = b.y, w[j][6] = b.z, w[j][7] = b.w;
+    }
+#pragma unroll
+    for (int kc = 0; kc < 8; ++kc) {
+        uint32_t la[4];
+        if constexpr (kBig) {
+            const uint4 x = lds128(qlo + (kc * 32 + lane) * 16);
+            la[0] = x.x, la[1] = x.y, la[2] = x.z, la[3] = x.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t x = w[j][kc] ^ 0x80808080u;
+            const uint32_t b0 = u8x2_to_h2(x, 0x4140), b1 = u8x2_to_h2(x, 0x4342);
+            mma16816(sc[j], qa[kc], b0, b1);
+            if constexpr (kBig) mma16816(sc[j], la, b0, b1);
+        }
+    }
+    if constexpr (!kBig) {  // q hi (rows 0-7) + q lo (rows 8-15)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            sc[j][0] += sc[j][2];
+            sc[j][1] += sc[j][3];
+        }
+    }
+    const float kofs = fmaf(-1024.f, sk.z, sk.w);
+    const float c0 = kofs * qs0, c1 = kofs * qs1;
+    // ---- online softmax (log2 domain)
+    float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const bool valid = tok + 8 * j + e < T;
+            sc[j][e] = valid ? fmaf(sc[j][e], sk.z, c0) * scale_log2 : -CUDART_INF_F;
+            mx0 = fmaxf(mx0, sc[j][e]);
+            if constexpr (kBig) {
+                sc[j][2 + e] = valid ? fmaf(sc[j][2 + e], sk.z, c1) * scale_log2 : -CUDART_INF_F;
+                mx1 = fmaxf(mx1, sc[j][2 + e]);
+            }
+        }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    const float mn0 = fmaxf(m0, mx0);
+    const float a0 = exp2f(m0 - mn0);
+    m0 = mn0;
+    float a1 = 1.f;
+    if constexpr (kBig) {
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn1 = fmaxf(m1, mx1);
+        a1 = exp2f(m1 - mn1);
+        m1 = mn1;
+    }
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            sc[j][e] = exp2f(sc[j][e] - m0);
+            ps0 += sc[j][e];
+            if constexpr (kBig) {
+                sc[j][2 + e] = exp2f(sc[j][2 + e] - m1);
+                ps1 += sc[j][2 + e];
+            }
+        }
+    l0 = l0 * a0 + ps0;
+    if constexpr (kBig) l1 = l1 * a1 + ps1;
+    // P' = p * scale_v as fp16 hi + lo (masked tokens stay exactly 0); the
+    // zero-point scalar takes the rounded values the mma sees
+    auto wv = [&](float pv) { return pv == 0.f ? 0.f : pv * sv.z; };
+    float rs0 = 0.f, rs1 = 0.f;
+    auto split = [&](float x, float y, uint32_t &hi, uint32_t &lo, float &sum) {
+        hi = pack_h2(x, y);
+        const float2 h = h2_to_f2(hi);
+        lo = pack_h2(x - h.x, y - h.y);
+        const float2 l = h2_to_f2(lo);
+        sum += (h.x + h.y) + (l.x + l.y);
+    };
+    uint32_t pa[4], pl[4];
+    split(wv(sc[0][0]), wv(sc[0][1]), pa[0], pl[0], rs0);
+    split(wv(sc[1][0]), wv(sc[1][1]), pa[2], pl[2], rs0);
+    if constexpr (kBig) {
+        split(wv(sc[0][2]), wv(sc[0][3]), pa[1], pl[1], rs1);
+        split(wv(sc[1][2]), wv(sc[1][3]), pa[3], pl[3], rs1);
+        z1 = z1 * a1 + (sv.w * ps1 - 1024.f * rs1);
+    } else {  // rows 8-15: the lo parts
+        pa[1] = pl[0];
+        pa[3] = pl[2];
+    }
+    z0 = z0 * a0 + (sv.w * ps0 - 1024.f * rs0);
+    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= a0;
+            o[n][1] *= a0;
+            o[n][2] *= kBig ? a1 : a0;
+            o[n][3] *= kBig ? a1 : a0;
+        }
+    }
+    // ---- O += P' (1024 + u): lane (g, r) reads dims 16g .. 16g+15 of tokens
+    // 2r, 2r+1 (B rows k, k+1) and 2r+8, 2r+9 (rows k+8, k+9)
+    const uint32_t vbase = kbase + kBox;
+    const uint4 t0 = lds128(vbase + swz(2 * r, g)), t1 = lds128(vbase + swz(2 * r + 1, g));
+    const uint4 t8 = lds128(vbase + swz(2 * r + 8, g)), t9 = lds128(vbase + swz(2 * r + 9, g));
+    const uint32_t w0[4] = {t0.x, t0.y, t0.z, t0.w}, w1[4] = {t1.x, t1.y, t1.z, t1.w};
+    const uint32_t w8[4] = {t8.x, t8.y, t8.z, t8.w}, w9[4] = {t9.x, t9.y, t9.z, t9.w};
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {  // word a: dims 16g + 4a .. +3 = n-tiles 4a .. 4a+3
+        const uint32_t xlo = __byte_perm(w0[a], w1[a], 0x5140) ^ 0x80808080u;  // tok 2r|2r+1, bytes 0,1
+        const uint32_t xhi = __byte_perm(w0[a], w1[a], 0x7362) ^ 0x80808080u;  // bytes 2,3
+        const uint32_t ylo = __byte_perm(w8[a], w9[a], 0x5140) ^ 0x80808080u;
+        const uint32_t yhi = __byte_perm(w8[a], w9[a], 0x7362) ^ 0x80808080u;
+        const uint32_t b0[4] = {u8x2_to_h2(xlo, 0x4140), u8x2_to_h2(xlo, 0x4342), u8x2_to_h2(xhi, 0x4140),
+                                u8x2_to_h2(xhi, 0x4342)};
+        const uint32_t b1[4] = {u8x2_to_h2(ylo, 0x4140), u8x2_to_h2(ylo, 0x4342), u8x2_to_h2(yhi, 0x4140),
+                                u8x2_to_h2(yhi, 0x4342)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            mma16816(o[4 * a + e], pa, b0[e], b1[e]);
+            if constexpr (kBig) mma16816(o[4 * a + e], pl, b0[e], b1[e]);
+        }
+    }
+}
+
+// Where lane (g, r) parks O element (row, n-tile jn, column 2r + e) for the
+// merge: fp16 kernel dim 8 jn + 2r + e, row stride 128; int8 kernel dim
+// 16 (2r + e) + jn, row stride 132 and the dim's low bits XOR (dim >> 5) so
+// that the 32 lanes of one store hit 32 banks.
+template <bool kI8> __device__ __forceinline__ int park_ofs(int row, int d) {
+    if constexpr (kI8) return row * 132 + (d ^ ((d >> 5) & 3));
+    return row * kHeadDim + d;
+}
+
+template <typename QT, bool kBig, bool kI8>
 __global__ void __launch_bounds__(kTcThreads, 3)
 tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
+    using Cfg = TcCfg<kI8>;
+    constexpr int kTcStages = Cfg::kStages;
+    constexpr int kTcStage = Cfg::kStage;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
-    const bool fused = p.positions != nullptr;
+    const bool fused = !kI8 && p.positions != nullptr;
     int T = fused ? p.positions[s] + 1 : max(p.seq_lens[s], 0);
     if (fused && T <= 0) T = 0;
     if (T > p.max_pages * kPageTokens) {
@@ -237,9 +458,14 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
 
     uint8_t *wbuf = smem + warp * kTcStages * kTcStage;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcWarps * kTcStages * kTcStage) + warp * kTcStages;
-    float *s_m = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8);
+    float *wstat = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8) +
+                   warp * kTcStages * 8;  // int8: per stage K stats | V stats
+    float *s_m = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8 +
+                                           Cfg::kStatBytes);
     float *s_l = s_m + kTcWarps * 16;
     int *s_flag = reinterpret_cast<int *>(s_l + kTcWarps * 16);
+    uint4 *s_qlo = reinterpret_cast<uint4 *>(s_flag + 4);  // [8][32] A fragments (group > 8)
+    int *wbt = reinterpret_cast<int *>(s_qlo + 8 * 32) + warp * kBtCache;  // this warp's physical pages
 
     if (lane == 0) {
         for (int i = 0; i < kTcStages; ++i) mbar_init(&bars[i], 1);
@@ -267,52 +493,91 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     const int n_my = (p1 - p0 - warp + kTcWarps - 1) / kTcWarps;
     const int32_t *bt = p.block_table + (size_t)s * p.max_pages;
     const uint32_t wbase = smem_addr(wbuf);
+    // the warp's block-table entries, staged once (one global round trip per
+    // warp instead of two per page)
+    for (int i = lane; i < min(n_my, kBtCache); i += 32) wbt[i] = bt[p0 + warp + kTcWarps * i];
+    __syncwarp();
+    auto phys_of = [&](int i) { return i < kBtCache ? wbt[i] : bt[p0 + warp + kTcWarps * i]; };
 
     auto issue = [&](int i, int st) {
-        const int lp = p0 + warp + kTcWarps * i;
-        const int phys = bt[lp];
+        const int phys = phys_of(i);
         uint64_t *bar = &bars[st];
         if (phys < 0 || phys >= p.num_pages) {
             if (p.error_flag) atomicOr(p.error_flag, 2);
             mbar_arrive_expect_tx(bar, 0);
             return;
         }
-        const int yk = (((phys * 2) * p.hkv) + kvh) * kPageTokens;
+        const int kb = (phys * 2) * p.hkv + kvh;  // (page, K, head) block; V block = kb + hkv
+        const int yk = kb * kPageTokens;
         const int yv = yk + p.hkv * kPageTokens;
         const uint32_t dst = wbase + st * kTcStage;
         const uint32_t b = smem_addr(bar);
-        mbar_arrive_expect_tx(bar, kTcStage);
-        tma_load_2d(dst, &tm, 0, yk, b);
-        tma_load_2d(dst + kBox, &tm, 64, yk, b);
-        tma_load_2d(dst + 2 * kBox, &tm, 0, yv, b);
-        tma_load_2d(dst + 3 * kBox, &tm, 64, yv, b);
+        if constexpr (kI8) {
+            mbar_arrive_expect_tx(bar, kTcStage + 32);
+            tma_load_2d(dst, &tm, 0, yk, b);
+            tma_load_2d(dst + kBox, &tm, 0, yv, b);
+            bulk_g2s(wstat + st * 8, p.stats + (size_t)kb * 4, 16, bar);
+            bulk_g2s(wstat + st * 8 + 4, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
+        } else {
+            mbar_arrive_expect_tx(bar, kTcStage);
+            tma_load_2d(dst, &tm, 0, yk, b);
+            tma_load_2d(dst + kBox, &tm, 64, yk, b);
+            tma_load_2d(dst + 2 * kBox, &tm, 0, yv, b);
+            tma_load_2d(dst + 3 * kBox, &tm, 64, yv, b);
+        }
     };
     if (lane == 0)
         for (int i = 0; i < min(kTcStages, n_my); ++i) issue(i, i);
 
     // Q as m16n8k16 A fragments: rows = q-heads of this kv-head (zero padded),
     // k = head_dim in 8 steps of 16.
+    // Q as fp16 hi + lo A fragments.  int8: k-step kk of lane (gq, tq)
+    // covers dims 32 tq + 4 kk .. +3 (the order the codes are read in), and
+    // qs0 / qs1 are the sums of what the mma is fed for rows gq / gq + 8.
     uint32_t qa[8][4];
+    float qs0 = 0.f, qs1 = 0.f;
     {
         const QT *qb = reinterpret_cast<const QT *>(p.q) + ((size_t)s * p.hq + h0) * kHeadDim;
         const bool r0 = gq < nh, r1 = kBig && gq + 8 < nh;
+        auto ld = [&](bool ok, int row, int col) -> float {
+            return ok ? io_traits<QT>::load(qb + row * kHeadDim + col) : 0.f;
+        };
+        auto split = [](float x, float y, uint32_t &hi, uint32_t &lo, float &sum) {
+            hi = pack_h2(x, y);
+            const float2 h = h2_to_f2(hi);
+            lo = pack_h2(x - h.x, y - h.y);
+            const float2 l = h2_to_f2(lo);
+            sum += (h.x + h.y) + (l.x + l.y);
+        };
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-            const int c0 = 16 * kk + 2 * tq;
-            auto ld = [&](bool ok, int row, int col) -> float {
-                return ok ? io_traits<QT>::load(qb + row * kHeadDim + col) : 0.f;
-            };
-            qa[kk][0] = pack_h2(ld(r0, gq, c0), ld(r0, gq, c0 + 1));
-            qa[kk][1] = pack_h2(ld(r1, gq + 8, c0), ld(r1, gq + 8, c0 + 1));
-            qa[kk][2] = pack_h2(ld(r0, gq, c0 + 8), ld(r0, gq, c0 + 9));
-            qa[kk][3] = pack_h2(ld(r1, gq + 8, c0 + 8), ld(r1, gq + 8, c0 + 9));
+            const int c0 = kI8 ? 32 * tq + 4 * kk : 16 * kk + 2 * tq;
+            const int c8 = kI8 ? c0 + 2 : c0 + 8;
+            uint32_t lo[4];
+            split(ld(r0, gq, c0), ld(r0, gq, c0 + 1), qa[kk][0], lo[0], qs0);
+            split(ld(r0, gq, c8), ld(r0, gq, c8 + 1), qa[kk][2], lo[2], qs0);
+            if constexpr (kBig) {
+                split(ld(r1, gq + 8, c0), ld(r1, gq + 8, c0 + 1), qa[kk][1], lo[1], qs1);
+                split(ld(r1, gq + 8, c8), ld(r1, gq + 8, c8 + 1), qa[kk][3], lo[3], qs1);
+                if (warp == 0) s_qlo[kk * 32 + lane] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            } else {  // rows 8-15: q lo
+                qa[kk][1] = lo[0];
+                qa[kk][3] = lo[2];
+            }
         }
+        qs0 += __shfl_xor_sync(0xffffffffu, qs0, 1);
+        qs0 += __shfl_xor_sync(0xffffffffu, qs0, 2);
+        qs1 += __shfl_xor_sync(0xffffffffu, qs1, 1);
+        qs1 += __shfl_xor_sync(0xffffffffu, qs1, 2);
     }
+    if constexpr (kBig) __syncthreads();  // q lo fragments visible to every warp
+    const uint32_t qlo = smem_addr(s_qlo);
 
     float o[16][4];
 #pragma unroll
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+    float z0 = 0.f, z1 = 0.f;  // int8 zero-point terms
 
     bool ok = true;
     int done = 0;
@@ -325,7 +590,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
         done = i + 1;
         const int lp = p0 + warp + kTcWarps * i;
-        const int phys = bt[lp];
+        const int phys = phys_of(i);
         const uint32_t sbase = wbase + st * kTcStage;
         if (phys >= 0 && phys < p.num_pages) {
             if (lp == lp_new) {  // fused append: patch the new rows into the staged tiles
@@ -336,8 +601,15 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
                     reinterpret_cast<const uint4 *>(src)[c];
                 __syncwarp();
             }
-            tc_page<kBig>(sbase, qa, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
-                          p.scale_log2, lane);
+            if constexpr (kI8) {
+                const float4 sk = *reinterpret_cast<const float4 *>(wstat + st * 8);
+                const float4 sv = *reinterpret_cast<const float4 *>(wstat + st * 8 + 4);
+                tc_page_i8<kBig>(sbase, sk, sv, qa, qlo, qs0, qs1, o, m0, m1, l0, l1, z0, z1,
+                                 lp * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane);
+            } else {
+                tc_page<kBig>(sbase, qa, qlo, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
+                              p.scale_log2, lane);
+            }
         }
         __syncwarp();
         if (lane == 0 && i + kTcStages < n_my) {
@@ -370,12 +642,31 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     }
     float *wacc = reinterpret_cast<float *>(wbuf);
+    if constexpr (kI8) {
+        z0 += __shfl_xor_sync(0xffffffffu, z0, 1);
+        z0 += __shfl_xor_sync(0xffffffffu, z0, 2);
+        z1 += __shfl_xor_sync(0xffffffffu, z1, 1);
+        z1 += __shfl_xor_sync(0xffffffffu, z1, 2);
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-        *reinterpret_cast<float2 *>(wacc + gq * kHeadDim + 8 * n + 2 * tq) = make_float2(o[n][0], o[n][1]);
-        if constexpr (kBig)
-            *reinterpret_cast<float2 *>(wacc + (gq + 8) * kHeadDim + 8 * n + 2 * tq) =
-                make_float2(o[n][2], o[n][3]);
+        for (int n = 0; n < 16; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int d = 16 * (2 * tq + e) + n;
+                if constexpr (kBig) {
+                    wacc[park_ofs<true>(gq, d)] = o[n][e] + z0;
+                    wacc[park_ofs<true>(gq + 8, d)] = o[n][2 + e] + z1;
+                } else {
+                    wacc[park_ofs<true>(gq, d)] = (o[n][e] + o[n][2 + e]) + z0;
+                }
+            }
+    } else {
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            *reinterpret_cast<float2 *>(wacc + gq * kHeadDim + 8 * n + 2 * tq) = make_float2(o[n][0], o[n][1]);
+            if constexpr (kBig)
+                *reinterpret_cast<float2 *>(wacc + (gq + 8) * kHeadDim + 8 * n + 2 * tq) =
+                    make_float2(o[n][2], o[n][3]);
+        }
     }
     if (tq == 0) {
         s_m[warp * 16 + gq] = m0;
@@ -394,7 +685,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         for (int w = 0; w < kTcWarps; ++w) {
             const float mw = s_m[w * 16 + g];
             const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
-            O += sw * reinterpret_cast<const float *>(smem + w * kTcStages * kTcStage)[g * kHeadDim + d];
+            O += sw * reinterpret_cast<const float *>(smem + w * kTcStages * kTcStage)[park_ofs<kI8>(g, d)];
             L += sw * s_l[w * 16 + g];
         }
         const int h = h0 + g;
@@ -474,31 +765,56 @@ bool make_pool_map(CUtensorMap *tm, const void *pool, long long rows) {
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename QT, bool kBig>
+// 2D view of an int8 pool: rows of 128 codes, box = 128 x 16 bytes (one
+// (page, K|V, head) block), 128-byte swizzle.
+bool make_pool_map_i8(CUtensorMap *tm, const void *pool, long long rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || rows <= 0 || rows > (1ll << 31)) return false;
+    cuuint64_t gdim[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)kHeadDim};
+    cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kPageTokens};
+    cuuint32_t estride[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(pool), gdim, gstride, box, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename QT, bool kBig, bool kI8>
 int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorMap &tm) {
-    auto kern = tc_decode_kernel<QT, kBig>;
+    auto kern = tc_decode_kernel<QT, kBig, kI8>;
+    constexpr int smem = TcCfg<kI8>::kSmem;
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return KVX_ECUDA;
         attr_set = true;
     }
     dim3 grid(p.max_splits, p.hkv, batch);
-    kern<<<grid, kTcThreads, kTcSmem, st>>>(p, tm);
+    kern<<<grid, kTcThreads, smem, st>>>(p, tm);
     return launch_status();
+}
+
+template <bool kI8>
+int launch_tc_io(const DecodeParams &p, int io_dtype, int batch, cudaStream_t st, const CUtensorMap &tm) {
+    const bool big = p.group > 8;
+    if (io_dtype == KVX_F32)
+        return big ? launch_tc<float, true, kI8>(p, batch, st, tm) : launch_tc<float, false, kI8>(p, batch, st, tm);
+    return big ? launch_tc<__half, true, kI8>(p, batch, st, tm) : launch_tc<__half, false, kI8>(p, batch, st, tm);
 }
 
 }  // namespace
 
-int launch_decode_tc(DecodeParams &p, int io_dtype, int batch, cudaStream_t st) {
+int launch_decode_tc(DecodeParams &p, int kv_dtype, int io_dtype, int batch, cudaStream_t st) {
     if (p.group > 16) return KVX_EUNSUPPORTED;
+    if (kv_dtype == KVX_I8 && (p.positions || !p.stats)) return KVX_EUNSUPPORTED;
     CUtensorMap tm;
     const long long rows = (long long)p.num_pages * 2 * p.hkv * kPageTokens;
-    if (!make_pool_map(&tm, p.pool, rows)) return KVX_EUNSUPPORTED;
-    const bool big = p.group > 8;
-    if (io_dtype == KVX_F32)
-        return big ? launch_tc<float, true>(p, batch, st, tm) : launch_tc<float, false>(p, batch, st, tm);
-    return big ? launch_tc<__half, true>(p, batch, st, tm) : launch_tc<__half, false>(p, batch, st, tm);
+    if (kv_dtype == KVX_I8) {
+        if (!make_pool_map_i8(&tm, p.pool, rows)) return KVX_EUNSUPPORTED;
+        return launch_tc_io<true>(p, io_dtype, batch, st, tm);
+    }
+    if (kv_dtype != KVX_F16 || !make_pool_map(&tm, p.pool, rows)) return KVX_EUNSUPPORTED;
+    return launch_tc_io<false>(p, io_dtype, batch, st, tm);
 }
 
 }  // namespace kvx

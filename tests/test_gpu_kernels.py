@@ -231,6 +231,20 @@ def test_decode_tensor_core_path_matches_oracle(kvx, oracle, monkeypatch, hkv, h
     assert_close(simt, ref)
 
 
+@pytest.mark.parametrize("hkv,hq", [(8, 24), (1, 12), (2, 32)])
+def test_decode_outlier_keys_keep_fp32_query_accuracy(kvx, oracle, hkv, hq):
+    """Keys with outlier channels (1% of entries x20, as K caches have):
+    the query must not be rounded to fp16 on its way into the mma."""
+    lens = kvgen.randint(110 + hq, 6, 1, 900)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=111)
+    pool = kvgen.normal(112, (num_pages, 2, hkv, 16, 128))
+    pool[kvgen.uniform(113, pool.size).reshape(pool.shape) < 0.01] *= 20
+    pool = pool.astype(np.float16)
+    q = kvgen.normal(114, (lens.size, hq, 128)) * 2.0
+    out = kvx.decode(dev(pool), dev(bt), dev(lens.astype(np.int32)), dev(q)).cpu().numpy()
+    assert_close(out, oracle.paged_decode(pool, bt, lens.astype(np.int32), q))
+
+
 def test_decode_gqa_grouping_matches_mha_expansion(kvx):
     """Property: GQA with group G equals MHA on a pool whose kv heads are
     repeated G times."""
@@ -331,6 +345,34 @@ def test_int8_decode_matches_reference_golden(kvx, oracle):
     cpool = codes.view(num_pages, 2, hkv, pt, dim)
     out = kvx.decode(cpool, dev(g["block_table"]), dev(g["seq_lens"]), dev(Q), stats=stats)
     assert_close(out.cpu().numpy(), g["out"])
+
+
+@pytest.mark.parametrize("hkv,hq,io", [(8, 24, "f32"), (8, 24, "f16"), (2, 16, "f32"), (1, 12, "f32"),
+                                       (4, 4, "f32")])
+def test_int8_decode_tensor_core_path_matches_oracle(kvx, oracle, monkeypatch, hkv, hq, io):
+    """int8 pools run on the tensor-core kernel (codes widened in registers,
+    scale / zero point folded into scores and weights); the SIMT kernel
+    must agree with it and both with the oracle's dequantise-then-attend."""
+    lens = kvgen.randint(90 + hq, 7, 1, 1200)
+    lens[0], lens[1] = 1, 16
+    bt, num_pages = kvgen.paged_layout(lens, 16, 5, seed=91)
+    pool = kvgen.normal(92, (num_pages, 2, hkv, 16, 128))
+    pool[kvgen.uniform(93, pool.size).reshape(pool.shape) < 0.01] *= 20
+    pool[0] += 3.0  # blocks far from zero: the zero-point terms matter
+    pool = pool.astype(np.float16)
+    codes, stats = kvx.compress_int8(dev(pool))
+    cpool = codes.view(num_pages, 2, hkv, 16, 128)
+    q = kvgen.normal(94, (lens.size, hq, 128))
+    qd = dev(q) if io == "f32" else dev(q.astype(np.float16))
+    args = (cpool, dev(bt), dev(lens.astype(np.int32)), qd)
+    tc = kvx.decode(*args, stats=stats).float().cpu().numpy()
+    monkeypatch.setenv("KVX_DECODE_SIMT", "1")
+    simt = kvx.decode(*args, stats=stats).float().cpu().numpy()
+    qref = q if io == "f32" else q.astype(np.float16).astype(np.float32)
+    ref = oracle.paged_decode(codes.cpu().numpy().reshape(cpool.shape), bt, lens.astype(np.int32), qref,
+                              stats=stats.cpu().numpy().reshape(num_pages, 2, hkv, 4))
+    assert_close(tc, ref)
+    assert_close(simt, ref)
 
 
 # ------------------------------------------------------- fp16 trunc codec ---
