@@ -1,0 +1,444 @@
+// tier.cpp -- kvx_tier: device frame pool + pinned host arena under the
+// reference's LRU policy (include/kvx_tier.h).
+//
+// Policy (cache/kv_cache.cpp:86-148, KVManager): one recency list over the
+// resident frames.  A hit moves the frame to the front; a miss first evicts
+// the back when `capacity` frames are resident, then inserts at the front.
+// The list is intrusive (prev/next arrays indexed by frame id), so a step of
+// n accesses costs O(n) however large the universe is.
+//
+// Slots.  Residency (which frames) is the policy's; placement (which slot)
+// is ours and never changes a decision:
+//   * a load takes a device slot freed in an EARLIER step (or a spare one),
+//     so this step's loads never wait for this step's write-backs;
+//   * a victim's device slot becomes free for the next step;
+//   * a victim accessed again later in the same step keeps its slot and
+//     bytes: its write-back is cancelled, the policy still counts the
+//     eviction and the miss;
+//   * host slots alike: a write-back takes a host slot freed earlier, a
+//     load frees its host slot for the next step.
+//
+// Copies.  Per step one gather/scatter launch per direction
+// (kvx_migrate_frames) on two streams, so loads (H2D) and write-backs (D2H)
+// use both directions of the host link at once.  The only writers are the
+// copies; ordering (step s):
+//   D2H_s waits H2D_{s-1}: it may write host slots H2D_{s-1} read;
+//   H2D_s waits D2H_{s-1}: it may write device slots D2H_{s-1} read, and
+//         it may read host slots D2H_{s-1} wrote;
+//   H2D_s waits the reads marked for step s-2: a device slot it writes was
+//         last read at step s-2 or earlier (a victim of step s-1 cannot be
+//         a frame step s-1 read, since a step is shorter than the capacity),
+//         and reads are marked in step order.
+// Pinned list staging is double-buffered by step parity; before reusing a
+// parity the host waits for the copies of step s-2.
+#include "kvx_tier.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+extern "C" int kvx_migrate_frames(void *dev_base, int32_t dev_capacity, void *host_base,
+                                  int32_t host_capacity, const int32_t *dev_frames,
+                                  const int32_t *host_frames, int32_t num_frames, size_t frame_bytes,
+                                  int32_t direction, int32_t ctas, int32_t *error_flag, void *stream);
+
+namespace {
+
+struct Copy {
+    int32_t dev, host, frame;
+    bool cancelled;
+};
+
+// FIFO of free slots with O(1) push/pop (ring over a fixed array).
+struct SlotQueue {
+    std::vector<int32_t> ring;
+    size_t head = 0, count = 0;
+    void init(size_t cap) { ring.assign(cap ? cap : 1, -1); head = count = 0; }
+    bool empty() const { return count == 0; }
+    void push(int32_t s) { ring[(head + count++) % ring.size()] = s; }
+    void push_front(int32_t s) {
+        head = (head + ring.size() - 1) % ring.size();
+        ring[head] = s;
+        ++count;
+    }
+    int32_t pop() {
+        const int32_t s = ring[head];
+        head = (head + 1) % ring.size();
+        --count;
+        return s;
+    }
+};
+
+}  // namespace
+
+struct kvx_tier {
+    kvx_tier_config cfg{};
+    int64_t dev_slots = 0, host_slots = 0;
+    bool bookkeeping = false;
+    std::mutex mu;
+
+    // per frame
+    std::vector<int32_t> dslot, hslot, prev, next, victim_idx;
+    std::vector<int64_t> last_step;
+    int32_t head = -1, tail = -1;
+    int64_t resident = 0;
+    SlotQueue dev_free, host_free;
+    std::vector<int32_t> freed_dev, freed_host;
+    std::vector<int64_t> reclaimed;  // per device slot: step in which a victim kept it
+    std::vector<Copy> d2h;
+    std::vector<int32_t> h2d_dev, h2d_host;
+    int64_t step = 0;
+    kvx_tier_stats totals{};
+
+    // device side
+    uint8_t *dev_base = nullptr, *host_base = nullptr;
+    cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
+    cudaEvent_t ev_h2d[2] = {}, ev_d2h[2] = {}, ev_read[2] = {};
+    bool ev_used[2] = {false, false};
+    int32_t *stage[2] = {};   // pinned: [4][spare] (h2d dev, h2d host, d2h dev, d2h host)
+    int32_t *lists[2] = {};   // device copies of the same
+    int32_t *err = nullptr;   // device error flag
+    int last_parity = 0;
+};
+
+namespace {
+
+void unlink(kvx_tier *t, int32_t f) {
+    const int32_t p = t->prev[f], n = t->next[f];
+    if (p >= 0) t->next[p] = n; else t->head = n;
+    if (n >= 0) t->prev[n] = p; else t->tail = p;
+    t->prev[f] = t->next[f] = -1;
+}
+
+void push_front(kvx_tier *t, int32_t f) {
+    t->prev[f] = -1;
+    t->next[f] = t->head;
+    if (t->head >= 0) t->prev[t->head] = f;
+    t->head = f;
+    if (t->tail < 0) t->tail = f;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? KVX_OK : KVX_ECUDA; }
+
+void release(kvx_tier *t) {
+    if (!t->bookkeeping) {
+        if (t->s_h2d) cudaStreamSynchronize(t->s_h2d);
+        if (t->s_d2h) cudaStreamSynchronize(t->s_d2h);
+        for (int p = 0; p < 2; ++p) {
+            if (t->ev_h2d[p]) cudaEventDestroy(t->ev_h2d[p]);
+            if (t->ev_d2h[p]) cudaEventDestroy(t->ev_d2h[p]);
+            if (t->ev_read[p]) cudaEventDestroy(t->ev_read[p]);
+            if (t->stage[p]) cudaFreeHost(t->stage[p]);
+            if (t->lists[p]) cudaFree(t->lists[p]);
+        }
+        if (t->s_h2d) cudaStreamDestroy(t->s_h2d);
+        if (t->s_d2h) cudaStreamDestroy(t->s_d2h);
+        if (t->dev_base) cudaFree(t->dev_base);
+        if (t->host_base) cudaFreeHost(t->host_base);
+        if (t->err) cudaFree(t->err);
+    }
+}
+
+int setup_device(kvx_tier *t) {
+    if (cudaSetDevice(t->cfg.device) != cudaSuccess) return KVX_ENODEV;
+    const size_t fb = t->cfg.frame_bytes;
+    if (cudaMalloc(&t->dev_base, (size_t)t->dev_slots * fb) != cudaSuccess) {
+        cudaGetLastError();
+        return KVX_ENOSPC;
+    }
+    if (cudaHostAlloc(&t->host_base, (size_t)t->host_slots * fb, cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        t->host_base = nullptr;
+        return KVX_ENOSPC;
+    }
+    if (cudaStreamCreateWithFlags(&t->s_h2d, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&t->s_d2h, cudaStreamNonBlocking) != cudaSuccess)
+        return KVX_ECUDA;
+    const size_t lb = 4 * (size_t)(t->cfg.spare ? t->cfg.spare : 1) * sizeof(int32_t);
+    for (int p = 0; p < 2; ++p) {
+        if (cudaEventCreateWithFlags(&t->ev_h2d[p], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&t->ev_d2h[p], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&t->ev_read[p], cudaEventDisableTiming) != cudaSuccess)
+            return KVX_ECUDA;
+        if (cudaHostAlloc(reinterpret_cast<void **>(&t->stage[p]), lb, cudaHostAllocPortable) != cudaSuccess ||
+            cudaMalloc(&t->lists[p], lb) != cudaSuccess)
+            return KVX_ENOSPC;
+    }
+    if (cudaMalloc(&t->err, sizeof(int32_t)) != cudaSuccess) return KVX_ENOSPC;
+    return cuda_status(cudaMemset(t->err, 0, sizeof(int32_t)));
+}
+
+// Enqueue the copies of the step just planned.
+int issue(kvx_tier *t, int parity) {
+    const int64_t sp = t->cfg.spare;
+    int32_t *st = t->stage[parity], *dl = t->lists[parity];
+    if (t->ev_used[parity]) {  // the copies of step s-2 read this staging
+        if (cudaEventSynchronize(t->ev_h2d[parity]) != cudaSuccess ||
+            cudaEventSynchronize(t->ev_d2h[parity]) != cudaSuccess)
+            return KVX_ECUDA;
+    }
+    int32_t nd = 0;
+    for (const Copy &c : t->d2h)
+        if (!c.cancelled) {
+            st[2 * sp + nd] = c.dev;
+            st[3 * sp + nd] = c.host;
+            ++nd;
+        }
+    const int32_t nh = (int32_t)t->h2d_dev.size();
+    if (nh) {
+        std::memcpy(st, t->h2d_dev.data(), nh * sizeof(int32_t));
+        std::memcpy(st + sp, t->h2d_host.data(), nh * sizeof(int32_t));
+    }
+    const int prev = parity ^ 1;
+    const int ctas = t->cfg.copy_ctas > 0 ? t->cfg.copy_ctas : 8;
+    const int32_t dcap = (int32_t)t->dev_slots, hcap = (int32_t)t->host_slots;
+    // write-backs
+    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_d2h, t->ev_h2d[prev], 0) != cudaSuccess) return KVX_ECUDA;
+    if (nd) {
+        if (cudaMemcpyAsync(dl + 2 * sp, st + 2 * sp, nd * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_d2h) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(dl + 3 * sp, st + 3 * sp, nd * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_d2h) !=
+                cudaSuccess)
+            return KVX_ECUDA;
+        const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl + 2 * sp, dl + 3 * sp, nd,
+                                          t->cfg.frame_bytes, 0, ctas, t->err, t->s_d2h);
+        if (rc != KVX_OK) return rc;
+    }
+    if (cudaEventRecord(t->ev_d2h[parity], t->s_d2h) != cudaSuccess) return KVX_ECUDA;
+    // loads
+    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[prev], 0) != cudaSuccess) return KVX_ECUDA;
+    if (cudaStreamWaitEvent(t->s_h2d, t->ev_read[parity], 0) != cudaSuccess) return KVX_ECUDA;  // step s-2
+    if (nh) {
+        if (cudaMemcpyAsync(dl, st, nh * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_h2d) != cudaSuccess ||
+            cudaMemcpyAsync(dl + sp, st + sp, nh * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_h2d) !=
+                cudaSuccess)
+            return KVX_ECUDA;
+        const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl, dl + sp, nh,
+                                          t->cfg.frame_bytes, 1, ctas, t->err, t->s_h2d);
+        if (rc != KVX_OK) return rc;
+    }
+    if (cudaEventRecord(t->ev_h2d[parity], t->s_h2d) != cudaSuccess) return KVX_ECUDA;
+    t->ev_used[parity] = true;
+    t->last_parity = parity;
+    return KVX_OK;
+}
+
+}  // namespace
+
+extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **out) {
+    if (!cfg || !out) return KVX_EINVAL;
+    *out = nullptr;
+    if (cfg->frame_bytes == 0 || cfg->frame_bytes % 16 || cfg->universe <= 0 || cfg->capacity <= 0 ||
+        cfg->spare < 0 || cfg->universe > INT32_MAX)
+        return KVX_EINVAL;
+    kvx_tier *t = new (std::nothrow) kvx_tier;
+    if (!t) return KVX_ENOSPC;
+    t->cfg = *cfg;
+    t->bookkeeping = cfg->device < 0;
+    const int64_t U = cfg->universe, C = cfg->capacity, S = cfg->spare;
+    const int64_t resident0 = U < C ? U : C;
+    t->dev_slots = C + S;
+    t->host_slots = (U - resident0) + S;
+    if (t->dev_slots > INT32_MAX || t->host_slots > INT32_MAX) {
+        delete t;
+        return KVX_EINVAL;
+    }
+    try {
+        t->dslot.assign(U, -1);
+        t->hslot.assign(U, -1);
+        t->prev.assign(U, -1);
+        t->next.assign(U, -1);
+        t->victim_idx.assign(U, -1);
+        t->last_step.assign(U, -1);
+        t->reclaimed.assign(t->dev_slots, -1);
+        t->dev_free.init(t->dev_slots);
+        t->host_free.init(t->host_slots);
+    } catch (const std::bad_alloc &) {
+        delete t;
+        return KVX_ENOSPC;
+    }
+    for (int64_t f = 0; f < resident0; ++f) {  // loaded in id order: frame 0 ends at the back
+        t->dslot[f] = (int32_t)f;
+        push_front(t, (int32_t)f);
+    }
+    t->resident = resident0;
+    for (int64_t f = resident0; f < U; ++f) t->hslot[f] = (int32_t)(f - resident0);
+    for (int64_t s = resident0; s < t->dev_slots; ++s) t->dev_free.push((int32_t)s);
+    for (int64_t s = U - resident0; s < t->host_slots; ++s) t->host_free.push((int32_t)s);
+    if (!t->bookkeeping) {
+        const int rc = setup_device(t);
+        if (rc != KVX_OK) {
+            release(t);
+            delete t;
+            return rc;
+        }
+    }
+    *out = t;
+    return KVX_OK;
+}
+
+extern "C" KVX_API void kvx_tier_destroy(kvx_tier *t) {
+    if (!t) return;
+    release(t);
+    delete t;
+}
+
+extern "C" KVX_API int kvx_tier_device_arena(kvx_tier *t, void **base, int64_t *slots) {
+    if (!t) return KVX_EINVAL;
+    if (base) *base = t->dev_base;
+    if (slots) *slots = t->dev_slots;
+    return KVX_OK;
+}
+
+extern "C" KVX_API int kvx_tier_host_arena(kvx_tier *t, void **base, int64_t *slots) {
+    if (!t) return KVX_EINVAL;
+    if (base) *base = t->host_base;
+    if (slots) *slots = t->host_slots;
+    return KVX_OK;
+}
+
+extern "C" KVX_API int kvx_tier_location(kvx_tier *t, int64_t frame, int32_t *tier, int64_t *slot) {
+    if (!t || frame < 0 || frame >= t->cfg.universe) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    const bool on_dev = t->dslot[frame] >= 0;
+    if (tier) *tier = on_dev ? 0 : 1;
+    if (slot) *slot = on_dev ? t->dslot[frame] : t->hslot[frame];
+    return KVX_OK;
+}
+
+extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
+                                     int32_t *evicted, uint8_t *hit, kvx_tier_stats *stats) {
+    if (!t || n < 0 || (n > 0 && (!frames || !dev_slot))) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    if (n >= t->cfg.capacity && t->cfg.universe > t->cfg.capacity) return KVX_EINVAL;
+    const int64_t s = t->step;
+    // pre-pass: ids valid, and the distinct frames to load fit the free slots
+    int64_t loads = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t f = frames[i];
+        if (f < 0 || f >= t->cfg.universe) return KVX_EINVAL;
+        if (t->dslot[f] < 0 && t->victim_idx[f] != -2) {
+            t->victim_idx[f] = -2;  // counted
+            ++loads;
+        }
+    }
+    for (int64_t i = 0; i < n; ++i)
+        if (t->victim_idx[frames[i]] == -2) t->victim_idx[frames[i]] = -1;
+    if (loads > t->cfg.spare || (uint64_t)loads > t->dev_free.count || (uint64_t)loads > t->host_free.count)
+        return KVX_ENOSPC;
+
+    kvx_tier_stats st{};
+    st.accesses = n;
+    t->d2h.clear();
+    t->h2d_dev.clear();
+    t->h2d_host.clear();
+    t->freed_dev.clear();
+    t->freed_host.clear();
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t f = frames[i];
+        if (evicted) evicted[i] = -1;
+        if (t->dslot[f] >= 0) {  // hit
+            if (hit) hit[i] = 1;
+            ++st.hits;
+            if (t->head != f) {
+                unlink(t, f);
+                push_front(t, f);
+            }
+        } else {
+            if (hit) hit[i] = 0;
+            ++st.misses;
+            if (t->resident >= t->cfg.capacity) {  // evict the back first
+                const int32_t v = t->tail;
+                unlink(t, v);
+                --t->resident;
+                ++st.evictions;
+                if (evicted) evicted[i] = v;
+                const int32_t hs = t->host_free.pop();
+                t->victim_idx[v] = (int32_t)t->d2h.size();
+                t->d2h.push_back(Copy{t->dslot[v], hs, v, false});
+                t->freed_dev.push_back(t->dslot[v]);
+                t->hslot[v] = hs;
+                t->dslot[v] = -1;
+            }
+            if (t->victim_idx[f] >= 0) {  // evicted earlier in this step: keep slot and bytes
+                Copy &c = t->d2h[t->victim_idx[f]];
+                c.cancelled = true;
+                ++st.reloads;
+                t->dslot[f] = c.dev;
+                t->reclaimed[c.dev] = s;
+                t->host_free.push_front(c.host);
+                t->hslot[f] = -1;
+                t->victim_idx[f] = -1;
+            } else {
+                const int32_t ds = t->dev_free.pop();
+                t->h2d_dev.push_back(ds);
+                t->h2d_host.push_back(t->hslot[f]);
+                t->freed_host.push_back(t->hslot[f]);
+                t->hslot[f] = -1;
+                t->dslot[f] = ds;
+            }
+            push_front(t, f);
+            ++t->resident;
+        }
+        t->last_step[f] = s;
+        dev_slot[i] = t->dslot[f];
+    }
+    for (const Copy &c : t->d2h) {
+        t->victim_idx[c.frame] = -1;
+        if (!c.cancelled) ++st.frames_d2h;
+    }
+    st.frames_h2d = (int64_t)t->h2d_dev.size();
+    int rc = KVX_OK;
+    if (!t->bookkeeping) rc = issue(t, (int)(s & 1));
+    // slots freed by this step serve the next one
+    for (int32_t d : t->freed_dev)
+        if (t->reclaimed[d] != s) t->dev_free.push(d);
+    for (int32_t h : t->freed_host) t->host_free.push(h);
+    ++t->step;
+    t->totals.accesses += st.accesses;
+    t->totals.hits += st.hits;
+    t->totals.misses += st.misses;
+    t->totals.evictions += st.evictions;
+    t->totals.reloads += st.reloads;
+    t->totals.frames_h2d += st.frames_h2d;
+    t->totals.frames_d2h += st.frames_d2h;
+    if (stats) *stats = st;
+    return rc;
+}
+
+extern "C" KVX_API int kvx_tier_wait_resident(kvx_tier *t, void *stream) {
+    if (!t) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    if (t->bookkeeping || !t->ev_used[t->last_parity]) return KVX_OK;
+    return cuda_status(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), t->ev_h2d[t->last_parity], 0));
+}
+
+extern "C" KVX_API int kvx_tier_mark_read(kvx_tier *t, void *stream) {
+    if (!t) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    if (t->bookkeeping || t->step == 0) return KVX_OK;
+    const int parity = (int)((t->step - 1) & 1);
+    return cuda_status(cudaEventRecord(t->ev_read[parity], static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" KVX_API int kvx_tier_sync(kvx_tier *t) {
+    if (!t) return KVX_EINVAL;
+    if (t->bookkeeping) return KVX_OK;
+    if (cudaStreamSynchronize(t->s_h2d) != cudaSuccess || cudaStreamSynchronize(t->s_d2h) != cudaSuccess)
+        return KVX_ECUDA;
+    int32_t e = 0;
+    if (cudaMemcpy(&e, t->err, sizeof(e), cudaMemcpyDeviceToHost) != cudaSuccess) return KVX_ECUDA;
+    return e ? KVX_EINVAL : KVX_OK;
+}
+
+extern "C" KVX_API int kvx_tier_totals(kvx_tier *t, kvx_tier_stats *stats) {
+    if (!t || !stats) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    *stats = t->totals;
+    return KVX_OK;
+}

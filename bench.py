@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 5],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     return ap.parse_args()
 
@@ -523,6 +523,187 @@ def cpu_compress_baseline(blocks=16384):
             "sample": f"{blocks} blocks of 2048 through KVCompressionEngine::compress(INT8)"}
 
 
+def pinned_peaks(nbytes=2 << 30):
+    """cudaMemcpyAsync over the host link with pinned memory: H2D, D2H and
+    both at once on two streams (GB/s)."""
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    h2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d2 = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(fn, reps=4):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / reps
+
+    def h2d():
+        with torch.cuda.stream(s1):
+            d.copy_(h, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(s2):
+            h2.copy_(d2, non_blocking=True)
+
+    def both():
+        h2d()
+        d2h()
+
+    th, td, tb = timed(h2d), timed(d2h), timed(both)
+    res = {"h2d": round(nbytes / th / 1e9, 1), "d2h": round(nbytes / td / 1e9, 1),
+           "bidir_sum": round(2 * nbytes / tb / 1e9, 1)}
+    del h, h2, d, d2
+    return res
+
+
+def cpu_tier_baseline(universe=4096, accesses=20000):
+    """The reference's page tier on the host: KVManager (cache/kv_cache.cpp)
+    with a third of the pages in memory and the rest as fp16 page files,
+    serving load_page over a Zipf(1.1) stream; bytes = misses x 64 KiB."""
+    try:
+        from oracle import Reference
+        ref = Reference()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference library not loadable: {e}"}
+    ids = kvgen.permutation(SEED + 41, universe)[kvgen.zipf_pages(SEED + 42, accesses, universe, 1.1)]
+    with tempfile.TemporaryDirectory() as d:
+        sec, misses = ref.time_tier(ids.astype(np.int32), universe, universe // 3, PT * HKV * DIM, d)
+    return {"value": round(misses * 65536 / sec / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
+            "sample": f"KVManager capacity {universe // 3} of {universe} pages (64 KiB fp16 page files), "
+                      f"{accesses} Zipf(1.1) load_page calls, {misses} misses"}
+
+
+def run_config4(args):
+    """Tiered eviction under memory pressure.  Llama-3.2-3B KV (28 layers, 8
+    kv heads x 128, fp16) at batch 16 with 65,536-token contexts: 1,835,008
+    page frames of 64 KiB (one 16-token page of all 8 heads, K and V), 120 GB,
+    against a device pool capped at 40 GB (610,351 frames); the rest lives in
+    a pinned host arena.  Each decode step every (layer, sequence) reads 256 of
+    its 4096 pages, drawn Zipf(1.1) over a seeded per-(layer, sequence)
+    ranking.  The store (kvx_tier) applies KVManager's LRU to the step's
+    accesses in order, then loads the misses and writes the victims back over
+    the host link on two copy streams while the previous step's decode runs;
+    decode (B16, 4096 tokens of pages per sequence, 24 q-heads) reads the
+    frames in place.  Reported: frames moved per second per direction against
+    the measured pinned-copy peak, decode GB/s, hit rate, step time."""
+    import torch
+    import kvx
+    from kvx.tier import Tier
+    L, B, P, ACC = 28, 16, 65536 // PT, 256
+    FB = 2 * HKV * PT * DIM * 2
+    U = L * B * P
+    C = int(40e9) // FB
+    S = 49152
+    steps = args.steps
+    warm = max(args.warmup, 16)
+    link = pinned_peaks()
+    # access stream: per (layer, sequence) ranks Zipf(1.1), ranks -> pages by a seeded permutation
+    rows = L * B
+    perms = np.stack([kvgen.permutation(SEED + 1000 + i, P) for i in range(rows)]).astype(np.int32)
+    base = (np.arange(rows, dtype=np.int64) * P)[:, None]
+
+    def step_ids(k):
+        r = kvgen.zipf_pages(SEED + 5000 + k, rows * ACC, P, 1.1).reshape(rows, ACC)
+        return (base + np.take_along_axis(perms, r, axis=1)).astype(np.int32).ravel()
+
+    t0 = time.perf_counter()
+    tier = Tier(FB, U, C, S, device=0)
+    alloc_s = time.perf_counter() - t0
+    dev = tier.device_tensor()
+    host = tier.host_array()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 4)
+    chunk = 1 << 30
+    for o in range(0, dev.numel(), chunk):  # device frames: random fp16
+        n = min(chunk, dev.numel() - o)
+        dev[o:o + n] = torch.randn(n // 2, generator=g, device="cuda", dtype=torch.float16).view(torch.uint8)
+    src = torch.randn(chunk // 2, generator=g, device="cuda", dtype=torch.float16).view(torch.uint8)
+    ht = torch.from_numpy(host)
+    for o in range(0, ht.numel(), chunk):  # host frames: copies of one random GiB
+        n = min(chunk, ht.numel() - o)
+        ht[o:o + n].copy_(src[:n])
+    torch.cuda.synchronize()
+    del src
+    # warm-up: the policy and the copies only, in chunks that fit the spare slots
+    for k in range(warm):
+        ids = step_ids(k)
+        for o in range(0, ids.size, 16384):
+            tier.step(ids[o:o + 16384], evicted=False, hit=False)
+    tier.sync()
+    q = torch.randn((L, B, HQ, DIM), generator=g, device="cuda", dtype=torch.float16)
+    lens = torch.full((B,), ACC * PT, dtype=torch.int32, device="cuda")
+    out = torch.empty((L, B, HQ, DIM), device="cuda", dtype=torch.float16)
+    ws = kvx.decode_workspace(B, HQ, ACC)
+    pool = tier.paged(HKV)
+    bt_host = [torch.empty(rows * ACC, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+    bt_dev = [torch.empty((L, B, ACC), dtype=torch.int32, device="cuda") for _ in range(2)]
+    up = [torch.cuda.Event() for _ in range(2)]
+    stream_ids = [step_ids(warm + k) for k in range(steps)]
+    before = tier.totals()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    plan_s = 0.0
+    e0.record()
+    for k in range(steps):
+        p = k & 1
+        if k >= 2:
+            up[p].synchronize()  # the block-table upload of step k-2 read this buffer
+        h0 = time.perf_counter()
+        tier.step(stream_ids[k], dev_slot=bt_host[p].numpy(), evicted=False, hit=False)
+        plan_s += time.perf_counter() - h0
+        tier.wait_resident()
+        bt_dev[p].view(-1).copy_(bt_host[p], non_blocking=True)
+        up[p].record()
+        for l in range(L):
+            kvx.decode(pool, bt_dev[p][l], lens, q[l], out=out[l], workspace=ws)
+        tier.mark_read()
+    e1.record()
+    tier.sync()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    after = tier.totals()
+    mv = {k2: after[k2] - before[k2] for k2 in after}
+    # decode alone, frames resident (last step's tables)
+    dec_ms = _events_time(lambda: [kvx.decode(pool, bt_dev[(steps - 1) & 1][l], lens, q[l], out=out[l],
+                                              workspace=ws) for l in range(L)], 3)
+    dec_bytes = rows * ACC * FB
+    h2d_gbs = mv["frames_h2d"] * FB / (ms / 1e3) / 1e9
+    d2h_gbs = mv["frames_d2h"] * FB / (ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    cpu = cpu_tier_baseline() if not args.no_cpu_baseline else None
+    res = {
+        "config": 4, "workload": "tiered eviction: Llama-3.2-3B KV (28L, 8kv x128, fp16), B16, ctx 65536 = "
+                                 "1,835,008 frames x 64 KiB; device pool 40 GB (610,351 frames); per step each "
+                                 "(layer, seq) reads 256 pages drawn Zipf(1.1); KVManager LRU",
+        "steps": steps, "warmup_steps": warm, "ms_per_step": round(ms / steps, 3),
+        "hit_rate": round(mv["hits"] / max(1, mv["accesses"]), 4),
+        "frames_per_step": {"h2d": round(mv["frames_h2d"] / steps, 1), "d2h": round(mv["frames_d2h"] / steps, 1),
+                            "reloads": round(mv["reloads"] / steps, 2)},
+        "migrate": {"h2d_GBps": round(h2d_gbs, 1), "d2h_GBps": round(d2h_gbs, 1),
+                    "h2d_frac_of_pinned_peak": round(h2d_gbs / link["h2d"], 3),
+                    "d2h_frac_of_pinned_peak": round(d2h_gbs / link["d2h"], 3),
+                    "sum_frac_of_bidir_peak": round((h2d_gbs + d2h_gbs) / link["bidir_sum"], 3)},
+        "pinned_peak_GBps": link,
+        "decode": {"GBps_overlapped": round(steps * dec_bytes / (ms / 1e3) / 1e9, 1),
+                   "ms_alone_per_step": round(dec_ms, 3),
+                   "GBps_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9, 1),
+                   "frac_of_hbm_peak_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9 / peak, 3)},
+        "host_plan_ms_per_step": round(plan_s / steps * 1e3, 3),
+        "host_arena_GB": round((U - C + S) * FB / 1e9, 1), "device_arena_GB": round((C + S) * FB / 1e9, 1),
+        "alloc_s": round(alloc_s, 1), "clocks": clk, "peak": peak, "peak_kind": peak_kind,
+        "cpu_baseline": cpu}
+    print(json.dumps(res), flush=True)
+    tier.close()
+
+
 def run_config5(args):
     """Llama-3-70B KV geometry (80 layers, 64 q-heads, 8 KV heads x 128,
     GQA group 8, fp16), batch 64, 32,768-token contexts, 16-token pages
@@ -615,6 +796,8 @@ def main():
         run_config1(args)
     elif args.config == 3:
         run_config3(args)
+    elif args.config == 4:
+        run_config4(args)
     elif args.config == 5:
         run_config5(args)
     else:

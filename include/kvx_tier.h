@@ -1,0 +1,112 @@
+/*
+ * kvx_tier.h -- the tiered page-frame store: a device pool of fixed-size KV
+ * frames backed by a pinned host arena, with the reference's LRU policy
+ * deciding residency and batched copy kernels moving the frames.
+ *
+ * Replaces, for page frames:
+ *   KVManager::load_page / evict_page / contains   cache/kv_cache.cpp:86-148
+ *     (LRU list: a hit moves the page to the front; a miss with
+ *      size >= capacity evicts lru_.back() first, then inserts at the front)
+ *   KVCacheGPU::transferToGPU / transferToHost / evictLRUPage
+ *                                                 native-engine/cpp/KVCacheGPU.cpp:68-152
+ *     (one synchronous cudaMemcpy per page there; here one gather/scatter
+ *      launch per step and direction, kvx_migrate_frames)
+ *   RuntimeMemory::allocatePinnedHost             native-engine/cpp/RuntimeMemory.cpp:362-410
+ *     (one pinned arena sliced into frames instead of a first-fit pool)
+ *
+ * Frames live in exactly one tier.  A frame id is any integer in
+ * [0, universe); a frame's bytes are opaque (for the KV pools of this
+ * library a frame is one page of all kv heads: [2][kv_heads][16][128] fp16,
+ * 64 KiB for 8 heads, so the device arena is directly a kvx_paged pool with
+ * num_pages = device frames).
+ *
+ * Initial state: frames 0 .. capacity-1 are resident in device slots
+ * 0 .. capacity-1, in LRU order by id (frame 0 least recent), exactly as if
+ * they had been loaded one by one in that order; every other frame f sits
+ * in host slot f - capacity.  `spare` more device and host slots are free:
+ * they let the loads of a step (H2D) run on one copy stream while the
+ * write-backs of its victims (D2H) run on another, so both directions of
+ * the host link are busy at once.
+ *
+ * A step takes the accesses of one decode step in order and applies the
+ * policy serially (decisions bit-identical to replaying the same id stream
+ * through KVManager with the same capacity), then enqueues the copies.  The
+ * caller makes its decode wait for them (kvx_tier_wait_resident) and tells
+ * the store when that decode has been enqueued (kvx_tier_mark_read), so a
+ * later step never overwrites a frame before the decode that reads it ran.
+ *
+ * Bookkeeping-only stores (device = -1) allocate no device or pinned memory
+ * and copy nothing: they run the policy and the slot assignment alone.
+ */
+#ifndef KVX_TIER_H
+#define KVX_TIER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kvx.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kvx_tier kvx_tier;
+
+typedef struct kvx_tier_config {
+    size_t frame_bytes;  /* bytes per frame, multiple of 16 */
+    int64_t universe;    /* frame ids are [0, universe) */
+    int64_t capacity;    /* frames resident on the device at most (the policy's capacity) */
+    int64_t spare;       /* extra device and host slots; must cover the misses of one step */
+    int32_t device;      /* CUDA device ordinal, or -1 for a bookkeeping-only store */
+    int32_t copy_ctas;   /* CTAs per copy launch (0: 8, enough for the host link) */
+} kvx_tier_config;
+
+typedef struct kvx_tier_stats {
+    int64_t accesses;
+    int64_t hits;
+    int64_t misses;
+    int64_t evictions;
+    int64_t reloads;     /* victims of a step accessed again later in the same step */
+    int64_t frames_h2d;  /* frames copied host -> device */
+    int64_t frames_d2h;  /* frames copied device -> host */
+} kvx_tier_stats;
+
+/* Allocate the store (device arena of capacity + spare frames, pinned host
+ * arena of universe - capacity + spare frames) and place the initial state.
+ * KVX_EINVAL for a bad config, KVX_ENOSPC / KVX_ECUDA when memory cannot be
+ * had. */
+KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **out);
+/* Wait for outstanding copies and free everything. */
+KVX_API void kvx_tier_destroy(kvx_tier *t);
+
+/* Base address and slot count of the device arena (slot s at base + s *
+ * frame_bytes) and of the pinned host arena (mapped: usable from kernels). */
+KVX_API int kvx_tier_device_arena(kvx_tier *t, void **base, int64_t *slots);
+KVX_API int kvx_tier_host_arena(kvx_tier *t, void **base, int64_t *slots);
+
+/* Where frame f is now: *tier = 0 device / 1 host, *slot its slot there. */
+KVX_API int kvx_tier_location(kvx_tier *t, int64_t frame, int32_t *tier, int64_t *slot);
+
+/* One step: accesses frames[0..n) in order.  For access i, dev_slot[i]
+ * receives the device slot the frame occupies for this step's reads;
+ * evicted[i] (optional) the frame evicted by this access or -1; hit[i]
+ * (optional) 1 for a hit.  Copies are enqueued on the store's copy streams
+ * and not waited for.  n must be smaller than capacity; KVX_ENOSPC when the
+ * step misses more frames than `spare` can take (nothing is changed then). */
+KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
+                          int32_t *evicted, uint8_t *hit, kvx_tier_stats *stats);
+/* Make `stream` wait until every frame of the last step is resident. */
+KVX_API int kvx_tier_wait_resident(kvx_tier *t, void *stream);
+/* The reads of the last step's frames have been enqueued on `stream`; a
+ * later step that evicts one of them first waits for that work. */
+KVX_API int kvx_tier_mark_read(kvx_tier *t, void *stream);
+/* Block until all enqueued copies finished; KVX_EINVAL if a copy met a bad
+ * slot (never expected), KVX_ECUDA on a CUDA error. */
+KVX_API int kvx_tier_sync(kvx_tier *t);
+/* Cumulative counters since create. */
+KVX_API int kvx_tier_totals(kvx_tier *t, kvx_tier_stats *stats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -221,6 +221,8 @@ class Reference:
         L.kvref_time_decode.restype = C.c_double
         L.kvref_time_compress.argtypes = [_f32p, _i8p, _f32p, _sz, _sz, C.c_int]
         L.kvref_time_compress.restype = C.c_double
+        L.kvref_time_tier.argtypes = [_i32p, _sz, _sz, _sz, _sz, C.c_char_p, C.POINTER(C.c_int64)]
+        L.kvref_time_tier.restype = C.c_double
         L.kvref_time_append.argtypes = [_f32p, _sz, _sz, _sz, _sz, C.c_char_p]
         L.kvref_time_append.restype = C.c_double
 
@@ -305,6 +307,17 @@ class Reference:
         if nk < 0:
             raise FileNotFoundError(pid)
         return k[:nk].copy(), v[: nv.value].copy()
+
+    def time_tier(self, ids, universe, capacity, page_floats, workdir):
+        """Seconds KVManager (capacity pages, fp16 page files in workdir) takes
+        to serve load_page over `ids`, and how many of them read a file."""
+        ids = _c(ids, np.int32)
+        misses = C.c_int64()
+        s = self.L.kvref_time_tier(ids, ids.size, universe, capacity, page_floats,
+                                   workdir.encode(), C.byref(misses))
+        if s < 0:
+            raise RuntimeError("kvref_time_tier failed")
+        return s, misses.value
 
     def prefetch_depth(self, latencies, size, capacity, max_depth=4):
         lat = _c(latencies, np.float64)

@@ -287,4 +287,37 @@ double kvref_time_append(const float *rows, size_t n, size_t heads, size_t head_
     return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 
+
+// The reference's page tier (cache/kv_cache.cpp): KVManager with `capacity`
+// pages in memory and every page persisted as an fp16 file in `dir`.  Saves
+// pages 0..universe-1 (K and V of `page_floats` fp32 each), then times
+// load_page over the id stream: a hit is a list move, a miss reads the page
+// file back (fp16 -> fp32) and evicts the least recent page.  Returns
+// elapsed seconds of the loads; *misses_out counts the file reads.
+double kvref_time_tier(const int32_t *ids, size_t n, size_t universe, size_t capacity,
+                       size_t page_floats, const char *dir, int64_t *misses_out) {
+    try {
+        KVManager m(capacity, dir);
+        KVPage p;
+        p.key.assign(page_floats, 0.5f);
+        p.value.assign(page_floats, 0.25f);
+        for (size_t i = 0; i < universe; ++i) {
+            p.id = (int)i;
+            p.key[0] = (float)i;
+            m.save_page(p);
+        }
+        int64_t misses = 0;
+        auto t0 = std::chrono::steady_clock::now();
+        for (size_t i = 0; i < n; ++i) {
+            if (!m.contains(ids[i])) ++misses;
+            (void)m.load_page(ids[i]);
+        }
+        const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        *misses_out = misses;
+        return s;
+    } catch (...) {
+        return -1.0;
+    }
+}
+
 }  // extern "C"

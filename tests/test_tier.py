@@ -1,0 +1,107 @@
+"""The tiered frame store's policy and slot bookkeeping, on the CPU
+(bookkeeping-only stores: no device memory, no copies).
+
+Residency decisions must equal, access for access, a serial replay of the
+same id stream through KVManager's LRU (cache/kv_cache.cpp:86-148: a hit
+moves the page to the front; a miss evicts lru_.back() when size >=
+capacity, then inserts at the front) -- here the oracle's restatement, whose
+own parity with the compiled reference is pinned by the lru golden fixture.
+The store starts with frames 0..capacity-1 resident in that order, so the
+replay is fed that prefix first.
+"""
+import numpy as np
+import pytest
+
+import kvgen
+
+from kvx import KvxError
+from kvx.tier import Tier
+
+
+def zipf_stream(seed, steps, per_step, universe):
+    ranks = kvgen.zipf_pages(seed, steps * per_step, universe, 1.1)
+    perm = kvgen.permutation(seed + 1, universe)  # hot ranks scattered over the ids
+    return perm[ranks].astype(np.int32).reshape(steps, per_step)
+
+
+def check_slots(t, universe):
+    dev, host = {}, {}
+    for f in range(universe):
+        tier, slot = t.location(f)
+        d = dev if tier == "device" else host
+        assert slot not in d, (tier, slot)
+        d[slot] = f
+    return dev, host
+
+
+@pytest.mark.parametrize("universe,capacity,spare,per_step", [(3000, 900, 300, 250), (1200, 1500, 10, 100),
+                                                                 (5000, 400, 200, 150)])
+def test_policy_matches_kvmanager_replay(oracle, universe, capacity, spare, per_step):
+    t = Tier(4096, universe, capacity, spare, device=-1)
+    stream = zipf_stream(7 + universe, 24, per_step, universe)
+    got_ev, got_hit = [], []
+    for s in range(stream.shape[0]):
+        slots, ev, hit, st = t.step(stream[s])
+        got_ev.append(ev)
+        got_hit.append(hit)
+        assert st["hits"] + st["misses"] == per_step
+        assert st["frames_h2d"] + st["reloads"] == st["misses"]
+        for f in set(stream[s].tolist()):  # every frame of the step ends on the device
+            assert t.location(f)[0] == "device"
+    ids = np.concatenate([np.arange(min(capacity, universe), dtype=np.int32), stream.ravel()])
+    want_ev, want_hit = oracle.lru_replay(ids, np.zeros(ids.size, np.uint8), capacity)
+    k = min(capacity, universe)
+    assert np.array_equal(np.concatenate(got_hit), want_hit[k:])
+    assert np.array_equal(np.concatenate(got_ev), want_ev[k:])
+    dev, host = check_slots(t, universe)
+    assert len(dev) == min(capacity, universe) and len(dev) + len(host) == universe
+    tot = t.totals()
+    assert tot["accesses"] == stream.size and tot["evictions"] == int((np.concatenate(got_ev) >= 0).sum())
+
+
+def test_slots_within_a_step_are_stable_and_distinct():
+    universe, capacity = 2000, 600
+    t = Tier(4096, universe, capacity, 200, device=-1)
+    stream = zipf_stream(3, 10, 400, universe)
+    for s in range(stream.shape[0]):
+        slots, ev, hit, st = t.step(stream[s])
+        seen = {}
+        for f, sl in zip(stream[s].tolist(), slots.tolist()):
+            assert 0 <= sl < capacity + 200
+            assert seen.setdefault(f, sl) == sl  # a frame keeps one slot for the whole step
+        assert len(set(seen.values())) == len(seen)  # distinct frames, distinct slots
+        for f, sl in seen.items():
+            assert t.location(f) == ("device", sl)
+
+
+def test_reload_within_a_step_keeps_slot_and_counts_miss(oracle):
+    # capacity 4: frames 0..3 resident, 0 least recent
+    t = Tier(64, 10, 4, 4, device=-1)
+    slot0 = t.location(0)[1]
+    # 5 evicts 0, then 0 comes back in the same step (evicting 1)
+    slots, ev, hit, st = t.step(np.array([5, 0], np.int32))
+    assert ev.tolist() == [0, 1] and hit.tolist() == [0, 0]
+    assert st["reloads"] == 1 and st["frames_h2d"] == 1 and st["frames_d2h"] == 1
+    assert slots[1] == slot0  # no bytes moved for frame 0
+    ids = np.array([0, 1, 2, 3, 5, 0], np.int32)
+    want_ev, want_hit = oracle.lru_replay(ids, np.zeros(6, np.uint8), 4)
+    assert want_ev[4:].tolist() == [0, 1] and want_hit[4:].tolist() == [0, 0]
+
+
+def test_errors_leave_the_store_unchanged():
+    t = Tier(64, 100, 20, 3, device=-1)
+    with pytest.raises(KvxError) as e:
+        t.step(np.array([1, 200], np.int32))  # id outside the universe
+    assert e.value.status == -1
+    with pytest.raises(KvxError) as e:
+        t.step(np.arange(20, dtype=np.int32))  # a step must be shorter than the capacity
+    assert e.value.status == -1
+    with pytest.raises(KvxError) as e:
+        t.step(np.array([50, 51, 52, 53], np.int32))  # 4 loads, 3 spare slots
+    assert e.value.status == -6
+    assert t.totals()["accesses"] == 0
+    assert t.location(50) == ("host", 30)
+    slots, ev, hit, st = t.step(np.array([50, 51, 52], np.int32))
+    assert st["misses"] == 3 and ev.tolist() == [0, 1, 2]
+    with pytest.raises(KvxError):
+        Tier(60, 100, 20, 3, device=-1)  # frame bytes not a multiple of 16
