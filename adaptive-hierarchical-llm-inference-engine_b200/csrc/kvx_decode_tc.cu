@@ -23,9 +23,9 @@
 //
 // int8 pools (codes of the reference's KVCompressionEngine scheme, one
 // {min, max, scale, zero_point} per (page, K|V, head) block) run the same
-// kernel with kI8: a stage is the two 2 KiB code blocks (TMA box 128 x 16
-// bytes, 128-byte swizzle) plus both 16-byte stats rows (bulk copies), four
-// stages per warp.  Codes become fp16 in registers: x = c ^ 0x80 is the
+// kernel with kI8: a stage is two (page, head)s, each two 2 KiB code blocks
+// (TMA box 128 x 16 bytes, 128-byte swizzle) plus two 16-byte stats rows
+// (bulk copies), two stages per warp.  Codes become fp16 in registers: x = c ^ 0x80 is the
 // unsigned code u = c + 128, and the bytes {u, 0x64} are the fp16 1024 + u
 // (byte permutes, no conversion instruction).  With k = zp + scale * u:
 //   q.k = scale * (q . (1024 + u)) + (zp - 1024 * scale) * sum(q)
@@ -34,10 +34,11 @@
 // and the zero point enters through one scalar per row,
 //   sum_t p_t v_t = P' . (1024 + u) + sum_t (zp * p_t - 1024 * P'_t),
 // with P'_t the rounded values the mma used, so the 1024 terms cancel.
-// The head dimension is permuted to make every fragment a contiguous run of
-// codes: for QK, k-step kc of lane (g, r) takes bytes 32r + 4kc .. +3 of its
-// token row (Q loaded in the same order); for PV, lane (g, r) reads bytes
-// 16g .. 16g + 15 of four token rows and n-tile jn column g is dim 16g + jn.
+// The head dimension is permuted so fragments come straight from shared
+// memory: for QK, k-step kc of lane (g, r) takes bytes 32r + 4kc .. +3 of
+// its token row (Q loaded in the same order); for PV, ldmatrix.trans of the
+// codes as 16-bit pairs hands lane (g, r) dims 2g, 2g+1 of tokens 2r, 2r+1,
+// so n-tile 2c + par column g is dim 16c + 2g + par.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <math_constants.h>
@@ -55,13 +56,16 @@ constexpr int kBox = 2048;          // 16 tokens x 64 dims x fp16 (or 128 int8),
 constexpr int kQloBytes = 8 * 32 * 16;  // q lo A fragments, 8 k-steps x 32 lanes x 4 regs (group > 8)
 constexpr int kBtCache = 64;            // block-table entries staged per warp
 
-// Per-warp staging ring.  fp16: 2 stages of K dims 0-63 | K 64-127 | V 0-63 |
-// V 64-127.  int8: 4 stages of K codes | V codes, stats rows kept apart.
+// Per-warp staging ring of 2 stages.  fp16: a stage is one page, K dims 0-63
+// | K 64-127 | V 0-63 | V 64-127.  int8: a stage is two pages, K codes | V
+// codes | K codes | V codes, their four stats rows kept apart.
 template <bool kI8> struct TcCfg {
-    static constexpr int kStages = kI8 ? 4 : 2;
-    static constexpr int kStage = kI8 ? 2 * kBox : 4 * kBox;
+    static constexpr int kStages = 2;
+    static constexpr int kStage = 4 * kBox;
+    static constexpr int kPages = kI8 ? 2 : 1;      // pages per stage
     static constexpr int kRing = kStages * kStage;  // >= 16 KiB: parks O at the end
-    static constexpr int kStatBytes = kI8 ? kTcWarps * kStages * 32 : 0;
+    static constexpr int kStatFloats = 16;          // int8: 4 stats rows per stage
+    static constexpr int kStatBytes = kI8 ? kTcWarps * kStages * kStatFloats * 4 : 0;
     static constexpr int kSmem = 1024 /* alignment slack */ + kTcWarps * kRing + kTcWarps * kStages * 8 +
                                  kStatBytes + 2 * kTcWarps * 16 * 4 + 16 + kQloBytes + kTcWarps * kBtCache * 4;
 };
@@ -262,10 +266,14 @@ __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][
 // fp16 pair {1024 + byte lo, 1024 + byte hi} of two bytes of x.
 __device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t x, uint32_t sel) { return __byte_perm(x, 0x64u, sel); }
 
-// One staged int8 (page, head): K codes at kbase, V codes at kbase + kBox
-// (128-byte rows, 128B-swizzled); sk / sv = {min, max, scale, zero_point};
-// qs0 / qs1 = sum of the q fed to the mma for rows g / g + 8; z0 / z1 the
-// zero-point scalars of rows g / g + 8 (partial over this lane's tokens).
+// One staged pair of int8 (page, head)s: K codes of page a at base, V at
+// base + kBox, page b's at base + 2 kBox / 3 kBox (128-byte rows,
+// 128B-swizzled); st = their stats rows {min, max, scale, zero_point} in the
+// order K a, V a, K b, V b; va / vb: the page is there (a missing page is
+// masked to weight 0, whatever its staged bytes).  qs0 / qs1 = sum of the q
+// fed to the mma for rows g / g + 8; z0 / z1 the zero-point scalars of rows
+// g / g + 8 (partial over this lane's tokens).  Two pages per call give four
+// independent QK accumulation chains and one softmax update per 32 tokens.
 //
 // The weights multiply v - zp = scale * u, which in a block with outliers
 // can be far larger than v itself, so one fp16 rounding of P' would cost up
@@ -275,60 +283,67 @@ __device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t x, uint32_t sel) { retur
 // larger group the lo parts take a second mma into the same accumulators
 // (q lo fragments from shared memory, `qlo`).
 template <bool kBig>
-__device__ __forceinline__ void tc_page_i8(uint32_t kbase, float4 sk, float4 sv, const uint32_t (&qa)[8][4],
-                                           uint32_t qlo, float qs0, float qs1, float (&o)[16][4], float &m0,
-                                           float &m1, float &l0, float &l1, float &z0, float &z1, int tok,
-                                           int T, float scale_log2, int lane) {
+__device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool va, bool vb,
+                                           const uint32_t (&qa)[8][4], uint32_t qlo, float qs0, float qs1,
+                                           float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
+                                           float &z0, float &z1, int tok_a, int tok_b, int T,
+                                           float scale_log2, int lane) {
     const int g = lane >> 2, r = lane & 3;
-    // ---- S = scale * Q (1024 + u) + (zp - 1024 scale) sum(q)
-    float sc[2][4];
-    uint32_t w[2][8];
+    const float4 ska = *reinterpret_cast<const float4 *>(st), sva = *reinterpret_cast<const float4 *>(st + 4);
+    const float4 skb = *reinterpret_cast<const float4 *>(st + 8), svb = *reinterpret_cast<const float4 *>(st + 12);
+    // ---- S = scale * Q (1024 + u) + (zp - 1024 scale) sum(q); tile t = 2 page + j
+    float sc[4][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-        const uint4 a = lds128(kbase + swz(8 * j + g, 2 * r));
-        const uint4 b = lds128(kbase + swz(8 * j + g, 2 * r + 1));
-        w[j][0] = a.x, w[j][1] = a.y, w[j][2] = a.z, w[j][3] = a.w;
-        w[j][4] = b.x, w[j][5] = b.y, w[j][6] = b.z, w[j][7] = b.w;
-    }
+    for (int t = 0; t < 4; ++t) sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.f;
 #pragma unroll
-    for (int kc = 0; kc < 8; ++kc) {
-        uint32_t la[4];
-        if constexpr (kBig) {
-            const uint4 x = lds128(qlo + (kc * 32 + lane) * 16);
-            la[0] = x.x, la[1] = x.y, la[2] = x.z, la[3] = x.w;
-        }
+    for (int half = 0; half < 2; ++half) {  // chunk 2r + half holds k-steps 4 half .. 4 half + 3
+        uint4 kw[4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const uint32_t x = w[j][kc] ^ 0x80808080u;
-            const uint32_t b0 = u8x2_to_h2(x, 0x4140), b1 = u8x2_to_h2(x, 0x4342);
-            mma16816(sc[j], qa[kc], b0, b1);
-            if constexpr (kBig) mma16816(sc[j], la, b0, b1);
+        for (int t = 0; t < 4; ++t) kw[t] = lds128(base + (t >> 1) * 2 * kBox + swz(8 * (t & 1) + g, 2 * r + half));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const int kc = 4 * half + kk;
+            uint32_t la[4];
+            if constexpr (kBig) {
+                const uint4 x = lds128(qlo + (kc * 32 + lane) * 16);
+                la[0] = x.x, la[1] = x.y, la[2] = x.z, la[3] = x.w;
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint32_t w = (kk == 0 ? kw[t].x : kk == 1 ? kw[t].y : kk == 2 ? kw[t].z : kw[t].w) ^ 0x80808080u;
+                const uint32_t b0 = u8x2_to_h2(w, 0x4140), b1 = u8x2_to_h2(w, 0x4342);
+                mma16816(sc[t], qa[kc], b0, b1);
+                if constexpr (kBig) mma16816(sc[t], la, b0, b1);
+            }
         }
     }
     if constexpr (!kBig) {  // q hi (rows 0-7) + q lo (rows 8-15)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            sc[j][0] += sc[j][2];
-            sc[j][1] += sc[j][3];
+        for (int t = 0; t < 4; ++t) {
+            sc[t][0] += sc[t][2];
+            sc[t][1] += sc[t][3];
         }
     }
-    const float kofs = fmaf(-1024.f, sk.z, sk.w);
-    const float c0 = kofs * qs0, c1 = kofs * qs1;
-    // ---- online softmax (log2 domain)
+    // ---- online softmax (log2 domain) over the 32 tokens
+    const float ks[2] = {ska.z * scale_log2, skb.z * scale_log2};
+    const float ko[2] = {fmaf(-1024.f, ska.z, ska.w) * scale_log2, fmaf(-1024.f, skb.z, skb.w) * scale_log2};
+    const bool have[2] = {va, vb};
+    const int tok[2] = {tok_a, tok_b};
     float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int t = 0; t < 4; ++t) {
+        const int pg = t >> 1, j = t & 1;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const bool valid = tok + 8 * j + e < T;
-            sc[j][e] = valid ? fmaf(sc[j][e], sk.z, c0) * scale_log2 : -CUDART_INF_F;
-            mx0 = fmaxf(mx0, sc[j][e]);
+            const bool valid = have[pg] && tok[pg] + 8 * j + e < T;
+            sc[t][e] = valid ? fmaf(sc[t][e], ks[pg], ko[pg] * qs0) : -CUDART_INF_F;
+            mx0 = fmaxf(mx0, sc[t][e]);
             if constexpr (kBig) {
-                sc[j][2 + e] = valid ? fmaf(sc[j][2 + e], sk.z, c1) * scale_log2 : -CUDART_INF_F;
-                mx1 = fmaxf(mx1, sc[j][2 + e]);
+                sc[t][2 + e] = valid ? fmaf(sc[t][2 + e], ks[pg], ko[pg] * qs1) : -CUDART_INF_F;
+                mx1 = fmaxf(mx1, sc[t][2 + e]);
             }
         }
+    }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     const float mn0 = fmaxf(m0, mx0);
@@ -342,43 +357,47 @@ __device__ __forceinline__ void tc_page_i8(uint32_t kbase, float4 sk, float4 sv,
         a1 = exp2f(m1 - mn1);
         m1 = mn1;
     }
-    float ps0 = 0.f, ps1 = 0.f;
+    float ps0[2] = {0.f, 0.f}, ps1[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int t = 0; t < 4; ++t)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            sc[j][e] = exp2f(sc[j][e] - m0);
-            ps0 += sc[j][e];
+            sc[t][e] = exp2f(sc[t][e] - m0);
+            ps0[t >> 1] += sc[t][e];
             if constexpr (kBig) {
-                sc[j][2 + e] = exp2f(sc[j][2 + e] - m1);
-                ps1 += sc[j][2 + e];
+                sc[t][2 + e] = exp2f(sc[t][2 + e] - m1);
+                ps1[t >> 1] += sc[t][2 + e];
             }
         }
-    l0 = l0 * a0 + ps0;
-    if constexpr (kBig) l1 = l1 * a1 + ps1;
-    // P' = p * scale_v as fp16 hi + lo (masked tokens stay exactly 0); the
-    // zero-point scalar takes the rounded values the mma sees
-    auto wv = [&](float pv) { return pv == 0.f ? 0.f : pv * sv.z; };
-    float rs0 = 0.f, rs1 = 0.f;
-    auto split = [&](float x, float y, uint32_t &hi, uint32_t &lo, float &sum) {
+    l0 = l0 * a0 + (ps0[0] + ps0[1]);
+    if constexpr (kBig) l1 = l1 * a1 + (ps1[0] + ps1[1]);
+    // P' = p * scale_v as fp16 hi + lo (masked tokens stay exactly 0).  hi +
+    // lo equals P' to 2^-22 relative, so the zero-point scalar may use the
+    // unrounded sum: (zp - 1024 scale_v) * sum(p), off by < 2.5e-4 * scale_v
+    // of the output.
+    const float svs[2] = {sva.z, svb.z};
+    auto split = [](float x, float y, uint32_t &hi, uint32_t &lo) {
         hi = pack_h2(x, y);
         const float2 h = h2_to_f2(hi);
         lo = pack_h2(x - h.x, y - h.y);
-        const float2 l = h2_to_f2(lo);
-        sum += (h.x + h.y) + (l.x + l.y);
     };
-    uint32_t pa[4], pl[4];
-    split(wv(sc[0][0]), wv(sc[0][1]), pa[0], pl[0], rs0);
-    split(wv(sc[1][0]), wv(sc[1][1]), pa[2], pl[2], rs0);
-    if constexpr (kBig) {
-        split(wv(sc[0][2]), wv(sc[0][3]), pa[1], pl[1], rs1);
-        split(wv(sc[1][2]), wv(sc[1][3]), pa[3], pl[3], rs1);
-        z1 = z1 * a1 + (sv.w * ps1 - 1024.f * rs1);
-    } else {  // rows 8-15: the lo parts
-        pa[1] = pl[0];
-        pa[3] = pl[2];
+    uint32_t pa[2][4], pl[2][4];
+#pragma unroll
+    for (int pg = 0; pg < 2; ++pg) {
+        auto wv = [&](float pv) { return pv == 0.f ? 0.f : pv * svs[pg]; };
+        split(wv(sc[2 * pg][0]), wv(sc[2 * pg][1]), pa[pg][0], pl[pg][0]);
+        split(wv(sc[2 * pg + 1][0]), wv(sc[2 * pg + 1][1]), pa[pg][2], pl[pg][2]);
+        if constexpr (kBig) {
+            split(wv(sc[2 * pg][2]), wv(sc[2 * pg][3]), pa[pg][1], pl[pg][1]);
+            split(wv(sc[2 * pg + 1][2]), wv(sc[2 * pg + 1][3]), pa[pg][3], pl[pg][3]);
+        } else {  // rows 8-15: the lo parts
+            pa[pg][1] = pl[pg][0];
+            pa[pg][3] = pl[pg][2];
+        }
     }
-    z0 = z0 * a0 + (sv.w * ps0 - 1024.f * rs0);
+    const float voa = va ? fmaf(-1024.f, sva.z, sva.w) : 0.f, vob = vb ? fmaf(-1024.f, svb.z, svb.w) : 0.f;
+    z0 = fmaf(z0, a0, fmaf(voa, ps0[0], vob * ps0[1]));
+    if constexpr (kBig) z1 = fmaf(z1, a1, fmaf(voa, ps1[0], vob * ps1[1]));
     if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
@@ -388,37 +407,45 @@ __device__ __forceinline__ void tc_page_i8(uint32_t kbase, float4 sk, float4 sv,
             o[n][3] *= kBig ? a1 : a0;
         }
     }
-    // ---- O += P' (1024 + u): lane (g, r) reads dims 16g .. 16g+15 of tokens
-    // 2r, 2r+1 (B rows k, k+1) and 2r+8, 2r+9 (rows k+8, k+9)
-    const uint32_t vbase = kbase + kBox;
-    const uint4 t0 = lds128(vbase + swz(2 * r, g)), t1 = lds128(vbase + swz(2 * r + 1, g));
-    const uint4 t8 = lds128(vbase + swz(2 * r + 8, g)), t9 = lds128(vbase + swz(2 * r + 9, g));
-    const uint32_t w0[4] = {t0.x, t0.y, t0.z, t0.w}, w1[4] = {t1.x, t1.y, t1.z, t1.w};
-    const uint32_t w8[4] = {t8.x, t8.y, t8.z, t8.w}, w9[4] = {t9.x, t9.y, t9.z, t9.w};
+    // ---- O += P' (1024 + u).  ldmatrix.trans over the V codes as 16-bit
+    // pairs gives lane (g, r) the bytes {V[2r][2g], V[2r][2g+1], V[2r+1][2g],
+    // V[2r+1][2g+1]} of a 16-dim chunk (tokens 8-15 in the next matrix):
+    // bytes 0,2 are B rows k, k+1 of n-tile column "dim 2g", bytes 1,3 of
+    // "dim 2g+1".  n-tile 2c + par, column g = dim 16c + 2g + par.
+    const int lrow = lane & 7, lmat = lane >> 3;
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {  // word a: dims 16g + 4a .. +3 = n-tiles 4a .. 4a+3
-        const uint32_t xlo = __byte_perm(w0[a], w1[a], 0x5140) ^ 0x80808080u;  // tok 2r|2r+1, bytes 0,1
-        const uint32_t xhi = __byte_perm(w0[a], w1[a], 0x7362) ^ 0x80808080u;  // bytes 2,3
-        const uint32_t ylo = __byte_perm(w8[a], w9[a], 0x5140) ^ 0x80808080u;
-        const uint32_t yhi = __byte_perm(w8[a], w9[a], 0x7362) ^ 0x80808080u;
-        const uint32_t b0[4] = {u8x2_to_h2(xlo, 0x4140), u8x2_to_h2(xlo, 0x4342), u8x2_to_h2(xhi, 0x4140),
-                                u8x2_to_h2(xhi, 0x4342)};
-        const uint32_t b1[4] = {u8x2_to_h2(ylo, 0x4140), u8x2_to_h2(ylo, 0x4342), u8x2_to_h2(yhi, 0x4140),
-                                u8x2_to_h2(yhi, 0x4342)};
+    for (int pg = 0; pg < 2; ++pg) {
+        if (!have[pg]) continue;  // warp-uniform
+        const uint32_t vbase = base + pg * 2 * kBox + kBox;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            mma16816(o[4 * a + e], pa, b0[e], b1[e]);
-            if constexpr (kBig) mma16816(o[4 * a + e], pl, b0[e], b1[e]);
+        for (int cp = 0; cp < 4; ++cp) {  // chunks 2cp, 2cp+1
+            const int chunk = 2 * cp + (lmat >> 1);
+            const int vrow = (lmat & 1) * 8 + lrow;
+            uint32_t v0, v1, v2, v3;  // (tok 0-7, chunk 2cp) (8-15, 2cp) (0-7, 2cp+1) (8-15, 2cp+1)
+            ldsm_x4_t(vbase + swz(vrow, chunk), v0, v1, v2, v3);
+            v0 ^= 0x80808080u;
+            v1 ^= 0x80808080u;
+            v2 ^= 0x80808080u;
+            v3 ^= 0x80808080u;
+            const uint32_t b0[4] = {u8x2_to_h2(v0, 0x4240), u8x2_to_h2(v0, 0x4341), u8x2_to_h2(v2, 0x4240),
+                                    u8x2_to_h2(v2, 0x4341)};
+            const uint32_t b1[4] = {u8x2_to_h2(v1, 0x4240), u8x2_to_h2(v1, 0x4341), u8x2_to_h2(v3, 0x4240),
+                                    u8x2_to_h2(v3, 0x4341)};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {  // n-tiles 4cp .. 4cp+3
+                mma16816(o[4 * cp + e], pa[pg], b0[e], b1[e]);
+                if constexpr (kBig) mma16816(o[4 * cp + e], pl[pg], b0[e], b1[e]);
+            }
         }
     }
 }
 
 // Where lane (g, r) parks O element (row, n-tile jn, column 2r + e) for the
-// merge: fp16 kernel dim 8 jn + 2r + e, row stride 128; int8 kernel dim
-// 16 (2r + e) + jn, row stride 132 and the dim's low bits XOR (dim >> 5) so
-// that the 32 lanes of one store hit 32 banks.
+// merge: fp16 kernel dim 8 jn + 2r + e; int8 kernel dim 16 (jn / 2) +
+// 2 (2r + e) + jn % 2, whose bits 2-3 are r, so the row's bits XOR-ed into
+// dim bits 0, 1 and 4 make the 32 lanes of one store hit 32 banks.
 template <bool kI8> __device__ __forceinline__ int park_ofs(int row, int d) {
-    if constexpr (kI8) return row * 132 + (d ^ ((d >> 5) & 3));
+    if constexpr (kI8) return row * kHeadDim + (d ^ ((row & 3) | (((row >> 2) & 1) << 4)));
     return row * kHeadDim + d;
 }
 
@@ -459,7 +486,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     uint8_t *wbuf = smem + warp * kTcStages * kTcStage;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcWarps * kTcStages * kTcStage) + warp * kTcStages;
     float *wstat = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8) +
-                   warp * kTcStages * 8;  // int8: per stage K stats | V stats
+                   warp * kTcStages * Cfg::kStatFloats;  // int8: per stage K a | V a | K b | V b stats
     float *s_m = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8 +
                                            Cfg::kStatBytes);
     float *s_l = s_m + kTcWarps * 16;
@@ -490,18 +517,43 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
     }
 
-    const int n_my = (p1 - p0 - warp + kTcWarps - 1) / kTcWarps;
+    const int n_pg = (p1 - p0 - warp + kTcWarps - 1) / kTcWarps;  // this warp's pages
+    const int n_my = (n_pg + Cfg::kPages - 1) / Cfg::kPages;          // and stages
     const int32_t *bt = p.block_table + (size_t)s * p.max_pages;
     const uint32_t wbase = smem_addr(wbuf);
     // the warp's block-table entries, staged once (one global round trip per
     // warp instead of two per page)
-    for (int i = lane; i < min(n_my, kBtCache); i += 32) wbt[i] = bt[p0 + warp + kTcWarps * i];
+    for (int i = lane; i < min(n_pg, kBtCache); i += 32) wbt[i] = bt[p0 + warp + kTcWarps * i];
     __syncwarp();
     auto phys_of = [&](int i) { return i < kBtCache ? wbt[i] : bt[p0 + warp + kTcWarps * i]; };
 
+    auto page_ok = [&](int phys) { return phys >= 0 && phys < p.num_pages; };
     auto issue = [&](int i, int st) {
-        const int phys = phys_of(i);
         uint64_t *bar = &bars[st];
+        if constexpr (kI8) {  // pages 2i and (if any) 2i + 1 of this warp
+            const int pa_ = phys_of(2 * i), pb_ = 2 * i + 1 < n_pg ? phys_of(2 * i + 1) : 0;
+            const bool va = page_ok(pa_), vb = 2 * i + 1 < n_pg && page_ok(pb_);
+            if ((!va || (2 * i + 1 < n_pg && !vb)) && p.error_flag) atomicOr(p.error_flag, 2);
+            const uint32_t dst = wbase + st * kTcStage, b = smem_addr(bar);
+            float *sd = wstat + st * Cfg::kStatFloats;
+            mbar_arrive_expect_tx(bar, (va ? 2 * kBox + 32 : 0) + (vb ? 2 * kBox + 32 : 0));
+            if (va) {
+                const int kb = (pa_ * 2) * p.hkv + kvh;  // (page, K, head) block; V block = kb + hkv
+                tma_load_2d(dst, &tm, 0, kb * kPageTokens, b);
+                tma_load_2d(dst + kBox, &tm, 0, (kb + p.hkv) * kPageTokens, b);
+                bulk_g2s(sd, p.stats + (size_t)kb * 4, 16, bar);
+                bulk_g2s(sd + 4, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
+            }
+            if (vb) {
+                const int kb = (pb_ * 2) * p.hkv + kvh;
+                tma_load_2d(dst + 2 * kBox, &tm, 0, kb * kPageTokens, b);
+                tma_load_2d(dst + 3 * kBox, &tm, 0, (kb + p.hkv) * kPageTokens, b);
+                bulk_g2s(sd + 8, p.stats + (size_t)kb * 4, 16, bar);
+                bulk_g2s(sd + 12, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
+            }
+            return;
+        }
+        const int phys = phys_of(i);
         if (phys < 0 || phys >= p.num_pages) {
             if (p.error_flag) atomicOr(p.error_flag, 2);
             mbar_arrive_expect_tx(bar, 0);
@@ -512,19 +564,11 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         const int yv = yk + p.hkv * kPageTokens;
         const uint32_t dst = wbase + st * kTcStage;
         const uint32_t b = smem_addr(bar);
-        if constexpr (kI8) {
-            mbar_arrive_expect_tx(bar, kTcStage + 32);
-            tma_load_2d(dst, &tm, 0, yk, b);
-            tma_load_2d(dst + kBox, &tm, 0, yv, b);
-            bulk_g2s(wstat + st * 8, p.stats + (size_t)kb * 4, 16, bar);
-            bulk_g2s(wstat + st * 8 + 4, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
-        } else {
-            mbar_arrive_expect_tx(bar, kTcStage);
-            tma_load_2d(dst, &tm, 0, yk, b);
-            tma_load_2d(dst + kBox, &tm, 64, yk, b);
-            tma_load_2d(dst + 2 * kBox, &tm, 0, yv, b);
-            tma_load_2d(dst + 3 * kBox, &tm, 64, yv, b);
-        }
+        mbar_arrive_expect_tx(bar, kTcStage);
+        tma_load_2d(dst, &tm, 0, yk, b);
+        tma_load_2d(dst + kBox, &tm, 64, yk, b);
+        tma_load_2d(dst + 2 * kBox, &tm, 0, yv, b);
+        tma_load_2d(dst + 3 * kBox, &tm, 64, yv, b);
     };
     if (lane == 0)
         for (int i = 0; i < min(kTcStages, n_my); ++i) issue(i, i);
@@ -589,10 +633,19 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
             break;
         }
         done = i + 1;
+        const uint32_t sbase = wbase + st * kTcStage;
+        if constexpr (kI8) {
+            const int lpa = p0 + warp + kTcWarps * (2 * i);
+            const bool va = page_ok(phys_of(2 * i));
+            const bool vb = 2 * i + 1 < n_pg && page_ok(phys_of(2 * i + 1));
+            if (va || vb)
+                tc_pair_i8<kBig>(sbase, wstat + st * Cfg::kStatFloats, va, vb, qa, qlo, qs0, qs1, o, m0, m1, l0,
+                                 l1, z0, z1, lpa * kPageTokens + 2 * (lane & 3),
+                                 (lpa + kTcWarps) * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane);
+        }
         const int lp = p0 + warp + kTcWarps * i;
         const int phys = phys_of(i);
-        const uint32_t sbase = wbase + st * kTcStage;
-        if (phys >= 0 && phys < p.num_pages) {
+        if (!kI8 && phys >= 0 && phys < p.num_pages) {
             if (lp == lp_new) {  // fused append: patch the new rows into the staged tiles
                 const int kv = lane >> 4, c = lane & 15;
                 const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;
@@ -601,15 +654,8 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
                     reinterpret_cast<const uint4 *>(src)[c];
                 __syncwarp();
             }
-            if constexpr (kI8) {
-                const float4 sk = *reinterpret_cast<const float4 *>(wstat + st * 8);
-                const float4 sv = *reinterpret_cast<const float4 *>(wstat + st * 8 + 4);
-                tc_page_i8<kBig>(sbase, sk, sv, qa, qlo, qs0, qs1, o, m0, m1, l0, l1, z0, z1,
-                                 lp * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane);
-            } else {
-                tc_page<kBig>(sbase, qa, qlo, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
-                              p.scale_log2, lane);
-            }
+            tc_page<kBig>(sbase, qa, qlo, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
+                          p.scale_log2, lane);
         }
         __syncwarp();
         if (lane == 0 && i + kTcStages < n_my) {
@@ -651,7 +697,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         for (int n = 0; n < 16; ++n)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const int d = 16 * (2 * tq + e) + n;
+                const int d = 16 * (n >> 1) + 2 * (2 * tq + e) + (n & 1);
                 if constexpr (kBig) {
                     wacc[park_ofs<true>(gq, d)] = o[n][e] + z0;
                     wacc[park_ofs<true>(gq + 8, d)] = o[n][2 + e] + z1;
