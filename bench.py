@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
+    ap.add_argument("--pages", type=int, default=1 << 20,
+                    help="config 3: pages compressed (1,048,576 defines the configuration; fewer for profiling)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     return ap.parse_args()
@@ -452,7 +454,7 @@ def run_config3(args):
     import torch
     import kvx
     peak, peak_kind = peaks()
-    pages = 1 << 20
+    pages = args.pages
     blocks = pages * HKV  # one (page, head) block of 2048 elements
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED + 3)
@@ -491,9 +493,9 @@ def run_config3(args):
     ws = kvx.decode_workspace(B, HQ, npg)
     ms_q = _events_time(lambda: kvx.decode(pool, bt, lens, q, stats=pstats, workspace=ws), 20)
     q_bytes = B * T * 2 * HKV * DIM * 1 + B * npg * 2 * HKV * 16
-    cpu = cpu_compress_baseline()
+    cpu = cpu_compress_baseline() if not args.no_cpu_baseline else None
     print(json.dumps({
-        "config": 3, "workload": "1,048,576 pages x 16 tok x 8 heads x 128 fp16, 1% outliers x20; int8 per (page, head)",
+        "config": 3, "workload": f"{pages:,} pages x 16 tok x 8 heads x 128 fp16, 1% outliers x20; int8 per (page, head)",
         "compress": {"GBps": round(c_bytes / (ms_c / 1e3) / 1e9, 1), "ms": round(ms_c, 3),
                      "frac_of_peak": round(c_bytes / (ms_c / 1e3) / 1e9 / peak, 3)},
         "decompress": {"GBps": round(d_bytes / (ms_d / 1e3) / 1e9, 1), "ms": round(ms_d, 3),
