@@ -107,14 +107,12 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 // they occupy no long-lived registers.
 __device__ __forceinline__ void mma16816_lo(float &c0, float &c1, const uint32_t (&a)[4], uint32_t b0,
                                             uint32_t b1) {
-    float d2, d3;
+    float d2 __attribute__((unused)), d3 __attribute__((unused));  // rows 8-15, discarded
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%10,%11,%12,%12};"
         : "=f"(c0), "=f"(c1), "=f"(d2), "=f"(d3)
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f));
-    (void)d2;
-    (void)d3;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
@@ -149,7 +147,7 @@ template <bool kBig>
 __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][4], uint32_t qlo,
                                         float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
                                         int tok, int T, float scale_log2, int lane) {
-    const int tq = lane & 3, lrow = lane & 7, lmat = lane >> 3;
+    const int lrow = lane & 7, lmat = lane >> 3;
     // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
     float sc[2][4];
 #pragma unroll
@@ -505,7 +503,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     const int lp_new = append_ok ? p.positions[s] / kPageTokens : -1;
     const int slot_new = append_ok ? p.positions[s] % kPageTokens : 0;
     if (append_ok && lp_new >= p0 && lp_new < p1 && warp == 0) {
-        const int phys = p.block_table[(size_t)s * p.max_pages + lp_new];
+        const int phys = p.block_table[(size_t)s * p.max_pages + (size_t)lp_new];
         if (phys >= 0 && phys < p.num_pages) {
             const int kv = lane >> 4, e = lane & 15;  // 2 rows x 16 vectors of 16 B
             const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;

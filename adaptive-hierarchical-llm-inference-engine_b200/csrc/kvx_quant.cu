@@ -6,8 +6,14 @@
 //    (2048 elements = one (page, K|V, head) block at 16 x 128), 16-byte
 //    loads, the block held in registers between the min/max pass and the
 //    quantise pass, 16-byte code stores.
+//  * NF4 (uniform 4-bit) per-block quantisation, bit-exact with
+//    compressToNF4 / decompressNF4 (KVCompressionEngine.cpp:124-180): the
+//    same pipeline with 15 levels and two codes per byte (high nibble
+//    first).
 //  * the truncating fp32<->fp16 converter of the disk tier, bit-exact with
-//    float_to_half / half_to_float (compression/kv_compress.cpp:6-46).
+//    float_to_half / half_to_float (compression/kv_compress.cpp:6-46), and
+//    the engine's own exponent-wrapping FP16 codec (compressToFP16 /
+//    decompressFP16, KVCompressionEngine.cpp:36-80).
 //
 // Bit-exactness notes.  The reference is plain x86-64 SSE fp32 without FMA,
 // so every step here uses the explicitly rounded intrinsics (__fsub_rn,
@@ -42,11 +48,17 @@ __device__ __forceinline__ float x86_nan(float r, float a, float b) {
     return __uint_as_float(0xFFC00000u);
 }
 
-__device__ __forceinline__ int8_t quant_one(float x, float mn, float scale) {
+// clamp((int)std::round((x - mn) / scale), 0, kLevels) with the reference's
+// rounding and x86 conversion.
+template <int kLevels>
+__device__ __forceinline__ int32_t quant_level(float x, float mn, float scale) {
     const float normalized = __fdiv_rn(__fsub_rn(x, mn), scale);
     int32_t q = cvt_trunc_i32_x86(roundf(normalized));
-    q = q < 0 ? 0 : (q > 255 ? 255 : q);
-    return (int8_t)(q - 128);
+    return q < 0 ? 0 : (q > kLevels ? kLevels : q);
+}
+
+__device__ __forceinline__ int8_t quant_one(float x, float mn, float scale) {
+    return (int8_t)(quant_level<255>(x, mn, scale) - 128);
 }
 
 // (value, index) candidates in index order; strict comparisons keep the
@@ -87,6 +99,7 @@ template <> __device__ __forceinline__ float ld_elem<__half>(const __half *p, si
 }
 
 // Finish stats from the reduced min/max; writes stats[4] from lane 0.
+template <int kLevels>
 __device__ __forceinline__ void finish_stats(MinMax r, float first, float *stats, int lane,
                                              float &mn, float &scale) {
     if (first != first) {  // NaN first element: the reference keeps NaN
@@ -95,7 +108,7 @@ __device__ __forceinline__ void finish_stats(MinMax r, float first, float *stats
     }
     mn = r.mn;
     const float range = x86_nan(__fsub_rn(r.mx, r.mn), r.mx, r.mn);
-    float sc = x86_nan(__fdiv_rn(range, 255.0f), range, 255.0f);
+    float sc = x86_nan(__fdiv_rn(range, (float)kLevels), range, (float)kLevels);
     if (sc == 0.0f) sc = 1.0f;
     scale = sc;
     if (lane == 0) *reinterpret_cast<float4 *>(stats) = make_float4(r.mn, r.mx, sc, r.mn);
@@ -126,10 +139,12 @@ __device__ __forceinline__ float max_nan(float a, float b) {  // NaN wins
 // second pass pick the first such element in index order.  Codes come from
 // the reciprocal shortcut above; a lane holding a near-tie or a NaN then
 // rewrites those codes with the exact division (quant_one).
-template <typename T>
+template <typename T, int kLevels>
 __global__ void __launch_bounds__(256)
-compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
+compress_2048_kernel(const T *__restrict__ src, uint8_t *__restrict__ codes,
                      float *__restrict__ stats, size_t num_blocks) {
+    constexpr bool kNf4 = kLevels == 15;
+    constexpr int kCodeBytes = kNf4 ? 1024 : 2048;  // code bytes per block
     constexpr int kBlock = 2048;
     constexpr int kPerVec = 16 / sizeof(T);             // elements per 16-byte load
     constexpr int kVecs = kBlock / kPerVec / 32;        // loads per lane
@@ -185,9 +200,9 @@ compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
             a = mm_warp_reduce(z);
         }
         float mnv, scale;
-        finish_stats(a, first, stats + 4 * b, lane, mnv, scale);
+        finish_stats<kLevels>(a, first, stats + 4 * b, lane, mnv, scale);
         const float rcp = __frcp_rn(scale);
-        int8_t *out = codes + b * kBlock;
+        uint8_t *out = codes + b * kCodeBytes;
         if (isfinite(scale) && isfinite(rcp)) {  // warp-uniform; mn, mx finite too
             float worst = 0.f;
 #pragma unroll
@@ -204,38 +219,63 @@ compress_2048_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
                         worst = max_nan(worst, fabsf(__fsub_rn(t, __fsub_rn(s, kTwo23))));
                         u[k] = __float_as_uint(s);
                     }
-                    word[k4] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040),
-                                           0x5410) ^ 0x80808080u;
+                    if constexpr (kNf4)  // 2 bytes: (q0 << 4 | q1), (q2 << 4 | q3)
+                        word[k4] = ((u[0] & 0xFu) << 4) | (u[1] & 0xFu) | ((u[2] & 0xFu) << 12) |
+                                   ((u[3] & 0xFu) << 8);
+                    else
+                        word[k4] = __byte_perm(__byte_perm(u[0], u[1], 0x0040),
+                                               __byte_perm(u[2], u[3], 0x0040), 0x5410) ^ 0x80808080u;
                 }
-                if constexpr (kPerVec == 8)
-                    __stcs(reinterpret_cast<uint2 *>(out) + j * 32 + lane, make_uint2(word[0], word[1]));
-                else
-                    __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0]);
+                if constexpr (kNf4) {
+                    if constexpr (kPerVec == 8)
+                        __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0] | (word[1] << 16));
+                    else
+                        __stcs(reinterpret_cast<unsigned short *>(out) + j * 32 + lane, (unsigned short)word[0]);
+                } else {
+                    if constexpr (kPerVec == 8)
+                        __stcs(reinterpret_cast<uint2 *>(out) + j * 32 + lane, make_uint2(word[0], word[1]));
+                    else
+                        __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0]);
+                }
             }
             if (!(worst <= kTieLimit)) {  // rare: near-ties or NaN in this lane
 #pragma unroll 1
                 for (int j = 0; j < kVecs; ++j) {
                     const int base = (j * 32 + lane) * kPerVec;
+                    if constexpr (kNf4) {  // redo the lane's bytes exactly (two codes each)
 #pragma unroll 1
-                    for (int k = 0; k < kPerVec; ++k) {
-                        const float x = ld_elem<T>(in, base + k);
-                        const float t = __fmul_rn(__fsub_rn(x, mnv), rcp);
-                        if (!(fabsf(__fsub_rn(t, rintf(t))) <= kTieLimit))
-                            out[base + k] = quant_one(x, mnv, scale);
+                        for (int k = 0; k < kPerVec; k += 2)
+                            out[(base + k) / 2] = (uint8_t)((quant_level<15>(ld_elem<T>(in, base + k), mnv, scale) << 4) |
+                                                            quant_level<15>(ld_elem<T>(in, base + k + 1), mnv, scale));
+                    } else {
+#pragma unroll 1
+                        for (int k = 0; k < kPerVec; ++k) {
+                            const float x = ld_elem<T>(in, base + k);
+                            const float t = __fmul_rn(__fsub_rn(x, mnv), rcp);
+                            if (!(fabsf(__fsub_rn(t, rintf(t))) <= kTieLimit))
+                                out[base + k] = (uint8_t)quant_one(x, mnv, scale);
+                        }
                     }
                 }
             }
         } else {  // inf / NaN range or denormal scale: exact division throughout
+            if constexpr (kNf4) {
 #pragma unroll 1
-            for (int i = lane; i < kBlock; i += 32) out[i] = quant_one(ld_elem<T>(in, i), mnv, scale);
+                for (int i = lane; i < kBlock / 2; i += 32)
+                    out[i] = (uint8_t)((quant_level<15>(ld_elem<T>(in, 2 * i), mnv, scale) << 4) |
+                                       quant_level<15>(ld_elem<T>(in, 2 * i + 1), mnv, scale));
+            } else {
+#pragma unroll 1
+                for (int i = lane; i < kBlock; i += 32) out[i] = (uint8_t)quant_one(ld_elem<T>(in, i), mnv, scale);
+            }
         }
     }
 }
 
 // Generic path: any block size, one warp per block, two passes over global.
-template <typename T>
+template <typename T, int kLevels>
 __global__ void __launch_bounds__(256)
-compress_generic_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
+compress_generic_kernel(const T *__restrict__ src, uint8_t *__restrict__ codes,
                         float *__restrict__ stats, size_t num_blocks, int block_elems) {
     const int lane = threadIdx.x & 31;
     const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
@@ -249,9 +289,19 @@ compress_generic_kernel(const T *__restrict__ src, int8_t *__restrict__ codes,
         if (a.imn == (1 << 30)) a.mn = first;
         if (a.imx == (1 << 30)) a.mx = first;
         float mn, scale;
-        finish_stats(a, first, stats + 4 * b, lane, mn, scale);
-        int8_t *out = codes + b * (size_t)block_elems;
-        for (int i = lane; i < block_elems; i += 32) out[i] = quant_one(ld_elem<T>(in, i), mn, scale);
+        finish_stats<kLevels>(a, first, stats + 4 * b, lane, mn, scale);
+        if constexpr (kLevels == 15) {  // two codes per byte, high nibble first; odd tail -> 0
+            const int nb = (block_elems + 1) / 2;
+            uint8_t *out = codes + b * (size_t)nb;
+            for (int i = lane; i < nb; i += 32) {
+                const int32_t q1 = quant_level<15>(ld_elem<T>(in, 2 * i), mn, scale);
+                const int32_t q2 = 2 * i + 1 < block_elems ? quant_level<15>(ld_elem<T>(in, 2 * i + 1), mn, scale) : 0;
+                out[i] = (uint8_t)((q1 << 4) | q2);
+            }
+        } else {
+            uint8_t *out = codes + b * (size_t)block_elems;
+            for (int i = lane; i < block_elems; i += 32) out[i] = (uint8_t)quant_one(ld_elem<T>(in, i), mn, scale);
+        }
     }
 }
 
@@ -386,6 +436,120 @@ decode_trunc_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, s
         dst[i] = f16_trunc_to_f32(src[i]);
 }
 
+__device__ __forceinline__ float dequant_level(uint32_t q, float zp, float scale) {
+    const float qf = (float)q;
+    const float m = x86_nan(__fmul_rn(qf, scale), qf, scale);
+    return x86_nan(__fadd_rn(zp, m), zp, m);
+}
+
+template <typename T> __device__ __forceinline__ void st_out(T *p, float v);
+template <> __device__ __forceinline__ void st_out<float>(float *p, float v) { *p = v; }
+template <> __device__ __forceinline__ void st_out<__half>(__half *p, float v) { *p = __float2half_rn(v); }
+
+// NF4 decode, warp per 2048-element block: 1024 code bytes as two 16-byte
+// loads per lane, 64 values out per lane.
+template <typename T>
+__global__ void __launch_bounds__(256)
+decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ stats,
+                           T *__restrict__ dst, size_t num_blocks) {
+    const int lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
+         b += warps) {
+        const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
+        const float scale = st.z, zp = st.w;
+        const bool finite = isfinite(scale) && isfinite(zp);
+        const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 1024);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint4 w = __ldcs(src + j * 32 + lane);
+            const uint8_t *c = reinterpret_cast<const uint8_t *>(&w);
+            float v[32];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const uint32_t hi = c[k] >> 4, lo = c[k] & 0xFu;
+                v[2 * k] = finite ? __fadd_rn(zp, __fmul_rn((float)hi, scale)) : dequant_level(hi, zp, scale);
+                v[2 * k + 1] = finite ? __fadd_rn(zp, __fmul_rn((float)lo, scale)) : dequant_level(lo, zp, scale);
+            }
+            const size_t e0 = (size_t)b * 2048 + (size_t)(j * 32 + lane) * 32;
+            if constexpr (sizeof(T) == 4) {
+                float4 *o = reinterpret_cast<float4 *>(dst + e0);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) __stcs(o + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+            } else {
+                uint4 o[4];
+                uint32_t *u = reinterpret_cast<uint32_t *>(o);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+                    u[k] = *reinterpret_cast<uint32_t *>(&h);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) __stcs(reinterpret_cast<uint4 *>(dst + e0) + k, o[k]);
+            }
+        }
+    }
+}
+
+// NF4 decode, any block size: one thread per element.
+template <typename T>
+__global__ void decompress_nf4_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ stats,
+                                      T *__restrict__ dst, size_t num_blocks, int block_elems) {
+    const size_t n = num_blocks * (size_t)block_elems;
+    const size_t cb = (size_t)(block_elems + 1) / 2;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += stride) {
+        const size_t b = e / (size_t)block_elems, i = e % (size_t)block_elems;
+        const uint32_t byte = codes[b * cb + i / 2];
+        const uint32_t q = (i & 1) ? (byte & 0xFu) : (byte >> 4);
+        st_out<T>(dst + e, dequant_level(q, stats[4 * b + 3], stats[4 * b + 2]));
+    }
+}
+
+// compressToFP16 (KVCompressionEngine.cpp:36-61): Inf/NaN -> +-Inf, zero
+// exponent -> +-0, else exponent rebiased modulo 32, mantissa truncated.
+__device__ __forceinline__ uint32_t fp16_wrap_enc(float f) {
+    const uint32_t bits = __float_as_uint(f);
+    const uint32_t sign = bits >> 31, e = (bits >> 23) & 0xFFu, m = bits & 0x7FFFFFu;
+    if (e == 0xFFu) return (sign << 15) | 0x7C00u;
+    if (e == 0u) return sign << 15;
+    return (sign << 15) | ((((int32_t)e - 127 + 15) & 0x1F) << 10) | ((m >> 13) & 0x3FFu);
+}
+
+// decompressFP16 (KVCompressionEngine.cpp:63-80): exponent rebiased modulo
+// 256 with no special cases.
+__device__ __forceinline__ float fp16_wrap_dec(uint32_t h) {
+    const uint32_t sign = (h >> 15) & 1u, e = (h >> 10) & 0x1Fu, m = h & 0x3FFu;
+    return __uint_as_float((sign << 31) | (((e + 112u) & 0xFFu) << 23) | (m << 13));
+}
+
+__global__ void fp16_wrap_encode_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, size_t n,
+                                        bool vec) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t quads = vec ? n / 4 : 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(src) + i);
+        __stcs(reinterpret_cast<uint2 *>(dst) + i,
+               make_uint2(fp16_wrap_enc(v.x) | (fp16_wrap_enc(v.y) << 16), fp16_wrap_enc(v.z) | (fp16_wrap_enc(v.w) << 16)));
+    }
+    for (size_t i = quads * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = (uint16_t)fp16_wrap_enc(src[i]);
+}
+
+__global__ void fp16_wrap_decode_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, size_t n,
+                                        bool vec) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t quads = vec ? n / 4 : 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += stride) {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src) + i);
+        __stcs(reinterpret_cast<float4 *>(dst) + i,
+               make_float4(fp16_wrap_dec(v.x & 0xFFFFu), fp16_wrap_dec(v.x >> 16), fp16_wrap_dec(v.y & 0xFFFFu),
+                           fp16_wrap_dec(v.y >> 16)));
+    }
+    for (size_t i = quads * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = fp16_wrap_dec(src[i]);
+}
+
 unsigned grid_for(size_t work, int per_block) {
     size_t b = (work + per_block - 1) / per_block;
     const size_t cap = 148ull * 16;  // persistent-ish: 16 CTAs per SM, grid-stride beyond
@@ -410,17 +574,85 @@ extern "C" KVX_API int kvx_compress_int8(const void *src, int32_t src_dtype, int
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = grid_for(num_blocks, 8);
     const bool fast = block_elems == 2048 && aligned16(src) && aligned16(codes);
+    uint8_t *c = reinterpret_cast<uint8_t *>(codes);
     if (src_dtype == KVX_F16) {
         if (fast)
-            compress_2048_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks);
+            compress_2048_kernel<__half, 255><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks);
         else
-            compress_generic_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks, block_elems);
+            compress_generic_kernel<__half, 255><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks, block_elems);
     } else {
         if (fast)
-            compress_2048_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks);
+            compress_2048_kernel<float, 255><<<grid, 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks);
         else
-            compress_generic_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks, block_elems);
+            compress_generic_kernel<float, 255><<<grid, 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks, block_elems);
     }
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_compress_nf4(const void *src, int32_t src_dtype, uint8_t *codes, float *stats,
+                                        size_t num_blocks, int32_t block_elems, void *stream) {
+    if (!src || !codes || !stats || block_elems <= 0) return KVX_EINVAL;
+    if (src_dtype != KVX_F16 && src_dtype != KVX_F32) return KVX_EINVAL;
+    if (!aligned16(stats)) return KVX_EINVAL;
+    if (num_blocks == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(num_blocks, 8);
+    const bool fast = block_elems == 2048 && aligned16(src) && aligned16(codes);
+    if (src_dtype == KVX_F16) {
+        if (fast)
+            compress_2048_kernel<__half, 15><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks);
+        else
+            compress_generic_kernel<__half, 15><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks, block_elems);
+    } else {
+        if (fast)
+            compress_2048_kernel<float, 15><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks);
+        else
+            compress_generic_kernel<float, 15><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks, block_elems);
+    }
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_decompress_nf4(const uint8_t *codes, const float *stats, void *dst, int32_t dst_dtype,
+                                          size_t num_blocks, int32_t block_elems, void *stream) {
+    if (!codes || !stats || !dst || block_elems <= 0) return KVX_EINVAL;
+    if (dst_dtype != KVX_F16 && dst_dtype != KVX_F32) return KVX_EINVAL;
+    const size_t esz = dst_dtype == KVX_F32 ? 4 : 2;
+    if (!aligned16(stats) || (reinterpret_cast<uintptr_t>(dst) & (esz - 1))) return KVX_EINVAL;
+    if (num_blocks == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (block_elems == 2048 && aligned16(codes) && aligned16(dst)) {
+        const unsigned grid = grid_for(num_blocks, 8);
+        if (dst_dtype == KVX_F32)
+            decompress_nf4_2048_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+        else
+            decompress_nf4_2048_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+        return launch_status();
+    }
+    const unsigned grid = grid_for(num_blocks * (size_t)block_elems, 256);
+    if (dst_dtype == KVX_F32)
+        decompress_nf4_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+    else
+        decompress_nf4_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_fp16_wrap_encode(const float *src, uint16_t *dst, size_t n, void *stream) {
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(dst) & 1))
+        return KVX_EINVAL;
+    if (n == 0) return KVX_OK;
+    const bool vec = aligned16(src) && !(reinterpret_cast<uintptr_t>(dst) & 7);
+    fp16_wrap_encode_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, dst, n, vec);
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_fp16_wrap_decode(const uint16_t *src, float *dst, size_t n, void *stream) {
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 1) || (reinterpret_cast<uintptr_t>(dst) & 3))
+        return KVX_EINVAL;
+    if (n == 0) return KVX_OK;
+    const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
+    fp16_wrap_decode_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, dst, n, vec);
     return launch_status();
 }
 

@@ -195,7 +195,8 @@ int issue(kvx_tier *t, int parity) {
         std::memcpy(st + sp, t->h2d_host.data(), nh * sizeof(int32_t));
     }
     const int prev = parity ^ 1;
-    const int ctas = t->cfg.copy_ctas > 0 ? t->cfg.copy_ctas : 8;
+    const int load_ctas = t->cfg.load_ctas > 0 ? t->cfg.load_ctas : 16;
+    const int store_ctas = t->cfg.store_ctas > 0 ? t->cfg.store_ctas : 4;
     const int32_t dcap = (int32_t)t->dev_slots, hcap = (int32_t)t->host_slots;
     // write-backs
     if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_d2h, t->ev_h2d[prev], 0) != cudaSuccess) return KVX_ECUDA;
@@ -206,7 +207,7 @@ int issue(kvx_tier *t, int parity) {
                 cudaSuccess)
             return KVX_ECUDA;
         const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl + 2 * sp, dl + 3 * sp, nd,
-                                          t->cfg.frame_bytes, 0, ctas, t->err, t->s_d2h);
+                                          t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
         if (rc != KVX_OK) return rc;
     }
     if (cudaEventRecord(t->ev_d2h[parity], t->s_d2h) != cudaSuccess) return KVX_ECUDA;
@@ -219,7 +220,7 @@ int issue(kvx_tier *t, int parity) {
                 cudaSuccess)
             return KVX_ECUDA;
         const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl, dl + sp, nh,
-                                          t->cfg.frame_bytes, 1, ctas, t->err, t->s_h2d);
+                                          t->cfg.frame_bytes, 1, load_ctas, t->err, t->s_h2d);
         if (rc != KVX_OK) return rc;
     }
     if (cudaEventRecord(t->ev_h2d[parity], t->s_h2d) != cudaSuccess) return KVX_ECUDA;

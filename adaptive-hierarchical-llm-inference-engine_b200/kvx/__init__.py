@@ -71,11 +71,16 @@ lib.kvx_decode_noalloc.restype = C.c_int
 lib.kvx_decode_noalloc_scratch_bytes.restype = _sz
 lib.kvx_compress_int8.argtypes = [_vp, _i32, _vp, _vp, _sz, _i32, _vp]
 lib.kvx_decompress_int8.argtypes = [_vp, _vp, _vp, _i32, _sz, _i32, _vp]
+lib.kvx_compress_nf4.argtypes = [_vp, _i32, _vp, _vp, _sz, _i32, _vp]
+lib.kvx_decompress_nf4.argtypes = [_vp, _vp, _vp, _i32, _sz, _i32, _vp]
+lib.kvx_fp16_wrap_encode.argtypes = [_vp, _vp, _sz, _vp]
+lib.kvx_fp16_wrap_decode.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_f32_to_f16_trunc.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_f16_trunc_to_f32.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_lru_select.argtypes = [_vp, _sz, _vp, _vp]
 lib.kvx_migrate_frames.argtypes = [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _sz, _i32, _i32, _vp, _vp]
 for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
+            "kvx_compress_nf4", "kvx_decompress_nf4", "kvx_fp16_wrap_encode", "kvx_fp16_wrap_decode",
             "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
             "kvx_migrate_frames"):
     getattr(lib, _fn).restype = C.c_int
@@ -197,6 +202,49 @@ def decompress_int8(codes, stats, dtype=None, block_elems=PAGE_TOKENS * HEAD_DIM
     rc = lib.kvx_decompress_int8(_ptr(codes), _ptr(stats), _ptr(out), _dtype_code(out),
                                  codes.numel() // block_elems, block_elems, _stream(stream))
     _check("kvx_decompress_int8", rc)
+    return out
+
+
+def compress_nf4(src, block_elems=PAGE_TOKENS * HEAD_DIM, codes=None, stats=None, stream=None):
+    """KVCompressionEngine NF4 per block: codes (uint8, two per byte) and stats."""
+    torch = _torch()
+    nb = src.numel() // block_elems
+    if codes is None:
+        codes = torch.empty(nb * ((block_elems + 1) // 2), dtype=torch.uint8, device=src.device)
+    if stats is None:
+        stats = torch.empty((nb, 4), dtype=torch.float32, device=src.device)
+    rc = lib.kvx_compress_nf4(_ptr(src), _dtype_code(src), _ptr(codes), _ptr(stats), nb, block_elems,
+                              _stream(stream))
+    _check("kvx_compress_nf4", rc)
+    return codes, stats
+
+
+def decompress_nf4(codes, stats, dtype=None, block_elems=PAGE_TOKENS * HEAD_DIM, out=None, stream=None):
+    torch = _torch()
+    dtype = dtype or torch.float32
+    nb = stats.numel() // 4
+    if out is None:
+        out = torch.empty(nb * block_elems, dtype=dtype, device=codes.device)
+    rc = lib.kvx_decompress_nf4(_ptr(codes), _ptr(stats), _ptr(out), _dtype_code(out), nb, block_elems,
+                                _stream(stream))
+    _check("kvx_decompress_nf4", rc)
+    return out
+
+
+def fp16_wrap_encode(x, out=None, stream=None):
+    """KVCompressionEngine FP16 (exponent-wrapping): fp32 -> uint16 bits as int16 tensor."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(x.numel(), dtype=torch.int16, device=x.device)
+    _check("kvx_fp16_wrap_encode", lib.kvx_fp16_wrap_encode(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
+    return out
+
+
+def fp16_wrap_decode(h, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(h.numel(), dtype=torch.float32, device=h.device)
+    _check("kvx_fp16_wrap_decode", lib.kvx_fp16_wrap_decode(_ptr(h), _ptr(out), h.numel(), _stream(stream)))
     return out
 
 

@@ -25,7 +25,8 @@ from . import HEAD_DIM, KVX_F16, PAGE_TOKENS, KvPaged, _check, lib
 
 class TierConfig(C.Structure):
     _fields_ = [("frame_bytes", C.c_size_t), ("universe", C.c_int64), ("capacity", C.c_int64),
-                ("spare", C.c_int64), ("device", C.c_int32), ("copy_ctas", C.c_int32)]
+                ("spare", C.c_int64), ("device", C.c_int32), ("load_ctas", C.c_int32),
+                ("store_ctas", C.c_int32)]
 
 
 _STAT_FIELDS = ("accesses", "hits", "misses", "evictions", "reloads", "frames_h2d", "frames_d2h")
@@ -76,8 +77,8 @@ class _DeviceBytes:
 
 
 class Tier:
-    def __init__(self, frame_bytes, universe, capacity, spare, device=0, copy_ctas=0):
-        self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, copy_ctas)
+    def __init__(self, frame_bytes, universe, capacity, spare, device=0, load_ctas=0, store_ctas=0):
+        self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, load_ctas, store_ctas)
         h = _vp()
         _check("kvx_tier_create", lib.kvx_tier_create(C.byref(self.cfg), C.byref(h)))
         self.h = h

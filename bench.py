@@ -479,7 +479,20 @@ def run_config3(args):
     n = x.numel()
     c_bytes = n * 2 + n + blocks * 16
     d_bytes = n + blocks * 16 + n * 2
-    del back
+    # the engine's other codecs on the same pages: NF4 (uniform 4-bit) ...
+    nf4_codes = torch.empty(n // 2, device="cuda", dtype=torch.uint8)
+    nf4_stats = torch.empty((blocks, 4), device="cuda", dtype=torch.float32)
+    ms_nc = _events_time(lambda: kvx.compress_nf4(x, codes=nf4_codes, stats=nf4_stats), 5)
+    ms_nd = _events_time(lambda: kvx.decompress_nf4(nf4_codes, nf4_stats, dtype=torch.float16, out=back), 5)
+    nc_bytes = n * 2 + n // 2 + blocks * 16
+    del nf4_codes, nf4_stats, back
+    # ... and the exponent-wrapping FP16 of fp32 data (4 GiB in)
+    x32 = torch.randn(1 << 30, generator=g, device="cuda", dtype=torch.float32)
+    h16 = torch.empty(1 << 30, device="cuda", dtype=torch.int16)
+    ms_we = _events_time(lambda: kvx.fp16_wrap_encode(x32, out=h16), 5)
+    ms_wd = _events_time(lambda: kvx.fp16_wrap_decode(h16, out=x32), 5)
+    w_bytes = (1 << 30) * 6
+    del x32, h16
     # decode over int8 pages: batch 32, context 4096, one layer, 24 q-heads
     B, T = 32, 4096
     npg = T // PT
@@ -501,6 +514,14 @@ def run_config3(args):
         "decompress": {"GBps": round(d_bytes / (ms_d / 1e3) / 1e9, 1), "ms": round(ms_d, 3),
                        "frac_of_peak": round(d_bytes / (ms_d / 1e3) / 1e9 / peak, 3)},
         "roundtrip_error_within_scale_half": bool(err),
+        "nf4": {"compress_GBps": round(nc_bytes / (ms_nc / 1e3) / 1e9, 1),
+                "compress_frac_of_peak": round(nc_bytes / (ms_nc / 1e3) / 1e9 / peak, 3),
+                "decompress_GBps": round(nc_bytes / (ms_nd / 1e3) / 1e9, 1),
+                "decompress_frac_of_peak": round(nc_bytes / (ms_nd / 1e3) / 1e9 / peak, 3)},
+        "fp16_wrap": {"encode_GBps": round(w_bytes / (ms_we / 1e3) / 1e9, 1),
+                      "decode_GBps": round(w_bytes / (ms_wd / 1e3) / 1e9, 1),
+                      "encode_frac_of_peak": round(w_bytes / (ms_we / 1e3) / 1e9 / peak, 3),
+                      "decode_frac_of_peak": round(w_bytes / (ms_wd / 1e3) / 1e9 / peak, 3)},
         "int8_decode": {"GBps": round(q_bytes / (ms_q / 1e3) / 1e9, 1), "us": round(ms_q * 1e3, 1),
                         "batch": B, "context": T, "frac_of_peak": round(q_bytes / (ms_q / 1e3) / 1e9 / peak, 3)},
         "peak": peak, "peak_kind": peak_kind, "cpu_baseline": cpu}), flush=True)
@@ -614,7 +635,8 @@ def run_config4(args):
         return (base + np.take_along_axis(perms, r, axis=1)).astype(np.int32).ravel()
 
     t0 = time.perf_counter()
-    tier = Tier(FB, U, C, S, device=0)
+    tier = Tier(FB, U, C, S, device=0, load_ctas=int(os.environ.get("KVX_TIER_LOAD_CTAS", "0")),
+                store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")))
     alloc_s = time.perf_counter() - t0
     dev = tier.device_tensor()
     host = tier.host_array()

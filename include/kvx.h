@@ -152,6 +152,35 @@ KVX_API int kvx_decompress_int8(const int8_t *codes, const float *stats, void *d
                                 int32_t dst_dtype, size_t num_blocks, int32_t block_elems,
                                 void *stream);
 
+/* Per-block 4-bit quantisation.  Replaces KVCompressionEngine::compressToNF4
+ * (native-engine/cpp/KVCompressionEngine.cpp:124-163), which despite its
+ * name is uniform: min/max, scale=(max-min)/15 (0 -> 1), zeroPoint=min,
+ * q = clamp(round((x-min)/scale), 0, 15), two codes per byte with element
+ * 2k in the high nibble (a block of odd length leaves the last low nibble
+ * 0).  codes: num_blocks * ((block_elems + 1) / 2) bytes; stats as for int8.
+ * Bit-exact with the reference. */
+KVX_API int kvx_compress_nf4(const void *src, int32_t src_dtype, uint8_t *codes, float *stats,
+                             size_t num_blocks, int32_t block_elems, void *stream);
+
+/* Inverse.  Replaces KVCompressionEngine::decompressNF4
+ * (native-engine/cpp/KVCompressionEngine.cpp:165-180): zeroPoint + q*scale
+ * in fp32 (no FMA).  dst_dtype KVX_F32 (bit-exact) or KVX_F16. */
+KVX_API int kvx_decompress_nf4(const uint8_t *codes, const float *stats, void *dst,
+                               int32_t dst_dtype, size_t num_blocks, int32_t block_elems,
+                               void *stream);
+
+/* The compression engine's own fp32 -> fp16.  Replaces
+ * KVCompressionEngine::compressToFP16 (native-engine/cpp/KVCompressionEngine.cpp:36-61):
+ * Inf and NaN -> +-Inf, a zero exponent -> +-0, otherwise the exponent is
+ * rebiased modulo 32 (it wraps outside [2^-14, 2^16)) and the mantissa
+ * truncated.  Bit-exact, including the wrap. */
+KVX_API int kvx_fp16_wrap_encode(const float *src, uint16_t *dst, size_t n, void *stream);
+/* Inverse.  Replaces KVCompressionEngine::decompressFP16
+ * (native-engine/cpp/KVCompressionEngine.cpp:63-80): exponent rebiased
+ * modulo 256 with no special cases (+-0 decodes to +-2^-15, Inf to 65536).
+ * Bit-exact. */
+KVX_API int kvx_fp16_wrap_decode(const uint16_t *src, float *dst, size_t n, void *stream);
+
 /* Truncating fp32 -> fp16 of the disk tier.  Replaces float32_to_float16
  * (compression/kv_compress.cpp:6-25,48-53).  Bit-exact.  Any naturally
  * aligned arrays (4 elements per access when 16 / 8-byte aligned). */

@@ -58,7 +58,11 @@ typedef struct kvx_tier_config {
     int64_t capacity;    /* frames resident on the device at most (the policy's capacity) */
     int64_t spare;       /* extra device and host slots; must cover the misses of one step */
     int32_t device;      /* CUDA device ordinal, or -1 for a bookkeeping-only store */
-    int32_t copy_ctas;   /* CTAs per copy launch (0: 8, enough for the host link) */
+    int32_t load_ctas;   /* CTAs of a load launch (0: 16) */
+    int32_t store_ctas;  /* CTAs of a write-back launch (0: 4).  Loads are reads of
+                            host memory by the SMs and need more requests in
+                            flight than write-backs; 16 + 4 keeps both directions
+                            of the host link busy when they run together */
 } kvx_tier_config;
 
 typedef struct kvx_tier_stats {

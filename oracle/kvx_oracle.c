@@ -319,3 +319,98 @@ int kvo_prefetch_depth(const double *lat, size_t n, size_t cache_size,
     int depth = r < max_depth ? r : max_depth;
     return depth > 1 ? depth : 1;
 }
+
+/* ---- native-engine/cpp/KVCompressionEngine.cpp:124-163 (compressToNF4) --
+ * Uniform 4-bit asymmetric quantisation (15 steps between min and max),
+ * two codes per byte, element 2k in the high nibble, 2k+1 in the low one
+ * (0 when the count is odd). */
+void kvo_compress_nf4(const float *in, uint8_t *out, size_t count, float stats[4]) {
+    float mn = in[0], mx = in[0];
+    for (size_t i = 1; i < count; ++i) {
+        mn = (in[i] < mn) ? in[i] : mn;
+        mx = (mx < in[i]) ? in[i] : mx;
+    }
+    float scale = (mx - mn) / 15.0f;
+    if (scale == 0.0f) scale = 1.0f;
+    stats[0] = mn;
+    stats[1] = mx;
+    stats[2] = scale;
+    stats[3] = mn;
+    for (size_t i = 0; i < count; i += 2) {
+        int32_t q1 = cvt_trunc_i32(roundf((in[i] - mn) / scale));
+        q1 = q1 < 0 ? 0 : (q1 > 15 ? 15 : q1);
+        int32_t q2 = 0;
+        if (i + 1 < count) {
+            q2 = cvt_trunc_i32(roundf((in[i + 1] - mn) / scale));
+            q2 = q2 < 0 ? 0 : (q2 > 15 ? 15 : q2);
+        }
+        out[i / 2] = (uint8_t)((q1 << 4) | q2);
+    }
+}
+
+/* ---- native-engine/cpp/KVCompressionEngine.cpp:165-180 (decompressNF4) */
+void kvo_decompress_nf4(const uint8_t *in, float *out, size_t count, const float stats[4]) {
+    for (size_t i = 0; i < count; i += 2) {
+        uint8_t packed = in[i / 2];
+        out[i] = stats[3] + (float)((packed >> 4) & 0xF) * stats[2];
+        if (i + 1 < count) out[i + 1] = stats[3] + (float)(packed & 0xF) * stats[2];
+    }
+}
+
+void kvo_compress_nf4_blocks_f16(const uint16_t *in, uint8_t *codes, float *stats,
+                                 size_t num_blocks, size_t block_elems) {
+    float *tmp = (float *)malloc(block_elems * sizeof(float));
+    const size_t cb = (block_elems + 1) / 2;
+    for (size_t b = 0; b < num_blocks; ++b) {
+        const uint16_t *src = in + b * block_elems;
+        for (size_t i = 0; i < block_elems; ++i) tmp[i] = kvo_f16_to_f32(src[i]);
+        kvo_compress_nf4(tmp, codes + b * cb, block_elems, stats + 4 * b);
+    }
+    free(tmp);
+}
+
+void kvo_compress_nf4_blocks_f32(const float *in, uint8_t *codes, float *stats,
+                                 size_t num_blocks, size_t block_elems) {
+    const size_t cb = (block_elems + 1) / 2;
+    for (size_t b = 0; b < num_blocks; ++b)
+        kvo_compress_nf4(in + b * block_elems, codes + b * cb, block_elems, stats + 4 * b);
+}
+
+void kvo_decompress_nf4_blocks(const uint8_t *codes, const float *stats, float *out,
+                               size_t num_blocks, size_t block_elems) {
+    const size_t cb = (block_elems + 1) / 2;
+    for (size_t b = 0; b < num_blocks; ++b)
+        kvo_decompress_nf4(codes + b * cb, out + b * block_elems, block_elems, stats + 4 * b);
+}
+
+/* ---- native-engine/cpp/KVCompressionEngine.cpp:36-61 (compressToFP16) --
+ * Not IEEE rounding: Inf and NaN become +-Inf, a zero exponent (zero or
+ * denormal) becomes +-0, and otherwise the exponent is rebiased modulo 32
+ * (it wraps for |x| >= 2^16 or < 2^-14) and the mantissa truncated. */
+uint16_t kvo_fp16_wrap_encode(float f) {
+    uint32_t bits;
+    memcpy(&bits, &f, sizeof bits);
+    uint32_t sign = (bits >> 31) & 1u, exponent = (bits >> 23) & 0xFFu, mantissa = bits & 0x7FFFFFu;
+    if (exponent == 0xFFu) return (uint16_t)((sign << 15) | 0x7C00u);
+    if (exponent == 0u) return (uint16_t)(sign << 15);
+    uint32_t e16 = (uint32_t)((int32_t)exponent - 127 + 15) & 0x1Fu;
+    return (uint16_t)((sign << 15) | (e16 << 10) | ((mantissa >> 13) & 0x3FFu));
+}
+
+/* ---- native-engine/cpp/KVCompressionEngine.cpp:63-80 (decompressFP16) -
+ * The exponent is rebiased modulo 256 with no special cases: a zero
+ * exponent decodes to +-2^-15 x (1 + m), exponent 31 to 2^16 x (1 + m). */
+float kvo_fp16_wrap_decode(uint16_t h) {
+    uint32_t sign = ((uint32_t)h >> 15) & 1u, e = ((uint32_t)h >> 10) & 0x1Fu, m = (uint32_t)h & 0x3FFu;
+    uint32_t bits = (sign << 31) | (((e + 127u - 15u) & 0xFFu) << 23) | (m << 13);
+    float f;
+    memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
+void kvo_fp16_wrap_encode_n(const float *in, uint16_t *out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = kvo_fp16_wrap_encode(in[i]);
+}
+void kvo_fp16_wrap_decode_n(const uint16_t *in, float *out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = kvo_fp16_wrap_decode(in[i]);
+}

@@ -49,6 +49,24 @@ void kvo_compress_int8_blocks_f32(const float *in, int8_t *codes, float *stats,
 void kvo_decompress_int8_blocks(const int8_t *codes, const float *stats, float *out,
                                 size_t num_blocks, size_t block_elems);
 
+/* native-engine/cpp/KVCompressionEngine.cpp:124-180: uniform 4-bit codes,
+ * two per byte (high nibble first); blocks of block_elems take
+ * (block_elems + 1) / 2 code bytes each. */
+void kvo_compress_nf4(const float *in, uint8_t *out, size_t count, float stats[4]);
+void kvo_decompress_nf4(const uint8_t *in, float *out, size_t count, const float stats[4]);
+void kvo_compress_nf4_blocks_f16(const uint16_t *in, uint8_t *codes, float *stats,
+                                 size_t num_blocks, size_t block_elems);
+void kvo_compress_nf4_blocks_f32(const float *in, uint8_t *codes, float *stats,
+                                 size_t num_blocks, size_t block_elems);
+void kvo_decompress_nf4_blocks(const uint8_t *codes, const float *stats, float *out,
+                               size_t num_blocks, size_t block_elems);
+/* native-engine/cpp/KVCompressionEngine.cpp:36-80: the engine's own fp16
+ * conversion (exponent rebiased with wrap-around, mantissa truncated). */
+uint16_t kvo_fp16_wrap_encode(float f);
+float kvo_fp16_wrap_decode(uint16_t h);
+void kvo_fp16_wrap_encode_n(const float *in, uint16_t *out, size_t n);
+void kvo_fp16_wrap_decode_n(const uint16_t *in, float *out, size_t n);
+
 /* IEEE fp16 <-> fp32 (round to nearest even), used to share input bits. */
 float kvo_f16_to_f32(uint16_t h);
 uint16_t kvo_f32_to_f16_rn(float f);

@@ -66,6 +66,13 @@ class Oracle:
         L.kvo_compress_int8_blocks_f16.argtypes = [_u16p, _i8p, _f32p, _sz, _sz]
         L.kvo_compress_int8_blocks_f32.argtypes = [_f32p, _i8p, _f32p, _sz, _sz]
         L.kvo_decompress_int8_blocks.argtypes = [_i8p, _f32p, _f32p, _sz, _sz]
+        L.kvo_compress_nf4.argtypes = [_f32p, _u8p, _sz, _f32p]
+        L.kvo_decompress_nf4.argtypes = [_u8p, _f32p, _sz, _f32p]
+        L.kvo_compress_nf4_blocks_f16.argtypes = [_u16p, _u8p, _f32p, _sz, _sz]
+        L.kvo_compress_nf4_blocks_f32.argtypes = [_f32p, _u8p, _f32p, _sz, _sz]
+        L.kvo_decompress_nf4_blocks.argtypes = [_u8p, _f32p, _f32p, _sz, _sz]
+        L.kvo_fp16_wrap_encode_n.argtypes = [_f32p, _u16p, _sz]
+        L.kvo_fp16_wrap_decode_n.argtypes = [_u16p, _f32p, _sz]
         L.kvo_append.argtypes = [C.c_void_p, _sz, C.c_int, C.c_int, C.c_int, C.c_int,
                                  _i32p, C.c_int, _i32p, C.c_int, C.c_void_p, C.c_void_p]
         L.kvo_append.restype = C.c_int
@@ -128,6 +135,49 @@ class Oracle:
         out = np.empty(codes.size, np.float32)
         self.L.kvo_decompress_int8_blocks(codes, _c(stats, np.float32).ravel(), out, nb,
                                           block_elems)
+        return out
+
+    # KVCompressionEngine NF4 (uniform 4-bit) and FP16 (exponent-wrap)
+    def compress_nf4(self, x):
+        x = _c(x, np.float32).ravel()
+        codes = np.empty((x.size + 1) // 2, np.uint8)
+        stats = np.empty(4, np.float32)
+        self.L.kvo_compress_nf4(x, codes, x.size, stats)
+        return codes, stats
+
+    def decompress_nf4(self, codes, stats, count):
+        out = np.empty(count, np.float32)
+        self.L.kvo_decompress_nf4(_c(codes, np.uint8).ravel(), out, count, _c(stats, np.float32))
+        return out
+
+    def compress_nf4_blocks(self, data, block_elems):
+        flat = np.ascontiguousarray(data).ravel()
+        nb = flat.size // block_elems
+        codes = np.empty(nb * ((block_elems + 1) // 2), np.uint8)
+        stats = np.empty(nb * 4, np.float32)
+        if flat.dtype == np.float16:
+            self.L.kvo_compress_nf4_blocks_f16(flat.view(np.uint16), codes, stats, nb, block_elems)
+        else:
+            self.L.kvo_compress_nf4_blocks_f32(_c(flat, np.float32), codes, stats, nb, block_elems)
+        return codes, stats.reshape(nb, 4)
+
+    def decompress_nf4_blocks(self, codes, stats, block_elems):
+        st = _c(stats, np.float32).ravel()
+        nb = st.size // 4
+        out = np.empty(nb * block_elems, np.float32)
+        self.L.kvo_decompress_nf4_blocks(_c(codes, np.uint8).ravel(), st, out, nb, block_elems)
+        return out
+
+    def fp16_wrap_encode(self, x):
+        x = _c(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint16)
+        self.L.kvo_fp16_wrap_encode_n(x, out, x.size)
+        return out
+
+    def fp16_wrap_decode(self, h):
+        h = _c(h, np.uint16).ravel()
+        out = np.empty(h.size, np.float32)
+        self.L.kvo_fp16_wrap_decode_n(h, out, h.size)
         return out
 
     def append(self, pool, block_table, positions, new_k, new_v, page_tokens):
@@ -200,6 +250,10 @@ class Reference:
         L.kvref_f16_to_f32.argtypes = [_u16p, _f32p, _sz]
         L.kvref_compress_int8.argtypes = [_f32p, _i8p, _sz, _f32p]
         L.kvref_decompress_int8.argtypes = [_i8p, _f32p, _sz, _f32p]
+        L.kvref_compress_nf4.argtypes = [_f32p, _u8p, _sz, _f32p]
+        L.kvref_decompress_nf4.argtypes = [_u8p, _f32p, _sz, _f32p]
+        L.kvref_fp16_wrap_encode.argtypes = [_f32p, _u16p, _sz]
+        L.kvref_fp16_wrap_decode.argtypes = [_u16p, _f32p, _sz]
         L.kvref_attention.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _f32p]
         L.kvref_attention.restype = C.c_int
         L.kvref_softmax.argtypes = [_f32p, _sz, _sz, _f32p]
@@ -249,6 +303,30 @@ class Reference:
         codes = _c(codes, np.int8).ravel()
         out = np.empty(codes.size, np.float32)
         self.L.kvref_decompress_int8(codes, out, codes.size, _c(stats, np.float32))
+        return out
+
+    def compress_nf4(self, x):
+        x = _c(x, np.float32).ravel()
+        codes = np.empty((x.size + 1) // 2, np.uint8)
+        stats = np.empty(4, np.float32)
+        self.L.kvref_compress_nf4(x, codes, x.size, stats)
+        return codes, stats
+
+    def decompress_nf4(self, codes, stats, count):
+        out = np.empty(count, np.float32)
+        self.L.kvref_decompress_nf4(_c(codes, np.uint8).ravel(), out, count, _c(stats, np.float32))
+        return out
+
+    def fp16_wrap_encode(self, x):
+        x = _c(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint16)
+        self.L.kvref_fp16_wrap_encode(x, out, x.size)
+        return out
+
+    def fp16_wrap_decode(self, h):
+        h = _c(h, np.uint16).ravel()
+        out = np.empty(h.size, np.float32)
+        self.L.kvref_fp16_wrap_decode(h, out, h.size)
         return out
 
     def attention(self, q, k, v):

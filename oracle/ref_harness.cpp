@@ -69,6 +69,53 @@ void kvref_decompress_int8(const int8_t *in, float *out, size_t count, const flo
     eng->decompress(in, out, count, st);
 }
 
+// native-engine/cpp/KVCompressionEngine.cpp:124-163 via compress() with NF4
+void kvref_compress_nf4(const float *in, uint8_t *out, size_t count, float *stats) {
+    static thread_local KVCompressionEngine *eng = nullptr;
+    if (!eng) {
+        eng = new KVCompressionEngine();
+        eng->setCompressionType(CompressionType::NF4);
+    }
+    QuantizationStats st{};
+    eng->compress(in, out, count, st);
+    stats[0] = st.minVal;
+    stats[1] = st.maxVal;
+    stats[2] = st.scale;
+    stats[3] = st.zeroPoint;
+}
+
+// native-engine/cpp/KVCompressionEngine.cpp:165-180 via decompress() with NF4
+void kvref_decompress_nf4(const uint8_t *in, float *out, size_t count, const float *stats) {
+    static thread_local KVCompressionEngine *eng = nullptr;
+    if (!eng) eng = new KVCompressionEngine();
+    QuantizationStats st{};
+    st.minVal = stats[0];
+    st.maxVal = stats[1];
+    st.scale = stats[2];
+    st.zeroPoint = stats[3];
+    st.type = CompressionType::NF4;
+    eng->decompress(in, out, count, st);
+}
+
+// native-engine/cpp/KVCompressionEngine.cpp:36-80 via compress()/decompress() with FP16
+void kvref_fp16_wrap_encode(const float *in, uint16_t *out, size_t count) {
+    static thread_local KVCompressionEngine *eng = nullptr;
+    if (!eng) {
+        eng = new KVCompressionEngine();
+        eng->setCompressionType(CompressionType::FP16);
+    }
+    QuantizationStats st{};
+    eng->compress(in, out, count, st);
+}
+
+void kvref_fp16_wrap_decode(const uint16_t *in, float *out, size_t count) {
+    static thread_local KVCompressionEngine *eng = nullptr;
+    if (!eng) eng = new KVCompressionEngine();
+    QuantizationStats st{};
+    st.type = CompressionType::FP16;
+    eng->decompress(in, out, count, st);
+}
+
 // runtime/tensor_ops.cpp:179-219
 int kvref_attention(const float *Q, const float *K, const float *V, size_t seq, size_t dim,
                     float *out) {

@@ -103,6 +103,70 @@ def gen_int8(R: Reference):
                         f16_blocks=f16.view(np.uint16))
 
 
+def codec_cases(seed0):
+    """Edge-case blocks shared by the block codecs: sizes 1..2048 (odd ones
+    too), outliers, constants, signed zeros, NaN first / inside, huge,
+    denormal, Inf, and fp16 page blocks as the engine stores them."""
+    cases = []
+    for n in (1, 2, 3, 17, 2048):
+        base = kvgen.normal(seed0 + n, (n,))
+        cases.append(("normal", base))
+        out = base.copy()
+        out[kvgen.uniform(seed0 + 100 + n, n) < 0.01] *= np.float32(20.0)
+        cases.append(("outliers", out))
+        cases.append(("constant", np.full(n, 3.0, np.float32)))
+        z = np.abs(base)
+        z[n // 2] = 0.0
+        z[0] = -0.0
+        cases.append(("signed_zero_min", z))
+    for name, fill in (("nan_first", 0), ("nan_mid", 7)):
+        v = kvgen.normal(seed0 + 300 + fill, (65,))
+        v[fill] = np.nan
+        cases.append((name, v))
+    cases.append(("huge", kvgen.normal(seed0 + 302, (64,)) * np.float32(1e30)))
+    cases.append(("denormal", kvgen.normal(seed0 + 303, (64,)) * np.float32(1e-42)))
+    inf = kvgen.normal(seed0 + 304, (64,))
+    inf[3] = np.inf
+    cases.append(("inf", inf))
+    ties = ((np.arange(2048) % 16) + 0.5) / 15.0 * 7.0  # quotients on k + 1/2
+    ties[0], ties[1] = 0.0, 7.0
+    cases.append(("half_ties", ties.astype(np.float32)))
+    f16 = (kvgen.normal(seed0 + 305, (8, 2048)) *
+           np.where(kvgen.uniform(seed0 + 306, 8 * 2048).reshape(8, 2048) < 0.01, 20.0, 1.0)
+           ).astype(np.float16)
+    for b in range(8):
+        cases.append(("f16_page_block", f16[b].astype(np.float32)))
+    return cases, f16
+
+
+def gen_nf4(R: Reference):
+    """KVCompressionEngine NF4 (native-engine/cpp/KVCompressionEngine.cpp:124-180)."""
+    cases, f16 = codec_cases(700)
+    data, codes, stats, dec, lens, names = [], [], [], [], [], []
+    for name, v in cases:
+        c, st = R.compress_nf4(v)
+        data.append(v)
+        codes.append(c)
+        stats.append(st)
+        dec.append(R.decompress_nf4(c, st, v.size))
+        lens.append(v.size)
+        names.append(name)
+    np.savez_compressed(os.path.join(HERE, "nf4.npz"), data=np.concatenate(data),
+                        codes=np.concatenate(codes), stats=np.stack(stats), dec=np.concatenate(dec),
+                        lens=np.array(lens), names=np.array(names), f16_blocks=f16.view(np.uint16))
+
+
+def gen_fp16_wrap(R: Reference):
+    """KVCompressionEngine FP16 (native-engine/cpp/KVCompressionEngine.cpp:36-80):
+    every half decoded, special and random floats encoded."""
+    h = np.arange(65536, dtype=np.uint16)
+    rnd = kvgen.randint(900, 20000, 0, 2 ** 32 - 1).astype(np.uint32).view(np.float32)
+    x = np.concatenate([special_floats(), kvgen.normal(901, (4096,)) * np.float32(1e3),
+                        np.ldexp(np.float32(1.5), np.arange(-40, 40)).astype(np.float32), rnd])
+    np.savez_compressed(os.path.join(HERE, "fp16_wrap.npz"), x=x, enc=R.fp16_wrap_encode(x),
+                        dec_bits=R.fp16_wrap_decode(h).view(np.uint32))
+
+
 def gen_attention(R: Reference):
     # cpu_ops_test (tests/cpu_ops_test.cpp:35-47) identity case + seeded rows
     out = {}
@@ -259,14 +323,11 @@ def main():
     if not build_reference():
         raise SystemExit("reference checkout not found")
     R = Reference()
-    gen_kv_compress(R)
-    gen_int8(R)
-    gen_attention(R)
-    gen_paged(R)
-    gen_int8_decode(R)
-    gen_lru(R)
-    gen_depth(R)
-    gen_disk(R)
+    gens = {"kv_compress": gen_kv_compress, "int8": gen_int8, "attention": gen_attention,
+            "paged": gen_paged, "int8_decode": gen_int8_decode, "lru": gen_lru, "depth": gen_depth,
+            "disk": gen_disk, "nf4": gen_nf4, "fp16_wrap": gen_fp16_wrap}
+    for name in (sys.argv[1:] or gens):  # e.g. `make_golden.py nf4 fp16_wrap` for one fixture
+        gens[name](R)
     print("golden fixtures written to", HERE)
 
 

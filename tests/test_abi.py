@@ -12,11 +12,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_symbols():
     names = set()
-    for h in ("kvx.h", "adaptive_engine.h"):
-        path = os.path.join(ROOT, "include", h)
-        if not os.path.exists(path):
+    inc = os.path.join(ROOT, "include")
+    for h in sorted(os.listdir(inc)):
+        if not h.endswith(".h"):
             continue
-        text = open(path).read()
+        text = open(os.path.join(inc, h)).read()
         for m in re.finditer(r"(?:KVX_API|ADAPTIVE_ENGINE_EXPORT)\s+[\w\s\*]+?\b(\w+)\s*\(", text):
             names.add(m.group(1))
     return sorted(names)
@@ -27,7 +27,8 @@ def test_header_declares_entry_points():
     for n in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init",
               "kvx_compress_int8", "kvx_decompress_int8",
               "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
-              "kvx_migrate_frames", "kvx_decode_workspace_bytes"):
+              "kvx_migrate_frames", "kvx_decode_workspace_bytes", "kvx_tier_create", "kvx_tier_step",
+              "kvx_tier_wait_resident", "kvx_tier_mark_read", "kvx_tier_sync", "adaptive_engine_get_api"):
         assert n in names
 
 

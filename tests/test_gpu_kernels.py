@@ -322,6 +322,73 @@ def test_compress_int8_half_ties_bitexact(kvx, oracle, np_dtype):
     assert np.array_equal(dec16.view(np.uint16), want.view(np.uint16))
 
 
+def test_nf4_golden_cases(kvx):
+    """KVCompressionEngine NF4 (native-engine/cpp/KVCompressionEngine.cpp:124-180) on the
+    reference's own outputs: edge blocks of 1..2048 elements (odd ones too)."""
+    g = golden("nf4.npz")
+    off = coff = 0
+    for i, n in enumerate(g["lens"]):
+        n = int(n)
+        cb = (n + 1) // 2
+        codes, stats = kvx.compress_nf4(dev(g["data"][off:off + n]), block_elems=n)
+        torch.cuda.synchronize()
+        assert np.array_equal(codes.cpu().numpy(), g["codes"][coff:coff + cb]), g["names"][i]
+        assert np.array_equal(stats.cpu().numpy().view(np.uint32).ravel(), g["stats"][i].view(np.uint32)), g["names"][i]
+        dec = kvx.decompress_nf4(codes, stats, block_elems=n).cpu().numpy()
+        assert np.array_equal(dec.view(np.uint32), g["dec"][off:off + n].view(np.uint32)), g["names"][i]
+        off += n
+        coff += cb
+
+
+@pytest.mark.parametrize("np_dtype", [np.float16, np.float32])
+def test_nf4_pages_bitexact(kvx, oracle, np_dtype):
+    nb = 3000
+    data = kvgen.normal(61, (nb, 2048))
+    data[kvgen.uniform(62, data.size).reshape(data.shape) < 0.01] *= 20
+    data[5, :] = 0.0
+    data[6, ::2] = -0.0
+    data[7, :] = 1.5
+    ties = ((np.arange(2048) % 16) + 0.5) / 15.0 * 3.0  # quotients on k + 1/2
+    ties[0], ties[1] = 0.0, 3.0
+    data[8] = ties
+    data[9] = np.nextafter(ties.astype(np_dtype), np_dtype(np.inf)).astype(np.float64)
+    data[10, 100] = np.nan
+    data = data.astype(np_dtype)
+    codes, stats = kvx.compress_nf4(dev(data))
+    rc, rs = oracle.compress_nf4_blocks(data, 2048)
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    dec = kvx.decompress_nf4(codes, stats).cpu().numpy()
+    want = oracle.decompress_nf4_blocks(rc, rs, 2048)
+    assert np.array_equal(dec.view(np.uint32), want.view(np.uint32))
+    dec16 = kvx.decompress_nf4(codes, stats, dtype=torch.float16).cpu().numpy()
+    assert np.array_equal(dec16.view(np.uint16), want.astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("block_elems", [17, 2047, 4096])
+def test_nf4_other_block_sizes(kvx, oracle, block_elems):
+    data = (kvgen.normal(63, (40, block_elems)) * 3).astype(np.float32)
+    codes, stats = kvx.compress_nf4(dev(data), block_elems=block_elems)
+    rc, rs = oracle.compress_nf4_blocks(data, block_elems)
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    assert np.array_equal(stats.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    dec = kvx.decompress_nf4(codes, stats, block_elems=block_elems).cpu().numpy()
+    assert np.array_equal(dec.view(np.uint32), oracle.decompress_nf4_blocks(rc, rs, block_elems).view(np.uint32))
+
+
+def test_fp16_wrap_codec_bitexact(kvx):
+    """KVCompressionEngine FP16 (native-engine/cpp/KVCompressionEngine.cpp:36-80), the
+    exponent-wrapping conversion, on the reference's own outputs."""
+    g = golden("fp16_wrap.npz")
+    enc = kvx.fp16_wrap_encode(dev(g["x"])).cpu().numpy().view(np.uint16)
+    assert np.array_equal(enc, g["enc"])
+    h = torch.arange(65536, dtype=torch.int32).to(torch.int16).cuda()
+    dec = kvx.fp16_wrap_decode(h).cpu().numpy()
+    assert np.array_equal(dec.view(np.uint32), g["dec_bits"])
+    odd = kvx.fp16_wrap_encode(dev(g["x"])[1:]).cpu().numpy().view(np.uint16)  # unaligned: scalar path
+    assert np.array_equal(odd, g["enc"][1:])
+
+
 def test_compress_roundtrip_error_bound(kvx):
     """Property at scale: |x - dequant(quant(x))| <= scale/2 (+1 ulp) per block."""
     nb = 65536  # 128 Mi elements = 256 MiB fp16, larger than L2

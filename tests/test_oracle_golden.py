@@ -63,6 +63,38 @@ def test_int8_f16_page_blocks(oracle):
     assert np.array_equal(stats.view(np.uint32), g["stats"][first:first + 8].view(np.uint32))
 
 
+def test_nf4_codes_stats_exact(oracle):
+    """KVCompressionEngine NF4 (native-engine/cpp/KVCompressionEngine.cpp:124-180)."""
+    g = golden("nf4.npz")
+    off = coff = 0
+    for i, n in enumerate(g["lens"]):
+        data = g["data"][off:off + n]
+        cb = (n + 1) // 2
+        codes, stats = oracle.compress_nf4(data)
+        assert np.array_equal(codes, g["codes"][coff:coff + cb]), g["names"][i]
+        assert np.array_equal(stats.view(np.uint32), g["stats"][i].view(np.uint32)), g["names"][i]
+        dec = oracle.decompress_nf4(codes, stats, n)
+        assert np.array_equal(dec.view(np.uint32), g["dec"][off:off + n].view(np.uint32)), g["names"][i]
+        off += n
+        coff += cb
+    blocks = g["f16_blocks"].view(np.float16)
+    codes, stats = oracle.compress_nf4_blocks(blocks, 2048)
+    first = list(g["names"]).index("f16_page_block")
+    start = int(np.sum((g["lens"][:first] + 1) // 2))
+    assert np.array_equal(codes, g["codes"][start:start + codes.size])
+    assert np.array_equal(stats.view(np.uint32), g["stats"][first:first + 8].view(np.uint32))
+
+
+def test_fp16_wrap_exact(oracle):
+    """KVCompressionEngine FP16 (native-engine/cpp/KVCompressionEngine.cpp:36-80): the
+    exponent-wrapping conversion, not IEEE; every half decoded."""
+    g = golden("fp16_wrap.npz")
+    assert np.array_equal(oracle.fp16_wrap_encode(g["x"]), g["enc"])
+    dec = oracle.fp16_wrap_decode(np.arange(65536, dtype=np.uint16))
+    assert np.array_equal(dec.view(np.uint32), g["dec_bits"])
+    assert dec[0] == np.float32(2.0 ** -15) and dec[0x7C00] == np.float32(65536.0)  # the quirks kept
+
+
 def test_attention_rows(oracle):
     g = golden("attention.npz")
     for i, T in enumerate((1, 2, 3, 16, 33, 257)):
