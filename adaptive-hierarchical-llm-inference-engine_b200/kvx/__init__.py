@@ -79,10 +79,12 @@ lib.kvx_f32_to_f16_trunc.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_f16_trunc_to_f32.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_lru_select.argtypes = [_vp, _sz, _vp, _vp]
 lib.kvx_migrate_frames.argtypes = [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _sz, _i32, _i32, _vp, _vp]
+lib.kvx_evict_select.argtypes = [_i32, _vp, _sz, _f32, _vp, _vp, _vp]
+lib.kvx_evict_select_composite.argtypes = [_vp, _vp, _i32, _vp, _sz, _f32, _vp, _vp, _vp]
 for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
             "kvx_compress_nf4", "kvx_decompress_nf4", "kvx_fp16_wrap_encode", "kvx_fp16_wrap_decode",
             "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
-            "kvx_migrate_frames"):
+            "kvx_migrate_frames", "kvx_evict_select", "kvx_evict_select_composite"):
     getattr(lib, _fn).restype = C.c_int
 
 
@@ -284,3 +286,29 @@ def migrate_frames(dev_base, dev_capacity, host_base, host_capacity, dev_frames,
                                 _ptr(dev_frames), _ptr(host_frames), dev_frames.numel(),
                                 frame_bytes, direction, ctas, _ptr(error_flag), _stream(stream))
     _check("kvx_migrate_frames", rc)
+
+
+EVICT_LRU, EVICT_TOKEN_WEIGHTED, EVICT_ATTENTION_BASED, EVICT_PREDICTIVE = 0, 1, 2, 3
+
+
+def evict_select(policy, pages, decay=0.95, predicted=None, out=None, stream=None):
+    """AdvancedEvictionPolicy selectPageToEvict on the device.  pages: CUDA
+    uint8 tensor holding n EvictionMetrics records of 48 bytes."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=pages.device)
+    _check("kvx_evict_select", lib.kvx_evict_select(policy, _ptr(pages), pages.numel() // 48, decay,
+                                                    _ptr(predicted), _ptr(out), _stream(stream)))
+    return out
+
+
+def evict_select_composite(policies, weights, pages, decay=0.95, predicted=None, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=pages.device)
+    pol = (C.c_int32 * len(policies))(*policies)
+    w = (C.c_float * len(weights))(*[float(x) for x in weights])
+    _check("kvx_evict_select_composite",
+           lib.kvx_evict_select_composite(pol, w, len(policies), _ptr(pages), pages.numel() // 48, decay,
+                                          _ptr(predicted), _ptr(out), _stream(stream)))
+    return out

@@ -211,6 +211,49 @@ KVX_API int kvx_attention_dense(const float *Q, const float *K, const float *V, 
  * Writes the index to *victim (device int32).  No workspace. */
 KVX_API int kvx_lru_select(const uint64_t *stamps, size_t n, int32_t *victim, void *stream);
 
+/* The reference's EvictionMetrics (native-engine/include/AdvancedEvictionPolicy.h:19-27),
+ * same layout (48 bytes on LP64), so a std::vector<EvictionMetrics> can be
+ * copied to the device as is. */
+typedef struct kvx_evict_metrics {
+    uint64_t last_access_token;
+    float total_attention;
+    float average_attention;
+    float access_frequency;
+    uint64_t creation_time;
+    size_t page_size;
+    int32_t page_id;
+} kvx_evict_metrics;
+
+enum kvx_evict_policy {  /* EvictionStrategy (AdvancedEvictionPolicy.h:29-34) */
+    KVX_EVICT_LRU = 0,
+    KVX_EVICT_TOKEN_WEIGHTED = 1,
+    KVX_EVICT_ATTENTION_BASED = 2,
+    KVX_EVICT_PREDICTIVE = 3
+};
+
+/* selectPageToEvict of one policy over n pages (device array), as the
+ * reference evaluates it (native-engine/cpp/AdvancedEvictionPolicy.cpp:9-152):
+ * scores use currentToken = 0, so token ages wrap modulo 2^64 (kept, not
+ * fixed); LRU takes the smallest lastAccessToken below UINT64_MAX, the
+ * others the highest score strictly above -1; lowest index on ties.
+ * TokenWeighted: 1 - decay^age (reference default decay 0.95).
+ * AttentionBased: (1 - averageAttention) * log(age + 1).
+ * Predictive: 1000 when predicted[i] < 0 (or predicted == NULL), else
+ * 0 - predicted[i]; predicted[i] is PredictiveEvictionPolicy::predictNextAccess
+ * of page i (device float array).  Writes the chosen pageId, or -1, to
+ * *page_id (device int32). */
+KVX_API int kvx_evict_select(int32_t policy, const kvx_evict_metrics *pages, size_t n, float decay,
+                             const float *predicted, int32_t *page_id, void *stream);
+/* CompositeEvictionManager::selectPageToEvict (:238-263): with one policy
+ * that policy's rule, else score = sum over policies (in order) of
+ * weights[p] * score_p, highest above -1 wins.  policies / weights: host
+ * arrays of num_policies <= 8, weights already normalised as the manager
+ * keeps them. */
+KVX_API int kvx_evict_select_composite(const int32_t *policies, const float *weights,
+                                       int32_t num_policies, const kvx_evict_metrics *pages,
+                                       size_t n, float decay, const float *predicted,
+                                       int32_t *page_id, void *stream);
+
 /* Page-frame migration between the device pool and a host frame arena
  * (pinned, mapped with cudaHostAlloc(..., cudaHostAllocMapped) or registered).
  * Replaces KVCacheGPU::transferToHost / transferToGPU

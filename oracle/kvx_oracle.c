@@ -414,3 +414,81 @@ void kvo_fp16_wrap_encode_n(const float *in, uint16_t *out, size_t n) {
 void kvo_fp16_wrap_decode_n(const uint16_t *in, float *out, size_t n) {
     for (size_t i = 0; i < n; ++i) out[i] = kvo_fp16_wrap_decode(in[i]);
 }
+
+/* ---- native-engine/cpp/AdvancedEvictionPolicy.cpp: the policies' scores as
+ * selectPageToEvict evaluates them, i.e. with currentToken = 0, so every
+ * token age is 0 - lastAccessToken modulo 2^64. */
+float kvo_evict_score(int policy, const kvo_evict_metrics *m, float decay, float predicted) {
+    const uint64_t age = (uint64_t)0 - m->last_access_token;
+    switch (policy) {
+    case 0: /* LRU :29-31 */
+        return (float)age;
+    case 1: /* TokenWeighted :60-64 */
+        return 1.0f - powf(decay, (float)age);
+    case 2: { /* AttentionBased :95-105 */
+        const float recency = logf((float)age + 1.0f);
+        return (1.0f - m->average_attention) * recency;
+    }
+    default: /* Predictive :142-152 */
+        if (predicted < 0) return 1000.0f;
+        return (float)(uint64_t)0 - predicted;
+    }
+}
+
+/* selectPageToEvict (:9-23 LRU; :35-50, :69-84, :119-135 the others). */
+int kvo_evict_select(int policy, const kvo_evict_metrics *pages, size_t n, float decay,
+                     const float *predicted) {
+    if (n == 0) return -1;
+    int sel = -1;
+    if (policy == 0) {
+        uint64_t mn = UINT64_MAX;
+        for (size_t i = 0; i < n; ++i)
+            if (pages[i].last_access_token < mn) {
+                mn = pages[i].last_access_token;
+                sel = pages[i].page_id;
+            }
+        return sel;
+    }
+    float best = -1.0f;
+    for (size_t i = 0; i < n; ++i) {
+        const float s = kvo_evict_score(policy, &pages[i], decay, predicted ? predicted[i] : -1.0f);
+        if (s > best) {
+            best = s;
+            sel = pages[i].page_id;
+        }
+    }
+    return sel;
+}
+
+/* CompositeEvictionManager::selectPageToEvict with several policies
+ * (:238-263): scores[i] += weights[p] * calculateScore_p(m, 0), policy
+ * order, then the highest score > -1 (first wins).  One policy: that
+ * policy's selectPageToEvict. */
+int kvo_evict_select_composite(const int *policies, const float *weights, int np,
+                               const kvo_evict_metrics *pages, size_t n, float decay,
+                               const float *predicted) {
+    if (n == 0) return -1;
+    if (np == 1) return kvo_evict_select(policies[0], pages, n, decay, predicted);
+    int sel = -1;
+    float best = -1.0f;
+    for (size_t i = 0; i < n; ++i) {
+        float s = 0.0f;
+        for (int p = 0; p < np; ++p)
+            s += weights[p] * kvo_evict_score(policies[p], &pages[i], decay, predicted ? predicted[i] : -1.0f);
+        if (s > best) {
+            best = s;
+            sel = pages[i].page_id;
+        }
+    }
+    return sel;
+}
+
+/* PredictiveEvictionPolicy::predictNextAccess (:154-172): the last access
+ * plus the mean interval (integer division), as float; -1 with fewer than
+ * two accesses. */
+float kvo_predict_next_access(const uint64_t *times, size_t count) {
+    if (count < 2) return -1.0f;
+    uint64_t total = 0;
+    for (size_t i = 1; i < count; ++i) total += times[i] - times[i - 1];
+    return (float)(times[count - 1] + total / (count - 1));
+}

@@ -107,6 +107,24 @@ int kvo_lru_select(const uint64_t *stamps, size_t n);
  * accesses (ops[i]==0 load_page, 1 save_page) of ids with a capacity; for
  * every access write the id evicted by it (or -1) to evicted[i] and whether
  * it was a hit to hit[i].  Returns 0. */
+/* native-engine/include/AdvancedEvictionPolicy.h:19-27 (same layout). */
+typedef struct kvo_evict_metrics {
+    uint64_t last_access_token;
+    float total_attention;
+    float average_attention;
+    float access_frequency;
+    uint64_t creation_time;
+    size_t page_size;
+    int page_id;
+} kvo_evict_metrics;
+/* policy: 0 LRU, 1 TokenWeighted, 2 AttentionBased, 3 Predictive. */
+float kvo_evict_score(int policy, const kvo_evict_metrics *m, float decay, float predicted);
+int kvo_evict_select(int policy, const kvo_evict_metrics *pages, size_t n, float decay,
+                     const float *predicted);
+int kvo_evict_select_composite(const int *policies, const float *weights, int np,
+                               const kvo_evict_metrics *pages, size_t n, float decay,
+                               const float *predicted);
+float kvo_predict_next_access(const uint64_t *times, size_t count);
 int kvo_lru_replay(const int32_t *ids, const uint8_t *ops, size_t n, size_t capacity,
                    int32_t *evicted, uint8_t *hit);
 

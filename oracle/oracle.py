@@ -51,6 +51,13 @@ def _c(a, dtype):
     return np.ascontiguousarray(a, dtype=dtype)
 
 
+EVICT_METRICS = np.dtype([("last_access_token", "<u8"), ("total_attention", "<f4"),
+                          ("average_attention", "<f4"), ("access_frequency", "<f4"), ("_pad0", "<u4"),
+                          ("creation_time", "<u8"), ("page_size", "<u8"), ("page_id", "<i4"),
+                          ("_pad1", "<u4")])
+assert EVICT_METRICS.itemsize == 48
+
+
 class Oracle:
     """The C restatement (oracle/kvx_oracle.c)."""
 
@@ -71,6 +78,15 @@ class Oracle:
         L.kvo_compress_nf4_blocks_f16.argtypes = [_u16p, _u8p, _f32p, _sz, _sz]
         L.kvo_compress_nf4_blocks_f32.argtypes = [_f32p, _u8p, _f32p, _sz, _sz]
         L.kvo_decompress_nf4_blocks.argtypes = [_u8p, _f32p, _f32p, _sz, _sz]
+        L.kvo_evict_select.argtypes = [C.c_int, C.c_void_p, _sz, C.c_float, C.c_void_p]
+        L.kvo_evict_select.restype = C.c_int
+        L.kvo_evict_score.argtypes = [C.c_int, C.c_void_p, C.c_float, C.c_float]
+        L.kvo_evict_score.restype = C.c_float
+        L.kvo_evict_select_composite.argtypes = [_i32p, _f32p, C.c_int, C.c_void_p, _sz, C.c_float,
+                                                 C.c_void_p]
+        L.kvo_evict_select_composite.restype = C.c_int
+        L.kvo_predict_next_access.argtypes = [_u64p, _sz]
+        L.kvo_predict_next_access.restype = C.c_float
         L.kvo_fp16_wrap_encode_n.argtypes = [_f32p, _u16p, _sz]
         L.kvo_fp16_wrap_decode_n.argtypes = [_u16p, _f32p, _sz]
         L.kvo_append.argtypes = [C.c_void_p, _sz, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -174,6 +190,32 @@ class Oracle:
         self.L.kvo_fp16_wrap_encode_n(x, out, x.size)
         return out
 
+    # AdvancedEvictionPolicy (pages: EVICT_METRICS records)
+    def evict_select(self, policy, pages, decay=0.95, predicted=None):
+        pages = np.ascontiguousarray(pages, EVICT_METRICS)
+        pred = None if predicted is None else _c(predicted, np.float32)
+        return self.L.kvo_evict_select(policy, pages.ctypes.data, pages.size, decay,
+                                       None if pred is None else pred.ctypes.data)
+
+    def evict_scores(self, policy, pages, decay=0.95, predicted=None):
+        pages = np.ascontiguousarray(pages, EVICT_METRICS)
+        out = np.empty(pages.size, np.float32)
+        for i in range(pages.size):
+            p = -1.0 if predicted is None else float(predicted[i])
+            out[i] = self.L.kvo_evict_score(policy, pages[i:i + 1].ctypes.data, decay, p)
+        return out
+
+    def evict_select_composite(self, policies, weights, pages, decay=0.95, predicted=None):
+        pages = np.ascontiguousarray(pages, EVICT_METRICS)
+        pred = None if predicted is None else _c(predicted, np.float32)
+        return self.L.kvo_evict_select_composite(_c(policies, np.int32), _c(weights, np.float32),
+                                                 len(policies), pages.ctypes.data, pages.size, decay,
+                                                 None if pred is None else pred.ctypes.data)
+
+    def predict_next_access(self, times):
+        t = _c(times, np.uint64)
+        return self.L.kvo_predict_next_access(t, t.size)
+
     def fp16_wrap_decode(self, h):
         h = _c(h, np.uint16).ravel()
         out = np.empty(h.size, np.float32)
@@ -252,6 +294,11 @@ class Reference:
         L.kvref_decompress_int8.argtypes = [_i8p, _f32p, _sz, _f32p]
         L.kvref_compress_nf4.argtypes = [_f32p, _u8p, _sz, _f32p]
         L.kvref_decompress_nf4.argtypes = [_u8p, _f32p, _sz, _f32p]
+        L.kvref_evict_select.argtypes = [C.c_int, C.c_void_p, _sz, C.c_float, C.c_void_p, C.c_void_p,
+                                         C.c_void_p]
+        L.kvref_evict_select.restype = C.c_int
+        L.kvref_evict_composite.argtypes = [_i32p, _f32p, C.c_int, C.c_void_p, _sz, _f32p]
+        L.kvref_evict_composite.restype = C.c_int
         L.kvref_fp16_wrap_encode.argtypes = [_f32p, _u16p, _sz]
         L.kvref_fp16_wrap_decode.argtypes = [_u16p, _f32p, _sz]
         L.kvref_attention.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _f32p]
@@ -328,6 +375,25 @@ class Reference:
         out = np.empty(h.size, np.float32)
         self.L.kvref_fp16_wrap_decode(h, out, h.size)
         return out
+
+    def evict_select(self, policy, pages, decay=0.95, hist=None, hist_len=None):
+        """Returns (selected page id, every page's calculateScore(m, 0))."""
+        pages = np.ascontiguousarray(pages, EVICT_METRICS)
+        scores = np.empty(pages.size, np.float32)
+        h = None if hist is None else _c(hist, np.uint64)
+        hl = None if hist_len is None else _c(hist_len, np.int32)
+        sel = self.L.kvref_evict_select(policy, pages.ctypes.data, pages.size, decay,
+                                        None if h is None else h.ctypes.data,
+                                        None if hl is None else hl.ctypes.data, scores.ctypes.data)
+        return sel, scores
+
+    def evict_composite(self, policies, weights, pages):
+        """Returns (selected page id, the manager's normalised weights)."""
+        pages = np.ascontiguousarray(pages, EVICT_METRICS)
+        nw = np.empty(len(policies), np.float32)
+        sel = self.L.kvref_evict_composite(_c(policies, np.int32), _c(weights, np.float32), len(policies),
+                                           pages.ctypes.data, pages.size, nw)
+        return sel, nw
 
     def attention(self, q, k, v):
         q, k, v = (_c(a, np.float32) for a in (q, k, v))

@@ -20,6 +20,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <set>
 #include <string>
 #include <thread>
@@ -114,6 +115,56 @@ void kvref_fp16_wrap_decode(const uint16_t *in, float *out, size_t count) {
     QuantizationStats st{};
     st.type = CompressionType::FP16;
     eng->decompress(in, out, count, st);
+}
+
+// native-engine/cpp/AdvancedEvictionPolicy.cpp: selectPageToEvict of one
+// policy and every page's calculateScore(m, 0).  Predictive: hist holds,
+// per page, up to 10 access tokens (hist_len[i] of them) replayed through
+// recordAccess first.
+static std::unique_ptr<EvictionPolicy> make_policy(int policy, float decay) {
+    switch (policy) {
+    case 0: return std::make_unique<LRUEvictionPolicy>();
+    case 1: return std::make_unique<TokenWeightedEvictionPolicy>(decay);
+    case 2: return std::make_unique<AttentionBasedEvictionPolicy>();
+    default: return std::make_unique<PredictiveEvictionPolicy>();
+    }
+}
+
+int kvref_evict_select(int policy, const EvictionMetrics *pages, size_t n, float decay,
+                       const uint64_t *hist, const int32_t *hist_len, float *scores) {
+    auto pol = make_policy(policy, decay);
+    if (policy == 3 && hist) {
+        auto *pp = static_cast<PredictiveEvictionPolicy *>(pol.get());
+        for (size_t i = 0; i < n; ++i)
+            for (int k = 0; k < hist_len[i]; ++k) pp->recordAccess(pages[i].pageId, hist[i * 10 + k]);
+    }
+    std::vector<EvictionMetrics> v(pages, pages + n);
+    if (scores)
+        for (size_t i = 0; i < n; ++i) scores[i] = pol->calculateScore(v[i], 0);
+    return pol->selectPageToEvict(v);
+}
+
+// CompositeEvictionManager (:176-263) with the given policies and raw
+// weights (normalised by the manager), pages registered in order.
+int kvref_evict_composite(const int32_t *policies, const float *weights, int np,
+                          const EvictionMetrics *pages, size_t n, float *norm_weights) {
+    CompositeEvictionManager mgr;
+    mgr.switchPolicy(static_cast<EvictionStrategy>(policies[0]));
+    for (int p = 1; p < np; ++p) {
+        switch (policies[p]) {
+        case 0: mgr.addPolicy(std::make_unique<LRUEvictionPolicy>(), weights[p]); break;
+        case 1: mgr.addPolicy(std::make_unique<TokenWeightedEvictionPolicy>(), weights[p]); break;
+        case 2: mgr.addPolicy(std::make_unique<AttentionBasedEvictionPolicy>(), weights[p]); break;
+        default: mgr.addPolicy(std::make_unique<PredictiveEvictionPolicy>(), weights[p]); break;
+        }
+    }
+    std::vector<float> w(weights, weights + np);
+    mgr.setPolicyWeights(w);
+    float total = 0.0f;
+    for (float x : w) total += x;
+    for (int p = 0; p < np; ++p) norm_weights[p] = w[p] / total;
+    for (size_t i = 0; i < n; ++i) mgr.updatePageMetrics(pages[i].pageId, pages[i]);
+    return mgr.selectPageToEvict();
 }
 
 // runtime/tensor_ops.cpp:179-219

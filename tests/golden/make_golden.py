@@ -167,6 +167,41 @@ def gen_fp16_wrap(R: Reference):
                         dec_bits=R.fp16_wrap_decode(h).view(np.uint32))
 
 
+def gen_evict(R: Reference):
+    """AdvancedEvictionPolicy selectPageToEvict and calculateScore(m, 0) of
+    every policy (native-engine/cpp/AdvancedEvictionPolicy.cpp), Predictive
+    after replaying per-page access histories, and one composite manager."""
+    from oracle import EVICT_METRICS
+    res = {}
+    for c in range(12):
+        n = int(kvgen.randint(1000 + c, 1, 1, 400)[0])
+        m = np.zeros(n, EVICT_METRICS)
+        m["last_access_token"] = kvgen.randint(1100 + c, n, 0, 10 ** 6).astype(np.uint64)
+        m["last_access_token"][kvgen.uniform(1200 + c, n) < (0.0 if c % 3 == 0 else 0.1)] = 0
+        if c == 5:
+            m["last_access_token"][:] = 0
+        if c == 7:
+            m["last_access_token"][0] = np.uint64(2 ** 64 - 5)
+        m["average_attention"] = kvgen.uniform(1300 + c, n).astype(np.float32)
+        m["average_attention"][n // 2] = m["average_attention"][0]
+        m["page_id"] = kvgen.permutation(1400 + c, n) + 100
+        hl = kvgen.randint(1500 + c, n, 0, 10).astype(np.int32)
+        hist = np.zeros((n, 10), np.uint64)
+        for i in range(n):
+            hist[i, :hl[i]] = np.sort(kvgen.randint(1600 + c * 1000 + i, int(hl[i]), 0, 10 ** 6)).astype(np.uint64)
+        res[f"pages{c}"] = m.view(np.uint8)
+        res[f"hist{c}"] = hist
+        res[f"hist_len{c}"] = hl
+        for pol in (0, 1, 2, 3):
+            sel, sc = R.evict_select(pol, m, 0.95, hist if pol == 3 else None, hl if pol == 3 else None)
+            res[f"sel{c}_{pol}"] = np.int32(sel)
+            res[f"scores{c}_{pol}"] = sc
+        sel, nw = R.evict_composite([0, 1, 2], np.array([1.0, 2.0, 0.5], np.float32), m)
+        res[f"composite{c}"] = np.int32(sel)
+        res[f"composite_w{c}"] = nw
+    np.savez_compressed(os.path.join(HERE, "evict.npz"), **res)
+
+
 def gen_attention(R: Reference):
     # cpu_ops_test (tests/cpu_ops_test.cpp:35-47) identity case + seeded rows
     out = {}
@@ -325,7 +360,7 @@ def main():
     R = Reference()
     gens = {"kv_compress": gen_kv_compress, "int8": gen_int8, "attention": gen_attention,
             "paged": gen_paged, "int8_decode": gen_int8_decode, "lru": gen_lru, "depth": gen_depth,
-            "disk": gen_disk, "nf4": gen_nf4, "fp16_wrap": gen_fp16_wrap}
+            "disk": gen_disk, "nf4": gen_nf4, "fp16_wrap": gen_fp16_wrap, "evict": gen_evict}
     for name in (sys.argv[1:] or gens):  # e.g. `make_golden.py nf4 fp16_wrap` for one fixture
         gens[name](R)
     print("golden fixtures written to", HERE)

@@ -143,3 +143,52 @@ def test_kv_attention_backend_matches_oracle(built, tmp_path, oracle):
             oracle.append(pools[l], bt, pos, k, v, 16)
             ref = oracle.paged_decode(pools[l], bt, pos + 1, q)
             assert close(got[s, l], ref), (s, l)
+
+
+@pytest.mark.gpu
+def test_kv_compression_engine_dropin_matches_reference(built, tmp_path, oracle):
+    """include/KVCompressionEngine.h (the reference's native-engine class) on the
+    GPU: every mode's ratio, stats, compressed bytes and round trip equal the
+    reference's (through the oracle, itself pinned to the reference's golden
+    outputs), one block per call as the reference computes it."""
+    g = golden("nf4.npz")
+    blocks, off = [], 0
+    for n in g["lens"]:
+        blocks.append(g["data"][off:off + int(n)])
+        off += int(n)
+    blocks.append(golden("fp16_wrap.npz")["x"])
+    cases = [(t, b) for b in blocks for t in (0, 1, 2, 3)]
+    with open(tmp_path / "in.bin", "wb") as f:
+        for t, b in cases:
+            f.write(np.int32(t).tobytes() + np.uint64(b.size).tobytes() + np.ascontiguousarray(b, np.float32).tobytes())
+    rc, out = run(built, "kv_compression_engine_io", tmp_path / "in.bin", tmp_path / "out.bin")
+    assert rc == 0, out
+    raw = (tmp_path / "out.bin").read_bytes()
+    pos = 0
+    for t, b in cases:
+        ratio, = np.frombuffer(raw, np.float32, 1, pos)
+        stats = np.frombuffer(raw, np.float32, 4, pos + 4)
+        typ, = np.frombuffer(raw, np.int32, 1, pos + 20)
+        nbytes, = np.frombuffer(raw, np.uint64, 1, pos + 24)
+        pos += 32
+        comp = np.frombuffer(raw, np.uint8, int(nbytes), pos)
+        pos += int(nbytes)
+        back = np.frombuffer(raw, np.float32, b.size, pos)
+        pos += 4 * b.size
+        assert typ == t and ratio == (1.0, 0.5, 0.25, 0.125)[t]
+        if t == 0:
+            want_c, want_s, want_b = b.view(np.uint8), None, b
+        elif t == 1:
+            enc = oracle.fp16_wrap_encode(b)
+            want_c, want_s, want_b = enc.view(np.uint8), None, oracle.fp16_wrap_decode(enc)
+        elif t == 2:
+            c, s = oracle.compress_int8(b)
+            want_c, want_s, want_b = c.view(np.uint8), s, oracle.decompress_int8(c, s)
+        else:
+            c, s = oracle.compress_nf4(b)
+            want_c, want_s, want_b = c, s, oracle.decompress_nf4(c, s, b.size)
+        assert np.array_equal(comp, want_c), (t, b.size)
+        if want_s is not None:
+            assert np.array_equal(stats.view(np.uint32), want_s.view(np.uint32)), (t, b.size)
+        assert np.array_equal(back.view(np.uint32), want_b.view(np.uint32)), (t, b.size)
+    assert pos == len(raw)

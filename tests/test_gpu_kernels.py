@@ -495,3 +495,32 @@ def test_migrate_frames_roundtrip(kvx):
                        dev(np.array([0], np.int32)), frame, 1, error_flag=err)
     torch.cuda.synchronize()
     assert err.item() & 2
+
+
+def test_eviction_policies_on_device_match_reference(kvx, oracle):
+    """kvx_evict_select / _composite against the reference's selectPageToEvict
+    (golden), for 12 page sets of up to 400 pages, and against the oracle on a
+    large set (1,000,000 pages, single-CTA scan)."""
+    from oracle import EVICT_METRICS
+    g = golden("evict.npz")
+    for c in range(12):
+        m = g[f"pages{c}"].view(EVICT_METRICS)
+        hist, hl = g[f"hist{c}"], g[f"hist_len{c}"]
+        pred = np.array([oracle.predict_next_access(hist[i, :hl[i]]) for i in range(m.size)], np.float32)
+        pages = dev(m.view(np.uint8))
+        for pol in (0, 1, 2, 3):
+            got = kvx.evict_select(pol, pages, 0.95, dev(pred) if pol == 3 else None).item()
+            assert got == int(g[f"sel{c}_{pol}"]), (c, pol)
+        got = kvx.evict_select_composite([0, 1, 2], g[f"composite_w{c}"], pages).item()
+        assert got == int(g[f"composite{c}"]), c
+    n = 1_000_000
+    m = np.zeros(n, EVICT_METRICS)
+    m["last_access_token"] = kvgen.randint(71, n, 1, 10 ** 9).astype(np.uint64)
+    m["average_attention"] = kvgen.uniform(72, n).astype(np.float32)
+    m["average_attention"][[17, 500_000]] = -0.25  # the best score twice: the lower index wins
+    m["page_id"] = np.arange(n) + 7
+    pages = dev(m.view(np.uint8))
+    for pol in (0, 1, 2):
+        assert kvx.evict_select(pol, pages).item() == oracle.evict_select(pol, m), pol
+    assert kvx.evict_select(2, pages).item() == 17 + 7
+    assert kvx.evict_select(0, pages[:0]).item() == -1

@@ -194,3 +194,22 @@ def test_disk_page_format():
     from oracle import persist_bytes
     g = golden("disk_page.npz")
     assert persist_bytes(g["key"], g["value"]) == g["blob"].tobytes()
+
+
+def test_eviction_policies_exact(oracle):
+    """AdvancedEvictionPolicy (native-engine/cpp/AdvancedEvictionPolicy.cpp): every
+    policy's calculateScore(m, 0) and selectPageToEvict, the currentToken = 0
+    wrap-around kept; Predictive from replayed access histories; composite."""
+    from oracle import EVICT_METRICS
+    g = golden("evict.npz")
+    for c in range(12):
+        m = g[f"pages{c}"].view(EVICT_METRICS)
+        hist, hl = g[f"hist{c}"], g[f"hist_len{c}"]
+        pred = np.array([oracle.predict_next_access(hist[i, :hl[i]]) for i in range(m.size)], np.float32)
+        for pol in (0, 1, 2, 3):
+            p = pred if pol == 3 else None
+            assert oracle.evict_select(pol, m, 0.95, p) == int(g[f"sel{c}_{pol}"]), (c, pol)
+            assert np.array_equal(oracle.evict_scores(pol, m, 0.95, p).view(np.uint32),
+                                  g[f"scores{c}_{pol}"].view(np.uint32)), (c, pol)
+        got = oracle.evict_select_composite(np.array([0, 1, 2], np.int32), g[f"composite_w{c}"], m)
+        assert got == int(g[f"composite{c}"]), c
