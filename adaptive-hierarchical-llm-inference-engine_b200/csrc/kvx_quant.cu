@@ -355,6 +355,21 @@ decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict
     }
 }
 
+// Any block size or alignment: one thread per element.
+template <typename T>
+__global__ void decompress_scalar_kernel(const int8_t *__restrict__ codes, const float *__restrict__ stats,
+                                         T *__restrict__ dst, size_t num_blocks, int block_elems) {
+    const size_t n = num_blocks * (size_t)block_elems;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t b = e / (size_t)block_elems;
+        const float v = dequant_one(codes[e], stats[4 * b + 3], stats[4 * b + 2]);
+        if constexpr (sizeof(T) == 4)
+            dst[e] = v;
+        else
+            dst[e] = __float2half_rn(v);
+    }
+}
+
 // One thread per 4 codes; block_elems % 4 == 0.
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -617,10 +632,10 @@ extern "C" KVX_API int kvx_decompress_nf4(const uint8_t *codes, const float *sta
     if (!codes || !stats || !dst || block_elems <= 0) return KVX_EINVAL;
     if (dst_dtype != KVX_F16 && dst_dtype != KVX_F32) return KVX_EINVAL;
     const size_t esz = dst_dtype == KVX_F32 ? 4 : 2;
-    if (!aligned16(stats) || (reinterpret_cast<uintptr_t>(dst) & (esz - 1))) return KVX_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(stats) & 3) || (reinterpret_cast<uintptr_t>(dst) & (esz - 1))) return KVX_EINVAL;
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (block_elems == 2048 && aligned16(codes) && aligned16(dst)) {
+    if (block_elems == 2048 && aligned16(codes) && aligned16(dst) && aligned16(stats)) {
         const unsigned grid = grid_for(num_blocks, 8);
         if (dst_dtype == KVX_F32)
             decompress_nf4_2048_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
@@ -661,11 +676,19 @@ extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *sta
                                            int32_t block_elems, void *stream) {
     if (!codes || !stats || !dst || block_elems <= 0) return KVX_EINVAL;
     if (dst_dtype != KVX_F16 && dst_dtype != KVX_F32) return KVX_EINVAL;
-    if (block_elems % 4 || !aligned16(stats) || (reinterpret_cast<uintptr_t>(codes) & 3) ||
-        !aligned16(dst))
+    const uintptr_t esz = dst_dtype == KVX_F32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(stats) & 3) || (reinterpret_cast<uintptr_t>(dst) & (esz - 1)))
         return KVX_EINVAL;
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (block_elems % 4 || !aligned16(stats) || (reinterpret_cast<uintptr_t>(codes) & 3) || !aligned16(dst)) {
+        const unsigned grid = grid_for(num_blocks * (size_t)block_elems, 256);
+        if (dst_dtype == KVX_F32)
+            decompress_scalar_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+        else
+            decompress_scalar_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+        return launch_status();
+    }
     if (block_elems == 2048 && aligned16(codes)) {
         const unsigned grid = grid_for(num_blocks, 8);
         if (dst_dtype == KVX_F32)
