@@ -579,7 +579,7 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
                const int32_t *seq_lens, const int32_t *positions, const void *new_k,
                const void *new_v, int32_t batch, int32_t num_q_heads, const void *q, void *out,
                int32_t io_dtype, float sm_scale, void *workspace, size_t workspace_bytes_,
-               int32_t *error_flag, void *stream, int min_chunk = 0) {
+               int32_t *error_flag, void *stream, int min_chunk = 0, float *attn = nullptr) {
     if (!kv || !kv->pool || !block_table || !q || !out) return KVX_EINVAL;
     if (!seq_lens && !positions) return KVX_EINVAL;
     if (batch <= 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || num_q_heads <= 0) return KVX_EINVAL;
@@ -615,6 +615,10 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     p.q = q;
     p.out = out;
     p.error_flag = error_flag;
+    if (attn) {  // [batch][hq][max_pages][2] then [batch][hq][2]
+        p.attn_pm = attn;
+        p.attn_ml = attn + (size_t)batch * num_q_heads * max_pages * 2;
+    }
     p.num_pages = kv->num_pages;
     p.hkv = kv->num_kv_heads;
     p.hq = num_q_heads;
@@ -639,9 +643,10 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     const float scale = sm_scale > 0.f ? sm_scale : 1.0f / sqrtf((float)kHeadDim);
     p.scale_log2 = scale * 1.4426950408889634f;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (attn && !tc) return KVX_EUNSUPPORTED;  // attention mass: tensor-core path only
     if (tc) {
         const int rc = launch_decode_tc(p, kv->dtype, io_dtype, batch, st);
-        if (rc != KVX_EUNSUPPORTED) return rc;
+        if (rc != KVX_EUNSUPPORTED || attn) return rc;
         p.nhg = (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;  // no tensor map: SIMT kernel
         p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages), min_chunk_r);
         p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
@@ -763,4 +768,109 @@ extern "C" KVX_API int kvx_decode_noalloc(const kvx_paged *kv, const int32_t *bl
     return run_decode(kv, block_table, max_pages, seq_lens, nullptr, nullptr, nullptr, batch,
                       num_q_heads, q, out, io_dtype, sm_scale, scratch, kNoAllocScratchBytes,
                       error_flag, stream, min_chunk);
+}
+
+namespace kvx {
+namespace {
+
+// Per (sequence, logical page): the attention the page received, averaged
+// over the q-heads: mean_h sum_{t in page} softmax_h(t) =
+// mean_h s_hp * exp2(m_hp - M_h) / L_h.  Zero for pages past the context.
+__global__ void attn_mass_kernel(const float *__restrict__ pm, const float *__restrict__ ml,
+                                 const int32_t *__restrict__ seq_lens, int batch, int hq, int max_pages,
+                                 float *__restrict__ mass) {
+    const size_t n = (size_t)batch * max_pages;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const int s = (int)(e / max_pages), lp = (int)(e % max_pages);
+        const int T = min(max(seq_lens[s], 0), max_pages * kPageTokens);
+        float acc = 0.f;
+        if (lp * kPageTokens < T) {
+            for (int h = 0; h < hq; ++h) {
+                const float2 f = *reinterpret_cast<const float2 *>(ml + ((size_t)s * hq + h) * 2);
+                const float2 v = *reinterpret_cast<const float2 *>(pm + (((size_t)s * hq + h) * max_pages + lp) * 2);
+                acc += v.y * exp2f(v.x - f.x) / f.y;
+            }
+            acc /= (float)hq;
+        }
+        mass[e] = acc;
+    }
+}
+
+struct EvictMetricsRec {  // native-engine/include/AdvancedEvictionPolicy.h:19-27
+    unsigned long long last_access_token;
+    float total_attention, average_attention, access_frequency;
+    uint32_t pad0;
+    unsigned long long creation_time, page_size;
+    int32_t page_id;
+    uint32_t pad1;
+};
+
+// updateMetrics of AttentionBasedEvictionPolicy (:88-91: lastAccessToken =
+// currentToken) with the attention the decode measured: per physical page
+// read this step, averageAttention = the page's mass, totalAttention and
+// accessFrequency accumulate.
+__global__ void attn_to_metrics_kernel(const float *__restrict__ mass, const int32_t *__restrict__ bt,
+                                       const int32_t *__restrict__ seq_lens, int batch, int max_pages,
+                                       EvictMetricsRec *metrics, int num_metrics, unsigned long long token) {
+    const size_t n = (size_t)batch * max_pages;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const int s = (int)(e / max_pages), lp = (int)(e % max_pages);
+        const int T = min(max(seq_lens[s], 0), max_pages * kPageTokens);
+        if (lp * kPageTokens >= T) continue;
+        const int phys = bt[e];
+        if (phys < 0 || phys >= num_metrics) continue;
+        EvictMetricsRec &m = metrics[phys];
+        m.last_access_token = token;
+        m.average_attention = mass[e];
+        atomicAdd(&m.total_attention, mass[e]);
+        atomicAdd(&m.access_frequency, 1.0f);
+    }
+}
+
+size_t attn_bytes(int batch, int hq, int max_pages) {
+    return ((size_t)batch * hq * max_pages * 2 + (size_t)batch * hq * 2) * sizeof(float);
+}
+
+}  // namespace
+}  // namespace kvx
+
+extern "C" KVX_API size_t kvx_decode_attn_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t max_pages,
+                                                          int32_t page_tokens) {
+    const size_t base = kvx_decode_workspace_bytes(batch, num_q_heads, max_pages, page_tokens);
+    if (!base) return 0;
+    return base + (attn_bytes(batch, num_q_heads, max_pages) + 15) / 16 * 16;
+}
+
+extern "C" KVX_API int kvx_decode_attn(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                                       const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                                       const void *q, void *out, int32_t io_dtype, float sm_scale,
+                                       void *workspace, size_t workspace_bytes_, float *page_mass,
+                                       int32_t *error_flag, void *stream) {
+    if (!seq_lens || !page_mass || !workspace || batch <= 0 || num_q_heads <= 0 || max_pages <= 0)
+        return KVX_EINVAL;
+    const size_t base = workspace_bytes(batch, num_q_heads, max_pages);
+    if (workspace_bytes_ < base + attn_bytes(batch, num_q_heads, max_pages)) return KVX_ENOSPC;
+    if (reinterpret_cast<uintptr_t>(page_mass) & 3) return KVX_EINVAL;
+    float *attn = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + base);
+    int rc = run_decode(kv, block_table, max_pages, seq_lens, nullptr, nullptr, nullptr, batch, num_q_heads, q, out,
+                        io_dtype, sm_scale, workspace, base, error_flag, stream, 0, attn);
+    if (rc != KVX_OK) return rc;
+    const size_t n = (size_t)batch * max_pages;
+    attn_mass_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        attn, attn + (size_t)batch * num_q_heads * max_pages * 2, seq_lens, batch, num_q_heads, max_pages, page_mass);
+    return launch_status();
+}
+
+extern "C" KVX_API int kvx_attn_to_metrics(const float *page_mass, const int32_t *block_table, int32_t max_pages,
+                                           const int32_t *seq_lens, int32_t batch, kvx_evict_metrics *metrics,
+                                           int32_t num_metrics, uint64_t current_token, void *stream) {
+    if (!page_mass || !block_table || !seq_lens || !metrics || batch <= 0 || max_pages <= 0 || num_metrics <= 0)
+        return KVX_EINVAL;
+    if (reinterpret_cast<uintptr_t>(metrics) & 7) return KVX_EINVAL;
+    const size_t n = (size_t)batch * max_pages;
+    attn_to_metrics_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0,
+                             static_cast<cudaStream_t>(stream)>>>(
+        page_mass, block_table, seq_lens, batch, max_pages, reinterpret_cast<EvictMetricsRec *>(metrics), num_metrics,
+        (unsigned long long)current_token);
+    return launch_status();
 }

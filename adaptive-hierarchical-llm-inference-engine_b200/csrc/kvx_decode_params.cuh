@@ -19,6 +19,11 @@ struct DecodeParams {
     const int32_t *positions;  // fused append: token position per sequence (else null)
     const uint8_t *new_k, *new_v;  // fused append rows [batch][hkv][128]
     int32_t *error_flag;
+    // attention mass (tensor-core path only; null = off): per (sequence,
+    // q-head, logical page) the running max and the page's sum of
+    // exp2(score - max) [batch][hq][max_pages][2]; per (sequence, q-head)
+    // the final max and sum [batch][hq][2]
+    float *attn_pm, *attn_ml;
     int num_pages, hkv, hq, max_pages, max_splits, chunk, group, nhg;
     float scale_log2;
 };

@@ -146,7 +146,7 @@ __device__ __forceinline__ uint32_t swz(int row, int c) {
 template <bool kBig>
 __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][4], uint32_t qlo,
                                         float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
-                                        int tok, int T, float scale_log2, int lane) {
+                                        int tok, int T, float scale_log2, int lane, float &psum0, float &psum1) {
     const int lrow = lane & 7, lmat = lane >> 3;
     // ---- S = Q K^T for tokens 0-7 (n-tile 0) and 8-15 (n-tile 1)
     float sc[2][4];
@@ -223,6 +223,8 @@ __device__ __forceinline__ void tc_page(uint32_t sbase, const uint32_t (&qa)[8][
         }
     l0 = l0 * a0 + ps0;
     if constexpr (kBig) l1 = l1 * a1 + ps1;
+    psum0 = ps0;
+    psum1 = ps1;
     uint32_t pa[4];
     pa[0] = pack_h2(sc[0][0], sc[0][1]);
     pa[2] = pack_h2(sc[1][0], sc[1][1]);
@@ -285,7 +287,7 @@ __device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool 
                                            const uint32_t (&qa)[8][4], uint32_t qlo, float qs0, float qs1,
                                            float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
                                            float &z0, float &z1, int tok_a, int tok_b, int T,
-                                           float scale_log2, int lane) {
+                                           float scale_log2, int lane, float (&psum)[2][2]) {
     const int g = lane >> 2, r = lane & 3;
     const float4 ska = *reinterpret_cast<const float4 *>(st), sva = *reinterpret_cast<const float4 *>(st + 4);
     const float4 skb = *reinterpret_cast<const float4 *>(st + 8), svb = *reinterpret_cast<const float4 *>(st + 12);
@@ -369,6 +371,7 @@ __device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool 
         }
     l0 = l0 * a0 + (ps0[0] + ps0[1]);
     if constexpr (kBig) l1 = l1 * a1 + (ps1[0] + ps1[1]);
+    psum[0][0] = ps0[0], psum[0][1] = ps1[0], psum[1][0] = ps0[1], psum[1][1] = ps1[1];
     // P' = p * scale_v as fp16 hi + lo (masked tokens stay exactly 0).  hi +
     // lo equals P' to 2^-22 relative, so the zero-point scalar may use the
     // unrounded sum: (zp - 1024 scale_v) * sum(p), off by < 2.5e-4 * scale_v
@@ -447,7 +450,7 @@ template <bool kI8> __device__ __forceinline__ int park_ofs(int row, int d) {
     return row * kHeadDim + d;
 }
 
-template <typename QT, bool kBig, bool kI8>
+template <typename QT, bool kBig, bool kI8, bool kAttn>
 __global__ void __launch_bounds__(kTcThreads, 3)
 tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     using Cfg = TcCfg<kI8>;
@@ -621,6 +624,25 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
     float z0 = 0.f, z1 = 0.f;  // int8 zero-point terms
 
+    // attention mass of one page: the rows' sums over its tokens, with the
+    // running max they are relative to (warp-uniform call)
+    auto record_mass = [&](int lp, float a, float b) {
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        if constexpr (kBig) {
+            b += __shfl_xor_sync(0xffffffffu, b, 1);
+            b += __shfl_xor_sync(0xffffffffu, b, 2);
+        }
+        if (tq == 0) {
+            if (gq < nh)
+                *reinterpret_cast<float2 *>(p.attn_pm + (((size_t)s * p.hq + h0 + gq) * p.max_pages + lp) * 2) =
+                    make_float2(m0, a);
+            if (kBig && gq + 8 < nh)
+                *reinterpret_cast<float2 *>(p.attn_pm + (((size_t)s * p.hq + h0 + gq + 8) * p.max_pages + lp) * 2) =
+                    make_float2(m1, b);
+        }
+    };
+
     bool ok = true;
     int done = 0;
     for (int i = 0; i < n_my; ++i) {
@@ -636,10 +658,16 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
             const int lpa = p0 + warp + kTcWarps * (2 * i);
             const bool va = page_ok(phys_of(2 * i));
             const bool vb = 2 * i + 1 < n_pg && page_ok(phys_of(2 * i + 1));
-            if (va || vb)
+            if (va || vb) {
+                float psum[2][2];
                 tc_pair_i8<kBig>(sbase, wstat + st * Cfg::kStatFloats, va, vb, qa, qlo, qs0, qs1, o, m0, m1, l0,
                                  l1, z0, z1, lpa * kPageTokens + 2 * (lane & 3),
-                                 (lpa + kTcWarps) * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane);
+                                 (lpa + kTcWarps) * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane, psum);
+                if constexpr (kAttn) {
+                    if (va) record_mass(lpa, psum[0][0], psum[0][1]);
+                    if (vb) record_mass(lpa + kTcWarps, psum[1][0], psum[1][1]);
+                }
+            }
         }
         const int lp = p0 + warp + kTcWarps * i;
         const int phys = phys_of(i);
@@ -652,8 +680,10 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
                     reinterpret_cast<const uint4 *>(src)[c];
                 __syncwarp();
             }
+            float ps0_, ps1_;
             tc_page<kBig>(sbase, qa, qlo, o, m0, m1, l0, l1, lp * kPageTokens + 2 * (lane & 3), T,
-                          p.scale_log2, lane);
+                          p.scale_log2, lane, ps0_, ps1_);
+            if constexpr (kAttn) record_mass(lp, ps0_, ps1_);
         }
         __syncwarp();
         if (lane == 0 && i + kTcStages < n_my) {
@@ -736,6 +766,8 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         if (nsplit == 1) {
             QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
             io_traits<QT>::store(out + d, O / L);
+            if (kAttn && d == 0)
+                *reinterpret_cast<float2 *>(p.attn_ml + ((size_t)s * p.hq + h) * 2) = make_float2(M, L);
         } else {
             const size_t pi = ((size_t)s * p.hq + h) * p.max_splits + split;
             p.part_o[pi * kHeadDim + d] = O;
@@ -772,6 +804,8 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
         QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim;
         io_traits<QT>::store(out + d, O / L);
+        if (kAttn && d == 0)
+            *reinterpret_cast<float2 *>(p.attn_ml + ((size_t)s * p.hq + h0 + g) * 2) = make_float2(M, L);
     }
 }
 
@@ -823,9 +857,9 @@ bool make_pool_map_i8(CUtensorMap *tm, const void *pool, long long rows) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename QT, bool kBig, bool kI8>
+template <typename QT, bool kBig, bool kI8, bool kAttn>
 int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorMap &tm) {
-    auto kern = tc_decode_kernel<QT, kBig, kI8>;
+    auto kern = tc_decode_kernel<QT, kBig, kI8, kAttn>;
     constexpr int smem = TcCfg<kI8>::kSmem;
     static bool attr_set = false;
     if (!attr_set) {
@@ -838,12 +872,22 @@ int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorM
     return launch_status();
 }
 
-template <bool kI8>
-int launch_tc_io(const DecodeParams &p, int io_dtype, int batch, cudaStream_t st, const CUtensorMap &tm) {
+template <bool kI8, bool kAttn>
+int launch_tc_io2(const DecodeParams &p, int io_dtype, int batch, cudaStream_t st, const CUtensorMap &tm) {
     const bool big = p.group > 8;
     if (io_dtype == KVX_F32)
-        return big ? launch_tc<float, true, kI8>(p, batch, st, tm) : launch_tc<float, false, kI8>(p, batch, st, tm);
-    return big ? launch_tc<__half, true, kI8>(p, batch, st, tm) : launch_tc<__half, false, kI8>(p, batch, st, tm);
+        return big ? launch_tc<float, true, kI8, kAttn>(p, batch, st, tm)
+                   : launch_tc<float, false, kI8, kAttn>(p, batch, st, tm);
+    return big ? launch_tc<__half, true, kI8, kAttn>(p, batch, st, tm)
+               : launch_tc<__half, false, kI8, kAttn>(p, batch, st, tm);
+}
+
+// Attention-mass recording is a separate instantiation, so the plain
+// decode carries none of its code.
+template <bool kI8>
+int launch_tc_io(const DecodeParams &p, int io_dtype, int batch, cudaStream_t st, const CUtensorMap &tm) {
+    return p.attn_pm ? launch_tc_io2<kI8, true>(p, io_dtype, batch, st, tm)
+                     : launch_tc_io2<kI8, false>(p, io_dtype, batch, st, tm);
 }
 
 }  // namespace

@@ -80,6 +80,13 @@ lib.kvx_f16_trunc_to_f32.argtypes = [_vp, _vp, _sz, _vp]
 lib.kvx_lru_select.argtypes = [_vp, _sz, _vp, _vp]
 lib.kvx_migrate_frames.argtypes = [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _sz, _i32, _i32, _vp, _vp]
 lib.kvx_evict_select.argtypes = [_i32, _vp, _sz, _f32, _vp, _vp, _vp]
+lib.kvx_decode_attn_workspace_bytes.restype = _sz
+lib.kvx_decode_attn_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32]
+lib.kvx_decode_attn.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32, _f32,
+                                _vp, _sz, _vp, _vp, _vp]
+lib.kvx_decode_attn.restype = C.c_int
+lib.kvx_attn_to_metrics.argtypes = [_vp, _vp, _i32, _vp, _i32, _vp, _i32, C.c_uint64, _vp]
+lib.kvx_attn_to_metrics.restype = C.c_int
 lib.kvx_evict_select_composite.argtypes = [_vp, _vp, _i32, _vp, _sz, _f32, _vp, _vp, _vp]
 for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
             "kvx_compress_nf4", "kvx_decompress_nf4", "kvx_fp16_wrap_encode", "kvx_fp16_wrap_decode",
@@ -312,3 +319,34 @@ def evict_select_composite(policies, weights, pages, decay=0.95, predicted=None,
            lib.kvx_evict_select_composite(pol, w, len(policies), _ptr(pages), pages.numel() // 48, decay,
                                           _ptr(predicted), _ptr(out), _stream(stream)))
     return out
+
+
+def decode_attn(pool, block_table, seq_lens, q, out=None, stats=None, page_mass=None, workspace=None,
+                error_flag=None, sm_scale=0.0, stream=None):
+    """Paged decode plus each page's attention mass ([batch][max_pages], mean
+    over q-heads).  Returns (out, page_mass)."""
+    torch = _torch()
+    kv = paged(pool, stats)
+    batch, hq, _ = q.shape
+    mp = block_table.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    if page_mass is None:
+        page_mass = torch.empty((batch, mp), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = torch.zeros(lib.kvx_decode_attn_workspace_bytes(batch, hq, mp, PAGE_TOKENS),
+                                dtype=torch.uint8, device=q.device)
+    rc = lib.kvx_decode_attn(C.byref(kv), _ptr(block_table), mp, _ptr(seq_lens), batch, hq, _ptr(q), _ptr(out),
+                             _dtype_code(q), sm_scale, _ptr(workspace), workspace.numel(), _ptr(page_mass),
+                             _ptr(error_flag), _stream(stream))
+    _check("kvx_decode_attn", rc)
+    return out, page_mass
+
+
+def attn_to_metrics(page_mass, block_table, seq_lens, metrics, current_token, stream=None):
+    """Fold one step's page_mass into EvictionMetrics records (CUDA uint8
+    tensor of 48-byte records indexed by physical page)."""
+    rc = lib.kvx_attn_to_metrics(_ptr(page_mass), _ptr(block_table), block_table.shape[1], _ptr(seq_lens),
+                                 block_table.shape[0], _ptr(metrics), metrics.numel() // 48, current_token,
+                                 _stream(stream))
+    _check("kvx_attn_to_metrics", rc)

@@ -254,6 +254,34 @@ KVX_API int kvx_evict_select_composite(const int32_t *policies, const float *wei
                                        size_t n, float decay, const float *predicted,
                                        int32_t *page_id, void *stream);
 
+/* Decode (as kvx_decode) that also measures the attention each page got:
+ * page_mass[batch][max_pages] (device float) receives, per sequence and
+ * logical page, the softmax probability mass on the page's tokens averaged
+ * over the q-heads (each sequence's masses sum to 1; 0 past the context).
+ * This is the per-page attention AttentionBasedEvictionPolicy scores on
+ * (native-engine/cpp/AdvancedEvictionPolicy.cpp:95-111, whose
+ * setAttentionWeights is a stub there): the decode kernel records each
+ * page's softmax sum with its running max (8 bytes per q-head and page)
+ * and a small kernel normalises with the final (max, sum).  fp16 and int8
+ * pools (tensor-core path); KVX_EUNSUPPORTED otherwise.  Workspace:
+ * kvx_decode_attn_workspace_bytes, zero-filled once like the decode's. */
+KVX_API size_t kvx_decode_attn_workspace_bytes(int32_t batch, int32_t num_q_heads,
+                                               int32_t max_pages, int32_t page_tokens);
+KVX_API int kvx_decode_attn(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                            const int32_t *seq_lens, int32_t batch, int32_t num_q_heads,
+                            const void *q, void *out, int32_t io_dtype, float sm_scale,
+                            void *workspace, size_t workspace_bytes, float *page_mass,
+                            int32_t *error_flag, void *stream);
+/* AttentionBasedEvictionPolicy::updateMetrics (:88-91) fed with measured
+ * attention: for every page the step read (block_table / seq_lens as given
+ * to the decode), metrics[physical page]: lastAccessToken = current_token,
+ * averageAttention = the page's mass, totalAttention += mass,
+ * accessFrequency += 1 (atomic; a page shared by several sequences keeps
+ * the last writer's average).  metrics: device array of num_metrics. */
+KVX_API int kvx_attn_to_metrics(const float *page_mass, const int32_t *block_table, int32_t max_pages,
+                                const int32_t *seq_lens, int32_t batch, kvx_evict_metrics *metrics,
+                                int32_t num_metrics, uint64_t current_token, void *stream);
+
 /* Page-frame migration between the device pool and a host frame arena
  * (pinned, mapped with cudaHostAlloc(..., cudaHostAllocMapped) or registered).
  * Replaces KVCacheGPU::transferToHost / transferToGPU

@@ -523,3 +523,79 @@ def test_eviction_policies_on_device_match_reference(kvx, oracle):
         assert kvx.evict_select(pol, pages).item() == oracle.evict_select(pol, m), pol
     assert kvx.evict_select(2, pages).item() == 17 + 7
     assert kvx.evict_select(0, pages[:0]).item() == -1
+
+
+def _page_mass_ref(pool_f, bt, lens, q, hkv):
+    """float64 softmax per (sequence, q-head), summed per page, mean over q-heads."""
+    B, hq, _ = q.shape
+    G = hq // hkv
+    mp = bt.shape[1]
+    mass = np.zeros((B, mp))
+    for s in range(B):
+        T = int(lens[s])
+        if T == 0:
+            continue
+        npg = (T + 15) // 16
+        K = pool_f[bt[s, :npg], 0].transpose(1, 0, 2, 3).reshape(hkv, npg * 16, 128)[:, :T]
+        for h in range(hq):
+            sc = K[h // G].astype(np.float64) @ q[s, h].astype(np.float64) / np.sqrt(128.0)
+            p = np.exp(sc - sc.max())
+            p /= p.sum()
+            mass[s, :npg] += np.add.reduceat(p, np.arange(0, T, 16)) / hq
+    return mass
+
+
+@pytest.mark.parametrize("kind,hkv,hq", [("f16", 8, 24), ("f16", 1, 12), ("i8", 8, 24)])
+def test_decode_attention_mass(kvx, monkeypatch, kind, hkv, hq):
+    """kvx_decode_attn: same output as kvx_decode, each page's softmax mass
+    (mean over q-heads) as a float64 softmax gives it, masses summing to 1,
+    independent of the split."""
+    lens = kvgen.randint(130 + hq, 6, 1, 1500)
+    lens[0] = 1
+    bt, num_pages = kvgen.paged_layout(lens, 16, 3, seed=131)
+    pool = kvgen.normal(132, (num_pages, 2, hkv, 16, 128)).astype(np.float16)
+    q = kvgen.normal(133, (lens.size, hq, 128))
+    args = [dev(bt), dev(lens.astype(np.int32)), dev(q)]
+    if kind == "f16":
+        gpool, stats, pool_f = dev(pool), None, pool.astype(np.float32)
+    else:
+        codes, stats = kvx.compress_int8(dev(pool))
+        gpool = codes.view(num_pages, 2, hkv, 16, 128)
+        pool_f = kvx.decompress_int8(codes, stats).view(num_pages, 2, hkv, 16, 128).cpu().numpy()
+    out, mass = kvx.decode_attn(gpool, *args, stats=stats)
+    plain = kvx.decode(gpool, *args, stats=stats)
+    assert torch.equal(out, plain)
+    mass = mass.cpu().numpy()
+    ref = _page_mass_ref(pool_f, bt, lens, q, hkv)
+    assert np.abs(mass - ref).max() < 2e-4
+    assert np.abs(mass.sum(1) - 1.0).max() < 1e-4
+    monkeypatch.setenv("KVX_DECODE_CHUNK", "4")
+    _, mass4 = kvx.decode_attn(gpool, *args, stats=stats)
+    assert np.abs(mass4.cpu().numpy() - mass).max() < 1e-5
+
+
+def test_attention_based_eviction_from_measured_attention(kvx):
+    """decode -> per-page attention -> EvictionMetrics -> AttentionBased victim:
+    the least-attended page of the step (the reference's policy on measured
+    attention instead of its stub)."""
+    from oracle import EVICT_METRICS
+    lens = np.array([300, 41, 700], np.int64)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=141)
+    pool = kvgen.normal(142, (num_pages, 2, 8, 16, 128)).astype(np.float16)
+    q = kvgen.normal(143, (3, 24, 128)) * 3
+    m = np.zeros(num_pages, EVICT_METRICS)
+    m["page_id"] = np.arange(num_pages)
+    metrics = dev(m.view(np.uint8))
+    gbt, glens = dev(bt), dev(lens.astype(np.int32))
+    _, mass = kvx.decode_attn(dev(pool), gbt, glens, dev(q))
+    kvx.attn_to_metrics(mass, gbt, glens, metrics, 12345)
+    got = metrics.cpu().numpy().view(EVICT_METRICS)
+    mass = mass.cpu().numpy()
+    want_avg = np.zeros(num_pages, np.float32)
+    for s in range(3):
+        npg = (int(lens[s]) + 15) // 16
+        want_avg[bt[s, :npg]] = mass[s, :npg]
+    assert np.array_equal(got["average_attention"], want_avg)
+    assert np.all(got["last_access_token"] == 12345) and np.all(got["access_frequency"] == 1)
+    victim = kvx.evict_select(kvx.EVICT_ATTENTION_BASED, metrics).item()
+    assert victim == int(np.argmin(want_avg))
