@@ -115,6 +115,13 @@ __device__ __forceinline__ void mma16816_lo(float &c0, float &c1, const uint32_t
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f));
 }
 
+// Programmatic dependent launch (launches with
+// cudaLaunchAttributeProgrammaticStreamSerialization): let the next grid on
+// the stream be scheduled once every CTA of this one got here, and wait for
+// the previous grid's completion (a no-op without such a launch).
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -475,6 +482,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     const int h0 = kvh * p.group;
     const int nh = p.group;
     if (p0 >= npages) {
+        grid_dependency_wait();  // the previous decode may still use the workspace / output
         if (npages == 0 && split == 0) {
             QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0) * kHeadDim;
             for (int i = threadIdx.x; i < nh * kHeadDim; i += kTcThreads) io_traits<QT>::store(o + i, 0.f);
@@ -692,6 +700,11 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
     }
 
+    // Streaming done: the next launch on this stream (the next layer's decode)
+    // may start filling SMs; it waits for this grid before it touches the
+    // split workspace or the output, as this one does here.
+    grid_dependents_launch();
+    grid_dependency_wait();
     if (threadIdx.x == 0) s_flag[0] = 0;
     __syncthreads();
     if (!ok) {
@@ -867,8 +880,20 @@ int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorM
             return KVX_ECUDA;
         attr_set = true;
     }
-    dim3 grid(p.max_splits, p.hkv, batch);
-    kern<<<grid, kTcThreads, smem, st>>>(p, tm);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.max_splits, p.hkv, batch);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = kAttn ? 0 : 1;  // plain decode only
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, p, tm) != cudaSuccess) {
+        cudaGetLastError();
+        return KVX_ECUDA;
+    }
     return launch_status();
 }
 

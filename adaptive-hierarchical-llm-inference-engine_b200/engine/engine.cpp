@@ -16,6 +16,10 @@
 namespace kvx_engine {
 namespace {
 
+// Layers per group of a decode step: inputs are copied and outputs read back
+// per group (one event each way), the group's launches run back to back.
+constexpr int kLayerGroup = 7;
+
 int env_int(const char *name, int dflt) {
     const char *v = getenv(name);
     if (!v || !*v) return dflt;
@@ -637,51 +641,75 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     memcpy(h_pos_, lens_.data(), B * sizeof(int32_t));
     if (cudaMemcpyAsync(d_pos_, h_pos_, B * sizeof(int32_t), cudaMemcpyHostToDevice, compute_) != cudaSuccess)
         return KVX_ECUDA;
-    for (int l = 0; l < L; ++l) {  // inputs of every layer, one event per layer
-        if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
-            cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
-            cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
-            cudaEventRecord(ev_in_[l], copy_))
-            return KVX_ECUDA;
+    // Layers run in groups: one input copy event and one output event per
+    // group, so within a group the decode launches follow each other with
+    // nothing in between and each may start while the previous drains
+    // (programmatic dependent launch); the groups' copies overlap the other
+    // groups' kernels.
+    const int G = L < kLayerGroup ? L : kLayerGroup;
+    const int ngroups = (L + G - 1) / G;
+    for (int gi = 0; gi < ngroups; ++gi) {
+        for (int l = gi * G; l < std::min(L, (gi + 1) * G); ++l)
+            if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
+                cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
+                cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_))
+                return KVX_ECUDA;
+        if (cudaEventRecord(ev_in_[gi], copy_)) return KVX_ECUDA;
     }
     int rc = KVX_OK;
-    for (int l = 0; l < L && rc == KVX_OK; ++l) {
-        if (layers_[l].tier != kGpu) {  // tiered: bring the layer back (may evict the LRU layer)
-            const int r = to_gpu_locked(l);
-            if (r < 0) {
-                rc = r;
-                break;
-            }
-        }
-        layers_[l].last_used = ++clock_;
-        kvx_paged view{arena_ + (size_t)layers_[l].slab * slab_bytes_, nullptr, KVX_F16,
-                       cfg_.pages_per_layer, hkv, 128, 16};
-        if (cudaStreamWaitEvent(compute_, ev_in_[l], 0) != cudaSuccess) {
+    for (int gi = 0; gi < ngroups && rc == KVX_OK; ++gi) {
+        const int l0 = gi * G, l1 = std::min(L, l0 + G);
+        if (cudaStreamWaitEvent(compute_, ev_in_[gi], 0) != cudaSuccess) {
             rc = KVX_ECUDA;
             break;
         }
-        rc = kvx_append_decode(&view, d_table_, max_pages_, d_pos_, B, d_k_ + l * kstride,
-                               d_v_ + l * kstride, hq, d_q_ + l * qstride, d_out_ + l * qstride,
-                               KVX_F16, 0.f, d_ws_, ws_bytes_, d_err_, compute_);
-        if (rc) break;
-        if (cudaEventRecord(ev_out_[l], compute_)) {
-            rc = KVX_ECUDA;
-        } else if (comm_) {  // all-gather this layer's rows over NCCL, then read them back
-            uint16_t *g = d_gather_ + (size_t)l * world_ * qrow;
-            if (cudaStreamWaitEvent(comm_stream_, ev_out_[l], 0) ||
-                nccl().all_gather(d_out_ + l * qstride, g, qrow, ncclFloat16, static_cast<ncclComm_t>(comm_),
-                                  comm_stream_) != ncclSuccess ||
-                cudaEventRecord(ev_gath_[l], comm_stream_) ||
-                (out && (cudaStreamWaitEvent(copy_, ev_gath_[l], 0) ||
-                         cudaMemcpyAsync(out + l * world_ * qrow, g, world_ * qrow * 2, cudaMemcpyDeviceToHost,
-                                         copy_))))
-                rc = KVX_ECUDA;
-        } else if (out && (cudaStreamWaitEvent(copy_, ev_out_[l], 0) ||
-                           cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost,
-                                           copy_))) {
-            rc = KVX_ECUDA;
+        for (int l = l0; l < l1 && rc == KVX_OK; ++l) {
+            if (layers_[l].tier != kGpu) {  // tiered: bring the layer back (may evict the LRU layer)
+                const int r = to_gpu_locked(l);
+                if (r < 0) {
+                    rc = r;
+                    break;
+                }
+            }
+            layers_[l].last_used = ++clock_;
+            kvx_paged view{arena_ + (size_t)layers_[l].slab * slab_bytes_, nullptr, KVX_F16,
+                           cfg_.pages_per_layer, hkv, 128, 16};
+            rc = kvx_append_decode(&view, d_table_, max_pages_, d_pos_, B, d_k_ + l * kstride,
+                                   d_v_ + l * kstride, hq, d_q_ + l * qstride, d_out_ + l * qstride,
+                                   KVX_F16, 0.f, d_ws_, ws_bytes_, d_err_, compute_);
+            current_layer_ = l;
         }
-        current_layer_ = l;
+        if (rc) break;
+        if (cudaEventRecord(ev_out_[gi], compute_)) {
+            rc = KVX_ECUDA;
+        } else if (comm_) {  // all-gather the group's rows over NCCL, then read them back
+            if (cudaStreamWaitEvent(comm_stream_, ev_out_[gi], 0)) {
+                rc = KVX_ECUDA;
+                break;
+            }
+            for (int l = l0; l < l1; ++l)
+                if (nccl().all_gather(d_out_ + l * qstride, d_gather_ + (size_t)l * world_ * qrow, qrow, ncclFloat16,
+                                      static_cast<ncclComm_t>(comm_), comm_stream_) != ncclSuccess)
+                    rc = KVX_ECUDA;
+            if (rc || cudaEventRecord(ev_gath_[gi], comm_stream_)) {
+                rc = KVX_ECUDA;
+                break;
+            }
+            if (out) {
+                if (cudaStreamWaitEvent(copy_, ev_gath_[gi], 0) ||
+                    cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
+                                    (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                    rc = KVX_ECUDA;
+            }
+        } else if (out) {
+            if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) {
+                rc = KVX_ECUDA;
+                break;
+            }
+            for (int l = l0; l < l1; ++l)
+                if (cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                    rc = KVX_ECUDA;
+        }
     }
     int32_t err = 0;
     if (cudaStreamSynchronize(compute_) != cudaSuccess || cudaStreamSynchronize(copy_) != cudaSuccess ||

@@ -173,14 +173,13 @@ def run_ours(args):
     main = torch.cuda.current_stream()
     layer_done = [torch.cuda.Event() for _ in range(LAYERS)]
 
-    def step(ev=None):
+    def step():
+        # the layers' launches follow each other with nothing in between, so
+        # each may start while the previous drains (programmatic dependent
+        # launch); per-layer events would serialise them
         for l in range(LAYERS):
-            if ev is not None:
-                ev[l][0].record()
             kvx.append_decode(views[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
                               error_flag=err)
-            if ev is not None:
-                ev[l][1].record()
             if world > 1:
                 layer_done[l].record()
                 with torch.cuda.stream(comm):
@@ -200,22 +199,19 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
 
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(LAYERS)] for _ in range(steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
     t0.record()
     for k in range(steps):
-        step(ev[k])
+        step()
     t1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1)
-    dec_ms = [a.elapsed_time(b) for row in ev for (a, b) in row]
     assert err.item() == 0, f"device error flag {err.item()}"
 
     lens_timed = [lens0 + warm + k + 1 for k in range(steps)]
@@ -231,7 +227,10 @@ def run_ours(args):
     # roofline of the decode kernel: algorithmic bytes per launch / mean launch time
     mean_layer_bytes = rank_bytes / (steps * LAYERS)
     qo_bytes = 2 * B * hq * DIM * 2 + B * max_pages * 4 + B * 4 + 2 * B * hkv * DIM * 2
-    mean_dec_ms = sum(dec_ms) / len(dec_ms)
+    # launches overlap by design (each starts while the previous drains), so
+    # a launch's duration is the timed region (CUDA events on the launching
+    # stream) divided by the launches in it
+    mean_dec_ms = ms / (steps * LAYERS)
     achieved = (mean_layer_bytes + qo_bytes) / (mean_dec_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
     traffic = None
@@ -255,7 +254,8 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_kind": peak_kind, "kernel": "tc_decode_kernel (append + decode + split combine fused)",
-                     "mean_launch_us": round(mean_dec_ms * 1e3, 2)},
+                     "mean_launch_us": round(mean_dec_ms * 1e3, 2),
+                     "launch_duration": "timed region / launches (consecutive launches overlap)"},
         "gpu_launches": steps * LAYERS,
         "clocks": clk,
     }
