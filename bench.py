@@ -173,6 +173,8 @@ def run_ours(args):
     main = torch.cuda.current_stream()
     layer_done = [torch.cuda.Event() for _ in range(LAYERS)]
 
+    GROUP = 7  # layers per all-gather group (N > 1)
+
     def step():
         # the layers' launches follow each other with nothing in between, so
         # each may start while the previous drains (programmatic dependent
@@ -180,11 +182,13 @@ def run_ours(args):
         for l in range(LAYERS):
             kvx.append_decode(views[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
                               error_flag=err)
-            if world > 1:
+            if world > 1 and (l % GROUP == GROUP - 1 or l == LAYERS - 1):
+                # all-gather a group of layers' outputs once the group is done
                 layer_done[l].record()
                 with torch.cuda.stream(comm):
                     comm.wait_event(layer_done[l])
-                    dist.all_gather_into_tensor(gathered[l], out[l])
+                    for j in range(l - l % GROUP, l + 1):
+                        dist.all_gather_into_tensor(gathered[j], out[j])
         pos.add_(1)
         if world > 1:
             main.wait_stream(comm)
