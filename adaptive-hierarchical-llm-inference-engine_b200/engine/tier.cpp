@@ -31,9 +31,19 @@
 //         and reads are marked in step order.
 // Pinned list staging is double-buffered by step parity; before reusing a
 // parity the host waits for the copies of step s-2.
+//
+// Disk tier (host_frames > 0): RAM is a FIFO of arrivals (ram_prev/next).
+// A write-back that finds RAM full first spills the oldest RAM frame to
+// the spill file (pwrite, after waiting for the copy that wrote its slot if
+// it was one of the last two steps'), which frees its slot at once.  A
+// miss on a disk frame is read (pread) into a host slot during planning,
+// after the previous step's loads -- which may still read slots freed at
+// its end -- have finished, and is then loaded like a RAM frame.
 #include "kvx_tier.h"
 
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <unistd.h>
 
 #include <cstdint>
 #include <cstring>
@@ -94,6 +104,15 @@ struct kvx_tier {
     int64_t step = 0;
     kvx_tier_stats totals{};
 
+    // disk tier
+    bool disk = false;
+    int fd = -1;
+    int64_t host_cap = 0, in_ram = 0;
+    std::vector<int32_t> ram_prev, ram_next;  // RAM arrival order (head newest)
+    int32_t ram_head = -1, ram_tail = -1;
+    std::vector<int64_t> slot_step;           // per host slot: step whose write-back filled it
+    bool h2d_prev_synced = false;             // this step waited for the previous step's loads
+
     // device side
     uint8_t *dev_base = nullptr, *host_base = nullptr;
     cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
@@ -122,7 +141,74 @@ void push_front(kvx_tier *t, int32_t f) {
     if (t->tail < 0) t->tail = f;
 }
 
+void ram_unlink(kvx_tier *t, int32_t f) {
+    const int32_t p = t->ram_prev[f], n = t->ram_next[f];
+    if (p >= 0) t->ram_next[p] = n; else t->ram_head = n;
+    if (n >= 0) t->ram_prev[n] = p; else t->ram_tail = p;
+    t->ram_prev[f] = t->ram_next[f] = -1;
+    --t->in_ram;
+}
+
+void ram_push(kvx_tier *t, int32_t f) {
+    t->ram_prev[f] = -1;
+    t->ram_next[f] = t->ram_head;
+    if (t->ram_head >= 0) t->ram_prev[t->ram_head] = f;
+    t->ram_head = f;
+    if (t->ram_tail < 0) t->ram_tail = f;
+    ++t->in_ram;
+}
+
+bool file_io(int fd, void *buf, size_t n, off_t off, bool write) {
+    uint8_t *b = static_cast<uint8_t *>(buf);
+    while (n) {
+        const ssize_t r = write ? pwrite(fd, b, n, off) : pread(fd, b, n, off);
+        if (r <= 0) return false;
+        b += r;
+        n -= (size_t)r;
+        off += r;
+    }
+    return true;
+}
+
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? KVX_OK : KVX_ECUDA; }
+
+// Wait until the write-back that filled host slot hs (if recent) is done.
+int wait_slot_written(kvx_tier *t, int32_t hs) {
+    const int64_t w = t->slot_step[hs];
+    if (t->bookkeeping || w < 0 || w < t->step - 2) return KVX_OK;
+    if (w == t->step) return KVX_ENOSPC;  // written by this very step: RAM tier too small
+    return cuda_status(cudaEventSynchronize(t->ev_d2h[w & 1]));
+}
+
+// Move the oldest RAM frame to the spill file; its host slot is free again.
+int spill_oldest(kvx_tier *t, kvx_tier_stats &st) {
+    const int32_t f = t->ram_tail;
+    if (f < 0) return KVX_ENOSPC;
+    const int32_t hs = t->hslot[f];
+    int rc = wait_slot_written(t, hs);
+    if (rc != KVX_OK) return rc;
+    if (!t->bookkeeping &&
+        !file_io(t->fd, t->host_base + (size_t)hs * t->cfg.frame_bytes, t->cfg.frame_bytes,
+                 (off_t)f * (off_t)t->cfg.frame_bytes, true))
+        return KVX_ECUDA;
+    ram_unlink(t, f);
+    t->hslot[f] = -1;
+    t->slot_step[hs] = -1;
+    t->host_free.push_front(hs);
+    ++st.frames_disk_write;
+    return KVX_OK;
+}
+
+// A free host slot, spilling the oldest RAM frame when there is none.
+int take_host_slot(kvx_tier *t, kvx_tier_stats &st, int32_t &hs) {
+    if (t->host_free.empty()) {
+        if (!t->disk) return KVX_ENOSPC;
+        const int rc = spill_oldest(t, st);
+        if (rc != KVX_OK) return rc;
+    }
+    hs = t->host_free.pop();
+    return KVX_OK;
+}
 
 void release(kvx_tier *t) {
     if (!t->bookkeeping) {
@@ -141,6 +227,7 @@ void release(kvx_tier *t) {
         if (t->host_base) cudaFreeHost(t->host_base);
         if (t->err) cudaFree(t->err);
     }
+    if (t->fd >= 0) close(t->fd);
 }
 
 int setup_device(kvx_tier *t) {
@@ -243,8 +330,14 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
     t->bookkeeping = cfg->device < 0;
     const int64_t U = cfg->universe, C = cfg->capacity, S = cfg->spare;
     const int64_t resident0 = U < C ? U : C;
+    t->disk = cfg->host_frames > 0 && cfg->host_frames < U - resident0;
+    if (t->disk && (!cfg->spill_path || cfg->host_frames < 3 * S)) {
+        delete t;
+        return KVX_EINVAL;  // the RAM tier must outlast three steps' write-backs
+    }
+    t->host_cap = t->disk ? cfg->host_frames : U - resident0;
     t->dev_slots = C + S;
-    t->host_slots = (U - resident0) + S;
+    t->host_slots = t->host_cap + S;
     if (t->dev_slots > INT32_MAX || t->host_slots > INT32_MAX) {
         delete t;
         return KVX_EINVAL;
@@ -257,6 +350,11 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
         t->victim_idx.assign(U, -1);
         t->last_step.assign(U, -1);
         t->reclaimed.assign(t->dev_slots, -1);
+        t->slot_step.assign(t->host_slots, -1);
+        if (t->disk) {
+            t->ram_prev.assign(U, -1);
+            t->ram_next.assign(U, -1);
+        }
         t->dev_free.init(t->dev_slots);
         t->host_free.init(t->host_slots);
     } catch (const std::bad_alloc &) {
@@ -268,9 +366,20 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
         push_front(t, (int32_t)f);
     }
     t->resident = resident0;
-    for (int64_t f = resident0; f < U; ++f) t->hslot[f] = (int32_t)(f - resident0);
+    for (int64_t f = resident0; f < resident0 + t->host_cap; ++f) {  // the rest start on disk
+        t->hslot[f] = (int32_t)(f - resident0);
+        if (t->disk) ram_push(t, (int32_t)f);
+    }
     for (int64_t s = resident0; s < t->dev_slots; ++s) t->dev_free.push((int32_t)s);
-    for (int64_t s = U - resident0; s < t->host_slots; ++s) t->host_free.push((int32_t)s);
+    for (int64_t s = t->host_cap; s < t->host_slots; ++s) t->host_free.push((int32_t)s);
+    if (t->disk && !t->bookkeeping) {
+        t->fd = open(cfg->spill_path, O_RDWR | O_CREAT | O_TRUNC, 0600);
+        if (t->fd < 0 || ftruncate(t->fd, (off_t)U * (off_t)cfg->frame_bytes) != 0) {
+            release(t);
+            delete t;
+            return KVX_EINVAL;
+        }
+    }
     if (!t->bookkeeping) {
         const int rc = setup_device(t);
         if (rc != KVX_OK) {
@@ -306,9 +415,9 @@ extern "C" KVX_API int kvx_tier_host_arena(kvx_tier *t, void **base, int64_t *sl
 extern "C" KVX_API int kvx_tier_location(kvx_tier *t, int64_t frame, int32_t *tier, int64_t *slot) {
     if (!t || frame < 0 || frame >= t->cfg.universe) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
-    const bool on_dev = t->dslot[frame] >= 0;
-    if (tier) *tier = on_dev ? 0 : 1;
-    if (slot) *slot = on_dev ? t->dslot[frame] : t->hslot[frame];
+    const bool on_dev = t->dslot[frame] >= 0, in_ram = !on_dev && t->hslot[frame] >= 0;
+    if (tier) *tier = on_dev ? 0 : in_ram ? 1 : 2;
+    if (slot) *slot = on_dev ? t->dslot[frame] : in_ram ? t->hslot[frame] : frame;
     return KVX_OK;
 }
 
@@ -330,8 +439,10 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     }
     for (int64_t i = 0; i < n; ++i)
         if (t->victim_idx[frames[i]] == -2) t->victim_idx[frames[i]] = -1;
-    if (loads > t->cfg.spare || (uint64_t)loads > t->dev_free.count || (uint64_t)loads > t->host_free.count)
+    if (loads > t->cfg.spare || (uint64_t)loads > t->dev_free.count ||
+        (!t->disk && (uint64_t)loads > t->host_free.count))
         return KVX_ENOSPC;
+    t->h2d_prev_synced = false;
 
     kvx_tier_stats st{};
     st.accesses = n;
@@ -359,7 +470,17 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
                 --t->resident;
                 ++st.evictions;
                 if (evicted) evicted[i] = v;
-                const int32_t hs = t->host_free.pop();
+                int32_t hs = -1;
+                if (t->disk) {  // RAM full: the oldest RAM frame goes to disk first
+                    int rc = KVX_OK;
+                    while (rc == KVX_OK && t->in_ram >= t->host_cap) rc = spill_oldest(t, st);
+                    if (rc == KVX_OK) rc = take_host_slot(t, st, hs);
+                    if (rc != KVX_OK) return rc;
+                    t->slot_step[hs] = s;
+                    ram_push(t, v);
+                } else {
+                    hs = t->host_free.pop();
+                }
                 t->victim_idx[v] = (int32_t)t->d2h.size();
                 t->d2h.push_back(Copy{t->dslot[v], hs, v, false});
                 t->freed_dev.push_back(t->dslot[v]);
@@ -372,10 +493,36 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
                 ++st.reloads;
                 t->dslot[f] = c.dev;
                 t->reclaimed[c.dev] = s;
+                if (t->disk) {
+                    ram_unlink(t, f);
+                    t->slot_step[c.host] = -1;
+                }
                 t->host_free.push_front(c.host);
                 t->hslot[f] = -1;
                 t->victim_idx[f] = -1;
             } else {
+                if (t->disk) {
+                    if (t->hslot[f] >= 0) {
+                        ram_unlink(t, f);
+                    } else {  // on disk: read it into a host slot, then load as from RAM
+                        int32_t hs = -1;
+                        int rc = take_host_slot(t, st, hs);
+                        if (rc == KVX_OK && !t->bookkeeping && !t->h2d_prev_synced) {
+                            // slots freed at the previous step's end may still be read by its loads
+                            if (t->ev_used[(s - 1) & 1] && cudaEventSynchronize(t->ev_h2d[(s - 1) & 1]) != cudaSuccess)
+                                rc = KVX_ECUDA;
+                            t->h2d_prev_synced = true;
+                        }
+                        if (rc == KVX_OK && !t->bookkeeping &&
+                            !file_io(t->fd, t->host_base + (size_t)hs * t->cfg.frame_bytes, t->cfg.frame_bytes,
+                                     (off_t)f * (off_t)t->cfg.frame_bytes, false))
+                            rc = KVX_ECUDA;
+                        if (rc != KVX_OK) return rc;
+                        t->hslot[f] = hs;
+                        ++st.frames_disk_read;
+                    }
+                    t->slot_step[t->hslot[f]] = -1;
+                }
                 const int32_t ds = t->dev_free.pop();
                 t->h2d_dev.push_back(ds);
                 t->h2d_host.push_back(t->hslot[f]);
@@ -408,6 +555,8 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     t->totals.reloads += st.reloads;
     t->totals.frames_h2d += st.frames_h2d;
     t->totals.frames_d2h += st.frames_d2h;
+    t->totals.frames_disk_read += st.frames_disk_read;
+    t->totals.frames_disk_write += st.frames_disk_write;
     if (stats) *stats = st;
     return rc;
 }
@@ -442,4 +591,35 @@ extern "C" KVX_API int kvx_tier_totals(kvx_tier *t, kvx_tier_stats *stats) {
     std::lock_guard<std::mutex> lk(t->mu);
     *stats = t->totals;
     return KVX_OK;
+}
+
+namespace {
+
+int frame_io(kvx_tier *t, int64_t frame, void *buf, bool to_store) {
+    if (!t || !buf || frame < 0 || frame >= t->cfg.universe || t->bookkeeping) return KVX_EINVAL;
+    int rc = kvx_tier_sync(t);
+    if (rc != KVX_OK) return rc;
+    std::lock_guard<std::mutex> lk(t->mu);
+    const size_t fb = t->cfg.frame_bytes;
+    if (t->dslot[frame] >= 0) {
+        uint8_t *d = t->dev_base + (size_t)t->dslot[frame] * fb;
+        return cuda_status(to_store ? cudaMemcpy(d, buf, fb, cudaMemcpyHostToDevice)
+                                    : cudaMemcpy(buf, d, fb, cudaMemcpyDeviceToHost));
+    }
+    if (t->hslot[frame] >= 0) {
+        uint8_t *h = t->host_base + (size_t)t->hslot[frame] * fb;
+        if (to_store) std::memcpy(h, buf, fb); else std::memcpy(buf, h, fb);
+        return KVX_OK;
+    }
+    return file_io(t->fd, buf, fb, (off_t)frame * (off_t)fb, to_store) ? KVX_OK : KVX_ECUDA;
+}
+
+}  // namespace
+
+extern "C" KVX_API int kvx_tier_write_frame(kvx_tier *t, int64_t frame, const void *buf) {
+    return frame_io(t, frame, const_cast<void *>(buf), true);
+}
+
+extern "C" KVX_API int kvx_tier_read_frame(kvx_tier *t, int64_t frame, void *buf) {
+    return frame_io(t, frame, buf, false);
 }

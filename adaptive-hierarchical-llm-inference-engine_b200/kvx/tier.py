@@ -26,10 +26,11 @@ from . import HEAD_DIM, KVX_F16, PAGE_TOKENS, KvPaged, _check, lib
 class TierConfig(C.Structure):
     _fields_ = [("frame_bytes", C.c_size_t), ("universe", C.c_int64), ("capacity", C.c_int64),
                 ("spare", C.c_int64), ("device", C.c_int32), ("load_ctas", C.c_int32),
-                ("store_ctas", C.c_int32)]
+                ("store_ctas", C.c_int32), ("host_frames", C.c_int64), ("spill_path", C.c_char_p)]
 
 
-_STAT_FIELDS = ("accesses", "hits", "misses", "evictions", "reloads", "frames_h2d", "frames_d2h")
+_STAT_FIELDS = ("accesses", "hits", "misses", "evictions", "reloads", "frames_h2d", "frames_d2h",
+                "frames_disk_read", "frames_disk_write")
 
 
 class TierStats(C.Structure):
@@ -52,8 +53,11 @@ lib.kvx_tier_wait_resident.argtypes = [_vp, _vp]
 lib.kvx_tier_mark_read.argtypes = [_vp, _vp]
 lib.kvx_tier_sync.argtypes = [_vp]
 lib.kvx_tier_totals.argtypes = [_vp, C.POINTER(TierStats)]
+lib.kvx_tier_write_frame.argtypes = [_vp, _i64, _vp]
+lib.kvx_tier_read_frame.argtypes = [_vp, _i64, _vp]
 for _fn in ("kvx_tier_device_arena", "kvx_tier_host_arena", "kvx_tier_location", "kvx_tier_step",
-            "kvx_tier_wait_resident", "kvx_tier_mark_read", "kvx_tier_sync", "kvx_tier_totals"):
+            "kvx_tier_wait_resident", "kvx_tier_mark_read", "kvx_tier_sync", "kvx_tier_totals",
+            "kvx_tier_write_frame", "kvx_tier_read_frame"):
     getattr(lib, _fn).restype = C.c_int
 
 
@@ -77,8 +81,11 @@ class _DeviceBytes:
 
 
 class Tier:
-    def __init__(self, frame_bytes, universe, capacity, spare, device=0, load_ctas=0, store_ctas=0):
-        self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, load_ctas, store_ctas)
+    def __init__(self, frame_bytes, universe, capacity, spare, device=0, load_ctas=0, store_ctas=0,
+                 host_frames=0, spill_path=None):
+        self._path = None if spill_path is None else str(spill_path).encode()
+        self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, load_ctas, store_ctas,
+                              host_frames, self._path)
         h = _vp()
         _check("kvx_tier_create", lib.kvx_tier_create(C.byref(self.cfg), C.byref(h)))
         self.h = h
@@ -126,7 +133,18 @@ class Tier:
     def location(self, frame):
         tier, slot = C.c_int32(), _i64()
         _check("kvx_tier_location", lib.kvx_tier_location(self.h, frame, C.byref(tier), C.byref(slot)))
-        return ("device", "host")[tier.value], slot.value
+        return ("device", "host", "disk")[tier.value], slot.value
+
+    def write_frame(self, frame, data):
+        """Set frame's bytes wherever it lives (numpy array of frame_bytes)."""
+        buf = np.ascontiguousarray(data).view(np.uint8)
+        assert buf.size == self.frame_bytes
+        _check("kvx_tier_write_frame", lib.kvx_tier_write_frame(self.h, frame, buf.ctypes.data))
+
+    def read_frame(self, frame):
+        out = np.empty(self.frame_bytes, np.uint8)
+        _check("kvx_tier_read_frame", lib.kvx_tier_read_frame(self.h, frame, out.ctypes.data))
+        return out
 
     def step(self, frames, dev_slot=None, evicted=True, hit=True):
         """Apply the policy to `frames` (int32, in order) and enqueue the copies.

@@ -35,6 +35,19 @@
  * the store when that decode has been enqueued (kvx_tier_mark_read), so a
  * later step never overwrites a frame before the decode that reads it ran.
  *
+ * Disk tier (optional).  With host_frames > 0 the pinned arena holds at
+ * most host_frames frames (plus `spare`); every other non-resident frame
+ * lives in one spill file (spill_path) at offset frame * frame_bytes -- the
+ * GPU -> RAM -> SSD chain of the reference's KVPageState
+ * (src/main/java/com/adaptivellm/kv/KVPageState.java).  Initially frames
+ * capacity .. capacity+host_frames-1 are in RAM (host slots 0..), the rest
+ * on disk (their bytes: kvx_tier_write_frame).  The RAM tier is a FIFO of
+ * arrivals: when a write-back needs a host slot and RAM is full, the frame
+ * that entered RAM first goes to disk (pwrite, after any copy still writing
+ * its slot finished); a miss on a disk frame is read into a host slot
+ * during kvx_tier_step (pread) and then loaded like any RAM frame.  Device
+ * residency decisions are unchanged (KVManager's LRU).
+ *
  * Bookkeeping-only stores (device = -1) allocate no device or pinned memory
  * and copy nothing: they run the policy and the slot assignment alone.
  */
@@ -63,6 +76,8 @@ typedef struct kvx_tier_config {
                             host memory by the SMs and need more requests in
                             flight than write-backs; 16 + 4 keeps both directions
                             of the host link busy when they run together */
+    int64_t host_frames; /* RAM tier size; 0: every non-resident frame in RAM (no disk) */
+    const char *spill_path; /* disk tier file (created / truncated) when host_frames > 0 */
 } kvx_tier_config;
 
 typedef struct kvx_tier_stats {
@@ -73,6 +88,8 @@ typedef struct kvx_tier_stats {
     int64_t reloads;     /* victims of a step accessed again later in the same step */
     int64_t frames_h2d;  /* frames copied host -> device */
     int64_t frames_d2h;  /* frames copied device -> host */
+    int64_t frames_disk_read;   /* frames read from the spill file */
+    int64_t frames_disk_write;  /* frames written to the spill file */
 } kvx_tier_stats;
 
 /* Allocate the store (device arena of capacity + spare frames, pinned host
@@ -88,8 +105,14 @@ KVX_API void kvx_tier_destroy(kvx_tier *t);
 KVX_API int kvx_tier_device_arena(kvx_tier *t, void **base, int64_t *slots);
 KVX_API int kvx_tier_host_arena(kvx_tier *t, void **base, int64_t *slots);
 
-/* Where frame f is now: *tier = 0 device / 1 host, *slot its slot there. */
+/* Where frame f is now: *tier = 0 device / 1 host / 2 disk, *slot its slot
+ * there (disk: the frame id, its file offset / frame_bytes). */
 KVX_API int kvx_tier_location(kvx_tier *t, int64_t frame, int32_t *tier, int64_t *slot);
+/* Copy frame f's bytes from / to host memory `buf` wherever the frame is
+ * (synchronous; waits for the store's copies first).  For filling a store
+ * and for checking it. */
+KVX_API int kvx_tier_write_frame(kvx_tier *t, int64_t frame, const void *buf);
+KVX_API int kvx_tier_read_frame(kvx_tier *t, int64_t frame, void *buf);
 
 /* One step: accesses frames[0..n) in order.  For access i, dev_slot[i]
  * receives the device slot the frame occupies for this step's reads;

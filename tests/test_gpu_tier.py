@@ -71,3 +71,46 @@ def test_tier_moves_bytes_exactly_and_decode_sees_them(kvx, oracle):
     tot = t.totals()
     assert tot["frames_h2d"] > 0 and tot["frames_d2h"] > 0
     t.close()
+
+
+def test_tier_with_disk_keeps_bytes_through_three_tiers(kvx, oracle, tmp_path):
+    """RAM tier smaller than the non-resident frames: frames go GPU -> RAM ->
+    disk and back; every frame keeps its bytes, decode over each step's
+    frames matches the oracle, decisions equal KVManager's LRU."""
+    from kvx.tier import Tier
+    U, C, S, H, steps, per = 6000, 1500, 600, 2000, 10, 500
+    data = kvgen.normal(51, (U, 2, 1, 16, 128)).astype(np.float16)
+    raw = data.reshape(U, -1).view(np.uint8)
+    t = Tier(FB, U, C, S, device=0, host_frames=H, spill_path=tmp_path / "spill.bin")
+    assert t.location(C + H) == ("disk", C + H)
+    for f in range(U):
+        t.write_frame(f, raw[f])
+    ranks = kvgen.zipf_pages(52, steps * per, U, 1.1)
+    stream = kvgen.permutation(53, U)[ranks].astype(np.int32).reshape(steps, per)
+    q = kvgen.normal(54, (steps, 2, 3, 128))
+    lens = torch.full((2,), 250 * 16, dtype=torch.int32, device="cuda")
+    outs, evs = [], []
+    for s in range(steps):
+        slots, ev, hit, st = t.step(stream[s])
+        evs.append(ev)
+        t.wait_resident()
+        outs.append(kvx.decode(t.paged(1), torch.from_numpy(slots.reshape(2, 250)).cuda(), lens,
+                               torch.from_numpy(q[s]).cuda()))
+        t.mark_read()
+    t.sync()
+    torch.cuda.synchronize()
+    for s in range(steps):
+        ref = oracle.paged_decode(data, stream[s].reshape(2, 250), np.full(2, 4000, np.int32), q[s])
+        got = outs[s].cpu().numpy()
+        assert (np.abs(got - ref) - (ATOL + RTOL * np.abs(ref))).max() <= 0, s
+    tiers = {"device": 0, "host": 0, "disk": 0}
+    for f in range(U):
+        tiers[t.location(f)[0]] += 1
+        assert np.array_equal(t.read_frame(f), raw[f]), f
+    assert tiers["device"] == C and tiers["host"] <= H and tiers["disk"] > 0
+    ids = np.concatenate([np.arange(C, dtype=np.int32), stream.ravel()])
+    want_ev, _ = oracle.lru_replay(ids, np.zeros(ids.size, np.uint8), C)
+    assert np.array_equal(np.concatenate(evs), want_ev[C:])
+    tot = t.totals()
+    assert tot["frames_disk_read"] > 0 and tot["frames_disk_write"] > 0
+    t.close()

@@ -105,3 +105,28 @@ def test_errors_leave_the_store_unchanged():
     assert st["misses"] == 3 and ev.tolist() == [0, 1, 2]
     with pytest.raises(KvxError):
         Tier(60, 100, 20, 3, device=-1)  # frame bytes not a multiple of 16
+
+
+def test_disk_tier_policy_and_placement(oracle):
+    """With a RAM tier smaller than the non-resident frames, the rest live on
+    disk; device decisions stay KVManager's LRU, RAM never holds more than its
+    size at a step boundary, and RAM evicts in arrival order."""
+    universe, capacity, spare, host = 4000, 900, 200, 800
+    t = Tier(4096, universe, capacity, spare, device=-1, host_frames=host, spill_path="unused")
+    assert t.location(capacity) == ("host", 0) and t.location(capacity + host) == ("disk", capacity + host)
+    stream = zipf_stream(29, 20, 250, universe)
+    evs = []
+    for s in range(stream.shape[0]):
+        slots, ev, hit, st = t.step(stream[s])
+        evs.append(ev)
+        tiers = [t.location(f)[0] for f in range(universe)]
+        assert tiers.count("device") == capacity and tiers.count("host") <= host
+        for f in set(stream[s].tolist()):
+            assert t.location(f)[0] == "device"
+    ids = np.concatenate([np.arange(capacity, dtype=np.int32), stream.ravel()])
+    want_ev, _ = oracle.lru_replay(ids, np.zeros(ids.size, np.uint8), capacity)
+    assert np.array_equal(np.concatenate(evs), want_ev[capacity:])
+    tot = t.totals()
+    assert tot["frames_disk_read"] > 0 and tot["frames_disk_write"] > 0
+    with pytest.raises(KvxError):
+        Tier(4096, universe, capacity, spare, device=-1, host_frames=3 * spare - 1, spill_path="x")
