@@ -34,21 +34,25 @@
 //
 // Disk tier (host_frames > 0): RAM is a FIFO of arrivals (ram_prev/next).
 // A write-back that finds RAM full first spills the oldest RAM frame to
-// the spill file (pwrite, after waiting for the copy that wrote its slot if
-// it was one of the last two steps'), which frees its slot at once.  A
-// miss on a disk frame is read (pread) into a host slot during planning,
-// after the previous step's loads -- which may still read slots freed at
-// its end -- have finished, and is then loaded like a RAM frame.
+// the spill file (after waiting for the copy that wrote its slot if it was
+// one of the last two steps'), which frees its slot at once.  A miss on a
+// disk frame is read into a host slot (after waiting for a load of the last
+// two steps that read the slot, if any) and then loaded like a RAM frame.
+// The step's file writes and then reads run on 8 host threads before its
+// copies are issued.
 #include "kvx_tier.h"
 
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <unistd.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <thread>
 #include <vector>
 
 extern "C" int kvx_migrate_frames(void *dev_base, int32_t dev_capacity, void *host_base,
@@ -111,7 +115,12 @@ struct kvx_tier {
     std::vector<int32_t> ram_prev, ram_next;  // RAM arrival order (head newest)
     int32_t ram_head = -1, ram_tail = -1;
     std::vector<int64_t> slot_step;           // per host slot: step whose write-back filled it
+    std::vector<int64_t> slot_load_step;      // per host slot: step whose load read it last
     bool h2d_prev_synced = false;             // this step waited for the previous step's loads
+    struct DiskIo {
+        int32_t slot, frame;
+    };
+    std::vector<DiskIo> spills, reads;        // this step's file writes, then reads
 
     // device side
     uint8_t *dev_base = nullptr, *host_base = nullptr;
@@ -185,18 +194,44 @@ int spill_oldest(kvx_tier *t, kvx_tier_stats &st) {
     const int32_t f = t->ram_tail;
     if (f < 0) return KVX_ENOSPC;
     const int32_t hs = t->hslot[f];
-    int rc = wait_slot_written(t, hs);
+    const int rc = wait_slot_written(t, hs);
     if (rc != KVX_OK) return rc;
-    if (!t->bookkeeping &&
-        !file_io(t->fd, t->host_base + (size_t)hs * t->cfg.frame_bytes, t->cfg.frame_bytes,
-                 (off_t)f * (off_t)t->cfg.frame_bytes, true))
-        return KVX_ECUDA;
+    t->spills.push_back({hs, f});  // written before any later use of the slot (run_disk_io)
     ram_unlink(t, f);
     t->hslot[f] = -1;
     t->slot_step[hs] = -1;
     t->host_free.push_front(hs);
     ++st.frames_disk_write;
     return KVX_OK;
+}
+
+// The step's file traffic, 8 host threads per phase: every spill write, then
+// every read (a read may land in a slot a spill of this step vacated).
+int run_disk_io(kvx_tier *t) {
+    if (t->bookkeeping) {
+        t->spills.clear();
+        t->reads.clear();
+        return KVX_OK;
+    }
+    std::atomic<bool> ok{true};
+    auto phase = [&](const std::vector<kvx_tier::DiskIo> &ios, bool write) {
+        if (ios.empty()) return;
+        const size_t nt = std::min<size_t>(8, (ios.size() + 7) / 8);
+        std::vector<std::thread> th;
+        for (size_t w = 0; w < nt; ++w)
+            th.emplace_back([&, w] {
+                for (size_t i = w; i < ios.size(); i += nt)
+                    if (!file_io(t->fd, t->host_base + (size_t)ios[i].slot * t->cfg.frame_bytes, t->cfg.frame_bytes,
+                                 (off_t)ios[i].frame * (off_t)t->cfg.frame_bytes, write))
+                        ok = false;
+            });
+        for (auto &x : th) x.join();
+    };
+    phase(t->spills, true);
+    phase(t->reads, false);
+    t->spills.clear();
+    t->reads.clear();
+    return ok ? KVX_OK : KVX_ECUDA;
 }
 
 // A free host slot, spilling the oldest RAM frame when there is none.
@@ -351,6 +386,7 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
         t->last_step.assign(U, -1);
         t->reclaimed.assign(t->dev_slots, -1);
         t->slot_step.assign(t->host_slots, -1);
+        t->slot_load_step.assign(t->host_slots, -1);
         if (t->disk) {
             t->ram_prev.assign(U, -1);
             t->ram_next.assign(U, -1);
@@ -507,23 +543,23 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
                     } else {  // on disk: read it into a host slot, then load as from RAM
                         int32_t hs = -1;
                         int rc = take_host_slot(t, st, hs);
-                        if (rc == KVX_OK && !t->bookkeeping && !t->h2d_prev_synced) {
-                            // slots freed at the previous step's end may still be read by its loads
-                            if (t->ev_used[(s - 1) & 1] && cudaEventSynchronize(t->ev_h2d[(s - 1) & 1]) != cudaSuccess)
-                                rc = KVX_ECUDA;
-                            t->h2d_prev_synced = true;
+                        const int64_t w = t->slot_load_step[hs];
+                        if (rc == KVX_OK && !t->bookkeeping && w >= 0 && w >= s - 2 &&
+                            !(w == s - 1 && t->h2d_prev_synced)) {
+                            // a load of one of the last two steps may still read this slot
+                            // (older loads finished: issue() waited for step s-3's copies)
+                            if (cudaEventSynchronize(t->ev_h2d[w & 1]) != cudaSuccess) rc = KVX_ECUDA;
+                            if (w == s - 1) t->h2d_prev_synced = true;
                         }
-                        if (rc == KVX_OK && !t->bookkeeping &&
-                            !file_io(t->fd, t->host_base + (size_t)hs * t->cfg.frame_bytes, t->cfg.frame_bytes,
-                                     (off_t)f * (off_t)t->cfg.frame_bytes, false))
-                            rc = KVX_ECUDA;
                         if (rc != KVX_OK) return rc;
+                        t->reads.push_back({hs, f});  // read before this step's loads are issued
                         t->hslot[f] = hs;
                         ++st.frames_disk_read;
                     }
                     t->slot_step[t->hslot[f]] = -1;
                 }
                 const int32_t ds = t->dev_free.pop();
+                if (t->disk) t->slot_load_step[t->hslot[f]] = s;
                 t->h2d_dev.push_back(ds);
                 t->h2d_host.push_back(t->hslot[f]);
                 t->freed_host.push_back(t->hslot[f]);
@@ -541,8 +577,8 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
         if (!c.cancelled) ++st.frames_d2h;
     }
     st.frames_h2d = (int64_t)t->h2d_dev.size();
-    int rc = KVX_OK;
-    if (!t->bookkeeping) rc = issue(t, (int)(s & 1));
+    int rc = t->disk ? run_disk_io(t) : KVX_OK;
+    if (rc == KVX_OK && !t->bookkeeping) rc = issue(t, (int)(s & 1));
     // slots freed by this step serve the next one
     for (int32_t d : t->freed_dev)
         if (t->reclaimed[d] != s) t->dev_free.push(d);

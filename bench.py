@@ -54,6 +54,12 @@ def parse():
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
     ap.add_argument("--pages", type=int, default=1 << 20,
                     help="config 3: pages compressed (1,048,576 defines the configuration; fewer for profiling)")
+    ap.add_argument("--tier-context", type=int, default=65536,
+                    help="config 4: tokens per sequence (65,536 defines the configuration)")
+    ap.add_argument("--tier-device-gb", type=float, default=40.0, help="config 4: device pool cap")
+    ap.add_argument("--tier-ram-gb", type=float, default=0.0,
+                    help="config 4: RAM tier size (0: every non-resident frame in pinned RAM; "
+                         "else the rest go to a spill file, the disk tier)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     return ap.parse_args()
@@ -621,11 +627,14 @@ def run_config4(args):
     import torch
     import kvx
     from kvx.tier import Tier
-    L, B, P, ACC = 28, 16, 65536 // PT, 256
+    L, B, P = 28, 16, args.tier_context // PT
+    ACC = P // 16  # pages read per (layer, sequence) per step: 256 at 65,536 tokens
     FB = 2 * HKV * PT * DIM * 2
     U = L * B * P
-    C = int(40e9) // FB
-    S = 49152
+    C = int(args.tier_device_gb * 1e9) // FB
+    S = max(4096, ((L * B * ACC) * 3 // 7) // 4096 * 4096)  # 49152 at full size
+    H = int(args.tier_ram_gb * 1e9) // FB if args.tier_ram_gb > 0 else 0
+    spill_dir = tempfile.mkdtemp(prefix="kvx_spill_", dir=os.environ.get("KVX_SPILL_DIR")) if H else None
     steps = args.steps
     warm = max(args.warmup, 16)
     link = pinned_peaks()
@@ -640,7 +649,8 @@ def run_config4(args):
 
     t0 = time.perf_counter()
     tier = Tier(FB, U, C, S, device=0, load_ctas=int(os.environ.get("KVX_TIER_LOAD_CTAS", "0")),
-                store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")))
+                store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")), host_frames=H,
+                spill_path=None if not H else os.path.join(spill_dir, "frames.bin"))
     alloc_s = time.perf_counter() - t0
     dev = tier.device_tensor()
     host = tier.host_array()
@@ -656,6 +666,16 @@ def run_config4(args):
         n = min(chunk, ht.numel() - o)
         ht[o:o + n].copy_(src[:n])
     torch.cuda.synchronize()
+    if H:  # disk frames (ids C + H ..): the same GiB, written once at their offsets
+        blob = src.cpu().numpy().tobytes()
+        with open(os.path.join(spill_dir, "frames.bin"), "r+b") as f:
+            f.seek((C + H) * FB)
+            left = (U - C - H) * FB
+            while left:
+                n = min(len(blob), left)
+                f.write(blob[:n])
+                left -= n
+        del blob
     del src
     # warm-up: the policy and the copies only, in chunks that fit the spare slots
     for k in range(warm):
@@ -708,9 +728,10 @@ def run_config4(args):
     peak, peak_kind = peaks()
     cpu = cpu_tier_baseline() if not args.no_cpu_baseline else None
     res = {
-        "config": 4, "workload": "tiered eviction: Llama-3.2-3B KV (28L, 8kv x128, fp16), B16, ctx 65536 = "
-                                 "1,835,008 frames x 64 KiB; device pool 40 GB (610,351 frames); per step each "
-                                 "(layer, seq) reads 256 pages drawn Zipf(1.1); KVManager LRU",
+        "config": 4, "workload": f"tiered eviction: Llama-3.2-3B KV (28L, 8kv x128, fp16), B16, ctx {args.tier_context} = "
+                                 f"{U:,} frames x 64 KiB; device pool {args.tier_device_gb:g} GB ({C:,} frames); per step "
+                                 f"each (layer, seq) reads {ACC} pages drawn Zipf(1.1); KVManager LRU"
+                                 + (f"; RAM tier {args.tier_ram_gb:g} GB, the rest on disk" if H else ""),
         "steps": steps, "warmup_steps": warm, "ms_per_step": round(ms / steps, 3),
         "hit_rate": round(mv["hits"] / max(1, mv["accesses"]), 4),
         "frames_per_step": {"h2d": round(mv["frames_h2d"] / steps, 1), "d2h": round(mv["frames_d2h"] / steps, 1),
@@ -725,11 +746,20 @@ def run_config4(args):
                    "GBps_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9, 1),
                    "frac_of_hbm_peak_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9 / peak, 3)},
         "host_plan_ms_per_step": round(plan_s / steps * 1e3, 3),
-        "host_arena_GB": round((U - C + S) * FB / 1e9, 1), "device_arena_GB": round((C + S) * FB / 1e9, 1),
+        "disk_tier": None if not H else {
+            "ram_tier_GB": round(H * FB / 1e9, 1), "spill_file_GB": round(U * FB / 1e9, 1),
+            "frames_per_step": {"read": round(mv["frames_disk_read"] / steps, 1),
+                                "written": round(mv["frames_disk_write"] / steps, 1)},
+            "GBps": {"read": round(mv["frames_disk_read"] * FB / (ms / 1e3) / 1e9, 2),
+                     "write": round(mv["frames_disk_write"] * FB / (ms / 1e3) / 1e9, 2)}},
+        "host_arena_GB": round(((H if H else U - C) + S) * FB / 1e9, 1), "device_arena_GB": round((C + S) * FB / 1e9, 1),
         "alloc_s": round(alloc_s, 1), "clocks": clk, "peak": peak, "peak_kind": peak_kind,
         "cpu_baseline": cpu}
     print(json.dumps(res), flush=True)
     tier.close()
+    if spill_dir:
+        import shutil
+        shutil.rmtree(spill_dir, ignore_errors=True)
 
 
 def run_config5(args):
