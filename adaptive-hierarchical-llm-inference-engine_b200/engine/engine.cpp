@@ -89,7 +89,9 @@ int Engine::set_comm(int rank, int world, const void *id128) {
     if (n.comm_init_rank(&c, world, id, rank) != ncclSuccess) return KVX_ECUDA;
     const size_t gbytes = (size_t)cfg_.layers * world * cfg_.max_batch * cfg_.q_heads * 128 * 2;
     if (cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&d_gather_, gbytes) != cudaSuccess) {
+        cudaMalloc(&d_gather_, gbytes) != cudaSuccess ||
+        cudaMalloc(&d_status_, (2 + 2 * world) * sizeof(int32_t)) != cudaSuccess ||
+        cudaHostAlloc(&h_status_, (2 + 2 * world) * sizeof(int32_t), cudaHostAllocDefault) != cudaSuccess) {
         n.comm_destroy(c);
         return KVX_ECUDA;
     }
@@ -212,6 +214,10 @@ void Engine::release_all() {
     ev_gath_.clear();
     if (d_gather_) cudaFree(d_gather_);
     d_gather_ = nullptr;
+    if (d_status_) cudaFree(d_status_);
+    d_status_ = nullptr;
+    if (h_status_) cudaFreeHost(h_status_);
+    h_status_ = nullptr;
     if (comm_stream_) cudaStreamDestroy(comm_stream_);
     comm_stream_ = nullptr;
     for (size_t l = 0; l < layers_.size(); ++l) {
@@ -638,9 +644,15 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     const int L = cfg_.layers, B = batch_, hq = cfg_.q_heads, hkv = cfg_.kv_heads;
     const size_t qrow = (size_t)B * hq * 128, krow = (size_t)B * hkv * 128;  // elements per layer
     const size_t qstride = (size_t)cfg_.max_batch * hq * 128, kstride = (size_t)cfg_.max_batch * hkv * 128;
+    // With a communicator every rank takes the same collective steps in the
+    // same order whatever happens locally: a rank whose step fails launches
+    // nothing more but still joins every group's all-gathers and the status
+    // exchange at the end, so its peers finish the step and return
+    // KVX_EPEER instead of waiting in NCCL.
+    int rc = KVX_OK;
     memcpy(h_pos_, lens_.data(), B * sizeof(int32_t));
     if (cudaMemcpyAsync(d_pos_, h_pos_, B * sizeof(int32_t), cudaMemcpyHostToDevice, compute_) != cudaSuccess)
-        return KVX_ECUDA;
+        rc = KVX_ECUDA;
     // Layers run in groups: one input copy event and one output event per
     // group, so within a group the decode launches follow each other with
     // nothing in between and each may start while the previous drains
@@ -648,21 +660,18 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     // groups' kernels.
     const int G = L < kLayerGroup ? L : kLayerGroup;
     const int ngroups = (L + G - 1) / G;
-    for (int gi = 0; gi < ngroups; ++gi) {
-        for (int l = gi * G; l < std::min(L, (gi + 1) * G); ++l)
+    for (int gi = 0; gi < ngroups && rc == KVX_OK; ++gi) {
+        for (int l = gi * G; l < std::min(L, (gi + 1) * G) && rc == KVX_OK; ++l)
             if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
                 cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
                 cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_))
-                return KVX_ECUDA;
-        if (cudaEventRecord(ev_in_[gi], copy_)) return KVX_ECUDA;
+                rc = KVX_ECUDA;
+        if (rc == KVX_OK && cudaEventRecord(ev_in_[gi], copy_)) rc = KVX_ECUDA;
     }
-    int rc = KVX_OK;
-    for (int gi = 0; gi < ngroups && rc == KVX_OK; ++gi) {
+    if (rc && !comm_) return rc;
+    for (int gi = 0; gi < ngroups && (rc == KVX_OK || comm_); ++gi) {
         const int l0 = gi * G, l1 = std::min(L, l0 + G);
-        if (cudaStreamWaitEvent(compute_, ev_in_[gi], 0) != cudaSuccess) {
-            rc = KVX_ECUDA;
-            break;
-        }
+        if (rc == KVX_OK && cudaStreamWaitEvent(compute_, ev_in_[gi], 0) != cudaSuccess) rc = KVX_ECUDA;
         for (int l = l0; l < l1 && rc == KVX_OK; ++l) {
             if (layers_[l].tier != kGpu) {  // tiered: bring the layer back (may evict the LRU layer)
                 const int r = to_gpu_locked(l);
@@ -679,48 +688,60 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                                    KVX_F16, 0.f, d_ws_, ws_bytes_, d_err_, compute_);
             current_layer_ = l;
         }
-        if (rc) break;
-        if (cudaEventRecord(ev_out_[gi], compute_)) {
-            rc = KVX_ECUDA;
-        } else if (comm_) {  // all-gather the group's rows over NCCL, then read them back
-            if (cudaStreamWaitEvent(comm_stream_, ev_out_[gi], 0)) {
-                rc = KVX_ECUDA;
-                break;
-            }
+        // recorded after a failure too, so the gathers below never read rows
+        // that a kernel still writes
+        if (cudaEventRecord(ev_out_[gi], compute_) && rc == KVX_OK) rc = KVX_ECUDA;
+        if (comm_) {  // all-gather the group's rows over NCCL, then read them back
+            if (cudaStreamWaitEvent(comm_stream_, ev_out_[gi], 0) && rc == KVX_OK) rc = KVX_ECUDA;
             for (int l = l0; l < l1; ++l)
                 if (nccl().all_gather(d_out_ + l * qstride, d_gather_ + (size_t)l * world_ * qrow, qrow, ncclFloat16,
-                                      static_cast<ncclComm_t>(comm_), comm_stream_) != ncclSuccess)
+                                      static_cast<ncclComm_t>(comm_), comm_stream_) != ncclSuccess &&
+                    rc == KVX_OK)
                     rc = KVX_ECUDA;
-            if (rc || cudaEventRecord(ev_gath_[gi], comm_stream_)) {
+            if (rc == KVX_OK && cudaEventRecord(ev_gath_[gi], comm_stream_)) rc = KVX_ECUDA;
+            if (rc == KVX_OK && out &&
+                (cudaStreamWaitEvent(copy_, ev_gath_[gi], 0) ||
+                 cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
+                                 (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_)))
                 rc = KVX_ECUDA;
-                break;
-            }
-            if (out) {
-                if (cudaStreamWaitEvent(copy_, ev_gath_[gi], 0) ||
-                    cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
-                                    (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
-                    rc = KVX_ECUDA;
-            }
-        } else if (out) {
-            if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) {
-                rc = KVX_ECUDA;
-                break;
-            }
-            for (int l = l0; l < l1; ++l)
+        } else if (rc == KVX_OK && out) {
+            if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) rc = KVX_ECUDA;
+            for (int l = l0; l < l1 && rc == KVX_OK; ++l)
                 if (cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
                     rc = KVX_ECUDA;
         }
+    }
+    // Status exchange: {host status, device error flag} of every rank,
+    // gathered after the last group's kernels, read with the same sync.
+    bool peer_failed = false;
+    if (comm_) {
+        h_status_[0] = rc;
+        if ((cudaStreamWaitEvent(comm_stream_, ev_out_[ngroups - 1], 0) ||
+             cudaMemcpyAsync(d_status_, h_status_, sizeof(int32_t), cudaMemcpyHostToDevice, comm_stream_) ||
+             cudaMemcpyAsync(d_status_ + 1, d_err_, sizeof(int32_t), cudaMemcpyDeviceToDevice, comm_stream_)) &&
+            rc == KVX_OK)
+            rc = KVX_ECUDA;
+        if (nccl().all_gather(d_status_, d_status_ + 2, 2, ncclInt32, static_cast<ncclComm_t>(comm_),
+                              comm_stream_) != ncclSuccess &&
+            rc == KVX_OK)
+            rc = KVX_ECUDA;
+        if (cudaMemcpyAsync(h_status_ + 2, d_status_ + 2, 2 * world_ * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                            comm_stream_) &&
+            rc == KVX_OK)
+            rc = KVX_ECUDA;
     }
     int32_t err = 0;
     if (cudaStreamSynchronize(compute_) != cudaSuccess || cudaStreamSynchronize(copy_) != cudaSuccess ||
         (comm_stream_ && cudaStreamSynchronize(comm_stream_) != cudaSuccess) ||
         cudaMemcpy(&err, d_err_, sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
         return KVX_ECUDA;
+    if (comm_)
+        for (int r = 0; r < world_; ++r)
+            if (r != rank_ && (h_status_[2 + 2 * r] != KVX_OK || h_status_[3 + 2 * r] != 0)) peer_failed = true;
+    if (err) cudaMemset(d_err_, 0, sizeof(int32_t));
     if (rc) return rc;
-    if (err) {
-        cudaMemset(d_err_, 0, sizeof(int32_t));
-        return (err & 1) ? KVX_ETIMEOUT : KVX_EINVAL;
-    }
+    if (err) return (err & 1) ? KVX_ETIMEOUT : KVX_EINVAL;
+    if (peer_failed) return KVX_EPEER;
     for (int s = 0; s < B; ++s) ++lens_[s];
     return KVX_OK;
 }

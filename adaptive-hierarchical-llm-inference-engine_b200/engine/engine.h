@@ -111,6 +111,8 @@ private:
     std::vector<int32_t> free_pages_;   // physical pages not owned by a sequence
     int32_t *d_table_ = nullptr, *d_pos_ = nullptr, *d_err_ = nullptr;
     int32_t *h_pos_ = nullptr;          // pinned positions for the step
+    int32_t *d_status_ = nullptr;       // {host status, error flag} then every rank's pair
+    int32_t *h_status_ = nullptr;       // pinned mirror of d_status_
     void *d_ws_ = nullptr;
     size_t ws_bytes_ = 0;
     uint16_t *d_q_ = nullptr, *d_k_ = nullptr, *d_v_ = nullptr, *d_out_ = nullptr;

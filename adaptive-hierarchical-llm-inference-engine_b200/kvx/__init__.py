@@ -21,7 +21,8 @@ HEAD_DIM, PAGE_TOKENS = 128, 16
 STATUS = {0: "ok", -1: "invalid argument", -2: "object pinned", -3: "CUDA error",
           -4: "unsupported geometry or dtype", -5: "bounded device wait expired",
           -6: "workspace or pool too small", -7: "no sm_100 device",
-          -8: "request exceeds the static scratch of kvx_decode_noalloc"}
+          -8: "request exceeds the static scratch of kvx_decode_noalloc",
+          -9: "another rank's part of the multi-GPU step failed"}
 
 
 class KvxError(RuntimeError):

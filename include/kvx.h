@@ -41,7 +41,8 @@ enum kvx_status {
     KVX_ETIMEOUT = -5,     /* a bounded device wait expired (see error_flag) */
     KVX_ENOSPC = -6,       /* workspace / pool too small */
     KVX_ENODEV = -7,       /* no sm_100 device current */
-    KVX_ETOOBIG = -8       /* request exceeds kvx_decode_noalloc's static scratch */
+    KVX_ETOOBIG = -8,      /* request exceeds kvx_decode_noalloc's static scratch */
+    KVX_EPEER = -9         /* another rank's part of a multi-GPU engine step failed */
 };
 
 enum kvx_dtype { KVX_F32 = 0, KVX_F16 = 1, KVX_I8 = 2 };

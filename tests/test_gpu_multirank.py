@@ -12,7 +12,12 @@ cache/kv_cache.cpp and runtime/cpu_ops.cpp), within the attention tolerance:
   NCCL communicator (adaptive_engine_set_comm), rank 0 reading the gathered
   rows back.
 
-The process group has a short timeout, so a rank that fails makes the other
+A third case makes rank 1's step fail on the host (the layer it must bring
+to the device cannot evict a victim: both device slabs hold pinned layers):
+rank 1 returns KVX_EBUSY and rank 0, whose own work succeeded, returns
+KVX_EPEER; neither waits in NCCL, because the failing rank still takes every
+collective step.  No GPU fault is involved, NVLS is off, and the process
+group has a short timeout, so a rank that fails otherwise makes the other
 one end with an error rather than wait.
 """
 import os
@@ -29,7 +34,7 @@ RTOL, ATOL = 1e-3, 1e-2
 HKV, HQ, DIM, PT = 8, 24, 128, 16
 
 
-def _worker(rank, world, port, tmpdir, result_q):
+def _worker(rank, world, port, tmpdir, result_q, mode):
     sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests"),
                     os.path.join(ROOT, "adaptive-hierarchical-llm-inference-engine_b200")]
     import datetime
@@ -44,7 +49,7 @@ def _worker(rank, world, port, tmpdir, result_q):
     from oracle import Oracle
 
     torch.cuda.set_device(rank)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
@@ -54,6 +59,11 @@ def _worker(rank, world, port, tmpdir, result_q):
         o = Oracle()
         (k0, k1), (q0, q1) = head_ranges(HKV, HQ, world, rank)
 
+        if mode == "fail":
+            report.update(_failing_step(rank, world, tmpdir, dist, E))
+            dist.barrier()
+            result_q.put((rank, report, None))
+            return
         # kvx.decode per shard + torch NCCL all-gather
         lens = np.array([1, 17, 300, 1000, 64], np.int32)
         bt, num_pages = kvgen.paged_layout(lens, PT, 0, seed=21)
@@ -114,9 +124,41 @@ def _worker(rank, world, port, tmpdir, result_q):
             pass
 
 
-def test_two_gpu_sharded_decode_matches_oracle(tmp_path):
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two CUDA devices")
+def _failing_step(rank, world, tmpdir, dist, E):
+    """Rank 1 keeps 2 of its 3 layers on the device, both pinned, so bringing
+    layer 2 back fails (KVX_EBUSY) in the middle of the step."""
+    layers, pages, batch = 3, 16, 2
+    api = E.api()
+    api.stop()
+    E.configure(layers=layers, pages_per_layer=pages, max_batch=batch,
+                gpu_layer_slots=layers if rank == 0 else 2, kv_heads=HKV // world,
+                q_heads=HQ // world, device=rank, offload_dir=os.path.join(tmpdir, f"f{rank}"))
+    api.start()
+    try:
+        uid = [E.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        E.set_comm(rank, world, uid[0])
+        E.set_sequences(np.array([20, 7], np.int32), reserve_tokens=2, seed=1)
+        if rank == 1:
+            assert api.keepLayer(0) >= 1 and api.keepLayer(1) >= 1
+        hq, hkv = HQ // world, HKV // world
+        q = np.zeros((layers, batch, hq, DIM), np.float16)
+        kv = np.zeros((layers, batch, hkv, DIM), np.float16)
+        out = np.zeros((layers, world, batch, hq, DIM), np.float16) if rank == 0 else None
+        status = 0
+        try:
+            E.decode_step(q, kv, kv, out)
+        except E.KvxError as e:
+            status = e.status
+        if rank == 1:
+            for l in (0, 1):
+                E.lib.adaptive_engine_test_release_layer(l)
+        return {"status": status}
+    finally:
+        api.stop()
+
+
+def _spawn(tmp_path, mode):
     import multiprocessing as mp
     import socket
     ctx = mp.get_context("spawn")
@@ -126,14 +168,34 @@ def test_two_gpu_sharded_decode_matches_oracle(tmp_path):
     port = s.getsockname()[1]
     s.close()
     world = 2
-    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), q, mode))
              for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=600) for _ in procs)
     for p in procs:
         p.join(timeout=120)
+    return res
+
+
+def _need_two_gpus():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+
+
+def test_two_gpu_sharded_decode_matches_oracle(tmp_path):
+    _need_two_gpus()
+    res = _spawn(tmp_path, "parity")
     for rank, report, err in res:
         assert err is None, (rank, err)
         assert report["kvx_excess"] <= 0, (rank, report)
     assert res[0][1]["engine_excess"] <= 0, res[0][1]
+
+
+def test_failing_rank_does_not_hang_its_peer(tmp_path):
+    _need_two_gpus()
+    res = _spawn(tmp_path, "fail")
+    for rank, report, err in res:
+        assert err is None, (rank, err)
+    assert res[1][1]["status"] == -2, res   # KVX_EBUSY: victims pinned
+    assert res[0][1]["status"] == -9, res   # KVX_EPEER
