@@ -27,6 +27,10 @@
 #include <cuda_fp16.h>
 #include <math_constants.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "kvx_common.cuh"
 
 namespace kvx {
@@ -204,11 +208,12 @@ compress_2048_kernel(const T *__restrict__ src, uint8_t *__restrict__ codes,
         const float rcp = __frcp_rn(scale);
         uint8_t *out = codes + b * kCodeBytes;
         if (isfinite(scale) && isfinite(rcp)) {  // warp-uniform; mn, mx finite too
-            float worst = 0.f;
+            uint32_t bad = 0;  // vectors holding a near-tie or a NaN
 #pragma unroll
             for (int j = 0; j < kVecs; ++j) {
                 const T *e = reinterpret_cast<const T *>(&w[j]);
                 uint32_t word[kPerVec / 4];
+                float worst = 0.f;
 #pragma unroll
                 for (int k4 = 0; k4 < kPerVec / 4; ++k4) {
                     uint32_t u[4];
@@ -226,6 +231,7 @@ compress_2048_kernel(const T *__restrict__ src, uint8_t *__restrict__ codes,
                         word[k4] = __byte_perm(__byte_perm(u[0], u[1], 0x0040),
                                                __byte_perm(u[2], u[3], 0x0040), 0x5410) ^ 0x80808080u;
                 }
+                if (!(worst <= kTieLimit)) bad |= 1u << j;
                 if constexpr (kNf4) {
                     if constexpr (kPerVec == 8)
                         __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0] | (word[1] << 16));
@@ -238,9 +244,13 @@ compress_2048_kernel(const T *__restrict__ src, uint8_t *__restrict__ codes,
                         __stcs(reinterpret_cast<uint32_t *>(out) + j * 32 + lane, word[0]);
                 }
             }
-            if (!(worst <= kTieLimit)) {  // rare: near-ties or NaN in this lane
+            // rare: redo the flagged vectors' codes with the exact division
+            // (x re-read from global, no indexed register array)
 #pragma unroll 1
-                for (int j = 0; j < kVecs; ++j) {
+            while (bad) {
+                const int j = __ffs(bad) - 1;
+                bad &= bad - 1;
+                {
                     const int base = (j * 32 + lane) * kPerVec;
                     if constexpr (kNf4) {  // redo the lane's bytes exactly (two codes each)
 #pragma unroll 1
@@ -311,8 +321,33 @@ __device__ __forceinline__ float dequant_one(int8_t c, float zp, float scale) {
     return x86_nan(__fadd_rn(zp, m), zp, m);
 }
 
-// Warp per 2048-element block: stats read once, 16 codes per lane-load,
-// NaN rebuild only for blocks whose scale or zero point is not finite.
+// fp32 value of byte k of w, exactly: the bytes {b, 0, 0, 0x4B} are the
+// float 2^23 + b, and subtracting 2^23 is exact (no conversion instruction).
+__device__ __forceinline__ float byte_value(uint32_t w, int k) {
+    return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)k)), 8388608.0f);
+}
+
+template <typename T> __device__ __forceinline__ void store16(T *dst, const float (&v)[16]);
+template <> __device__ __forceinline__ void store16<float>(float *dst, const float (&v)[16]) {
+    float4 *o = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) __stcs(o + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+}
+template <> __device__ __forceinline__ void store16<__half>(__half *dst, const float (&v)[16]) {
+    uint32_t u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        u[k] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    __stcs(reinterpret_cast<uint4 *>(dst), make_uint4(u[0], u[1], u[2], u[3]));
+    __stcs(reinterpret_cast<uint4 *>(dst) + 1, make_uint4(u[4], u[5], u[6], u[7]));
+}
+
+// Warp per 2048-element block: stats read once, 16 codes per lane-load.
+// Finite scale and zero point (every block the quantiser writes from finite
+// data): zp + u * scale with u taken from the code byte exactly; otherwise
+// the x86 NaN rebuild, element by element, in a loop kept out of line.
 template <typename T>
 __global__ void __launch_bounds__(256)
 decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict__ stats,
@@ -323,33 +358,28 @@ decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict
          b += warps) {
         const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
         const float scale = st.z, zp = st.w;
-        const bool finite = isfinite(scale) && isfinite(zp);
         const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 2048);
+        uint4 w[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {  // 4 x 16 codes per lane
-            const uint4 w = __ldcs(src + j * 32 + lane);
-            const int8_t *c = reinterpret_cast<const int8_t *>(&w);
-            float v[16];
+        for (int j = 0; j < 4; ++j) w[j] = __ldcs(src + j * 32 + lane);
+        if (isfinite(scale) && isfinite(zp)) {  // warp-uniform
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float q = (float)((int32_t)c[k] + 128);
-                v[k] = finite ? __fadd_rn(zp, __fmul_rn(q, scale)) : dequant_one(c[k], zp, scale);
+            for (int j = 0; j < 4; ++j) {  // 4 x 16 codes per lane
+                const uint32_t u[4] = {w[j].x ^ 0x80808080u, w[j].y ^ 0x80808080u, w[j].z ^ 0x80808080u,
+                                       w[j].w ^ 0x80808080u};  // c + 128
+                float v[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = __fadd_rn(zp, __fmul_rn(byte_value(u[k >> 2], k & 3), scale));
+                store16<T>(dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 16, v);
             }
-            const size_t e0 = (size_t)b * 2048 + (size_t)(j * 32 + lane) * 16;
-            if constexpr (sizeof(T) == 4) {
-                float4 *o = reinterpret_cast<float4 *>(dst + e0);
+        } else {  // rare: codes re-read from global, no indexed register array
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j) {
+                const int8_t *c = codes + b * 2048 + (size_t)(j * 32 + lane) * 16;
+                float v[16];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) __stcs(o + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
-            } else {
-                uint4 o[2];
-                uint32_t *u = reinterpret_cast<uint32_t *>(o);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-                    u[k] = *reinterpret_cast<uint32_t *>(&h);
-                }
-                __stcs(reinterpret_cast<uint4 *>(dst + e0), o[0]);
-                __stcs(reinterpret_cast<uint4 *>(dst + e0) + 1, o[1]);
+                for (int k = 0; k < 16; ++k) v[k] = dequant_one(c[k], zp, scale);
+                store16<T>(dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 16, v);
             }
         }
     }
@@ -473,34 +503,40 @@ decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__res
          b += warps) {
         const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
         const float scale = st.z, zp = st.w;
-        const bool finite = isfinite(scale) && isfinite(zp);
         const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 1024);
+        uint4 w[2];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const uint4 w = __ldcs(src + j * 32 + lane);
-            const uint8_t *c = reinterpret_cast<const uint8_t *>(&w);
-            float v[32];
+        for (int j = 0; j < 2; ++j) w[j] = __ldcs(src + j * 32 + lane);
+        if (isfinite(scale) && isfinite(zp)) {  // warp-uniform
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const uint32_t hi = c[k] >> 4, lo = c[k] & 0xFu;
-                v[2 * k] = finite ? __fadd_rn(zp, __fmul_rn((float)hi, scale)) : dequant_level(hi, zp, scale);
-                v[2 * k + 1] = finite ? __fadd_rn(zp, __fmul_rn((float)lo, scale)) : dequant_level(lo, zp, scale);
-            }
-            const size_t e0 = (size_t)b * 2048 + (size_t)(j * 32 + lane) * 32;
-            if constexpr (sizeof(T) == 4) {
-                float4 *o = reinterpret_cast<float4 *>(dst + e0);
+            for (int j = 0; j < 2; ++j) {  // 16 bytes = 32 codes per lane, high nibble first
+                const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+                T *out = dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 32;
 #pragma unroll
-                for (int k = 0; k < 8; ++k) __stcs(o + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
-            } else {
-                uint4 o[4];
-                uint32_t *u = reinterpret_cast<uint32_t *>(o);
+                for (int h = 0; h < 2; ++h) {  // bytes 8h .. 8h + 7 -> elements 16h .. 16h + 15
+                    float v[16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-                    u[k] = *reinterpret_cast<uint32_t *>(&h);
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t word = ww[2 * h + (k >> 2)];
+                        const uint32_t hi = (word >> 4) & 0x0F0F0F0Fu, lo = word & 0x0F0F0F0Fu;
+                        v[2 * k] = __fadd_rn(zp, __fmul_rn(byte_value(hi, k & 3), scale));
+                        v[2 * k + 1] = __fadd_rn(zp, __fmul_rn(byte_value(lo, k & 3), scale));
+                    }
+                    store16<T>(out + 16 * h, v);
                 }
+            }
+        } else {  // rare: codes re-read from global, no indexed register array
+#pragma unroll 1
+            for (int i = 0; i < 4; ++i) {  // 8 bytes -> 16 values per step
+                const int j = i >> 1, h = i & 1;
+                const uint8_t *c = codes + b * 1024 + (size_t)(j * 32 + lane) * 16 + 8 * h;
+                float v[16];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) __stcs(reinterpret_cast<uint4 *>(dst + e0) + k, o[k]);
+                for (int k = 0; k < 8; ++k) {
+                    v[2 * k] = dequant_level(c[k] >> 4, zp, scale);
+                    v[2 * k + 1] = dequant_level(c[k] & 0xFu, zp, scale);
+                }
+                store16<T>(dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 32 + 16 * h, v);
             }
         }
     }
@@ -565,10 +601,37 @@ __global__ void fp16_wrap_decode_kernel(const uint16_t *__restrict__ src, float 
         dst[i] = fp16_wrap_dec(src[i]);
 }
 
-unsigned grid_for(size_t work, int per_block) {
+// CTAs that fit on the current GPU at once for `kernel` at 256 threads (its
+// occupancy times the SM count), cached per kernel and device.
+int resident_ctas(const void *kernel) {
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({kernel, dev});
+    if (it != cache.end()) return it->second;
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+    cudaGetLastError();  // leave no error from the queries for launch_status()
+    return cache[{kernel, dev}] = sms * per_sm;
+}
+
+// Grid for a grid-stride kernel: `work` items, `per_block` per CTA, capped
+// at `waves` times the CTAs that fit at once (0: no cap, one CTA per
+// `per_block` items).  The SMs' shares of HBM bandwidth differ, so CTAs
+// handed out dynamically balance better than equal static shares: the
+// decoders run uncapped, the encoders (heavier per CTA) at 16 waves, the
+// element-wise converters at 8.
+template <typename K> unsigned grid_for(K kernel, size_t work, int per_block, int waves) {
     size_t b = (work + per_block - 1) / per_block;
-    const size_t cap = 148ull * 16;  // persistent-ish: 16 CTAs per SM, grid-stride beyond
+    const size_t cap = waves > 0 ? (size_t)waves * resident_ctas(reinterpret_cast<const void *>(kernel)) : b;
     if (b > cap) b = cap;
+    if (b > 0x7FFFFFFFu) b = 0x7FFFFFFFu;
     return (unsigned)(b ? b : 1);
 }
 
@@ -587,19 +650,18 @@ extern "C" KVX_API int kvx_compress_int8(const void *src, int32_t src_dtype, int
     if (!aligned16(stats)) return KVX_EINVAL;
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const unsigned grid = grid_for(num_blocks, 8);
     const bool fast = block_elems == 2048 && aligned16(src) && aligned16(codes);
     uint8_t *c = reinterpret_cast<uint8_t *>(codes);
     if (src_dtype == KVX_F16) {
         if (fast)
-            compress_2048_kernel<__half, 255><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks);
+            compress_2048_kernel<__half, 255><<<grid_for(compress_2048_kernel<__half, 255>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks);
         else
-            compress_generic_kernel<__half, 255><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks, block_elems);
+            compress_generic_kernel<__half, 255><<<grid_for(compress_generic_kernel<__half, 255>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const __half *>(src), c, stats, num_blocks, block_elems);
     } else {
         if (fast)
-            compress_2048_kernel<float, 255><<<grid, 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks);
+            compress_2048_kernel<float, 255><<<grid_for(compress_2048_kernel<float, 255>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks);
         else
-            compress_generic_kernel<float, 255><<<grid, 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks, block_elems);
+            compress_generic_kernel<float, 255><<<grid_for(compress_generic_kernel<float, 255>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const float *>(src), c, stats, num_blocks, block_elems);
     }
     return launch_status();
 }
@@ -611,18 +673,17 @@ extern "C" KVX_API int kvx_compress_nf4(const void *src, int32_t src_dtype, uint
     if (!aligned16(stats)) return KVX_EINVAL;
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const unsigned grid = grid_for(num_blocks, 8);
     const bool fast = block_elems == 2048 && aligned16(src) && aligned16(codes);
     if (src_dtype == KVX_F16) {
         if (fast)
-            compress_2048_kernel<__half, 15><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks);
+            compress_2048_kernel<__half, 15><<<grid_for(compress_2048_kernel<__half, 15>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks);
         else
-            compress_generic_kernel<__half, 15><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks, block_elems);
+            compress_generic_kernel<__half, 15><<<grid_for(compress_generic_kernel<__half, 15>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const __half *>(src), codes, stats, num_blocks, block_elems);
     } else {
         if (fast)
-            compress_2048_kernel<float, 15><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks);
+            compress_2048_kernel<float, 15><<<grid_for(compress_2048_kernel<float, 15>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks);
         else
-            compress_generic_kernel<float, 15><<<grid, 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks, block_elems);
+            compress_generic_kernel<float, 15><<<grid_for(compress_generic_kernel<float, 15>, num_blocks, 8, 16), 256, 0, st>>>(static_cast<const float *>(src), codes, stats, num_blocks, block_elems);
     }
     return launch_status();
 }
@@ -636,18 +697,16 @@ extern "C" KVX_API int kvx_decompress_nf4(const uint8_t *codes, const float *sta
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (block_elems == 2048 && aligned16(codes) && aligned16(dst) && aligned16(stats)) {
-        const unsigned grid = grid_for(num_blocks, 8);
         if (dst_dtype == KVX_F32)
-            decompress_nf4_2048_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+            decompress_nf4_2048_kernel<float><<<grid_for(decompress_nf4_2048_kernel<float>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
         else
-            decompress_nf4_2048_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+            decompress_nf4_2048_kernel<__half><<<grid_for(decompress_nf4_2048_kernel<__half>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
         return launch_status();
     }
-    const unsigned grid = grid_for(num_blocks * (size_t)block_elems, 256);
     if (dst_dtype == KVX_F32)
-        decompress_nf4_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+        decompress_nf4_kernel<float><<<grid_for(decompress_nf4_kernel<float>, num_blocks * (size_t)block_elems, 256, 8), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
     else
-        decompress_nf4_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+        decompress_nf4_kernel<__half><<<grid_for(decompress_nf4_kernel<__half>, num_blocks * (size_t)block_elems, 256, 8), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
     return launch_status();
 }
 
@@ -656,7 +715,7 @@ extern "C" KVX_API int kvx_fp16_wrap_encode(const float *src, uint16_t *dst, siz
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
     const bool vec = aligned16(src) && !(reinterpret_cast<uintptr_t>(dst) & 7);
-    fp16_wrap_encode_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    fp16_wrap_encode_kernel<<<grid_for(fp16_wrap_encode_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         src, dst, n, vec);
     return launch_status();
 }
@@ -666,7 +725,7 @@ extern "C" KVX_API int kvx_fp16_wrap_decode(const uint16_t *src, float *dst, siz
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
     const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
-    fp16_wrap_decode_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    fp16_wrap_decode_kernel<<<grid_for(fp16_wrap_decode_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         src, dst, n, vec);
     return launch_status();
 }
@@ -682,26 +741,23 @@ extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *sta
     if (num_blocks == 0) return KVX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (block_elems % 4 || !aligned16(stats) || (reinterpret_cast<uintptr_t>(codes) & 3) || !aligned16(dst)) {
-        const unsigned grid = grid_for(num_blocks * (size_t)block_elems, 256);
         if (dst_dtype == KVX_F32)
-            decompress_scalar_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+            decompress_scalar_kernel<float><<<grid_for(decompress_scalar_kernel<float>, num_blocks * (size_t)block_elems, 256, 8), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
         else
-            decompress_scalar_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+            decompress_scalar_kernel<__half><<<grid_for(decompress_scalar_kernel<__half>, num_blocks * (size_t)block_elems, 256, 8), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
         return launch_status();
     }
     if (block_elems == 2048 && aligned16(codes)) {
-        const unsigned grid = grid_for(num_blocks, 8);
         if (dst_dtype == KVX_F32)
-            decompress_2048_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+            decompress_2048_kernel<float><<<grid_for(decompress_2048_kernel<float>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
         else
-            decompress_2048_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+            decompress_2048_kernel<__half><<<grid_for(decompress_2048_kernel<__half>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
         return launch_status();
     }
-    const unsigned grid = grid_for(num_blocks * (size_t)(block_elems / 4), 256);
     if (dst_dtype == KVX_F32)
-        decompress_kernel<float><<<grid, 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
+        decompress_kernel<float><<<grid_for(decompress_kernel<float>, num_blocks * (size_t)(block_elems / 4), 256, 8), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks, block_elems);
     else
-        decompress_kernel<__half><<<grid, 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
+        decompress_kernel<__half><<<grid_for(decompress_kernel<__half>, num_blocks * (size_t)(block_elems / 4), 256, 8), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks, block_elems);
     return launch_status();
 }
 
@@ -710,7 +766,7 @@ extern "C" KVX_API int kvx_f32_to_f16_trunc(const float *src, uint16_t *dst, siz
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
     const bool vec = aligned16(src) && !(reinterpret_cast<uintptr_t>(dst) & 7);
-    encode_trunc_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    encode_trunc_kernel<<<grid_for(encode_trunc_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         src, dst, n, vec);
     return launch_status();
 }
@@ -720,7 +776,7 @@ extern "C" KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, siz
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
     const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
-    decode_trunc_kernel<<<grid_for(vec ? n / 4 + 1 : n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    decode_trunc_kernel<<<grid_for(decode_trunc_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         src, dst, n, vec);
     return launch_status();
 }
