@@ -513,20 +513,40 @@ int sm_count() {
     return n;
 }
 
-int choose_chunk(int batch, int hkv, int nhg, int max_pages, int page_scale = 1) {
+int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
     if (const char *e = getenv("KVX_DECODE_CHUNK")) {
         int c = atoi(e);
         if (c >= kMinChunk) return c;
     }
-    // aim at ~4 waves of 3 resident CTAs per SM, counting half of max_pages
-    // as the mean sequence length; page_scale > 1 for pages that carry less
-    // data each (int8: a warp's fixed per-page cost is the same for half
-    // the bytes, so a CTA takes more of them)
-    const long long work = (long long)batch * hkv * nhg * max_pages * page_scale;
+    // SIMT kernel: aim at ~4 waves of 3 resident CTAs per SM, counting half
+    // of max_pages as the mean sequence length
+    const long long work = (long long)batch * hkv * nhg * max_pages;
     const long long target = (long long)sm_count() * 3 * 4;
     long long c = (work / 2 + target - 1) / target;
     if (c < kMinChunk) c = kMinChunk;
     if (c > 64) c = 64;
+    return (int)((c + kWarps - 1) / kWarps * kWarps);
+}
+
+// Tensor-core decode: the largest chunk that still leaves about two waves
+// of resident CTAs (3 per SM), counting half of max_pages as the mean
+// sequence length, then evened out over the longest sequence's splits.
+// Every CTA pays a fixed cost (q fragments, pipeline fill, the merge of its
+// warps, the split combine), so fewer and longer CTAs win while all SMs stay
+// busy; programmatic dependent launch lets the next launch fill the SMs
+// that one launch's last wave leaves idle.  page_scale > 1 for pages that
+// carry less data each (int8: half the bytes, the same per-page cost).
+int choose_chunk_tc(int batch, int hkv, int max_pages, int page_scale) {
+    if (const char *e = getenv("KVX_DECODE_CHUNK")) {
+        int c = atoi(e);
+        if (c >= kMinChunk) return c;
+    }
+    const long long work = (long long)batch * hkv * max_pages * page_scale;
+    const long long target = (long long)sm_count() * 3 * 2;
+    long long c = (work / 2 + target - 1) / target;
+    c = std::min<long long>(std::max<long long>(c, kMinChunk), 256);
+    const long long nsplit = (max_pages + c - 1) / c;
+    c = (max_pages + nsplit - 1) / nsplit;
     return (int)((c + kWarps - 1) / kWarps * kWarps);
 }
 
@@ -632,7 +652,8 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
                     !(force_simt && force_simt[0] == '1');
     p.nhg = tc ? 1 : (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
     const int G = (p.group + p.nhg - 1) / p.nhg;
-    p.chunk = std::max(choose_chunk(batch, p.hkv, p.nhg, max_pages, tc && kv->dtype == KVX_I8 ? 3 : 1),
+    p.chunk = std::max(tc ? choose_chunk_tc(batch, p.hkv, max_pages, kv->dtype == KVX_I8 ? 3 : 1)
+                          : choose_chunk(batch, p.hkv, p.nhg, max_pages),
                        min_chunk_r);
     p.max_splits = (max_pages + p.chunk - 1) / p.chunk;
     const size_t splits_cap = min_chunk_r > 0 ? (size_t)(max_pages + min_chunk_r - 1) / min_chunk_r

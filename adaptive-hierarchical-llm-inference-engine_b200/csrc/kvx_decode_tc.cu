@@ -64,8 +64,7 @@ template <bool kI8> struct TcCfg {
     static constexpr int kStage = 4 * kBox;
     static constexpr int kPages = kI8 ? 2 : 1;      // pages per stage
     static constexpr int kRing = kStages * kStage;  // >= 16 KiB: parks O at the end
-    static constexpr int kStatFloats = 16;          // int8: 4 stats rows per stage
-    static constexpr int kStatBytes = kI8 ? kTcWarps * kStages * kStatFloats * 4 : 0;
+    static constexpr int kStatBytes = 0;  // int8 stats travel in registers (lanes 0-3), one stage ahead
     static constexpr int kSmem = 1024 /* alignment slack */ + kTcWarps * kRing + kTcWarps * kStages * 8 +
                                  kStatBytes + 2 * kTcWarps * 16 * 4 + 16 + kQloBytes + kTcWarps * kBtCache * 4;
 };
@@ -290,14 +289,18 @@ __device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t x, uint32_t sel) { retur
 // larger group the lo parts take a second mma into the same accumulators
 // (q lo fragments from shared memory, `qlo`).
 template <bool kBig>
-__device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool va, bool vb,
+__device__ __forceinline__ void tc_pair_i8(uint32_t base, float2 st, bool va, bool vb,
                                            const uint32_t (&qa)[8][4], uint32_t qlo, float qs0, float qs1,
                                            float (&o)[16][4], float &m0, float &m1, float &l0, float &l1,
                                            float &z0, float &z1, int tok_a, int tok_b, int T,
                                            float scale_log2, int lane, float (&psum)[2][2]) {
     const int g = lane >> 2, r = lane & 3;
-    const float4 ska = *reinterpret_cast<const float4 *>(st), sva = *reinterpret_cast<const float4 *>(st + 4);
-    const float4 skb = *reinterpret_cast<const float4 *>(st + 8), svb = *reinterpret_cast<const float4 *>(st + 12);
+    // {scale, zero_point} of K a, V a, K b, V b sit in lanes 0-3
+    float2 ska, sva, skb, svb;
+    ska.x = __shfl_sync(0xffffffffu, st.x, 0), ska.y = __shfl_sync(0xffffffffu, st.y, 0);
+    sva.x = __shfl_sync(0xffffffffu, st.x, 1), sva.y = __shfl_sync(0xffffffffu, st.y, 1);
+    skb.x = __shfl_sync(0xffffffffu, st.x, 2), skb.y = __shfl_sync(0xffffffffu, st.y, 2);
+    svb.x = __shfl_sync(0xffffffffu, st.x, 3), svb.y = __shfl_sync(0xffffffffu, st.y, 3);
     // ---- S = scale * Q (1024 + u) + (zp - 1024 scale) sum(q); tile t = 2 page + j
     float sc[4][4];
 #pragma unroll
@@ -332,8 +335,8 @@ __device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool 
         }
     }
     // ---- online softmax (log2 domain) over the 32 tokens
-    const float ks[2] = {ska.z * scale_log2, skb.z * scale_log2};
-    const float ko[2] = {fmaf(-1024.f, ska.z, ska.w) * scale_log2, fmaf(-1024.f, skb.z, skb.w) * scale_log2};
+    const float ks[2] = {ska.x * scale_log2, skb.x * scale_log2};
+    const float ko[2] = {fmaf(-1024.f, ska.x, ska.y) * scale_log2, fmaf(-1024.f, skb.x, skb.y) * scale_log2};
     const bool have[2] = {va, vb};
     const int tok[2] = {tok_a, tok_b};
     float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
@@ -383,7 +386,7 @@ __device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool 
     // lo equals P' to 2^-22 relative, so the zero-point scalar may use the
     // unrounded sum: (zp - 1024 scale_v) * sum(p), off by < 2.5e-4 * scale_v
     // of the output.
-    const float svs[2] = {sva.z, svb.z};
+    const float svs[2] = {sva.x, svb.x};
     auto split = [](float x, float y, uint32_t &hi, uint32_t &lo) {
         hi = pack_h2(x, y);
         const float2 h = h2_to_f2(hi);
@@ -403,7 +406,7 @@ __device__ __forceinline__ void tc_pair_i8(uint32_t base, const float *st, bool 
             pa[pg][3] = pl[pg][2];
         }
     }
-    const float voa = va ? fmaf(-1024.f, sva.z, sva.w) : 0.f, vob = vb ? fmaf(-1024.f, svb.z, svb.w) : 0.f;
+    const float voa = va ? fmaf(-1024.f, sva.x, sva.y) : 0.f, vob = vb ? fmaf(-1024.f, svb.x, svb.y) : 0.f;
     z0 = fmaf(z0, a0, fmaf(voa, ps0[0], vob * ps0[1]));
     if constexpr (kBig) z1 = fmaf(z1, a1, fmaf(voa, ps1[0], vob * ps1[1]));
     if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
@@ -494,8 +497,6 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
 
     uint8_t *wbuf = smem + warp * kTcStages * kTcStage;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcWarps * kTcStages * kTcStage) + warp * kTcStages;
-    float *wstat = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8) +
-                   warp * kTcStages * Cfg::kStatFloats;  // int8: per stage K a | V a | K b | V b stats
     float *s_m = reinterpret_cast<float *>(smem + kTcWarps * kTcStages * kTcStage + kTcWarps * kTcStages * 8 +
                                            Cfg::kStatBytes);
     float *s_l = s_m + kTcWarps * 16;
@@ -544,21 +545,16 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
             const bool va = page_ok(pa_), vb = 2 * i + 1 < n_pg && page_ok(pb_);
             if ((!va || (2 * i + 1 < n_pg && !vb)) && p.error_flag) atomicOr(p.error_flag, 2);
             const uint32_t dst = wbase + st * kTcStage, b = smem_addr(bar);
-            float *sd = wstat + st * Cfg::kStatFloats;
-            mbar_arrive_expect_tx(bar, (va ? 2 * kBox + 32 : 0) + (vb ? 2 * kBox + 32 : 0));
+            mbar_arrive_expect_tx(bar, (va ? 2 * kBox : 0) + (vb ? 2 * kBox : 0));
             if (va) {
                 const int kb = (pa_ * 2) * p.hkv + kvh;  // (page, K, head) block; V block = kb + hkv
                 tma_load_2d(dst, &tm, 0, kb * kPageTokens, b);
                 tma_load_2d(dst + kBox, &tm, 0, (kb + p.hkv) * kPageTokens, b);
-                bulk_g2s(sd, p.stats + (size_t)kb * 4, 16, bar);
-                bulk_g2s(sd + 4, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
             }
             if (vb) {
                 const int kb = (pb_ * 2) * p.hkv + kvh;
                 tma_load_2d(dst + 2 * kBox, &tm, 0, kb * kPageTokens, b);
                 tma_load_2d(dst + 3 * kBox, &tm, 0, (kb + p.hkv) * kPageTokens, b);
-                bulk_g2s(sd + 8, p.stats + (size_t)kb * 4, 16, bar);
-                bulk_g2s(sd + 12, p.stats + (size_t)(kb + p.hkv) * 4, 16, bar);
             }
             return;
         }
@@ -651,11 +647,26 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
     };
 
+    // int8: {scale, zero_point} of stage i's K a, V a, K b, V b blocks, one
+    // per lane 0-3, loaded while stage i - 1 is processed
+    auto stats_of = [&](int i) -> float2 {
+        if (!kI8 || lane >= 4) return make_float2(0.f, 0.f);
+        const int pg = 2 * i + (lane >> 1);
+        if (pg >= n_pg) return make_float2(0.f, 0.f);
+        const int ph = phys_of(pg);
+        if (!page_ok(ph)) return make_float2(0.f, 0.f);
+        const int blk = (ph * 2 + (lane & 1)) * p.hkv + kvh;
+        return __ldg(reinterpret_cast<const float2 *>(p.stats + (size_t)blk * 4) + 1);
+    };
+    float2 st_next = stats_of(0);
+
     bool ok = true;
     int done = 0;
     for (int i = 0; i < n_my; ++i) {
         const int st = i % kTcStages;
         const uint32_t par = (i / kTcStages) & 1;
+        const float2 st_cur = st_next;
+        if (kI8 && i + 1 < n_my) st_next = stats_of(i + 1);
         if (!mbar_wait_bounded(&bars[st], par, p.error_flag)) {
             ok = false;
             break;
@@ -668,7 +679,7 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
             const bool vb = 2 * i + 1 < n_pg && page_ok(phys_of(2 * i + 1));
             if (va || vb) {
                 float psum[2][2];
-                tc_pair_i8<kBig>(sbase, wstat + st * Cfg::kStatFloats, va, vb, qa, qlo, qs0, qs1, o, m0, m1, l0,
+                tc_pair_i8<kBig>(sbase, st_cur, va, vb, qa, qlo, qs0, qs1, o, m0, m1, l0,
                                  l1, z0, z1, lpa * kPageTokens + 2 * (lane & 3),
                                  (lpa + kTcWarps) * kPageTokens + 2 * (lane & 3), T, p.scale_log2, lane, psum);
                 if constexpr (kAttn) {
