@@ -492,3 +492,84 @@ float kvo_predict_next_access(const uint64_t *times, size_t count) {
     for (size_t i = 1; i < count; ++i) total += times[i] - times[i - 1];
     return (float)(times[count - 1] + total / (count - 1));
 }
+
+/* ---- KVCacheGPU page policy (native-engine/cpp/KVCacheGPU.cpp) ----------- */
+
+int kvo_kvcache_gpu_replay(const int64_t *ops, size_t n, uint64_t total, uint64_t page_size,
+                           int64_t *result, uint64_t *used_out) {
+    (void)page_size; /* maxPages is computed but never consulted (KVCacheGPU.cpp:9) */
+    int64_t maxid = -1;
+    for (size_t i = 0; i < n; ++i) {
+        if ((ops[3 * i] == 0) && ops[3 * i + 1] < 0) return -1;
+        if ((ops[3 * i] == 0 || ops[3 * i] == 1 || ops[3 * i] == 4) && ops[3 * i + 1] > maxid)
+            maxid = ops[3 * i + 1];
+    }
+    size_t cap = (size_t)(maxid + 1);
+    uint8_t *live = (uint8_t *)calloc(cap ? cap : 1, 1);
+    uint64_t *size = (uint64_t *)calloc(cap ? cap : 1, sizeof(uint64_t));
+    uint64_t *last = (uint64_t *)calloc(cap ? cap : 1, sizeof(uint64_t));
+    size_t len = 0; /* pages.size() */
+    uint64_t used = 0;
+    for (size_t i = 0; i < n; ++i) {
+        const int64_t op = ops[3 * i], a = ops[3 * i + 1], b = ops[3 * i + 2];
+        int64_t r = 0;
+        /* evictLRUPage (:136-152) over findLRUPage (:54-66): the first page
+         * with the strictly smallest lastUsedToken */
+#define KVO_EVICT(res)                                                        \
+        do {                                                                  \
+            int64_t lru = -1;                                                 \
+            uint64_t mn = UINT64_MAX;                                         \
+            for (size_t k = 0; k < len; ++k)                                  \
+                if (live[k] && last[k] < mn) {                                \
+                    mn = last[k];                                             \
+                    lru = (int64_t)k;                                         \
+                }                                                             \
+            if (lru < 0) {                                                    \
+                (res) = 0;                                                    \
+            } else {                                                          \
+                used -= size[lru];                                            \
+                live[lru] = 0;                                                \
+                (res) = 1;                                                    \
+            }                                                                 \
+        } while (0)
+        if (op == 0) {
+            /* allocateGPUPage (:21-40): over the budget -> null; a 0-byte
+             * cudaMalloc succeeds with a null pointer (nothing counted) */
+            uint64_t want = (uint64_t)b;
+            int got = used + want <= total && want > 0;
+            if (got) used += want;
+            if (!got) { /* transferToGPU (:68-79): evict once and retry */
+                int ev;
+                KVO_EVICT(ev);
+                if (ev) {
+                    got = used + want <= total && want > 0;
+                    if (got) used += want;
+                }
+            }
+            if (got) { /* :89-105; a replaced entry's bytes stay counted */
+                if ((size_t)a >= len) len = (size_t)a + 1;
+                live[a] = 1;
+                size[a] = want;
+                last[a] = 0;
+            }
+            r = got;
+        } else if (op == 1) {
+            if (a >= 0 && (size_t)a < len && live[a]) last[a] = (uint64_t)b;
+        } else if (op == 2) {
+            KVO_EVICT(r);
+        } else if (op == 3) {
+            memset(live, 0, cap ? cap : 1);
+            len = 0;
+            used = 0;
+        } else if (op == 4) {
+            r = (a >= 0 && (size_t)a < len && live[a]) ? (int64_t)last[a] : -1;
+        }
+#undef KVO_EVICT
+        result[i] = r;
+        used_out[i] = used;
+    }
+    free(live);
+    free(size);
+    free(last);
+    return 0;
+}

@@ -128,6 +128,15 @@ float kvo_predict_next_access(const uint64_t *times, size_t count);
 int kvo_lru_replay(const int32_t *ids, const uint8_t *ops, size_t n, size_t capacity,
                    int32_t *evicted, uint8_t *hit);
 
+/* KVCacheGPU (native-engine/cpp/KVCacheGPU.cpp:21-163): replays ops[n][3]
+ * = (op, a, b) on a cache of total bytes and page_size:
+ *   0 transferToGPU(pageId a, size b) -> 1 / 0    1 markPageUsed(a, token b)
+ *   2 evictLRUPage() -> 1 / 0   3 clear()   4 getPage(a) -> lastUsedToken / -1
+ * result[i] per op, used[i] = getUsedMemory() after it.  0, or -1 for a
+ * negative page id in a transfer (the reference indexes out of bounds). */
+int kvo_kvcache_gpu_replay(const int64_t *ops, size_t n, uint64_t total, uint64_t page_size,
+                           int64_t *result, uint64_t *used);
+
 /* Scheduler::getPrefetchDepth (scheduler/scheduler.cpp:23-37) after the
  * latencies lat[0..n) were observed (window of 16, scheduler.cpp:15-21). */
 int kvo_prefetch_depth(const double *lat, size_t n, size_t cache_size,

@@ -103,6 +103,8 @@ class Oracle:
         L.kvo_lru_replay.restype = C.c_int
         L.kvo_prefetch_depth.argtypes = [_f64p, _sz, _sz, _sz, C.c_int]
         L.kvo_prefetch_depth.restype = C.c_int
+        L.kvo_kvcache_gpu_replay.argtypes = [C.c_void_p, _sz, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]
+        L.kvo_kvcache_gpu_replay.restype = C.c_int
 
     # compression/kv_compress.cpp
     def f32_to_f16_trunc(self, x):
@@ -274,6 +276,18 @@ class Oracle:
         if rc != 0:
             raise ValueError("lru_replay: negative id")
         return ev, hit
+
+    def kvcache_gpu_replay(self, ops, total, page_size):
+        """KVCacheGPU (native-engine/cpp/KVCacheGPU.cpp) over ops [n][3] =
+        (op, a, b); returns (result[n], used[n]) (see kvx_oracle.h)."""
+        ops = _c(ops, np.int64).reshape(-1, 3)
+        res = np.empty(len(ops), np.int64)
+        used = np.empty(len(ops), np.uint64)
+        rc = self.L.kvo_kvcache_gpu_replay(ops.ctypes.data, len(ops), int(total), int(page_size),
+                                          res.ctypes.data, used.ctypes.data)
+        if rc != 0:
+            raise ValueError("kvcache_gpu_replay: negative page id in a transfer")
+        return res, used
 
     def prefetch_depth(self, latencies, size, capacity, max_depth=4):
         lat = _c(latencies, np.float64)
@@ -462,6 +476,18 @@ class Reference:
         if s < 0:
             raise RuntimeError("kvref_time_tier failed")
         return s, misses.value
+
+    def kvcache_gpu_replay(self, ops, total, page_size):
+        """KVCacheGPU (native-engine/cpp/KVCacheGPU.cpp) over ops [n][3] =
+        (op, a, b); returns (result[n], used[n]) (see kvx_oracle.h)."""
+        ops = _c(ops, np.int64).reshape(-1, 3)
+        res = np.empty(len(ops), np.int64)
+        used = np.empty(len(ops), np.uint64)
+        rc = self.L.kvo_kvcache_gpu_replay(ops.ctypes.data, len(ops), int(total), int(page_size),
+                                          res.ctypes.data, used.ctypes.data)
+        if rc != 0:
+            raise ValueError("kvcache_gpu_replay: negative page id in a transfer")
+        return res, used
 
     def prefetch_depth(self, latencies, size, capacity, max_depth=4):
         lat = _c(latencies, np.float64)

@@ -353,6 +353,59 @@ def gen_disk(R: Reference):
                         blob=np.frombuffer(blob, np.uint8), key_back=k2, value_back=v2)
 
 
+def kvcache_gpu_traces():
+    """Op traces for KVCacheGPU: (op, a, b) rows as in oracle/kvx_oracle.h,
+    with the budget and page size of each trace.  Mostly page-size
+    transfers, some half and double size, re-sent page ids, tokens that
+    grow, explicit evictions, lookups and a clear now and then."""
+    rng = np.random.default_rng(2024)
+    traces = []
+    for t in range(8):
+        page = (131072, 4096, 65536, 131072)[t % 4]
+        budget = page * int(rng.integers(3, 14)) + (0 if t % 3 else page // 2)
+        ids = int(rng.integers(6, 40))
+        token = 1
+        ops = []
+        for _ in range(int(rng.integers(150, 400))):
+            u = rng.random()
+            if u < 0.45:
+                size = page * (2 if rng.random() < 0.08 else 1) // (2 if rng.random() < 0.15 else 1)
+                ops.append((0, int(rng.integers(0, ids)), int(size)))
+            elif u < 0.75:
+                token += int(rng.integers(1, 50))
+                ops.append((1, int(rng.integers(-1, ids + 2)), token if rng.random() < 0.9 else 0))
+            elif u < 0.83:
+                ops.append((2, 0, 0))
+            elif u < 0.98:
+                ops.append((4, int(rng.integers(-1, ids + 2)), 0))
+            else:
+                ops.append((3, 0, 0))
+        traces.append((budget, page, np.array(ops, np.int64)))
+    return traces
+
+
+def gen_kvcache_gpu(R: Reference):
+    """KVCacheGPU (native-engine/cpp/KVCacheGPU.cpp) replayed by
+    oracle/_ref/kvcachegpu_ref: the reference's class compiled unmodified
+    against a host-memory stand-in for its four CUDA calls."""
+    import subprocess
+    exe = os.path.join(ROOT, "oracle", "_ref", "kvcachegpu_ref")
+    out = {}
+    for i, (budget, page, ops) in enumerate(kvcache_gpu_traces()):
+        text = f"{budget} {page}\n" + "".join(f"{o} {a} {b}\n" for o, a, b in ops)
+        r = subprocess.run([exe], input=text, capture_output=True, text=True, check=True,
+                           env=dict(os.environ, ADAPTIVE_LOG_LEVEL="0"))
+        rows = np.array([list(map(int, ln.split())) for ln in r.stdout.split("\n") if ln.strip()], np.int64)
+        assert rows.shape == (len(ops), 2)
+        out[f"ops{i}"] = ops
+        out[f"budget{i}"] = np.int64(budget)
+        out[f"page{i}"] = np.int64(page)
+        out[f"result{i}"] = rows[:, 0]
+        out[f"used{i}"] = rows[:, 1].astype(np.uint64)
+    out["n_traces"] = np.int64(len(kvcache_gpu_traces()))
+    np.savez_compressed(os.path.join(HERE, "kvcache_gpu.npz"), **out)
+
+
 def main():
     os.environ.setdefault("ADAPTIVE_LOG_LEVEL", "ERROR")
     if not build_reference():
@@ -360,7 +413,8 @@ def main():
     R = Reference()
     gens = {"kv_compress": gen_kv_compress, "int8": gen_int8, "attention": gen_attention,
             "paged": gen_paged, "int8_decode": gen_int8_decode, "lru": gen_lru, "depth": gen_depth,
-            "disk": gen_disk, "nf4": gen_nf4, "fp16_wrap": gen_fp16_wrap, "evict": gen_evict}
+            "disk": gen_disk, "nf4": gen_nf4, "fp16_wrap": gen_fp16_wrap, "evict": gen_evict,
+            "kvcache_gpu": gen_kvcache_gpu}
     for name in (sys.argv[1:] or gens):  # e.g. `make_golden.py nf4 fp16_wrap` for one fixture
         gens[name](R)
     print("golden fixtures written to", HERE)

@@ -192,3 +192,75 @@ def test_kv_compression_engine_dropin_matches_reference(built, tmp_path, oracle)
             assert np.array_equal(stats.view(np.uint32), want_s.view(np.uint32)), (t, b.size)
         assert np.array_equal(back.view(np.uint32), want_b.view(np.uint32)), (t, b.size)
     assert pos == len(raw)
+
+
+@pytest.mark.gpu
+def test_kvcache_gpu_dropin_matches_reference(built):
+    """include/KVCacheGPU.h on the device slot pool against the reference's
+    KVCacheGPU (golden traces): the same result and byte count after every op,
+    one call per op and with transfers batched; page bytes intact."""
+    g = golden("kvcache_gpu.npz")
+    for i in range(int(g["n_traces"])):
+        ops, res, used = g[f"ops{i}"], g[f"result{i}"], g[f"used{i}"]
+        text = f"{int(g[f'budget{i}'])} {int(g[f'page{i}'])}\n" + "".join(f"{o} {a} {b}\n" for o, a, b in ops)
+        rc, out = run(built, "kv_cache_gpu_io", stdin=text)
+        assert rc == 0, out[-500:]
+        lines = out.split("\n")
+        p1 = lines.index("pass 1")
+        p2 = lines.index("pass 2")
+        one = [tuple(map(int, ln.split())) for ln in lines[p1 + 1:p2]]
+        assert one == [(int(r), int(u)) for r, u in zip(res, used)], i
+        k = 0
+        for ln in lines[p2 + 1:]:
+            if ln.startswith("corrupt"):
+                assert ln == "corrupt 0", ln
+                break
+            a, b = ln.split()
+            if a == "used":  # end of a batch of transfers
+                assert int(b) == int(used[k - 1]), (i, k)
+            elif b == "-":
+                assert ops[k][0] == 0 and int(a) == int(res[k]), (i, k)
+                k += 1
+            else:
+                assert (int(a), int(b)) == (int(res[k]), int(used[k])), (i, k)
+                k += 1
+        assert k == len(ops)
+
+
+@pytest.mark.gpu
+def test_kvcache_gpu_manager_natives():
+    """The KVCacheGPUManager natives' C entry points (include/kvx_gpu_cache.h):
+    handles, byte count, LRU eviction, copy back + release, stale handles."""
+    import ctypes as C
+    import kvx
+    L = kvx.lib
+    L.kvx_gpu_cache_transfer_to_gpu.restype = C.c_int64
+    L.kvx_gpu_cache_transfer_to_gpu.argtypes = [C.c_void_p, C.c_int64, C.c_int32]
+    L.kvx_gpu_cache_transfer_from_gpu.restype = C.c_int32
+    L.kvx_gpu_cache_transfer_from_gpu.argtypes = [C.c_int64, C.c_void_p, C.c_int64]
+    L.kvx_gpu_cache_used_memory.restype = C.c_int64
+    L.kvx_gpu_cache_evict_lru.restype = C.c_int32
+    L.kvx_gpu_cache_mark_page_used.argtypes = [C.c_int32, C.c_int64]
+    L.kvx_gpu_cache_init.argtypes = [C.c_uint64, C.c_uint64]
+    page = 64 * 1024
+    assert L.kvx_gpu_cache_init(3 * page, page) == 0
+    try:
+        data = [np.random.default_rng(s).integers(0, 256, page, dtype=np.uint8) for s in range(4)]
+        h = [L.kvx_gpu_cache_transfer_to_gpu(d.ctypes.data, page, i) for i, d in enumerate(data[:3])]
+        assert all(x > 0 for x in h) and len(set(h)) == 3
+        assert L.kvx_gpu_cache_used_memory() == 3 * page
+        for pid, tok in ((0, 30), (1, 10), (2, 20)):
+            L.kvx_gpu_cache_mark_page_used(pid, tok)
+        h3 = L.kvx_gpu_cache_transfer_to_gpu(data[3].ctypes.data, page, 3)  # evicts page 1 (token 10)
+        assert h3 > 0 and L.kvx_gpu_cache_used_memory() == 3 * page
+        back = np.zeros(page, np.uint8)
+        assert L.kvx_gpu_cache_transfer_from_gpu(h[1], back.ctypes.data, page) == 0  # evicted
+        assert L.kvx_gpu_cache_transfer_from_gpu(h[2], back.ctypes.data, page) == 1
+        assert np.array_equal(back, data[2]) and L.kvx_gpu_cache_used_memory() == 2 * page
+        assert L.kvx_gpu_cache_transfer_from_gpu(h[2], back.ctypes.data, page) == 0  # handle spent
+        assert L.kvx_gpu_cache_evict_lru() == 1  # page 3 (token 0)
+        assert L.kvx_gpu_cache_transfer_from_gpu(h[0], back.ctypes.data, page) == 1
+        assert np.array_equal(back, data[0]) and L.kvx_gpu_cache_used_memory() == 0
+        assert L.kvx_gpu_cache_evict_lru() == 0
+    finally:
+        L.kvx_gpu_cache_shutdown()

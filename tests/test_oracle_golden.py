@@ -213,3 +213,14 @@ def test_eviction_policies_exact(oracle):
                                   g[f"scores{c}_{pol}"].view(np.uint32)), (c, pol)
         got = oracle.evict_select_composite(np.array([0, 1, 2], np.int32), g[f"composite_w{c}"], m)
         assert got == int(g[f"composite{c}"]), c
+
+
+def test_kvcache_gpu_policy_matches_reference(oracle):
+    """KVCacheGPU (native-engine/cpp/KVCacheGPU.cpp): every transfer's
+    success, evictions, lookups and the byte count after each op, replayed
+    on the reference's own class (golden) and on the restatement."""
+    g = golden("kvcache_gpu.npz")
+    for i in range(int(g["n_traces"])):
+        res, used = oracle.kvcache_gpu_replay(g[f"ops{i}"], int(g[f"budget{i}"]), int(g[f"page{i}"]))
+        assert np.array_equal(res, g[f"result{i}"]), i
+        assert np.array_equal(used, g[f"used{i}"]), i
