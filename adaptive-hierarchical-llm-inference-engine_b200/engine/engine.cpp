@@ -660,12 +660,24 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     // groups' kernels.
     const int G = L < kLayerGroup ? L : kLayerGroup;
     const int ngroups = (L + G - 1) / G;
+    // with the batch at max_batch the layers are contiguous on both sides:
+    // one copy per tensor per group instead of one per layer
+    const bool packed = qstride == qrow && kstride == krow;
     for (int gi = 0; gi < ngroups && rc == KVX_OK; ++gi) {
-        for (int l = gi * G; l < std::min(L, (gi + 1) * G) && rc == KVX_OK; ++l)
-            if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
-                cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
-                cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_))
+        const int l0 = gi * G, l1 = std::min(L, l0 + G);
+        if (packed) {
+            const size_t n = (size_t)(l1 - l0);
+            if (cudaMemcpyAsync(d_q_ + l0 * qstride, q + l0 * qrow, n * qrow * 2, cudaMemcpyHostToDevice, copy_) ||
+                cudaMemcpyAsync(d_k_ + l0 * kstride, k + l0 * krow, n * krow * 2, cudaMemcpyHostToDevice, copy_) ||
+                cudaMemcpyAsync(d_v_ + l0 * kstride, v + l0 * krow, n * krow * 2, cudaMemcpyHostToDevice, copy_))
                 rc = KVX_ECUDA;
+        } else {
+            for (int l = l0; l < l1 && rc == KVX_OK; ++l)
+                if (cudaMemcpyAsync(d_q_ + l * qstride, q + l * qrow, qrow * 2, cudaMemcpyHostToDevice, copy_) ||
+                    cudaMemcpyAsync(d_k_ + l * kstride, k + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_) ||
+                    cudaMemcpyAsync(d_v_ + l * kstride, v + l * krow, krow * 2, cudaMemcpyHostToDevice, copy_))
+                    rc = KVX_ECUDA;
+        }
         if (rc == KVX_OK && cudaEventRecord(ev_in_[gi], copy_)) rc = KVX_ECUDA;
     }
     if (rc && !comm_) return rc;
@@ -706,9 +718,15 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                 rc = KVX_ECUDA;
         } else if (rc == KVX_OK && out) {
             if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) rc = KVX_ECUDA;
-            for (int l = l0; l < l1 && rc == KVX_OK; ++l)
-                if (cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
+            if (packed) {
+                if (rc == KVX_OK && cudaMemcpyAsync(out + l0 * qrow, d_out_ + l0 * qstride, (size_t)(l1 - l0) * qrow * 2,
+                                                    cudaMemcpyDeviceToHost, copy_))
                     rc = KVX_ECUDA;
+            } else {
+                for (int l = l0; l < l1 && rc == KVX_OK; ++l)
+                    if (cudaMemcpyAsync(out + l * qrow, d_out_ + l * qstride, qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                        rc = KVX_ECUDA;
+            }
         }
     }
     // Status exchange: {host status, device error flag} of every rank,
