@@ -441,6 +441,29 @@ def test_int8_decode_tensor_core_path_matches_oracle(kvx, oracle, monkeypatch, h
     assert_close(simt, ref)
 
 
+@pytest.mark.parametrize("qscale", [20.0, 200.0])
+def test_int8_decode_query_outlier_channels(kvx, oracle, qscale):
+    """Queries with outlier channels (two dims x20 / x200) over int8 pages
+    with outlier keys and values stay within the attention tolerance: q
+    enters the mma as fp16 hi + lo, each element with its own exponent (q
+    as 16-bit integers per row, one scale for all dims, misses it at x200)."""
+    hkv, hq = 8, 24
+    lens = kvgen.randint(130, 6, 200, 2500)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=131)
+    pool = kvgen.normal(132, (num_pages, 2, hkv, 16, 128))
+    pool[kvgen.uniform(133, pool.size).reshape(pool.shape) < 0.01] *= 20
+    pool = pool.astype(np.float16)
+    codes, stats = kvx.compress_int8(dev(pool))
+    cpool = codes.view(num_pages, 2, hkv, 16, 128)
+    q = kvgen.normal(134, (lens.size, hq, 128))
+    q[:, :, 17] *= qscale
+    q[:, :, 90] *= -qscale
+    out = kvx.decode(cpool, dev(bt), dev(lens.astype(np.int32)), dev(q), stats=stats).cpu().numpy()
+    ref = oracle.paged_decode(codes.cpu().numpy().reshape(cpool.shape), bt, lens.astype(np.int32), q,
+                              stats=stats.cpu().numpy().reshape(num_pages, 2, hkv, 4))
+    assert_close(out, ref)
+
+
 # ------------------------------------------------------- fp16 trunc codec ---
 
 def test_f16_trunc_codec_bitexact(kvx):
