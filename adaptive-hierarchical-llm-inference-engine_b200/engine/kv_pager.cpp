@@ -22,7 +22,11 @@ void KVPager::start() {
 void KVPager::stop() {
     bool expected = true;
     if (running_.compare_exchange_strong(expected, false)) {
+        // pass through the mutex: a worker between its predicate check and
+        // its wait would otherwise miss this notification and never wake
+        { std::lock_guard<std::mutex> lk(mu_); }
         cv_.notify_all();
+        idle_cv_.notify_all();
         if (thread_.joinable()) thread_.join();
     }
 }
