@@ -6,9 +6,10 @@
 //    KVCacheGPU::findLRUPage (native-engine/cpp/KVCacheGPU.cpp:54-66): the
 //    strictly smallest stamp wins, the lowest index on ties, and a stamp of
 //    UINT64_MAX (the reference's initial minToken) is never chosen.
-//    One CTA of 1024 threads reads the stamps with 16-byte loads; each thread
+//    One cluster of 8 CTAs x 1024 threads scans the stamps; each thread
 //    keeps its first minimum in index order, then a (stamp, index)
-//    lexicographic tree reduction.  No workspace, deterministic.
+//    lexicographic reduction over warps, CTAs and -- through distributed
+//    shared memory -- the cluster.  One launch, no workspace, deterministic.
 //  * kvx_evict_select / kvx_evict_select_composite: the other policies of
 //    native-engine/cpp/AdvancedEvictionPolicy.cpp (TokenWeighted :35-64,
 //    AttentionBased :69-105, Predictive :119-152) and the weighted
@@ -18,64 +19,14 @@
 //    those ages are evaluated in double and rounded to float; with wrapped
 //    ages they are 0 / 1 and one shared value in practice.  Highest score
 //    strictly above -1 wins, the lowest index on ties (+0 and -0 tie), NaN
-//    scores never.  Same single-CTA scan and tree reduction as above.
+//    scores never.  Same cluster scan: a score becomes a rank (smaller is
+//    better) so both reductions are one (rank, index) minimum.
+#include <cooperative_groups.h>
+
 #include "kvx_common.cuh"
 
 namespace kvx {
 namespace {
-
-__device__ __forceinline__ void take(uint64_t &best, long long &bi, uint64_t v, long long i) {
-    if (v < best || (v == best && v != UINT64_MAX && i < bi)) {
-        best = v;
-        bi = i;
-    }
-}
-
-__global__ void __launch_bounds__(1024)
-lru_select_kernel(const uint64_t *__restrict__ stamps, size_t n, int32_t *victim) {
-    uint64_t best = UINT64_MAX;
-    long long bi = -1;
-    const size_t pairs = n / 2;
-    for (size_t i = threadIdx.x; i < pairs; i += blockDim.x) {
-        const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2 *>(stamps) + i);
-        take(best, bi, v.x, (long long)(2 * i));
-        take(best, bi, v.y, (long long)(2 * i + 1));
-    }
-    if ((n & 1) && threadIdx.x == 0) take(best, bi, stamps[n - 1], (long long)(n - 1));
-    // warp then block reduction on (stamp, index)
-#pragma unroll
-    for (int off = 16; off; off >>= 1) {
-        const uint64_t ov = __shfl_xor_sync(0xffffffffu, best, off);
-        const long long oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (oi >= 0 && (bi < 0 || ov < best || (ov == best && oi < bi))) {
-            best = ov;
-            bi = oi;
-        }
-    }
-    __shared__ uint64_t sv[32];
-    __shared__ long long si[32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        sv[warp] = best;
-        si[warp] = bi;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        best = lane < nw ? sv[lane] : UINT64_MAX;
-        bi = lane < nw ? si[lane] : -1;
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const uint64_t ov = __shfl_xor_sync(0xffffffffu, best, off);
-            const long long oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (oi >= 0 && (bi < 0 || ov < best || (ov == best && oi < bi))) {
-                best = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) *victim = (int32_t)bi;
-    }
-}
 
 // native-engine/include/AdvancedEvictionPolicy.h:19-27, same layout.
 struct EvictMetrics {
@@ -110,27 +61,25 @@ __device__ __forceinline__ float policy_score(int type, const EvictMetrics &m, f
     }
 }
 
-__device__ __forceinline__ bool better(float s, long long i, float best, long long bi) {
-    return i >= 0 && (bi < 0 || s > best || (s == best && i < bi));
-}
+constexpr int kSelCtas = 8;        // one portable cluster
+constexpr int kSelThreads = 1024;
 
-// One CTA.  lru: selectPageToEvict of LRU (smallest lastAccessToken below
-// UINT64_MAX); otherwise the (weighted) scores of `ps`.
-__global__ void __launch_bounds__(1024)
-policy_select_kernel(const EvictMetrics *__restrict__ pages, size_t n, PolicySet ps, float decay,
-                     const float *__restrict__ predicted, bool lru, int32_t *page_id) {
-    float best = -1.0f;
-    uint64_t bmin = UINT64_MAX;
-    long long bi = -1;
-    for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const EvictMetrics m = pages[i];
-        if (lru) {
-            if (m.last_access_token < bmin) {
-                bmin = m.last_access_token;
-                bi = (long long)i;
-            }
-            continue;
-        }
+// Rank of a candidate, smaller is better; UINT64_MAX never wins.
+struct StampRank {  // LRU over raw stamps: the stamp itself, the index out
+    const uint64_t *stamps;
+    __device__ uint64_t rank(size_t i) const { return __ldg(stamps + i); }
+    __device__ int32_t result(long long i) const { return (int32_t)i; }
+};
+
+struct PolicyRank {  // selectPageToEvict over EvictionMetrics, the page id out
+    const EvictMetrics *pages;
+    PolicySet ps;
+    float decay;
+    const float *predicted;
+    bool lru;
+    __device__ uint64_t rank(size_t i) const {
+        const EvictMetrics &m = pages[i];
+        if (lru) return m.last_access_token;
         const float pred = predicted ? predicted[i] : -1.0f;
         float sc;
         if (ps.n == 1) {
@@ -140,57 +89,92 @@ policy_select_kernel(const EvictMetrics *__restrict__ pages, size_t n, PolicySet
             for (int p = 0; p < ps.n; ++p)
                 sc = __fadd_rn(sc, __fmul_rn(ps.weight[p], policy_score(ps.type[p], m, decay, pred)));
         }
-        if (sc > best) {
-            best = sc;
+        if (!(sc > -1.0f)) return UINT64_MAX;  // best starts at -1, strict '>': NaN never
+        // larger score -> smaller rank; +0 and -0 tie
+        const uint32_t u = __float_as_uint(sc == 0.0f ? 0.0f : sc);
+        const uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        return (uint64_t)(0xFFFFFFFFu - key);
+    }
+    __device__ int32_t result(long long i) const { return pages[i].page_id; }
+};
+
+__device__ __forceinline__ void min_rank(uint64_t &best, long long &bi, uint64_t v, long long i) {
+    if (i >= 0 && v != UINT64_MAX && (bi < 0 || v < best || (v == best && i < bi))) {
+        best = v;
+        bi = i;
+    }
+}
+
+__device__ __forceinline__ void warp_min_rank(uint64_t &best, long long &bi) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const uint64_t ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const long long oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        min_rank(best, bi, ov, oi);
+    }
+}
+
+template <typename Src>
+__global__ void __cluster_dims__(kSelCtas, 1, 1) __launch_bounds__(kSelThreads)
+select_kernel(Src src, size_t n, int32_t *out) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned cr = cluster.block_rank();
+    uint64_t best = UINT64_MAX;
+    long long bi = -1;
+    // each thread visits its indices in increasing order: the first minimum stays
+    for (size_t i = (size_t)cr * kSelThreads + threadIdx.x; i < n; i += (size_t)kSelCtas * kSelThreads) {
+        const uint64_t r = src.rank(i);
+        if (r < best) {
+            best = r;
             bi = (long long)i;
         }
     }
-    // (score, index) reduction; LRU compares negated order through bmin
-    auto reduce = [&](float &b, uint64_t &bm, long long &i0) {
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const float ob = __shfl_xor_sync(0xffffffffu, b, off);
-            const uint64_t om = __shfl_xor_sync(0xffffffffu, bm, off);
-            const long long oi = __shfl_xor_sync(0xffffffffu, i0, off);
-            const bool take = lru ? (oi >= 0 && (i0 < 0 || om < bm || (om == bm && oi < i0)))
-                                  : better(ob, oi, b, i0);
-            if (take) {
-                b = ob;
-                bm = om;
-                i0 = oi;
-            }
-        }
-    };
-    reduce(best, bmin, bi);
-    __shared__ float sb[32];
-    __shared__ uint64_t sm[32];
+    warp_min_rank(best, bi);
+    __shared__ uint64_t sv[32];
     __shared__ long long si[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
-        sb[warp] = best;
-        sm[warp] = bmin;
+        sv[warp] = best;
         si[warp] = bi;
     }
     __syncthreads();
     if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        best = lane < nw ? sb[lane] : -1.0f;
-        bmin = lane < nw ? sm[lane] : UINT64_MAX;
-        bi = lane < nw ? si[lane] : -1;
-        reduce(best, bmin, bi);
-        if (lane == 0) *page_id = bi >= 0 ? pages[bi].page_id : -1;
+        best = sv[lane];
+        bi = si[lane];
+        warp_min_rank(best, bi);
+        if (lane == 0) {
+            sv[0] = best;
+            si[0] = bi;
+        }
     }
+    cluster.sync();  // every CTA's (rank, index) is in its shared memory
+    if (cr == 0 && warp == 0) {
+        best = UINT64_MAX;
+        bi = -1;
+        if (lane < kSelCtas) {
+            best = *cluster.map_shared_rank(&sv[0], lane);
+            bi = *cluster.map_shared_rank(&si[0], lane);
+        }
+        warp_min_rank(best, bi);
+        if (lane == 0) *out = bi >= 0 ? src.result(bi) : -1;
+    }
+    cluster.sync();  // keep the other CTAs' shared memory until it was read
+}
+
+template <typename Src> int launch_select(const Src &src, size_t n, int32_t *out, void *stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n == 0) return cudaMemsetAsync(out, 0xff, sizeof(int32_t), st) == cudaSuccess ? KVX_OK : KVX_ECUDA;
+    select_kernel<Src><<<kSelCtas, kSelThreads, 0, st>>>(src, n, out);
+    return launch_status();
 }
 
 int launch_policy_select(const void *pages, size_t n, const PolicySet &ps, float decay, const float *predicted,
                          bool lru, int32_t *page_id, void *stream) {
     if (!page_id || (n && !pages) || n > 0x7fffffffull) return KVX_EINVAL;
     if (reinterpret_cast<uintptr_t>(pages) & 7) return KVX_EINVAL;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (n == 0) return cudaMemsetAsync(page_id, 0xff, sizeof(int32_t), st) == cudaSuccess ? KVX_OK : KVX_ECUDA;
-    policy_select_kernel<<<1, 1024, 0, st>>>(static_cast<const EvictMetrics *>(pages), n, ps, decay, predicted, lru,
-                                             page_id);
-    return launch_status();
+    return launch_select(PolicyRank{static_cast<const EvictMetrics *>(pages), ps, decay, predicted, lru}, n, page_id,
+                         stream);
 }
 
 }  // namespace
@@ -229,10 +213,5 @@ extern "C" KVX_API int kvx_lru_select(const uint64_t *stamps, size_t n, int32_t 
     if (!victim || (n && !stamps)) return KVX_EINVAL;
     if (n > 0x7fffffffull) return KVX_EINVAL;
     if (reinterpret_cast<uintptr_t>(stamps) & 15) return KVX_EINVAL;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (n == 0) {
-        return cudaMemsetAsync(victim, 0xff, sizeof(int32_t), st) == cudaSuccess ? KVX_OK : KVX_ECUDA;
-    }
-    lru_select_kernel<<<1, 1024, 0, st>>>(stamps, n, victim);
-    return launch_status();
+    return launch_select(StampRank{stamps}, n, victim, stream);
 }

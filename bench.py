@@ -501,6 +501,9 @@ def run_config3(args):
     h16 = torch.empty(1 << 30, device="cuda", dtype=torch.int16)
     ms_we = _events_time(lambda: kvx.fp16_wrap_encode(x32, out=h16), 5)
     ms_wd = _events_time(lambda: kvx.fp16_wrap_decode(h16, out=x32), 5)
+    # the disk tier's truncating codec (compression/kv_compress.cpp:6-60) on the same arrays
+    ms_te = _events_time(lambda: kvx.f32_to_f16_trunc(x32, out=h16), 5)
+    ms_td = _events_time(lambda: kvx.f16_trunc_to_f32(h16, out=x32), 5)
     w_bytes = (1 << 30) * 6
     del x32, h16
     # decode over int8 pages: batch 32, context 4096, one layer, 24 q-heads
@@ -532,6 +535,10 @@ def run_config3(args):
                       "decode_GBps": round(w_bytes / (ms_wd / 1e3) / 1e9, 1),
                       "encode_frac_of_peak": round(w_bytes / (ms_we / 1e3) / 1e9 / peak, 3),
                       "decode_frac_of_peak": round(w_bytes / (ms_wd / 1e3) / 1e9 / peak, 3)},
+        "fp16_trunc": {"encode_GBps": round(w_bytes / (ms_te / 1e3) / 1e9, 1),
+                       "decode_GBps": round(w_bytes / (ms_td / 1e3) / 1e9, 1),
+                       "encode_frac_of_peak": round(w_bytes / (ms_te / 1e3) / 1e9 / peak, 3),
+                       "decode_frac_of_peak": round(w_bytes / (ms_td / 1e3) / 1e9 / peak, 3)},
         "int8_decode": {"GBps": round(q_bytes / (ms_q / 1e3) / 1e9, 1), "us": round(ms_q * 1e3, 1),
                         "batch": B, "context": T, "frac_of_peak": round(q_bytes / (ms_q / 1e3) / 1e9 / peak, 3)},
         "peak": peak, "peak_kind": peak_kind, "cpu_baseline": cpu}), flush=True)
@@ -609,6 +616,36 @@ def cpu_tier_baseline(universe=4096, accesses=20000):
     return {"value": round(misses * 65536 / sec / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
             "sample": f"KVManager capacity {universe // 3} of {universe} pages (64 KiB fp16 page files), "
                       f"{accesses} Zipf(1.1) load_page calls, {misses} misses"}
+
+
+def select_timing(n):
+    """Victim selection on the device over n frames: kvx_lru_select over
+    access stamps (LRUEvictionPolicy / KVCacheGPU::findLRUPage) and
+    kvx_evict_select over EvictionMetrics records for LRU, TokenWeighted and
+    AttentionBased (AdvancedEvictionPolicy::selectPageToEvict); seeded
+    synthetic stamps and attention values."""
+    import torch
+    import kvx
+    # kvx_evict_metrics (include/kvx.h): the reference's EvictionMetrics layout
+    rec = np.dtype([("last_access_token", "<u8"), ("total_attention", "<f4"), ("average_attention", "<f4"),
+                    ("access_frequency", "<f4"), ("_pad0", "<u4"), ("creation_time", "<u8"),
+                    ("page_size", "<u8"), ("page_id", "<i4"), ("_pad1", "<u4")])
+    assert rec.itemsize == 48
+    rng = np.random.default_rng(SEED + 9)
+    m = np.zeros(n, rec)
+    m["last_access_token"] = rng.integers(0, 1 << 40, n, dtype=np.uint64)
+    m["average_attention"] = rng.random(n, dtype=np.float32)
+    m["total_attention"] = m["average_attention"] * 4
+    m["page_id"] = np.arange(n, dtype=np.int32)
+    pages = torch.from_numpy(m.view(np.uint8).copy()).cuda()
+    stamps = torch.from_numpy(m["last_access_token"].copy().view(np.int64)).cuda()
+    out = {"frames": n}
+    ms = _events_time(lambda: kvx.lru_select(stamps), 20)
+    out["lru_stamps"] = {"us": round(ms * 1e3, 1), "GBps": round(n * 8 / (ms / 1e3) / 1e9, 1)}
+    for name, pol in (("lru", 0), ("token_weighted", 1), ("attention_based", 2)):
+        ms = _events_time(lambda: kvx.evict_select(pol, pages), 10)
+        out[name] = {"us": round(ms * 1e3, 1), "GBps": round(n * 48 / (ms / 1e3) / 1e9, 1)}
+    return out
 
 
 def run_config4(args):
@@ -723,6 +760,7 @@ def run_config4(args):
     dec_ms = _events_time(lambda: [kvx.decode(pool, bt_dev[(steps - 1) & 1][l], lens, q[l], out=out[l],
                                               workspace=ws) for l in range(L)], 3)
     dec_bytes = rows * ACC * FB
+    sel = select_timing(C)
     h2d_gbs = mv["frames_h2d"] * FB / (ms / 1e3) / 1e9
     d2h_gbs = mv["frames_d2h"] * FB / (ms / 1e3) / 1e9
     peak, peak_kind = peaks()
@@ -746,6 +784,7 @@ def run_config4(args):
                    "GBps_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9, 1),
                    "frac_of_hbm_peak_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9 / peak, 3)},
         "host_plan_ms_per_step": round(plan_s / steps * 1e3, 3),
+        "victim_select": sel,
         "disk_tier": None if not H else {
             "ram_tier_GB": round(H * FB / 1e9, 1), "spill_file_GB": round(U * FB / 1e9, 1),
             "frames_per_step": {"read": round(mv["frames_disk_read"] / steps, 1),
