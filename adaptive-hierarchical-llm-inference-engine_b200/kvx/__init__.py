@@ -276,6 +276,29 @@ def f16_trunc_to_f32(h, out=None, stream=None):
     return out
 
 
+def softmax_rows(x, out=None, stream=None):
+    """Row softmax of a [rows][cols] fp32 CUDA tensor (TensorOps::softmax)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(x)
+    _check("kvx_softmax_rows", lib.kvx_softmax_rows(_ptr(x), _ptr(out), C.c_int64(x.shape[0]),
+                                                    C.c_int64(x.shape[1]), _stream(stream)))
+    return out
+
+
+def attention_dense(q, k, v, out=None, scale=0.0, stream=None):
+    """softmax(q k^T * scale) v for fp32 CUDA tensors q [seq_q][dim],
+    k / v [seq_k][dim] (TensorOps::attention; scale <= 0 -> 1/sqrt(dim))."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(q)
+    _check("kvx_attention_dense",
+           lib.kvx_attention_dense(_ptr(q), _ptr(k), _ptr(v), _ptr(out), C.c_int64(q.shape[0]),
+                                   C.c_int64(k.shape[0]), C.c_int32(q.shape[1]), C.c_float(scale),
+                                   _stream(stream)))
+    return out
+
+
 def lru_select(stamps, victim=None, stream=None):
     torch = _torch()
     if victim is None:

@@ -446,14 +446,33 @@ def run_config1(args):
         for t in range(T):
             kvx.append(pool, bt, pos[t], rows[t, 0], rows[t, 1])
     ms_app = _events_time(appends, 5, 1)
+    # the same 1024 single-token launches captured once in a CUDA graph and
+    # replayed: what a token costs on the device without the host's launches
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        appends()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        appends()
+    ms_graph = _events_time(graph.replay, 5, 1)
     ms_dec = _events_time(lambda: kvx.decode(pool, bt, lens, q, workspace=ws), 200)
     kv_bytes = T * 2 * HKV * DIM * 4
+    # TensorOps::attention over the whole sequence for one head (the
+    # cuda_attention drop-in): [1024][128] fp32 queries, keys and values
+    qd, kd, vd = (torch.randn((T, DIM), generator=g, device="cuda") for _ in range(3))
+    ms_att = _events_time(lambda: kvx.attention_dense(qd, kd, vd), 20)
     print(json.dumps({"config": 1, "workload": "1 layer, 24q/8kv x128, fp32, B1, 1024 tokens appended one by one, then decode",
                       "append_tokens_per_s": round(T / (ms_app / 1e3), 1),
                       "append_us_per_token": round(ms_app * 1e3 / T, 2),
+                      "append_us_per_token_graph": round(ms_graph * 1e3 / T, 2),
+                      "dense_attention": {"us": round(ms_att * 1e3, 1),
+                                          "GFLOPs": round(4 * T * T * DIM / (ms_att / 1e3) / 1e9, 1)},
                       "decode_us": round(ms_dec * 1e3, 2),
                       "decode_GBps": round(kv_bytes / (ms_dec / 1e3) / 1e9, 1),
-                      "note": "latency-bound: one launch per token, 8 MiB of K/V per decode"}), flush=True)
+                      "note": "latency-bound: one launch per token (from Python, or replayed from a CUDA graph), "
+                              "8 MiB of K/V per decode"}), flush=True)
 
 
 def run_config3(args):

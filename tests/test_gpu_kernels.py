@@ -464,6 +464,23 @@ def test_int8_decode_query_outlier_channels(kvx, oracle, qscale):
     assert_close(out, ref)
 
 
+def test_attention_dense_and_softmax_match_reference_rows(kvx, oracle):
+    """kvx.attention_dense / kvx.softmax_rows (the cuda_attention and
+    cuda_softmax kernels) against TensorOps::attention rows of the golden
+    fixture and the restatement's row attention."""
+    g = golden("attention.npz")
+    for i, T in enumerate((1, 2, 3, 16, 33, 257)):
+        q = kvgen.normal(400 + i, (128,))
+        k = kvgen.normal(500 + i, (T, 128))
+        v = kvgen.normal(600 + i, (T, 128))
+        out = kvx.attention_dense(dev(q[None, :].copy()), dev(k), dev(v)).cpu().numpy()[0]
+        assert_close(out, g["rows"][i])
+    x = kvgen.normal(77, (5, 300)) * 4
+    sm = kvx.softmax_rows(dev(x)).cpu().numpy()
+    e = np.exp(x.astype(np.float64) - x.max(axis=1, keepdims=True))
+    assert np.abs(sm - e / e.sum(axis=1, keepdims=True)).max() < 1e-6
+
+
 # ------------------------------------------------------- fp16 trunc codec ---
 
 def test_f16_trunc_codec_bitexact(kvx):
