@@ -62,6 +62,19 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32
         : "memory");
 }
 
+// Bulk shared -> global copy (TMA, no tensor map): both addresses 16-byte
+// aligned, bytes a multiple of 16.  Completion through bulk groups.
+__device__ __forceinline__ void bulk_s2g(void *dst_global, const void *src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_global),
+                 "r"(smem_addr(src_smem)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the source shared memory of every committed group may be reused
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed group is complete (its global writes done)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

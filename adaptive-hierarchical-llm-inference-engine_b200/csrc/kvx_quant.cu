@@ -344,18 +344,44 @@ template <> __device__ __forceinline__ void store16<__half>(__half *dst, const f
     __stcs(reinterpret_cast<uint4 *>(dst) + 1, make_uint4(u[4], u[5], u[6], u[7]));
 }
 
+// The same 16 values into a shared-memory image of the block.
+template <typename T> __device__ __forceinline__ void store16_shared(T *dst, const float (&v)[16]);
+template <> __device__ __forceinline__ void store16_shared<float>(float *dst, const float (&v)[16]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        reinterpret_cast<float4 *>(dst)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+template <> __device__ __forceinline__ void store16_shared<__half>(__half *dst, const float (&v)[16]) {
+    uint32_t u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        u[k] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(u[0], u[1], u[2], u[3]);
+    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(u[4], u[5], u[6], u[7]);
+}
+
+// Decoders write a block's output (4 KiB fp16 / 8 KiB fp32) into a
+// per-warp shared-memory image and send it with one bulk copy: one TMA
+// operation per block instead of 256 16-byte stores, which had the store
+// queue throttling the warps.  32 KiB of images per CTA.
+template <typename T> constexpr int kDqWarps = sizeof(T) == 2 ? 8 : 4;
+
 // Warp per 2048-element block: stats read once, 16 codes per lane-load.
 // Finite scale and zero point (every block the quantiser writes from finite
 // data): zp + u * scale with u taken from the code byte exactly; otherwise
 // the x86 NaN rebuild, element by element, in a loop kept out of line.
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDqWarps<T> * 32)
 decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict__ stats,
                        T *__restrict__ dst, size_t num_blocks) {
-    const int lane = threadIdx.x & 31;
+    __shared__ __align__(128) T image[kDqWarps<T>][2048];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    T *img = image[warp];
+    bool sent = false;
     const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
-    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
-         b += warps) {
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + warp; b < num_blocks; b += warps) {
         const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
         const float scale = st.z, zp = st.w;
         const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 2048);
@@ -363,6 +389,10 @@ decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict
 #pragma unroll
         for (int j = 0; j < 4; ++j) w[j] = __ldcs(src + j * 32 + lane);
         if (isfinite(scale) && isfinite(zp)) {  // warp-uniform
+            if (sent) {  // the previous block's copy has read the image
+                if (lane == 0) bulk_wait_read_all();
+                __syncwarp();
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {  // 4 x 16 codes per lane
                 const uint32_t u[4] = {w[j].x ^ 0x80808080u, w[j].y ^ 0x80808080u, w[j].z ^ 0x80808080u,
@@ -370,8 +400,15 @@ decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict
                 float v[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) v[k] = __fadd_rn(zp, __fmul_rn(byte_value(u[k >> 2], k & 3), scale));
-                store16<T>(dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 16, v);
+                store16_shared<T>(img + (j * 32 + lane) * 16, v);
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_s2g(dst + (size_t)b * 2048, img, 2048 * sizeof(T));
+                bulk_commit();
+            }
+            sent = true;
         } else {  // rare: codes re-read from global, no indexed register array
 #pragma unroll 1
             for (int j = 0; j < 4; ++j) {
@@ -383,6 +420,7 @@ decompress_2048_kernel(const int8_t *__restrict__ codes, const float *__restrict
             }
         }
     }
+    if (sent && lane == 0) bulk_wait_all();  // the images stay until the copies are done
 }
 
 // Any block size or alignment: one thread per element.
@@ -494,13 +532,15 @@ template <> __device__ __forceinline__ void st_out<__half>(__half *p, float v) {
 // NF4 decode, warp per 2048-element block: 1024 code bytes as two 16-byte
 // loads per lane, 64 values out per lane.
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDqWarps<T> * 32)
 decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ stats,
                            T *__restrict__ dst, size_t num_blocks) {
-    const int lane = threadIdx.x & 31;
+    __shared__ __align__(128) T image[kDqWarps<T>][2048];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    T *img = image[warp];
+    bool sent = false;
     const size_t warps = (size_t)gridDim.x * (blockDim.x >> 5);
-    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < num_blocks;
-         b += warps) {
+    for (size_t b = blockIdx.x * (size_t)(blockDim.x >> 5) + warp; b < num_blocks; b += warps) {
         const float4 st = __ldg(reinterpret_cast<const float4 *>(stats) + b);
         const float scale = st.z, zp = st.w;
         const uint4 *src = reinterpret_cast<const uint4 *>(codes + b * 1024);
@@ -508,10 +548,14 @@ decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__res
 #pragma unroll
         for (int j = 0; j < 2; ++j) w[j] = __ldcs(src + j * 32 + lane);
         if (isfinite(scale) && isfinite(zp)) {  // warp-uniform
+            if (sent) {  // the previous block's copy has read the image
+                if (lane == 0) bulk_wait_read_all();
+                __syncwarp();
+            }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {  // 16 bytes = 32 codes per lane, high nibble first
                 const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-                T *out = dst + (size_t)b * 2048 + (size_t)(j * 32 + lane) * 32;
+                T *out = img + (j * 32 + lane) * 32;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {  // bytes 8h .. 8h + 7 -> elements 16h .. 16h + 15
                     float v[16];
@@ -522,9 +566,16 @@ decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__res
                         v[2 * k] = __fadd_rn(zp, __fmul_rn(byte_value(hi, k & 3), scale));
                         v[2 * k + 1] = __fadd_rn(zp, __fmul_rn(byte_value(lo, k & 3), scale));
                     }
-                    store16<T>(out + 16 * h, v);
+                    store16_shared<T>(out + 16 * h, v);
                 }
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_s2g(dst + (size_t)b * 2048, img, 2048 * sizeof(T));
+                bulk_commit();
+            }
+            sent = true;
         } else {  // rare: codes re-read from global, no indexed register array
 #pragma unroll 1
             for (int i = 0; i < 4; ++i) {  // 8 bytes -> 16 values per step
@@ -540,6 +591,7 @@ decompress_nf4_2048_kernel(const uint8_t *__restrict__ codes, const float *__res
             }
         }
     }
+    if (sent && lane == 0) bulk_wait_all();  // the images stay until the copies are done
 }
 
 // NF4 decode, any block size: one thread per element.
@@ -698,9 +750,11 @@ extern "C" KVX_API int kvx_decompress_nf4(const uint8_t *codes, const float *sta
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (block_elems == 2048 && aligned16(codes) && aligned16(dst) && aligned16(stats)) {
         if (dst_dtype == KVX_F32)
-            decompress_nf4_2048_kernel<float><<<grid_for(decompress_nf4_2048_kernel<float>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+            decompress_nf4_2048_kernel<float><<<(unsigned)((num_blocks + kDqWarps<float> - 1) / kDqWarps<float>),
+                                                kDqWarps<float> * 32, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
         else
-            decompress_nf4_2048_kernel<__half><<<grid_for(decompress_nf4_2048_kernel<__half>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+            decompress_nf4_2048_kernel<__half><<<(unsigned)((num_blocks + kDqWarps<__half> - 1) / kDqWarps<__half>),
+                                                 kDqWarps<__half> * 32, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
         return launch_status();
     }
     if (dst_dtype == KVX_F32)
@@ -749,9 +803,11 @@ extern "C" KVX_API int kvx_decompress_int8(const int8_t *codes, const float *sta
     }
     if (block_elems == 2048 && aligned16(codes)) {
         if (dst_dtype == KVX_F32)
-            decompress_2048_kernel<float><<<grid_for(decompress_2048_kernel<float>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
+            decompress_2048_kernel<float><<<(unsigned)((num_blocks + kDqWarps<float> - 1) / kDqWarps<float>),
+                                            kDqWarps<float> * 32, 0, st>>>(codes, stats, static_cast<float *>(dst), num_blocks);
         else
-            decompress_2048_kernel<__half><<<grid_for(decompress_2048_kernel<__half>, num_blocks, 8, 0), 256, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
+            decompress_2048_kernel<__half><<<(unsigned)((num_blocks + kDqWarps<__half> - 1) / kDqWarps<__half>),
+                                             kDqWarps<__half> * 32, 0, st>>>(codes, stats, static_cast<__half *>(dst), num_blocks);
         return launch_status();
     }
     if (dst_dtype == KVX_F32)
