@@ -653,6 +653,33 @@ __global__ void fp16_wrap_decode_kernel(const uint16_t *__restrict__ src, float 
         dst[i] = fp16_wrap_dec(src[i]);
 }
 
+// fp16 -> fp32 decoders over whole tiles of 2048 elements: one CTA per tile,
+// each thread one 16-byte load of 8 halves; the 8 KiB of floats go out as
+// one bulk copy from a shared-memory image (as the block decoders do).
+struct TruncDec {
+    __device__ static float dec(uint32_t h) { return f16_trunc_to_f32((uint16_t)h); }
+};
+struct WrapDec {
+    __device__ static float dec(uint32_t h) { return fp16_wrap_dec(h); }
+};
+
+template <typename Op>
+__global__ void __launch_bounds__(256) f16_decode_tile_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst) {
+    __shared__ __align__(128) float img[2048];
+    const size_t t = blockIdx.x;
+    const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(src + t * 2048) + threadIdx.x);
+    float4 *o = reinterpret_cast<float4 *>(img) + 2 * threadIdx.x;
+    o[0] = make_float4(Op::dec(v.x & 0xFFFFu), Op::dec(v.x >> 16), Op::dec(v.y & 0xFFFFu), Op::dec(v.y >> 16));
+    o[1] = make_float4(Op::dec(v.z & 0xFFFFu), Op::dec(v.z >> 16), Op::dec(v.w & 0xFFFFu), Op::dec(v.w >> 16));
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bulk_s2g(dst + t * 2048, img, 2048 * sizeof(float));
+        bulk_commit();
+        bulk_wait_all();
+    }
+}
+
 // CTAs that fit on the current GPU at once for `kernel` at 256 threads (its
 // occupancy times the SM count), cached per kernel and device.
 int resident_ctas(const void *kernel) {
@@ -778,8 +805,16 @@ extern "C" KVX_API int kvx_fp16_wrap_decode(const uint16_t *src, float *dst, siz
     if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 1) || (reinterpret_cast<uintptr_t>(dst) & 3))
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    size_t done = 0;
+    if (aligned16(src) && aligned16(dst) && n >= 2048) {
+        done = n / 2048 * 2048;
+        f16_decode_tile_kernel<WrapDec><<<(unsigned)(n / 2048), 256, 0, st>>>(src, dst);
+        if (done == n) return launch_status();
+    }
+    src += done, dst += done, n -= done;
     const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
-    fp16_wrap_decode_kernel<<<grid_for(fp16_wrap_decode_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    fp16_wrap_decode_kernel<<<grid_for(fp16_wrap_decode_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, st>>>(
         src, dst, n, vec);
     return launch_status();
 }
@@ -831,8 +866,16 @@ extern "C" KVX_API int kvx_f16_trunc_to_f32(const uint16_t *src, float *dst, siz
     if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 1) || (reinterpret_cast<uintptr_t>(dst) & 3))
         return KVX_EINVAL;
     if (n == 0) return KVX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    size_t done = 0;
+    if (aligned16(src) && aligned16(dst) && n >= 2048) {
+        done = n / 2048 * 2048;
+        f16_decode_tile_kernel<TruncDec><<<(unsigned)(n / 2048), 256, 0, st>>>(src, dst);
+        if (done == n) return launch_status();
+    }
+    src += done, dst += done, n -= done;
     const bool vec = !(reinterpret_cast<uintptr_t>(src) & 7) && aligned16(dst);
-    decode_trunc_kernel<<<grid_for(decode_trunc_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    decode_trunc_kernel<<<grid_for(decode_trunc_kernel, vec ? n / 4 + 1 : n, 256, 8), 256, 0, st>>>(
         src, dst, n, vec);
     return launch_status();
 }
