@@ -486,15 +486,8 @@ paged_decode_kernel(const DecodeParams p) {
     for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kThreads) {
         const int g = idx / kHeadDim, d = idx % kHeadDim;
         const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
-        float M = -CUDART_INF_F;
-        for (int c = 0; c < nsplit; ++c) M = fmaxf(M, __ldcg(p.part_ml + (base + c) * 2));
-        float O = 0.f, L = 0.f;
-        for (int c = 0; c < nsplit; ++c) {
-            const float mc = __ldcg(p.part_ml + (base + c) * 2);
-            const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
-            L += w * __ldcg(p.part_ml + (base + c) * 2 + 1);
-            O += w * __ldcg(p.part_o + (base + c) * kHeadDim + d);
-        }
+        float M, L;
+        const float O = fold_splits(p.part_ml, p.part_o, base, nsplit, d, M, L);
         QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim;
         io_traits<QT>::store(o + d, O / L);
     }
@@ -530,13 +523,15 @@ int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
 
 // Tensor-core decode: the largest chunk that still leaves about two waves
 // of resident CTAs (3 per SM), counting half of max_pages as the mean
-// sequence length, then evened out over the longest sequence's splits.
+// sequence length -- twice that for GQA groups above 4, at least 32 pages
+// and at most 32 splits per sequence -- then evened out over the longest
+// sequence's splits.
 // Every CTA pays a fixed cost (q fragments, pipeline fill, the merge of its
 // warps, the split combine), so fewer and longer CTAs win while all SMs stay
 // busy; programmatic dependent launch lets the next launch fill the SMs
 // that one launch's last wave leaves idle.  page_scale > 1 for pages that
 // carry less data each (int8: half the bytes, the same per-page cost).
-int choose_chunk_tc(int batch, int hkv, int max_pages, int page_scale) {
+int choose_chunk_tc(int batch, int hkv, int group, int max_pages, int page_scale) {
     if (const char *e = getenv("KVX_DECODE_CHUNK")) {
         int c = atoi(e);
         if (c >= kMinChunk) return c;
@@ -544,6 +539,10 @@ int choose_chunk_tc(int batch, int hkv, int max_pages, int page_scale) {
     const long long work = (long long)batch * hkv * max_pages * page_scale;
     const long long target = (long long)sm_count() * 3 * 2;
     long long c = (work / 2 + target - 1) / target;
+    if (group > 4) c *= 2;  // a CTA's merge and combine grow with the rows it carries
+    // at most 32 splits per sequence: the last CTA folds them all (small
+    // batches with long contexts), and at least 32 pages (8 per warp) a CTA
+    c = std::max<long long>(c, std::max<long long>((max_pages + 31) / 32, 32));
     c = std::min<long long>(std::max<long long>(c, kMinChunk), 256);
     const long long nsplit = (max_pages + c - 1) / c;
     c = (max_pages + nsplit - 1) / nsplit;
@@ -652,7 +651,7 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
                     !(force_simt && force_simt[0] == '1');
     p.nhg = tc ? 1 : (p.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
     const int G = (p.group + p.nhg - 1) / p.nhg;
-    p.chunk = std::max(tc ? choose_chunk_tc(batch, p.hkv, max_pages, kv->dtype == KVX_I8 ? 3 : 1)
+    p.chunk = std::max(tc ? choose_chunk_tc(batch, p.hkv, p.group, max_pages, kv->dtype == KVX_I8 ? 3 : 1)
                           : choose_chunk(batch, p.hkv, p.nhg, max_pages),
                        min_chunk_r);
     p.max_splits = (max_pages + p.chunk - 1) / p.chunk;

@@ -1,6 +1,7 @@
 // kvx_decode_params.cuh -- parameters shared by the paged decode kernels
 // (SIMT path in kvx_decode.cu, tensor-core path in kvx_decode_tc.cu).
 #pragma once
+#include <math_constants.h>
 
 #include "kvx_common.cuh"
 
@@ -27,6 +28,49 @@ struct DecodeParams {
     int num_pages, hkv, hq, max_pages, max_splits, chunk, group, nhg;
     float scale_log2;
 };
+
+// Flash-decoding combine of one output element: the splits' (m, l) pairs
+// at part_ml[(base + c) * 2] and partial sums part_o[(base + c) * 128 + d],
+// c < nsplit, folded in split order; returns O and sets the row's max M and
+// sum L.  Loads go out in groups of 8: a long sequence has up to
+// max_pages / 4 splits, walked by one thread per (row, dim), so they must
+// not wait one by one.
+__device__ __forceinline__ float fold_splits(const float *part_ml, const float *part_o, size_t base, int nsplit,
+                                             int d, float &M, float &L) {
+    const float2 *ml = reinterpret_cast<const float2 *>(part_ml) + base;
+    const float *po = part_o + base * 128 + d;
+    M = -CUDART_INF_F;
+    int c = 0;
+    for (; c + 8 <= nsplit; c += 8) {
+        float mv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mv[u] = __ldcg(&ml[c + u].x);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
+    }
+    for (; c < nsplit; ++c) M = fmaxf(M, __ldcg(&ml[c].x));
+    float O = 0.f;
+    L = 0.f;
+    auto fold = [&](float2 m_l, float o) {
+        const float w = m_l.x == -CUDART_INF_F ? 0.f : exp2f(m_l.x - M);
+        L += w * m_l.y;
+        O += w * o;
+    };
+    c = 0;
+    for (; c + 8 <= nsplit; c += 8) {
+        float2 mlv[8];
+        float ov[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            mlv[u] = __ldcg(ml + c + u);
+            ov[u] = __ldcg(po + (size_t)(c + u) * 128);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) fold(mlv[u], ov[u]);
+    }
+    for (; c < nsplit; ++c) fold(__ldcg(ml + c), __ldcg(po + (size_t)c * 128));
+    return O;
+}
 
 // Tensor-core path for fp16 and int8 pools (kvx_decode_tc.cu).  Returns a
 // kvx_status; KVX_EUNSUPPORTED when the geometry has no tensor-core kernel.

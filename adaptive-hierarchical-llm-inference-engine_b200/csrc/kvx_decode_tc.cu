@@ -817,15 +817,8 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kTcThreads) {
         const int g = idx / kHeadDim, d = idx % kHeadDim;
         const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
-        float M = -CUDART_INF_F;
-        for (int c = 0; c < nsplit; ++c) M = fmaxf(M, __ldcg(p.part_ml + (base + c) * 2));
-        float O = 0.f, L = 0.f;
-        for (int c = 0; c < nsplit; ++c) {
-            const float mc = __ldcg(p.part_ml + (base + c) * 2);
-            const float w = mc == -CUDART_INF_F ? 0.f : exp2f(mc - M);
-            L += w * __ldcg(p.part_ml + (base + c) * 2 + 1);
-            O += w * __ldcg(p.part_o + (base + c) * kHeadDim + d);
-        }
+        float M, L;
+        const float O = fold_splits(p.part_ml, p.part_o, base, nsplit, d, M, L);
         QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim;
         io_traits<QT>::store(out + d, O / L);
         if (kAttn && d == 0)
