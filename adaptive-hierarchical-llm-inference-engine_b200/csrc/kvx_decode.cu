@@ -523,7 +523,7 @@ int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
 
 // Tensor-core decode: the largest chunk that still leaves about two waves
 // of resident CTAs (3 per SM), counting half of max_pages as the mean
-// sequence length -- twice that for GQA groups above 4, at least 32 pages
+// sequence length -- twice that for GQA groups above 4, at least 64 pages
 // and at most 32 splits per sequence -- then evened out over the longest
 // sequence's splits.
 // Every CTA pays a fixed cost (q fragments, pipeline fill, the merge of its
@@ -541,8 +541,8 @@ int choose_chunk_tc(int batch, int hkv, int group, int max_pages, int page_scale
     long long c = (work / 2 + target - 1) / target;
     if (group > 4) c *= 2;  // a CTA's merge and combine grow with the rows it carries
     // at most 32 splits per sequence: the last CTA folds them all (small
-    // batches with long contexts), and at least 32 pages (8 per warp) a CTA
-    c = std::max<long long>(c, std::max<long long>((max_pages + 31) / 32, 32));
+    // batches with long contexts), and at least 64 pages (16 per warp) a CTA
+    c = std::max<long long>(c, std::max<long long>((max_pages + 31) / 32, 64));
     c = std::min<long long>(std::max<long long>(c, kMinChunk), 256);
     const long long nsplit = (max_pages + c - 1) / c;
     c = (max_pages + nsplit - 1) / nsplit;
