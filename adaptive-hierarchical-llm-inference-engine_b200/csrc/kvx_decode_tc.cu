@@ -55,6 +55,7 @@ constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kBox = 2048;          // 16 tokens x 64 dims x fp16 (or 128 int8), 128B-swizzled
 constexpr int kQloBytes = 8 * 32 * 16;  // q lo A fragments, 8 k-steps x 32 lanes x 4 regs (group > 8)
 constexpr int kBtCache = 64;            // block-table entries staged per warp
+constexpr int kCombineFloats = 4096;    // split weights kept in the ring for the combine
 
 // Per-warp staging ring of 2 stages.  fp16: a stage is one page, K dims 0-63
 // | K 64-127 | V 0-63 | V 64-127.  int8: a stage is two pages, K codes | V
@@ -814,6 +815,67 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     }
     __syncthreads();
     if (!s_flag[1]) return;
+    if (nh * nsplit <= kCombineFloats) {
+        // the splits' weights exp2(m_c - M) and each row's M and L once, in
+        // the (now idle) staging ring: one warp per row, lanes over splits
+        float *wts = reinterpret_cast<float *>(smem);  // [nh][nsplit]
+        float *row_m = wts + kCombineFloats, *row_l = row_m + 16;
+        for (int g = warp; g < nh; g += kTcWarps) {
+            const float2 *ml = reinterpret_cast<const float2 *>(p.part_ml) + ((size_t)s * p.hq + h0 + g) * p.max_splits;
+            float mx = -CUDART_INF_F;
+            for (int c = lane; c < nsplit; c += 32) mx = fmaxf(mx, __ldcg(&ml[c].x));
+#pragma unroll
+            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            float l = 0.f;
+            for (int c = lane; c < nsplit; c += 32) {
+                const float2 v = __ldcg(ml + c);
+                const float w = v.x == -CUDART_INF_F ? 0.f : exp2f(v.x - mx);
+                wts[g * nsplit + c] = w;
+                l += w * v.y;
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            if (lane == 0) {
+                row_m[g] = mx;
+                row_l[g] = l;
+            }
+        }
+        __syncthreads();
+        // O: a thread per (row, 4 dims), the splits' partial sums read in
+        // groups of 8 (float4), summed in split order
+        for (int idx = threadIdx.x; idx < nh * (kHeadDim / 4); idx += kTcThreads) {
+            const int g = idx / (kHeadDim / 4), d4 = idx % (kHeadDim / 4);
+            const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
+            const float4 *po = reinterpret_cast<const float4 *>(p.part_o + base * kHeadDim) + d4;
+            const float *w = wts + g * nsplit;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            auto add = [&](float wc, float4 v) {
+                o.x += wc * v.x;
+                o.y += wc * v.y;
+                o.z += wc * v.z;
+                o.w += wc * v.w;
+            };
+            int c = 0;
+            for (; c + 8 <= nsplit; c += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(po + (size_t)(c + u) * (kHeadDim / 4));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) add(w[c + u], v[u]);
+            }
+            for (; c < nsplit; ++c) add(w[c], __ldcg(po + (size_t)c * (kHeadDim / 4)));
+            const float inv_l = 1.f / row_l[g];
+            QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0 + g) * kHeadDim + 4 * d4;
+            io_traits<QT>::store(out + 0, o.x * inv_l);
+            io_traits<QT>::store(out + 1, o.y * inv_l);
+            io_traits<QT>::store(out + 2, o.z * inv_l);
+            io_traits<QT>::store(out + 3, o.w * inv_l);
+            if (kAttn && d4 == 0)
+                *reinterpret_cast<float2 *>(p.attn_ml + ((size_t)s * p.hq + h0 + g) * 2) =
+                    make_float2(row_m[g], row_l[g]);
+        }
+        return;
+    }
     for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kTcThreads) {
         const int g = idx / kHeadDim, d = idx % kHeadDim;
         const size_t base = ((size_t)s * p.hq + h0 + g) * p.max_splits;
