@@ -272,6 +272,8 @@ def run_ours(args):
     if not args.no_e2e:
         result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
         torch.cuda.synchronize()
+        if world == 1:  # after everything timed: it rewrites layer 0
+            result["engine_ops"] = run_engine_ops(api, need_pages * 2 * hkv * PT * DIM * 2)
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -281,6 +283,27 @@ def run_ours(args):
     api.stop()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_engine_ops(api, slab_bytes):
+    """The NativeEngineApi layer moves (native-engine/llama_wrapper/
+    llama_wrapper.cpp:220-433 in the reference, simulations there) on layer
+    0 of the bench's engine: wall time of each blocking call, and its bytes
+    per second for the moves that carry the whole layer."""
+    out = {"layer_bytes": int(slab_bytes)}
+    # the first move to RAM pins the layer's host slab (cudaHostAlloc); the
+    # second one reuses it
+    for name, fn, moved in (("moveKvToRam_first", api.moveKvToRam, True), ("moveKvToGpu", api.moveKvToGpu, True),
+                            ("moveKvToRam", api.moveKvToRam, True), ("moveKvToGpu_again", api.moveKvToGpu, True),
+                            ("compressKv", api.compressKv, True), ("moveKvToGpu_from_int8", api.moveKvToGpu, True),
+                            ("offloadKv", api.offloadKv, True), ("moveKvToGpu_from_file", api.moveKvToGpu, True)):
+        t0 = time.perf_counter()
+        rc = fn(0)
+        ms = (time.perf_counter() - t0) * 1e3
+        out[name] = {"ms": round(ms, 2), "returned": int(rc)}
+        if moved and rc > 0:
+            out[name]["GBps"] = round(slab_bytes / (ms / 1e3) / 1e9, 1)
+    return out
 
 
 def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
