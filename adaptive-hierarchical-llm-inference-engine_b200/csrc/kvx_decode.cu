@@ -512,10 +512,13 @@ int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
         if (c >= kMinChunk) return c;
     }
     // SIMT kernel: aim at ~4 waves of 3 resident CTAs per SM, counting half
-    // of max_pages as the mean sequence length
+    // of max_pages as the mean sequence length; at least 8 pages (2 per
+    // warp) and at most 32 splits per sequence, as a CTA's fixed cost and the
+    // last CTA's combine outweigh more parallelism for small batches
     const long long work = (long long)batch * hkv * nhg * max_pages;
     const long long target = (long long)sm_count() * 3 * 4;
     long long c = (work / 2 + target - 1) / target;
+    c = std::max<long long>(c, std::max<long long>((max_pages + 31) / 32, 8));
     if (c < kMinChunk) c = kMinChunk;
     if (c > 64) c = 64;
     return (int)((c + kWarps - 1) / kWarps * kWarps);

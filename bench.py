@@ -481,6 +481,18 @@ def run_config1(args):
         appends()
     ms_graph = _events_time(graph.replay, 5, 1)
     ms_dec = _events_time(lambda: kvx.decode(pool, bt, lens, q, workspace=ws), 200)
+    # 20 decodes captured once and replayed: the device time of one, without
+    # the host's per-call cost (which the loop above measures)
+    dout = torch.empty_like(q)
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            kvx.decode(pool, bt, lens, q, out=dout, workspace=ws)
+    torch.cuda.current_stream().wait_stream(side)
+    dgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dgraph):
+        for _ in range(20):
+            kvx.decode(pool, bt, lens, q, out=dout, workspace=ws)
+    ms_dec_graph = _events_time(dgraph.replay, 10, 2) / 20
     kv_bytes = T * 2 * HKV * DIM * 4
     # TensorOps::attention over the whole sequence for one head (the
     # cuda_attention drop-in): [1024][128] fp32 queries, keys and values
@@ -494,6 +506,8 @@ def run_config1(args):
                                           "GFLOPs": round(4 * T * T * DIM / (ms_att / 1e3) / 1e9, 1)},
                       "decode_us": round(ms_dec * 1e3, 2),
                       "decode_GBps": round(kv_bytes / (ms_dec / 1e3) / 1e9, 1),
+                      "decode_us_graph": round(ms_dec_graph * 1e3, 2),
+                      "decode_GBps_graph": round(kv_bytes / (ms_dec_graph / 1e3) / 1e9, 1),
                       "note": "latency-bound: one launch per token (from Python, or replayed from a CUDA graph), "
                               "8 MiB of K/V per decode"}), flush=True)
 
