@@ -168,6 +168,7 @@ void Engine::start() {
          cudaMalloc(&d_pos_, cfg_.max_batch * sizeof(int32_t)) == cudaSuccess &&
          cudaMalloc(&d_err_, sizeof(int32_t)) == cudaSuccess && cudaMemset(d_err_, 0, 4) == cudaSuccess &&
          cudaHostAlloc(&h_pos_, cfg_.max_batch * sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok && ensure_staging() != KVX_OK) cudaGetLastError();  // else made on the first file move
     ev_in_.assign(cfg_.layers, nullptr);
     ev_out_.assign(cfg_.layers, nullptr);
     for (int l = 0; ok && l < cfg_.layers; ++l)
@@ -249,6 +250,12 @@ void Engine::release_all() {
     d_ws_ = nullptr;
     if (h_pos_) cudaFreeHost(h_pos_);
     h_pos_ = nullptr;
+    for (int b = 0; b < 2; ++b) {
+        if (stage_[b]) cudaFreeHost(stage_[b]);
+        if (stage_ev_[b]) cudaEventDestroy(stage_ev_[b]);
+        stage_[b] = nullptr;
+        stage_ev_[b] = nullptr;
+    }
     if (compute_) cudaStreamDestroy(compute_);
     if (copy_) cudaStreamDestroy(copy_);
     compute_ = copy_ = nullptr;
@@ -317,6 +324,82 @@ int Engine::alloc_slab(int for_layer) {
     return s;
 }
 
+int Engine::ensure_staging() {
+    for (int b = 0; b < 2; ++b) {
+        if (!stage_[b] && cudaHostAlloc(&stage_[b], kStageBytes, cudaHostAllocDefault) != cudaSuccess) {
+            stage_[b] = nullptr;
+            return KVX_ENOSPC;
+        }
+        if (!stage_ev_[b] && cudaEventCreateWithFlags(&stage_ev_[b], cudaEventDisableTiming) != cudaSuccess) {
+            stage_ev_[b] = nullptr;
+            return KVX_ECUDA;
+        }
+    }
+    return KVX_OK;
+}
+
+// A layer's page file straight to device memory: 64 MiB pieces read into
+// one pinned buffer while the other one's copy runs.  No host copy of the
+// whole layer is pinned for it (pinning 0.6 GB took ~240 ms on its own).
+int Engine::file_to_device(int l, uint8_t *dst) {
+    if (ensure_staging() != KVX_OK) return KVX_ENOSPC;
+    FILE *f = fopen(offload_path(l).c_str(), "rb");
+    if (!f) return KVX_EINVAL;
+    int rc = KVX_OK;
+    bool pending[2] = {false, false};
+    size_t off = 0;
+    for (int b = 0; off < slab_bytes_; b ^= 1) {
+        const size_t n = std::min(kStageBytes, slab_bytes_ - off);
+        if (pending[b] && cudaEventSynchronize(stage_ev_[b]) != cudaSuccess) {
+            rc = KVX_ECUDA;
+            break;
+        }
+        if (fread(stage_[b], 1, n, f) != n) {
+            rc = KVX_EINVAL;
+            break;
+        }
+        if (cudaMemcpyAsync(dst + off, stage_[b], n, cudaMemcpyHostToDevice, copy_) != cudaSuccess ||
+            cudaEventRecord(stage_ev_[b], copy_) != cudaSuccess) {
+            rc = KVX_ECUDA;
+            break;
+        }
+        pending[b] = true;
+        off += n;
+    }
+    fclose(f);
+    if (cudaStreamSynchronize(copy_) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
+    return rc;
+}
+
+// Device memory to the layer's page file, the same way round: one piece's
+// copy runs while the previous one is written.
+int Engine::device_to_file(int l, const uint8_t *src) {
+    if (ensure_staging() != KVX_OK) return KVX_ENOSPC;
+    FILE *f = fopen(offload_path(l).c_str(), "wb");
+    if (!f) return KVX_EINVAL;
+    int rc = KVX_OK;
+    size_t n_prev = 0, off = 0;
+    int b = 0;
+    while (rc == KVX_OK && (off < slab_bytes_ || n_prev)) {
+        const size_t n = std::min(kStageBytes, slab_bytes_ - off);
+        if (n && (cudaMemcpyAsync(stage_[b], src + off, n, cudaMemcpyDeviceToHost, copy_) != cudaSuccess ||
+                  cudaEventRecord(stage_ev_[b], copy_) != cudaSuccess))
+            rc = KVX_ECUDA;
+        if (rc == KVX_OK && n_prev) {  // the previous piece: wait for it, write it
+            if (cudaEventSynchronize(stage_ev_[b ^ 1]) != cudaSuccess)
+                rc = KVX_ECUDA;
+            else if (fwrite(stage_[b ^ 1], 1, n_prev, f) != n_prev)
+                rc = KVX_EINVAL;
+        }
+        n_prev = n;
+        off += n;
+        b ^= 1;
+    }
+    if (fclose(f) != 0 && rc == KVX_OK) rc = KVX_EINVAL;
+    if (cudaStreamSynchronize(copy_) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
+    return rc;
+}
+
 int Engine::to_ram_locked(int l) {
     Layer &L = layers_[l];
     if (L.tier == kRam) return 0;
@@ -356,15 +439,10 @@ int Engine::to_gpu_locked(int l) {
     int rc = KVX_OK;
     if (L.tier == kCompressed) {
         rc = kvx_decompress_int8(L.codes, L.stats, dst, KVX_F16, blocks_per_slab_, 2048, copy_);
-    } else {
-        if (L.tier == kOffloaded) {
-            if (ensure_host(l) != KVX_OK) rc = KVX_ENOSPC;
-            FILE *f = rc ? nullptr : fopen(offload_path(l).c_str(), "rb");
-            if (!rc && !(f && fread(L.host, 1, slab_bytes_, f) == slab_bytes_)) rc = KVX_EINVAL;
-            if (f) fclose(f);
-        }
-        if (!rc && cudaMemcpyAsync(dst, L.host, slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess)
-            rc = KVX_ECUDA;
+    } else if (L.tier == kOffloaded) {
+        rc = file_to_device(l, dst);
+    } else if (cudaMemcpyAsync(dst, L.host, slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess) {
+        rc = KVX_ECUDA;
     }
     if (!rc && cudaStreamSynchronize(copy_) != cudaSuccess) rc = KVX_ECUDA;
     if (rc) {
@@ -423,15 +501,23 @@ int Engine::compress_locked(int l) {
 int Engine::offload_locked(int l) {
     Layer &L = layers_[l];
     if (L.tier == kOffloaded) return 0;
-    if (L.tier != kRam) {
-        const int rc = to_ram_locked(l);
+    if (L.tier == kCompressed) {
+        const int rc = to_gpu_locked(l);
         if (rc < 0) return rc;
     }
-    FILE *f = fopen(offload_path(l).c_str(), "wb");
-    const bool ok = f && fwrite(L.host, 1, slab_bytes_, f) == slab_bytes_;
-    if (f) fclose(f);
-    if (!ok) return KVX_EINVAL;
-    cudaFreeHost(L.host);
+    if (L.tier == kGpu) {  // device -> file, then the slab is free
+        cudaStreamSynchronize(compute_);
+        const int rc = device_to_file(l, arena_ + (size_t)L.slab * slab_bytes_);
+        if (rc != KVX_OK) return rc;
+        free_slabs_.push_back(L.slab);
+        L.slab = -1;
+    } else {
+        FILE *f = fopen(offload_path(l).c_str(), "wb");
+        const bool ok = f && fwrite(L.host, 1, slab_bytes_, f) == slab_bytes_;
+        if (f) fclose(f);
+        if (!ok) return KVX_EINVAL;
+    }
+    if (L.host) cudaFreeHost(L.host);
     L.host = nullptr;
     L.tier = kOffloaded;
     return 1;

@@ -87,6 +87,10 @@ private:
     int compress_locked(int l);
     int offload_locked(int l);
     int ensure_host(int l);
+    // file <-> device through a pinned staging pair, no whole-layer host slab
+    int file_to_device(int l, uint8_t *dst);
+    int device_to_file(int l, const uint8_t *src);
+    int ensure_staging();
     std::string offload_path(int l) const;
     void release_all();
 
@@ -111,6 +115,9 @@ private:
     std::vector<int32_t> free_pages_;   // physical pages not owned by a sequence
     int32_t *d_table_ = nullptr, *d_pos_ = nullptr, *d_err_ = nullptr;
     int32_t *h_pos_ = nullptr;          // pinned positions for the step
+    static constexpr size_t kStageBytes = size_t(64) << 20;
+    uint8_t *stage_[2] = {nullptr, nullptr};  // pinned staging for file moves
+    cudaEvent_t stage_ev_[2] = {nullptr, nullptr};
     int32_t *d_status_ = nullptr;       // {host status, error flag} then every rank's pair
     int32_t *h_status_ = nullptr;       // pinned mirror of d_status_
     void *d_ws_ = nullptr;
