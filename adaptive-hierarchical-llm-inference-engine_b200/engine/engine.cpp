@@ -744,13 +744,24 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     // nothing in between and each may start while the previous drains
     // (programmatic dependent launch); the groups' copies overlap the other
     // groups' kernels.
-    const int G = L < kLayerGroup ? L : kLayerGroup;
-    const int ngroups = (L + G - 1) / G;
+    // group starts: 2 layers, then kLayerGroup at a time, the last 2 alone
+    // -- the first group's input copy and the last group's output copy are
+    // not overlapped by any kernel, so they are kept short
+    int gstart[64];
+    int ngroups = 0;
+    gstart[ngroups++] = 0;
+    if (L > kLayerGroup) {
+        int l = 2;
+        gstart[ngroups++] = l;
+        while (L - l > kLayerGroup + 2 && ngroups < 62) gstart[ngroups++] = (l += kLayerGroup);
+        if (L - l > 2) gstart[ngroups++] = L - 2;
+    }
+    gstart[ngroups] = L;
     // with the batch at max_batch the layers are contiguous on both sides:
     // one copy per tensor per group instead of one per layer
     const bool packed = qstride == qrow && kstride == krow;
     for (int gi = 0; gi < ngroups && rc == KVX_OK; ++gi) {
-        const int l0 = gi * G, l1 = std::min(L, l0 + G);
+        const int l0 = gstart[gi], l1 = gstart[gi + 1];
         if (packed) {
             const size_t n = (size_t)(l1 - l0);
             if (cudaMemcpyAsync(d_q_ + l0 * qstride, q + l0 * qrow, n * qrow * 2, cudaMemcpyHostToDevice, copy_) ||
@@ -768,7 +779,7 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     }
     if (rc && !comm_) return rc;
     for (int gi = 0; gi < ngroups && (rc == KVX_OK || comm_); ++gi) {
-        const int l0 = gi * G, l1 = std::min(L, l0 + G);
+        const int l0 = gstart[gi], l1 = gstart[gi + 1];
         if (rc == KVX_OK && cudaStreamWaitEvent(compute_, ev_in_[gi], 0) != cudaSuccess) rc = KVX_ECUDA;
         for (int l = l0; l < l1 && rc == KVX_OK; ++l) {
             if (layers_[l].tier != kGpu) {  // tiered: bring the layer back (may evict the LRU layer)
