@@ -534,13 +534,23 @@ int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
 // busy; programmatic dependent launch lets the next launch fill the SMs
 // that one launch's last wave leaves idle.  page_scale > 1 for pages that
 // carry less data each (int8: half the bytes, the same per-page cost).
+//
+// When that choice launches at most 3 waves, wave quantisation decides: 512
+// CTAs on 444 resident slots (1.15 waves) leave the second wave at 15 %
+// occupancy and ran 20-25 % slower than 352 or 704 CTAs of the same work
+// (B4 x 16384, B8 x 8192).  Those launches instead take the chunk that
+// minimises  max(1, ceil(ctas / slots)) * (chunk + 24)  -- waves times the
+// length of one CTA, with 24 pages standing for its fixed cost -- over 1-32
+// splits per sequence and chunks of 16-256 pages.  Larger launches keep the
+// first rule: their last wave is a small part of the time.
 int choose_chunk_tc(int batch, int hkv, int group, int max_pages, int page_scale) {
     if (const char *e = getenv("KVX_DECODE_CHUNK")) {
         int c = atoi(e);
         if (c >= kMinChunk) return c;
     }
     const long long work = (long long)batch * hkv * max_pages * page_scale;
-    const long long target = (long long)sm_count() * 3 * 2;
+    const long long slots = (long long)sm_count() * 3;
+    const long long target = slots * 2;
     long long c = (work / 2 + target - 1) / target;
     if (group > 4) c *= 2;  // a CTA's merge and combine grow with the rows it carries
     // at most 32 splits per sequence: the last CTA folds them all (small
@@ -549,7 +559,22 @@ int choose_chunk_tc(int batch, int hkv, int group, int max_pages, int page_scale
     c = std::min<long long>(std::max<long long>(c, kMinChunk), 256);
     const long long nsplit = (max_pages + c - 1) / c;
     c = (max_pages + nsplit - 1) / nsplit;
-    return (int)((c + kWarps - 1) / kWarps * kWarps);
+    c = (c + kWarps - 1) / kWarps * kWarps;
+
+    const long long rows = (long long)batch * hkv;
+    auto ctas = [&](long long chunk) { return rows * ((max_pages + chunk - 1) / chunk); };
+    if (ctas(c) > 3 * slots) return (int)c;
+    long long best = c, best_cost = -1;
+    for (int k = 1; k <= 32; ++k) {
+        long long ck = (max_pages + k - 1) / k;
+        ck = (ck + kWarps - 1) / kWarps * kWarps;
+        if (ck > 256) continue;
+        if (ck < 16 && k > 1) break;
+        const long long waves = std::max<long long>(1, (ctas(ck) + slots - 1) / slots);
+        const long long cost = waves * (ck + 24);
+        if (best_cost < 0 || cost < best_cost) best = ck, best_cost = cost;  // ties: fewer splits
+    }
+    return (int)best;
 }
 
 template <typename KVT, typename QT, int G>

@@ -386,6 +386,10 @@ def test_fp16_wrap_codec_bitexact(kvx):
     assert np.array_equal(dec.view(np.uint32), g["dec_bits"])
     odd = kvx.fp16_wrap_encode(dev(g["x"])[1:]).cpu().numpy().view(np.uint16)  # unaligned: scalar path
     assert np.array_equal(odd, g["enc"][1:])
+    # decode: misaligned start, and aligned starts with a partial last tile
+    for sl in (slice(3, None), slice(8, None), slice(None, -5), slice(8, 8 + 2048 + 1)):
+        d = kvx.fp16_wrap_decode(h[sl]).cpu().numpy()
+        assert np.array_equal(d.view(np.uint32), g["dec_bits"][sl]), sl
 
 
 def test_compress_roundtrip_error_bound(kvx):
@@ -495,6 +499,11 @@ def test_f16_trunc_codec_bitexact(kvx):
     assert np.array_equal(enc_odd, g["enc"][1:])
     dec_odd = kvx.f16_trunc_to_f32(allh[3:]).cpu().numpy().view(np.uint32)
     assert np.array_equal(dec_odd, g["dec_bits"][3:])
+    # 16-byte aligned starts whose length is not a whole number of 2048-element
+    # tiles: the tile kernel takes the prefix, the element-wise kernel the rest
+    for sl in (slice(8, None), slice(None, -5), slice(8, 8 + 2048 + 1)):
+        dec_tail = kvx.f16_trunc_to_f32(allh[sl]).cpu().numpy().view(np.uint32)
+        assert np.array_equal(dec_tail, g["dec_bits"][sl]), sl
 
 
 # ------------------------------------------------------------- eviction ---
