@@ -62,6 +62,12 @@ def parse():
                          "else the rest go to a spill file, the disk tier)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
+    ap.add_argument("--shapes", action="store_true",
+                    help="decode across batch x context shapes (fp16 and int8 pools, GQA 3 and 8), "
+                         "one JSON line per shape")
+    ap.add_argument("--shape-chunks", default="",
+                    help="with --shapes: comma-separated chunk sizes (pages per CTA) to time beside "
+                         "the library's own choice, forced through KVX_DECODE_CHUNK")
     return ap.parse_args()
 
 
@@ -857,6 +863,85 @@ def run_config4(args):
         shutil.rmtree(spill_dir, ignore_errors=True)
 
 
+SHAPES = ((1, 32768), (1, 131072), (4, 16384), (8, 32768), (16, 8192), (32, 4096), (64, 2048),
+          (128, 1024), (256, 512))
+SHAPES_I8 = ((32, 4096), (8, 32768), (32, 8192))
+
+
+def run_shapes(args):
+    """kvx.decode over uniform-length batches: 8 KV heads x 128, 16-token
+    pages in a seeded random permutation, q-heads 24 (GQA 3) and 64 (GQA 8);
+    fp16 pools for SHAPES, int8 pools (random codes, one {min, max, scale,
+    zero point} per block) for SHAPES_I8.  GB/s of K/V (+ stats) read per
+    launch: CUDA events around 60 back-to-back launches that rotate over 3
+    copies of the pool when one copy is under 1 GiB, so no launch finds its
+    pages in L2."""
+    import torch
+    import kvx
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)
+    forced = [int(c) for c in args.shape_chunks.split(",") if c.strip()]
+
+    def timed(fns, iters=60, warm=6):
+        for i in range(warm):
+            fns[i % len(fns)]()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(iters):
+            fns[i % len(fns)]()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / iters
+
+    def sweep(fns, nbytes):
+        res = {}
+        for c in [None] + forced:
+            if c is None:
+                os.environ.pop("KVX_DECODE_CHUNK", None)
+            else:
+                os.environ["KVX_DECODE_CHUNK"] = str(c)
+            try:
+                ms = timed(fns)
+            finally:
+                os.environ.pop("KVX_DECODE_CHUNK", None)
+            res["default" if c is None else str(c)] = round(nbytes / (ms / 1e3) / 1e9, 1)
+        return res
+
+    for pool_kind, shapes in (("fp16", SHAPES), ("int8", SHAPES_I8)):
+        for B, T in shapes:
+            npg = T // PT
+            lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
+            if pool_kind == "fp16":
+                page_bytes = 2 * HKV * PT * DIM * 2
+                nrot = 3 if B * npg * page_bytes < (1 << 30) else 1
+                pools = [torch.randn((B * npg, 2, HKV, PT, DIM), generator=g, device="cuda",
+                                     dtype=torch.float16) for _ in range(nrot)]
+                stats = None
+                nbytes = B * npg * page_bytes
+            else:
+                page_bytes = 2 * HKV * PT * DIM
+                nrot = 3 if B * npg * page_bytes < (1 << 30) else 1
+                pools = [torch.randint(-128, 127, (B * npg, 2, HKV, PT, DIM), generator=g, device="cuda",
+                                       dtype=torch.int8) for _ in range(nrot)]
+                stats = torch.zeros((B * npg, 2, HKV, 4), device="cuda")
+                stats[..., 2] = 0.01
+                stats[..., 3] = -1.0
+                nbytes = B * npg * (page_bytes + 2 * HKV * 16)
+            bts = [torch.randperm(B * npg, generator=g, device="cuda").to(torch.int32).view(B, npg).contiguous()
+                   for _ in range(nrot)]
+            for hq in (24, 64):
+                q = torch.randn((B, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+                ws = kvx.decode_workspace(B, hq, npg)
+                out = torch.empty_like(q)
+                fns = [lambda r=r: kvx.decode(pools[r], bts[r], lens, q, stats=stats, out=out, workspace=ws)
+                       for r in range(nrot)]
+                print(json.dumps({"shapes": "paged decode", "pool": pool_kind, "batch": B, "context": T,
+                                  "q_heads": hq, "kv_heads": HKV, "GBps": sweep(fns, nbytes)}), flush=True)
+            del pools, bts, stats
+            torch.cuda.empty_cache()
+
+
 def run_config5(args):
     """Llama-3-70B KV geometry (80 layers, 64 q-heads, 8 KV heads x 128,
     GQA group 8, fp16), batch 64, 32,768-token contexts, 16-token pages
@@ -945,6 +1030,8 @@ def main():
     LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
+    elif args.shapes:
+        run_shapes(args)
     elif args.config == 1:
         run_config1(args)
     elif args.config == 3:
