@@ -774,28 +774,57 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         s_l[warp * 16 + gq + 8] = kBig ? l1 : 0.f;
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kTcThreads) {
-        const int g = idx / kHeadDim, d = idx % kHeadDim;
-        float M = -CUDART_INF_F;
+    // per row, once: the maximum M over the warps, each warp's weight
+    // exp2(m_w - M) (written over m_w) and the merged L, M (over l_0, l_1).
+    // Thread g owns every entry of row g, so the rewrite is race free.
+    if (threadIdx.x < 16) {
+        const int g = threadIdx.x;
+        float mw[kTcWarps], M = -CUDART_INF_F;
 #pragma unroll
-        for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, s_m[w * 16 + g]);
-        float O = 0.f, L = 0.f;
+        for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, mw[w] = s_m[w * 16 + g]);
+        float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kTcWarps; ++w) {
-            const float mw = s_m[w * 16 + g];
-            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
-            O += sw * reinterpret_cast<const float *>(smem + w * kTcStages * kTcStage)[park_ofs<kI8>(g, d)];
+            const float sw = mw[w] == -CUDART_INF_F ? 0.f : exp2f(mw[w] - M);
             L += sw * s_l[w * 16 + g];
+            s_m[w * 16 + g] = sw;
         }
+        s_l[g] = L;
+        s_l[16 + g] = M;
+    }
+    __syncthreads();
+    // a thread per (row, 4 dims): the warps' parked O weighted and summed in
+    // warp order
+    for (int idx = threadIdx.x; idx < nh * (kHeadDim / 4); idx += kTcThreads) {
+        const int g = idx / (kHeadDim / 4), d = 4 * (idx % (kHeadDim / 4));
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) {
+            const float sw = s_m[w * 16 + g];
+            const float *pw = reinterpret_cast<const float *>(smem + w * kTcStages * kTcStage);
+            if constexpr (kI8) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o4[e] += sw * pw[park_ofs<true>(g, d + e)];
+            } else {
+                const float4 v = *reinterpret_cast<const float4 *>(pw + park_ofs<false>(g, d));
+                o4[0] += sw * v.x;
+                o4[1] += sw * v.y;
+                o4[2] += sw * v.z;
+                o4[3] += sw * v.w;
+            }
+        }
+        const float L = s_l[g], M = s_l[16 + g];
         const int h = h0 + g;
         if (nsplit == 1) {
-            QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
-            io_traits<QT>::store(out + d, O / L);
+            QT *out = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim + d;
+            const float inv_l = 1.f / L;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) io_traits<QT>::store(out + e, o4[e] * inv_l);
             if (kAttn && d == 0)
                 *reinterpret_cast<float2 *>(p.attn_ml + ((size_t)s * p.hq + h) * 2) = make_float2(M, L);
         } else {
             const size_t pi = ((size_t)s * p.hq + h) * p.max_splits + split;
-            p.part_o[pi * kHeadDim + d] = O;
+            *reinterpret_cast<float4 *>(p.part_o + pi * kHeadDim + d) = make_float4(o4[0], o4[1], o4[2], o4[3]);
             if (d == 0) {
                 p.part_ml[pi * 2] = M;
                 p.part_ml[pi * 2 + 1] = L;
