@@ -444,26 +444,52 @@ paged_decode_kernel(const DecodeParams p) {
         }
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < nh * kHeadDim; idx += kThreads) {
-        const int g = idx / kHeadDim, d = idx % kHeadDim;
-        float M = -CUDART_INF_F;
+    // per head, once: the maximum M over the warps, each warp's weight
+    // exp2(m_w - M) (written over m_w) and the merged L, M (over l_0, l_1).
+    // Thread g owns every entry of head g, so the rewrite is race free.
+    if (threadIdx.x < nh) {
+        const int g = threadIdx.x;
+        float mw[kWarps], M = -CUDART_INF_F;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w * kMaxHeadsPerCta + g]);
-        float O = 0.f, L = 0.f;
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w] = s_m[w * kMaxHeadsPerCta + g]);
+        float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) {
-            const float mw = s_m[w * kMaxHeadsPerCta + g];
-            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
-            O += sw * reinterpret_cast<const float *>(smem + w * kStages * kStage)[g * kHeadDim + d];
+            const float sw = mw[w] == -CUDART_INF_F ? 0.f : exp2f(mw[w] - M);
             L += sw * s_l[w * kMaxHeadsPerCta + g];
+            s_m[w * kMaxHeadsPerCta + g] = sw;
         }
+        s_l[g] = L;
+        s_l[kMaxHeadsPerCta + g] = M;
+    }
+    __syncthreads();
+    // a thread per (head, 4 dims): the warps' parked accumulators weighted
+    // and summed in warp order
+    for (int idx = threadIdx.x; idx < nh * (kHeadDim / 4); idx += kThreads) {
+        const int g = idx / (kHeadDim / 4), d = 4 * (idx % (kHeadDim / 4));
+        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float sw = s_m[w * kMaxHeadsPerCta + g];
+            const float4 v = *reinterpret_cast<const float4 *>(
+                reinterpret_cast<const float *>(smem + w * kStages * kStage) + g * kHeadDim + d);
+            o4.x += sw * v.x;
+            o4.y += sw * v.y;
+            o4.z += sw * v.z;
+            o4.w += sw * v.w;
+        }
+        const float L = s_l[g], M = s_l[kMaxHeadsPerCta + g];
         const int h = h0 + g;
         if (nsplit == 1) {
-            QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim;
-            io_traits<QT>::store(o + d, O / L);
+            QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h) * kHeadDim + d;
+            const float inv_l = 1.f / L;
+            io_traits<QT>::store(o + 0, o4.x * inv_l);
+            io_traits<QT>::store(o + 1, o4.y * inv_l);
+            io_traits<QT>::store(o + 2, o4.z * inv_l);
+            io_traits<QT>::store(o + 3, o4.w * inv_l);
         } else {
             const size_t pi = ((size_t)s * p.hq + h) * p.max_splits + split;
-            p.part_o[pi * kHeadDim + d] = O;
+            *reinterpret_cast<float4 *>(p.part_o + pi * kHeadDim + d) = o4;
             if (d == 0) {
                 p.part_ml[pi * 2] = M;
                 p.part_ml[pi * 2 + 1] = L;

@@ -63,7 +63,7 @@ def parse():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     ap.add_argument("--shapes", action="store_true",
-                    help="decode across batch x context shapes (fp16 and int8 pools, GQA 3 and 8), "
+                    help="decode across batch x context shapes (fp16, int8 and fp32 pools, GQA 3 and 8), "
                          "one JSON line per shape")
     ap.add_argument("--shape-chunks", default="",
                     help="with --shapes: comma-separated chunk sizes (pages per CTA) to time beside "
@@ -866,13 +866,15 @@ def run_config4(args):
 SHAPES = ((1, 32768), (1, 131072), (4, 16384), (8, 32768), (16, 8192), (32, 4096), (64, 2048),
           (128, 1024), (256, 512))
 SHAPES_I8 = ((32, 4096), (8, 32768), (32, 8192))
+SHAPES_F32 = ((1, 32768), (32, 4096), (128, 1024))
 
 
 def run_shapes(args):
     """kvx.decode over uniform-length batches: 8 KV heads x 128, 16-token
     pages in a seeded random permutation, q-heads 24 (GQA 3) and 64 (GQA 8);
     fp16 pools for SHAPES, int8 pools (random codes, one {min, max, scale,
-    zero point} per block) for SHAPES_I8.  GB/s of K/V (+ stats) read per
+    zero point} per block) for SHAPES_I8, fp32 pools with fp32 queries (the
+    SIMT kernel) for SHAPES_F32.  GB/s of K/V (+ stats) read per
     launch: CUDA events around 60 back-to-back launches that rotate over 3
     copies of the pool when one copy is under 1 GiB, so no launch finds its
     pages in L2."""
@@ -908,15 +910,16 @@ def run_shapes(args):
             res["default" if c is None else str(c)] = round(nbytes / (ms / 1e3) / 1e9, 1)
         return res
 
-    for pool_kind, shapes in (("fp16", SHAPES), ("int8", SHAPES_I8)):
+    for pool_kind, shapes in (("fp16", SHAPES), ("int8", SHAPES_I8), ("fp32", SHAPES_F32)):
         for B, T in shapes:
             npg = T // PT
             lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
-            if pool_kind == "fp16":
-                page_bytes = 2 * HKV * PT * DIM * 2
+            if pool_kind in ("fp16", "fp32"):
+                dt = torch.float16 if pool_kind == "fp16" else torch.float32
+                page_bytes = 2 * HKV * PT * DIM * dt.itemsize
                 nrot = 3 if B * npg * page_bytes < (1 << 30) else 1
-                pools = [torch.randn((B * npg, 2, HKV, PT, DIM), generator=g, device="cuda",
-                                     dtype=torch.float16) for _ in range(nrot)]
+                pools = [torch.randn((B * npg, 2, HKV, PT, DIM), generator=g, device="cuda", dtype=dt)
+                         for _ in range(nrot)]
                 stats = None
                 nbytes = B * npg * page_bytes
             else:
@@ -931,7 +934,8 @@ def run_shapes(args):
             bts = [torch.randperm(B * npg, generator=g, device="cuda").to(torch.int32).view(B, npg).contiguous()
                    for _ in range(nrot)]
             for hq in (24, 64):
-                q = torch.randn((B, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+                q = torch.randn((B, hq, DIM), generator=g, device="cuda",
+                                dtype=torch.float32 if pool_kind == "fp32" else torch.float16)
                 ws = kvx.decode_workspace(B, hq, npg)
                 out = torch.empty_like(q)
                 fns = [lambda r=r: kvx.decode(pools[r], bts[r], lens, q, stats=stats, out=out, workspace=ws)
