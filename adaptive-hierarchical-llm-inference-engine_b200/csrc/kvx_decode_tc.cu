@@ -485,9 +485,9 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     const int p0 = split * p.chunk;
     const int h0 = kvh * p.group;
     const int nh = p.group;
-    if (p0 >= npages) {
-        grid_dependency_wait();  // the previous decode may still use the workspace / output
+    if (p0 >= npages) {  // nothing to read: exit (which releases the next launch)
         if (npages == 0 && split == 0) {
+            grid_dependency_wait();  // the previous decode may still use the output
             QT *o = reinterpret_cast<QT *>(p.out) + ((size_t)s * p.hq + h0) * kHeadDim;
             for (int i = threadIdx.x; i < nh * kHeadDim; i += kTcThreads) io_traits<QT>::store(o + i, 0.f);
         }
@@ -511,22 +511,21 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
     }
     __syncwarp();
 
-    // fused append: one CTA writes the new token's rows into the pool
+    // fused append: the CTA whose split holds the new token patches its rows
+    // into the staged tiles (below) and writes them into the pool once the
+    // previous launch on this stream has finished (it may read that slot:
+    // the same pool appended at the same position again).
     const bool append_ok = fused && p.positions[s] >= 0 && p.positions[s] < p.max_pages * kPageTokens;
     const int lp_new = append_ok ? p.positions[s] / kPageTokens : -1;
     const int slot_new = append_ok ? p.positions[s] % kPageTokens : 0;
-    if (append_ok && lp_new >= p0 && lp_new < p1 && warp == 0) {
-        const int phys = p.block_table[(size_t)s * p.max_pages + (size_t)lp_new];
-        if (phys >= 0 && phys < p.num_pages) {
-            const int kv = lane >> 4, e = lane & 15;  // 2 rows x 16 vectors of 16 B
-            const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;
-            uint8_t *dst = const_cast<uint8_t *>(p.pool) +
-                           ((((size_t)phys * 2 + kv) * p.hkv + kvh) * kPageTokens + slot_new) * 256;
-            reinterpret_cast<uint4 *>(dst)[e] = reinterpret_cast<const uint4 *>(src)[e];
-        } else if (p.error_flag && lane == 0) {
-            atomicOr(p.error_flag, 2);
-        }
-    }
+    const bool appends = append_ok && lp_new >= p0 && lp_new < p1;  // CTA-uniform
+    // The next launch on this stream (the next layer's decode) may start
+    // filling SMs once every CTA of this one has got here: its CTAs stream
+    // their own pages and wait for this grid before they touch the split
+    // workspace or the output, so this launch's last partial wave leaves no
+    // SM idle.  The appending CTA lets it start only after its pool write is
+    // visible device-wide (the next launch may read that page).
+    if (!appends) grid_dependents_launch();
 
     const int n_pg = (p1 - p0 - warp + kTcWarps - 1) / kTcWarps;  // this warp's pages
     const int n_my = (n_pg + Cfg::kPages - 1) / Cfg::kPages;          // and stages
@@ -712,11 +711,26 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         }
     }
 
-    // Streaming done: the next launch on this stream (the next layer's decode)
-    // may start filling SMs; it waits for this grid before it touches the
-    // split workspace or the output, as this one does here.
-    grid_dependents_launch();
+    // Streaming done: wait for the previous launch before touching the split
+    // workspace, the output or the appended slot, which it may still be using.
     grid_dependency_wait();
+    if (appends) {
+        if (warp == 0) {
+            const int phys = p.block_table[(size_t)s * p.max_pages + (size_t)lp_new];
+            if (phys >= 0 && phys < p.num_pages) {
+                const int kv = lane >> 4, e = lane & 15;  // 2 rows x 16 vectors of 16 B
+                const uint8_t *src = (kv ? p.new_v : p.new_k) + ((size_t)s * p.hkv + kvh) * 256;
+                uint8_t *dst = const_cast<uint8_t *>(p.pool) +
+                               ((((size_t)phys * 2 + kv) * p.hkv + kvh) * kPageTokens + slot_new) * 256;
+                reinterpret_cast<uint4 *>(dst)[e] = reinterpret_cast<const uint4 *>(src)[e];
+                __threadfence();
+            } else if (p.error_flag && lane == 0) {
+                atomicOr(p.error_flag, 2);
+            }
+        }
+        __syncthreads();
+        grid_dependents_launch();
+    }
     if (threadIdx.x == 0) s_flag[0] = 0;
     __syncthreads();
     if (!ok) {
