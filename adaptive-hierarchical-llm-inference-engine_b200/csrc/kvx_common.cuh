@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "kvx.h"
 
 namespace kvx {
@@ -22,6 +24,27 @@ constexpr uint32_t kWaitPolls = 1u << 22;
 inline int launch_status() {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KVX_OK : KVX_ECUDA;
+}
+
+// Device ordinals with a cached per-device flag; a higher ordinal sets the
+// attribute on every launch.
+constexpr int kMaxDevices = 64;
+
+// Raise a kernel's dynamic shared-memory limit on the current device.  The
+// attribute belongs to the (kernel, device) pair, so a process decoding on
+// several GPUs needs it once per device: `done` is the calling launcher's own
+// per-device flag array (a static of that kernel instantiation).  Threads
+// racing on the first call both set it, which is harmless.
+template <typename Kernel>
+inline int ensure_smem_attr(std::atomic<bool> (&done)[kMaxDevices], Kernel kern, int smem) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return KVX_ECUDA;
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    if (cached && done[dev].load(std::memory_order_acquire)) return KVX_OK;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return KVX_ECUDA;
+    if (cached) done[dev].store(true, std::memory_order_release);
+    return KVX_OK;
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {

@@ -521,13 +521,16 @@ paged_decode_kernel(const DecodeParams p) {
 
 constexpr int kMinChunk = 4;
 
+// SM count of the current device, looked up once per device.
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
+    static std::atomic<int> cache[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    int n = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        if (cached) cache[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }
@@ -607,12 +610,8 @@ template <typename KVT, typename QT, int G>
 int launch(DecodeParams &p, int batch, cudaStream_t st) {
     auto kern = paged_decode_kernel<KVT, QT, G>;
     constexpr int smem = smem_bytes<KVT>();
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return KVX_ECUDA;
-        attr_set = true;
-    }
+    static std::atomic<bool> attr_done[kMaxDevices];
+    if (ensure_smem_attr(attr_done, kern, smem) != KVX_OK) return KVX_ECUDA;
     dim3 grid(p.nhg * p.max_splits, p.hkv, batch);
     kern<<<grid, kThreads, smem, st>>>(p);
     return launch_status();

@@ -983,12 +983,8 @@ template <typename QT, bool kBig, bool kI8, bool kAttn>
 int launch_tc(const DecodeParams &p, int batch, cudaStream_t st, const CUtensorMap &tm) {
     auto kern = tc_decode_kernel<QT, kBig, kI8, kAttn>;
     constexpr int smem = TcCfg<kI8>::kSmem;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return KVX_ECUDA;
-        attr_set = true;
-    }
+    static std::atomic<bool> attr_done[kMaxDevices];
+    if (ensure_smem_attr(attr_done, kern, smem) != KVX_OK) return KVX_ECUDA;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.max_splits, p.hkv, batch);
     cfg.blockDim = dim3(kTcThreads);
