@@ -124,8 +124,8 @@ template <typename KVT> __host__ __device__ constexpr int smem_bytes() {
 }
 
 template <typename KVT, typename QT, int G>
-__global__ void __launch_bounds__(kThreads)
-paged_decode_kernel(const DecodeParams p) {
+__device__ __forceinline__ void
+paged_decode_body(const DecodeParams &p) {
     using TR = KvTraits<KVT>;
     constexpr int kVec = TR::kVec;
     constexpr int kNv = 16 / kVec;                // 16-byte vectors per lane per K row
@@ -519,6 +519,13 @@ paged_decode_kernel(const DecodeParams p) {
     }
 }
 
+template <typename KVT, typename QT, int G>
+__global__ void __launch_bounds__(kThreads)
+paged_decode_kernel(const DecodeParams p) {
+    paged_decode_body<KVT, QT, G>(p);
+    if (p.done) grid_done_signal(p.done, p.epoch);  // every exit of the body is CTA-uniform
+}
+
 constexpr int kMinChunk = 4;
 
 // SM count of the current device, looked up once per device.
@@ -651,7 +658,8 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
                const int32_t *seq_lens, const int32_t *positions, const void *new_k,
                const void *new_v, int32_t batch, int32_t num_q_heads, const void *q, void *out,
                int32_t io_dtype, float sm_scale, void *workspace, size_t workspace_bytes_,
-               int32_t *error_flag, void *stream, int min_chunk = 0, float *attn = nullptr) {
+               int32_t *error_flag, void *stream, int min_chunk = 0, float *attn = nullptr,
+               uint32_t *done = nullptr, uint32_t epoch = 0) {
     if (!kv || !kv->pool || !block_table || !q || !out) return KVX_EINVAL;
     if (!seq_lens && !positions) return KVX_EINVAL;
     if (batch <= 0 || max_pages <= 0 || kv->num_kv_heads <= 0 || num_q_heads <= 0) return KVX_EINVAL;
@@ -687,6 +695,9 @@ int run_decode(const kvx_paged *kv, const int32_t *block_table, int32_t max_page
     p.q = q;
     p.out = out;
     p.error_flag = error_flag;
+    if (done && (reinterpret_cast<uintptr_t>(done) & 7)) return KVX_EINVAL;
+    p.done = done;
+    p.epoch = epoch;
     if (attn) {  // [batch][hq][max_pages][2] then [batch][hq][2]
         p.attn_pm = attn;
         p.attn_ml = attn + (size_t)batch * num_q_heads * max_pages * 2;
@@ -771,6 +782,19 @@ extern "C" KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *blo
     return run_decode(kv, block_table, max_pages, nullptr, positions, new_k, new_v, batch,
                       num_q_heads, q, out, io_dtype, sm_scale, workspace, workspace_bytes_,
                       error_flag, stream);
+}
+
+extern "C" KVX_API int kvx_append_decode_signal(const kvx_paged *kv, const int32_t *block_table,
+                                                int32_t max_pages, const int32_t *positions, int32_t batch,
+                                                const void *new_k, const void *new_v, int32_t num_q_heads,
+                                                const void *q, void *out, int32_t io_dtype, float sm_scale,
+                                                void *workspace, size_t workspace_bytes_,
+                                                int32_t *error_flag, uint32_t *done, uint32_t epoch,
+                                                void *stream) {
+    if (!positions || !done) return KVX_EINVAL;
+    return run_decode(kv, block_table, max_pages, nullptr, positions, new_k, new_v, batch,
+                      num_q_heads, q, out, io_dtype, sm_scale, workspace, workspace_bytes_,
+                      error_flag, stream, 0, nullptr, done, epoch);
 }
 
 // ---------------------------------------------------------------------------

@@ -25,9 +25,42 @@ struct DecodeParams {
     // exp2(score - max) [batch][hq][max_pages][2]; per (sequence, q-head)
     // the final max and sum [batch][hq][2]
     float *attn_pm, *attn_ml;
+    // launch completion signal (null = off): done[0] counts finished CTAs
+    // (left at zero), done[1] receives `epoch` once every CTA has finished
+    uint32_t *done;
+    uint32_t epoch;
     int num_pages, hkv, hq, max_pages, max_splits, chunk, group, nhg;
     float scale_log2;
 };
+
+// Programmatic dependent launch (launches with
+// cudaLaunchAttributeProgrammaticStreamSerialization): let the next grid on
+// the stream be scheduled once every CTA of this one got here, and wait for
+// the previous grid's completion (a no-op without such a launch).
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Completion signal of a whole launch, called by every CTA after its last
+// global write: the CTA's writes are released (barrier, then a GPU-scope
+// fence by thread 0) before it counts itself in done[0]; the CTA that counts
+// last resets done[0] and stores `epoch` to done[1] with release semantics,
+// so whoever observes done[1] >= epoch (a stream memory wait on another
+// stream) sees every output of the launch.  Each CTA first waits for the
+// previous grid on the stream, whose last CTA resets the same counter:
+// launches that share `done` must be ordered on one stream.
+__device__ __forceinline__ void grid_done_signal(uint32_t *done, uint32_t epoch) {
+    grid_dependency_wait();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+        __threadfence();
+        if (atomicAdd(done, 1u) == total - 1) {
+            atomicExch(done, 0u);
+            __threadfence();
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(done + 1), "r"(epoch) : "memory");
+        }
+    }
+}
 
 // Flash-decoding combine of one output element: the splits' (m, l) pairs
 // at part_ml[(base + c) * 2] and partial sums part_o[(base + c) * 128 + d],

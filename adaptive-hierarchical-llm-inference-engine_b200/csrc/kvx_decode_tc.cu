@@ -115,13 +115,6 @@ __device__ __forceinline__ void mma16816_lo(float &c0, float &c1, const uint32_t
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(0.f));
 }
 
-// Programmatic dependent launch (launches with
-// cudaLaunchAttributeProgrammaticStreamSerialization): let the next grid on
-// the stream be scheduled once every CTA of this one got here, and wait for
-// the previous grid's completion (a no-op without such a launch).
-__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -462,8 +455,7 @@ template <bool kI8> __device__ __forceinline__ int park_ofs(int row, int d) {
 }
 
 template <typename QT, bool kBig, bool kI8, bool kAttn>
-__global__ void __launch_bounds__(kTcThreads, 3)
-tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
+__device__ __forceinline__ void tc_decode_body(const DecodeParams &p, const CUtensorMap &tm) {
     using Cfg = TcCfg<kI8>;
     constexpr int kTcStages = Cfg::kStages;
     constexpr int kTcStage = Cfg::kStage;
@@ -929,6 +921,13 @@ tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
         if (kAttn && d == 0)
             *reinterpret_cast<float2 *>(p.attn_ml + ((size_t)s * p.hq + h0 + g) * 2) = make_float2(M, L);
     }
+}
+
+template <typename QT, bool kBig, bool kI8, bool kAttn>
+__global__ void __launch_bounds__(kTcThreads, 3)
+tc_decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm) {
+    tc_decode_body<QT, kBig, kI8, kAttn>(p, tm);
+    if (p.done) grid_done_signal(p.done, p.epoch);  // every exit of the body is CTA-uniform
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link

@@ -65,6 +65,9 @@ lib.kvx_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, 
                            _vp, _sz, _vp, _vp]
 lib.kvx_append_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
                                   _vp, _i32, _f32, _vp, _sz, _vp, _vp]
+lib.kvx_append_decode_signal.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp,
+                                         _vp, _i32, _f32, _vp, _sz, _vp, _vp, C.c_uint32, _vp]
+lib.kvx_stream_wait_geq.argtypes = [_vp, C.c_uint32, _vp]
 lib.kvx_decode_workspace_init.argtypes = [_vp, _sz, _vp]
 lib.kvx_decode_noalloc.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32,
                                    _f32, _vp, _vp]
@@ -89,7 +92,8 @@ lib.kvx_decode_attn.restype = C.c_int
 lib.kvx_attn_to_metrics.argtypes = [_vp, _vp, _i32, _vp, _i32, _vp, _i32, C.c_uint64, _vp]
 lib.kvx_attn_to_metrics.restype = C.c_int
 lib.kvx_evict_select_composite.argtypes = [_vp, _vp, _i32, _vp, _sz, _f32, _vp, _vp, _vp]
-for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
+for _fn in ("kvx_append", "kvx_decode", "kvx_append_decode", "kvx_append_decode_signal", "kvx_stream_wait_geq",
+            "kvx_decode_workspace_init", "kvx_compress_int8", "kvx_decompress_int8",
             "kvx_compress_nf4", "kvx_decompress_nf4", "kvx_fp16_wrap_encode", "kvx_fp16_wrap_decode",
             "kvx_f32_to_f16_trunc", "kvx_f16_trunc_to_f32", "kvx_lru_select",
             "kvx_migrate_frames", "kvx_evict_select", "kvx_evict_select_composite"):
@@ -131,6 +135,23 @@ def paged(pool, stats=None) -> KvPaged:
     assert two == 2
     return KvPaged(pool.data_ptr(), 0 if stats is None else stats.data_ptr(), _dtype_code(pool),
                    pages, hkv, dim, pt)
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over a raw device address (no ownership)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+def pool_tensor(view):
+    """A torch view [pages][2][hkv][16][128] of a KvPaged pool (e.g. an
+    engine layer from kvx.engine.layer_view); the memory stays the owner's."""
+    torch = _torch()
+    typestr = {KVX_F32: "<f4", KVX_F16: "<f2", KVX_I8: "|i1"}[view.dtype]
+    shape = (view.num_pages, 2, view.num_kv_heads, view.page_tokens, view.head_dim)
+    return torch.as_tensor(_DeviceArray(view.pool, shape, typestr), device="cuda")
 
 
 def append(pool, block_table, positions, new_k, new_v, error_flag=None, stream=None):
@@ -187,6 +208,32 @@ def append_decode(pool, block_table, positions, new_k, new_v, q, out=None, works
                                _stream(stream))
     _check("kvx_append_decode", rc)
     return out
+
+
+def append_decode_signal(pool, block_table, positions, new_k, new_v, q, done, epoch, out=None,
+                         workspace=None, error_flag=None, sm_scale=0.0, stream=None):
+    """append_decode that stores `epoch` to done[1] once the whole launch has
+    finished (done: int32 CUDA tensor of 2, done[0] zero-filled once)."""
+    torch = _torch()
+    kv = paged(pool)
+    batch, hq, _ = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        workspace = decode_workspace(batch, hq, block_table.shape[1], q.device)
+    rc = lib.kvx_append_decode_signal(C.byref(kv), _ptr(block_table), block_table.shape[1],
+                                      _ptr(positions), batch, _ptr(new_k), _ptr(new_v), hq, _ptr(q),
+                                      _ptr(out), _dtype_code(q), sm_scale, _ptr(workspace),
+                                      workspace.numel() * workspace.element_size(), _ptr(error_flag),
+                                      _ptr(done), epoch & 0xFFFFFFFF, _stream(stream))
+    _check("kvx_append_decode_signal", rc)
+    return out
+
+
+def stream_wait_geq(word, value, stream=None):
+    """Make `stream` wait until the device word reaches `value` (cyclic
+    32-bit comparison).  word: a CUDA tensor whose first element is waited on."""
+    _check("kvx_stream_wait_geq", lib.kvx_stream_wait_geq(_ptr(word), value & 0xFFFFFFFF, _stream(stream)))
 
 
 def compress_int8(src, block_elems=PAGE_TOKENS * HEAD_DIM, codes=None, stats=None, stream=None):

@@ -116,6 +116,34 @@ KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *block_table, i
                               int32_t io_dtype, float sm_scale, void *workspace,
                               size_t workspace_bytes, int32_t *error_flag, void *stream);
 
+/* kvx_append_decode that also tells other streams when it is done: once
+ * every CTA of the launch has written its outputs (out, the appended rows,
+ * the workspace counters), the last one stores `epoch` to done[1] with
+ * release ordering at GPU scope.  done: two device uint32 words, done[0]
+ * zero-filled once before first use (the launch counts its CTAs there and
+ * leaves it at zero); launches sharing `done` must be ordered on one
+ * stream.  A consumer on another stream waits with kvx_stream_wait_geq
+ * (done + 1, epoch) instead of an event recorded on this stream: anything
+ * enqueued between two dependent decode launches (an event record, a
+ * stream wait) ends their overlap.  The all-gather of a KV-head-sharded
+ * step waits this way for the last layer of each group (the reference has
+ * no multi-GPU path; its attention is TensorOps::attention,
+ * runtime/tensor_ops.cpp:179-219, after KVManager::save_page,
+ * cache/kv_cache.cpp:111-127). */
+KVX_API int kvx_append_decode_signal(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                                     const int32_t *positions, int32_t batch, const void *new_k,
+                                     const void *new_v, int32_t num_q_heads, const void *q, void *out,
+                                     int32_t io_dtype, float sm_scale, void *workspace,
+                                     size_t workspace_bytes, int32_t *error_flag, uint32_t *done,
+                                     uint32_t epoch, void *stream);
+
+/* Enqueue on `stream` a wait until the device word *word reaches `value`
+ * (compared cyclically: (int32_t)(*word - value) >= 0), as a stream memory
+ * operation (cuStreamWaitValue32): no kernel, no host involvement.  Later
+ * work on `stream` sees every write released before the word was stored.
+ * KVX_EUNSUPPORTED when the driver offers no stream memory operations. */
+KVX_API int kvx_stream_wait_geq(const uint32_t *word, uint32_t value, void *stream);
+
 /* kvx_decode without any allocation, for callers that cannot allocate
  * device memory when they decode: a JNI / FFI caller holding only the
  * buffers it was given, an engine whose KV memory is capped at a fixed
@@ -125,7 +153,9 @@ KVX_API int kvx_append_decode(const kvx_paged *kv, const int32_t *block_table, i
  * array of kvx_decode_noalloc_scratch_bytes() (8 MiB) that each GPU loading
  * this library holds until exit.  The first call on a device looks up that
  * array's device address (cudaGetSymbolAddress), so make it before any
- * stream capture.  All calls on a device share the array: calls that
+ * stream capture.  The address is kept for the life of the process: after
+ * cudaDeviceReset() of a device, do not call this entry point on that
+ * device again.  All calls on a device share the array: calls that
  * overlap on the GPU race, so order them on one stream.  A batch whose
  * batch*num_q_heads rows do not fit even at one split per row returns
  * KVX_ETOOBIG.  Calls no cudaMalloc / cudaFree. */
