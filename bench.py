@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after the timed region")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
     ap.add_argument("--pages", type=int, default=1 << 20,
@@ -132,6 +133,166 @@ def workload_lens(batch=BATCH):
 
 
 # --------------------------------------------------------------------------
+GROUP = 7      # layers per all-gather group (N > 1)
+OUT_RING = 8   # output buffers an N > 1 run rotates through
+
+
+def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=1, gathered=None,
+                     comm=None, dist=None, group=GROUP):
+    """The timed step.  step(k) appends, for every layer l, the token at
+    positions[k] (rows nk[l] / nv[l]) and decodes over positions[k] + 1
+    tokens into outs[k % len(outs)][l]: one kvx.append_decode launch per
+    layer, all on the current stream with nothing in between, so each launch
+    may start while the previous one drains (programmatic dependent launch);
+    the layers share one decode workspace.
+
+    With world > 1 the layers' outputs are all-gathered (NCCL) on `comm` in
+    groups of `group` layers.  The last launch of a group signals its
+    completion (kvx_append_decode_signal: the last CTA stores the step's
+    epoch) and `comm` waits for that word (kvx_stream_wait_geq) before the
+    group's all-gathers, so no event sits between two decode launches.
+    Outputs rotate through len(outs) buffers; every len(outs) - 1 steps the
+    compute stream waits for the all-gathers of two steps back, the only
+    point where it waits for `comm`."""
+    import torch
+    L = len(views)
+    R = len(outs)
+    main = torch.cuda.current_stream()
+    ngroups = (L + group - 1) // group
+    done = torch.zeros((ngroups, 2), dtype=torch.int32, device=bt.device) if world > 1 else None
+    gathers_done = [torch.cuda.Event() for _ in range(R)] if world > 1 else None
+    sync = "stream memory wait on the group's completion word"
+    if world > 1:
+        try:
+            kvx.stream_wait_geq(done[0, 1:], 0, stream=comm)  # satisfied at once
+        except kvx.KvxError:
+            sync = "event per group (no stream memory operations)"
+    assert world == 1 or R >= 3, "the output ring needs at least 3 buffers"
+
+    def step(k):
+        out = outs[k % R]
+        if world > 1 and k >= 2 and k % (R - 1) == 0:
+            # steps k .. k + R - 2 reuse buffers whose all-gathers ran at
+            # steps up to k - 2
+            main.wait_event(gathers_done[(k - 2) % R])
+        for l in range(L):
+            last_of_group = world > 1 and (l % group == group - 1 or l == L - 1)
+            if last_of_group and sync.startswith("stream"):
+                gi = l // group
+                kvx.append_decode_signal(views[l], bt, positions[k], nk[l], nv[l], q[l], done[gi], k + 1,
+                                         out=out[l], workspace=ws, error_flag=err)
+                with torch.cuda.stream(comm):
+                    kvx.stream_wait_geq(done[gi, 1:], k + 1, stream=comm)
+                    for j in range(l - l % group, l + 1):
+                        dist.all_gather_into_tensor(gathered[j], out[j])
+            else:
+                kvx.append_decode(views[l], bt, positions[k], nk[l], nv[l], q[l], out=out[l], workspace=ws,
+                                  error_flag=err)
+                if last_of_group:
+                    ev = torch.cuda.Event()
+                    ev.record()
+                    with torch.cuda.stream(comm):
+                        comm.wait_event(ev)
+                        for j in range(l - l % group, l + 1):
+                            dist.all_gather_into_tensor(gathered[j], out[j])
+        if world > 1:
+            gathers_done[k % R].record(comm)
+
+    step.gather_sync = sync
+    return step
+
+
+class ParitySample:
+    """An oracle check of the timed run, outside the timed region: for a
+    seeded sample of layers and sequences, the pages as they were before the
+    first step are copied to the host; afterwards the oracle appends every
+    step's rows to them (KVManager::save_page semantics,
+    cache/kv_cache.cpp:111-127), the result must equal the device pages bit
+    for bit, and the oracle's decode over the final context
+    (TensorOps::attention, runtime/tensor_ops.cpp:179-219) must match this
+    rank's rows of the last step within 1e-3 relative / 1e-2 absolute.
+    With several ranks every rank checks its own KV heads, and the gathered
+    buffer's slot of each rank must equal that rank's local rows bit for bit
+    (compared through per-rank checksums); the figures are reduced over the
+    ranks."""
+    RTOL, ATOL = 1e-3, 1e-2
+
+    def __init__(self, bt_np, lens0, hkv, hq, world, rank, views, layers=None, seqs=4):
+        import torch
+        self.bt, self.lens0, self.hkv, self.hq, self.world, self.rank = bt_np, lens0, hkv, hq, world, rank
+        L = len(views)
+        self.layers = sorted({0, L // 2, L - 1} if layers is None else set(layers))
+        rng = np.random.default_rng(SEED + 99)
+        self.seqs = np.sort(rng.choice(len(lens0), size=min(seqs, len(lens0)), replace=False))
+        self.views = views
+        self.before = {}
+        for l in self.layers:
+            pool = self._pool(views[l])
+            for s in self.seqs:
+                pages = self.bt[s][self.bt[s] >= 0]
+                self.before[(l, s)] = pool[torch.from_numpy(pages.astype(np.int64)).cuda()].cpu().numpy()
+
+    @staticmethod
+    def _pool(view):
+        if not hasattr(view, "num_pages"):  # already a tensor
+            return view
+        from kvx import pool_tensor
+        return pool_tensor(view)
+
+    def verify(self, q, nk, nv, total_steps, last_out, gathered, dist):
+        import torch
+        from oracle import Oracle
+        o = Oracle()
+        rows = 0
+        excess = -np.inf
+        pool_ok = True
+        for l in self.layers:
+            pool = self._pool(self.views[l])
+            k_l, v_l, q_l = nk[l].cpu().numpy(), nv[l].cpu().numpy(), q[l].float().cpu().numpy()
+            for s in self.seqs:
+                pages = self.bt[s][self.bt[s] >= 0]
+                host = self.before[(l, s)].copy()
+                bt1 = np.arange(pages.size, dtype=np.int32)[None, :]
+                for k in range(total_steps):
+                    pos = np.array([self.lens0[s] + k], np.int32)
+                    o.append(host, bt1, pos, k_l[s:s + 1], v_l[s:s + 1], 16)
+                dev = pool[torch.from_numpy(pages.astype(np.int64)).cuda()].cpu().numpy()
+                pool_ok = pool_ok and np.array_equal(dev.view(np.uint16), host.view(np.uint16))
+                T = np.array([self.lens0[s] + total_steps], np.int32)
+                ref = o.paged_decode(host, bt1, T, q_l[s:s + 1])
+                got = last_out[l, s:s + 1].float().cpu().numpy()
+                excess = max(excess, float((np.abs(got - ref) - (self.ATOL + self.RTOL * np.abs(ref))).max()))
+                rows += self.hq
+        gather_mismatch = 0
+        if dist is not None:
+            # this rank's local rows of the last step and every rank's slot of
+            # the gathered buffer, compared as checksums of the raw bits
+            def csum(t):
+                return int(t.contiguous().view(torch.int16).to(torch.int64).sum().item())
+            nl, B = last_out.shape[0], last_out.shape[1]
+            mine = torch.tensor([csum(last_out[l]) for l in range(nl)], dtype=torch.int64, device="cuda")
+            every = [torch.empty_like(mine) for _ in range(self.world)]
+            dist.all_gather(every, mine)
+            for l in range(nl):
+                for r in range(self.world):
+                    if csum(gathered[l, r * B:(r + 1) * B]) != every[r][l].item():
+                        gather_mismatch += 1
+            t = torch.tensor([excess, float(rows), 0.0 if pool_ok else 1.0, float(gather_mismatch)],
+                             dtype=torch.float64, device="cuda")
+            mx, sm = t.clone(), t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            excess, rows, pool_ok = mx[0].item(), int(sm[1].item()), mx[2].item() == 0
+            gather_mismatch = int(sm[3].item())
+        return {"ok": bool(pool_ok and excess <= 0 and gather_mismatch == 0), "rows_checked": rows,
+                "max_excess": round(excess, 6), "tolerance": "|gpu - oracle| <= 1e-2 + 1e-3 |oracle|",
+                "pool_pages_bitexact": bool(pool_ok), "gather_slot_mismatches": gather_mismatch,
+                "sample": f"layers {list(self.layers)} x sequences {list(map(int, self.seqs))} per rank "
+                          f"(all {self.hq} local q-heads), {total_steps} appended tokens each",
+                "oracle": "C restatement of the reference's save_page + TensorOps::attention"}
+
+
+# --------------------------------------------------------------------------
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -175,41 +336,28 @@ def run_ours(args):
     q = torch.randn((LAYERS, B, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
     nk = torch.randn((LAYERS, B, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
     nv = torch.randn((LAYERS, B, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
-    out = torch.empty((LAYERS, B, hq, DIM), device="cuda", dtype=torch.float16)
+    ring = OUT_RING if world > 1 else 1
+    outs = [torch.empty((LAYERS, B, hq, DIM), device="cuda", dtype=torch.float16) for _ in range(ring)]
     gathered = torch.empty((LAYERS, world * B, hq, DIM), device="cuda", dtype=torch.float16) \
         if world > 1 else None  # per layer: [world][B][hq/world][D] -> kvx.shard.gathered_to_heads
     ws = kvx.decode_workspace(B, hq, max_pages)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    pos = torch.from_numpy(lens0.astype(np.int32)).cuda()
+    # every step's positions up front: no kernel between two steps' launches
+    positions = torch.from_numpy(np.stack([lens0 + k for k in range(total_steps)]).astype(np.int32)).cuda()
     comm = torch.cuda.Stream() if world > 1 else None
     main = torch.cuda.current_stream()
-    layer_done = [torch.cuda.Event() for _ in range(LAYERS)]
-
-    GROUP = 7  # layers per all-gather group (N > 1)
-
-    def step():
-        # the layers' launches follow each other with nothing in between, so
-        # each may start while the previous drains (programmatic dependent
-        # launch); per-layer events would serialise them
-        for l in range(LAYERS):
-            kvx.append_decode(views[l], bt, pos, nk[l], nv[l], q[l], out=out[l], workspace=ws,
-                              error_flag=err)
-            if world > 1 and (l % GROUP == GROUP - 1 or l == LAYERS - 1):
-                # all-gather a group of layers' outputs once the group is done
-                layer_done[l].record()
-                with torch.cuda.stream(comm):
-                    comm.wait_event(layer_done[l])
-                    for j in range(l - l % GROUP, l + 1):
-                        dist.all_gather_into_tensor(gathered[j], out[j])
-        pos.add_(1)
-        if world > 1:
-            main.wait_stream(comm)
+    # the parity sample: its pages as they are before the first step
+    check = ParitySample(bt_np, lens0, hkv, hq, world, rank, views) if not args.no_parity else None
+    step = make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=world,
+                            gathered=gathered, comm=comm, dist=dist if world > 1 else None)
 
     def kv_bytes(lens_after):  # algorithmic K+V bytes decode reads for one layer
         return int(lens_after.sum()) * 2 * hkv * DIM * 2
 
-    for _ in range(warm):
-        step()
+    for k in range(warm):
+        step(k)
+    if world > 1:
+        main.wait_stream(comm)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -220,8 +368,10 @@ def run_ours(args):
     clocks.start()
     time.sleep(0.3)
     t0.record()
-    for k in range(steps):
-        step()
+    for k in range(warm, warm + steps):
+        step(k)
+    if world > 1:  # the last group's all-gathers belong to the timed work
+        main.wait_stream(comm)
     t1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -229,6 +379,10 @@ def run_ours(args):
         dist.barrier()
     ms = t0.elapsed_time(t1)
     assert err.item() == 0, f"device error flag {err.item()}"
+    parity = None
+    if check is not None:  # outside the timed region, before anything else writes the pools
+        last = outs[(total_steps - 1) % ring]
+        parity = check.verify(q, nk, nv, total_steps, last, gathered, dist if world > 1 else None)
 
     lens_timed = [lens0 + warm + k + 1 for k in range(steps)]
     rank_bytes = sum(kv_bytes(L) * LAYERS for L in lens_timed)
@@ -274,7 +428,10 @@ def run_ours(args):
                      "launch_duration": "timed region / launches (consecutive launches overlap)"},
         "gpu_launches": steps * LAYERS,
         "clocks": clk,
+        "parity": parity,
     }
+    if world > 1:
+        result["config"]["gather_sync"] = step.gather_sync
     if not args.no_e2e:
         result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
         torch.cuda.synchronize()

@@ -153,3 +153,45 @@ def test_decode_step_with_layers_in_other_tiers(engine, oracle):
         ref = oracle.paged_decode(pools[l], bt, lens + 1, q[l].astype(np.float32))
         excess = np.abs(out[l].astype(np.float32) - ref) - (ATOL + RTOL * np.abs(ref))
         assert excess.max() <= 0, l
+
+
+def test_decode_step_28_layers_with_split_contexts(engine, oracle):
+    """adaptive_engine_decode_step at the bench's depth: 28 layers, run in
+    groups of 2, 7, 7, 7, 3 and 2 layers (dependent launches within a group,
+    copies between groups), batch 8 with contexts of 2,048-8,192 tokens so
+    the longer sequences are split over several CTAs; two steps, every
+    layer's output against the oracle and every pool bit for bit."""
+    E, api, tmp = engine
+    L, B = 28, 8
+    lens = kvgen.randint(626, B, 2048, 8192).astype(np.int32)
+    pages = int(((lens + 2 + 15) // 16).sum())
+    E.configure(layers=L, kv_heads=HKV, q_heads=HQ, max_batch=B, pages_per_layer=pages, gpu_layer_slots=L,
+                offload_dir=str(tmp))
+    api.start()
+    E.set_sequences(lens, reserve_tokens=2, seed=627)
+    bt = E.block_table(B)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(628)
+    pools0 = []
+    for l in range(L):
+        p = torch.randn((pages, 2, HKV, 16, 128), generator=g, device="cuda", dtype=torch.float16)
+        E.load_layer(l, p)
+        pools0.append(p)
+    q = kvgen.normal(629, (L, B, HQ, 128)).astype(np.float16)
+    k = kvgen.normal(630, (L, B, HKV, 128)).astype(np.float16)
+    v = kvgen.normal(631, (L, B, HKV, 128)).astype(np.float16)
+    outs = [np.zeros_like(q) for _ in range(2)]
+    for step in range(2):
+        E.decode_step(q, k, v, outs[step])
+    assert [E.lib.adaptive_engine_seq_len(s) for s in range(B)] == list(lens + 2)
+    back = torch.empty_like(pools0[0])
+    for l in range(L):
+        host = pools0[l].cpu().numpy()
+        for step in range(2):
+            pos = (lens + step).astype(np.int32)
+            oracle.append(host, bt, pos, k[l], v[l], 16)
+            ref = oracle.paged_decode(host, bt, pos + 1, q[l].astype(np.float32))
+            excess = np.abs(outs[step][l].astype(np.float32) - ref) - (ATOL + RTOL * np.abs(ref))
+            assert excess.max() <= 0, (step, l, excess.max())
+        E.read_layer(l, back)
+        assert np.array_equal(back.cpu().numpy().view(np.uint16), host.view(np.uint16)), l

@@ -245,6 +245,36 @@ def test_decode_outlier_keys_keep_fp32_query_accuracy(kvx, oracle, hkv, hq):
     assert_close(out, oracle.paged_decode(pool, bt, lens.astype(np.int32), q))
 
 
+@pytest.mark.parametrize("hq", [24, 64])
+def test_decode_dominant_scores_fp16_weights(kvx, oracle, hq):
+    """A few keys aligned with the query take almost all the softmax mass
+    (scores 12, 11.5, 11 against ~N(0,1) for the rest: weights 1, 0.61, 0.37
+    and ~1e-5 each), over values with 1% outliers x20.  The fp16 pool's
+    kernel rounds the softmax weights to fp16 for the P.V mma (relative error
+    2^-11 per weight); the output must still meet the tolerance."""
+    hkv = 8
+    G = hq // hkv
+    lens = kvgen.randint(140 + hq, 8, 300, 4000)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=141)
+    pool = kvgen.normal(142, (num_pages, 2, hkv, 16, 128))
+    vals = pool[:, 1]
+    vals[kvgen.uniform(143, vals.size).reshape(vals.shape) < 0.01] *= 20
+    q = kvgen.normal(144, (lens.size, hq, 128))
+    pick = kvgen.uniform(145, lens.size * hkv * 3).reshape(lens.size, hkv, 3)
+    for s in range(lens.size):
+        for h in range(hkv):
+            qd = q[s, h * G]  # the group's first q-head sets the direction
+            unit = qd / np.linalg.norm(qd)
+            for j, a in enumerate((12.0, 11.5, 11.0)):
+                t = int(pick[s, h, j] * lens[s])
+                page = bt[s, t // 16]
+                # score = q . k / sqrt(128) = a for the direction head
+                pool[page, 0, h, t % 16] = a * np.sqrt(128.0) / np.linalg.norm(qd) * unit
+    pool = pool.astype(np.float16)
+    out = kvx.decode(dev(pool), dev(bt), dev(lens.astype(np.int32)), dev(q)).cpu().numpy()
+    assert_close(out, oracle.paged_decode(pool, bt, lens.astype(np.int32), q))
+
+
 def test_decode_gqa_grouping_matches_mha_expansion(kvx):
     """Property: GQA with group G equals MHA on a pool whose kv heads are
     repeated G times."""

@@ -32,8 +32,8 @@ def kvx():
     return k
 
 
-def noalloc(kvx, pool, bt, lens, q, out, err):
-    kv = kvx.paged(pool)
+def noalloc(kvx, pool, bt, lens, q, out, err, stats=None):
+    kv = kvx.paged(pool, stats)
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     return kvx.lib.kvx_decode_noalloc(
         C.byref(kv), C.c_void_p(bt.data_ptr()), bt.shape[1], C.c_void_p(lens.data_ptr()),
@@ -42,26 +42,73 @@ def noalloc(kvx, pool, bt, lens, q, out, err):
         C.c_void_p(err.data_ptr()), stream)
 
 
-@pytest.mark.parametrize("io", ["f16", "f32"])
-def test_noalloc_matches_allocating_decode_twice(kvx, io):
-    lens = kvgen.randint(515, 32, 512, 8192).astype(np.int32)
-    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=516)
-    dtype = torch.float16 if io == "f16" else torch.float32
+# (pool dtype, q/out dtype, batch, q-heads, context range, seed)
+CASES = {
+    # the library's own chunk choice already fits the scratch
+    "f16-pool-f16-io": ("f16", torch.float16, 32, 24, (512, 8192), 515),
+    "f16-pool-f32-io": ("f16", torch.float32, 32, 24, (512, 8192), 525),
+    # 4096 rows of GQA-16 over contexts up to 16K tokens: the scratch holds 3
+    # splits per row, so its floor (344 pages) overrides the chunk choice and
+    # the CTAs run longer than the block-table slice they stage
+    "f16-pool-scratch-bound": ("f16", torch.float16, 32, 128, (12288, 16384), 535),
+    # fp32 pools take the SIMT kernel, whose chunks are short: the floor binds
+    "f32-pool-scratch-bound": ("f32", torch.float32, 32, 24, (4096, 8192), 545),
+    # int8 pools with per-block statistics
+    "i8-pool": ("i8", torch.float16, 32, 24, (512, 8192), 555),
+}
+
+
+def make_case(case):
+    kind, qdt, batch, hq, (lo, hi), seed = CASES[case]
+    lens = kvgen.randint(seed, batch, lo, hi).astype(np.int32)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 0, seed=seed + 1)
     g = torch.Generator(device="cuda")
-    g.manual_seed(517)
-    pool = torch.randn((num_pages, 2, 8, 16, 128), generator=g, device="cuda", dtype=torch.float16)
-    q = torch.randn((32, 24, 128), generator=g, device="cuda", dtype=dtype)
-    bt_d = torch.from_numpy(bt).cuda()
-    lens_d = torch.from_numpy(lens).cuda()
-    want = kvx.decode(pool, bt_d, lens_d, q).float().cpu().numpy()
+    g.manual_seed(seed + 2)
+    shape = (num_pages, 2, 8, 16, 128)
+    stats = None
+    if kind == "i8":
+        pool = torch.randint(-128, 128, shape, generator=g, device="cuda", dtype=torch.int8)
+        lo_v = torch.randn((num_pages, 2, 8), generator=g, device="cuda") - 2.0
+        scale = torch.rand((num_pages, 2, 8), generator=g, device="cuda") * 0.03 + 1e-3
+        stats = torch.stack([lo_v, lo_v + 255 * scale, scale, lo_v], dim=-1).contiguous()
+    else:
+        pool = torch.randn(shape, generator=g, device="cuda",
+                           dtype=torch.float16 if kind == "f16" else torch.float32)
+    q = torch.randn((batch, hq, 128), generator=g, device="cuda", dtype=qdt)
+    return pool, stats, torch.from_numpy(bt).cuda(), torch.from_numpy(lens).cuda(), q
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_noalloc_matches_allocating_decode_twice(kvx, case):
+    pool, stats, bt_d, lens_d, q = make_case(case)
+    want = kvx.decode(pool, bt_d, lens_d, q, stats=stats).float().cpu().numpy()
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     for call in range(2):
         out = torch.full_like(q, float("nan"))
-        assert noalloc(kvx, pool, bt_d, lens_d, q, out, err) == 0
+        assert noalloc(kvx, pool, bt_d, lens_d, q, out, err, stats) == 0
         torch.cuda.synchronize()
         got = out.float().cpu().numpy()
         excess = np.abs(got - want) - (ATOL + RTOL * np.abs(want))
         assert excess.max() <= 0, f"call {call}: max excess {excess.max():.3e}"
+    assert err.item() == 0
+
+
+def test_noalloc_allocates_nothing(kvx):
+    """A warm call changes neither torch's allocator nor the device's free
+    memory (cudaMemGetInfo)."""
+    pool, stats, bt_d, lens_d, q = make_case("f16-pool-scratch-bound")
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert noalloc(kvx, pool, bt_d, lens_d, q, out, err) == 0  # first call: address lookup
+    torch.cuda.synchronize()
+    torch_before = torch.cuda.memory_allocated()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert noalloc(kvx, pool, bt_d, lens_d, q, out, err) == 0
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == torch_before
+    assert free_after == free_before
     assert err.item() == 0
 
 
