@@ -104,6 +104,13 @@ int Engine::set_comm(int rank, int world, const void *id128) {
     return KVX_OK;
 }
 
+int Engine::set_readback_share(int share) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (share != 0 && share != 1) return KVX_EINVAL;
+    readback_share_ = share == 1;
+    return KVX_OK;
+}
+
 Engine &Engine::instance() {
     static Engine *e = new Engine();  // lives until exit; never destroyed mid-call
     return *e;
@@ -211,6 +218,7 @@ void Engine::release_all() {
     comm_ = nullptr;
     world_ = 1;
     rank_ = 0;
+    readback_share_ = false;
     for (auto &e : ev_gath_) if (e) cudaEventDestroy(e);
     ev_gath_.clear();
     if (d_gather_) cudaFree(d_gather_);
@@ -808,11 +816,16 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                     rc == KVX_OK)
                     rc = KVX_ECUDA;
             if (rc == KVX_OK && cudaEventRecord(ev_gath_[gi], comm_stream_)) rc = KVX_ECUDA;
-            if (rc == KVX_OK && out &&
-                (cudaStreamWaitEvent(copy_, ev_gath_[gi], 0) ||
-                 cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
-                                 (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_)))
+            if (rc == KVX_OK && out && cudaStreamWaitEvent(copy_, ev_gath_[gi], 0)) rc = KVX_ECUDA;
+            if (rc == KVX_OK && out && !readback_share_ &&
+                cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
+                                (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
                 rc = KVX_ECUDA;
+            for (int l = l0; rc == KVX_OK && out && readback_share_ && l < l1; ++l)
+                if (l % world_ == rank_ &&
+                    cudaMemcpyAsync(out + (size_t)l * world_ * qrow, d_gather_ + (size_t)l * world_ * qrow,
+                                    (size_t)world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
+                    rc = KVX_ECUDA;
         } else if (rc == KVX_OK && out) {
             if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) rc = KVX_ECUDA;
             if (packed) {

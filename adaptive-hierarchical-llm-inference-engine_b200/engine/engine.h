@@ -72,6 +72,7 @@ public:
     int32_t seq_len(int s);
     int copy_layer(int layer, void *ptr, bool load);
     int set_comm(int rank, int world, const void *id128);
+    int set_readback_share(int share);
     int32_t block_table(int32_t *dst);
     long long device_bytes();
 
@@ -129,6 +130,7 @@ private:
     int world_ = 1, rank_ = 0;
     cudaStream_t comm_stream_ = nullptr;
     uint16_t *d_gather_ = nullptr;
+    bool readback_share_ = false;  // each rank reads back layers l % world == rank only
     std::vector<cudaEvent_t> ev_gath_;
 };
 

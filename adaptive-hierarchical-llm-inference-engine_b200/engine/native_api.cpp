@@ -79,6 +79,10 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const v
     return Engine::instance().set_comm(rank, world, id128);
 }
 
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_readback_share(int share) {
+    return Engine::instance().set_readback_share(share);
+}
+
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_block_table(int32_t *dst) {
     return Engine::instance().block_table(dst);
 }

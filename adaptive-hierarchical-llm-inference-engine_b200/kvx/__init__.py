@@ -59,6 +59,8 @@ lib.kvx_status_string.restype = C.c_char_p
 lib.kvx_status_string.argtypes = [C.c_int]
 lib.kvx_device_check.restype = C.c_int
 lib.kvx_append.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp]
+lib.kvx_append_chunk.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]
+lib.kvx_append_chunk.restype = C.c_int
 lib.kvx_decode_workspace_bytes.restype = _sz
 lib.kvx_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32]
 lib.kvx_decode.argtypes = [C.POINTER(KvPaged), _vp, _i32, _vp, _i32, _i32, _vp, _vp, _i32, _f32,
@@ -160,6 +162,16 @@ def append(pool, block_table, positions, new_k, new_v, error_flag=None, stream=N
                         positions.shape[0], _ptr(new_k), _ptr(new_v), _ptr(error_flag),
                         _stream(stream))
     _check("kvx_append", rc)
+
+
+def append_chunk(pool, block_table, positions, new_k, new_v, error_flag=None, stream=None):
+    """Append new_k / new_v [batch][n_new][hkv][128] at positions[s] ..
+    positions[s] + n_new - 1 of each sequence."""
+    kv = paged(pool)
+    batch, n_new = new_k.shape[0], new_k.shape[1]
+    rc = lib.kvx_append_chunk(C.byref(kv), _ptr(block_table), block_table.shape[1], _ptr(positions), batch,
+                              n_new, _ptr(new_k), _ptr(new_v), _ptr(error_flag), _stream(stream))
+    _check("kvx_append_chunk", rc)
 
 
 def decode_workspace_bytes(batch, num_q_heads, max_pages):

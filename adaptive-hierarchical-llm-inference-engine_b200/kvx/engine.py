@@ -57,6 +57,9 @@ lib.adaptive_engine_nccl_unique_id.restype = C.c_int
 lib.adaptive_engine_set_comm.argtypes = [C.c_int, C.c_int, C.c_void_p]
 lib.adaptive_engine_set_comm.restype = C.c_int
 
+lib.adaptive_engine_set_readback_share.argtypes = [C.c_int]
+lib.adaptive_engine_set_readback_share.restype = C.c_int
+
 TIERS = {0: "GPU", 1: "RAM", 2: "COMPRESSED", 3: "OFFLOADED"}
 
 
@@ -147,3 +150,10 @@ def set_comm(rank: int, world: int, uid: bytes):
     rc = lib.adaptive_engine_set_comm(rank, world, buf)
     if rc != 0:
         raise KvxError("adaptive_engine_set_comm", rc)
+
+
+def set_readback_share(share: bool):
+    """Multi-GPU read-back: each rank copies back only layers l % world == rank."""
+    rc = lib.adaptive_engine_set_readback_share(1 if share else 0)
+    if rc != 0:
+        raise KvxError("adaptive_engine_set_readback_share", rc)

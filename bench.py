@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check after the timed region")
+    ap.add_argument("--no-append-compress", action="store_true", help="skip the append / compressKv measurement")
+    ap.add_argument("--no-config5", action="store_true", help="skip the 70B-geometry workload")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (profiling of a smaller case; the metric is defined at 28)")
     ap.add_argument("--pages", type=int, default=1 << 20,
@@ -239,10 +241,15 @@ class ParitySample:
         from kvx import pool_tensor
         return pool_tensor(view)
 
-    def verify(self, q, nk, nv, total_steps, last_out, gathered, dist):
+    def verify(self, q, nk, nv, positions, last_out, gathered, dist):
+        """positions: [steps][batch] (host or device) -- every step's append
+        position per sequence, in order; last_out: this rank's rows of the
+        last step."""
         import torch
         from oracle import Oracle
         o = Oracle()
+        positions = positions.cpu().numpy() if hasattr(positions, "cpu") else np.asarray(positions)
+        total_steps = positions.shape[0]
         rows = 0
         excess = -np.inf
         pool_ok = True
@@ -254,11 +261,11 @@ class ParitySample:
                 host = self.before[(l, s)].copy()
                 bt1 = np.arange(pages.size, dtype=np.int32)[None, :]
                 for k in range(total_steps):
-                    pos = np.array([self.lens0[s] + k], np.int32)
+                    pos = positions[k, s:s + 1].astype(np.int32)
                     o.append(host, bt1, pos, k_l[s:s + 1], v_l[s:s + 1], 16)
                 dev = pool[torch.from_numpy(pages.astype(np.int64)).cuda()].cpu().numpy()
                 pool_ok = pool_ok and np.array_equal(dev.view(np.uint16), host.view(np.uint16))
-                T = np.array([self.lens0[s] + total_steps], np.int32)
+                T = positions[-1, s:s + 1].astype(np.int32) + 1
                 ref = o.paged_decode(host, bt1, T, q_l[s:s + 1])
                 got = last_out[l, s:s + 1].float().cpu().numpy()
                 excess = max(excess, float((np.abs(got - ref) - (self.ATOL + self.RTOL * np.abs(ref))).max()))
@@ -288,8 +295,152 @@ class ParitySample:
                 "max_excess": round(excess, 6), "tolerance": "|gpu - oracle| <= 1e-2 + 1e-3 |oracle|",
                 "pool_pages_bitexact": bool(pool_ok), "gather_slot_mismatches": gather_mismatch,
                 "sample": f"layers {list(self.layers)} x sequences {list(map(int, self.seqs))} per rank "
-                          f"(all {self.hq} local q-heads), {total_steps} appended tokens each",
+                          f"(all {self.hq} local q-heads), {total_steps} appends each",
                 "oracle": "C restatement of the reference's save_page + TensorOps::attention"}
+
+
+# --------------------------------------------------------------------------
+APPEND_CHUNK = 256      # tokens each sequence appends per layer in the append measurement
+COMPRESS_PAGES = 1 << 20  # the compressKv sweep's pages (16 tokens x 8 KV heads x 128, fp16)
+
+
+def _max_over_ranks(ms, dist):
+    import torch
+    if dist is None:
+        return ms
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def _timed_events(fn, iters, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def run_append_compress(world, rank, hkv, dist=None, compress_pages=COMPRESS_PAGES, layers=None, check=True):
+    """The metric's second half: append tokens/s and compressKv tokens/s.
+
+    Append (KVManager::save_page per token, cache/kv_cache.cpp:111-127): each
+    of 32 x N sequences appends a chunk of 256 tokens, starting at a seeded
+    offset inside a page, into every one of the 28 layers' pools (this rank's
+    KV heads, randomly permuted pages); one kvx_append_chunk launch per layer.
+    A token is one sequence position of one layer (its K and V rows of every
+    KV head, split over the ranks), so the job's tokens grow with N (weak
+    scaling, as the decode).  Bytes per token and rank: 2 x hkv x 256 B read
+    and the same written.
+
+    Compress (KVCompressionEngine::compressToINT8, native-engine/cpp/
+    KVCompressionEngine.cpp:83-113, one call per (page, head) block of 2048
+    elements): the 1,048,576 pages x 16 tokens x 8 KV heads x 128 fp16 of the
+    compressKv sweep (N(0,1), 1% of elements x20), each rank compressing its
+    8/N heads of every page (strong scaling: the job is fixed).  A token is
+    one of the 16 rows of a page.  Bytes per (page, head) block: 4 KiB read,
+    2 KiB + 16 B written.
+
+    Both are timed with CUDA events over several launches (max over ranks)
+    and checked against the oracle on a sample: appended pages bit for bit,
+    codes and QuantizationStats bit for bit."""
+    import torch
+    import kvx
+    L = LAYERS if layers is None else layers
+    peak, peak_kind = peaks()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 31 + rank)
+    res = {}
+    # ---- append
+    B, n = BATCH * world, APPEND_CHUNK
+    slices = n // PT + 1
+    starts_np = kvgen.randint(SEED + 32, B, 0, PT - 1).astype(np.int32)
+    pages = B * slices
+    perm = kvgen.permutation(SEED + 33, pages).astype(np.int32)
+    bt_np = perm.reshape(B, slices)
+    bt = torch.from_numpy(bt_np).cuda()
+    starts = torch.from_numpy(starts_np).cuda()
+    pools = [torch.zeros((pages, 2, hkv, PT, DIM), device="cuda", dtype=torch.float16) for _ in range(L)]
+    rows_k = [torch.randn((B, n, hkv, DIM), generator=g, device="cuda", dtype=torch.float16) for _ in range(L)]
+    rows_v = [torch.randn((B, n, hkv, DIM), generator=g, device="cuda", dtype=torch.float16) for _ in range(L)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def append_all():
+        for l in range(L):
+            kvx.append_chunk(pools[l], bt, starts, rows_k[l], rows_v[l], error_flag=err)
+
+    if dist is not None:
+        dist.barrier()
+    ms = _max_over_ranks(_timed_events(append_all, 10), dist)
+    tok_rank_bytes = 2 * hkv * DIM * 2 * 2  # K and V rows read + written
+    launch_ms = ms / L
+    per_launch_bytes = B * n * tok_rank_bytes
+    app = {"tokens_per_s": round(B * n * L / (ms / 1e3), 1), "unit": "tokens/s",
+           "token": "one sequence position of one layer (K and V rows of all 8 KV heads, over the ranks)",
+           "sequences": B, "chunk_tokens": n, "layers": L, "ms_per_step": round(ms, 4),
+           "scaling": "weak (32 sequences per GPU)",
+           "roofline": {"bound": "hbm", "achieved": round(per_launch_bytes / (launch_ms / 1e3) / 1e9, 1),
+                        "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                        "frac": round(per_launch_bytes / (launch_ms / 1e3) / 1e9 / peak, 4),
+                        "kernel": "append_chunk_kernel", "mean_launch_us": round(launch_ms * 1e3, 2),
+                        "bytes_per_launch": per_launch_bytes}}
+    assert err.item() == 0, f"append error flag {err.item()}"
+    if check:
+        from oracle import Oracle
+        o = Oracle()
+        host = np.zeros((pages, 2, hkv, PT, DIM), np.float16)
+        rk, rv = rows_k[0].cpu().numpy(), rows_v[0].cpu().numpy()
+        for t in range(n):
+            o.append(host, bt_np, starts_np + t, rk[:, t], rv[:, t], 16)
+        app["parity"] = {"layer0_pool_bitexact": bool(np.array_equal(pools[0].cpu().numpy().view(np.uint16),
+                                                                     host.view(np.uint16))),
+                         "oracle": "KVManager::save_page per token (C restatement)"}
+    del pools, rows_k, rows_v
+    torch.cuda.empty_cache()
+    res["append"] = app
+    # ---- compress: this rank's KV heads of every page, [pages][hkv] blocks
+    blocks = compress_pages * hkv
+    x = torch.empty((blocks, PT * DIM), device="cuda", dtype=torch.float16)
+    for c in range(0, blocks, 1 << 20):
+        part = torch.randn((min(1 << 20, blocks - c), PT * DIM), generator=g, device="cuda")
+        part[torch.rand(part.shape, generator=g, device="cuda") < 0.01] *= 20.0
+        x[c:c + part.shape[0]] = part.half()
+        del part
+    codes = torch.empty((blocks, PT * DIM), device="cuda", dtype=torch.int8)
+    stats = torch.empty((blocks, 4), device="cuda", dtype=torch.float32)
+    if dist is not None:
+        dist.barrier()
+    ms = _max_over_ranks(_timed_events(lambda: kvx.compress_int8(x, codes=codes, stats=stats), 5), dist)
+    nbytes = blocks * (PT * DIM * 3 + 16)
+    comp = {"tokens_per_s": round(compress_pages * PT / (ms / 1e3), 1), "unit": "tokens/s",
+            "token": "one of a page's 16 rows (8 KV heads x 128 fp16, over the ranks)",
+            "pages": compress_pages, "blocks_per_gpu": blocks, "ms": round(ms, 4),
+            "scaling": "strong (the 1,048,576 pages split by KV head)",
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms / 1e3) / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "peak_kind": peak_kind,
+                         "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4), "kernel": "compress_2048_kernel",
+                         "bytes_per_launch": nbytes}}
+    if check:
+        from oracle import Oracle
+        o = Oracle()
+        pick = np.sort(np.random.default_rng(SEED + 34).choice(blocks, size=64, replace=False))
+        idx = torch.from_numpy(pick).cuda()
+        rc, rs = o.compress_int8_blocks(x[idx].cpu().numpy(), PT * DIM)
+        comp["parity"] = {"blocks_checked": int(pick.size),
+                          "codes_bitexact": bool(np.array_equal(codes[idx].cpu().numpy().ravel(), rc.ravel())),
+                          "stats_bitexact": bool(np.array_equal(stats[idx].cpu().numpy().view(np.uint32).ravel(),
+                                                                rs.view(np.uint32).ravel())),
+                          "oracle": "KVCompressionEngine::compressToINT8 per block (C restatement)"}
+    del x, codes, stats
+    torch.cuda.empty_cache()
+    res["compress"] = comp
+    return res
 
 
 # --------------------------------------------------------------------------
@@ -382,7 +533,7 @@ def run_ours(args):
     parity = None
     if check is not None:  # outside the timed region, before anything else writes the pools
         last = outs[(total_steps - 1) % ring]
-        parity = check.verify(q, nk, nv, total_steps, last, gathered, dist if world > 1 else None)
+        parity = check.verify(q, nk, nv, positions, last, gathered, dist if world > 1 else None)
 
     lens_timed = [lens0 + warm + k + 1 for k in range(steps)]
     rank_bytes = sum(kv_bytes(L) * LAYERS for L in lens_timed)
@@ -432,6 +583,9 @@ def run_ours(args):
     }
     if world > 1:
         result["config"]["gather_sync"] = step.gather_sync
+    del outs, gathered, ws, check
+    if not args.no_append_compress:
+        result["append_compress"] = run_append_compress(world, rank, hkv, dist if world > 1 else None)
     if not args.no_e2e:
         result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
         torch.cuda.synchronize()
@@ -439,12 +593,17 @@ def run_ours(args):
             result["engine_ops"] = run_engine_ops(api, need_pages * 2 * hkv * PT * DIM * 2)
     if world > 1:
         dist.barrier()
+    api.stop()
+    del views
+    torch.cuda.empty_cache()
+    if not args.no_config5:
+        result["config5_70b"] = run_config5_sharded(args, world, rank, dist if world > 1 else None)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(sample_layers=LAYERS, min_seconds=10.0)
         print(json.dumps(result), flush=True)
-    api.stop()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -486,8 +645,12 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
     h_q = torch.randn((LAYERS, B, hq, DIM), dtype=torch.float16).pin_memory()
     h_k = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
     h_v = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
-    # one copy of the gathered result comes back to the host (rank 0)
-    h_o = torch.empty((LAYERS, world, B, hq, DIM), dtype=torch.float16).pin_memory() if rank == 0 else None
+    # the gathered result comes back to the host once per step: with several
+    # GPUs each rank reads back its share of the layers (l % N == rank) over
+    # its own host link
+    h_o = torch.empty((LAYERS, world, B, hq, DIM), dtype=torch.float16).pin_memory()
+    if world > 1:
+        E.set_readback_share(True)
     E.decode_step(h_q, h_k, h_v, h_o)  # warm-up: the engine's sequences start at lens0
     torch.cuda.synchronize()
     if world > 1:
@@ -506,8 +669,8 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
             "h2d_bytes_per_step": int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2),
             "d2h_bytes_per_step": LAYERS * world * B * hq * DIM * 2, "steps": steps,
             "path": "adaptive_engine_decode_step (C ABI) with pinned host buffers" +
-                    (", NCCL all-gather of outputs in the engine, gathered result read back on rank 0"
-                     if world > 1 else "")}
+                    (", NCCL all-gather of outputs in the engine, each rank reading back its share of the "
+                     "gathered layers (d2h bytes summed over ranks)" if world > 1 else "")}
 
 
 # --------------------------------------------------------------------------
@@ -1109,16 +1272,96 @@ def run_shapes(args):
             torch.cuda.empty_cache()
 
 
-def run_config5(args):
+L5_FULL, HQ5, HKV5, B5, T5 = 80, 64, 8, 64, 32768
+
+
+def run_config5_sharded(args, world, rank, dist=None, budget_bytes=150e9):
     """Llama-3-70B KV geometry (80 layers, 64 q-heads, 8 KV heads x 128,
     GQA group 8, fp16), batch 64, 32,768-token contexts, 16-token pages
-    randomly permuted; KV heads sharded over the GPUs with an NCCL
-    all-gather of each layer's output.  The full cache (687 GB) fits only
-    on 8 GPUs; with fewer, each GPU holds its shard of as many layers as fit
-    in ~150 GB and the result is reported per layer and projected to 80."""
+    randomly permuted; KV heads sharded over the N GPUs (8/N heads each),
+    outputs all-gathered over NCCL per group of layers -- the same step as
+    the headline (make_decode_step), each step appending token 32,767 and
+    decoding over 32,768.  The whole cache (687 GB) fits only at N = 8 (86 GB
+    per GPU, all 80 layers); with fewer GPUs each holds its shard of as many
+    layers as fit in ~150 GB and the result is given per layer and projected
+    to 80 (the layers are identical, so a step's time is linear in them).
+    The same fixed job is split N ways (strong scaling per layer)."""
+    import torch
+    import kvx
+    hkv, hq = HKV5 // world, HQ5 // world
+    npg = T5 // PT
+    pages = B5 * npg + B5  # one spare page per sequence
+    layer_bytes = pages * 2 * hkv * PT * DIM * 2
+    free, _ = torch.cuda.mem_get_info()
+    L = int(max(1, min(L5_FULL, min(budget_bytes, free - 12e9) // layer_bytes)))
+    if dist is not None:  # the same layer count on every rank
+        t = torch.tensor([L], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        L = int(t.item())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 5 + 101 * rank)
+    pools = [torch.empty((pages, 2, hkv, PT, DIM), device="cuda", dtype=torch.float16).normal_(generator=g)
+             for _ in range(L)]
+    perm = kvgen.permutation(SEED + 6, pages).astype(np.int32)
+    bt_np = perm[: B5 * (npg + 1)].reshape(B5, npg + 1)
+    bt = torch.from_numpy(bt_np).cuda()
+    lens0 = np.full(B5, T5 - 1, np.int64)  # each step appends token T-1: context T
+    steps = max(3, min(args.steps, 6))
+    warm = 2
+    positions = torch.full((warm + steps, B5), T5 - 1, dtype=torch.int32, device="cuda")
+    q = torch.randn((L, B5, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
+    nk = torch.randn((L, B5, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
+    ring = OUT_RING if world > 1 else 1
+    outs = [torch.empty((L, B5, hq, DIM), device="cuda", dtype=torch.float16) for _ in range(ring)]
+    gathered = torch.empty((L, world * B5, hq, DIM), device="cuda", dtype=torch.float16) if world > 1 else None
+    ws = kvx.decode_workspace(B5, hq, npg + 1)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    comm = torch.cuda.Stream() if world > 1 else None
+    main = torch.cuda.current_stream()
+    check = ParitySample(bt_np, lens0, hkv, hq, world, rank, pools, layers=(0, L - 1), seqs=2) \
+        if not args.no_parity else None
+    step = make_decode_step(kvx, pools, bt, positions, nk, nk, q, ws, err, outs, world=world,
+                            gathered=gathered, comm=comm, dist=dist)
+    for k in range(warm):
+        step(k)
+    if world > 1:
+        main.wait_stream(comm)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(warm, warm + steps):
+        step(k)
+    if world > 1:
+        main.wait_stream(comm)
+    b.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(a.elapsed_time(b) / steps, dist)
+    assert err.item() == 0, f"device error flag {err.item()}"
+    parity = None
+    if check is not None:
+        parity = check.verify(q, nk, nk, positions, outs[(warm + steps - 1) % ring], gathered, dist)
+    kv_rank = B5 * T5 * 2 * hkv * DIM * 2 * L  # bytes one rank reads per step
+    peak, peak_kind = peaks()
+    res = {"workload": "Llama-3-70B KV (80L, 64q/8kv x128, G8), fp16, B64, ctx 32768, permuted pages",
+           "layers_resident": L, "layers_full": L5_FULL, "kv_heads_per_gpu": hkv,
+           "ms_per_step": round(ms, 3), "ms_per_layer": round(ms / L, 4),
+           "projected_80_layer_step_ms": round(ms / L * L5_FULL, 2),
+           "value": round(kv_rank * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "per_gpu_frac_of_peak": round(kv_rank / (ms / 1e3) / 1e9 / peak, 4), "peak": peak,
+           "peak_kind": peak_kind, "scaling": "strong per layer (the 8 KV heads split over the GPUs)",
+           "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+           "parity": parity}
+    del pools, outs, gathered, ws, q, nk
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_config5(args):
+    """Config 5 alone (see run_config5_sharded); one JSON line from rank 0."""
     import torch
     import torch.distributed as dist
-    import kvx
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1127,63 +1370,8 @@ def run_config5(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    L_FULL, HQ5, HKV5, B5, T5 = 80, 64, 8, 64, 32768
-    hkv, hq = HKV5 // world, HQ5 // world
-    npg = T5 // PT
-    pages = B5 * npg + B5  # room for one more page per sequence
-    layer_bytes = pages * 2 * hkv * PT * DIM * 2
-    L = min(L_FULL, int(150e9 // layer_bytes))
-    g = torch.Generator(device="cuda")
-    g.manual_seed(SEED + 5)
-    pools = [torch.empty((pages, 2, hkv, PT, DIM), device="cuda", dtype=torch.float16).normal_(generator=g)
-             for _ in range(L)]
-    perm = torch.randperm(pages, generator=torch.Generator().manual_seed(SEED + 6)).to(torch.int32)
-    bt = perm[: B5 * (npg + 1)].view(B5, npg + 1).cuda()
-    pos = torch.full((B5,), T5 - 1, dtype=torch.int32, device="cuda")  # appends token T-1: context T
-    q = torch.randn((B5, hq, DIM), generator=g, device="cuda", dtype=torch.float16)
-    nk = torch.randn((B5, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
-    out = torch.empty((L, B5, hq, DIM), device="cuda", dtype=torch.float16)
-    gathered = torch.empty((L, world * B5, hq, DIM), device="cuda", dtype=torch.float16) if world > 1 else None
-    ws = kvx.decode_workspace(B5, hq, npg + 1)
-    comm = torch.cuda.Stream() if world > 1 else None
-    done = [torch.cuda.Event() for _ in range(L)]
-
-    def step():
-        for l in range(L):
-            kvx.append_decode(pools[l], bt, pos, nk, nk, q, out=out[l], workspace=ws)
-            if world > 1:
-                done[l].record()
-                with torch.cuda.stream(comm):
-                    comm.wait_event(done[l])
-                    dist.all_gather_into_tensor(gathered[l], out[l])
-        if world > 1:
-            torch.cuda.current_stream().wait_stream(comm)
-
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    steps = max(2, min(args.steps, 5))
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    kv = B5 * T5 * 2 * hkv * DIM * 2 * L  # bytes one rank reads per step
-    peak, peak_kind = peaks()
-    res = {"config": 5, "workload": "Llama-3-70B KV (80L, 64q/8kv x128, G8), fp16, B64, ctx 32768, permuted pages",
-           "n_gpus": world, "layers_resident": L, "ms_per_step": round(ms, 3),
-           "ms_per_layer": round(ms / L, 4), "projected_80_layer_step_ms": round(ms / L * L_FULL, 2),
-           "value": round(kv * world / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
-           "per_gpu_frac_of_peak": round(kv / (ms / 1e3) / 1e9 / peak, 3), "peak": peak, "peak_kind": peak_kind,
-           "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else "")}
+    res = run_config5_sharded(args, world, rank, dist if world > 1 else None)
+    res.update({"config": 5, "n_gpus": world})
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

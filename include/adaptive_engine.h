@@ -131,6 +131,13 @@ ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_block_table(int32_t *dst);
  * Return kvx_status (KVX_EUNSUPPORTED if NCCL cannot be loaded). */
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_nccl_unique_id(void *id128);
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const void *id128);
+/* Read-back of a multi-GPU decode step.  share = 0 (the default): `out`
+ * receives every layer's gathered rows on each rank that passes it.
+ * share = 1: rank r copies back only the layers l with l % world == r into
+ * their place in `out`, so the ranks together read the step's result once
+ * and the copies spread over every GPU's host link instead of one.  No
+ * effect without a communicator.  Returns a kvx_status. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_readback_share(int share);
 /* Current context length of sequence s (-1 if none). */
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_seq_len(int32_t s);
 /* Tier of layer l: 0 GPU, 1 RAM, 2 COMPRESSED (int8 on device),

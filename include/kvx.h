@@ -76,6 +76,20 @@ KVX_API int kvx_append(const kvx_paged *kv, const int32_t *block_table, int32_t 
                        const int32_t *positions, int32_t batch, const void *new_k,
                        const void *new_v, int32_t *error_flag, void *stream);
 
+/* Chunked paged append: sequence s appends n_new consecutive tokens at
+ * positions[s] .. positions[s] + n_new - 1, token t going to physical page
+ * block_table[s*max_pages + t/16], slot t % 16 (a prefill chunk, or a step
+ * that appends several tokens).  Replaces the per-token KVManager::save_page
+ * calls (cache/kv_cache.cpp:111-127) of InferenceController::appendKVPage
+ * (runtime/inference.cpp:50-54) for a run of tokens.  new_k/new_v:
+ * [batch][n_new][num_kv_heads][128] in the pool's dtype (KVX_F16 or
+ * KVX_F32), 16-token pages, head_dim 128.  Bit-exact copy.  A negative
+ * position, or a page outside the block table or pool, skips those rows
+ * and sets bit 1 of *error_flag (may be NULL). */
+KVX_API int kvx_append_chunk(const kvx_paged *kv, const int32_t *block_table, int32_t max_pages,
+                             const int32_t *positions, int32_t batch, int32_t n_new,
+                             const void *new_k, const void *new_v, int32_t *error_flag, void *stream);
+
 /* Bytes of scratch kvx_decode / kvx_append_decode need: split-K partial
  * results plus one arrival counter per (sequence, q-head). */
 KVX_API size_t kvx_decode_workspace_bytes(int32_t batch, int32_t num_q_heads, int32_t max_pages,

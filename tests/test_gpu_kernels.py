@@ -56,6 +56,44 @@ def test_append_bitexact(kvx, oracle, np_dtype):
     assert err.item() == 0
 
 
+@pytest.mark.parametrize("np_dtype", [np.float32, np.float16])
+@pytest.mark.parametrize("n_new", [1, 5, 16, 17, 100, 256])
+def test_append_chunk_bitexact(kvx, oracle, np_dtype, n_new):
+    """A chunk of n_new tokens per sequence from ragged start positions
+    (page starts, mid-page, page ends) equals n_new single-token appends of
+    the oracle (KVManager::save_page per token)."""
+    start = np.array([0, 1, 15, 16, 31, 100, 7, 250], np.int64)
+    bt, num_pages = kvgen.paged_layout(start, 16, n_new, seed=97 + n_new)
+    hkv = 8
+    pool = kvgen.normal(98, (num_pages, 2, hkv, 16, 128)).astype(np_dtype)
+    nk = kvgen.normal(99, (start.size, n_new, hkv, 128)).astype(np_dtype)
+    nv = kvgen.normal(100, (start.size, n_new, hkv, 128)).astype(np_dtype)
+    g_pool = dev(pool)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kvx.append_chunk(g_pool, dev(bt), dev(start.astype(np.int32)), dev(nk), dev(nv), error_flag=err)
+    for t in range(n_new):
+        oracle.append(pool, bt, (start + t).astype(np.int32), nk[:, t], nv[:, t], 16)
+    assert np.array_equal(g_pool.cpu().numpy().view(np.uint8), pool.view(np.uint8))
+    assert err.item() == 0
+
+
+def test_append_chunk_out_of_range_rows_are_reported_not_written(kvx):
+    """Rows past the block table (or of a negative start) are skipped and
+    flagged; the rows that fit are written."""
+    bt = np.array([[0, 1], [2, -1]], np.int32)
+    pool = torch.zeros((3, 2, 1, 16, 128), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rows = torch.ones((2, 20, 1, 128), dtype=torch.float16, device="cuda")
+    kvx.append_chunk(pool, dev(bt), dev(np.array([20, 10], np.int32)), rows, rows, error_flag=err)
+    torch.cuda.synchronize()
+    assert err.item() & 2
+    # sequence 0: tokens 20..31 land in page 1 (12 rows), 32..39 have no page
+    assert int(pool[1, :, 0, 4:].sum().item()) == 2 * 12 * 128 and int(pool[1, :, 0, :4].abs().sum().item()) == 0
+    # sequence 1: tokens 10..15 land in page 2, 16..29 have no page
+    assert int(pool[2, :, 0, 10:].sum().item()) == 2 * 6 * 128 and int(pool[2, :, 0, :10].abs().sum().item()) == 0
+    assert int(pool[0].abs().sum().item()) == 0
+
+
 def test_append_out_of_range_is_reported_not_written(kvx):
     bt = np.array([[0, 1]], np.int32)
     pool = torch.zeros((2, 2, 1, 16, 128), dtype=torch.float16, device="cuda")

@@ -119,7 +119,7 @@ def test_bench_parity_sample_passes_on_a_correct_run(kvx):
     for k in range(STEPS):
         step(k)
     torch.cuda.synchronize()
-    res = check.verify(q, nk, nv, STEPS, outs[0], None, None)
+    res = check.verify(q, nk, nv, positions, outs[0], None, None)
     assert res["ok"] and res["pool_pages_bitexact"] and res["rows_checked"] == 3 * 4 * HQ, res
 
 
