@@ -60,6 +60,12 @@ append_chunk_kernel(uint8_t *pool, const uint8_t *new_k, const uint8_t *new_v,
     constexpr int kRowBytes = kRowVecs * 16;
     constexpr int kRowsPerOp = 32 / kRowVecs;          // rows one warp instruction covers
     constexpr int kOps = (kPageTokens + kRowsPerOp - 1) / kRowsPerOp;
+    // Dependent launch: the next launch on the stream may be scheduled now,
+    // and this grid touches memory only once the previous one has finished
+    // (it may have written the rows or the pool), so back-to-back appends
+    // keep their order and lose only the launch gap.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const long long run = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const long long runs = (long long)batch * slices * 2 * hkv;
@@ -123,17 +129,27 @@ extern "C" KVX_API int kvx_append_chunk(const kvx_paged *kv, const int32_t *bloc
     const long long runs = (long long)batch * slices * 2 * kv->num_kv_heads;
     const long long blocks = (runs + 7) / 8;
     if (blocks > 0x7fffffffLL) return KVX_EINVAL;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto *pool = static_cast<uint8_t *>(kv->pool);
     auto *k = static_cast<const uint8_t *>(new_k), *v = static_cast<const uint8_t *>(new_v);
-    if (kv->dtype == KVX_F16)
-        append_chunk_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(pool, k, v, block_table, positions, error_flag, batch,
-                                                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages,
-                                                                 slices);
-    else
-        append_chunk_kernel<32><<<(unsigned)blocks, 256, 0, st>>>(pool, k, v, block_table, positions, error_flag, batch,
-                                                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages,
-                                                                 slices);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e =
+        kv->dtype == KVX_F16
+            ? cudaLaunchKernelEx(&cfg, append_chunk_kernel<16>, pool, k, v, block_table, positions, error_flag, batch,
+                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages, slices)
+            : cudaLaunchKernelEx(&cfg, append_chunk_kernel<32>, pool, k, v, block_table, positions, error_flag, batch,
+                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages, slices);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return KVX_ECUDA;
+    }
     return launch_status();
 }
 

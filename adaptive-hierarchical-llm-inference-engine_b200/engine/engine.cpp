@@ -66,6 +66,17 @@ const Nccl &nccl() {
     return n;
 }
 
+// The moves' stream at the device's highest priority: a running decode step
+// keeps a grid pending at all times (dependent launches), so a move kernel
+// (int8 compress / decompress) on a default-priority stream would get SMs
+// only after the whole step; at high priority its CTAs are dispatched as the
+// decode's CTAs retire.
+bool create_move_stream(cudaStream_t *st) {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) greatest = 0;
+    return cudaStreamCreateWithPriority(st, cudaStreamNonBlocking, greatest) == cudaSuccess;
+}
+
 }  // namespace
 
 int nccl_unique_id(void *id128) {
@@ -78,7 +89,8 @@ int nccl_unique_id(void *id128) {
 }
 
 int Engine::set_comm(int rank, int world, const void *id128) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !step_active_; });
     if (!started_ || world < 1 || rank < 0 || rank >= world || !id128) return KVX_EINVAL;
     const Nccl &n = nccl();
     if (!n.ok) return KVX_EUNSUPPORTED;
@@ -105,7 +117,8 @@ int Engine::set_comm(int rank, int world, const void *id128) {
 }
 
 int Engine::set_readback_share(int share) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !step_active_; });
     if (share != 0 && share != 1) return KVX_EINVAL;
     readback_share_ = share == 1;
     return KVX_OK;
@@ -132,6 +145,13 @@ void Engine::default_config(adaptive_engine_config *cfg) const {
     cfg->device = dev ? atoi(dev) : 0;
     const char *dir = getenv("ADAPTIVELLM_KV_OFFLOAD_DIR");
     snprintf(cfg->offload_dir, sizeof(cfg->offload_dir), "%s", dir && *dir ? dir : "/tmp");
+    cfg->ram_layer_slots = env_int("ADAPTIVELLM_KV_RAM_LAYERS", cfg->layers);
+    cfg->int8_layer_slots = env_int("ADAPTIVELLM_KV_INT8_LAYERS", cfg->layers);
+}
+
+int Engine::step_in_flight() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return step_active_ ? 1 : 0;
 }
 
 int Engine::configure(const adaptive_engine_config &cfg) {
@@ -139,7 +159,8 @@ int Engine::configure(const adaptive_engine_config &cfg) {
     if (started_) return KVX_EBUSY;
     if (cfg.layers <= 0 || cfg.kv_heads <= 0 || cfg.q_heads <= 0 || cfg.q_heads % cfg.kv_heads ||
         cfg.head_dim != 128 || cfg.page_tokens != 16 || cfg.max_batch <= 0 || cfg.pages_per_layer <= 0 ||
-        cfg.gpu_layer_slots <= 0 || cfg.gpu_layer_slots > cfg.layers)
+        cfg.gpu_layer_slots <= 0 || cfg.gpu_layer_slots > cfg.layers || cfg.ram_layer_slots < 0 ||
+        cfg.int8_layer_slots < 0)
         return KVX_EINVAL;
     cfg_ = cfg;
     cfg_.offload_dir[sizeof(cfg_.offload_dir) - 1] = 0;
@@ -165,7 +186,33 @@ void Engine::start() {
     bool ok = cudaMalloc(&arena_, slab_bytes_ * cfg_.gpu_layer_slots) == cudaSuccess &&
               cudaMemset(arena_, 0, slab_bytes_ * cfg_.gpu_layer_slots) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&compute_, cudaStreamNonBlocking) == cudaSuccess &&
-         cudaStreamCreateWithFlags(&copy_, cudaStreamNonBlocking) == cudaSuccess;
+         cudaStreamCreateWithFlags(&copy_, cudaStreamNonBlocking) == cudaSuccess &&
+         create_move_stream(&move_);
+    // the RAM and int8 tiers' slabs, once: a move takes a slot, never memory.
+    // RAM holds at least the layers that start there (beyond the device slabs)
+    const int ram_slots = std::max(std::min(cfg_.ram_layer_slots, cfg_.layers), cfg_.layers - cfg_.gpu_layer_slots);
+    const int i8_slots = std::min(cfg_.int8_layer_slots, cfg_.layers);
+    if (ok && ram_slots > 0 &&
+        cudaHostAlloc((void **)&ram_arena_, slab_bytes_ * ram_slots, cudaHostAllocPortable) != cudaSuccess) {
+        ram_arena_ = nullptr;
+        ok = false;
+    }
+    if (ok && i8_slots > 0 &&
+        (cudaMalloc((void **)&i8_codes_, slab_bytes_ / 2 * i8_slots) != cudaSuccess ||
+         cudaMalloc((void **)&i8_stats_, blocks_per_slab_ * 16 * i8_slots) != cudaSuccess))
+        ok = false;
+    free_host_.clear();
+    free_i8_.clear();
+    for (int i = ram_slots - 1; i >= 0; --i) free_host_.push_back(i);
+    for (int i = i8_slots - 1; i >= 0; --i) free_i8_.push_back(i);
+    // Load the move kernels now: a kernel's first launch loads its code,
+    // which can wait for every kernel running on the device, so the first
+    // compressKv during a decode step would otherwise wait for the whole
+    // step.  One zero block of the zero-filled arena, round trip in place.
+    if (ok && i8_slots > 0)
+        ok = kvx_compress_int8(arena_, KVX_F16, i8_codes_, i8_stats_, 1, 2048, move_) == KVX_OK &&
+             kvx_decompress_int8(i8_codes_, i8_stats_, arena_, KVX_F16, 1, 2048, move_) == KVX_OK &&
+             cudaStreamSynchronize(move_) == cudaSuccess;
     const size_t qn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.q_heads * 128;
     const size_t kn = (size_t)cfg_.layers * cfg_.max_batch * cfg_.kv_heads * 128;
     // q / out also carry one layer of fp32 rows for decode_layer_f32
@@ -181,7 +228,8 @@ void Engine::start() {
     for (int l = 0; ok && l < cfg_.layers; ++l)
         ok = cudaEventCreateWithFlags(&ev_in_[l], cudaEventDisableTiming) == cudaSuccess &&
              cudaEventCreateWithFlags(&ev_out_[l], cudaEventDisableTiming) == cudaSuccess;
-    device_bytes_ = (long long)(slab_bytes_ * cfg_.gpu_layer_slots + 2 * qn * 2 + 2 * kn * 2);
+    device_bytes_ = (long long)(slab_bytes_ * cfg_.gpu_layer_slots + 2 * qn * 2 + 2 * kn * 2 +
+                                (slab_bytes_ / 2 + blocks_per_slab_ * 16) * i8_slots);
     layers_.assign(cfg_.layers, Layer{});
     free_slabs_.clear();
     for (int i = cfg_.gpu_layer_slots - 1; i >= 0; --i) free_slabs_.push_back(i);
@@ -192,8 +240,9 @@ void Engine::start() {
             free_slabs_.pop_back();
         } else {  // beyond the device budget: starts in RAM, zero-filled
             layers_[l].tier = kRam;
-            ok = ensure_host(l) == KVX_OK;
-            if (ok) memset(layers_[l].host, 0, slab_bytes_);
+            layers_[l].host_slot = take_host();
+            ok = layers_[l].host_slot >= 0;
+            if (ok) memset(host_ptr(layers_[l].host_slot), 0, slab_bytes_);
         }
     }
     free_pages_.clear();
@@ -229,14 +278,20 @@ void Engine::release_all() {
     h_status_ = nullptr;
     if (comm_stream_) cudaStreamDestroy(comm_stream_);
     comm_stream_ = nullptr;
+    if (move_) cudaStreamSynchronize(move_);
     for (size_t l = 0; l < layers_.size(); ++l) {
         Layer &L = layers_[l];
-        if (L.host) cudaFreeHost(L.host);
-        if (L.codes) cudaFree(L.codes);
-        if (L.stats) cudaFree(L.stats);
         if (L.tier == kOffloaded) remove(offload_path((int)l).c_str());
         L = Layer{};
     }
+    if (ram_arena_) cudaFreeHost(ram_arena_);
+    ram_arena_ = nullptr;
+    if (i8_codes_) cudaFree(i8_codes_);
+    if (i8_stats_) cudaFree(i8_stats_);
+    i8_codes_ = nullptr;
+    i8_stats_ = nullptr;
+    free_host_.clear();
+    free_i8_.clear();
     layers_.clear();
     for (auto &e : ev_in_) if (e) cudaEventDestroy(e);
     for (auto &e : ev_out_) if (e) cudaEventDestroy(e);
@@ -266,17 +321,20 @@ void Engine::release_all() {
     }
     if (compute_) cudaStreamDestroy(compute_);
     if (copy_) cudaStreamDestroy(copy_);
-    compute_ = copy_ = nullptr;
+    if (move_) cudaStreamDestroy(move_);
+    compute_ = copy_ = move_ = nullptr;
     free_slabs_.clear();
     device_bytes_ = 0;
     batch_ = 0;
 }
 
 void Engine::stop() {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !step_active_ && !any_moving(); });
     if (!started_) return;
     release_all();
     started_ = false;
+    cv_.notify_all();
 }
 
 bool Engine::valid(long layer) const {
@@ -292,11 +350,28 @@ std::string Engine::offload_path(int l) const {
     return std::string(cfg_.offload_dir) + "/adaptive_kv_layer_" + std::to_string(l) + ".bin";
 }
 
-int Engine::ensure_host(int l) {
-    if (layers_[l].host) return KVX_OK;
-    return cudaHostAlloc(&layers_[l].host, slab_bytes_, cudaHostAllocPortable) == cudaSuccess
-               ? KVX_OK
-               : KVX_ENOSPC;
+int Engine::take_host() {
+    if (free_host_.empty()) return -1;
+    const int s = free_host_.back();
+    free_host_.pop_back();
+    return s;
+}
+
+int Engine::take_i8() {
+    if (free_i8_.empty()) return -1;
+    const int s = free_i8_.back();
+    free_i8_.pop_back();
+    return s;
+}
+
+bool Engine::any_moving() const {
+    for (const Layer &L : layers_)
+        if (L.moving) return true;
+    return false;
+}
+
+void Engine::wait_not_moving(std::unique_lock<std::mutex> &lk, int l) {
+    cv_.wait(lk, [&] { return !started_ || l >= (int)layers_.size() || !layers_[l].moving; });
 }
 
 // A free device slab for layer `for_layer`, evicting the least recently used
@@ -310,12 +385,25 @@ int Engine::alloc_slab(int for_layer) {
         free_slabs_.pop_back();
         return s;
     }
+    const int victim = pick_victim(for_layer);
+    if (victim < 0) return victim;
+    if (to_ram_locked(victim) < 0) return -1;
+    const int s = free_slabs_.back();
+    free_slabs_.pop_back();
+    return s;
+}
+
+// The least recently used GPU-resident layer other than `for_layer`
+// (smallest last_used, lowest index on ties, KVCacheGPU::findLRUPage,
+// native-engine/cpp/KVCacheGPU.cpp:54-66), skipping pinned layers and
+// layers being moved; -2 when only pinned ones are left.
+int Engine::pick_victim(int for_layer) const {
     int victim = -1;
     uint64_t best = UINT64_MAX;
     bool any_pinned = false;
     for (int l = 0; l < (int)layers_.size(); ++l) {
         const Layer &L = layers_[l];
-        if (l == for_layer || L.tier != kGpu) continue;
+        if (l == for_layer || L.tier != kGpu || L.moving) continue;
         if (L.refcount > 0) {
             any_pinned = true;
             continue;
@@ -325,11 +413,7 @@ int Engine::alloc_slab(int for_layer) {
             victim = l;
         }
     }
-    if (victim < 0) return any_pinned ? -2 : -1;
-    if (to_ram_locked(victim) < 0) return -1;
-    const int s = free_slabs_.back();
-    free_slabs_.pop_back();
-    return s;
+    return victim >= 0 ? victim : (any_pinned ? -2 : -1);
 }
 
 int Engine::ensure_staging() {
@@ -408,17 +492,23 @@ int Engine::device_to_file(int l, const uint8_t *src) {
     return rc;
 }
 
+// Locked moves: the decode step's own tiered path (its victims may still be
+// read by its kernels, hence the compute-stream sync) and the file paths.
 int Engine::to_ram_locked(int l) {
     Layer &L = layers_[l];
     if (L.tier == kRam) return 0;
-    cudaStreamSynchronize(compute_);
-    if (ensure_host(l) != KVX_OK) return KVX_ENOSPC;
     if (L.tier == kOffloaded) {
+        const int hs = take_host();
+        if (hs < 0) return KVX_ENOSPC;
         FILE *f = fopen(offload_path(l).c_str(), "rb");
-        const bool ok = f && fread(L.host, 1, slab_bytes_, f) == slab_bytes_;
+        const bool ok = f && fread(host_ptr(hs), 1, slab_bytes_, f) == slab_bytes_;
         if (f) fclose(f);
-        if (!ok) return KVX_EINVAL;
+        if (!ok) {
+            free_host_.push_back(hs);
+            return KVX_EINVAL;
+        }
         remove(offload_path(l).c_str());
+        L.host_slot = hs;
         L.tier = kRam;
         return 1;
     }
@@ -426,13 +516,19 @@ int Engine::to_ram_locked(int l) {
         const int rc = to_gpu_locked(l);
         if (rc < 0) return rc;
     }
-    if (cudaMemcpyAsync(L.host, arena_ + (size_t)L.slab * slab_bytes_, slab_bytes_,
-                        cudaMemcpyDeviceToHost, copy_) != cudaSuccess ||
-        cudaStreamSynchronize(copy_) != cudaSuccess)
+    const int hs = take_host();
+    if (hs < 0) return KVX_ENOSPC;
+    cudaStreamSynchronize(compute_);
+    if (cudaMemcpyAsync(host_ptr(hs), slab_ptr(L.slab), slab_bytes_, cudaMemcpyDeviceToHost, copy_) != cudaSuccess ||
+        cudaStreamSynchronize(copy_) != cudaSuccess) {
+        free_host_.push_back(hs);
         return KVX_ECUDA;
+    }
     free_slabs_.push_back(L.slab);
     L.slab = -1;
+    L.host_slot = hs;
     L.tier = kRam;
+    L.last_use = nullptr;
     return 1;
 }
 
@@ -443,13 +539,14 @@ int Engine::to_gpu_locked(int l) {
     const int s = alloc_slab(l);
     if (s == -2) return KVX_EBUSY;
     if (s < 0) return KVX_ENOSPC;
-    uint8_t *dst = arena_ + (size_t)s * slab_bytes_;
+    uint8_t *dst = slab_ptr(s);
     int rc = KVX_OK;
     if (L.tier == kCompressed) {
-        rc = kvx_decompress_int8(L.codes, L.stats, dst, KVX_F16, blocks_per_slab_, 2048, copy_);
+        rc = kvx_decompress_int8(codes_ptr(L.i8_slot), stats_ptr(L.i8_slot), dst, KVX_F16, blocks_per_slab_, 2048,
+                                 copy_);
     } else if (L.tier == kOffloaded) {
         rc = file_to_device(l, dst);
-    } else if (cudaMemcpyAsync(dst, L.host, slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess) {
+    } else if (cudaMemcpyAsync(dst, host_ptr(L.host_slot), slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess) {
         rc = KVX_ECUDA;
     }
     if (!rc && cudaStreamSynchronize(copy_) != cudaSuccess) rc = KVX_ECUDA;
@@ -458,51 +555,17 @@ int Engine::to_gpu_locked(int l) {
         return rc;
     }
     if (L.tier == kCompressed) {
-        cudaFree(L.codes);
-        cudaFree(L.stats);
-        L.codes = nullptr;
-        L.stats = nullptr;
-        device_bytes_ -= (long long)(slab_bytes_ / 2 + blocks_per_slab_ * 16);
+        free_i8_.push_back(L.i8_slot);
+        L.i8_slot = -1;
     } else if (L.tier == kOffloaded) {
         remove(offload_path(l).c_str());
+    } else {
+        free_host_.push_back(L.host_slot);
+        L.host_slot = -1;
     }
     L.slab = s;
     L.tier = kGpu;
-    return 1;
-}
-
-int Engine::compress_locked(int l) {
-    Layer &L = layers_[l];
-    if (L.tier == kCompressed) return 0;
-    if (L.tier != kGpu) {
-        const int rc = to_gpu_locked(l);
-        if (rc < 0) return rc;
-    }
-    cudaStreamSynchronize(compute_);
-    if (cudaMalloc(&L.codes, slab_bytes_ / 2) != cudaSuccess) {
-        L.codes = nullptr;
-        return KVX_ENOSPC;
-    }
-    if (cudaMalloc(&L.stats, blocks_per_slab_ * 16) != cudaSuccess) {
-        cudaFree(L.codes);
-        L.codes = nullptr;
-        L.stats = nullptr;
-        return KVX_ENOSPC;
-    }
-    int rc = kvx_compress_int8(arena_ + (size_t)L.slab * slab_bytes_, KVX_F16, L.codes, L.stats,
-                               blocks_per_slab_, 2048, copy_);
-    if (!rc && cudaStreamSynchronize(copy_) != cudaSuccess) rc = KVX_ECUDA;
-    if (rc) {
-        cudaFree(L.codes);
-        cudaFree(L.stats);
-        L.codes = nullptr;
-        L.stats = nullptr;
-        return rc;
-    }
-    device_bytes_ += (long long)(slab_bytes_ / 2 + blocks_per_slab_ * 16);
-    free_slabs_.push_back(L.slab);
-    L.slab = -1;
-    L.tier = kCompressed;
+    L.last_use = nullptr;
     return 1;
 }
 
@@ -514,54 +577,207 @@ int Engine::offload_locked(int l) {
         if (rc < 0) return rc;
     }
     if (L.tier == kGpu) {  // device -> file, then the slab is free
-        cudaStreamSynchronize(compute_);
-        const int rc = device_to_file(l, arena_ + (size_t)L.slab * slab_bytes_);
+        if (L.last_use && cudaEventSynchronize(L.last_use) != cudaSuccess) return KVX_ECUDA;
+        const int rc = device_to_file(l, slab_ptr(L.slab));
         if (rc != KVX_OK) return rc;
         free_slabs_.push_back(L.slab);
         L.slab = -1;
     } else {
         FILE *f = fopen(offload_path(l).c_str(), "wb");
-        const bool ok = f && fwrite(L.host, 1, slab_bytes_, f) == slab_bytes_;
+        const bool ok = f && fwrite(host_ptr(L.host_slot), 1, slab_bytes_, f) == slab_bytes_;
         if (f) fclose(f);
         if (!ok) return KVX_EINVAL;
+        free_host_.push_back(L.host_slot);
+        L.host_slot = -1;
     }
-    if (L.host) cudaFreeHost(L.host);
-    L.host = nullptr;
     L.tier = kOffloaded;
+    L.last_use = nullptr;
     return 1;
+}
+
+// Moves whose copies run with the mutex released.  Under the mutex the
+// layer (and an eviction victim) is marked `moving`, arena slots are taken
+// and the copies queued on move_ behind each layer's last decode work (the
+// group event of the step that last read it; nothing else touches its
+// slab); the mutex is released while move_ drains, then retaken to commit
+// the new tiers.  A running decode step keeps going meanwhile, and so do
+// moves of other layers.  layers_ is not resized while a layer is moving
+// (stop() waits), so indices stay valid across the unlocked part.
+int Engine::gpu_to_ram(std::unique_lock<std::mutex> &lk, int l) {
+    const int hs = take_host();
+    if (hs < 0) return KVX_ENOSPC;
+    layers_[l].moving = true;
+    int rc = KVX_OK;
+    {
+        const Layer &L = layers_[l];
+        if ((L.last_use && cudaStreamWaitEvent(move_, L.last_use, 0) != cudaSuccess) ||
+            cudaMemcpyAsync(host_ptr(hs), slab_ptr(L.slab), slab_bytes_, cudaMemcpyDeviceToHost, move_) != cudaSuccess)
+            rc = KVX_ECUDA;
+    }
+    lk.unlock();
+    if (cudaStreamSynchronize(move_) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
+    lk.lock();
+    Layer &L = layers_[l];
+    L.moving = false;
+    if (rc == KVX_OK) {
+        free_slabs_.push_back(L.slab);
+        L.slab = -1;
+        L.host_slot = hs;
+        L.tier = kRam;
+        L.last_use = nullptr;
+    } else {
+        free_host_.push_back(hs);
+    }
+    cv_.notify_all();
+    return rc == KVX_OK ? 1 : rc;
+}
+
+int Engine::bring_to_gpu(std::unique_lock<std::mutex> &lk, int l) {
+    layers_[l].last_used = ++clock_;
+    if (layers_[l].tier == kGpu) return 0;
+    if (layers_[l].tier == kOffloaded) return to_gpu_locked(l);  // file reads stay under the mutex
+    int s = -1, victim = -1, vhs = -1;
+    if (!free_slabs_.empty()) {
+        s = free_slabs_.back();
+        free_slabs_.pop_back();
+    } else {  // the least recently used layer goes to RAM first (KVCacheGPU.cpp:68-109)
+        victim = pick_victim(l);
+        if (victim == -2) return KVX_EBUSY;
+        if (victim < 0) return KVX_ENOSPC;
+        vhs = take_host();
+        if (vhs < 0) return KVX_ENOSPC;
+        s = layers_[victim].slab;
+        layers_[victim].moving = true;
+    }
+    layers_[l].moving = true;
+    int rc_victim = KVX_OK, rc = KVX_OK;
+    if (victim >= 0) {
+        const Layer &V = layers_[victim];
+        if ((V.last_use && cudaStreamWaitEvent(move_, V.last_use, 0) != cudaSuccess) ||
+            cudaMemcpyAsync(host_ptr(vhs), slab_ptr(s), slab_bytes_, cudaMemcpyDeviceToHost, move_) != cudaSuccess)
+            rc_victim = rc = KVX_ECUDA;
+    }
+    if (rc == KVX_OK) {
+        const Layer &L = layers_[l];
+        if (L.tier == kCompressed)
+            rc = kvx_decompress_int8(codes_ptr(L.i8_slot), stats_ptr(L.i8_slot), slab_ptr(s), KVX_F16,
+                                     blocks_per_slab_, 2048, move_);
+        else if (cudaMemcpyAsync(slab_ptr(s), host_ptr(L.host_slot), slab_bytes_, cudaMemcpyHostToDevice, move_) !=
+                 cudaSuccess)
+            rc = KVX_ECUDA;
+    }
+    lk.unlock();
+    if (cudaStreamSynchronize(move_) != cudaSuccess) {
+        if (rc == KVX_OK) rc = KVX_ECUDA;
+        rc_victim = rc;
+    }
+    lk.lock();
+    Layer &L = layers_[l];
+    L.moving = false;
+    if (victim >= 0) {
+        Layer &V = layers_[victim];
+        V.moving = false;
+        if (rc_victim == KVX_OK) {  // its bytes are in RAM: the slab is the target's (or free again)
+            V.slab = -1;
+            V.host_slot = vhs;
+            V.tier = kRam;
+            V.last_use = nullptr;
+        } else {
+            free_host_.push_back(vhs);
+            s = -1;  // the victim keeps its slab
+        }
+    }
+    if (rc != KVX_OK) {
+        if (s >= 0) free_slabs_.push_back(s);
+        cv_.notify_all();
+        return rc;
+    }
+    if (L.tier == kCompressed) {
+        free_i8_.push_back(L.i8_slot);
+        L.i8_slot = -1;
+    } else {
+        free_host_.push_back(L.host_slot);
+        L.host_slot = -1;
+    }
+    L.slab = s;
+    L.tier = kGpu;
+    L.last_use = nullptr;
+    cv_.notify_all();
+    return 1;
+}
+
+int Engine::gpu_to_int8(std::unique_lock<std::mutex> &lk, int l) {
+    const int is = take_i8();
+    if (is < 0) return KVX_ENOSPC;
+    layers_[l].moving = true;
+    int rc = KVX_OK;
+    {
+        const Layer &L = layers_[l];
+        if (L.last_use && cudaStreamWaitEvent(move_, L.last_use, 0) != cudaSuccess) rc = KVX_ECUDA;
+        if (rc == KVX_OK)
+            rc = kvx_compress_int8(slab_ptr(L.slab), KVX_F16, codes_ptr(is), stats_ptr(is), blocks_per_slab_, 2048,
+                                   move_);
+    }
+    lk.unlock();
+    if (cudaStreamSynchronize(move_) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
+    lk.lock();
+    Layer &L = layers_[l];
+    L.moving = false;
+    if (rc == KVX_OK) {
+        free_slabs_.push_back(L.slab);
+        L.slab = -1;
+        L.i8_slot = is;
+        L.tier = kCompressed;
+        L.last_use = nullptr;
+    } else {
+        free_i8_.push_back(is);
+    }
+    cv_.notify_all();
+    return rc == KVX_OK ? 1 : rc;
 }
 
 // ---- NativeEngineApi operations ------------------------------------------
 
 long Engine::move_to_ram(long layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    wait_not_moving(lk, (int)layer);
     if (!valid(layer)) return -1;
     if (layers_[layer].refcount > 0 && layers_[layer].tier != kRam) return -2;
-    const int rc = to_ram_locked((int)layer);
+    const int rc = layers_[layer].tier == kGpu ? gpu_to_ram(lk, (int)layer) : to_ram_locked((int)layer);
     return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
 }
 
 long Engine::move_to_gpu(long layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
     if (!valid(layer)) return -1;
-    const int rc = to_gpu_locked((int)layer);
+    wait_not_moving(lk, (int)layer);
+    if (!valid(layer)) return -1;
+    const int rc = bring_to_gpu(lk, (int)layer);
     return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
 }
 
 long Engine::compress(long layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    wait_not_moving(lk, (int)layer);
     if (!valid(layer)) return -1;
     if (layers_[layer].refcount > 0 && layers_[layer].tier != kCompressed) return -2;
-    const int rc = compress_locked((int)layer);
+    if (layers_[layer].tier == kCompressed) return 0;
+    int rc = KVX_OK;
+    if (layers_[layer].tier != kGpu) rc = bring_to_gpu(lk, (int)layer);
+    if (rc >= 0) rc = gpu_to_int8(lk, (int)layer);
     return rc < 0 ? (rc == KVX_EBUSY ? -2 : -1) : ms_since(t0);
 }
 
 long Engine::offload(long layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    if (!valid(layer)) return -1;
+    wait_not_moving(lk, (int)layer);
     if (!valid(layer)) return -1;
     if (layers_[layer].refcount > 0 && layers_[layer].tier != kOffloaded) return -2;
     const int rc = offload_locked((int)layer);
@@ -573,39 +789,42 @@ long Engine::offload(long layer) {
 // residency: a cached layer has its KV on the device.
 long Engine::prefetch_layer(int layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
     if (!valid(layer)) return -1;
-    Layer &L = layers_[layer];
-    if (L.cached) return 0;
-    const int rc = to_gpu_locked(layer);
+    wait_not_moving(lk, layer);
+    if (!valid(layer)) return -1;
+    if (layers_[layer].cached) return 0;
+    const int rc = bring_to_gpu(lk, layer);
     if (rc < 0) return rc == KVX_EBUSY ? -2 : -1;
-    L.cached = true;
+    layers_[layer].cached = true;
     return ms_since(t0);
 }
 
 long Engine::evict_layer(int layer) {
     const double t0 = now_ms();
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
     if (!valid(layer)) return -1;
-    Layer &L = layers_[layer];
-    if (!L.cached) return 0;
-    if (L.refcount > 0) return -2;
-    const int rc = to_ram_locked(layer);
+    wait_not_moving(lk, layer);
+    if (!valid(layer)) return -1;
+    if (!layers_[layer].cached) return 0;
+    if (layers_[layer].refcount > 0) return -2;
+    const int rc = layers_[layer].tier == kGpu ? gpu_to_ram(lk, layer) : to_ram_locked(layer);
     if (rc < 0) return -1;
-    L.cached = false;
+    layers_[layer].cached = false;
     return ms_since(t0);
 }
 
 long Engine::keep_layer(int layer) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
     if (!valid(layer)) return -1;
-    Layer &L = layers_[layer];
-    if (!L.cached) {
-        const int rc = to_gpu_locked(layer);
+    wait_not_moving(lk, layer);
+    if (!valid(layer)) return -1;
+    if (!layers_[layer].cached) {
+        const int rc = bring_to_gpu(lk, layer);
         if (rc < 0) return rc == KVX_EBUSY ? -2 : -1;
-        L.cached = true;
+        layers_[layer].cached = true;
     }
-    return ++L.refcount;
+    return ++layers_[layer].refcount;
 }
 
 void Engine::release_layer(int layer) {
@@ -665,8 +884,10 @@ int32_t Engine::seq_len(int s) {
 }
 
 int Engine::copy_layer(int layer, void *ptr, bool load) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
     if (!ptr || !valid(layer)) return KVX_EINVAL;
+    cv_.wait(lk, [&] { return !started_ || (!step_active_ && !layers_[layer].moving); });
+    if (!valid(layer)) return KVX_EINVAL;
     const int rc = to_gpu_locked(layer);
     if (rc < 0) return rc;
     cudaStreamSynchronize(compute_);
@@ -685,7 +906,8 @@ int32_t Engine::block_table(int32_t *dst) {
 // ---- sequences and the decode step ---------------------------------------
 
 int Engine::set_sequences(int batch, const int32_t *lens, int reserve_tokens, uint64_t seed) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !step_active_; });
     if (!started_ || batch <= 0 || batch > cfg_.max_batch || !lens || reserve_tokens < 0) return KVX_EINVAL;
     cudaStreamSynchronize(compute_);
     // every physical page back into the free list, then hand them out
@@ -730,7 +952,10 @@ int Engine::set_sequences(int batch, const int32_t *lens, int reserve_tokens, ui
 }
 
 int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v, uint16_t *out) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    // one step at a time (they share the step buffers and the workspace),
+    // and none while a layer is being moved
+    cv_.wait(lk, [&] { return !step_active_ && !any_moving(); });
     if (!started_ || batch_ == 0 || !q || !k || !v) return KVX_EINVAL;
     for (int s = 0; s < batch_; ++s)  // every sequence needs a page for its next token
         if (lens_[s] / 16 >= max_pages_ || table_[(size_t)s * max_pages_ + lens_[s] / 16] < 0)
@@ -858,11 +1083,22 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
             rc == KVX_OK)
             rc = KVX_ECUDA;
     }
+    // each layer's last decode work is its group's output event: a move of
+    // that layer waits for it, not for the whole step
+    for (int gi = 0; gi < ngroups; ++gi)
+        for (int l = gstart[gi]; l < gstart[gi + 1]; ++l) layers_[l].last_use = ev_out_[gi];
+    // wait for the device with the mutex released, so layer moves proceed
+    step_active_ = true;
+    lk.unlock();
     int32_t err = 0;
-    if (cudaStreamSynchronize(compute_) != cudaSuccess || cudaStreamSynchronize(copy_) != cudaSuccess ||
-        (comm_stream_ && cudaStreamSynchronize(comm_stream_) != cudaSuccess) ||
-        cudaMemcpy(&err, d_err_, sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
-        return KVX_ECUDA;
+    const bool synced = cudaStreamSynchronize(compute_) == cudaSuccess &&
+                        cudaStreamSynchronize(copy_) == cudaSuccess &&
+                        (!comm_stream_ || cudaStreamSynchronize(comm_stream_) == cudaSuccess) &&
+                        cudaMemcpy(&err, d_err_, sizeof(err), cudaMemcpyDeviceToHost) == cudaSuccess;
+    lk.lock();
+    step_active_ = false;
+    cv_.notify_all();
+    if (!synced) return KVX_ECUDA;
     if (comm_)
         for (int r = 0; r < world_; ++r)
             if (r != rank_ && (h_status_[2 + 2 * r] != KVX_OK || h_status_[3 + 2 * r] != 0)) peer_failed = true;
@@ -875,7 +1111,8 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 }
 
 int Engine::decode_layer_f32(int layer, const float *q, const float *k, const float *v, float *out) {
-    std::lock_guard<std::mutex> lk(mu_);
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !step_active_ && !any_moving(); });
     if (!valid(layer) || batch_ == 0 || !q || !k || !v || !out) return KVX_EINVAL;
     for (int s = 0; s < batch_; ++s)
         if (lens_[s] / 16 >= max_pages_ || table_[(size_t)s * max_pages_ + lens_[s] / 16] < 0)

@@ -3,17 +3,25 @@
 // Owns, per layer, one fp16 page pool ("slab", [pages][2][kv_heads][16][128])
 // that lives in one of four tiers:
 //   GPU         a device slab from the engine's arena
-//   RAM         a pinned host copy (cudaHostAlloc), no device memory
-//   COMPRESSED  int8 codes + per-block QuantizationStats on the device
+//   RAM         a slab of the pinned host arena, no device memory
+//   COMPRESSED  a slab of the device int8 arena: codes + per-block
+//               QuantizationStats
 //   OFFLOADED   a file in the offload directory, no device or host memory
 // plus the sequence state (block table, context lengths) shared by all
-// layers, and the device buffers of a decode step.  All public methods take
-// the engine mutex (the reference serialises its C-ABI calls the same way,
-// native-engine/llama_wrapper/llama_wrapper.cpp:56,224).
+// layers, and the device buffers of a decode step.  Every arena is made by
+// start(), so no move allocates.  All public methods take the engine mutex
+// for their bookkeeping (the reference serialises its C-ABI calls with one
+// mutex, native-engine/llama_wrapper/llama_wrapper.cpp:56,224), but not for
+// their device work: a decode step queues its kernels and then waits for
+// them with the mutex released, and a layer move queues its copies on the
+// move stream behind that layer's last kernel and releases the mutex while
+// they run.  A layer being moved is marked `moving`; decode steps and other
+// operations on that layer wait for the mark to clear.
 #pragma once
 
 #include <cuda_runtime.h>
 
+#include <condition_variable>
 #include <cstdint>
 #include <mutex>
 #include <string>
@@ -28,12 +36,13 @@ enum Tier { kGpu = 0, kRam = 1, kCompressed = 2, kOffloaded = 3 };
 struct Layer {
     Tier tier = kGpu;
     int slab = -1;              // device slab index while on the GPU
-    void *host = nullptr;       // pinned fp16 copy (kept for reuse once made)
-    int8_t *codes = nullptr;    // device int8 codes while compressed
-    float *stats = nullptr;     // device QuantizationStats while compressed
+    int host_slot = -1;         // pinned RAM arena slot while in RAM
+    int i8_slot = -1;           // int8 arena slot (codes + stats) while compressed
     uint64_t last_used = 0;     // LRU stamp (KVCacheGPU lastUsedToken)
     bool cached = false;        // layer-cache bitmap of prefetch/evict/keep
     int refcount = 0;           // pins taken by keepLayer
+    bool moving = false;        // a move is copying it with the engine mutex released
+    cudaEvent_t last_use = nullptr;  // recorded after the last decode work on its slab
 };
 
 class Engine {
@@ -41,6 +50,7 @@ public:
     static Engine &instance();
 
     void default_config(adaptive_engine_config *cfg) const;
+    int step_in_flight();
     int configure(const adaptive_engine_config &cfg);
     void start();
     void stop();
@@ -81,13 +91,25 @@ private:
     ~Engine();
     bool valid(long layer) const;
     // helpers below expect the mutex held
-    int alloc_slab(int for_layer);  // >= 0, -1 failure, -2 every victim pinned
+    int alloc_slab(int for_layer);  // >= 0, -1 failure, -2 every victim pinned (locked path)
     long ms_since(double t0) const;
     int to_ram_locked(int l);       // kvx_status
     int to_gpu_locked(int l);       // kvx_status (KVX_EBUSY: victims pinned)
-    int compress_locked(int l);
     int offload_locked(int l);
-    int ensure_host(int l);
+    // arena slots
+    int take_host();
+    int take_i8();
+    uint8_t *slab_ptr(int slab) const { return arena_ + (size_t)slab * slab_bytes_; }
+    uint8_t *host_ptr(int slot) const { return ram_arena_ + (size_t)slot * slab_bytes_; }
+    int8_t *codes_ptr(int slot) const { return i8_codes_ + (size_t)slot * (slab_bytes_ / 2); }
+    float *stats_ptr(int slot) const { return i8_stats_ + (size_t)slot * blocks_per_slab_ * 4; }
+    // moves with the mutex released during their copies (see the class comment)
+    void wait_not_moving(std::unique_lock<std::mutex> &lk, int l);
+    bool any_moving() const;
+    int pick_victim(int for_layer) const;  // >= 0, -1 none, -2 every victim pinned
+    int gpu_to_ram(std::unique_lock<std::mutex> &lk, int l);
+    int bring_to_gpu(std::unique_lock<std::mutex> &lk, int l);
+    int gpu_to_int8(std::unique_lock<std::mutex> &lk, int l);
     // file <-> device through a pinned staging pair, no whole-layer host slab
     int file_to_device(int l, uint8_t *dst);
     int device_to_file(int l, const uint8_t *src);
@@ -96,6 +118,8 @@ private:
     void release_all();
 
     std::mutex mu_;
+    std::condition_variable cv_;  // signalled when a move or a step finishes
+    bool step_active_ = false;    // a step's device work may still run (mutex released)
     adaptive_engine_config cfg_{};
     bool configured_ = false;
     bool started_ = false;
@@ -107,6 +131,11 @@ private:
     uint64_t clock_ = 0;
     int current_layer_ = 0;
     cudaStream_t compute_ = nullptr, copy_ = nullptr;
+    cudaStream_t move_ = nullptr;        // the NativeEngineApi moves
+    uint8_t *ram_arena_ = nullptr;       // pinned host slabs, made by start()
+    int8_t *i8_codes_ = nullptr;         // int8 code slabs, made by start()
+    float *i8_stats_ = nullptr;          // their QuantizationStats
+    std::vector<int> free_host_, free_i8_;
     std::vector<cudaEvent_t> ev_in_, ev_out_;
 
     // sequences

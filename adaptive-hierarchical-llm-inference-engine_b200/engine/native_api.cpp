@@ -79,6 +79,8 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const v
     return Engine::instance().set_comm(rank, world, id128);
 }
 
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_step_in_flight(void) { return Engine::instance().step_in_flight(); }
+
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_readback_share(int share) {
     return Engine::instance().set_readback_share(share);
 }

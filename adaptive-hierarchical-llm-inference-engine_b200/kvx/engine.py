@@ -27,7 +27,8 @@ class EngineConfig(C.Structure):
     _fields_ = [("layers", C.c_int32), ("kv_heads", C.c_int32), ("q_heads", C.c_int32),
                 ("head_dim", C.c_int32), ("page_tokens", C.c_int32), ("max_batch", C.c_int32),
                 ("pages_per_layer", C.c_int32), ("gpu_layer_slots", C.c_int32),
-                ("device", C.c_int32), ("offload_dir", C.c_char * 256)]
+                ("device", C.c_int32), ("offload_dir", C.c_char * 256),
+                ("ram_layer_slots", C.c_int32), ("int8_layer_slots", C.c_int32)]
 
 
 lib.adaptive_engine_get_api.restype = C.POINTER(NativeEngineApi)
@@ -57,6 +58,7 @@ lib.adaptive_engine_nccl_unique_id.restype = C.c_int
 lib.adaptive_engine_set_comm.argtypes = [C.c_int, C.c_int, C.c_void_p]
 lib.adaptive_engine_set_comm.restype = C.c_int
 
+lib.adaptive_engine_step_in_flight.restype = C.c_int
 lib.adaptive_engine_set_readback_share.argtypes = [C.c_int]
 lib.adaptive_engine_set_readback_share.restype = C.c_int
 

@@ -470,8 +470,10 @@ def run_ours(args):
     lens0 = workload_lens(B)
     reserve = max(total_steps, 24)  # the e2e pass appends up to 17 more tokens
     need_pages = int(((lens0 + reserve + PT - 1) // PT).sum())
-    E.configure(layers=LAYERS, kv_heads=hkv, q_heads=hq, max_batch=B,
-                pages_per_layer=need_pages, gpu_layer_slots=LAYERS, device=local)
+    # the RAM and int8 tiers' slabs are made by start(): four of each (the
+    # layer moves below use layer 0)
+    E.configure(layers=LAYERS, kv_heads=hkv, q_heads=hq, max_batch=B, pages_per_layer=need_pages,
+                gpu_layer_slots=LAYERS, device=local, ram_layer_slots=4, int8_layer_slots=4)
     api = E.api()
     api.start()
     E.set_sequences(lens0.astype(np.int32), reserve_tokens=reserve, seed=SEED + 1)
@@ -587,10 +589,10 @@ def run_ours(args):
     if not args.no_append_compress:
         result["append_compress"] = run_append_compress(world, rank, hkv, dist if world > 1 else None)
     if not args.no_e2e:
-        result["e2e"] = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
+        result["e2e"], bufs = run_e2e(args, E, lens0, hq, hkv, world, rank, B)
         torch.cuda.synchronize()
         if world == 1:  # after everything timed: it rewrites layer 0
-            result["engine_ops"] = run_engine_ops(api, need_pages * 2 * hkv * PT * DIM * 2)
+            result["engine_ops"] = run_engine_ops(api, need_pages * 2 * hkv * PT * DIM * 2, E, bufs)
     if world > 1:
         dist.barrier()
     api.stop()
@@ -607,14 +609,35 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_engine_ops(api, slab_bytes):
+def run_engine_ops(api, slab_bytes, E=None, bufs=None):
     """The NativeEngineApi layer moves (native-engine/llama_wrapper/
     llama_wrapper.cpp:220-433 in the reference, simulations there) on layer
     0 of the bench's engine: wall time of each blocking call, and its bytes
-    per second for the moves that carry the whole layer."""
+    per second for the moves that carry the whole layer.  The RAM and int8
+    slabs were made by start(), so the first move to RAM costs what the
+    later ones do.  Then a move during a decode step: compressKv(0) issued
+    while a whole 28-layer step runs (the step waits for its kernels with the
+    engine lock released; the move waits only for layer 0's group)."""
+    import threading
     out = {"layer_bytes": int(slab_bytes)}
-    # the first move to RAM pins the layer's host slab (cudaHostAlloc); the
-    # second one reuses it
+    if E is not None and bufs is not None:
+        t0 = time.perf_counter()
+        E.decode_step(*bufs)
+        step_ms = (time.perf_counter() - t0) * 1e3
+        done = {}
+        th = threading.Thread(target=lambda: (E.decode_step(*bufs), done.setdefault("t", time.perf_counter())))
+        th.start()
+        while not E.lib.adaptive_engine_step_in_flight() and th.is_alive():
+            pass
+        t1 = time.perf_counter()
+        rc = api.compressKv(0)
+        t2 = time.perf_counter()
+        th.join()
+        out["compressKv_during_step"] = {
+            "ms": round((t2 - t1) * 1e3, 3), "returned": int(rc), "step_alone_ms": round(step_ms, 3),
+            "returned_before_step_end": bool(t2 < done.get("t", 0.0)),
+            "step_end_after_move_ms": round((done.get("t", t2) - t2) * 1e3, 3)}
+        assert api.moveKvToGpu(0) > 0
     for name, fn, moved in (("moveKvToRam_first", api.moveKvToRam, True), ("moveKvToGpu", api.moveKvToGpu, True),
                             ("moveKvToRam", api.moveKvToRam, True), ("moveKvToGpu_again", api.moveKvToGpu, True),
                             ("compressKv", api.compressKv, True), ("moveKvToGpu_from_int8", api.moveKvToGpu, True),
@@ -665,12 +688,13 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
         t = torch.tensor([secs], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         secs = t.item()
-    return {"value": round(nbytes * world / secs / 1e9, 1), "unit": "GB/s",
+    return ({"value": round(nbytes * world / secs / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2),
             "d2h_bytes_per_step": LAYERS * world * B * hq * DIM * 2, "steps": steps,
             "path": "adaptive_engine_decode_step (C ABI) with pinned host buffers" +
                     (", NCCL all-gather of outputs in the engine, each rank reading back its share of the "
-                     "gathered layers (d2h bytes summed over ranks)" if world > 1 else "")}
+                     "gathered layers (d2h bytes summed over ranks)" if world > 1 else "")},
+            (h_q, h_k, h_v, h_o))
 
 
 # --------------------------------------------------------------------------

@@ -85,6 +85,13 @@ typedef struct adaptive_engine_config {
     int32_t gpu_layer_slots;  /* device slabs (< layers: layers compete, LRU) */
     int32_t device;
     char offload_dir[256];
+    /* Slabs made once by start(), so that no move allocates: pinned host
+     * slabs for layers in RAM (at least layers - gpu_layer_slots) and
+     * device int8 slabs (codes + QuantizationStats) for compressed layers.
+     * Defaults: one of each per layer.  Environment overrides:
+     * ADAPTIVELLM_KV_RAM_LAYERS, ADAPTIVELLM_KV_INT8_LAYERS. */
+    int32_t ram_layer_slots;
+    int32_t int8_layer_slots;
 } adaptive_engine_config;
 
 /* Fill *cfg with the defaults (environment applied). */
@@ -138,6 +145,14 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const v
  * and the copies spread over every GPU's host link instead of one.  No
  * effect without a communicator.  Returns a kvx_status. */
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_readback_share(int share);
+/* 1 while a decode step's device work is still running: the step has
+ * queued its kernels and copies and waits for them with the engine lock
+ * released, so NativeEngineApi moves of layers proceed meanwhile (each
+ * waits only for its own layer's last kernel).  0 otherwise.  With pageable
+ * (not pinned) host buffers the step's copies hold the calling thread, and
+ * so the lock, until its kernels are done: pass pinned buffers to let moves
+ * run beside a step. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_step_in_flight(void);
 /* Current context length of sequence s (-1 if none). */
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_seq_len(int32_t s);
 /* Tier of layer l: 0 GPU, 1 RAM, 2 COMPRESSED (int8 on device),

@@ -195,3 +195,94 @@ def test_decode_step_28_layers_with_split_contexts(engine, oracle):
             assert excess.max() <= 0, (step, l, excess.max())
         E.read_layer(l, back)
         assert np.array_equal(back.cpu().numpy().view(np.uint16), host.view(np.uint16)), l
+
+
+def test_layer_move_overlaps_a_running_decode_step(engine, oracle):
+    """A NativeEngineApi move of a layer the running decode step is done with
+    runs while the step's later layers still decode: the step waits for its
+    kernels with the engine lock released, and the move waits only for its
+    own layer's last kernel (the output event of the step's first group of
+    layers).  16 layers x 16 sequences x 32,768 tokens make a step of a few
+    milliseconds; compressKv(0) is issued as soon as the step is in flight
+    and must return while the step still is.  The step's outputs are then
+    checked against the oracle (layer 0 was read before it was compressed)."""
+    import threading
+    E, api, tmp = engine
+    L, B, T = 16, 16, 32768
+    lens = np.full(B, T - 1, np.int32)
+    pages = B * (T // 16 + 1)
+    E.configure(layers=L, kv_heads=HKV, q_heads=HQ, max_batch=B, pages_per_layer=pages, gpu_layer_slots=L,
+                ram_layer_slots=0, int8_layer_slots=1, offload_dir=str(tmp))
+    api.start()
+    E.set_sequences(lens, reserve_tokens=1, seed=641)
+    bt = E.block_table(B)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(642)
+    pool = torch.randn((pages, 2, HKV, 16, 128), generator=g, device="cuda", dtype=torch.float16)
+    for l in range(L):
+        E.load_layer(l, pool)
+    q = kvgen.normal(643, (L, B, HQ, 128)).astype(np.float16)
+    k = kvgen.normal(644, (L, B, HKV, 128)).astype(np.float16)
+    v = kvgen.normal(645, (L, B, HKV, 128)).astype(np.float16)
+    # pinned host buffers: a copy to pageable memory would hold the calling
+    # thread (and with it the engine lock) until the step's kernels are done
+    h_q, h_k, h_v = (torch.from_numpy(a).pin_memory() for a in (q, k, v))
+    h_out = torch.zeros(q.shape, dtype=torch.float16).pin_memory()
+    E.decode_step(h_q, h_k, h_v, h_out)  # warm-up (lazy module loading), context now T
+    lens = lens + 1
+    E.set_sequences(lens - 1, reserve_tokens=1, seed=641)  # same pages, back to T - 1 tokens
+    status = {}
+
+    def run_step():
+        try:
+            E.decode_step(h_q, h_k, h_v, h_out)
+            status["step"] = "ok"
+        except Exception as e:  # noqa: BLE001
+            status["step"] = repr(e)
+
+    t = threading.Thread(target=run_step)
+    t.start()
+    for _ in range(2_000_000):
+        if E.lib.adaptive_engine_step_in_flight():
+            break
+    else:
+        t.join()
+        pytest.fail("the step never showed as in flight")
+    ms = api.compressKv(0)
+    still_running = E.lib.adaptive_engine_step_in_flight()
+    t.join()
+    assert status.get("step") == "ok", status
+    assert ms > 0 and E.tier(0) == "COMPRESSED"
+    assert still_running == 1, "the move waited for the whole step"
+    out = h_out.numpy()
+    host = pool.cpu().numpy()
+    for l in (0, 1, L - 1):
+        pl = host.copy()
+        oracle.append(pl, bt[:3], (lens[:3] - 1).astype(np.int32), k[l, :3], v[l, :3], 16)
+        ref = oracle.paged_decode(pl, bt[:3], lens[:3].astype(np.int32), q[l, :3].astype(np.float32))
+        excess = np.abs(out[l, :3].astype(np.float32) - ref) - (ATOL + RTOL * np.abs(ref))
+        assert excess.max() <= 0, (l, excess.max())
+
+
+def test_moves_use_the_slots_made_at_start(engine):
+    """RAM and int8 tiers take slots of arenas made by start(): with one RAM
+    slot, a second layer cannot move to RAM (-1) until the first leaves it."""
+    E, api, tmp = engine
+    E.configure(layers=LAYERS, pages_per_layer=PAGES, max_batch=4, gpu_layer_slots=LAYERS, ram_layer_slots=1,
+                int8_layer_slots=1, offload_dir=str(tmp))
+    api.start()
+    data = [slab(700 + l) for l in range(LAYERS)]
+    for l in range(LAYERS):
+        E.load_layer(l, data[l])
+    assert api.moveKvToRam(0) > 0
+    assert api.moveKvToRam(1) == -1 and E.tier(1) == "GPU"
+    assert api.compressKv(2) > 0
+    assert api.compressKv(3) == -1 and E.tier(3) == "GPU"
+    assert api.moveKvToGpu(0) > 0
+    assert api.moveKvToRam(1) > 0 and E.tier(1) == "RAM"
+    assert api.moveKvToGpu(2) > 0 and api.compressKv(3) > 0
+    for l in (0, 1):
+        assert api.moveKvToGpu(l) >= 0
+        back = np.empty_like(data[l])
+        E.read_layer(l, back)
+        assert np.array_equal(back.view(np.uint16), data[l].view(np.uint16)), l
