@@ -1035,22 +1035,44 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
         if (cudaEventRecord(ev_out_[gi], compute_) && rc == KVX_OK) rc = KVX_ECUDA;
         if (comm_) {  // all-gather the group's rows over NCCL, then read them back
             if (cudaStreamWaitEvent(comm_stream_, ev_out_[gi], 0) && rc == KVX_OK) rc = KVX_ECUDA;
-            for (int l = l0; l < l1; ++l)
-                if (nccl().all_gather(d_out_ + l * qstride, d_gather_ + (size_t)l * world_ * qrow, qrow, ncclFloat16,
+            // packed: one all-gather per group, the group's block of d_gather_
+            // is [world][layers][B][hq][128]; otherwise one per layer,
+            // [world][B][hq][128] at the layer's place
+            const int n = l1 - l0;
+            uint16_t *gbase = d_gather_ + (size_t)l0 * world_ * qrow;
+            if (packed) {
+                if (nccl().all_gather(d_out_ + l0 * qstride, gbase, (size_t)n * qrow, ncclFloat16,
                                       static_cast<ncclComm_t>(comm_), comm_stream_) != ncclSuccess &&
                     rc == KVX_OK)
                     rc = KVX_ECUDA;
+            } else {
+                for (int l = l0; l < l1; ++l)
+                    if (nccl().all_gather(d_out_ + l * qstride, d_gather_ + (size_t)l * world_ * qrow, qrow,
+                                          ncclFloat16, static_cast<ncclComm_t>(comm_), comm_stream_) != ncclSuccess &&
+                        rc == KVX_OK)
+                        rc = KVX_ECUDA;
+            }
             if (rc == KVX_OK && cudaEventRecord(ev_gath_[gi], comm_stream_)) rc = KVX_ECUDA;
             if (rc == KVX_OK && out && cudaStreamWaitEvent(copy_, ev_gath_[gi], 0)) rc = KVX_ECUDA;
-            if (rc == KVX_OK && out && !readback_share_ &&
-                cudaMemcpyAsync(out + (size_t)l0 * world_ * qrow, d_gather_ + (size_t)l0 * world_ * qrow,
-                                (size_t)(l1 - l0) * world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
-                rc = KVX_ECUDA;
-            for (int l = l0; rc == KVX_OK && out && readback_share_ && l < l1; ++l)
-                if (l % world_ == rank_ &&
-                    cudaMemcpyAsync(out + (size_t)l * world_ * qrow, d_gather_ + (size_t)l * world_ * qrow,
-                                    (size_t)world_ * qrow * 2, cudaMemcpyDeviceToHost, copy_))
-                    rc = KVX_ECUDA;
+            // host layout [layers][world][B][hq][128]; with the read-back
+            // shared, rank r copies the layers l % world == r
+            const size_t row = qrow * 2;  // bytes of one (layer, rank) block
+            if (rc == KVX_OK && out && packed && !readback_share_ && world_ <= n) {
+                for (int r = 0; r < world_ && rc == KVX_OK; ++r)  // rank r's block of every layer
+                    if (cudaMemcpy2DAsync(out + ((size_t)l0 * world_ + r) * qrow, world_ * row, gbase + (size_t)r * n * qrow,
+                                          row, row, n, cudaMemcpyDeviceToHost, copy_))
+                        rc = KVX_ECUDA;
+            } else if (rc == KVX_OK && out) {
+                for (int l = l0; l < l1 && rc == KVX_OK; ++l) {
+                    if (readback_share_ && l % world_ != rank_) continue;
+                    const cudaError_t e =
+                        packed ? cudaMemcpy2DAsync(out + (size_t)l * world_ * qrow, row, gbase + (size_t)(l - l0) * qrow,
+                                                   n * row, row, world_, cudaMemcpyDeviceToHost, copy_)
+                               : cudaMemcpyAsync(out + (size_t)l * world_ * qrow, d_gather_ + (size_t)l * world_ * qrow,
+                                                 world_ * row, cudaMemcpyDeviceToHost, copy_);
+                    if (e) rc = KVX_ECUDA;
+                }
+            }
         } else if (rc == KVX_OK && out) {
             if (cudaStreamWaitEvent(copy_, ev_out_[gi], 0)) rc = KVX_ECUDA;
             if (packed) {

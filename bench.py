@@ -139,8 +139,8 @@ GROUP = 7      # layers per all-gather group (N > 1)
 OUT_RING = 8   # output buffers an N > 1 run rotates through
 
 
-def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=1, gathered=None,
-                     comm=None, dist=None, group=GROUP):
+def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=1, comm=None, dist=None,
+                     group=GROUP):
     """The timed step.  step(k) appends, for every layer l, the token at
     positions[k] (rows nk[l] / nv[l]) and decodes over positions[k] + 1
     tokens into outs[k % len(outs)][l]: one kvx.append_decode launch per
@@ -148,11 +148,14 @@ def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=
     may start while the previous one drains (programmatic dependent launch);
     the layers share one decode workspace.
 
-    With world > 1 the layers' outputs are all-gathered (NCCL) on `comm` in
-    groups of `group` layers.  The last launch of a group signals its
-    completion (kvx_append_decode_signal: the last CTA stores the step's
-    epoch) and `comm` waits for that word (kvx_stream_wait_geq) before the
-    group's all-gathers, so no event sits between two decode launches.
+    With world > 1 the layers' outputs are all-gathered (NCCL) on `comm`,
+    one all-gather per group of `group` layers (a group's rows are
+    contiguous): step.gathered[g] is [world][layers of g][batch][hq][128],
+    step.gathered_rows(l, r) rank r's rows of layer l.  The last launch of a
+    group signals its completion (kvx_append_decode_signal: the last CTA
+    stores the step's epoch) and `comm` waits for that word
+    (kvx_stream_wait_geq) before the group's all-gather, so no event sits
+    between two decode launches.
     Outputs rotate through len(outs) buffers; every len(outs) - 1 steps the
     compute stream waits for the all-gathers of two steps back, the only
     point where it waits for `comm`."""
@@ -162,6 +165,8 @@ def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=
     main = torch.cuda.current_stream()
     ngroups = (L + group - 1) // group
     done = torch.zeros((ngroups, 2), dtype=torch.int32, device=bt.device) if world > 1 else None
+    gathered = [torch.empty((world, min(L, g0 + group) - g0) + tuple(outs[0].shape[1:]), device=bt.device,
+                            dtype=outs[0].dtype) for g0 in range(0, L, group)] if world > 1 else None
     gathers_done = [torch.cuda.Event() for _ in range(R)] if world > 1 else None
     sync = "stream memory wait on the group's completion word"
     if world > 1:
@@ -170,6 +175,11 @@ def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=
         except kvx.KvxError:
             sync = "event per group (no stream memory operations)"
     assert world == 1 or R >= 3, "the output ring needs at least 3 buffers"
+
+    def gather(gi, out):
+        l0 = gi * group
+        dst = gathered[gi]
+        dist.all_gather_into_tensor(dst.view((-1,) + tuple(dst.shape[2:])), out[l0:l0 + dst.shape[1]])
 
     def step(k):
         out = outs[k % R]
@@ -185,8 +195,7 @@ def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=
                                          out=out[l], workspace=ws, error_flag=err)
                 with torch.cuda.stream(comm):
                     kvx.stream_wait_geq(done[gi, 1:], k + 1, stream=comm)
-                    for j in range(l - l % group, l + 1):
-                        dist.all_gather_into_tensor(gathered[j], out[j])
+                    gather(gi, out)
             else:
                 kvx.append_decode(views[l], bt, positions[k], nk[l], nv[l], q[l], out=out[l], workspace=ws,
                                   error_flag=err)
@@ -195,12 +204,13 @@ def make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=
                     ev.record()
                     with torch.cuda.stream(comm):
                         comm.wait_event(ev)
-                        for j in range(l - l % group, l + 1):
-                            dist.all_gather_into_tensor(gathered[j], out[j])
+                        gather(l // group, out)
         if world > 1:
             gathers_done[k % R].record(comm)
 
     step.gather_sync = sync
+    step.gathered = gathered
+    step.gathered_rows = (lambda l, r: gathered[l // group][r, l % group]) if world > 1 else None
     return step
 
 
@@ -241,10 +251,11 @@ class ParitySample:
         from kvx import pool_tensor
         return pool_tensor(view)
 
-    def verify(self, q, nk, nv, positions, last_out, gathered, dist):
+    def verify(self, q, nk, nv, positions, last_out, gathered_rows, dist):
         """positions: [steps][batch] (host or device) -- every step's append
         position per sequence, in order; last_out: this rank's rows of the
-        last step."""
+        last step; gathered_rows(l, r): rank r's rows of layer l in the
+        gathered buffer (several ranks)."""
         import torch
         from oracle import Oracle
         o = Oracle()
@@ -282,7 +293,7 @@ class ParitySample:
             dist.all_gather(every, mine)
             for l in range(nl):
                 for r in range(self.world):
-                    if csum(gathered[l, r * B:(r + 1) * B]) != every[r][l].item():
+                    if csum(gathered_rows(l, r)) != every[r][l].item():
                         gather_mismatch += 1
             t = torch.tensor([excess, float(rows), 0.0 if pool_ok else 1.0, float(gather_mismatch)],
                              dtype=torch.float64, device="cuda")
@@ -491,8 +502,6 @@ def run_ours(args):
     nv = torch.randn((LAYERS, B, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
     ring = OUT_RING if world > 1 else 1
     outs = [torch.empty((LAYERS, B, hq, DIM), device="cuda", dtype=torch.float16) for _ in range(ring)]
-    gathered = torch.empty((LAYERS, world * B, hq, DIM), device="cuda", dtype=torch.float16) \
-        if world > 1 else None  # per layer: [world][B][hq/world][D] -> kvx.shard.gathered_to_heads
     ws = kvx.decode_workspace(B, hq, max_pages)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     # every step's positions up front: no kernel between two steps' launches
@@ -502,7 +511,7 @@ def run_ours(args):
     # the parity sample: its pages as they are before the first step
     check = ParitySample(bt_np, lens0, hkv, hq, world, rank, views) if not args.no_parity else None
     step = make_decode_step(kvx, views, bt, positions, nk, nv, q, ws, err, outs, world=world,
-                            gathered=gathered, comm=comm, dist=dist if world > 1 else None)
+                            comm=comm, dist=dist if world > 1 else None)
 
     def kv_bytes(lens_after):  # algorithmic K+V bytes decode reads for one layer
         return int(lens_after.sum()) * 2 * hkv * DIM * 2
@@ -535,7 +544,7 @@ def run_ours(args):
     parity = None
     if check is not None:  # outside the timed region, before anything else writes the pools
         last = outs[(total_steps - 1) % ring]
-        parity = check.verify(q, nk, nv, positions, last, gathered, dist if world > 1 else None)
+        parity = check.verify(q, nk, nv, positions, last, step.gathered_rows, dist if world > 1 else None)
 
     lens_timed = [lens0 + warm + k + 1 for k in range(steps)]
     rank_bytes = sum(kv_bytes(L) * LAYERS for L in lens_timed)
@@ -585,7 +594,7 @@ def run_ours(args):
     }
     if world > 1:
         result["config"]["gather_sync"] = step.gather_sync
-    del outs, gathered, ws, check
+    del outs, ws, check, step
     if not args.no_append_compress:
         result["append_compress"] = run_append_compress(world, rank, hkv, dist if world > 1 else None)
     if not args.no_e2e:
@@ -1337,7 +1346,6 @@ def run_config5_sharded(args, world, rank, dist=None, budget_bytes=150e9):
     nk = torch.randn((L, B5, hkv, DIM), generator=g, device="cuda", dtype=torch.float16)
     ring = OUT_RING if world > 1 else 1
     outs = [torch.empty((L, B5, hq, DIM), device="cuda", dtype=torch.float16) for _ in range(ring)]
-    gathered = torch.empty((L, world * B5, hq, DIM), device="cuda", dtype=torch.float16) if world > 1 else None
     ws = kvx.decode_workspace(B5, hq, npg + 1)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     comm = torch.cuda.Stream() if world > 1 else None
@@ -1345,7 +1353,7 @@ def run_config5_sharded(args, world, rank, dist=None, budget_bytes=150e9):
     check = ParitySample(bt_np, lens0, hkv, hq, world, rank, pools, layers=(0, L - 1), seqs=2) \
         if not args.no_parity else None
     step = make_decode_step(kvx, pools, bt, positions, nk, nk, q, ws, err, outs, world=world,
-                            gathered=gathered, comm=comm, dist=dist)
+                            comm=comm, dist=dist)
     for k in range(warm):
         step(k)
     if world > 1:
@@ -1365,7 +1373,7 @@ def run_config5_sharded(args, world, rank, dist=None, budget_bytes=150e9):
     assert err.item() == 0, f"device error flag {err.item()}"
     parity = None
     if check is not None:
-        parity = check.verify(q, nk, nk, positions, outs[(warm + steps - 1) % ring], gathered, dist)
+        parity = check.verify(q, nk, nk, positions, outs[(warm + steps - 1) % ring], step.gathered_rows, dist)
     kv_rank = B5 * T5 * 2 * hkv * DIM * 2 * L  # bytes one rank reads per step
     peak, peak_kind = peaks()
     res = {"workload": "Llama-3-70B KV (80L, 64q/8kv x128, G8), fp16, B64, ctx 32768, permuted pages",
@@ -1377,7 +1385,7 @@ def run_config5_sharded(args, world, rank, dist=None, budget_bytes=150e9):
            "peak_kind": peak_kind, "scaling": "strong per layer (the 8 KV heads split over the GPUs)",
            "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
            "parity": parity}
-    del pools, outs, gathered, ws, q, nk
+    del pools, outs, ws, q, nk, step
     torch.cuda.empty_cache()
     return res
 
