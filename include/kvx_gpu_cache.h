@@ -3,8 +3,8 @@
  * natives (native-engine/cpp/JNIInterface.cpp:159-224,
  * src/main/java/com/adaptivellm/runtime/services/KVCacheGPUManager.java:87-177),
  * over one process-wide KVCacheGPU (include/KVCacheGPU.h) on the current
- * device.  A JNI binding forwards each native to one call here (the stubs
- * are shown in INTEGRATION.md).
+ * device.  A JNI binding forwards each native to one call here, one line
+ * per native.
  *
  *   nativeTransferToGPU(hostPtr, size, pageId)  kvx_gpu_cache_transfer_to_gpu
  *   nativeTransferFromGPU(handle, hostPtr, size) kvx_gpu_cache_transfer_from_gpu

@@ -38,10 +38,12 @@ def build_oracle() -> None:
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
 
 
-def build_reference() -> bool:
-    """Compile the reference CPU sources when the checkout is present."""
-    ref = os.environ.get("KVX_REFERENCE_DIR", "/root/reference")
-    if not os.path.isdir(ref):
+def build_reference(ref_dir: str | None = None) -> bool:
+    """Compile the reference CPU sources from the checkout at `ref_dir`
+    (default: the KVX_REFERENCE_DIR environment variable); False when no
+    checkout is given or present."""
+    ref = ref_dir or os.environ.get("KVX_REFERENCE_DIR")
+    if not ref or not os.path.isdir(ref):
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
     return True

@@ -408,8 +408,9 @@ def gen_kvcache_gpu(R: Reference):
 
 def main():
     os.environ.setdefault("ADAPTIVE_LOG_LEVEL", "ERROR")
-    if not build_reference():
-        raise SystemExit("reference checkout not found")
+    # the reference checkout: KVX_REFERENCE_DIR, or the first argument
+    if not build_reference(sys.argv[1] if len(sys.argv) > 1 else None):
+        raise SystemExit("reference checkout not found: set KVX_REFERENCE_DIR or pass its path")
     R = Reference()
     gens = {"kv_compress": gen_kv_compress, "int8": gen_int8, "attention": gen_attention,
             "paged": gen_paged, "int8_decode": gen_int8_decode, "lru": gen_lru, "depth": gen_depth,
