@@ -149,6 +149,50 @@ void Engine::default_config(adaptive_engine_config *cfg) const {
     cfg->int8_layer_slots = env_int("ADAPTIVELLM_KV_INT8_LAYERS", cfg->layers);
 }
 
+long long Engine::clock_ms() const { return (long long)(now_ms() - t0_ms_); }
+
+long long Engine::layer_last_access_ms(int layer) {
+    std::lock_guard<std::mutex> lk(mu_);
+    return valid(layer) ? layers_[layer].last_access_ms : -1;
+}
+
+// KVCompressionEngine's age policy (src/main/java/com/adaptivellm/kv/
+// KVCompressionEngine.java:62-98) over the layers: age = now - last access;
+// age >= compressedThreshold -> COMPRESSED, else age >= int8Threshold ->
+// INT8, and only GPU-resident layers change (applyCompression's
+// GPU_RESIDENT -> COMPRESSED transition).  The reference only relabels the
+// page; here INT8 is the int8 tier (compressKv, a half of fp16) and
+// COMPRESSED the NF4 tier (a quarter: estimateSize's ratios).  Thresholds
+// must be positive (the constructor's IllegalArgumentException).  Pinned
+// layers are left as they are, as compressKv leaves them.
+int Engine::compress_aged(long long int8_thr, long long comp_thr, long long now, int apply, int32_t *decisions) {
+    if (int8_thr <= 0 || comp_thr <= 0) return KVX_EINVAL;
+    std::unique_lock<std::mutex> lk(mu_);
+    if (!started_) return KVX_EINVAL;
+    if (now < 0) now = clock_ms();
+    const int n = (int)layers_.size();
+    std::vector<int32_t> d(n, 0);
+    for (int l = 0; l < n; ++l) {
+        const Layer &L = layers_[l];
+        const long long age = now - L.last_access_ms;
+        const int want = age >= comp_thr ? 2 : (age >= int8_thr ? 1 : 0);
+        d[l] = (L.tier == kGpu && L.refcount == 0) ? want : 0;
+        if (decisions) decisions[l] = d[l];
+    }
+    if (!apply) return 0;
+    int done = 0;
+    for (int l = 0; l < n; ++l) {
+        if (!d[l]) continue;
+        wait_not_moving(lk, l);
+        if (!started_) return KVX_EINVAL;
+        if (layers_[l].tier != kGpu || layers_[l].refcount > 0) continue;  // changed meanwhile
+        const int rc = gpu_to_int8(lk, l, d[l] == 2);
+        if (rc < 0) return rc;
+        ++done;
+    }
+    return done;
+}
+
 int Engine::step_in_flight() {
     std::lock_guard<std::mutex> lk(mu_);
     return step_active_ ? 1 : 0;
@@ -251,6 +295,7 @@ void Engine::start() {
     max_pages_ = 0;
     clock_ = 0;
     current_layer_ = 0;
+    t0_ms_ = now_ms();  // every layer's last access: 0 on the engine clock
     if (!ok) {
         fprintf(stderr, "[adaptive_engine] start(): device allocation failed\n");
         release_all();
@@ -512,7 +557,7 @@ int Engine::to_ram_locked(int l) {
         L.tier = kRam;
         return 1;
     }
-    if (L.tier == kCompressed) {  // decompress into a slab first
+    if (is_compressed(L.tier)) {  // decompress into a slab first
         const int rc = to_gpu_locked(l);
         if (rc < 0) return rc;
     }
@@ -541,9 +586,8 @@ int Engine::to_gpu_locked(int l) {
     if (s < 0) return KVX_ENOSPC;
     uint8_t *dst = slab_ptr(s);
     int rc = KVX_OK;
-    if (L.tier == kCompressed) {
-        rc = kvx_decompress_int8(codes_ptr(L.i8_slot), stats_ptr(L.i8_slot), dst, KVX_F16, blocks_per_slab_, 2048,
-                                 copy_);
+    if (is_compressed(L.tier)) {
+        rc = decompress_into(L, dst, copy_);
     } else if (L.tier == kOffloaded) {
         rc = file_to_device(l, dst);
     } else if (cudaMemcpyAsync(dst, host_ptr(L.host_slot), slab_bytes_, cudaMemcpyHostToDevice, copy_) != cudaSuccess) {
@@ -554,7 +598,7 @@ int Engine::to_gpu_locked(int l) {
         free_slabs_.push_back(s);
         return rc;
     }
-    if (L.tier == kCompressed) {
+    if (is_compressed(L.tier)) {
         free_i8_.push_back(L.i8_slot);
         L.i8_slot = -1;
     } else if (L.tier == kOffloaded) {
@@ -572,7 +616,7 @@ int Engine::to_gpu_locked(int l) {
 int Engine::offload_locked(int l) {
     Layer &L = layers_[l];
     if (L.tier == kOffloaded) return 0;
-    if (L.tier == kCompressed) {
+    if (is_compressed(L.tier)) {
         const int rc = to_gpu_locked(l);
         if (rc < 0) return rc;
     }
@@ -659,9 +703,8 @@ int Engine::bring_to_gpu(std::unique_lock<std::mutex> &lk, int l) {
     }
     if (rc == KVX_OK) {
         const Layer &L = layers_[l];
-        if (L.tier == kCompressed)
-            rc = kvx_decompress_int8(codes_ptr(L.i8_slot), stats_ptr(L.i8_slot), slab_ptr(s), KVX_F16,
-                                     blocks_per_slab_, 2048, move_);
+        if (is_compressed(L.tier))
+            rc = decompress_into(L, slab_ptr(s), move_);
         else if (cudaMemcpyAsync(slab_ptr(s), host_ptr(L.host_slot), slab_bytes_, cudaMemcpyHostToDevice, move_) !=
                  cudaSuccess)
             rc = KVX_ECUDA;
@@ -692,7 +735,7 @@ int Engine::bring_to_gpu(std::unique_lock<std::mutex> &lk, int l) {
         cv_.notify_all();
         return rc;
     }
-    if (L.tier == kCompressed) {
+    if (is_compressed(L.tier)) {
         free_i8_.push_back(L.i8_slot);
         L.i8_slot = -1;
     } else {
@@ -706,7 +749,17 @@ int Engine::bring_to_gpu(std::unique_lock<std::mutex> &lk, int l) {
     return 1;
 }
 
-int Engine::gpu_to_int8(std::unique_lock<std::mutex> &lk, int l) {
+int Engine::decompress_into(const Layer &L, uint8_t *dst, cudaStream_t st) {
+    return L.tier == kCompressedNf4
+               ? kvx_decompress_nf4(reinterpret_cast<const uint8_t *>(codes_ptr(L.i8_slot)), stats_ptr(L.i8_slot), dst,
+                                    KVX_F16, blocks_per_slab_, 2048, st)
+               : kvx_decompress_int8(codes_ptr(L.i8_slot), stats_ptr(L.i8_slot), dst, KVX_F16, blocks_per_slab_, 2048,
+                                     st);
+}
+
+// Compress a GPU layer into a compressed-arena slot: int8 (compressKv) or
+// NF4 (4-bit codes, half of the slot; the age policy's heavy compression).
+int Engine::gpu_to_int8(std::unique_lock<std::mutex> &lk, int l, bool nf4) {
     const int is = take_i8();
     if (is < 0) return KVX_ENOSPC;
     layers_[l].moving = true;
@@ -715,8 +768,10 @@ int Engine::gpu_to_int8(std::unique_lock<std::mutex> &lk, int l) {
         const Layer &L = layers_[l];
         if (L.last_use && cudaStreamWaitEvent(move_, L.last_use, 0) != cudaSuccess) rc = KVX_ECUDA;
         if (rc == KVX_OK)
-            rc = kvx_compress_int8(slab_ptr(L.slab), KVX_F16, codes_ptr(is), stats_ptr(is), blocks_per_slab_, 2048,
-                                   move_);
+            rc = nf4 ? kvx_compress_nf4(slab_ptr(L.slab), KVX_F16, reinterpret_cast<uint8_t *>(codes_ptr(is)),
+                                        stats_ptr(is), blocks_per_slab_, 2048, move_)
+                     : kvx_compress_int8(slab_ptr(L.slab), KVX_F16, codes_ptr(is), stats_ptr(is), blocks_per_slab_,
+                                         2048, move_);
     }
     lk.unlock();
     if (cudaStreamSynchronize(move_) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
@@ -727,7 +782,7 @@ int Engine::gpu_to_int8(std::unique_lock<std::mutex> &lk, int l) {
         free_slabs_.push_back(L.slab);
         L.slab = -1;
         L.i8_slot = is;
-        L.tier = kCompressed;
+        L.tier = nf4 ? kCompressedNf4 : kCompressed;
         L.last_use = nullptr;
     } else {
         free_i8_.push_back(is);
@@ -765,8 +820,8 @@ long Engine::compress(long layer) {
     if (!valid(layer)) return -1;
     wait_not_moving(lk, (int)layer);
     if (!valid(layer)) return -1;
-    if (layers_[layer].refcount > 0 && layers_[layer].tier != kCompressed) return -2;
-    if (layers_[layer].tier == kCompressed) return 0;
+    if (layers_[layer].refcount > 0 && !is_compressed(layers_[layer].tier)) return -2;
+    if (is_compressed(layers_[layer].tier)) return 0;
     int rc = KVX_OK;
     if (layers_[layer].tier != kGpu) rc = bring_to_gpu(lk, (int)layer);
     if (rc >= 0) rc = gpu_to_int8(lk, (int)layer);
@@ -894,6 +949,7 @@ int Engine::copy_layer(int layer, void *ptr, bool load) {
     uint8_t *slab = arena_ + (size_t)layers_[layer].slab * slab_bytes_;
     const cudaError_t e = load ? cudaMemcpy(slab, ptr, slab_bytes_, cudaMemcpyDefault)
                                : cudaMemcpy(ptr, slab, slab_bytes_, cudaMemcpyDefault);
+    if (load) layers_[layer].last_access_ms = clock_ms();  // a write is an access
     return e == cudaSuccess ? KVX_OK : KVX_ECUDA;
 }
 
@@ -1023,6 +1079,7 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                 }
             }
             layers_[l].last_used = ++clock_;
+            layers_[l].last_access_ms = clock_ms();
             kvx_paged view{arena_ + (size_t)layers_[l].slab * slab_bytes_, nullptr, KVX_F16,
                            cfg_.pages_per_layer, hkv, 128, 16};
             rc = kvx_append_decode(&view, d_table_, max_pages_, d_pos_, B, d_k_ + l * kstride,
@@ -1151,6 +1208,7 @@ int Engine::decode_layer_f32(int layer, const float *q, const float *k, const fl
         if (r < 0) return r;
     }
     layers_[layer].last_used = ++clock_;
+    layers_[layer].last_access_ms = clock_ms();
     // fp32 q / out share the step buffers' space (the fp16 step buffers hold
     // twice the elements needed here)
     float *dq = reinterpret_cast<float *>(d_q_), *dout = reinterpret_cast<float *>(d_out_);

@@ -4,8 +4,10 @@
 // that lives in one of four tiers:
 //   GPU         a device slab from the engine's arena
 //   RAM         a slab of the pinned host arena, no device memory
-//   COMPRESSED  a slab of the device int8 arena: codes + per-block
-//               QuantizationStats
+//   COMPRESSED  a slab of the device compressed arena: int8 codes +
+//               per-block QuantizationStats (compressKv)
+//   COMPRESSED_NF4  the same arena slab holding 4-bit codes (the age
+//               policy's heavy compression, compress_aged)
 //   OFFLOADED   a file in the offload directory, no device or host memory
 // plus the sequence state (block table, context lengths) shared by all
 // layers, and the device buffers of a decode step.  Every arena is made by
@@ -31,7 +33,9 @@
 
 namespace kvx_engine {
 
-enum Tier { kGpu = 0, kRam = 1, kCompressed = 2, kOffloaded = 3 };
+enum Tier { kGpu = 0, kRam = 1, kCompressed = 2, kOffloaded = 3, kCompressedNf4 = 4 };
+
+inline bool is_compressed(Tier t) { return t == kCompressed || t == kCompressedNf4; }
 
 struct Layer {
     Tier tier = kGpu;
@@ -43,6 +47,7 @@ struct Layer {
     int refcount = 0;           // pins taken by keepLayer
     bool moving = false;        // a move is copying it with the engine mutex released
     cudaEvent_t last_use = nullptr;  // recorded after the last decode work on its slab
+    long long last_access_ms = 0;    // engine clock of the last decode or load (the age policy)
 };
 
 class Engine {
@@ -51,6 +56,11 @@ public:
 
     void default_config(adaptive_engine_config *cfg) const;
     int step_in_flight();
+    // KVCompressionEngine's age policy over the layers (see adaptive_engine.h)
+    int compress_aged(long long int8_threshold_ms, long long compressed_threshold_ms, long long now_ms,
+                      int apply, int32_t *decisions);
+    long long layer_last_access_ms(int layer);
+    long long clock_ms() const;
     int configure(const adaptive_engine_config &cfg);
     void start();
     void stop();
@@ -109,7 +119,8 @@ private:
     int pick_victim(int for_layer) const;  // >= 0, -1 none, -2 every victim pinned
     int gpu_to_ram(std::unique_lock<std::mutex> &lk, int l);
     int bring_to_gpu(std::unique_lock<std::mutex> &lk, int l);
-    int gpu_to_int8(std::unique_lock<std::mutex> &lk, int l);
+    int gpu_to_int8(std::unique_lock<std::mutex> &lk, int l, bool nf4 = false);
+    int decompress_into(const Layer &L, uint8_t *dst, cudaStream_t st);
     // file <-> device through a pinned staging pair, no whole-layer host slab
     int file_to_device(int l, uint8_t *dst);
     int device_to_file(int l, const uint8_t *src);
@@ -136,6 +147,7 @@ private:
     int8_t *i8_codes_ = nullptr;         // int8 code slabs, made by start()
     float *i8_stats_ = nullptr;          // their QuantizationStats
     std::vector<int> free_host_, free_i8_;
+    double t0_ms_ = 0;  // engine clock origin (start())
     std::vector<cudaEvent_t> ev_in_, ev_out_;
 
     // sequences

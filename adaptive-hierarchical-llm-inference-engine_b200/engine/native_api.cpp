@@ -81,6 +81,15 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_comm(int rank, int world, const v
 
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_step_in_flight(void) { return Engine::instance().step_in_flight(); }
 
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_compress_aged(int64_t int8_threshold_ms, int64_t compressed_threshold_ms,
+                                                        int64_t now_ms, int32_t apply, int32_t *decisions) {
+    return Engine::instance().compress_aged(int8_threshold_ms, compressed_threshold_ms, now_ms, apply, decisions);
+}
+
+ADAPTIVE_ENGINE_EXPORT int64_t adaptive_engine_layer_last_access_ms(int layer) {
+    return Engine::instance().layer_last_access_ms(layer);
+}
+
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_set_readback_share(int share) {
     return Engine::instance().set_readback_share(share);
 }

@@ -62,7 +62,12 @@ lib.adaptive_engine_step_in_flight.restype = C.c_int
 lib.adaptive_engine_set_readback_share.argtypes = [C.c_int]
 lib.adaptive_engine_set_readback_share.restype = C.c_int
 
-TIERS = {0: "GPU", 1: "RAM", 2: "COMPRESSED", 3: "OFFLOADED"}
+lib.adaptive_engine_compress_aged.argtypes = [C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_void_p]
+lib.adaptive_engine_compress_aged.restype = C.c_int
+lib.adaptive_engine_layer_last_access_ms.argtypes = [C.c_int]
+lib.adaptive_engine_layer_last_access_ms.restype = C.c_int64
+
+TIERS = {0: "GPU", 1: "RAM", 2: "COMPRESSED", 3: "OFFLOADED", 4: "COMPRESSED_NF4"}
 
 
 def api() -> NativeEngineApi:
@@ -159,3 +164,19 @@ def set_readback_share(share: bool):
     rc = lib.adaptive_engine_set_readback_share(1 if share else 0)
     if rc != 0:
         raise KvxError("adaptive_engine_set_readback_share", rc)
+
+
+def compress_aged(int8_threshold_ms, compressed_threshold_ms, now_ms=-1, apply=True, layers=None):
+    """The Java KVCompressionEngine's age policy over the engine's layers.
+    Returns (layers compressed, per-layer decisions 0 none / 1 INT8 / 2 COMPRESSED)."""
+    n = layers if layers is not None else lib.adaptive_engine_get_api().contents.getKvPages()
+    d = np.zeros(max(n, 1), np.int32)
+    rc = lib.adaptive_engine_compress_aged(int(int8_threshold_ms), int(compressed_threshold_ms), int(now_ms),
+                                           1 if apply else 0, d.ctypes.data)
+    if rc < 0:
+        raise KvxError("adaptive_engine_compress_aged", rc)
+    return rc, d[:n]
+
+
+def last_access_ms(layer: int) -> int:
+    return int(lib.adaptive_engine_layer_last_access_ms(layer))

@@ -156,8 +156,26 @@ ADAPTIVE_ENGINE_EXPORT int adaptive_engine_step_in_flight(void);
 /* Current context length of sequence s (-1 if none). */
 ADAPTIVE_ENGINE_EXPORT int32_t adaptive_engine_seq_len(int32_t s);
 /* Tier of layer l: 0 GPU, 1 RAM, 2 COMPRESSED (int8 on device),
- * 3 OFFLOADED (file), -1 invalid. */
+ * 3 OFFLOADED (file), 4 COMPRESSED_NF4 (4-bit codes on device, the age
+ * policy's heavy compression), -1 invalid. */
 ADAPTIVE_ENGINE_EXPORT int adaptive_engine_layer_tier(int layer);
+/* The age-based compression policy of the reference's Java
+ * KVCompressionEngine (src/main/java/com/adaptivellm/kv/
+ * KVCompressionEngine.java:62-98), over the layers: age = now_ms - the
+ * layer's last access (its last decode, or a load); age >=
+ * compressed_threshold_ms -> COMPRESSED, else age >= int8_threshold_ms ->
+ * INT8; only GPU-resident, unpinned layers change.  INT8 is the int8 tier of
+ * compressKv (half of fp16), COMPRESSED the NF4 tier (a quarter), the ratios
+ * of the reference's estimateSize.  decisions: NULL or int32[layers],
+ * receiving 0 (none), 1 (INT8) or 2 (COMPRESSED) per layer.  apply = 0
+ * decides only.  now_ms < 0: the engine clock (ms since start()).
+ * Thresholds <= 0 are invalid, as in the reference's constructor.  Returns
+ * the number of layers compressed, or a negative kvx_status. */
+ADAPTIVE_ENGINE_EXPORT int adaptive_engine_compress_aged(int64_t int8_threshold_ms, int64_t compressed_threshold_ms,
+                                                        int64_t now_ms, int32_t apply, int32_t *decisions);
+/* Layer l's last access on the engine clock (ms since start()), -1 if
+ * invalid. */
+ADAPTIVE_ENGINE_EXPORT int64_t adaptive_engine_layer_last_access_ms(int layer);
 /* Bytes of device memory the engine holds. */
 ADAPTIVE_ENGINE_EXPORT long long adaptive_engine_device_bytes(void);
 

@@ -39,6 +39,36 @@ def test_scheduler_depth_matches_reference(built):
     assert [int(x) for x in out.split()] == want
 
 
+def test_prefetcher_drop_in(built):
+    """Prefetcher (prefetch/prefetcher.h:14-38): requests are served in FIFO
+    order by the worker; a mover result of 0 is a hit (no load, nothing
+    observed), < 0 a failure, > 0 a load whose latency goes to the
+    Scheduler, which then decides exactly as one fed the same latencies;
+    schedule(5, 8) requests layers 6 .. 5 + depth below 8
+    (InferenceController::schedulePrefetch, runtime/inference.cpp:61-84)."""
+    rc, out = run(built, "prefetcher_io")
+    assert rc == 0, out
+    lines = dict(line.split(" ", 1) for line in out.strip().splitlines() if " " in line)
+    assert [int(x) for x in lines["order"].split()] == list(range(16))
+    loads = [i for i in range(16) if i % 3 != 0 and i != 13]
+    assert [int(x) for x in lines["counts"].split()] == [16, len(loads), 1]
+    d_sched, d_twin = map(int, lines["depth"].split())
+    assert d_sched == d_twin
+    sched = [int(x) for x in lines["schedule"].split()]
+    depth = sched[0]
+    assert sched[1:] == [l for l in range(6, 6 + depth) if l < 8]
+    assert out.strip().endswith("ok")
+
+
+@pytest.mark.gpu
+def test_prefetcher_moves_engine_layers(built, tmp_path):
+    """The Prefetcher's default mover is the engine's move to the GPU tier:
+    prefetched layers become GPU-resident, the least recently used ones go
+    to RAM (KVCacheGPU's evict-then-retry), a resident layer is a hit."""
+    rc, out = run(built, "prefetcher_engine", tmp_path)
+    assert rc == 0 and out.strip().endswith("ok"), out
+
+
 @pytest.mark.gpu
 def test_kv_test_known_answers(built, tmp_path):
     # tests/kv_test.cpp of the reference prints 0.0999756, 1.09961, 2.09961

@@ -286,3 +286,51 @@ def test_moves_use_the_slots_made_at_start(engine):
         back = np.empty_like(data[l])
         E.read_layer(l, back)
         assert np.array_equal(back.view(np.uint16), data[l].view(np.uint16)), l
+
+
+def test_age_policy_compresses_old_layers(engine, oracle):
+    """The Java KVCompressionEngine's age policy
+    (src/main/java/com/adaptivellm/kv/KVCompressionEngine.java:62-98) over
+    the engine's layers: age = now - last access; >= compressedThreshold ->
+    COMPRESSED (the NF4 tier here), else >= int8Threshold -> INT8 (the int8
+    tier); only GPU-resident, unpinned layers change.  Decisions are checked
+    at both thresholds' boundaries; applied, the NF4 round trip equals the
+    oracle's compressToNF4 / decompressNF4 rounded to fp16, bit for bit."""
+    from kvx import KvxError
+    E, api, tmp = engine
+    start(E, api, tmp)
+    data = [slab(900 + l) for l in range(LAYERS)]
+    for l in range(LAYERS):
+        E.load_layer(l, data[l])
+    a = [E.last_access_ms(l) for l in range(LAYERS)]
+    lo, hi = min(a), max(a)
+    for now in (lo + 99, lo + 100, hi + 99, hi + 100, hi + 999, hi + 1000, hi + 50000):
+        n, d = E.compress_aged(100, 1000, now, apply=False)
+        want = [2 if now - t >= 1000 else 1 if now - t >= 100 else 0 for t in a]
+        assert n == 0 and list(d) == want, (now, a)
+    for bad in ((0, 1000), (100, 0), (-5, 10)):
+        with pytest.raises(KvxError):
+            E.compress_aged(*bad, hi + 1000)
+    assert api.keepLayer(3) >= 1             # pinned: left alone
+    assert api.moveKvToRam(2) > 0            # not on the GPU: left alone
+    n, d = E.compress_aged(100, 1000, hi + 1000)
+    assert n == 2 and list(d) == [2, 2, 0, 0]
+    assert [E.tier(l) for l in range(LAYERS)] == ["COMPRESSED_NF4", "COMPRESSED_NF4", "RAM", "GPU"]
+    assert api.moveKvToGpu(0) > 0 and E.tier(0) == "GPU"
+    back = np.empty_like(data[0])
+    E.read_layer(0, back)
+    codes, stats = oracle.compress_nf4_blocks(data[0], 2048)
+    want = oracle.decompress_nf4_blocks(codes, stats, 2048).astype(np.float16).reshape(data[0].shape)
+    assert np.array_equal(back.view(np.uint16), want.view(np.uint16))
+    # INT8 branch: layer 0 written again (an access), 100 ms later it is INT8
+    E.load_layer(0, data[0])
+    t0 = E.last_access_ms(0)
+    n, d = E.compress_aged(100, 1000, t0 + 100)
+    assert n == 1 and d[0] == 1 and E.tier(0) == "COMPRESSED"
+    assert api.moveKvToGpu(0) > 0
+    E.read_layer(0, back)
+    codes, stats = oracle.compress_int8_blocks(data[0], 2048)
+    want = oracle.decompress_int8_blocks(codes, stats, 2048).astype(np.float16).reshape(data[0].shape)
+    assert np.array_equal(back.view(np.uint16), want.view(np.uint16))
+    for _ in range(2):
+        E.lib.adaptive_engine_test_release_layer(3)
