@@ -14,6 +14,7 @@
 //    one CTA of 4 warps per query row, each warp every 4th key, lanes split
 //    the head dimension, online softmax per warp, warps merged through
 //    shared memory.  Neither materialises the seq x seq score matrix.
+#include <cooperative_groups.h>
 #include <math_constants.h>
 
 #include "kvx_common.cuh"
@@ -194,6 +195,242 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
     }
 }
 
+// ---------------------------------------------------------------------------
+// head_dim 128 on the tensor cores (attention_tc128_kernel).
+//
+// mma.sync m16n8k8 with tf32 operands and fp32 accumulation, each product
+// split three ways for fp32-grade accuracy over fp32's whole range
+// ("3xTF32"): x = big + small with big = tf32(x), small = tf32(x - big),
+// and a.b ~ big_a.big_b + big_a.small_b + small_a.big_b (the dropped
+// small.small term and small's own rounding are ~2^-21 relative).
+//  * A CTA owns 16 query rows (the mma's M) and half of the keys: the two
+//    CTAs of a cluster split the keys and merge through distributed shared
+//    memory, so 1,024 queries make 128 CTAs.
+//  * K and V stream through shared memory in tiles of 64 keys (cp.async,
+//    double buffered, rows padded to 132 floats so that every fragment
+//    load below is bank-conflict free); warp w takes keys 8w .. 8w+7 of
+//    each tile: S = Q K^T (16 k-steps), online softmax in the log2 domain,
+//    O += P V (16 n-tiles).
+//  * P feeds the P.V mma straight from the S accumulators: a thread holds
+//    keys 2t, 2t+1 of its rows, which the A fragment wants at k positions
+//    t, t+4, so the P.V k order is permuted (position t <-> key 2t,
+//    position t+4 <-> key 2t+1) and V rows are read in the same order.
+//  * The 8 warps' (max, sum, O) merge through shared memory, then the
+//    cluster's two CTAs through DSMEM; rank 0 writes the rows.
+constexpr int kTcRows = 16, kTcKeys = 64, kTcWarpsD = 8, kTcPad = 132;
+constexpr int kTcTileFloats = kTcKeys * kTcPad;            // one K or V tile
+constexpr int kTcQFloats = kTcRows * kTcPad;               // Q big or small
+constexpr int kTcSmem = (4 * kTcTileFloats + 2 * kTcQFloats) * 4 + 2 * kTcWarpsD * kTcRows * 4 + 64;
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {
+    big = to_tf32(x);
+    small = to_tf32(x - __uint_as_float(big));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// c += A.B with A = (ab + as), B = (bb + bs), three tf32 mmas
+__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ab)[4], const uint32_t (&as)[4],
+                                     uint32_t bb0, uint32_t bb1, uint32_t bs0, uint32_t bs1) {
+    mma_tf32(c, as[0], as[1], as[2], as[3], bb0, bb1);
+    mma_tf32(c, ab[0], ab[1], ab[2], ab[3], bs0, bs1);
+    mma_tf32(c, ab[0], ab[1], ab[2], ab[3], bb0, bb1);
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    const uint32_t d = smem_addr(smem);
+    const int n = valid ? 16 : 0;  // 0: zero-fill, the source is not read
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcWarpsD * 32, 1)
+attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V,
+                       float *__restrict__ out, int seq_q, int seq_k, float scale_log2) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(16) float dsm[];
+    float *kt = dsm;                                    // [2][64][132]
+    float *vt = kt + 2 * kTcTileFloats;                 // [2][64][132]
+    uint32_t *qb = reinterpret_cast<uint32_t *>(vt + 2 * kTcTileFloats);  // [16][132] tf32 big
+    uint32_t *qs = qb + kTcQFloats;                                        // [16][132] tf32 small
+    float *wm = reinterpret_cast<float *>(qs + kTcQFloats);               // [8][16] warp maxima
+    float *wl = wm + kTcWarpsD * kTcRows;                                  // [8][16] warp sums
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int rank = (int)cluster.block_rank();
+    const int row0 = (blockIdx.x >> 1) * kTcRows;
+    // this CTA's keys: a half of them, in whole tiles
+    const int half = ((seq_k + 1) / 2 + kTcKeys - 1) / kTcKeys * kTcKeys;
+    const int kbeg = rank * half, kend = min(seq_k, kbeg + half);
+    const int ntiles = kend > kbeg ? (kend - kbeg + kTcKeys - 1) / kTcKeys : 0;
+
+    auto load_tile = [&](int i, int buf) {
+        const int key0 = kbeg + i * kTcKeys;
+        float *kd = kt + buf * kTcTileFloats, *vd = vt + buf * kTcTileFloats;
+        for (int c = threadIdx.x; c < kTcKeys * 32; c += blockDim.x) {  // 32 chunks of 16 B per row
+            const int r = c >> 5, ch = c & 31;
+            const bool ok = key0 + r < kend;
+            const size_t off = (size_t)(ok ? key0 + r : 0) * 128 + ch * 4;
+            cp_async16(kd + r * kTcPad + ch * 4, K + off, ok);
+            cp_async16(vd + r * kTcPad + ch * 4, V + off, ok);
+        }
+        cp_async_commit();
+    };
+    if (ntiles > 0) load_tile(0, 0);
+    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
+        const int r = i >> 7, d = i & 127;
+        const float x = row0 + r < seq_q ? Q[(size_t)(row0 + r) * 128 + d] : 0.f;
+        split_tf32(x, qb[r * kTcPad + d], qs[r * kTcPad + d]);
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;  // rows g, g + 8
+
+    for (int it = 0; it < ntiles; ++it) {
+        const int buf = it & 1;
+        if (it + 1 < ntiles) {
+            load_tile(it + 1, buf ^ 1);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_0();
+        }
+        __syncthreads();  // tile `it` (and Q, the first time) visible to every warp
+        const float *kd = kt + buf * kTcTileFloats + (8 * warp) * kTcPad;
+        const float *vd = vt + buf * kTcTileFloats + (8 * warp) * kTcPad;
+        // S = Q K^T over this warp's 8 keys
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 16; ++ks) {
+            const int d0 = 8 * ks + t;
+            const uint32_t ab[4] = {qb[g * kTcPad + d0], qb[(g + 8) * kTcPad + d0], qb[g * kTcPad + d0 + 4],
+                                    qb[(g + 8) * kTcPad + d0 + 4]};
+            const uint32_t as[4] = {qs[g * kTcPad + d0], qs[(g + 8) * kTcPad + d0], qs[g * kTcPad + d0 + 4],
+                                    qs[(g + 8) * kTcPad + d0 + 4]};
+            uint32_t bb0, bs0, bb1, bs1;
+            split_tf32(kd[g * kTcPad + d0], bb0, bs0);
+            split_tf32(kd[g * kTcPad + d0 + 4], bb1, bs1);
+            mma3(sacc, ab, as, bb0, bb1, bs0, bs1);
+        }
+        // online softmax (log2 domain) of rows g (keys 2t, 2t+1) and g + 8
+        const int kidx = kbeg + it * kTcKeys + 8 * warp + 2 * t;
+        float s00 = kidx < kend ? sacc[0] * scale_log2 : -CUDART_INF_F;
+        float s01 = kidx + 1 < kend ? sacc[1] * scale_log2 : -CUDART_INF_F;
+        float s10 = kidx < kend ? sacc[2] * scale_log2 : -CUDART_INF_F;
+        float s11 = kidx + 1 < kend ? sacc[3] * scale_log2 : -CUDART_INF_F;
+        float mx0 = fmaxf(s00, s01), mx1 = fmaxf(s10, s11);
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float a0 = n0 == -CUDART_INF_F ? 1.f : exp2f(m0 - n0);
+        const float a1 = n1 == -CUDART_INF_F ? 1.f : exp2f(m1 - n1);
+        const float p00 = n0 == -CUDART_INF_F ? 0.f : exp2f(s00 - n0);
+        const float p01 = n0 == -CUDART_INF_F ? 0.f : exp2f(s01 - n0);
+        const float p10 = n1 == -CUDART_INF_F ? 0.f : exp2f(s10 - n1);
+        const float p11 = n1 == -CUDART_INF_F ? 0.f : exp2f(s11 - n1);
+        m0 = n0;
+        m1 = n1;
+        l0 = l0 * a0 + (p00 + p01);
+        l1 = l1 * a1 + (p10 + p11);
+        // O = O * alpha + P V: A positions t / t+4 hold keys 2t / 2t+1
+        uint32_t pb[4], ps[4];
+        split_tf32(p00, pb[0], ps[0]);
+        split_tf32(p10, pb[1], ps[1]);
+        split_tf32(p01, pb[2], ps[2]);
+        split_tf32(p11, pb[3], ps[3]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            o[j][0] *= a0;
+            o[j][1] *= a0;
+            o[j][2] *= a1;
+            o[j][3] *= a1;
+            uint32_t bb0, bs0, bb1, bs1;
+            split_tf32(vd[(2 * t) * kTcPad + 8 * j + g], bb0, bs0);
+            split_tf32(vd[(2 * t + 1) * kTcPad + 8 * j + g], bb1, bs1);
+            mma3(o[j], pb, ps, bb0, bb1, bs0, bs1);
+        }
+        __syncthreads();  // every warp is done with this buffer before it is refilled
+    }
+
+    // ---- merge the 8 warps: per row M = max, weights exp2(m_w - M)
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (t == 0) {
+        wm[warp * kTcRows + g] = m0;
+        wm[warp * kTcRows + g + 8] = m1;
+        wl[warp * kTcRows + g] = l0;
+        wl[warp * kTcRows + g + 8] = l1;
+    }
+    float *po = dsm + warp * kTcRows * 128;  // the (idle) tiles: [8][16][128] partial O
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        *reinterpret_cast<float2 *>(po + g * 128 + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
+        *reinterpret_cast<float2 *>(po + (g + 8) * 128 + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
+    }
+    __syncthreads();
+    // this CTA's rows: unnormalised O (over its keys), max M and sum L, in
+    // the region after the 8 partials (read by the cluster's rank 0)
+    float *co = dsm + kTcWarpsD * kTcRows * 128;  // [16][128]
+    float *cml = co + kTcRows * 128;              // [16][2]
+    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
+        const int r = i >> 7, d = i & 127;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kTcWarpsD; ++w) M = fmaxf(M, wm[w * kTcRows + r]);
+        float acc = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarpsD; ++w) {
+            const float mw = wm[w * kTcRows + r];
+            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
+            acc += sw * dsm[(w * kTcRows + r) * 128 + d];
+            L += sw * wl[w * kTcRows + r];
+        }
+        co[i] = acc;
+        if (d == 0) {
+            cml[2 * r] = M;
+            cml[2 * r + 1] = L;
+        }
+    }
+    cluster.sync();  // both CTAs' rows are in shared memory
+    if (rank == 0) {
+        const float *ro = cluster.map_shared_rank(co, 1);
+        const float *rml = cluster.map_shared_rank(cml, 1);
+        for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
+            const int r = i >> 7;
+            if (row0 + r >= seq_q) continue;
+            const float Ma = cml[2 * r], La = cml[2 * r + 1], Mb = rml[2 * r], Lb = rml[2 * r + 1];
+            const float M = fmaxf(Ma, Mb);
+            const float wa = Ma == -CUDART_INF_F ? 0.f : exp2f(Ma - M);
+            const float wb = Mb == -CUDART_INF_F ? 0.f : exp2f(Mb - M);
+            float L = wa * La + wb * Lb;
+            if (L == 0.f) L = 1e-6f;  // TensorOps::softmax's guard
+            out[(size_t)(row0 + r) * 128 + (i & 127)] = (wa * co[i] + wb * ro[i]) / L;
+        }
+    }
+    cluster.sync();  // rank 1's shared memory stays until rank 0 has read it
+}
+
 }  // namespace
 }  // namespace kvx
 
@@ -215,6 +452,15 @@ extern "C" KVX_API int kvx_attention_dense(const float *Q, const float *K, const
     if (seq_q == 0) return KVX_OK;
     const float s = scale > 0.f ? scale : 1.0f / sqrtf((float)dim);
     const bool aligned = !((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15);
+    if (dim == kDD && aligned && !((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(out)) & 15) &&
+        seq_q <= (int64_t)0x3fffffff) {
+        static std::atomic<bool> attr_done[kMaxDevices];
+        if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
+        const unsigned tiles = (unsigned)((seq_q + kTcRows - 1) / kTcRows);
+        attention_tc128_kernel<<<2 * tiles, kTcWarpsD * 32, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
+            Q, K, V, out, (int)seq_q, (int)seq_k, s * 1.4426950408889634f);
+        return launch_status();
+    }
     if (dim == kDD && aligned) {
         attention_dense128_kernel<<<(unsigned)((seq_q + kDQ - 1) / kDQ), 256, 0, static_cast<cudaStream_t>(stream)>>>(
             Q, K, V, out, (int)seq_q, (int)seq_k, s);

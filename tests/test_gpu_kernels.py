@@ -553,6 +553,26 @@ def test_attention_dense_and_softmax_match_reference_rows(kvx, oracle):
     assert np.abs(sm - e / e.sum(axis=1, keepdims=True)).max() < 1e-6
 
 
+@pytest.mark.parametrize("seq_q,seq_k,mag", [(1024, 1024, 1.0), (1000, 777, 1.0), (1, 1, 1.0), (17, 65, 1.0),
+                                             (300, 2049, 1.0), (64, 500, 1e5), (128, 300, 1e-3)])
+def test_attention_dense_tensor_core_matches_fp64(kvx, seq_q, seq_k, mag):
+    """The head-dim-128 dense attention (tensor cores, 3xTF32 products) over
+    ragged query / key counts (partial key tiles, rows past the last query,
+    a second cluster CTA with no keys) and magnitudes far outside fp16's
+    range, against softmax(Q K^T / sqrt(128)) V in float64 (TensorOps::
+    attention, runtime/tensor_ops.cpp:179-219)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seq_q * 7 + seq_k)
+    q = torch.randn((seq_q, 128), generator=g, device="cuda") * mag
+    k = torch.randn((seq_k, 128), generator=g, device="cuda") * mag
+    v = torch.randn((seq_k, 128), generator=g, device="cuda")
+    v[torch.rand(v.shape, generator=g, device="cuda") < 0.01] *= 20
+    out = kvx.attention_dense(q, k, v)
+    s = (q.double() @ k.double().T) / np.sqrt(128.0)
+    ref = torch.softmax(s, dim=1) @ v.double()
+    assert_close(out.cpu().numpy(), ref.cpu().numpy())
+
+
 # ------------------------------------------------------- fp16 trunc codec ---
 
 def test_f16_trunc_codec_bitexact(kvx):
