@@ -65,6 +65,9 @@ def parse():
                          "else the rest go to a spill file, the disk tier)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
+    ap.add_argument("--kernels", action="store_true",
+                    help="time every kernel the headline line does not (one JSON line each; ncu target)")
+    ap.add_argument("--kernel-iters", type=int, default=10, help="with --kernels: timed launches per kernel")
     ap.add_argument("--shapes", action="store_true",
                     help="decode across batch x context shapes (fp16, int8 and fp32 pools, GQA 3 and 8), "
                          "one JSON line per shape")
@@ -1425,6 +1428,120 @@ def run_config5(args):
         dist.destroy_process_group()
 
 
+def run_kernel_profiles(args):
+    """One JSON line per kernel that the headline line does not time: a
+    stated size (a few GB on the device at most, inputs above L2), the
+    algorithmic bytes one launch moves and its mean duration over
+    args.kernel_iters launches (CUDA events, after one warm-up), against the
+    measured HBM copy peak (the host link's measured pinned copy peak for
+    frame migration).  Also the target of the per-kernel ncu captures."""
+    import torch
+    import kvx
+    peak, peak_kind = peaks()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 77)
+    iters = args.kernel_iters
+    rows = []
+
+    def emit(name, kernel, size, nbytes, fn, bound="hbm", ref=None):
+        ms = _timed_events(fn, iters, warm=1)
+        gbps = nbytes / (ms / 1e3) / 1e9
+        rows.append({"kernels": name, "kernel": kernel, "size": size, "bytes_per_launch": int(nbytes),
+                     "us": round(ms * 1e3, 2), "GBps": round(gbps, 1), "bound": bound,
+                     "frac": round(gbps / (ref if ref else peak), 4),
+                     "peak": ref if ref else peak, "peak_kind": "measured pinned copy" if ref else peak_kind})
+        print(json.dumps(rows[-1]), flush=True)
+
+    # single-token append (kvx_append): 4096 sequences x 8 kv heads, fp16
+    B = 4096
+    pool = torch.zeros((B, 2, HKV, PT, DIM), device="cuda", dtype=torch.float16)
+    bt = torch.randperm(B, generator=g, device="cuda").to(torch.int32).view(B, 1).contiguous()
+    pos = torch.randint(0, PT, (B,), generator=g, device="cuda", dtype=torch.int32)
+    nk = torch.randn((B, HKV, DIM), generator=g, device="cuda", dtype=torch.float16)
+    emit("append", "append_kernel", f"{B} sequences x 8 kv heads x 128, fp16, one token each",
+         B * 2 * HKV * DIM * 2 * 2, lambda: kvx.append(pool, bt, pos, nk, nk))
+    del pool, bt, pos, nk
+    # chunked append: the append measurement's launch (32 sequences x 256 tokens)
+    n = APPEND_CHUNK
+    pages = BATCH * (n // PT + 1)
+    pool = torch.zeros((pages, 2, HKV, PT, DIM), device="cuda", dtype=torch.float16)
+    bt = torch.randperm(pages, generator=g, device="cuda").to(torch.int32).view(BATCH, -1).contiguous()
+    starts = torch.randint(0, PT, (BATCH,), generator=g, device="cuda", dtype=torch.int32)
+    rk = torch.randn((BATCH, n, HKV, DIM), generator=g, device="cuda", dtype=torch.float16)
+    emit("append_chunk", "append_chunk_kernel", f"{BATCH} sequences x {n} tokens x 8 kv heads x 128, fp16",
+         BATCH * n * HKV * DIM * 2 * 2 * 2, lambda: kvx.append_chunk(pool, bt, starts, rk, rk))
+    del pool, bt, starts, rk
+    # SIMT decode over an fp32 pool: batch 32 x 4096 tokens, 24 q-heads
+    Bd, T = 32, 4096
+    npg = T // PT
+    pool = torch.randn((Bd * npg, 2, HKV, PT, DIM), generator=g, device="cuda", dtype=torch.float32)
+    bt = torch.randperm(Bd * npg, generator=g, device="cuda").to(torch.int32).view(Bd, npg).contiguous()
+    lens = torch.full((Bd,), T, dtype=torch.int32, device="cuda")
+    q = torch.randn((Bd, HQ, DIM), generator=g, device="cuda", dtype=torch.float32)
+    ws = kvx.decode_workspace(Bd, HQ, npg)
+    out = torch.empty_like(q)
+    emit("decode_fp32_pool", "paged_decode_kernel", "fp32 pool, batch 32 x 4096 tokens, 8 kv / 24 q heads",
+         Bd * T * 2 * HKV * DIM * 4, lambda: kvx.decode(pool, bt, lens, q, out=out, workspace=ws))
+    del pool, bt, lens, q, ws, out
+    # codecs over 256 Mi elements
+    N = 1 << 28
+    x32 = torch.randn(N, generator=g, device="cuda")
+    h16 = torch.empty(N, device="cuda", dtype=torch.int16)
+    emit("fp16_trunc_encode", "encode_trunc_kernel", "256 Mi fp32 -> fp16 bits", N * 6,
+         lambda: kvx.f32_to_f16_trunc(x32, out=h16))
+    emit("fp16_trunc_decode", "f16_decode_tile_kernel", "256 Mi fp16 bits -> fp32", N * 6,
+         lambda: kvx.f16_trunc_to_f32(h16, out=x32))
+    emit("fp16_wrap_encode", "fp16_wrap_encode_kernel", "256 Mi fp32 -> fp16 bits", N * 6,
+         lambda: kvx.fp16_wrap_encode(x32, out=h16))
+    emit("fp16_wrap_decode", "f16_decode_tile_kernel", "256 Mi fp16 bits -> fp32", N * 6,
+         lambda: kvx.fp16_wrap_decode(h16, out=x32))
+    xh = x32[: N // 2].half()
+    del h16
+    blocks = xh.numel() // 2048
+    nf4 = torch.empty(xh.numel() // 2, device="cuda", dtype=torch.uint8)
+    st = torch.empty((blocks, 4), device="cuda", dtype=torch.float32)
+    back = torch.empty_like(xh)
+    emit("nf4_compress", "compress_2048_kernel (15 steps)", "128 Mi fp16 in 2048-element blocks",
+         xh.numel() * 2 + nf4.numel() + blocks * 16, lambda: kvx.compress_nf4(xh, codes=nf4, stats=st))
+    emit("nf4_decompress", "decompress_nf4_2048_kernel", "128 Mi fp16 out of 2048-element blocks",
+         xh.numel() * 2 + nf4.numel() + blocks * 16,
+         lambda: kvx.decompress_nf4(nf4, st, dtype=torch.float16, out=back))
+    del x32, xh, nf4, st, back
+    # victim selection over the tiered-eviction pool's 610,351 frames
+    nfr = 610351
+    stamps = torch.randint(0, 1 << 40, (nfr,), generator=g, device="cuda", dtype=torch.int64)
+    emit("lru_select", "select_kernel", f"{nfr} u64 stamps", nfr * 8, lambda: kvx.lru_select(stamps))
+    recs = torch.randint(0, 255, (nfr * 48,), generator=g, device="cuda", dtype=torch.uint8)
+    emit("evict_select_lru", "select_kernel", f"{nfr} EvictionMetrics records (48 B)", nfr * 48,
+         lambda: kvx.evict_select(0, recs))
+    del stamps, recs
+    # frame migration: 8192 frames of 64 KiB each way, pinned mapped host arena
+    fb, nf = 65536, 8192
+    link = pinned_peaks(nbytes=fb * nf)
+    host = torch.empty(fb * nf, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(fb * nf, device="cuda", dtype=torch.uint8)
+    perm_d = torch.randperm(nf, generator=g, device="cuda").to(torch.int32)
+    perm_h = torch.randperm(nf, generator=g, device="cuda").to(torch.int32)
+    hp = host.data_ptr()
+    emit("migrate_h2d", "migrate_kernel", f"{nf} frames x 64 KiB, host -> device (scattered slots, 16 CTAs)",
+         fb * nf, lambda: kvx.migrate_frames(dev, nf, hp, nf, perm_d, perm_h, fb, 1, 16), "host link",
+         link["h2d"])
+    emit("migrate_d2h", "migrate_kernel", f"{nf} frames x 64 KiB, device -> host (scattered slots, 16 CTAs)",
+         fb * nf, lambda: kvx.migrate_frames(dev, nf, hp, nf, perm_d, perm_h, fb, 0, 16), "host link",
+         link["d2h"])
+    del host, dev
+    # dense attention (cuda_attention drop-in): 1024 x 1024 x 128 fp32
+    T = 1024
+    qd, kd, vd = (torch.randn((T, DIM), generator=g, device="cuda") for _ in range(3))
+    od = torch.empty_like(qd)
+    ms = _timed_events(lambda: kvx.attention_dense(qd, kd, vd, out=od), iters, warm=1)
+    flops = 4 * T * T * DIM
+    rows.append({"kernels": "attention_dense", "kernel": "attention_tc128_kernel", "size": "1024 x 1024 x 128 fp32",
+                 "us": round(ms * 1e3, 2), "TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
+                 "note": "3 tf32 mma per product (3xTF32): the tensor pipe runs 3x the algorithmic flops"})
+    print(json.dumps(rows[-1]), flush=True)
+
+
 def main():
     global LAYERS
     args = parse()
@@ -1433,6 +1550,8 @@ def main():
         run_reference(args)
     elif args.shapes:
         run_shapes(args)
+    elif args.kernels:
+        run_kernel_profiles(args)
     elif args.config == 1:
         run_config1(args)
     elif args.config == 3:
