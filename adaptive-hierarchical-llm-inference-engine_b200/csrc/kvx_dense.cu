@@ -14,8 +14,11 @@
 //    one CTA of 4 warps per query row, each warp every 4th key, lanes split
 //    the head dimension, online softmax per warp, warps merged through
 //    shared memory.  Neither materialises the seq x seq score matrix.
+#include <cuda.h>
 #include <cooperative_groups.h>
 #include <math_constants.h>
+
+#include <mutex>
 
 #include "kvx_common.cuh"
 
@@ -217,10 +220,11 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 //    position t+4 <-> key 2t+1) and V rows are read in the same order.
 //  * The 8 warps' (max, sum, O) merge through shared memory, then the
 //    cluster's two CTAs through DSMEM; rank 0 writes the rows.
-constexpr int kTcRows = 16, kTcKeys = 64, kTcWarpsD = 8, kTcPad = 132;
-constexpr int kTcTileFloats = kTcKeys * kTcPad;            // one K or V tile
-constexpr int kTcQFloats = kTcRows * kTcPad;               // Q big or small
-constexpr int kTcSmem = (4 * kTcTileFloats + 2 * kTcQFloats) * 4 + 2 * kTcWarpsD * kTcRows * 4 + 64;
+constexpr int kTcRows = 16, kTcKeys = 64, kTcWarpsD = 8, kTcOPad = 136;
+constexpr int kTcTileFloats = kTcKeys * 128;               // one K or V tile: 4 swizzled boxes of 64 x 32
+constexpr int kTcQWords = 16 * 32 * 8;                      // Q A-fragments: big [k-step][lane][4], then small
+constexpr int kTcSmem = 1024 /* alignment */ + (4 * kTcTileFloats + kTcQWords) * 4 + 2 * kTcWarpsD * kTcRows * 4 +
+                        2 * kTcRows * 4 + 64;
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
     uint32_t r;
@@ -250,27 +254,38 @@ __device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ab)[4], con
     mma_tf32(c, ab[0], ab[1], ab[2], ab[3], bb0, bb1);
 }
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
-    const uint32_t d = smem_addr(smem);
-    const int n = valid ? 16 : 0;  // 0: zero-fill, the source is not read
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem), "r"(n) : "memory");
+__device__ __forceinline__ void tma_load_2d_f(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Float index of (row r, dim d) in a tile of four 64 x 32 boxes loaded with
+// 128-byte swizzle: box d / 32, row r, 16-byte chunk ((d / 4) % 8) XOR
+// (r % 8).  The K and V fragment reads below hit 32 distinct banks.
+__device__ __forceinline__ int swz_f(int r, int d) {
+    return (d >> 5) * (kTcKeys * 32) + r * 32 + ((((d >> 2) & 7) ^ (r & 7)) << 2) + (d & 3);
+}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcWarpsD * 32, 1)
-attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V,
-                       float *__restrict__ out, int seq_q, int seq_k, float scale_log2) {
+attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int seq_q, int seq_k, float scale_log2,
+                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ __align__(16) float dsm[];
-    float *kt = dsm;                                    // [2][64][132]
-    float *vt = kt + 2 * kTcTileFloats;                 // [2][64][132]
-    uint32_t *qb = reinterpret_cast<uint32_t *>(vt + 2 * kTcTileFloats);  // [16][132] tf32 big
-    uint32_t *qs = qb + kTcQFloats;                                        // [16][132] tf32 small
-    float *wm = reinterpret_cast<float *>(qs + kTcQFloats);               // [8][16] warp maxima
+    extern __shared__ __align__(16) float dsm_raw[];
+    // 1024-byte alignment for the 128-byte-swizzled boxes
+    float *dsm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    float *kt = dsm;                                    // [2][4 boxes][64][32]
+    float *vt = kt + 2 * kTcTileFloats;                 // [2][4 boxes][64][32]
+    // Q as ready A fragments: lane l's {a0..a3} of k-step ks, big and small
+    // in separate arrays (a warp's 16-byte loads cover 512 contiguous bytes)
+    uint4 *qfb = reinterpret_cast<uint4 *>(vt + 2 * kTcTileFloats);       // [16][32]
+    uint4 *qfs = qfb + 16 * 32;                                           // [16][32]
+    float *wm = reinterpret_cast<float *>(qfs + 16 * 32);                 // [8][16] warp maxima
     float *wl = wm + kTcWarpsD * kTcRows;                                  // [8][16] warp sums
+    uint64_t *bars = reinterpret_cast<uint64_t *>(wl + kTcWarpsD * kTcRows + 2 * kTcRows);  // per tile buffer
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int rank = (int)cluster.block_rank();
@@ -280,23 +295,40 @@ attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K,
     const int kbeg = rank * half, kend = min(seq_k, kbeg + half);
     const int ntiles = kend > kbeg ? (kend - kbeg + kTcKeys - 1) / kTcKeys : 0;
 
-    auto load_tile = [&](int i, int buf) {
+    // A tile's K and V arrive as four 64-key x 32-dim boxes each (TMA tensor
+    // copies, 128-byte swizzle, rows past the keys filled with zeros),
+    // completing on the buffer's mbarrier; thread 0 issues them.
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    auto load_tile = [&](int i, int buf) {  // thread 0
         const int key0 = kbeg + i * kTcKeys;
         float *kd = kt + buf * kTcTileFloats, *vd = vt + buf * kTcTileFloats;
-        for (int c = threadIdx.x; c < kTcKeys * 32; c += blockDim.x) {  // 32 chunks of 16 B per row
-            const int r = c >> 5, ch = c & 31;
-            const bool ok = key0 + r < kend;
-            const size_t off = (size_t)(ok ? key0 + r : 0) * 128 + ch * 4;
-            cp_async16(kd + r * kTcPad + ch * 4, K + off, ok);
-            cp_async16(vd + r * kTcPad + ch * 4, V + off, ok);
+        fence_proxy_async_smem();  // the buffer's earlier generic reads before the async writes
+        mbar_arrive_expect_tx(&bars[buf], 2u * kTcTileFloats * 4u);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            tma_load_2d_f(kd + b * kTcKeys * 32, &tmk, 32 * b, key0, &bars[buf]);
+            tma_load_2d_f(vd + b * kTcKeys * 32, &tmv, 32 * b, key0, &bars[buf]);
         }
-        cp_async_commit();
     };
-    if (ntiles > 0) load_tile(0, 0);
-    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
-        const int r = i >> 7, d = i & 127;
-        const float x = row0 + r < seq_q ? Q[(size_t)(row0 + r) * 128 + d] : 0.f;
-        split_tf32(x, qb[r * kTcPad + d], qs[r * kTcPad + d]);
+    if (ntiles > 0 && threadIdx.x == 0) load_tile(0, 0);
+    // thread (ks, ln) builds lane ln's fragments of k-step ks: rows g, g + 8,
+    // dims 8ks + t, 8ks + t + 4
+    for (int i = threadIdx.x; i < 16 * 32; i += blockDim.x) {
+        const int ks = i >> 5, ln = i & 31, gg = ln >> 2, tt = ln & 3;
+        uint32_t b[4], sm[4];
+        const int rr[4] = {gg, gg + 8, gg, gg + 8}, dd[4] = {8 * ks + tt, 8 * ks + tt, 8 * ks + tt + 4, 8 * ks + tt + 4};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float x = row0 + rr[e] < seq_q ? Q[(size_t)(row0 + rr[e]) * 128 + dd[e]] : 0.f;
+            split_tf32(x, b[e], sm[e]);
+        }
+        qfb[i] = make_uint4(b[0], b[1], b[2], b[3]);
+        qfs[i] = make_uint4(sm[0], sm[1], sm[2], sm[3]);
     }
 
     float o[16][4];
@@ -306,29 +338,34 @@ attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 
     for (int it = 0; it < ntiles; ++it) {
         const int buf = it & 1;
-        if (it + 1 < ntiles) {
-            load_tile(it + 1, buf ^ 1);
-            cp_async_wait_1();
-        } else {
-            cp_async_wait_0();
-        }
+        if (it + 1 < ntiles && threadIdx.x == 0) load_tile(it + 1, buf ^ 1);
+        (void)mbar_wait_bounded(&bars[buf], (it >> 1) & 1, nullptr);
         __syncthreads();  // tile `it` (and Q, the first time) visible to every warp
-        const float *kd = kt + buf * kTcTileFloats + (8 * warp) * kTcPad;
-        const float *vd = vt + buf * kTcTileFloats + (8 * warp) * kTcPad;
-        // S = Q K^T over this warp's 8 keys
-        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float *kd = kt + buf * kTcTileFloats;
+        const float *vd = vt + buf * kTcTileFloats;
+        const int kr = 8 * warp;  // this warp's first key row in the tile
+        // S = Q K^T over this warp's 8 keys: six independent accumulator
+        // chains (product kind x k-step parity), so consecutive mmas do
+        // not wait for each other, summed at the end
+        float acc[6][4];
+#pragma unroll
+        for (int c = 0; c < 6; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks) {
             const int d0 = 8 * ks + t;
-            const uint32_t ab[4] = {qb[g * kTcPad + d0], qb[(g + 8) * kTcPad + d0], qb[g * kTcPad + d0 + 4],
-                                    qb[(g + 8) * kTcPad + d0 + 4]};
-            const uint32_t as[4] = {qs[g * kTcPad + d0], qs[(g + 8) * kTcPad + d0], qs[g * kTcPad + d0 + 4],
-                                    qs[(g + 8) * kTcPad + d0 + 4]};
+            const uint4 fb = qfb[ks * 32 + lane], fs = qfs[ks * 32 + lane];
             uint32_t bb0, bs0, bb1, bs1;
-            split_tf32(kd[g * kTcPad + d0], bb0, bs0);
-            split_tf32(kd[g * kTcPad + d0 + 4], bb1, bs1);
-            mma3(sacc, ab, as, bb0, bb1, bs0, bs1);
+            split_tf32(kd[swz_f(kr + g, d0)], bb0, bs0);
+            split_tf32(kd[swz_f(kr + g, d0 + 4)], bb1, bs1);
+            const int p = ks & 1;
+            mma_tf32(acc[p], fs.x, fs.y, fs.z, fs.w, bb0, bb1);
+            mma_tf32(acc[2 + p], fb.x, fb.y, fb.z, fb.w, bs0, bs1);
+            mma_tf32(acc[4 + p], fb.x, fb.y, fb.z, fb.w, bb0, bb1);
         }
+        float sacc[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            sacc[e] = ((acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e])) + (acc[4][e] + acc[5][e]);
         // online softmax (log2 domain) of rows g (keys 2t, 2t+1) and g + 8
         const int kidx = kbeg + it * kTcKeys + 8 * warp + 2 * t;
         float s00 = kidx < kend ? sacc[0] * scale_log2 : -CUDART_INF_F;
@@ -357,15 +394,20 @@ attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K,
         split_tf32(p10, pb[1], ps[1]);
         split_tf32(p01, pb[2], ps[2]);
         split_tf32(p11, pb[3], ps[3]);
+        if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                o[j][0] *= a0;
+                o[j][1] *= a0;
+                o[j][2] *= a1;
+                o[j][3] *= a1;
+            }
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            o[j][0] *= a0;
-            o[j][1] *= a0;
-            o[j][2] *= a1;
-            o[j][3] *= a1;
             uint32_t bb0, bs0, bb1, bs1;
-            split_tf32(vd[(2 * t) * kTcPad + 8 * j + g], bb0, bs0);
-            split_tf32(vd[(2 * t + 1) * kTcPad + 8 * j + g], bb1, bs1);
+            split_tf32(vd[swz_f(kr + 2 * t, 8 * j + g)], bb0, bs0);
+            split_tf32(vd[swz_f(kr + 2 * t + 1, 8 * j + g)], bb1, bs1);
             mma3(o[j], pb, ps, bb0, bb1, bs0, bs1);
         }
         __syncthreads();  // every warp is done with this buffer before it is refilled
@@ -382,35 +424,42 @@ attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K,
         wl[warp * kTcRows + g] = l0;
         wl[warp * kTcRows + g + 8] = l1;
     }
-    float *po = dsm + warp * kTcRows * 128;  // the (idle) tiles: [8][16][128] partial O
+    // the (idle) tiles: [8][16][136] partial O (rows padded: the float2
+    // stores of a half-warp hit distinct banks)
+    float *po = dsm + warp * kTcRows * kTcOPad;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        *reinterpret_cast<float2 *>(po + g * 128 + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
-        *reinterpret_cast<float2 *>(po + (g + 8) * 128 + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
+        *reinterpret_cast<float2 *>(po + g * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
+        *reinterpret_cast<float2 *>(po + (g + 8) * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
     }
     __syncthreads();
     // this CTA's rows: unnormalised O (over its keys), max M and sum L, in
     // the region after the 8 partials (read by the cluster's rank 0)
-    float *co = dsm + kTcWarpsD * kTcRows * 128;  // [16][128]
+    float *co = dsm + kTcWarpsD * kTcRows * kTcOPad;  // [16][128]
     float *cml = co + kTcRows * 128;              // [16][2]
-    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
-        const int r = i >> 7, d = i & 127;
+    if (threadIdx.x < kTcRows) {  // per row, once: M, each warp's weight (over its max), L
+        const int r = threadIdx.x;
         float M = -CUDART_INF_F;
 #pragma unroll
         for (int w = 0; w < kTcWarpsD; ++w) M = fmaxf(M, wm[w * kTcRows + r]);
-        float acc = 0.f, L = 0.f;
+        float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kTcWarpsD; ++w) {
             const float mw = wm[w * kTcRows + r];
             const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
-            acc += sw * dsm[(w * kTcRows + r) * 128 + d];
             L += sw * wl[w * kTcRows + r];
+            wm[w * kTcRows + r] = sw;
         }
+        cml[2 * r] = M;
+        cml[2 * r + 1] = L;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
+        const int r = i >> 7, d = i & 127;
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarpsD; ++w) acc += wm[w * kTcRows + r] * dsm[(w * kTcRows + r) * kTcOPad + d];
         co[i] = acc;
-        if (d == 0) {
-            cml[2 * r] = M;
-            cml[2 * r + 1] = L;
-        }
     }
     cluster.sync();  // both CTAs' rows are in shared memory
     if (rank == 0) {
@@ -429,6 +478,33 @@ attention_tc128_kernel(const float *__restrict__ Q, const float *__restrict__ K,
         }
     }
     cluster.sync();  // rank 1's shared memory stays until rank 0 has read it
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda): rows of 128 fp32, boxes of 64 rows x 32 floats, 128-byte
+// swizzle, zero fill past the last row.
+using EncodeTiledFnD = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_rows_map(CUtensorMap *tm, const float *base, long long rows) {
+    static EncodeTiledFnD fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFnD>(f);
+    });
+    if (!fn || rows <= 0 || rows > (1ll << 31)) return false;
+    cuuint64_t gdim[2] = {128, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {128 * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)kTcKeys};
+    cuuint32_t estride[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), gdim, gstride, box, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -455,11 +531,14 @@ extern "C" KVX_API int kvx_attention_dense(const float *Q, const float *K, const
     if (dim == kDD && aligned && !((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(out)) & 15) &&
         seq_q <= (int64_t)0x3fffffff) {
         static std::atomic<bool> attr_done[kMaxDevices];
-        if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
-        const unsigned tiles = (unsigned)((seq_q + kTcRows - 1) / kTcRows);
-        attention_tc128_kernel<<<2 * tiles, kTcWarpsD * 32, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
-            Q, K, V, out, (int)seq_q, (int)seq_k, s * 1.4426950408889634f);
-        return launch_status();
+        CUtensorMap tmk, tmv;
+        if (make_rows_map(&tmk, K, seq_k) && make_rows_map(&tmv, V, seq_k)) {
+            if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
+            const unsigned tiles = (unsigned)((seq_q + kTcRows - 1) / kTcRows);
+            attention_tc128_kernel<<<2 * tiles, kTcWarpsD * 32, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
+                Q, out, (int)seq_q, (int)seq_k, s * 1.4426950408889634f, tmk, tmv);
+            return launch_status();
+        }
     }
     if (dim == kDD && aligned) {
         attention_dense128_kernel<<<(unsigned)((seq_q + kDQ - 1) / kDQ), 256, 0, static_cast<cudaStream_t>(stream)>>>(
