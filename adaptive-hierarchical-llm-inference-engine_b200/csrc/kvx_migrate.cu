@@ -16,7 +16,9 @@ namespace {
 __global__ void __launch_bounds__(512)
 migrate_kernel(uint8_t *dev_base, int dev_cap, uint8_t *host_base, int host_cap,
                const int32_t *__restrict__ dev_frames, const int32_t *__restrict__ host_frames,
-               int num_frames, size_t frame_vecs, int to_device, int32_t *error_flag) {
+               int num_frames, size_t frame_vecs, int to_device, int32_t *error_flag,
+               const int32_t *__restrict__ num_frames_dev) {
+    if (num_frames_dev) num_frames = min(num_frames, *num_frames_dev);  // a count written on the device
     for (int f = blockIdx.x; f < num_frames; f += gridDim.x) {
         const int32_t dfi = dev_frames[f], hfi = host_frames[f];
         if (dfi < 0 || dfi >= dev_cap || hfi < 0 || hfi >= host_cap) {
@@ -64,6 +66,23 @@ extern "C" KVX_API int kvx_migrate_frames(void *dev_base, int32_t dev_capacity, 
     if (grid > num_frames) grid = num_frames;
     migrate_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<uint8_t *>(dev_base), dev_capacity, static_cast<uint8_t *>(host_base),
-        host_capacity, dev_frames, host_frames, num_frames, frame_bytes / 16, direction, error_flag);
+        host_capacity, dev_frames, host_frames, num_frames, frame_bytes / 16, direction, error_flag, nullptr);
+    return launch_status();
+}
+
+#include "kvx_tier_policy.h"
+
+int kvx_tier_dev::migrate_counted(void *dev_base, int32_t dev_capacity, void *host_base, int32_t host_capacity,
+                                  const int32_t *dev_frames, const int32_t *host_frames, const int32_t *count_dev,
+                                  int32_t max_frames, size_t frame_bytes, int32_t direction, int32_t ctas,
+                                  int32_t *error_flag, cudaStream_t st) {
+    if (!dev_base || !host_base || !dev_frames || !host_frames || !count_dev || max_frames < 0) return KVX_EINVAL;
+    if (frame_bytes == 0 || frame_bytes % 16 || (direction != 0 && direction != 1)) return KVX_EINVAL;
+    if (max_frames == 0) return KVX_OK;
+    int grid = ctas > 0 ? ctas : 16;
+    if (grid > max_frames) grid = max_frames;
+    migrate_kernel<<<grid, 512, 0, st>>>(static_cast<uint8_t *>(dev_base), dev_capacity,
+                                         static_cast<uint8_t *>(host_base), host_capacity, dev_frames, host_frames,
+                                         max_frames, frame_bytes / 16, direction, error_flag, count_dev);
     return launch_status();
 }

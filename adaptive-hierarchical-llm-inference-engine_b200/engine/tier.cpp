@@ -43,6 +43,8 @@
 #include "kvx_tier.h"
 
 #include <cuda_runtime.h>
+
+#include "../csrc/kvx_tier_policy.h"
 #include <fcntl.h>
 #include <unistd.h>
 
@@ -131,6 +133,14 @@ struct kvx_tier {
     int32_t *lists[2] = {};   // device copies of the same
     int32_t *err = nullptr;   // device error flag
     int last_parity = 0;
+
+    // device policy (config device_policy): the bookkeeping above lives on
+    // the device instead, in `pol`, and runs on s_pol
+    kvx_tier_dev::Policy *pol = nullptr;
+    cudaStream_t s_pol = nullptr;
+    cudaEvent_t ev_pol = nullptr, ev_caller = nullptr;
+    int32_t *d_frames = nullptr, *d_slot = nullptr, *d_evict = nullptr;  // host-array steps
+    uint8_t *d_hit = nullptr;
 };
 
 namespace {
@@ -246,6 +256,16 @@ int take_host_slot(kvx_tier *t, kvx_tier_stats &st, int32_t &hs) {
 }
 
 void release(kvx_tier *t) {
+    if (t->pol) {
+        if (t->s_pol) cudaStreamSynchronize(t->s_pol);
+        kvx_tier_dev::destroy(t->pol);
+        t->pol = nullptr;
+        if (t->s_pol) cudaStreamDestroy(t->s_pol);
+        if (t->ev_pol) cudaEventDestroy(t->ev_pol);
+        if (t->ev_caller) cudaEventDestroy(t->ev_caller);
+        for (void *q : {(void *)t->d_frames, (void *)t->d_slot, (void *)t->d_evict, (void *)t->d_hit})
+            if (q) cudaFree(q);
+    }
     if (!t->bookkeeping) {
         if (t->s_h2d) cudaStreamSynchronize(t->s_h2d);
         if (t->s_d2h) cudaStreamSynchronize(t->s_d2h);
@@ -351,6 +371,72 @@ int issue(kvx_tier *t, int parity) {
     return KVX_OK;
 }
 
+// The copies of a step planned on the device: the lists and their counts
+// are device arrays (kvx_tier_dev::lists), the launches read the counts
+// there; ordering as in issue().
+int issue_dev(kvx_tier *t, int parity) {
+    const int32_t *hd, *hh, *dd, *dh, *cnt;
+    kvx_tier_dev::lists(t->pol, parity, &hd, &hh, &dd, &dh, &cnt);
+    const int prev = parity ^ 1;
+    const int load_ctas = t->cfg.load_ctas > 0 ? t->cfg.load_ctas : 16;
+    const int store_ctas = t->cfg.store_ctas > 0 ? t->cfg.store_ctas : 4;
+    const int32_t dcap = (int32_t)t->dev_slots, hcap = (int32_t)t->host_slots, mx = (int32_t)t->cfg.max_step;
+    // write-backs: after the plan, and after the previous step's loads (host slots)
+    if (cudaStreamWaitEvent(t->s_d2h, t->ev_pol, 0) != cudaSuccess) return KVX_ECUDA;
+    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_d2h, t->ev_h2d[prev], 0) != cudaSuccess) return KVX_ECUDA;
+    int rc = kvx_tier_dev::migrate_counted(t->dev_base, dcap, t->host_base, hcap, dd, dh, cnt + 1, mx,
+                                           t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
+    if (rc != KVX_OK) return rc;
+    if (cudaEventRecord(t->ev_d2h[parity], t->s_d2h) != cudaSuccess) return KVX_ECUDA;
+    // loads: after the plan, the previous write-backs and the reads of step s-2
+    if (cudaStreamWaitEvent(t->s_h2d, t->ev_pol, 0) != cudaSuccess) return KVX_ECUDA;
+    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[prev], 0) != cudaSuccess) return KVX_ECUDA;
+    if (cudaStreamWaitEvent(t->s_h2d, t->ev_read[parity], 0) != cudaSuccess) return KVX_ECUDA;
+    rc = kvx_tier_dev::migrate_counted(t->dev_base, dcap, t->host_base, hcap, hd, hh, cnt, mx, t->cfg.frame_bytes, 1,
+                                       load_ctas, t->err, t->s_h2d);
+    if (rc != KVX_OK) return rc;
+    if (cudaEventRecord(t->ev_h2d[parity], t->s_h2d) != cudaSuccess) return KVX_ECUDA;
+    t->ev_used[parity] = true;
+    t->last_parity = parity;
+    return KVX_OK;
+}
+
+// One step planned on the device (policy kernels on s_pol), then its
+// copies.  With `wait_caller` the plan waits for the work queued on `caller`
+// (which produced `frames`; a null handle is the legacy default stream);
+// without, s_pol itself produced them.
+int step_device_core(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot, int32_t *evicted,
+                     uint8_t *hit, bool wait_caller, cudaStream_t caller) {
+    const int parity = (int)(t->step & 1);
+    if (wait_caller && (cudaEventRecord(t->ev_caller, caller) != cudaSuccess ||
+                        cudaStreamWaitEvent(t->s_pol, t->ev_caller, 0) != cudaSuccess))
+        return KVX_ECUDA;
+    // this parity's copy lists were read by the copies of step s-2
+    if (t->ev_used[parity] && (cudaStreamWaitEvent(t->s_pol, t->ev_h2d[parity], 0) != cudaSuccess ||
+                               cudaStreamWaitEvent(t->s_pol, t->ev_d2h[parity], 0) != cudaSuccess))
+        return KVX_ECUDA;
+    int rc = kvx_tier_dev::step(t->pol, parity, frames, n, dev_slot, hit, evicted, t->s_pol);
+    if (rc == KVX_OK && cudaEventRecord(t->ev_pol, t->s_pol) != cudaSuccess) rc = KVX_ECUDA;
+    if (rc == KVX_OK) rc = issue_dev(t, parity);
+    ++t->step;
+    return rc;
+}
+
+int setup_policy(kvx_tier *t, int64_t resident0) {
+    const int64_t mx = t->cfg.max_step;
+    int rc = kvx_tier_dev::create(&t->pol, t->cfg.universe, t->cfg.capacity, resident0, t->dev_slots, t->host_slots,
+                                  t->host_cap, mx);
+    if (rc != KVX_OK) return rc;
+    if (cudaStreamCreateWithFlags(&t->s_pol, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->ev_pol, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->ev_caller, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&t->d_frames, mx * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&t->d_slot, mx * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&t->d_evict, mx * sizeof(int32_t)) != cudaSuccess || cudaMalloc(&t->d_hit, mx) != cudaSuccess)
+        return KVX_ENOSPC;
+    return KVX_OK;
+}
+
 }  // namespace
 
 extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **out) {
@@ -376,6 +462,22 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
     if (t->dev_slots > INT32_MAX || t->host_slots > INT32_MAX) {
         delete t;
         return KVX_EINVAL;
+    }
+    if (cfg->device_policy) {  // bookkeeping on the device: RAM tier only, a bounded step
+        if (cfg->device < 0 || cfg->host_frames > 0 || cfg->max_step <= 0 || cfg->max_step >= C || U <= C) {
+            delete t;
+            return KVX_EINVAL;
+        }
+        t->resident = resident0;
+        int rc = setup_device(t);
+        if (rc == KVX_OK) rc = setup_policy(t, resident0);
+        if (rc != KVX_OK) {
+            release(t);
+            delete t;
+            return rc;
+        }
+        *out = t;
+        return KVX_OK;
     }
     try {
         t->dslot.assign(U, -1);
@@ -451,16 +553,72 @@ extern "C" KVX_API int kvx_tier_host_arena(kvx_tier *t, void **base, int64_t *sl
 extern "C" KVX_API int kvx_tier_location(kvx_tier *t, int64_t frame, int32_t *tier, int64_t *slot) {
     if (!t || frame < 0 || frame >= t->cfg.universe) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
+    if (t->pol) {
+        return kvx_tier_dev::location(t->pol, frame, tier, slot, t->s_pol);
+    }
     const bool on_dev = t->dslot[frame] >= 0, in_ram = !on_dev && t->hslot[frame] >= 0;
     if (tier) *tier = on_dev ? 0 : in_ram ? 1 : 2;
     if (slot) *slot = on_dev ? t->dslot[frame] : in_ram ? t->hslot[frame] : frame;
     return KVX_OK;
 }
 
+extern "C" KVX_API int kvx_tier_step_device(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
+                                            int32_t *evicted, uint8_t *hit, void *stream) {
+    if (!t) return KVX_EINVAL;
+    if (!t->pol) return KVX_EUNSUPPORTED;
+    if (n < 0 || n > t->cfg.max_step || (n > 0 && (!frames || !dev_slot))) return KVX_EINVAL;
+    std::lock_guard<std::mutex> lk(t->mu);
+    return step_device_core(t, frames, n, dev_slot, evicted, hit, true, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+// kvx_tier_step (host arrays) on a store whose bookkeeping is on the device:
+// through the device and back, waiting; per-step stats from the totals.
+int step_host_via_device(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot, int32_t *evicted,
+                         uint8_t *hit, kvx_tier_stats *stats) {
+    if (n > t->cfg.max_step) return KVX_EINVAL;
+    kvx_tier_stats before{}, after{};
+    int32_t err = 0;
+    int rc = kvx_tier_dev::totals(t->pol, &before, t->s_pol);
+    if (rc == KVX_OK) rc = kvx_tier_dev::error(t->pol, &err, true, t->s_pol);
+    if (rc != KVX_OK) return rc;
+    if (n > 0 && cudaMemcpyAsync(t->d_frames, frames, n * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_pol) !=
+                     cudaSuccess)
+        return KVX_ECUDA;
+    rc = step_device_core(t, t->d_frames, n, t->d_slot, evicted ? t->d_evict : nullptr, hit ? t->d_hit : nullptr,
+                          false, nullptr);
+    if (rc != KVX_OK) return rc;
+    if (n > 0 &&
+        (cudaMemcpyAsync(dev_slot, t->d_slot, n * sizeof(int32_t), cudaMemcpyDeviceToHost, t->s_pol) != cudaSuccess ||
+         (evicted && cudaMemcpyAsync(evicted, t->d_evict, n * sizeof(int32_t), cudaMemcpyDeviceToHost, t->s_pol) !=
+                         cudaSuccess) ||
+         (hit && cudaMemcpyAsync(hit, t->d_hit, n, cudaMemcpyDeviceToHost, t->s_pol) != cudaSuccess)))
+        return KVX_ECUDA;
+    if (cudaStreamSynchronize(t->s_pol) != cudaSuccess) return KVX_ECUDA;
+    rc = kvx_tier_dev::error(t->pol, &err, true, t->s_pol);
+    if (rc != KVX_OK) return rc;
+    if (err) return (err & 2) ? KVX_ENOSPC : KVX_EINVAL;  // rejected on the device, nothing changed
+    rc = kvx_tier_dev::totals(t->pol, &after, t->s_pol);
+    if (rc != KVX_OK) return rc;
+    kvx_tier_stats st{};
+    st.accesses = after.accesses - before.accesses;
+    st.hits = after.hits - before.hits;
+    st.misses = after.misses - before.misses;
+    st.evictions = after.evictions - before.evictions;
+    st.reloads = after.reloads - before.reloads;
+    st.frames_h2d = after.frames_h2d - before.frames_h2d;
+    st.frames_d2h = after.frames_d2h - before.frames_d2h;
+    t->totals = after;
+    if (stats) *stats = st;
+    return KVX_OK;
+}
+}  // namespace
+
 extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
                                      int32_t *evicted, uint8_t *hit, kvx_tier_stats *stats) {
     if (!t || n < 0 || (n > 0 && (!frames || !dev_slot))) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
+    if (t->pol) return step_host_via_device(t, frames, n, dev_slot, evicted, hit, stats);
     if (n >= t->cfg.capacity && t->cfg.universe > t->cfg.capacity) return KVX_EINVAL;
     const int64_t s = t->step;
     // pre-pass: ids valid, and the distinct frames to load fit the free slots
@@ -615,6 +773,11 @@ extern "C" KVX_API int kvx_tier_mark_read(kvx_tier *t, void *stream) {
 extern "C" KVX_API int kvx_tier_sync(kvx_tier *t) {
     if (!t) return KVX_EINVAL;
     if (t->bookkeeping) return KVX_OK;
+    if (t->pol) {  // the plan's stream, and a step the device rejected
+        int32_t perr = 0;
+        if (kvx_tier_dev::error(t->pol, &perr, true, t->s_pol) != KVX_OK) return KVX_ECUDA;  // reported once
+        if (perr) return (perr & 2) ? KVX_ENOSPC : KVX_EINVAL;
+    }
     if (cudaStreamSynchronize(t->s_h2d) != cudaSuccess || cudaStreamSynchronize(t->s_d2h) != cudaSuccess)
         return KVX_ECUDA;
     int32_t e = 0;
@@ -625,6 +788,9 @@ extern "C" KVX_API int kvx_tier_sync(kvx_tier *t) {
 extern "C" KVX_API int kvx_tier_totals(kvx_tier *t, kvx_tier_stats *stats) {
     if (!t || !stats) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
+    if (t->pol) {
+        return kvx_tier_dev::totals(t->pol, stats, t->s_pol);
+    }
     *stats = t->totals;
     return KVX_OK;
 }
@@ -637,6 +803,20 @@ int frame_io(kvx_tier *t, int64_t frame, void *buf, bool to_store) {
     if (rc != KVX_OK) return rc;
     std::lock_guard<std::mutex> lk(t->mu);
     const size_t fb = t->cfg.frame_bytes;
+    if (t->pol) {  // where the device's bookkeeping says the frame is
+        int32_t tier = 0;
+        int64_t slot = 0;
+        rc = kvx_tier_dev::location(t->pol, frame, &tier, &slot, t->s_pol);
+        if (rc != KVX_OK) return rc;
+        if (tier == 0) {
+            uint8_t *d = t->dev_base + (size_t)slot * fb;
+            return cuda_status(to_store ? cudaMemcpy(d, buf, fb, cudaMemcpyHostToDevice)
+                                        : cudaMemcpy(buf, d, fb, cudaMemcpyDeviceToHost));
+        }
+        uint8_t *h = t->host_base + (size_t)slot * fb;
+        if (to_store) std::memcpy(h, buf, fb); else std::memcpy(buf, h, fb);
+        return KVX_OK;
+    }
     if (t->dslot[frame] >= 0) {
         uint8_t *d = t->dev_base + (size_t)t->dslot[frame] * fb;
         return cuda_status(to_store ? cudaMemcpy(d, buf, fb, cudaMemcpyHostToDevice)

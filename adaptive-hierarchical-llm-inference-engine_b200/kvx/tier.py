@@ -26,7 +26,8 @@ from . import HEAD_DIM, KVX_F16, PAGE_TOKENS, KvPaged, _check, lib
 class TierConfig(C.Structure):
     _fields_ = [("frame_bytes", C.c_size_t), ("universe", C.c_int64), ("capacity", C.c_int64),
                 ("spare", C.c_int64), ("device", C.c_int32), ("load_ctas", C.c_int32),
-                ("store_ctas", C.c_int32), ("host_frames", C.c_int64), ("spill_path", C.c_char_p)]
+                ("store_ctas", C.c_int32), ("host_frames", C.c_int64), ("spill_path", C.c_char_p),
+                ("device_policy", C.c_int32), ("max_step", C.c_int64)]
 
 
 _STAT_FIELDS = ("accesses", "hits", "misses", "evictions", "reloads", "frames_h2d", "frames_d2h",
@@ -49,6 +50,7 @@ lib.kvx_tier_device_arena.argtypes = [_vp, C.POINTER(_vp), C.POINTER(_i64)]
 lib.kvx_tier_host_arena.argtypes = [_vp, C.POINTER(_vp), C.POINTER(_i64)]
 lib.kvx_tier_location.argtypes = [_vp, _i64, C.POINTER(C.c_int32), C.POINTER(_i64)]
 lib.kvx_tier_step.argtypes = [_vp, _vp, _i64, _vp, _vp, _vp, C.POINTER(TierStats)]
+lib.kvx_tier_step_device.argtypes = [_vp, _vp, _i64, _vp, _vp, _vp, _vp]
 lib.kvx_tier_wait_resident.argtypes = [_vp, _vp]
 lib.kvx_tier_mark_read.argtypes = [_vp, _vp]
 lib.kvx_tier_sync.argtypes = [_vp]
@@ -56,6 +58,7 @@ lib.kvx_tier_totals.argtypes = [_vp, C.POINTER(TierStats)]
 lib.kvx_tier_write_frame.argtypes = [_vp, _i64, _vp]
 lib.kvx_tier_read_frame.argtypes = [_vp, _i64, _vp]
 for _fn in ("kvx_tier_device_arena", "kvx_tier_host_arena", "kvx_tier_location", "kvx_tier_step",
+            "kvx_tier_step_device",
             "kvx_tier_wait_resident", "kvx_tier_mark_read", "kvx_tier_sync", "kvx_tier_totals",
             "kvx_tier_write_frame", "kvx_tier_read_frame"):
     getattr(lib, _fn).restype = C.c_int
@@ -82,10 +85,12 @@ class _DeviceBytes:
 
 class Tier:
     def __init__(self, frame_bytes, universe, capacity, spare, device=0, load_ctas=0, store_ctas=0,
-                 host_frames=0, spill_path=None):
+                 host_frames=0, spill_path=None, device_policy=False, max_step=0):
+        """device_policy: the LRU bookkeeping runs as kernels on the device
+        (step_device takes device tensors); max_step bounds a step's accesses."""
         self._path = None if spill_path is None else str(spill_path).encode()
         self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, load_ctas, store_ctas,
-                              host_frames, self._path)
+                              host_frames, self._path, 1 if device_policy else 0, max_step)
         h = _vp()
         _check("kvx_tier_create", lib.kvx_tier_create(C.byref(self.cfg), C.byref(h)))
         self.h = h
@@ -159,6 +164,17 @@ class Tier:
         _check("kvx_tier_step", lib.kvx_tier_step(self.h, _np_ptr(frames), n, _np_ptr(dev_slot),
                                                   _np_ptr(ev), _np_ptr(ht), C.byref(st)))
         return dev_slot, ev, ht, st.as_dict()
+
+    def step_device(self, frames, dev_slot, evicted=None, hit=None, stream=None):
+        """A step planned on the device (device_policy stores): frames, dev_slot
+        and the optional evicted (int32) / hit (uint8) are CUDA tensors; the
+        plan runs after the work queued on `stream`, dev_slot is ready for work
+        that waits with wait_resident."""
+        def p(t):
+            return None if t is None else _vp(t.data_ptr())
+        _check("kvx_tier_step_device",
+               lib.kvx_tier_step_device(self.h, p(frames), frames.numel(), p(dev_slot), p(evicted), p(hit),
+                                        _stream_ptr(stream)))
 
     def _sp(self, stream):
         return _vp(0) if self.cfg.device < 0 else _stream_ptr(stream)

@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--tier-ram-gb", type=float, default=0.0,
                     help="config 4: RAM tier size (0: every non-resident frame in pinned RAM; "
                          "else the rest go to a spill file, the disk tier)")
+    ap.add_argument("--tier-device-policy", action="store_true",
+                    help="config 4: the LRU bookkeeping as kernels on the device (kvx_tier_step_device): "
+                         "the step's ids go up, the block tables come out of the policy, no host planning")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     ap.add_argument("--kernels", action="store_true",
@@ -1086,6 +1089,37 @@ def select_timing(n):
     return out
 
 
+def device_plan_timing(U, C, S, n, step_ids, warm, steps=8):
+    """Latency of one device-planned step (kvx_tier_step_device) at config
+    4's geometry, copies made negligible by 16-byte frames: CUDA events on
+    the caller's stream around the plan and kvx_tier_wait_resident."""
+    import torch
+    from kvx.tier import Tier
+    t = Tier(16, U, C, S, device=0, device_policy=True, max_step=n)
+    for k in range(warm):
+        ids = step_ids(k)
+        for o in range(0, ids.size, 16384):
+            t.step(ids[o:o + 16384], evicted=False, hit=False)
+    t.sync()
+    ids_d = [torch.from_numpy(step_ids(warm + k)).cuda() for k in range(steps)]
+    slots = torch.empty(n, dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for k in range(steps):
+        ev[k][0].record(st)
+        t.step_device(ids_d[k], slots, stream=st)
+        t.wait_resident(st)
+        ev[k][1].record(st)
+        t.mark_read(st)
+        st.synchronize()
+    t.sync()
+    us = sorted(a.elapsed_time(b) * 1e3 for a, b in ev)
+    t.close()
+    return {"median_us": round(us[len(us) // 2], 1), "min_us": round(us[0], 1), "steps": steps,
+            "how": "16-byte frames, same ids and capacity; events around kvx_tier_step_device + wait_resident"}
+
+
 def run_config4(args):
     """Tiered eviction under memory pressure.  Llama-3.2-3B KV (28 layers, 8
     kv heads x 128, fp16) at batch 16 with 65,536-token contexts: 1,835,008
@@ -1123,9 +1157,11 @@ def run_config4(args):
         return (base + np.take_along_axis(perms, r, axis=1)).astype(np.int32).ravel()
 
     t0 = time.perf_counter()
+    dpol = bool(args.tier_device_policy) and not H
     tier = Tier(FB, U, C, S, device=0, load_ctas=int(os.environ.get("KVX_TIER_LOAD_CTAS", "0")),
                 store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")), host_frames=H,
-                spill_path=None if not H else os.path.join(spill_dir, "frames.bin"))
+                spill_path=None if not H else os.path.join(spill_dir, "frames.bin"),
+                device_policy=dpol, max_step=rows * ACC if dpol else 0)
     alloc_s = time.perf_counter() - t0
     dev = tier.device_tensor()
     host = tier.host_array()
@@ -1167,6 +1203,11 @@ def run_config4(args):
     bt_dev = [torch.empty((L, B, ACC), dtype=torch.int32, device="cuda") for _ in range(2)]
     up = [torch.cuda.Event() for _ in range(2)]
     stream_ids = [step_ids(warm + k) for k in range(steps)]
+    if dpol:  # the step's ids go up from pinned memory; the policy writes the block table
+        ids_pinned = torch.from_numpy(np.stack(stream_ids)).pin_memory()
+        ids_dev = [torch.empty(rows * ACC, dtype=torch.int32, device="cuda") for _ in range(2)]
+        plan = torch.cuda.Stream()  # plans run ahead of the decode stream, beside the copies
+        dec_done = [torch.cuda.Event() for _ in range(2)]
     before = tier.totals()
     torch.cuda.synchronize()
     clocks = ClockSampler(torch.cuda.current_device())
@@ -1176,17 +1217,29 @@ def run_config4(args):
     e0.record()
     for k in range(steps):
         p = k & 1
-        if k >= 2:
-            up[p].synchronize()  # the block-table upload of step k-2 read this buffer
-        h0 = time.perf_counter()
-        tier.step(stream_ids[k], dev_slot=bt_host[p].numpy(), evicted=False, hit=False)
-        plan_s += time.perf_counter() - h0
-        tier.wait_resident()
-        bt_dev[p].view(-1).copy_(bt_host[p], non_blocking=True)
-        up[p].record()
+        if dpol:
+            with torch.cuda.stream(plan):
+                if k >= 2:  # step k-2's decode read bt_dev[p] (and waited for its plan, which read ids_dev[p])
+                    plan.wait_event(dec_done[p])
+                ids_dev[p].copy_(ids_pinned[k], non_blocking=True)
+            h0 = time.perf_counter()
+            tier.step_device(ids_dev[p], bt_dev[p].view(-1), stream=plan)
+            plan_s += time.perf_counter() - h0
+            tier.wait_resident()
+        else:
+            if k >= 2:
+                up[p].synchronize()  # the block-table upload of step k-2 read this buffer
+            h0 = time.perf_counter()
+            tier.step(stream_ids[k], dev_slot=bt_host[p].numpy(), evicted=False, hit=False)
+            plan_s += time.perf_counter() - h0
+            tier.wait_resident()
+            bt_dev[p].view(-1).copy_(bt_host[p], non_blocking=True)
+            up[p].record()
         for l in range(L):
             kvx.decode(pool, bt_dev[p][l], lens, q[l], out=out[l], workspace=ws)
         tier.mark_read()
+        if dpol:
+            dec_done[p].record()
     e1.record()
     tier.sync()
     torch.cuda.synchronize()
@@ -1199,6 +1252,7 @@ def run_config4(args):
                                               workspace=ws) for l in range(L)], 3)
     dec_bytes = rows * ACC * FB
     sel = select_timing(C)
+    dplan = device_plan_timing(U, C, S, rows * ACC, step_ids, warm) if not H else None
     h2d_gbs = mv["frames_h2d"] * FB / (ms / 1e3) / 1e9
     d2h_gbs = mv["frames_d2h"] * FB / (ms / 1e3) / 1e9
     peak, peak_kind = peaks()
@@ -1221,7 +1275,9 @@ def run_config4(args):
                    "ms_alone_per_step": round(dec_ms, 3),
                    "GBps_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9, 1),
                    "frac_of_hbm_peak_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9 / peak, 3)},
+        "policy": "device (kvx_tier_step_device)" if dpol else "host (kvx_tier_step)",
         "host_plan_ms_per_step": round(plan_s / steps * 1e3, 3),
+        "device_plan_latency": dplan,
         "victim_select": sel,
         "disk_tier": None if not H else {
             "ram_tier_GB": round(H * FB / 1e9, 1), "spill_file_GB": round(U * FB / 1e9, 1),

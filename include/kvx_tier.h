@@ -78,6 +78,11 @@ typedef struct kvx_tier_config {
                             of the host link busy when they run together */
     int64_t host_frames; /* RAM tier size; 0: every non-resident frame in RAM (no disk) */
     const char *spill_path; /* disk tier file (created / truncated) when host_frames > 0 */
+    int32_t device_policy;  /* 1: the policy's bookkeeping (recency, free slots, copy lists)
+                               lives on the device and runs as kernels: steps take device
+                               arrays (kvx_tier_step_device) and no host work is left per
+                               step.  RAM tier only (host_frames 0), device >= 0 */
+    int64_t max_step;       /* device_policy: accesses per step at most (< capacity) */
 } kvx_tier_config;
 
 typedef struct kvx_tier_stats {
@@ -122,6 +127,19 @@ KVX_API int kvx_tier_read_frame(kvx_tier *t, int64_t frame, void *buf);
  * step misses more frames than `spare` can take (nothing is changed then). */
 KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
                           int32_t *evicted, uint8_t *hit, kvx_tier_stats *stats);
+/* A step with its bookkeeping on the device (config device_policy = 1):
+ * frames, dev_slot, evicted, hit are DEVICE arrays; the policy's kernels run
+ * on the store's own stream after the work queued so far on `stream` (so
+ * `frames` may be written there), the copies follow them, and dev_slot is
+ * ready for work that waits with kvx_tier_wait_resident (work queued on
+ * `stream` after that wait may rewrite frames and the outputs).  Decisions are
+ * KVManager's, exactly as kvx_tier_step makes them; placement (which free
+ * slot a load takes) may differ.  n <= max_step.  A step with an id out of
+ * range or more loads than free slots is rejected on the device (nothing
+ * changes) and reported by kvx_tier_sync (KVX_EINVAL, KVX_ENOSPC).  Host-array
+ * kvx_tier_step on such a store copies through the device and waits. */
+KVX_API int kvx_tier_step_device(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
+                                 int32_t *evicted, uint8_t *hit, void *stream);
 /* Make `stream` wait until every frame of the last step is resident. */
 KVX_API int kvx_tier_wait_resident(kvx_tier *t, void *stream);
 /* The reads of the last step's frames have been enqueued on `stream`; a

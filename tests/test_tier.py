@@ -15,7 +15,7 @@ import pytest
 import kvgen
 
 from kvx import KvxError
-from kvx.tier import Tier
+from kvx.tier import Tier, lib
 
 
 def zipf_stream(seed, steps, per_step, universe):
@@ -130,3 +130,20 @@ def test_disk_tier_policy_and_placement(oracle):
     assert tot["frames_disk_read"] > 0 and tot["frames_disk_write"] > 0
     with pytest.raises(KvxError):
         Tier(4096, universe, capacity, spare, device=-1, host_frames=3 * spare - 1, spill_path="x")
+
+
+def test_device_policy_config_is_checked():
+    """device_policy stores keep their bookkeeping on a device: a
+    bookkeeping-only store, a disk tier, a step bound of capacity or more
+    and a universe that fits the device are refused before any device is
+    touched; the device-array step is refused on a host-policy store."""
+    for kw in ({"device": -1, "max_step": 10}, {"device": 0, "max_step": 0}, {"device": 0, "max_step": 20},
+               {"device": 0, "max_step": 10, "host_frames": 40, "spill_path": "/nonexistent/x"}):
+        with pytest.raises(KvxError) as e:
+            Tier(64, 100, 20, 3, device_policy=True, **kw)
+        assert e.value.status == -1, kw
+    with pytest.raises(KvxError) as e:
+        Tier(64, 20, 20, 3, device=0, device_policy=True, max_step=10)  # everything resident
+    assert e.value.status == -1
+    t = Tier(64, 100, 20, 3, device=-1)
+    assert lib.kvx_tier_step_device(t.h, None, 0, None, None, None, None) == -4
