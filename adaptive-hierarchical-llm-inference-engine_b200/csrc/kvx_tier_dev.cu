@@ -37,16 +37,16 @@ namespace {
 constexpr int kT = 1024;     // threads of the single-CTA kernels
 
 // control block (device int64)
-enum { kHead, kBase, kResident, kDevFree, kHostFree, kErr, kCompact, kAccesses, kHits, kMisses, kEvictions,
-       kReloads, kH2d, kD2h, kCtlN };
+enum { kHead, kBase, kResident, kDevFree, kDevHead, kHostFree, kErr, kCompact, kAccesses, kHits, kMisses,
+       kEvictions, kReloads, kH2d, kD2h, kCtlN };
 // per-step counts (device int32): loads, write-backs, misses of non-resident
 // frames, events (misses), evictions, step rejected, and the free lists'
-// tops before the step
-enum { cLoads, cWbs, cM0, cEvents, cEvict, cBad, cDevTop, cHostTop, cCountsN };
+// state before the step (device: count and head of the FIFO; host: stack top)
+enum { cLoads, cWbs, cM0, cEvents, cEvict, cBad, cDevTop, cDevHead, cHostTop, cCountsN };
 
 struct View {  // the policy's device arrays, passed by value to the kernels
-    int64_t U, C, W, max_n;
-    long long *stamp, *ctl;
+    int64_t U, C, W, max_n, dev_slots;
+    long long *stamp, *ctl, *freed_at;  // freed_at: per device slot, the step that freed it
     int32_t *dslot, *hslot, *first, *evict_ev, *log, *tmp, *dev_free, *host_free;
     int32_t *m0flag, *m0list, *ev_time, *ev_victim, *ev_of_time, *heap;
     int32_t *h2d_dev, *h2d_host, *d2h_dev, *d2h_host, *counts;
@@ -94,8 +94,10 @@ __global__ void init_kernel(View s, int64_t resident0, int64_t host_cap, int64_t
         if (res) s.log[f] = (int32_t)f;
     }
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s.max_n; i += stride) s.ev_of_time[i] = -1;
-    for (int64_t d = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; d < dev_slots - resident0; d += stride)
-        s.dev_free[d] = (int32_t)(dev_slots - 1 - d);  // popped from the top: slot resident0 first
+    for (int64_t d = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; d < dev_slots; d += stride) {
+        if (d < dev_slots - resident0) s.dev_free[d] = (int32_t)(resident0 + d);  // a FIFO from slot resident0
+        s.freed_at[d] = LLONG_MIN / 2;  // never used: free for any step
+    }
     for (int64_t h = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; h < host_slots - host_cap; h += stride)
         s.host_free[h] = (int32_t)(host_slots - 1 - h);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -103,6 +105,7 @@ __global__ void init_kernel(View s, int64_t resident0, int64_t host_cap, int64_t
         s.ctl[kBase] = resident0;
         s.ctl[kResident] = resident0;
         s.ctl[kDevFree] = dev_slots - resident0;
+        s.ctl[kDevHead] = 0;
         s.ctl[kHostFree] = host_slots - host_cap;
     }
 }
@@ -128,7 +131,7 @@ __global__ void classify_kernel(View s, const int32_t *__restrict__ frames, int 
 }
 
 // the misses in time order, and the step's room check (one CTA)
-__global__ void __launch_bounds__(kT) scan_kernel(View s, int n) {
+__global__ void __launch_bounds__(kT) scan_kernel(View s, int n, long long min_freed) {
     __shared__ int ws[33];
     int base = 0, tot = 0;
     for (int i0 = 0; i0 < n; i0 += kT) {
@@ -140,9 +143,15 @@ __global__ void __launch_bounds__(kT) scan_kernel(View s, int n) {
     }
     if (threadIdx.x == 0) {
         s.counts[cM0] = base;
-        // every such miss loads into a free device slot, and a write-back
-        // (at most one per such miss) takes a free host slot
-        if ((long long)base > s.ctl[kDevFree] || (long long)base > s.ctl[kHostFree]) s.counts[cBad] |= 2;
+        // every such miss loads into a free device slot freed by step
+        // min_freed or earlier (the FIFO's first `base` entries), and a
+        // write-back (at most one per such miss) takes a free host slot
+        if ((long long)base > s.ctl[kDevFree] || (long long)base > s.ctl[kHostFree]) {
+            s.counts[cBad] |= 2;
+        } else if (base > 0) {
+            const int32_t last = s.dev_free[(s.ctl[kDevHead] + base - 1) % s.dev_slots];
+            if (s.freed_at[last] > min_freed) s.counts[cBad] |= 2;
+        }
         if (s.counts[cBad]) atomicOr(reinterpret_cast<unsigned long long *>(&s.ctl[kErr]),
                                      (unsigned long long)s.counts[cBad]);
     }
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(kT) apply_kernel(View s, const int32_t *__rest
     __shared__ int ws[33];
     if (s.counts[cBad]) return;
     const int E = s.counts[cEvents];
-    const long long dev_top = s.ctl[kDevFree], host_top = s.ctl[kHostFree];
+    const long long dev_head = s.ctl[kDevHead], host_top = s.ctl[kHostFree];
     int lb = 0, wb = 0, vb = 0, tot = 0;
     for (int k0 = 0; k0 < E; k0 += kT) {
         const int k = k0 + threadIdx.x;
@@ -376,7 +385,7 @@ __global__ void __launch_bounds__(kT) apply_kernel(View s, const int32_t *__rest
         block_scan(v >= 0 ? 1 : 0, ws, &tot);
         vb += tot;
         if (is_load) {
-            const int32_t ds = s.dev_free[dev_top - 1 - lo];
+            const int32_t ds = s.dev_free[(dev_head + lo) % s.dev_slots];
             s.h2d_dev[lo] = ds;
             s.h2d_host[lo] = s.hslot[f];
             s.dslot[f] = ds;
@@ -394,7 +403,8 @@ __global__ void __launch_bounds__(kT) apply_kernel(View s, const int32_t *__rest
         s.counts[cLoads] = lb;
         s.counts[cWbs] = wb;
         s.counts[cEvict] = vb;
-        s.counts[cDevTop] = (int32_t)dev_top;
+        s.counts[cDevTop] = (int32_t)s.ctl[kDevFree];
+        s.counts[cDevHead] = (int32_t)dev_head;
         s.counts[cHostTop] = (int32_t)host_top;
     }
 }
@@ -421,12 +431,12 @@ __global__ void finish_kernel(View s, const int32_t *__restrict__ frames, int n,
 
 // after finish: first touches and eviction marks reset, freed slots pushed,
 // counters and totals; the compaction flag when the log is nearly full
-__global__ void commit_kernel(View s, const int32_t *__restrict__ frames, int n) {
+__global__ void commit_kernel(View s, const int32_t *__restrict__ frames, int n, long long step_no) {
     const bool bad = s.counts[cBad] != 0;
     const int loads = bad ? 0 : s.counts[cLoads], wbs = bad ? 0 : s.counts[cWbs];
     const int E = bad ? 0 : s.counts[cEvents];
-    // the tops as apply_kernel saw them (thread 0 of block 0 updates ctl below)
-    const long long dev_top = s.counts[cDevTop], host_top = s.counts[cHostTop];
+    // the free lists as apply_kernel saw them (thread 0 of block 0 updates ctl below)
+    const long long dev_cnt = s.counts[cDevTop], dev_head = s.counts[cDevHead], host_top = s.counts[cHostTop];
     const int stride = gridDim.x * blockDim.x, id = blockIdx.x * blockDim.x + threadIdx.x;
     for (int i = id; i < n; i += stride) {
         const int32_t f = frames[i];
@@ -436,10 +446,15 @@ __global__ void commit_kernel(View s, const int32_t *__restrict__ frames, int n)
         const int32_t v = s.ev_victim[k];
         if (v >= 0) s.evict_ev[v] = -1;
     }
-    for (int w = id; w < wbs; w += stride) s.dev_free[dev_top - loads + w] = s.d2h_dev[w];
+    for (int w = id; w < wbs; w += stride) {  // appended behind the FIFO's last entry
+        const int32_t d = s.d2h_dev[w];
+        s.dev_free[(dev_head + dev_cnt + w) % s.dev_slots] = d;
+        s.freed_at[d] = step_no;
+    }
     for (int l = id; l < loads; l += stride) s.host_free[host_top - wbs + l] = s.h2d_host[l];
     if (id == 0 && !bad) {
-        s.ctl[kDevFree] = dev_top - loads + wbs;
+        s.ctl[kDevFree] = dev_cnt - loads + wbs;
+        s.ctl[kDevHead] = (dev_head + loads) % s.dev_slots;
         s.ctl[kHostFree] = host_top - wbs + loads;
         s.ctl[kResident] += E - s.counts[cEvict];
         s.ctl[kAccesses] += n;
@@ -516,8 +531,9 @@ int create(Policy **out, int64_t U, int64_t C, int64_t resident0, int64_t dev_sl
     v.U = U;
     v.C = C;
     v.max_n = max_n;
+    v.dev_slots = dev_slots;
     v.W = 4 * C + 2 * max_n;
-    bool ok = dalloc(&v.stamp, U) && dalloc(&v.ctl, kCtlN) && dalloc(&v.dslot, U) && dalloc(&v.hslot, U) &&
+    bool ok = dalloc(&v.stamp, U) && dalloc(&v.ctl, kCtlN) && dalloc(&v.freed_at, dev_slots) && dalloc(&v.dslot, U) && dalloc(&v.hslot, U) &&
               dalloc(&v.first, U) && dalloc(&v.evict_ev, U) && dalloc(&v.log, v.W) && dalloc(&v.tmp, C) &&
               dalloc(&v.dev_free, dev_slots) && dalloc(&v.host_free, host_slots) && dalloc(&v.m0flag, max_n) &&
               dalloc(&v.m0list, max_n) && dalloc(&v.ev_time, max_n) && dalloc(&v.ev_victim, max_n) &&
@@ -542,7 +558,7 @@ int create(Policy **out, int64_t U, int64_t C, int64_t resident0, int64_t dev_sl
 void destroy(Policy *p) {
     if (!p) return;
     View &v = p->v;
-    void *ptrs[] = {v.stamp, v.ctl, v.dslot, v.hslot, v.first, v.evict_ev, v.log, v.tmp, v.dev_free, v.host_free,
+    void *ptrs[] = {v.stamp, v.ctl, v.freed_at, v.dslot, v.hslot, v.first, v.evict_ev, v.log, v.tmp, v.dev_free, v.host_free,
                     v.m0flag, v.m0list, v.ev_time, v.ev_victim, v.ev_of_time, v.heap, v.h2d_dev, v.h2d_host, v.d2h_dev,
                     v.d2h_host, v.counts, p->scratch};
     for (void *q : ptrs)
@@ -563,8 +579,8 @@ View at_parity(const View &v0, int parity) {
     return v;
 }
 
-int step(Policy *p, int parity, const int32_t *frames, int64_t n, int32_t *dev_slot, uint8_t *hit,
-         int32_t *evicted, cudaStream_t st) {
+int step(Policy *p, int parity, int64_t step_no, int64_t min_freed, const int32_t *frames, int64_t n,
+         int32_t *dev_slot, uint8_t *hit, int32_t *evicted, cudaStream_t st) {
     if (!p || n < 0 || n > p->v.max_n || (n > 0 && (!frames || !dev_slot))) return KVX_EINVAL;
     const View v = at_parity(p->v, parity & 1);
     if (cudaMemsetAsync(v.counts, 0, cCountsN * sizeof(int32_t), st) != cudaSuccess) return KVX_ECUDA;
@@ -573,11 +589,11 @@ int step(Policy *p, int parity, const int32_t *frames, int64_t n, int32_t *dev_s
     if (n > 0) {
         touch_kernel<<<grid, 256, 0, st>>>(v, frames, ni);
         classify_kernel<<<grid, 256, 0, st>>>(v, frames, ni);
-        scan_kernel<<<1, kT, 0, st>>>(v, ni);
+        scan_kernel<<<1, kT, 0, st>>>(v, ni, (long long)min_freed);
         merge_kernel<<<1, kT, 0, st>>>(v, ni);
         apply_kernel<<<1, kT, 0, st>>>(v, frames);
         finish_kernel<<<grid, 256, 0, st>>>(v, frames, ni, dev_slot, hit, evicted);
-        commit_kernel<<<grid, 256, 0, st>>>(v, frames, ni);
+        commit_kernel<<<grid, 256, 0, st>>>(v, frames, ni, (long long)step_no);
         compact_kernel<<<1, kT, 0, st>>>(v);
     }
     return kvx::launch_status();  // an empty step: zero counts, no copies

@@ -23,15 +23,17 @@ int create(Policy **out, int64_t universe, int64_t capacity, int64_t resident0, 
            int64_t host_slots, int64_t host_cap, int64_t max_step);
 void destroy(Policy *p);
 
-// One step over frames[0..n) (device array), enqueued on `st`, its copy
-// lists in the buffers of `parity`:
+// One step (number step_no) over frames[0..n) (device array), enqueued on
+// `st`, its copy lists in the buffers of `parity`:
 // dev_slot[i] (device) receives the slot frame i occupies for this step's
 // reads, hit[i] / evicted[i] (device, optional) the decisions; the step's
 // copy lists are left on the device (lists()).  Decisions equal KVManager's
-// serial LRU replay.  A step with more loads than free slots, or an id out
-// of range, sets the policy's error word and changes nothing.
-int step(Policy *p, int parity, const int32_t *frames, int64_t n, int32_t *dev_slot, uint8_t *hit,
-         int32_t *evicted, cudaStream_t st);
+// serial LRU replay.  Free device slots form a FIFO; a load takes only a
+// slot freed by step min_freed or earlier.  A step with more loads than such
+// slots (or free host slots), or an id out of range, sets the policy's error
+// word and changes nothing.
+int step(Policy *p, int parity, int64_t step_no, int64_t min_freed, const int32_t *frames, int64_t n,
+         int32_t *dev_slot, uint8_t *hit, int32_t *evicted, cudaStream_t st);
 
 // Device arrays of the copies of the last step of that parity: loads
 // (h2d_dev[i] <- h2d_host[i]) and write-backs (d2h_dev[i] -> d2h_host[i]);

@@ -5,7 +5,10 @@
 
 #include <algorithm>
 #include <cmath>
+#include <new>
 #include <numeric>
+
+#include "kvx_scheduler.h"
 
 void Scheduler::observeLoadLatency(double ms) {
     std::lock_guard<std::mutex> lk(mu_);
@@ -25,4 +28,40 @@ int Scheduler::getPrefetchDepth(int /*current*/) {
     const int r = (int)std::round(raw);
     const int d = r < max_depth_ ? r : max_depth_;
     return d > 1 ? d : 1;
+}
+
+// C entry points (include/kvx_scheduler.h): the Scheduler over a cache whose
+// size and capacity the caller states with each question.
+
+struct kvx_scheduler {
+    struct Counts {
+        int64_t n = 0, cap = 0;
+        size_t size() const { return (size_t)n; }
+        size_t capacity() const { return (size_t)cap; }
+    } cache;
+    Scheduler sched;
+    explicit kvx_scheduler(int max_depth) : sched(cache, max_depth) {}
+};
+
+extern "C" KVX_API int kvx_scheduler_create(int32_t max_depth, kvx_scheduler **out) {
+    if (!out || max_depth < 1) return KVX_EINVAL;
+    *out = new (std::nothrow) kvx_scheduler(max_depth);
+    return *out ? KVX_OK : KVX_ENOSPC;
+}
+
+extern "C" KVX_API void kvx_scheduler_destroy(kvx_scheduler *s) { delete s; }
+
+extern "C" KVX_API int kvx_scheduler_observe(kvx_scheduler *s, double ms) {
+    if (!s || !(ms >= 0.0)) return KVX_EINVAL;
+    s->sched.observeLoadLatency(ms);
+    return KVX_OK;
+}
+
+extern "C" KVX_API int kvx_scheduler_depth(kvx_scheduler *s, int32_t current, int64_t size, int64_t capacity,
+                                           int32_t *depth) {
+    if (!s || !depth || size < 0 || capacity < 0) return KVX_EINVAL;
+    s->cache.n = size;
+    s->cache.cap = capacity;
+    *depth = s->sched.getPrefetchDepth(current);
+    return KVX_OK;
 }

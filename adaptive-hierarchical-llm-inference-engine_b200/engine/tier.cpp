@@ -25,10 +25,16 @@
 //   D2H_s waits H2D_{s-1}: it may write host slots H2D_{s-1} read;
 //   H2D_s waits D2H_{s-1}: it may write device slots D2H_{s-1} read, and
 //         it may read host slots D2H_{s-1} wrote;
-//   H2D_s waits the reads marked for step s-2: a device slot it writes was
-//         last read at step s-2 or earlier (a victim of step s-1 cannot be
-//         a frame step s-1 read, since a step is shorter than the capacity),
-//         and reads are marked in step order.
+//   H2D_s waits the reads marked for step s-L-2 (L = lookahead, the steps
+//         that may be planned ahead of the reads): a device slot it writes
+//         was freed by a victim of step s-L-1 or earlier (free device slots
+//         are a FIFO, and a slot freed at step j is taken no earlier than
+//         step j+L+1), and that victim was last read before the step that
+//         evicted it (a step is shorter than the capacity), so at step s-L-2
+//         or earlier; reads are marked in step order.
+// Completion and read events are rings of L+2 steps; planning step s needs
+// the reads of step s-L-2 marked (L = 0: the previous step's plan is all
+// that is needed, as a step's reads are marked before the next plan).
 // Pinned list staging is double-buffered by step parity; before reusing a
 // parity the host waits for the copies of step s-2.
 //
@@ -40,6 +46,14 @@
 // two steps that read the slot, if any) and then loaded like a RAM frame.
 // The step's file writes and then reads run on 8 host threads before its
 // copies are issued.
+//
+// Device policy (device_policy = 1): the same decisions, with the recency
+// order, the free slots and the copy lists held and updated by kernels
+// (csrc/kvx_tier_dev.cu) on the store's plan stream s_pol.  A step's copy
+// launches read their lists and counts from device memory (lists double-
+// buffered by parity, as the staging above); the copies wait for the plan's
+// event and are otherwise ordered exactly as above.  Nothing per step runs
+// on the host but the launches.
 #include "kvx_tier.h"
 
 #include <cuda_runtime.h>
@@ -127,12 +141,15 @@ struct kvx_tier {
     // device side
     uint8_t *dev_base = nullptr, *host_base = nullptr;
     cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
-    cudaEvent_t ev_h2d[2] = {}, ev_d2h[2] = {}, ev_read[2] = {};
-    bool ev_used[2] = {false, false};
+    int ring = 2;                                    // lookahead + 2
+    std::vector<cudaEvent_t> ev_h2d, ev_read;        // per step s at [s % ring]
+    std::vector<int64_t> h2d_step, read_step;        // the step each holds (-1: none)
+    cudaEvent_t ev_d2h[2] = {};                      // per step parity
+    int64_t marked = 0;                              // steps whose reads are marked
+    std::vector<int64_t> freed_at;                   // per device slot: step that freed it
     int32_t *stage[2] = {};   // pinned: [4][spare] (h2d dev, h2d host, d2h dev, d2h host)
     int32_t *lists[2] = {};   // device copies of the same
     int32_t *err = nullptr;   // device error flag
-    int last_parity = 0;
 
     // device policy (config device_policy): the bookkeeping above lives on
     // the device instead, in `pol`, and runs on s_pol
@@ -269,10 +286,12 @@ void release(kvx_tier *t) {
     if (!t->bookkeeping) {
         if (t->s_h2d) cudaStreamSynchronize(t->s_h2d);
         if (t->s_d2h) cudaStreamSynchronize(t->s_d2h);
+        for (cudaEvent_t e : t->ev_h2d)
+            if (e) cudaEventDestroy(e);
+        for (cudaEvent_t e : t->ev_read)
+            if (e) cudaEventDestroy(e);
         for (int p = 0; p < 2; ++p) {
-            if (t->ev_h2d[p]) cudaEventDestroy(t->ev_h2d[p]);
             if (t->ev_d2h[p]) cudaEventDestroy(t->ev_d2h[p]);
-            if (t->ev_read[p]) cudaEventDestroy(t->ev_read[p]);
             if (t->stage[p]) cudaFreeHost(t->stage[p]);
             if (t->lists[p]) cudaFree(t->lists[p]);
         }
@@ -302,11 +321,12 @@ int setup_device(kvx_tier *t) {
         cudaStreamCreateWithFlags(&t->s_d2h, cudaStreamNonBlocking) != cudaSuccess)
         return KVX_ECUDA;
     const size_t lb = 4 * (size_t)(t->cfg.spare ? t->cfg.spare : 1) * sizeof(int32_t);
-    for (int p = 0; p < 2; ++p) {
-        if (cudaEventCreateWithFlags(&t->ev_h2d[p], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&t->ev_d2h[p], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&t->ev_read[p], cudaEventDisableTiming) != cudaSuccess)
+    for (int r = 0; r < t->ring; ++r)
+        if (cudaEventCreateWithFlags(&t->ev_h2d[r], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&t->ev_read[r], cudaEventDisableTiming) != cudaSuccess)
             return KVX_ECUDA;
+    for (int p = 0; p < 2; ++p) {
+        if (cudaEventCreateWithFlags(&t->ev_d2h[p], cudaEventDisableTiming) != cudaSuccess) return KVX_ECUDA;
         if (cudaHostAlloc(reinterpret_cast<void **>(&t->stage[p]), lb, cudaHostAllocPortable) != cudaSuccess ||
             cudaMalloc(&t->lists[p], lb) != cudaSuccess)
             return KVX_ENOSPC;
@@ -315,12 +335,42 @@ int setup_device(kvx_tier *t) {
     return cuda_status(cudaMemset(t->err, 0, sizeof(int32_t)));
 }
 
-// Enqueue the copies of the step just planned.
-int issue(kvx_tier *t, int parity) {
+// Event helpers, by step number: completion of step s's loads, and the
+// reads marked for step j.
+bool loads_issued(const kvx_tier *t, int64_t s) { return s >= 0 && t->h2d_step[s % t->ring] == s; }
+
+int wait_loads(kvx_tier *t, cudaStream_t st, int64_t s) {
+    if (!loads_issued(t, s)) return KVX_OK;
+    return cuda_status(cudaStreamWaitEvent(st, t->ev_h2d[s % t->ring], 0));
+}
+
+// The newest mark of j's ring slot is j's own or an older step's (a newer
+// one would be at least `ring` steps later, which the plan contract rules
+// out), so waiting for it covers every read marked up to j in that slot.
+int wait_reads(kvx_tier *t, cudaStream_t st, int64_t j) {
+    if (j < 0 || t->read_step[j % t->ring] < 0) return KVX_OK;
+    return cuda_status(cudaStreamWaitEvent(st, t->ev_read[j % t->ring], 0));
+}
+
+int record_loads(kvx_tier *t, int64_t s) {
+    if (cudaEventRecord(t->ev_h2d[s % t->ring], t->s_h2d) != cudaSuccess) return KVX_ECUDA;
+    t->h2d_step[s % t->ring] = s;
+    return KVX_OK;
+}
+
+// Planning step s needs the reads of step s-L-2 marked (lookahead L > 0).
+int plan_allowed(const kvx_tier *t) {
+    const int64_t L = t->cfg.lookahead;
+    return (L > 0 && t->marked < t->step - L - 1) ? KVX_EBUSY : KVX_OK;
+}
+
+// Enqueue the copies of step s, just planned.
+int issue(kvx_tier *t, int64_t s) {
+    const int parity = (int)(s & 1);
     const int64_t sp = t->cfg.spare;
     int32_t *st = t->stage[parity], *dl = t->lists[parity];
-    if (t->ev_used[parity]) {  // the copies of step s-2 read this staging
-        if (cudaEventSynchronize(t->ev_h2d[parity]) != cudaSuccess ||
+    if (loads_issued(t, s - 2)) {  // the copies of step s-2 read this staging
+        if (cudaEventSynchronize(t->ev_h2d[(s - 2) % t->ring]) != cudaSuccess ||
             cudaEventSynchronize(t->ev_d2h[parity]) != cudaSuccess)
             return KVX_ECUDA;
     }
@@ -336,69 +386,68 @@ int issue(kvx_tier *t, int parity) {
         std::memcpy(st, t->h2d_dev.data(), nh * sizeof(int32_t));
         std::memcpy(st + sp, t->h2d_host.data(), nh * sizeof(int32_t));
     }
-    const int prev = parity ^ 1;
     const int load_ctas = t->cfg.load_ctas > 0 ? t->cfg.load_ctas : 16;
     const int store_ctas = t->cfg.store_ctas > 0 ? t->cfg.store_ctas : 4;
     const int32_t dcap = (int32_t)t->dev_slots, hcap = (int32_t)t->host_slots;
     // write-backs
-    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_d2h, t->ev_h2d[prev], 0) != cudaSuccess) return KVX_ECUDA;
+    int rc = wait_loads(t, t->s_d2h, s - 1);
+    if (rc != KVX_OK) return rc;
     if (nd) {
         if (cudaMemcpyAsync(dl + 2 * sp, st + 2 * sp, nd * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_d2h) !=
                 cudaSuccess ||
             cudaMemcpyAsync(dl + 3 * sp, st + 3 * sp, nd * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_d2h) !=
                 cudaSuccess)
             return KVX_ECUDA;
-        const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl + 2 * sp, dl + 3 * sp, nd,
-                                          t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
+        rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl + 2 * sp, dl + 3 * sp, nd,
+                                t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
         if (rc != KVX_OK) return rc;
     }
     if (cudaEventRecord(t->ev_d2h[parity], t->s_d2h) != cudaSuccess) return KVX_ECUDA;
-    // loads
-    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[prev], 0) != cudaSuccess) return KVX_ECUDA;
-    if (cudaStreamWaitEvent(t->s_h2d, t->ev_read[parity], 0) != cudaSuccess) return KVX_ECUDA;  // step s-2
+    // loads: after the previous write-backs and the reads of step s-L-2
+    if (loads_issued(t, s - 1) && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[parity ^ 1], 0) != cudaSuccess)
+        return KVX_ECUDA;
+    rc = wait_reads(t, t->s_h2d, s - t->cfg.lookahead - 2);
+    if (rc != KVX_OK) return rc;
     if (nh) {
         if (cudaMemcpyAsync(dl, st, nh * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_h2d) != cudaSuccess ||
             cudaMemcpyAsync(dl + sp, st + sp, nh * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_h2d) !=
                 cudaSuccess)
             return KVX_ECUDA;
-        const int rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl, dl + sp, nh,
-                                          t->cfg.frame_bytes, 1, load_ctas, t->err, t->s_h2d);
+        rc = kvx_migrate_frames(t->dev_base, dcap, t->host_base, hcap, dl, dl + sp, nh, t->cfg.frame_bytes, 1,
+                                load_ctas, t->err, t->s_h2d);
         if (rc != KVX_OK) return rc;
     }
-    if (cudaEventRecord(t->ev_h2d[parity], t->s_h2d) != cudaSuccess) return KVX_ECUDA;
-    t->ev_used[parity] = true;
-    t->last_parity = parity;
-    return KVX_OK;
+    return record_loads(t, s);
 }
 
-// The copies of a step planned on the device: the lists and their counts
+// The copies of step s planned on the device: the lists and their counts
 // are device arrays (kvx_tier_dev::lists), the launches read the counts
 // there; ordering as in issue().
-int issue_dev(kvx_tier *t, int parity) {
+int issue_dev(kvx_tier *t, int64_t s) {
+    const int parity = (int)(s & 1);
     const int32_t *hd, *hh, *dd, *dh, *cnt;
     kvx_tier_dev::lists(t->pol, parity, &hd, &hh, &dd, &dh, &cnt);
-    const int prev = parity ^ 1;
     const int load_ctas = t->cfg.load_ctas > 0 ? t->cfg.load_ctas : 16;
     const int store_ctas = t->cfg.store_ctas > 0 ? t->cfg.store_ctas : 4;
     const int32_t dcap = (int32_t)t->dev_slots, hcap = (int32_t)t->host_slots, mx = (int32_t)t->cfg.max_step;
     // write-backs: after the plan, and after the previous step's loads (host slots)
     if (cudaStreamWaitEvent(t->s_d2h, t->ev_pol, 0) != cudaSuccess) return KVX_ECUDA;
-    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_d2h, t->ev_h2d[prev], 0) != cudaSuccess) return KVX_ECUDA;
-    int rc = kvx_tier_dev::migrate_counted(t->dev_base, dcap, t->host_base, hcap, dd, dh, cnt + 1, mx,
-                                           t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
+    int rc = wait_loads(t, t->s_d2h, s - 1);
+    if (rc != KVX_OK) return rc;
+    rc = kvx_tier_dev::migrate_counted(t->dev_base, dcap, t->host_base, hcap, dd, dh, cnt + 1, mx,
+                                       t->cfg.frame_bytes, 0, store_ctas, t->err, t->s_d2h);
     if (rc != KVX_OK) return rc;
     if (cudaEventRecord(t->ev_d2h[parity], t->s_d2h) != cudaSuccess) return KVX_ECUDA;
-    // loads: after the plan, the previous write-backs and the reads of step s-2
+    // loads: after the plan, the previous write-backs and the reads of step s-L-2
     if (cudaStreamWaitEvent(t->s_h2d, t->ev_pol, 0) != cudaSuccess) return KVX_ECUDA;
-    if (t->ev_used[prev] && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[prev], 0) != cudaSuccess) return KVX_ECUDA;
-    if (cudaStreamWaitEvent(t->s_h2d, t->ev_read[parity], 0) != cudaSuccess) return KVX_ECUDA;
+    if (loads_issued(t, s - 1) && cudaStreamWaitEvent(t->s_h2d, t->ev_d2h[parity ^ 1], 0) != cudaSuccess)
+        return KVX_ECUDA;
+    rc = wait_reads(t, t->s_h2d, s - t->cfg.lookahead - 2);
+    if (rc != KVX_OK) return rc;
     rc = kvx_tier_dev::migrate_counted(t->dev_base, dcap, t->host_base, hcap, hd, hh, cnt, mx, t->cfg.frame_bytes, 1,
                                        load_ctas, t->err, t->s_h2d);
     if (rc != KVX_OK) return rc;
-    if (cudaEventRecord(t->ev_h2d[parity], t->s_h2d) != cudaSuccess) return KVX_ECUDA;
-    t->ev_used[parity] = true;
-    t->last_parity = parity;
-    return KVX_OK;
+    return record_loads(t, s);
 }
 
 // One step planned on the device (policy kernels on s_pol), then its
@@ -407,17 +456,20 @@ int issue_dev(kvx_tier *t, int parity) {
 // without, s_pol itself produced them.
 int step_device_core(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot, int32_t *evicted,
                      uint8_t *hit, bool wait_caller, cudaStream_t caller) {
-    const int parity = (int)(t->step & 1);
+    const int64_t s = t->step;
+    const int parity = (int)(s & 1);
     if (wait_caller && (cudaEventRecord(t->ev_caller, caller) != cudaSuccess ||
                         cudaStreamWaitEvent(t->s_pol, t->ev_caller, 0) != cudaSuccess))
         return KVX_ECUDA;
     // this parity's copy lists were read by the copies of step s-2
-    if (t->ev_used[parity] && (cudaStreamWaitEvent(t->s_pol, t->ev_h2d[parity], 0) != cudaSuccess ||
-                               cudaStreamWaitEvent(t->s_pol, t->ev_d2h[parity], 0) != cudaSuccess))
+    if (loads_issued(t, s - 2) &&
+        (cudaStreamWaitEvent(t->s_pol, t->ev_h2d[(s - 2) % t->ring], 0) != cudaSuccess ||
+         cudaStreamWaitEvent(t->s_pol, t->ev_d2h[parity], 0) != cudaSuccess))
         return KVX_ECUDA;
-    int rc = kvx_tier_dev::step(t->pol, parity, frames, n, dev_slot, hit, evicted, t->s_pol);
+    int rc = kvx_tier_dev::step(t->pol, parity, s, s - t->cfg.lookahead - 1, frames, n, dev_slot, hit, evicted,
+                                t->s_pol);
     if (rc == KVX_OK && cudaEventRecord(t->ev_pol, t->s_pol) != cudaSuccess) rc = KVX_ECUDA;
-    if (rc == KVX_OK) rc = issue_dev(t, parity);
+    if (rc == KVX_OK) rc = issue_dev(t, s);
     ++t->step;
     return rc;
 }
@@ -449,6 +501,15 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
     if (!t) return KVX_ENOSPC;
     t->cfg = *cfg;
     t->bookkeeping = cfg->device < 0;
+    if (cfg->lookahead < 0 || cfg->lookahead > 62) {
+        delete t;
+        return KVX_EINVAL;
+    }
+    t->ring = (int)cfg->lookahead + 2;
+    t->ev_h2d.assign(t->ring, nullptr);
+    t->ev_read.assign(t->ring, nullptr);
+    t->h2d_step.assign(t->ring, -1);
+    t->read_step.assign(t->ring, -1);
     const int64_t U = cfg->universe, C = cfg->capacity, S = cfg->spare;
     const int64_t resident0 = U < C ? U : C;
     t->disk = cfg->host_frames > 0 && cfg->host_frames < U - resident0;
@@ -487,6 +548,7 @@ extern "C" KVX_API int kvx_tier_create(const kvx_tier_config *cfg, kvx_tier **ou
         t->victim_idx.assign(U, -1);
         t->last_step.assign(U, -1);
         t->reclaimed.assign(t->dev_slots, -1);
+        t->freed_at.assign(t->dev_slots, INT64_MIN / 2);  // never used: free for any step
         t->slot_step.assign(t->host_slots, -1);
         t->slot_load_step.assign(t->host_slots, -1);
         if (t->disk) {
@@ -568,6 +630,8 @@ extern "C" KVX_API int kvx_tier_step_device(kvx_tier *t, const int32_t *frames, 
     if (!t->pol) return KVX_EUNSUPPORTED;
     if (n < 0 || n > t->cfg.max_step || (n > 0 && (!frames || !dev_slot))) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
+    const int rc = plan_allowed(t);
+    if (rc != KVX_OK) return rc;
     return step_device_core(t, frames, n, dev_slot, evicted, hit, true, static_cast<cudaStream_t>(stream));
 }
 
@@ -579,7 +643,9 @@ int step_host_via_device(kvx_tier *t, const int32_t *frames, int64_t n, int32_t 
     if (n > t->cfg.max_step) return KVX_EINVAL;
     kvx_tier_stats before{}, after{};
     int32_t err = 0;
-    int rc = kvx_tier_dev::totals(t->pol, &before, t->s_pol);
+    int rc = plan_allowed(t);
+    if (rc != KVX_OK) return rc;
+    rc = kvx_tier_dev::totals(t->pol, &before, t->s_pol);
     if (rc == KVX_OK) rc = kvx_tier_dev::error(t->pol, &err, true, t->s_pol);
     if (rc != KVX_OK) return rc;
     if (n > 0 && cudaMemcpyAsync(t->d_frames, frames, n * sizeof(int32_t), cudaMemcpyHostToDevice, t->s_pol) !=
@@ -620,6 +686,8 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     std::lock_guard<std::mutex> lk(t->mu);
     if (t->pol) return step_host_via_device(t, frames, n, dev_slot, evicted, hit, stats);
     if (n >= t->cfg.capacity && t->cfg.universe > t->cfg.capacity) return KVX_EINVAL;
+    const int rc0 = plan_allowed(t);
+    if (rc0 != KVX_OK) return rc0;
     const int64_t s = t->step;
     // pre-pass: ids valid, and the distinct frames to load fit the free slots
     int64_t loads = 0;
@@ -636,6 +704,10 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     if (loads > t->cfg.spare || (uint64_t)loads > t->dev_free.count ||
         (!t->disk && (uint64_t)loads > t->host_free.count))
         return KVX_ENOSPC;
+    if (loads > 0) {  // the loads take the FIFO's first slots: all freed by step s-L-1 or earlier
+        const auto &q = t->dev_free;
+        if (t->freed_at[q.ring[(q.head + loads - 1) % q.ring.size()]] > s - t->cfg.lookahead - 1) return KVX_ENOSPC;
+    }
     t->h2d_prev_synced = false;
 
     kvx_tier_stats st{};
@@ -706,7 +778,7 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
                             !(w == s - 1 && t->h2d_prev_synced)) {
                             // a load of one of the last two steps may still read this slot
                             // (older loads finished: issue() waited for step s-3's copies)
-                            if (cudaEventSynchronize(t->ev_h2d[w & 1]) != cudaSuccess) rc = KVX_ECUDA;
+                            if (cudaEventSynchronize(t->ev_h2d[w % t->ring]) != cudaSuccess) rc = KVX_ECUDA;
                             if (w == s - 1) t->h2d_prev_synced = true;
                         }
                         if (rc != KVX_OK) return rc;
@@ -736,10 +808,13 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     }
     st.frames_h2d = (int64_t)t->h2d_dev.size();
     int rc = t->disk ? run_disk_io(t) : KVX_OK;
-    if (rc == KVX_OK && !t->bookkeeping) rc = issue(t, (int)(s & 1));
-    // slots freed by this step serve the next one
+    if (rc == KVX_OK && !t->bookkeeping) rc = issue(t, s);
+    // slots freed by this step serve later ones (device slots: from step s+L+1)
     for (int32_t d : t->freed_dev)
-        if (t->reclaimed[d] != s) t->dev_free.push(d);
+        if (t->reclaimed[d] != s) {
+            t->dev_free.push(d);
+            t->freed_at[d] = s;
+        }
     for (int32_t h : t->freed_host) t->host_free.push(h);
     ++t->step;
     t->totals.accesses += st.accesses;
@@ -755,19 +830,40 @@ extern "C" KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t
     return rc;
 }
 
+extern "C" KVX_API int kvx_tier_plan_stream(kvx_tier *t, void **stream) {
+    if (!t || !stream) return KVX_EINVAL;
+    if (!t->pol) return KVX_EUNSUPPORTED;
+    *stream = t->s_pol;
+    return KVX_OK;
+}
+
+namespace {
+// The step whose reads come next: the last one planned (lookahead 0), or
+// the oldest one not yet marked.
+int64_t read_cursor(const kvx_tier *t) { return t->cfg.lookahead > 0 ? t->marked : t->step - 1; }
+}  // namespace
+
 extern "C" KVX_API int kvx_tier_wait_resident(kvx_tier *t, void *stream) {
     if (!t) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
-    if (t->bookkeeping || !t->ev_used[t->last_parity]) return KVX_OK;
-    return cuda_status(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), t->ev_h2d[t->last_parity], 0));
+    const int64_t j = read_cursor(t);
+    if (t->bookkeeping || j < 0 || j >= t->step) return KVX_OK;
+    return wait_loads(t, static_cast<cudaStream_t>(stream), j);
 }
 
 extern "C" KVX_API int kvx_tier_mark_read(kvx_tier *t, void *stream) {
     if (!t) return KVX_EINVAL;
     std::lock_guard<std::mutex> lk(t->mu);
-    if (t->bookkeeping || t->step == 0) return KVX_OK;
-    const int parity = (int)((t->step - 1) & 1);
-    return cuda_status(cudaEventRecord(t->ev_read[parity], static_cast<cudaStream_t>(stream)));
+    const int64_t j = read_cursor(t);
+    if (j < 0) return KVX_OK;
+    if (j >= t->step) return KVX_EINVAL;  // every planned step is marked already
+    if (!t->bookkeeping) {
+        if (cudaEventRecord(t->ev_read[j % t->ring], static_cast<cudaStream_t>(stream)) != cudaSuccess)
+            return KVX_ECUDA;
+        t->read_step[j % t->ring] = j;
+    }
+    t->marked = j + 1;
+    return KVX_OK;
 }
 
 extern "C" KVX_API int kvx_tier_sync(kvx_tier *t) {

@@ -27,7 +27,7 @@ class TierConfig(C.Structure):
     _fields_ = [("frame_bytes", C.c_size_t), ("universe", C.c_int64), ("capacity", C.c_int64),
                 ("spare", C.c_int64), ("device", C.c_int32), ("load_ctas", C.c_int32),
                 ("store_ctas", C.c_int32), ("host_frames", C.c_int64), ("spill_path", C.c_char_p),
-                ("device_policy", C.c_int32), ("max_step", C.c_int64)]
+                ("device_policy", C.c_int32), ("max_step", C.c_int64), ("lookahead", C.c_int32)]
 
 
 _STAT_FIELDS = ("accesses", "hits", "misses", "evictions", "reloads", "frames_h2d", "frames_d2h",
@@ -51,6 +51,7 @@ lib.kvx_tier_host_arena.argtypes = [_vp, C.POINTER(_vp), C.POINTER(_i64)]
 lib.kvx_tier_location.argtypes = [_vp, _i64, C.POINTER(C.c_int32), C.POINTER(_i64)]
 lib.kvx_tier_step.argtypes = [_vp, _vp, _i64, _vp, _vp, _vp, C.POINTER(TierStats)]
 lib.kvx_tier_step_device.argtypes = [_vp, _vp, _i64, _vp, _vp, _vp, _vp]
+lib.kvx_tier_plan_stream.argtypes = [_vp, C.POINTER(_vp)]
 lib.kvx_tier_wait_resident.argtypes = [_vp, _vp]
 lib.kvx_tier_mark_read.argtypes = [_vp, _vp]
 lib.kvx_tier_sync.argtypes = [_vp]
@@ -58,7 +59,7 @@ lib.kvx_tier_totals.argtypes = [_vp, C.POINTER(TierStats)]
 lib.kvx_tier_write_frame.argtypes = [_vp, _i64, _vp]
 lib.kvx_tier_read_frame.argtypes = [_vp, _i64, _vp]
 for _fn in ("kvx_tier_device_arena", "kvx_tier_host_arena", "kvx_tier_location", "kvx_tier_step",
-            "kvx_tier_step_device",
+            "kvx_tier_step_device", "kvx_tier_plan_stream",
             "kvx_tier_wait_resident", "kvx_tier_mark_read", "kvx_tier_sync", "kvx_tier_totals",
             "kvx_tier_write_frame", "kvx_tier_read_frame"):
     getattr(lib, _fn).restype = C.c_int
@@ -85,12 +86,14 @@ class _DeviceBytes:
 
 class Tier:
     def __init__(self, frame_bytes, universe, capacity, spare, device=0, load_ctas=0, store_ctas=0,
-                 host_frames=0, spill_path=None, device_policy=False, max_step=0):
+                 host_frames=0, spill_path=None, device_policy=False, max_step=0, lookahead=0):
         """device_policy: the LRU bookkeeping runs as kernels on the device
-        (step_device takes device tensors); max_step bounds a step's accesses."""
+        (step_device takes device tensors); max_step bounds a step's accesses.
+        lookahead: steps that may be planned ahead of the reads (wait_resident
+        and mark_read then address the oldest step not yet marked)."""
         self._path = None if spill_path is None else str(spill_path).encode()
         self.cfg = TierConfig(frame_bytes, universe, capacity, spare, device, load_ctas, store_ctas,
-                              host_frames, self._path, 1 if device_policy else 0, max_step)
+                              host_frames, self._path, 1 if device_policy else 0, max_step, lookahead)
         h = _vp()
         _check("kvx_tier_create", lib.kvx_tier_create(C.byref(self.cfg), C.byref(h)))
         self.h = h
@@ -175,6 +178,13 @@ class Tier:
         _check("kvx_tier_step_device",
                lib.kvx_tier_step_device(self.h, p(frames), frames.numel(), p(dev_slot), p(evicted), p(hit),
                                         _stream_ptr(stream)))
+
+    def plan_stream(self):
+        """Device-policy stores: the stream the plans run on (torch ExternalStream)."""
+        import torch
+        st = _vp()
+        _check("kvx_tier_plan_stream", lib.kvx_tier_plan_stream(self.h, C.byref(st)))
+        return torch.cuda.ExternalStream(st.value)
 
     def _sp(self, stream):
         return _vp(0) if self.cfg.device < 0 else _stream_ptr(stream)

@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--tier-device-policy", action="store_true",
                     help="config 4: the LRU bookkeeping as kernels on the device (kvx_tier_step_device): "
                          "the step's ids go up, the block tables come out of the policy, no host planning")
+    ap.add_argument("--tier-prefetch", action="store_true",
+                    help="config 4: plan and load per layer, the Scheduler's prefetch depth (kvx_scheduler_depth, "
+                         "fed each plan's load latency) deciding how many layers ahead of the decode")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline workload; 1, 3, 5: the other configurations of the path")
     ap.add_argument("--kernels", action="store_true",
@@ -74,6 +77,8 @@ def parse():
     ap.add_argument("--shapes", action="store_true",
                     help="decode across batch x context shapes (fp16, int8 and fp32 pools, GQA 3 and 8), "
                          "one JSON line per shape")
+    ap.add_argument("--shape-pools", default="fp16,int8,fp32",
+                    help="with --shapes: which pool kinds to run (comma-separated)")
     ap.add_argument("--shape-chunks", default="",
                     help="with --shapes: comma-separated chunk sizes (pages per CTA) to time beside "
                          "the library's own choice, forced through KVX_DECODE_CHUNK")
@@ -1089,10 +1094,94 @@ def select_timing(n):
     return out
 
 
+SCHED_MAX_DEPTH = 4  # the reference Scheduler's default max_depth
+
+
+def _config4_prefetch_loop(tier, kvx, pool, stream_ids, q, lens, out, ws, L, B, ACC, C, dpol):
+    """Config 4 planned and loaded per layer, as the reference's
+    InferenceController::schedulePrefetch (runtime/inference.cpp:61-84)
+    prefetches per layer: before the decode of layer unit g (step k, layer l)
+    the loop asks the Scheduler (scheduler/scheduler.cpp:15-37, through
+    kvx_scheduler_depth) for a depth d and plans units up to g + d, each
+    plan one kvx_tier step of that layer's B x ACC page accesses (the same
+    access order as a whole step, so KVManager's decisions are unchanged).
+    The latency of each unit's load (plan issued -> frames resident, CUDA
+    events) goes to observeLoadLatency; the cache pressure is the store's
+    (resident frames / capacity).  The store runs with lookahead
+    SCHED_MAX_DEPTH - 1, so any depth the Scheduler can answer is legal."""
+    import collections
+    import torch
+    from kvx.scheduler import Scheduler
+    steps = len(stream_ids)
+    G, n = steps * L, B * ACC
+    NB = SCHED_MAX_DEPTH + 3  # block-table / id buffers in flight
+    sched = Scheduler(SCHED_MAX_DEPTH)
+    btl = [torch.empty((B, ACC), dtype=torch.int32, device="cuda") for _ in range(NB)]
+    used = [torch.cuda.Event() for _ in range(NB)]
+    e_issue = [torch.cuda.Event(enable_timing=True) for _ in range(G)]
+    e_ready = [torch.cuda.Event(enable_timing=True) for _ in range(G)]
+    if dpol:
+        ids_pinned = torch.from_numpy(np.stack(stream_ids)).pin_memory()
+        ids_dev = [torch.empty(n, dtype=torch.int32, device="cuda") for _ in range(NB)]
+        planst = torch.cuda.Stream()
+    else:
+        bt_host = [torch.empty(n, dtype=torch.int32, pin_memory=True) for _ in range(NB)]
+        up = [torch.cuda.Event() for _ in range(NB)]
+    plan_s, planned, observed = 0.0, 0, []
+    depths = collections.Counter()
+
+    def plan(u):
+        nonlocal plan_s
+        i, (k, l) = u % NB, divmod(u, L)
+        h0 = time.perf_counter()
+        if dpol:
+            with torch.cuda.stream(planst):
+                if u >= NB:  # unit u-NB's decode read btl[i] (after its plan read ids_dev[i])
+                    planst.wait_event(used[i])
+                ids_dev[i].copy_(ids_pinned[k, l * n:(l + 1) * n], non_blocking=True)
+                e_issue[u].record(planst)
+            tier.step_device(ids_dev[i], btl[i].view(-1), stream=planst)
+        else:
+            if u >= NB:
+                up[i].synchronize()  # the upload of unit u-NB read bt_host[i]
+            e_issue[u].record()
+            tier.step(stream_ids[k][l * n:(l + 1) * n], dev_slot=bt_host[i].numpy(), evicted=False, hit=False)
+            btl[i].view(-1).copy_(bt_host[i], non_blocking=True)  # after unit u-NB's decode (same stream)
+            up[i].record()
+        plan_s += time.perf_counter() - h0
+
+    for u in range(G):
+        d = sched.depth(u, C, C)  # the store is full: resident == capacity
+        depths[d] += 1
+        while planned < G and planned <= u + d:
+            plan(planned)
+            planned += 1
+        tier.wait_resident()
+        e_ready[u].record()
+        kvx.decode(pool, btl[u % NB], lens, q[u % L], out=out[u % L], workspace=ws)
+        used[u % NB].record()
+        tier.mark_read()
+        if u >= 2 and e_ready[u - 2].query():
+            ms = e_issue[u - 2].elapsed_time(e_ready[u - 2])
+            sched.observe(ms)
+            observed.append(ms)
+    sched.close()
+    return {"driver": "Scheduler::getPrefetchDepth per layer (kvx_scheduler_depth), max_depth "
+                      f"{SCHED_MAX_DEPTH}, store lookahead {SCHED_MAX_DEPTH - 1}",
+            "units_per_step": L, "accesses_per_unit": n,
+            "depths": {str(k): v for k, v in sorted(depths.items())},
+            "observed_load_ms": {"mean": round(float(np.mean(observed)), 3) if observed else None,
+                                 "count": len(observed)},
+            "plan_s": plan_s,
+            # the last NB units' block tables (resident frames), for timing the decode alone
+            "tables": [btl[(G - NB + (l % NB)) % NB] for l in range(L)]}
+
+
 def device_plan_timing(U, C, S, n, step_ids, warm, steps=8):
-    """Latency of one device-planned step (kvx_tier_step_device) at config
-    4's geometry, copies made negligible by 16-byte frames: CUDA events on
-    the caller's stream around the plan and kvx_tier_wait_resident."""
+    """Device time of one step's plan (the policy kernels of
+    kvx_tier_step_device) at config 4's geometry: CUDA events on the store's
+    plan stream around the plan, every earlier copy finished (16-byte frames
+    keep the store small)."""
     import torch
     from kvx.tier import Tier
     t = Tier(16, U, C, S, device=0, device_policy=True, max_step=n)
@@ -1103,21 +1192,18 @@ def device_plan_timing(U, C, S, n, step_ids, warm, steps=8):
     t.sync()
     ids_d = [torch.from_numpy(step_ids(warm + k)).cuda() for k in range(steps)]
     slots = torch.empty(n, dtype=torch.int32, device="cuda")
-    st = torch.cuda.Stream()
+    plan = t.plan_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     for k in range(steps):
-        ev[k][0].record(st)
-        t.step_device(ids_d[k], slots, stream=st)
-        t.wait_resident(st)
-        ev[k][1].record(st)
-        t.mark_read(st)
-        st.synchronize()
-    t.sync()
+        ev[k][0].record(plan)
+        t.step_device(ids_d[k], slots, stream=plan)
+        ev[k][1].record(plan)
+        t.sync()
     us = sorted(a.elapsed_time(b) * 1e3 for a, b in ev)
     t.close()
     return {"median_us": round(us[len(us) // 2], 1), "min_us": round(us[0], 1), "steps": steps,
-            "how": "16-byte frames, same ids and capacity; events around kvx_tier_step_device + wait_resident"}
+            "accesses": n, "how": "CUDA events on the plan stream around kvx_tier_step_device"}
 
 
 def run_config4(args):
@@ -1158,10 +1244,11 @@ def run_config4(args):
 
     t0 = time.perf_counter()
     dpol = bool(args.tier_device_policy) and not H
+    look = SCHED_MAX_DEPTH - 1 if args.tier_prefetch else 0
     tier = Tier(FB, U, C, S, device=0, load_ctas=int(os.environ.get("KVX_TIER_LOAD_CTAS", "0")),
                 store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")), host_frames=H,
                 spill_path=None if not H else os.path.join(spill_dir, "frames.bin"),
-                device_policy=dpol, max_step=rows * ACC if dpol else 0)
+                device_policy=dpol, max_step=rows * ACC if dpol else 0, lookahead=look)
     alloc_s = time.perf_counter() - t0
     dev = tier.device_tensor()
     host = tier.host_array()
@@ -1193,6 +1280,8 @@ def run_config4(args):
         ids = step_ids(k)
         for o in range(0, ids.size, 16384):
             tier.step(ids[o:o + 16384], evicted=False, hit=False)
+            if look:
+                tier.mark_read()  # nothing reads warm-up frames
     tier.sync()
     q = torch.randn((L, B, HQ, DIM), generator=g, device="cuda", dtype=torch.float16)
     lens = torch.full((B,), ACC * PT, dtype=torch.int32, device="cuda")
@@ -1215,7 +1304,12 @@ def run_config4(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     plan_s = 0.0
     e0.record()
-    for k in range(steps):
+    pre = None
+    if args.tier_prefetch:
+        pre = _config4_prefetch_loop(tier, kvx, pool, stream_ids, q, lens, out, ws, L, B, ACC, C, dpol)
+        plan_s = pre.pop("plan_s")
+        last_tables = pre.pop("tables")
+    for k in range(steps if pre is None else 0):
         p = k & 1
         if dpol:
             with torch.cuda.stream(plan):
@@ -1248,7 +1342,9 @@ def run_config4(args):
     after = tier.totals()
     mv = {k2: after[k2] - before[k2] for k2 in after}
     # decode alone, frames resident (last step's tables)
-    dec_ms = _events_time(lambda: [kvx.decode(pool, bt_dev[(steps - 1) & 1][l], lens, q[l], out=out[l],
+    if pre is None:
+        last_tables = [bt_dev[(steps - 1) & 1][l] for l in range(L)]
+    dec_ms = _events_time(lambda: [kvx.decode(pool, last_tables[l], lens, q[l], out=out[l],
                                               workspace=ws) for l in range(L)], 3)
     dec_bytes = rows * ACC * FB
     sel = select_timing(C)
@@ -1276,6 +1372,7 @@ def run_config4(args):
                    "GBps_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9, 1),
                    "frac_of_hbm_peak_alone": round(dec_bytes / (dec_ms / 1e3) / 1e9 / peak, 3)},
         "policy": "device (kvx_tier_step_device)" if dpol else "host (kvx_tier_step)",
+        "prefetch": pre,
         "host_plan_ms_per_step": round(plan_s / steps * 1e3, 3),
         "device_plan_latency": dplan,
         "victim_select": sel,
@@ -1342,7 +1439,10 @@ def run_shapes(args):
             res["default" if c is None else str(c)] = round(nbytes / (ms / 1e3) / 1e9, 1)
         return res
 
+    kinds = {k.strip() for k in args.shape_pools.split(",")}
     for pool_kind, shapes in (("fp16", SHAPES), ("int8", SHAPES_I8), ("fp32", SHAPES_F32)):
+        if pool_kind not in kinds:
+            continue
         for B, T in shapes:
             npg = T // PT
             lens = torch.full((B,), T, dtype=torch.int32, device="cuda")

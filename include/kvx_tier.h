@@ -83,6 +83,14 @@ typedef struct kvx_tier_config {
                                arrays (kvx_tier_step_device) and no host work is left per
                                step.  RAM tier only (host_frames 0), device >= 0 */
     int64_t max_step;       /* device_policy: accesses per step at most (< capacity) */
+    int32_t lookahead;      /* L, 0..62: steps that may be planned ahead of the reads.  Step s
+                               may be planned once the reads of steps up to s-L-2 are marked
+                               (KVX_EBUSY otherwise); kvx_tier_wait_resident and
+                               kvx_tier_mark_read then address the oldest step not yet
+                               marked.  A device slot a victim frees is taken again no earlier
+                               than L+1 steps later, so `spare` must cover about L+1 steps'
+                               loads (KVX_ENOSPC otherwise).  0: plan, read, mark, one step
+                               at a time (wait / mark address the last step planned) */
 } kvx_tier_config;
 
 typedef struct kvx_tier_stats {
@@ -140,10 +148,17 @@ KVX_API int kvx_tier_step(kvx_tier *t, const int32_t *frames, int64_t n, int32_t
  * kvx_tier_step on such a store copies through the device and waits. */
 KVX_API int kvx_tier_step_device(kvx_tier *t, const int32_t *frames, int64_t n, int32_t *dev_slot,
                                  int32_t *evicted, uint8_t *hit, void *stream);
-/* Make `stream` wait until every frame of the last step is resident. */
+/* Device-policy stores: the stream the plans (the policy's kernels) run on,
+ * for ordering or timing other work against them; KVX_EUNSUPPORTED on a
+ * host-policy store. */
+KVX_API int kvx_tier_plan_stream(kvx_tier *t, void **stream);
+/* Make `stream` wait until every frame of the reading step is resident:
+ * the last step planned (lookahead 0) or the oldest step not yet marked. */
 KVX_API int kvx_tier_wait_resident(kvx_tier *t, void *stream);
-/* The reads of the last step's frames have been enqueued on `stream`; a
- * later step that evicts one of them first waits for that work. */
+/* The reads of the reading step's frames have been enqueued on `stream`; a
+ * later step that evicts one of them first waits for that work.  With a
+ * lookahead, the next step becomes the reading step (every step is marked
+ * once, in order; KVX_EINVAL when all planned steps are marked). */
 KVX_API int kvx_tier_mark_read(kvx_tier *t, void *stream);
 /* Block until all enqueued copies finished; KVX_EINVAL if a copy met a bad
  * slot (never expected), KVX_ECUDA on a CUDA error. */

@@ -39,6 +39,19 @@ def test_scheduler_depth_matches_reference(built):
     assert [int(x) for x in out.split()] == want
 
 
+def test_scheduler_c_entry_points_match_reference():
+    """kvx_scheduler_* (include/kvx_scheduler.h) over the same golden grid:
+    a fresh Scheduler per case, fed the case's latencies, asked once."""
+    from kvx.scheduler import Scheduler
+    g = golden("prefetch_depth.npz")
+    for li, size, cap, md, depth in g["grid"]:
+        s = Scheduler(int(md))
+        for x in g[f"lat{li}"]:
+            s.observe(float(x))
+        assert s.depth(0, int(size), int(cap)) == int(depth), (li, size, cap, md)
+        s.close()
+
+
 def test_prefetcher_drop_in(built):
     """Prefetcher (prefetch/prefetcher.h:14-38): requests are served in FIFO
     order by the worker; a mover result of 0 is a hit (no load, nothing

@@ -67,6 +67,7 @@ def test_device_policy_equals_host_policy_and_replay(kvx, oracle):
         s_dev, e_dev, h_dev, st_dev = dev.step(ids)
         assert np.array_equal(e_dev, e_ref), k
         assert np.array_equal(h_dev, h_ref), k
+        assert np.array_equal(s_dev, s_ref), k  # same FIFO of free slots: same placement
         assert st_dev == st_ref, (k, st_dev, st_ref)
         if ids.size:  # a frame read twice in a step sits in one slot
             assert (s_dev >= 0).all() and (s_dev < C + S).all()
@@ -222,3 +223,55 @@ def test_device_policy_rejects_bad_steps_and_changes_nothing(kvx, oracle):
         assert np.array_equal(t.read_frame(f), raw[f]), f
     t.close()
     t2.close()
+
+
+@pytest.mark.parametrize("device_policy", [False, True])
+def test_plans_ahead_of_the_decode(kvx, oracle, device_policy):
+    """lookahead 3: every step is planned (and its copies queued) four steps
+    before the decode that reads it; wait_resident / mark_read address the
+    oldest unmarked step.  Decode matches the oracle, decisions the replay,
+    and both policies place every frame in the same slot."""
+    from kvx.tier import Tier
+    U, C, S, steps, per, L = 6000, 1500, 2400, 12, 500, 3
+    data = kvgen.normal(111, (U, 2, 1, 16, 128)).astype(np.float16)
+    raw = data.reshape(U, -1).view(np.uint8)
+    kw = {"device_policy": True, "max_step": per} if device_policy else {}
+    t = Tier(FB_PAGE, U, C, S, device=0, lookahead=L, **kw)
+    for f in range(U):
+        t.write_frame(f, raw[f])
+    ranks = kvgen.zipf_pages(112, steps * per, U, 1.1)
+    stream = kvgen.permutation(113, U)[ranks].astype(np.int32).reshape(steps, per)
+    q = kvgen.normal(114, (steps, 2, 3, 128))
+    lens = torch.full((2,), 250 * 16, dtype=torch.int32, device="cuda")
+    slots = [torch.empty(per, dtype=torch.int32, device="cuda") for _ in range(steps)]
+    ids_d = [torch.from_numpy(stream[s]).cuda() for s in range(steps)]  # alive until the plans read them
+    host_slots = [None] * steps
+    outs = [None] * steps
+    for s in range(steps + L + 1):
+        if s < steps:
+            if device_policy:
+                t.step_device(ids_d[s], slots[s])
+            else:
+                host_slots[s] = t.step(stream[s])[0].copy()
+                slots[s].copy_(torch.from_numpy(host_slots[s]))
+        j = s - L - 1
+        if j >= 0:
+            t.wait_resident()
+            outs[j] = kvx.decode(t.paged(1), slots[j].view(2, 250), lens, torch.from_numpy(q[j]).cuda())
+            t.mark_read()
+    t.sync()
+    torch.cuda.synchronize()
+    for j in range(steps):
+        ref = oracle.paged_decode(data, stream[j].reshape(2, 250), np.full(2, 4000, np.int32), q[j])
+        got = outs[j].cpu().numpy()
+        assert (np.abs(got - ref) - (ATOL + RTOL * np.abs(ref))).max() <= 0, j
+    for f in range(0, U, 5):
+        assert np.array_equal(t.read_frame(f), raw[f]), f
+    # the placement equals a bookkeeping-only host store's with the same lookahead
+    b = Tier(FB_PAGE, U, C, S, device=-1, lookahead=L)
+    for s in range(steps):
+        if s - L - 1 >= 0:
+            b.mark_read()
+        want = b.step(stream[s])[0]
+        assert np.array_equal(slots[s].cpu().numpy(), want), s
+    t.close()

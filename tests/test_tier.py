@@ -147,3 +147,60 @@ def test_device_policy_config_is_checked():
     assert e.value.status == -1
     t = Tier(64, 100, 20, 3, device=-1)
     assert lib.kvx_tier_step_device(t.h, None, 0, None, None, None, None) == -4
+
+
+def test_lookahead_contract_and_slot_quarantine(oracle):
+    """With lookahead L a step may be planned while the reads of the last
+    L+1 steps are unmarked (one more: KVX_EBUSY); a device slot freed by a
+    victim is not loaded again within L+1 steps (too few older free slots:
+    KVX_ENOSPC, nothing changed); decisions stay KVManager's."""
+    t = Tier(64, 100, 20, 3, device=-1, lookahead=1)
+    t.step(np.array([30, 31, 32], np.int32))      # step 0: 3 loads into the 3 spare slots
+    with pytest.raises(KvxError) as e:             # step 1: the only free slots were freed at step 0
+        t.step(np.array([33], np.int32))
+    assert e.value.status == -6
+    t.step(np.array([30, 31], np.int32))           # step 1: hits need no slot
+    t.step(np.array([30], np.int32))               # step 2: three steps unmarked at L = 1
+    with pytest.raises(KvxError) as e:             # step 3 needs step 0's reads marked
+        t.step(np.array([33], np.int32))
+    assert e.value.status == -2
+    t.mark_read()                                  # step 0
+    _, ev, _, _ = t.step(np.array([33], np.int32))  # step 3: slots freed at step 0 are old enough
+    assert ev.tolist() == [3]
+    for _ in range(3):
+        t.mark_read()
+    with pytest.raises(KvxError) as e:             # every planned step is marked
+        t.mark_read()
+    assert e.value.status == -1
+    ids = np.concatenate([np.arange(20, dtype=np.int32), [30, 31, 32, 30, 31, 30, 33]]).astype(np.int32)
+    want_ev, _ = oracle.lru_replay(ids, np.zeros(ids.size, np.uint8), 20)
+    assert want_ev[20:].tolist() == [0, 1, 2, -1, -1, -1, 3]
+
+
+@pytest.mark.parametrize("lookahead", [0, 2, 5])
+def test_lookahead_never_loads_into_a_slot_read_since(oracle, lookahead):
+    """Zipf steps planned `lookahead` steps ahead of their (marked) reads: a
+    slot loaded at step s was read by none of steps s-L-1 .. s-1, and the
+    decisions equal the replay."""
+    U, C, S, per, steps = 3000, 600, 400, 60, 80
+    t = Tier(64, U, C, S, device=-1, lookahead=lookahead)
+    ranks = kvgen.zipf_pages(61, steps * per, U, 0.9)
+    stream = kvgen.permutation(62, U)[ranks].astype(np.int32).reshape(steps, per)
+    slots, evs, hits = [], [], []
+    for s in range(steps):
+        if lookahead and s - lookahead - 1 > 0:
+            t.mark_read()  # the reads of step s-L-2
+        sl, ev, ht, _ = t.step(stream[s])
+        slots.append(sl.copy())
+        evs.append(ev)
+        hits.append(ht)
+        # slots written by this step's loads: misses of frames not evicted
+        # earlier in the step (a second miss keeps its slot, no load)
+        victims = set(ev[ev >= 0].tolist())
+        loaded = {int(x) for x, h, f in zip(sl, ht, stream[s]) if h == 0 and int(f) not in victims}
+        for j in range(max(0, s - lookahead - 1), s):
+            assert not loaded & set(slots[j].tolist()), (s, j)
+    ids = np.concatenate([np.arange(C, dtype=np.int32), stream.ravel()])
+    want_ev, want_hit = oracle.lru_replay(ids, np.zeros(ids.size, np.uint8), C)
+    assert np.array_equal(np.concatenate(evs), want_ev[C:])
+    assert np.array_equal(np.concatenate(hits), want_hit[C:])
