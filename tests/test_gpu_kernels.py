@@ -513,6 +513,25 @@ def test_int8_decode_tensor_core_path_matches_oracle(kvx, oracle, monkeypatch, h
     assert_close(simt, ref)
 
 
+@pytest.mark.parametrize("hq", [24, 64])
+def test_int8_decode_long_contexts(kvx, oracle, hq):
+    """int8 pools with long contexts: 256-page CTAs (one split for 4,096
+    tokens, five folded for 20,000) match the oracle's dequantise-then-attend."""
+    hkv = 8
+    lens = np.array([4096, 20000, 777, 16, 4095], np.int32)
+    bt, num_pages = kvgen.paged_layout(lens, 16, 1, seed=191)
+    pool = kvgen.normal(192, (num_pages, 2, hkv, 16, 128))
+    pool[kvgen.uniform(193, pool.size).reshape(pool.shape) < 0.01] *= 20
+    pool = pool.astype(np.float16)
+    codes, stats = kvx.compress_int8(dev(pool))
+    cpool = codes.view(num_pages, 2, hkv, 16, 128)
+    q = kvgen.normal(194, (lens.size, hq, 128))
+    got = kvx.decode(cpool, dev(bt), dev(lens), dev(q), stats=stats).float().cpu().numpy()
+    ref = oracle.paged_decode(codes.cpu().numpy().reshape(cpool.shape), bt, lens, q,
+                              stats=stats.cpu().numpy().reshape(num_pages, 2, hkv, 4))
+    assert_close(got, ref)
+
+
 @pytest.mark.parametrize("qscale", [20.0, 200.0])
 def test_int8_decode_query_outlier_channels(kvx, oracle, qscale):
     """Queries with outlier channels (two dims x20 / x200) over int8 pages
