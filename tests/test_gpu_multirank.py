@@ -12,7 +12,9 @@ cache/kv_cache.cpp and runtime/cpu_ops.cpp), within the attention tolerance:
   NCCL communicator (adaptive_engine_set_comm), rank 0 reading the gathered
   rows back.
 
-A third case makes rank 1's step fail on the host (the layer it must bring
+A third case runs the engine at 28 layers (grouped all-gathers, contexts
+split over several CTAs) with the read-back first on rank 0, then shared
+between the ranks.  A fourth makes rank 1's step fail on the host (the layer it must bring
 to the device cannot evict a victim: both device slabs hold pinned layers):
 rank 1 returns KVX_EBUSY and rank 0, whose own work succeeded, returns
 KVX_EPEER; neither waits in NCCL, because the failing rank still takes every
@@ -61,6 +63,11 @@ def _worker(rank, world, port, tmpdir, result_q, mode):
 
         if mode == "fail":
             report.update(_failing_step(rank, world, tmpdir, dist, E))
+            dist.barrier()
+            result_q.put((rank, report, None))
+            return
+        if mode == "engine28":
+            report.update(_engine_28_layers(rank, world, tmpdir, dist, E, o, (k0, k1), (q0, q1)))
             dist.barrier()
             result_q.put((rank, report, None))
             return
@@ -122,6 +129,65 @@ def _worker(rank, world, port, tmpdir, result_q, mode):
             dist.destroy_process_group()
         except Exception:
             pass
+
+
+def _engine_28_layers(rank, world, tmpdir, dist, E, o, kr, qr):
+    """adaptive_engine_decode_step at 28 layers on two GPUs: layer groups of
+    2, 7, 7, 7, 3 and 2, one all-gather per group, contexts up to 5,000
+    tokens (several splits).  Step 0: rank 0 reads every layer back; step 1:
+    the read-back shared (rank r copies layers l % 2 == r).  Each rank checks
+    what it read against the oracle's unsharded append + decode."""
+    import kvgen
+    from kvx.shard import gathered_to_heads
+    (k0, k1), (q0, q1) = kr, qr
+    L, B = 28, 3
+    lens = np.array([5000, 2100, 777], np.int32)
+    pages = int(((lens + 2 + PT - 1) // PT).sum())
+    api = E.api()
+    api.stop()
+    E.configure(layers=L, pages_per_layer=pages, max_batch=B, gpu_layer_slots=L, kv_heads=HKV // world,
+                q_heads=HQ // world, device=rank, offload_dir=os.path.join(tmpdir, f"e28_{rank}"))
+    api.start()
+    try:
+        uid = [E.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        E.set_comm(rank, world, uid[0])
+        E.set_sequences(lens, reserve_tokens=2, seed=7)
+        bt = E.block_table(B)
+        keep = {}
+        for l in range(L):
+            pool = kvgen.normal(300 + l, (pages, 2, HKV, PT, DIM)).astype(np.float16)
+            E.load_layer(l, np.ascontiguousarray(pool[:, :, k0:k1]))
+            if rank == 0 or l % world == rank:
+                keep[l] = pool
+        q = kvgen.normal(330, (2, L, B, HQ, DIM)).astype(np.float16)
+        k = kvgen.normal(331, (2, L, B, HKV, DIM)).astype(np.float16)
+        v = kvgen.normal(332, (2, L, B, HKV, DIM)).astype(np.float16)
+        shape = (L, world, B, HQ // world, DIM)
+        out = [np.zeros(shape, np.float16) if rank == 0 else None, np.zeros(shape, np.float16)]
+        for step in range(2):
+            if step == 1:
+                E.set_readback_share(True)
+            E.decode_step(np.ascontiguousarray(q[step][:, :, q0:q1]), np.ascontiguousarray(k[step][:, :, k0:k1]),
+                          np.ascontiguousarray(v[step][:, :, k0:k1]), out[step])
+        E.set_readback_share(False)
+        worst, checked = -np.inf, 0
+        for l, pool in sorted(keep.items()):
+            for step in range(2):
+                pos = (lens + step).astype(np.int32)
+                o.append(pool, bt, pos, k[step][l], v[step][l], PT)
+                mine = (rank == 0) if step == 0 else (l % world == rank)
+                if not mine:
+                    continue
+                ref = o.paged_decode(pool, bt, pos + 1, q[step][l].astype(np.float32))
+                got = gathered_to_heads(out[step][l]).astype(np.float32)
+                worst = max(worst, float((np.abs(got - ref) - (ATOL + RTOL * np.abs(ref))).max()))
+                checked += 1
+        if rank != 0:  # layers rank 1 does not read stay untouched
+            assert not out[1][[l for l in range(L) if l % world != rank]].any()
+        return {"engine28_excess": worst, "engine28_checked": checked}
+    finally:
+        api.stop()
 
 
 def _failing_step(rank, world, tmpdir, dist, E):
@@ -192,6 +258,15 @@ def test_two_gpu_sharded_decode_matches_oracle(tmp_path):
     assert res[0][1]["engine_excess"] <= 0, res[0][1]
 
 
+def test_two_gpu_engine_28_layers_grouped_gathers_and_shared_read_back(tmp_path):
+    _need_two_gpus()
+    res = _spawn(tmp_path, "engine28")
+    for rank, report, err in res:
+        assert err is None, (rank, err)
+        assert report["engine28_excess"] <= 0, (rank, report)
+    assert res[0][1]["engine28_checked"] == 28 + 14 and res[1][1]["engine28_checked"] == 14, res
+
+
 def test_failing_rank_does_not_hang_its_peer(tmp_path):
     _need_two_gpus()
     res = _spawn(tmp_path, "fail")
@@ -199,3 +274,40 @@ def test_failing_rank_does_not_hang_its_peer(tmp_path):
         assert err is None, (rank, err)
     assert res[1][1]["status"] == -2, res   # KVX_EBUSY: victims pinned
     assert res[0][1]["status"] == -9, res   # KVX_EPEER
+
+
+def test_one_process_decodes_on_two_devices(oracle):
+    """The kernels that need more than 48 KB of shared memory (fp16 and int8
+    tensor-core decode, dense attention) set that attribute per device: a
+    process that decodes on device 0 and then on device 1 gets the oracle's
+    result on both."""
+    _need_two_gpus()
+    sys.path[:0] = [os.path.join(ROOT, "tests"), os.path.join(ROOT, "adaptive-hierarchical-llm-inference-engine_b200")]
+    import kvgen
+    import kvx
+    lens = np.array([900, 4096, 33], np.int32)
+    bt, num_pages = kvgen.paged_layout(lens, PT, 0, seed=401)
+    pool = kvgen.normal(402, (num_pages, 2, HKV, PT, DIM)).astype(np.float16)
+    q = kvgen.normal(403, (lens.size, HQ, DIM)).astype(np.float16)
+    ref = oracle.paged_decode(pool, bt, lens, q.astype(np.float32))
+    qd_, kd_ = kvgen.normal(404, (300, DIM)), kvgen.normal(405, (700, DIM))
+    vd_ = kvgen.normal(406, (700, DIM))
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            d = torch.device("cuda", dev)
+            got = kvx.decode(torch.from_numpy(pool).to(d), torch.from_numpy(bt).to(d), torch.from_numpy(lens).to(d),
+                             torch.from_numpy(q).to(d)).float().cpu().numpy()
+            assert (np.abs(got - ref) - (ATOL + RTOL * np.abs(ref))).max() <= 0, dev
+            codes, stats = kvx.compress_int8(torch.from_numpy(pool).to(d))
+            cpool = codes.view(num_pages, 2, HKV, PT, DIM)
+            got8 = kvx.decode(cpool, torch.from_numpy(bt).to(d), torch.from_numpy(lens).to(d),
+                              torch.from_numpy(q).to(d), stats=stats).float().cpu().numpy()
+            ref8 = oracle.paged_decode(codes.cpu().numpy().reshape(cpool.shape), bt, lens, q.astype(np.float32),
+                                       stats=stats.cpu().numpy().reshape(num_pages, 2, HKV, 4))
+            assert (np.abs(got8 - ref8) - (ATOL + RTOL * np.abs(ref8))).max() <= 0, dev
+            att = kvx.attention_dense(torch.from_numpy(qd_).float().to(d), torch.from_numpy(kd_).float().to(d),
+                                      torch.from_numpy(vd_).float().to(d)).cpu().numpy()
+            s = qd_ @ kd_.T / np.sqrt(DIM)
+            p = np.exp(s - s.max(1, keepdims=True))
+            want = (p / p.sum(1, keepdims=True)) @ vd_
+            assert np.abs(att - want).max() <= 1e-4 * max(1.0, np.abs(want).max()), dev
