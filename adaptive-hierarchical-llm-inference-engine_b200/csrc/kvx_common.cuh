@@ -74,6 +74,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One arrival on `bar` (release: this thread's earlier shared-memory reads
+// and writes are ordered before whoever waits on the phase it completes).
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Bulk global -> shared copy completing on `bar` (bytes % 16 == 0, both
 // addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32_t bytes,

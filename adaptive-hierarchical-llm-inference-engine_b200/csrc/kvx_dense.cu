@@ -209,11 +209,17 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 //  * A CTA owns 16 query rows (the mma's M) and half of the keys: the two
 //    CTAs of a cluster split the keys and merge through distributed shared
 //    memory, so 1,024 queries make 128 CTAs.
-//  * K and V stream through shared memory in tiles of 64 keys (cp.async,
-//    double buffered, rows padded to 132 floats so that every fragment
-//    load below is bank-conflict free); warp w takes keys 8w .. 8w+7 of
-//    each tile: S = Q K^T (16 k-steps), online softmax in the log2 domain,
-//    O += P V (16 n-tiles).
+//  * K and V stream through shared memory in tiles of 64 keys (TMA, four
+//    64 x 32 boxes each with 128-byte swizzle, so every fragment load below
+//    is bank-conflict free) in a ring of three buffers: one producer warp
+//    fills a buffer ("full" mbarrier) once all eight consumer warps have
+//    released it ("empty" mbarrier, one arrival per warp), so the consumer
+//    warps never meet at a block barrier inside the loop and drift apart
+//    (one warp's softmax overlaps another's mmas).  Consumer warp w takes
+//    keys 8w .. 8w+7 of each tile: S = Q K^T (16 k-steps), online softmax in
+//    the log2 domain, O += P V (16 n-tiles); it issues the S mmas of tile
+//    t+1 before the softmax and P V of tile t, so its own mma chains overlap
+//    its softmax.
 //  * P feeds the P.V mma straight from the S accumulators: a thread holds
 //    keys 2t, 2t+1 of its rows, which the A fragment wants at k positions
 //    t, t+4, so the P.V k order is permuted (position t <-> key 2t,
@@ -223,8 +229,6 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 constexpr int kTcRows = 16, kTcKeys = 64, kTcWarpsD = 8, kTcOPad = 136;
 constexpr int kTcTileFloats = kTcKeys * 128;               // one K or V tile: 4 swizzled boxes of 64 x 32
 constexpr int kTcQWords = 16 * 32 * 8;                      // Q A-fragments: big [k-step][lane][4], then small
-constexpr int kTcSmem = 1024 /* alignment */ + (4 * kTcTileFloats + kTcQWords) * 4 + 2 * kTcWarpsD * kTcRows * 4 +
-                        2 * kTcRows * 4 + 64;
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
     uint32_t r;
@@ -269,55 +273,43 @@ __device__ __forceinline__ int swz_f(int r, int d) {
     return (d >> 5) * (kTcKeys * 32) + r * 32 + ((((d >> 2) & 7) ^ (r & 7)) << 2) + (d & 3);
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcWarpsD * 32, 1)
-attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int seq_q, int seq_k, float scale_log2,
-                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv) {
+constexpr int kTcStagesD = 3;
+constexpr int kTcThreadsD = (kTcWarpsD + 1) * 32;  // 8 consumer warps + the producer
+constexpr int kTcSmem = 1024 /* alignment */ + (2 * kTcStagesD * kTcTileFloats + kTcQWords) * 4 +
+                       2 * kTcWarpsD * kTcRows * 4 + 2 * kTcRows * 4 + 2 * kTcStagesD * 8 + 16;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreadsD, 1)
+attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int seq_q, int seq_k,
+                        float scale_log2, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) float dsm_raw[];
-    // 1024-byte alignment for the 128-byte-swizzled boxes
     float *dsm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-    float *kt = dsm;                                    // [2][4 boxes][64][32]
-    float *vt = kt + 2 * kTcTileFloats;                 // [2][4 boxes][64][32]
-    // Q as ready A fragments: lane l's {a0..a3} of k-step ks, big and small
-    // in separate arrays (a warp's 16-byte loads cover 512 contiguous bytes)
-    uint4 *qfb = reinterpret_cast<uint4 *>(vt + 2 * kTcTileFloats);       // [16][32]
-    uint4 *qfs = qfb + 16 * 32;                                           // [16][32]
-    float *wm = reinterpret_cast<float *>(qfs + 16 * 32);                 // [8][16] warp maxima
-    float *wl = wm + kTcWarpsD * kTcRows;                                  // [8][16] warp sums
-    uint64_t *bars = reinterpret_cast<uint64_t *>(wl + kTcWarpsD * kTcRows + 2 * kTcRows);  // per tile buffer
+    float *kt = dsm;                                  // [3][4 boxes][64][32]
+    float *vt = kt + kTcStagesD * kTcTileFloats;        // [3][4 boxes][64][32]
+    uint4 *qfb = reinterpret_cast<uint4 *>(vt + kTcStagesD * kTcTileFloats);  // [16][32]
+    uint4 *qfs = qfb + 16 * 32;                                              // [16][32]
+    float *wm = reinterpret_cast<float *>(qfs + 16 * 32);                    // [8][16] warp maxima
+    float *wl = wm + kTcWarpsD * kTcRows;                                     // [8][16] warp sums
+    uint64_t *full = reinterpret_cast<uint64_t *>(wl + kTcWarpsD * kTcRows + 2 * kTcRows);
+    uint64_t *empty = full + kTcStagesD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int rank = (int)cluster.block_rank();
     const int row0 = (blockIdx.x >> 1) * kTcRows;
-    // this CTA's keys: a half of them, in whole tiles
     const int half = ((seq_k + 1) / 2 + kTcKeys - 1) / kTcKeys * kTcKeys;
     const int kbeg = rank * half, kend = min(seq_k, kbeg + half);
     const int ntiles = kend > kbeg ? (kend - kbeg + kTcKeys - 1) / kTcKeys : 0;
 
-    // A tile's K and V arrive as four 64-key x 32-dim boxes each (TMA tensor
-    // copies, 128-byte swizzle, rows past the keys filled with zeros),
-    // completing on the buffer's mbarrier; thread 0 issues them.
     if (threadIdx.x == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int b = 0; b < kTcStagesD; ++b) {
+            mbar_init(&full[b], 1);
+            mbar_init(&empty[b], kTcWarpsD);
+        }
         fence_barrier_init();
     }
-    __syncthreads();
-    auto load_tile = [&](int i, int buf) {  // thread 0
-        const int key0 = kbeg + i * kTcKeys;
-        float *kd = kt + buf * kTcTileFloats, *vd = vt + buf * kTcTileFloats;
-        fence_proxy_async_smem();  // the buffer's earlier generic reads before the async writes
-        mbar_arrive_expect_tx(&bars[buf], 2u * kTcTileFloats * 4u);
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            tma_load_2d_f(kd + b * kTcKeys * 32, &tmk, 32 * b, key0, &bars[buf]);
-            tma_load_2d_f(vd + b * kTcKeys * 32, &tmv, 32 * b, key0, &bars[buf]);
-        }
-    };
-    if (ntiles > 0 && threadIdx.x == 0) load_tile(0, 0);
-    // thread (ks, ln) builds lane ln's fragments of k-step ks: rows g, g + 8,
-    // dims 8ks + t, 8ks + t + 4
+    // Q as ready A fragments (all threads): lane ln's {a0..a3} of k-step ks
     for (int i = threadIdx.x; i < 16 * 32; i += blockDim.x) {
         const int ks = i >> 5, ln = i & 31, gg = ln >> 2, tt = ln & 3;
         uint32_t b[4], sm[4];
@@ -330,114 +322,137 @@ attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int
         qfb[i] = make_uint4(b[0], b[1], b[2], b[3]);
         qfs[i] = make_uint4(sm[0], sm[1], sm[2], sm[3]);
     }
+    __syncthreads();  // barriers initialised, Q fragments visible
 
     float o[16][4];
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;  // rows g, g + 8
 
-    for (int it = 0; it < ntiles; ++it) {
-        const int buf = it & 1;
-        if (it + 1 < ntiles && threadIdx.x == 0) load_tile(it + 1, buf ^ 1);
-        (void)mbar_wait_bounded(&bars[buf], (it >> 1) & 1, nullptr);
-        __syncthreads();  // tile `it` (and Q, the first time) visible to every warp
-        const float *kd = kt + buf * kTcTileFloats;
-        const float *vd = vt + buf * kTcTileFloats;
-        const int kr = 8 * warp;  // this warp's first key row in the tile
-        // S = Q K^T over this warp's 8 keys: six independent accumulator
-        // chains (product kind x k-step parity), so consecutive mmas do
-        // not wait for each other, summed at the end
-        float acc[6][4];
+    if (warp == kTcWarpsD) {  // ---- producer (the whole warp waits, lane 0 issues: it stays converged)
+        for (int it = 0; it < ntiles; ++it) {
+            const int b = it % kTcStagesD;
+            if (it >= kTcStagesD)  // the consumers released tile it - 3
+                (void)mbar_wait_bounded(&empty[b], ((it / kTcStagesD) - 1) & 1, nullptr);
+            if (lane == 0) {
+                const int key0 = kbeg + it * kTcKeys;
+                float *kd = kt + b * kTcTileFloats, *vd = vt + b * kTcTileFloats;
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&full[b], 2u * kTcTileFloats * 4u);
 #pragma unroll
-        for (int c = 0; c < 6; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < 16; ++ks) {
-            const int d0 = 8 * ks + t;
-            const uint4 fb = qfb[ks * 32 + lane], fs = qfs[ks * 32 + lane];
-            uint32_t bb0, bs0, bb1, bs1;
-            split_tf32(kd[swz_f(kr + g, d0)], bb0, bs0);
-            split_tf32(kd[swz_f(kr + g, d0 + 4)], bb1, bs1);
-            const int p = ks & 1;
-            mma_tf32(acc[p], fs.x, fs.y, fs.z, fs.w, bb0, bb1);
-            mma_tf32(acc[2 + p], fb.x, fb.y, fb.z, fb.w, bs0, bs1);
-            mma_tf32(acc[4 + p], fb.x, fb.y, fb.z, fb.w, bb0, bb1);
+                for (int x = 0; x < 4; ++x) {
+                    tma_load_2d_f(kd + x * kTcKeys * 32, &tmk, 32 * x, key0, &full[b]);
+                    tma_load_2d_f(vd + x * kTcKeys * 32, &tmv, 32 * x, key0, &full[b]);
+                }
+            }
+            __syncwarp();
         }
-        float sacc[4];
+    } else if (ntiles > 0) {  // ---- consumer warp: keys 8w .. 8w+7 of every tile
+        const int kr = 8 * warp;
+        // S = Q K^T over this warp's 8 keys of one tile: six independent
+        // accumulator chains (product kind x k-step parity)
+        auto qk = [&](const float *kd, float (&sacc)[4]) {
+            float acc[6][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            sacc[e] = ((acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e])) + (acc[4][e] + acc[5][e]);
-        // online softmax (log2 domain) of rows g (keys 2t, 2t+1) and g + 8
-        const int kidx = kbeg + it * kTcKeys + 8 * warp + 2 * t;
-        float s00 = kidx < kend ? sacc[0] * scale_log2 : -CUDART_INF_F;
-        float s01 = kidx + 1 < kend ? sacc[1] * scale_log2 : -CUDART_INF_F;
-        float s10 = kidx < kend ? sacc[2] * scale_log2 : -CUDART_INF_F;
-        float s11 = kidx + 1 < kend ? sacc[3] * scale_log2 : -CUDART_INF_F;
-        float mx0 = fmaxf(s00, s01), mx1 = fmaxf(s10, s11);
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-        const float a0 = n0 == -CUDART_INF_F ? 1.f : exp2f(m0 - n0);
-        const float a1 = n1 == -CUDART_INF_F ? 1.f : exp2f(m1 - n1);
-        const float p00 = n0 == -CUDART_INF_F ? 0.f : exp2f(s00 - n0);
-        const float p01 = n0 == -CUDART_INF_F ? 0.f : exp2f(s01 - n0);
-        const float p10 = n1 == -CUDART_INF_F ? 0.f : exp2f(s10 - n1);
-        const float p11 = n1 == -CUDART_INF_F ? 0.f : exp2f(s11 - n1);
-        m0 = n0;
-        m1 = n1;
-        l0 = l0 * a0 + (p00 + p01);
-        l1 = l1 * a1 + (p10 + p11);
-        // O = O * alpha + P V: A positions t / t+4 hold keys 2t / 2t+1
-        uint32_t pb[4], ps[4];
-        split_tf32(p00, pb[0], ps[0]);
-        split_tf32(p10, pb[1], ps[1]);
-        split_tf32(p01, pb[2], ps[2]);
-        split_tf32(p11, pb[3], ps[3]);
-        if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {  // a running max moved
+            for (int c = 0; c < 6; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < 16; ++ks) {
+                const int d0 = 8 * ks + t;
+                const uint4 fb = qfb[ks * 32 + lane], fs = qfs[ks * 32 + lane];
+                uint32_t bb0, bs0, bb1, bs1;
+                split_tf32(kd[swz_f(kr + g, d0)], bb0, bs0);
+                split_tf32(kd[swz_f(kr + g, d0 + 4)], bb1, bs1);
+                const int p = ks & 1;
+                mma_tf32(acc[p], fs.x, fs.y, fs.z, fs.w, bb0, bb1);
+                mma_tf32(acc[2 + p], fb.x, fb.y, fb.z, fb.w, bs0, bs1);
+                mma_tf32(acc[4 + p], fb.x, fb.y, fb.z, fb.w, bb0, bb1);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                sacc[e] = ((acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e])) + (acc[4][e] + acc[5][e]);
+        };
+        float scur[4], snext[4] = {0.f, 0.f, 0.f, 0.f};
+        (void)mbar_wait_bounded(&full[0], 0, nullptr);
+        qk(kt, scur);
+        for (int it = 0; it < ntiles; ++it) {
+            const int b = it % kTcStagesD;
+            if (it + 1 < ntiles) {  // the next tile's scores first: independent of this tile's softmax
+                const int nb = (it + 1) % kTcStagesD;
+                (void)mbar_wait_bounded(&full[nb], ((it + 1) / kTcStagesD) & 1, nullptr);
+                qk(kt + nb * kTcTileFloats, snext);
+            }
+            const float *vd = vt + b * kTcTileFloats;
+            // online softmax (log2 domain) of rows g (keys 2t, 2t+1) and g + 8
+            const int kidx = kbeg + it * kTcKeys + 8 * warp + 2 * t;
+            const float s00 = kidx < kend ? scur[0] * scale_log2 : -CUDART_INF_F;
+            const float s01 = kidx + 1 < kend ? scur[1] * scale_log2 : -CUDART_INF_F;
+            const float s10 = kidx < kend ? scur[2] * scale_log2 : -CUDART_INF_F;
+            const float s11 = kidx + 1 < kend ? scur[3] * scale_log2 : -CUDART_INF_F;
+            float mx0 = fmaxf(s00, s01), mx1 = fmaxf(s10, s11);
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+            const float a0 = n0 == -CUDART_INF_F ? 1.f : exp2f(m0 - n0);
+            const float a1 = n1 == -CUDART_INF_F ? 1.f : exp2f(m1 - n1);
+            const float p00 = n0 == -CUDART_INF_F ? 0.f : exp2f(s00 - n0);
+            const float p01 = n0 == -CUDART_INF_F ? 0.f : exp2f(s01 - n0);
+            const float p10 = n1 == -CUDART_INF_F ? 0.f : exp2f(s10 - n1);
+            const float p11 = n1 == -CUDART_INF_F ? 0.f : exp2f(s11 - n1);
+            m0 = n0;
+            m1 = n1;
+            l0 = l0 * a0 + (p00 + p01);
+            l1 = l1 * a1 + (p10 + p11);
+            uint32_t pb[4], ps[4];
+            split_tf32(p00, pb[0], ps[0]);
+            split_tf32(p10, pb[1], ps[1]);
+            split_tf32(p01, pb[2], ps[2]);
+            split_tf32(p11, pb[3], ps[3]);
+            // O = O * alpha + P V (alpha is 1 unless a running max moved;
+            // scaling unconditionally keeps the loop body one basic block)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 o[j][0] *= a0;
                 o[j][1] *= a0;
                 o[j][2] *= a1;
                 o[j][3] *= a1;
+                uint32_t bb0, bs0, bb1, bs1;
+                split_tf32(vd[swz_f(kr + 2 * t, 8 * j + g)], bb0, bs0);
+                split_tf32(vd[swz_f(kr + 2 * t + 1, 8 * j + g)], bb1, bs1);
+                mma3(o[j], pb, ps, bb0, bb1, bs0, bs1);
             }
-        }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with tile it's buffer
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            uint32_t bb0, bs0, bb1, bs1;
-            split_tf32(vd[swz_f(kr + 2 * t, 8 * j + g)], bb0, bs0);
-            split_tf32(vd[swz_f(kr + 2 * t + 1, 8 * j + g)], bb1, bs1);
-            mma3(o[j], pb, ps, bb0, bb1, bs0, bs1);
+            for (int e = 0; e < 4; ++e) scur[e] = snext[e];
         }
-        __syncthreads();  // every warp is done with this buffer before it is refilled
     }
+    __syncthreads();  // every warp is done with the ring: it holds the partials now
 
-    // ---- merge the 8 warps: per row M = max, weights exp2(m_w - M)
+    // ---- merge the 8 consumer warps, then the cluster's two CTAs
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    if (t == 0) {
-        wm[warp * kTcRows + g] = m0;
-        wm[warp * kTcRows + g + 8] = m1;
-        wl[warp * kTcRows + g] = l0;
-        wl[warp * kTcRows + g + 8] = l1;
-    }
-    // the (idle) tiles: [8][16][136] partial O (rows padded: the float2
-    // stores of a half-warp hit distinct banks)
-    float *po = dsm + warp * kTcRows * kTcOPad;
+    if (warp < kTcWarpsD) {
+        if (t == 0) {
+            wm[warp * kTcRows + g] = m0;
+            wm[warp * kTcRows + g + 8] = m1;
+            wl[warp * kTcRows + g] = l0;
+            wl[warp * kTcRows + g + 8] = l1;
+        }
+        float *po = dsm + warp * kTcRows * kTcOPad;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        *reinterpret_cast<float2 *>(po + g * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
-        *reinterpret_cast<float2 *>(po + (g + 8) * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
+        for (int j = 0; j < 16; ++j) {
+            *reinterpret_cast<float2 *>(po + g * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
+            *reinterpret_cast<float2 *>(po + (g + 8) * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
+        }
     }
     __syncthreads();
-    // this CTA's rows: unnormalised O (over its keys), max M and sum L, in
-    // the region after the 8 partials (read by the cluster's rank 0)
     float *co = dsm + kTcWarpsD * kTcRows * kTcOPad;  // [16][128]
-    float *cml = co + kTcRows * 128;              // [16][2]
-    if (threadIdx.x < kTcRows) {  // per row, once: M, each warp's weight (over its max), L
+    float *cml = co + kTcRows * 128;                  // [16][2]
+    if (threadIdx.x < kTcRows) {
         const int r = threadIdx.x;
         float M = -CUDART_INF_F;
 #pragma unroll
@@ -461,7 +476,7 @@ attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int
         for (int w = 0; w < kTcWarpsD; ++w) acc += wm[w * kTcRows + r] * dsm[(w * kTcRows + r) * kTcOPad + d];
         co[i] = acc;
     }
-    cluster.sync();  // both CTAs' rows are in shared memory
+    cluster.sync();
     if (rank == 0) {
         const float *ro = cluster.map_shared_rank(co, 1);
         const float *rml = cluster.map_shared_rank(cml, 1);
@@ -477,7 +492,7 @@ attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int
             out[(size_t)(row0 + r) * 128 + (i & 127)] = (wa * co[i] + wb * ro[i]) / L;
         }
     }
-    cluster.sync();  // rank 1's shared memory stays until rank 0 has read it
+    cluster.sync();
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
@@ -533,9 +548,9 @@ extern "C" KVX_API int kvx_attention_dense(const float *Q, const float *K, const
         static std::atomic<bool> attr_done[kMaxDevices];
         CUtensorMap tmk, tmv;
         if (make_rows_map(&tmk, K, seq_k) && make_rows_map(&tmv, V, seq_k)) {
-            if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
             const unsigned tiles = (unsigned)((seq_q + kTcRows - 1) / kTcRows);
-            attention_tc128_kernel<<<2 * tiles, kTcWarpsD * 32, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
+            if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
+            attention_tc128_kernel<<<2 * tiles, kTcThreadsD, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
                 Q, out, (int)seq_q, (int)seq_k, s * 1.4426950408889634f, tmk, tmv);
             return launch_status();
         }
