@@ -63,9 +63,10 @@ def parse():
     ap.add_argument("--tier-ram-gb", type=float, default=0.0,
                     help="config 4: RAM tier size (0: every non-resident frame in pinned RAM; "
                          "else the rest go to a spill file, the disk tier)")
-    ap.add_argument("--tier-device-policy", action="store_true",
-                    help="config 4: the LRU bookkeeping as kernels on the device (kvx_tier_step_device): "
-                         "the step's ids go up, the block tables come out of the policy, no host planning")
+    ap.add_argument("--tier-host-policy", action="store_true",
+                    help="config 4: the LRU bookkeeping on the host (kvx_tier_step) instead of as kernels on the "
+                         "device (kvx_tier_step_device, the default: the step's ids go up, the block tables come "
+                         "out of the policy, no host planning)")
     ap.add_argument("--tier-prefetch", action="store_true",
                     help="config 4: plan and load per layer, the Scheduler's prefetch depth (kvx_scheduler_depth, "
                          "fed each plan's load latency) deciding how many layers ahead of the decode")
@@ -1243,7 +1244,7 @@ def run_config4(args):
         return (base + np.take_along_axis(perms, r, axis=1)).astype(np.int32).ravel()
 
     t0 = time.perf_counter()
-    dpol = bool(args.tier_device_policy) and not H
+    dpol = not args.tier_host_policy and not H  # the disk tier runs on the host policy
     look = SCHED_MAX_DEPTH - 1 if args.tier_prefetch else 0
     tier = Tier(FB, U, C, S, device=0, load_ctas=int(os.environ.get("KVX_TIER_LOAD_CTAS", "0")),
                 store_ctas=int(os.environ.get("KVX_TIER_STORE_CTAS", "0")), host_frames=H,
