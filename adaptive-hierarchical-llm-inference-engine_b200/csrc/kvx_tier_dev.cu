@@ -42,7 +42,7 @@ enum { kHead, kBase, kResident, kDevFree, kDevHead, kHostFree, kErr, kCompact, k
 // per-step counts (device int32): loads, write-backs, misses of non-resident
 // frames, events (misses), evictions, step rejected, and the free lists'
 // state before the step (device: count and head of the FIFO; host: stack top)
-enum { cLoads, cWbs, cM0, cEvents, cEvict, cBad, cDevTop, cDevHead, cHostTop, cCountsN };
+enum { cLoads, cWbs, cM0, cEvents, cEvict, cBad, cDevCount, cDevHead, cHostTop, cCountsN };
 
 struct View {  // the policy's device arrays, passed by value to the kernels
     int64_t U, C, W, max_n, dev_slots;
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kT) apply_kernel(View s, const int32_t *__rest
         s.counts[cLoads] = lb;
         s.counts[cWbs] = wb;
         s.counts[cEvict] = vb;
-        s.counts[cDevTop] = (int32_t)s.ctl[kDevFree];
+        s.counts[cDevCount] = (int32_t)s.ctl[kDevFree];
         s.counts[cDevHead] = (int32_t)dev_head;
         s.counts[cHostTop] = (int32_t)host_top;
     }
@@ -436,7 +436,7 @@ __global__ void commit_kernel(View s, const int32_t *__restrict__ frames, int n,
     const int loads = bad ? 0 : s.counts[cLoads], wbs = bad ? 0 : s.counts[cWbs];
     const int E = bad ? 0 : s.counts[cEvents];
     // the free lists as apply_kernel saw them (thread 0 of block 0 updates ctl below)
-    const long long dev_cnt = s.counts[cDevTop], dev_head = s.counts[cDevHead], host_top = s.counts[cHostTop];
+    const long long dev_cnt = s.counts[cDevCount], dev_head = s.counts[cDevHead], host_top = s.counts[cHostTop];
     const int stride = gridDim.x * blockDim.x, id = blockIdx.x * blockDim.x + threadIdx.x;
     for (int i = id; i < n; i += stride) {
         const int32_t f = frames[i];
