@@ -52,6 +52,22 @@ def test_scheduler_c_entry_points_match_reference():
         s.close()
 
 
+def test_scheduler_c_entry_points_check_arguments():
+    import ctypes
+    from kvx import KvxError
+    from kvx.scheduler import Scheduler, lib as slib
+    with pytest.raises(KvxError):
+        Scheduler(0)  # max_depth >= 1
+    s = Scheduler(4)
+    with pytest.raises(KvxError):
+        s.observe(-1.0)
+    with pytest.raises(KvxError):
+        s.depth(0, -1, 10)
+    assert slib.kvx_scheduler_depth(s.h, 0, 0, 10, None) == -1
+    assert s.depth(0, 10, 10) == 1  # a full cache: depth 1 whatever the latency
+    s.close()
+
+
 def test_prefetcher_drop_in(built):
     """Prefetcher (prefetch/prefetcher.h:14-38): requests are served in FIFO
     order by the worker; a mover result of 0 is a hit (no load, nothing

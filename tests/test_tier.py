@@ -147,6 +147,11 @@ def test_device_policy_config_is_checked():
     assert e.value.status == -1
     t = Tier(64, 100, 20, 3, device=-1)
     assert lib.kvx_tier_step_device(t.h, None, 0, None, None, None, None) == -4
+    import ctypes
+    st = ctypes.c_void_p()
+    assert lib.kvx_tier_plan_stream(t.h, ctypes.byref(st)) == -4  # host-policy store: no plan stream
+    with pytest.raises(KvxError):
+        Tier(64, 100, 20, 3, device=-1, lookahead=63)  # lookahead 0..62
 
 
 def test_lookahead_contract_and_slot_quarantine(oracle):
