@@ -16,9 +16,15 @@
 namespace kvx_engine {
 namespace {
 
-// Layers per group of a decode step: inputs are copied and outputs read back
-// per group (one event each way), the group's launches run back to back.
-constexpr int kLayerGroup = 7;
+// Layers of the edge groups of a decode step: inputs are copied and outputs
+// read back per group (one event each way), the group's launches run back to
+// back.  The first group's input copy and the last group's read-back overlap
+// no kernel, so those groups are short; the layers between them form one
+// group (KVX_ENGINE_GROUP = n > 0 splits them into groups of n), because
+// every group boundary puts an event record and wait between two dependent
+// launches (about 25 us) while a layer's copies (about 6 us in, 4 us out at
+// batch 32) hide easily behind the 2-layer groups' kernels.
+constexpr int kEdgeGroup = 2;
 
 int env_int(const char *name, int dflt) {
     const char *v = getenv(name);
@@ -1033,17 +1039,18 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     // nothing in between and each may start while the previous drains
     // (programmatic dependent launch); the groups' copies overlap the other
     // groups' kernels.
-    // group starts: 2 layers, then kLayerGroup at a time, the last 2 alone
-    // -- the first group's input copy and the last group's output copy are
-    // not overlapped by any kernel, so they are kept short
+    // group starts: kEdgeGroup layers, the middle ones (in groups of
+    // KVX_ENGINE_GROUP when set), the last kEdgeGroup alone
     int gstart[64];
     int ngroups = 0;
     gstart[ngroups++] = 0;
-    if (L > kLayerGroup) {
-        int l = 2;
+    if (L > 3 * kEdgeGroup) {
+        const int mid = std::max(0, env_int("KVX_ENGINE_GROUP", 0));
+        int l = kEdgeGroup;
         gstart[ngroups++] = l;
-        while (L - l > kLayerGroup + 2 && ngroups < 62) gstart[ngroups++] = (l += kLayerGroup);
-        if (L - l > 2) gstart[ngroups++] = L - 2;
+        if (mid > 0)
+            while (L - kEdgeGroup - l > mid && ngroups < 62) gstart[ngroups++] = (l += mid);
+        gstart[ngroups++] = L - kEdgeGroup;
     }
     gstart[ngroups] = L;
     // with the batch at max_batch the layers are contiguous on both sides:

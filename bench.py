@@ -491,7 +491,7 @@ def run_ours(args):
     # the engine owns the paged KV cache: one fp16 pool per layer, this
     # rank's KV heads, sequences with seeded lengths and permuted pages
     lens0 = workload_lens(B)
-    reserve = max(total_steps, 24)  # the e2e pass appends up to 17 more tokens
+    reserve = max(total_steps, E2E_WARM + E2E_MAX_STEPS + 1)  # the e2e pass appends after the timed steps
     need_pages = int(((lens0 + reserve + PT - 1) // PT).sum())
     # the RAM and int8 tiers' slabs are made by start(): four of each (the
     # layer moves below use layer 0)
@@ -672,6 +672,9 @@ def run_engine_ops(api, slab_bytes, E=None, bufs=None):
     return out
 
 
+E2E_WARM, E2E_MAX_STEPS = 3, 64
+
+
 def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
     """The same step through the engine's public C ABI with host buffers:
     adaptive_engine_decode_step copies every layer's q / new K / new V from
@@ -685,7 +688,7 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
         uid = [E.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         E.set_comm(rank, world, uid[0])
-    steps = max(4, min(args.steps, 16))
+    steps = max(8, min(args.steps, E2E_MAX_STEPS))
     h_q = torch.randn((LAYERS, B, hq, DIM), dtype=torch.float16).pin_memory()
     h_k = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
     h_v = torch.randn((LAYERS, B, hkv, DIM), dtype=torch.float16).pin_memory()
@@ -695,7 +698,8 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
     h_o = torch.empty((LAYERS, world, B, hq, DIM), dtype=torch.float16).pin_memory()
     if world > 1:
         E.set_readback_share(True)
-    E.decode_step(h_q, h_k, h_v, h_o)  # warm-up: the engine's sequences start at lens0
+    for _ in range(E2E_WARM):  # warm-up: the engine's sequences start at lens0
+        E.decode_step(h_q, h_k, h_v, h_o)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -703,7 +707,7 @@ def run_e2e(args, E, lens0, hq, hkv, world, rank, B):
     t0 = time.perf_counter()
     for k in range(steps):
         E.decode_step(h_q, h_k, h_v, h_o)
-        nbytes += int((lens0 + 2 + k).sum()) * 2 * hkv * DIM * 2 * LAYERS
+        nbytes += int((lens0 + E2E_WARM + 1 + k).sum()) * 2 * hkv * DIM * 2 * LAYERS
     secs = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([secs], device="cuda")

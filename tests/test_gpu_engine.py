@@ -155,12 +155,13 @@ def test_decode_step_with_layers_in_other_tiers(engine, oracle):
         assert excess.max() <= 0, l
 
 
-def test_decode_step_28_layers_with_split_contexts(engine, oracle):
+def test_decode_step_28_layers_with_split_contexts(engine, oracle, monkeypatch):
     """adaptive_engine_decode_step at the bench's depth: 28 layers, run in
-    groups of 2, 7, 7, 7, 3 and 2 layers (dependent launches within a group,
-    copies between groups), batch 8 with contexts of 2,048-8,192 tokens so
-    the longer sequences are split over several CTAs; two steps, every
-    layer's output against the oracle and every pool bit for bit."""
+    groups (dependent launches within a group, copies between groups) of 2,
+    24 and 2 layers in the first step and 2, 7, 7, 7, 3 and 2 in the second
+    (KVX_ENGINE_GROUP=7), batch 8 with contexts of 2,048-8,192 tokens so the
+    longer sequences are split over several CTAs; every layer's output
+    against the oracle and every pool bit for bit."""
     E, api, tmp = engine
     L, B = 28, 8
     lens = kvgen.randint(626, B, 2048, 8192).astype(np.int32)
@@ -182,6 +183,8 @@ def test_decode_step_28_layers_with_split_contexts(engine, oracle):
     v = kvgen.normal(631, (L, B, HKV, 128)).astype(np.float16)
     outs = [np.zeros_like(q) for _ in range(2)]
     for step in range(2):
+        if step == 1:
+            monkeypatch.setenv("KVX_ENGINE_GROUP", "7")
         E.decode_step(q, k, v, outs[step])
     assert [E.lib.adaptive_engine_seq_len(s) for s in range(B)] == list(lens + 2)
     back = torch.empty_like(pools0[0])
