@@ -19,12 +19,15 @@ namespace {
 // Layers of the edge groups of a decode step: inputs are copied and outputs
 // read back per group (one event each way), the group's launches run back to
 // back.  The first group's input copy and the last group's read-back overlap
-// no kernel, so those groups are short; the layers between them form one
-// group (KVX_ENGINE_GROUP = n > 0 splits them into groups of n), because
-// every group boundary puts an event record and wait between two dependent
-// launches (about 25 us) while a layer's copies (about 6 us in, 4 us out at
-// batch 32) hide easily behind the 2-layer groups' kernels.
+// no kernel, so those groups are short.  On one GPU the layers between them
+// form one group: every group boundary puts an event record and wait between
+// two dependent launches (about 25 us), while a layer's copies (about 6 us
+// in, 4 us out at batch 32) hide easily behind the 2-layer groups' kernels.
+// With a communicator they form groups of kCommGroup, so each group's
+// all-gather and read-back run under the next group's kernels instead of
+// all at the end.  KVX_ENGINE_GROUP = n > 0 sets the middle groups' size.
 constexpr int kEdgeGroup = 2;
+constexpr int kCommGroup = 7;
 
 int env_int(const char *name, int dflt) {
     const char *v = getenv(name);
@@ -1045,7 +1048,7 @@ int Engine::decode_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
     int ngroups = 0;
     gstart[ngroups++] = 0;
     if (L > 3 * kEdgeGroup) {
-        const int mid = std::max(0, env_int("KVX_ENGINE_GROUP", 0));
+        const int mid = std::max(0, env_int("KVX_ENGINE_GROUP", comm_ ? kCommGroup : 0));
         int l = kEdgeGroup;
         gstart[ngroups++] = l;
         if (mid > 0)

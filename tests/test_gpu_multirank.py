@@ -133,7 +133,7 @@ def _worker(rank, world, port, tmpdir, result_q, mode):
 
 def _engine_28_layers(rank, world, tmpdir, dist, E, o, kr, qr):
     """adaptive_engine_decode_step at 28 layers on two GPUs: layer groups of
-    2, 24 and 2, one all-gather per group, contexts up to 5,000
+    2, 7, 7, 7, 3 and 2, one all-gather per group, contexts up to 5,000
     tokens (several splits).  Step 0: rank 0 reads every layer back; step 1:
     the read-back shared (rank r copies layers l % 2 == r).  Each rank checks
     what it read against the oracle's unsharded append + decode."""
