@@ -9,15 +9,19 @@
 // (the reference's cuda_attention leaves the scale out; TensorOps and
 // native-engine/cuda/attention.cu apply it).
 //  * softmax: one CTA per row, block reductions of max and sum.
-//  * attention, head_dim 128: 8 query rows per CTA over K / V tiles staged
-//    in shared memory (attention_dense128_kernel); other head dims (<= 1024):
-//    one CTA of 4 warps per query row, each warp every 4th key, lanes split
-//    the head dimension, online softmax per warp, warps merged through
-//    shared memory.  Neither materialises the seq x seq score matrix.
+//  * attention, head_dim 128 with 16-byte aligned rows: the 5th-generation
+//    tensor cores (attention_umma_kernel, tcgen05.mma kind::tf32 with
+//    3xTF32 products) over 128 query rows x 64 keys per CTA, then
+//    combine_splits_kernel over the key tiles.  Head dim 128 with only K / V
+//    aligned: 8 query rows per CTA over K / V tiles staged in shared memory
+//    (attention_dense128_kernel, fp32 CUDA cores).  Other head dims
+//    (<= 1024): one CTA of 4 warps per query row, each warp every 4th key,
+//    lanes split the head dimension, online softmax per warp, warps merged
+//    through shared memory.  None materialises the seq x seq score matrix.
 #include <cuda.h>
-#include <cooperative_groups.h>
 #include <math_constants.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kvx_common.cuh"
@@ -199,310 +203,363 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 }
 
 // ---------------------------------------------------------------------------
-// head_dim 128 on the tensor cores (attention_tc128_kernel).
+// head_dim 128 on the 5th-generation tensor cores (attention_umma_kernel).
 //
-// mma.sync m16n8k8 with tf32 operands and fp32 accumulation, each product
-// split three ways for fp32-grade accuracy over fp32's whole range
-// ("3xTF32"): x = big + small with big = tf32(x), small = tf32(x - big),
-// and a.b ~ big_a.big_b + big_a.small_b + small_a.big_b (the dropped
-// small.small term and small's own rounding are ~2^-21 relative).
-//  * A CTA owns 16 query rows (the mma's M) and half of the keys: the two
-//    CTAs of a cluster split the keys and merge through distributed shared
-//    memory, so 1,024 queries make 128 CTAs.
-//  * K and V stream through shared memory in tiles of 64 keys (TMA, four
-//    64 x 32 boxes each with 128-byte swizzle, so every fragment load below
-//    is bank-conflict free) in a ring of three buffers: one producer warp
-//    fills a buffer ("full" mbarrier) once all eight consumer warps have
-//    released it ("empty" mbarrier, one arrival per warp), so the consumer
-//    warps never meet at a block barrier inside the loop and drift apart
-//    (one warp's softmax overlaps another's mmas).  Consumer warp w takes
-//    keys 8w .. 8w+7 of each tile: S = Q K^T (16 k-steps), online softmax in
-//    the log2 domain, O += P V (16 n-tiles); it issues the S mmas of tile
-//    t+1 before the softmax and P V of tile t, so its own mma chains overlap
-//    its softmax.
-//  * P feeds the P.V mma straight from the S accumulators: a thread holds
-//    keys 2t, 2t+1 of its rows, which the A fragment wants at k positions
-//    t, t+4, so the P.V k order is permuted (position t <-> key 2t,
-//    position t+4 <-> key 2t+1) and V rows are read in the same order.
-//  * The 8 warps' (max, sum, O) merge through shared memory, then the
-//    cluster's two CTAs through DSMEM; rank 0 writes the rows.
-constexpr int kTcRows = 16, kTcKeys = 64, kTcWarpsD = 8, kTcOPad = 136;
-constexpr int kTcTileFloats = kTcKeys * 128;               // one K or V tile: 4 swizzled boxes of 64 x 32
-constexpr int kTcQWords = 16 * 32 * 8;                      // Q A-fragments: big [k-step][lane][4], then small
+// tcgen05.mma kind::tf32 (one thread issues, accumulators in tensor memory),
+// 3xTF32 products for fp32-grade accuracy: every operand element x enters
+// as big = x itself, of which the tensor core reads the top 19 bits (x with
+// the low 13 mantissa bits cleared), and small = x - that truncation
+// (exact); a.b ~ big.big + big.small + small.big.  A CTA owns 128 query
+// rows (the MMA's M, one tensor-memory lane per row) and one tile of 64
+// keys:
+//  * TMA brings the raw fp32 Q (4 boxes of 128 rows x 32 floats), K and V
+//    (4 boxes of 64 keys x 32 floats each), 128-byte swizzle: the K-major
+//    canonical layout of the MMA's shared-memory descriptors.  Rows past
+//    the ends read as zero.  The raw Q and K are the big operands;
+//  * the CTA's 256 threads write Q small and K small at the same swizzled
+//    offsets of their own regions;
+//  * S = Q K^T: 16 k-steps x 3 MMAs (M 128, N 64, K 8) into tensor-memory
+//    columns 0-63;
+//  * once S is complete each thread writes 32 keys of one dim of V, big and
+//    small, into the transposed (128 dims x 64 keys, K-major) V tiles over
+//    Q big; the two warpgroups load 32 columns each of their row of S
+//    (tcgen05.ld: the warps of either group reach all 128 lanes), agree on
+//    the row's max and sum in the log2 domain through shared memory and
+//    write their half of P big / small into the K-major P tiles over Q
+//    small.  (V as stored is an MN-major B operand; in the 128-byte swizzle
+//    layout that kind::tf32 MMA wrote zeros on B200 whatever its leading /
+//    stride offsets.)
+//  * O = P V: 8 k-steps x 3 MMAs (M 128, N 128, K 8) into columns 64-191;
+//    each warpgroup loads 64 columns of its row of O into a swizzled
+//    staging tile (over V), which leaves as 4 TMA tensor stores; the first
+//    warpgroup writes (max, sum): the key tile's partial.
+// combine_splits_kernel folds the key tiles' partials of every row.
+constexpr int kURows = 128, kUKeys = 64;
+constexpr int kUQBox = kURows * 128, kUKBox = kUKeys * 128;  // bytes of one Q / K (V) box
+constexpr int kUVtBox = 128 * 128;                             // 128 dims x 32 keys of the transposed V
+// Q big, Q small (64 KB each), K big, K small, raw V (32 KB each), barriers
+constexpr int kUSmem = 1024 + 224 * 1024 + 64;
+static_assert(kUSmem <= 227 * 1024, "tcgen05 attention exceeds the shared memory of a CTA");
 
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
+struct UmmaMaps {
+    CUtensorMap q, k, v, part_o;
+};
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)((lbo >> 4) & 0x3fff) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46) /* sm100 descriptor */ |
+           (2ull << 61) /* 128-byte swizzle */;
 }
 
-__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {
-    big = to_tf32(x);
-    small = to_tf32(x - __uint_as_float(big));
+// c_format F32, a/b TF32, A K-major, B K- or MN-major, N, M = 128
+__host__ __device__ constexpr uint32_t umma_idesc(int n, bool b_mn_major) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(kURows >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
-// c += A.B with A = (ab + as), B = (bb + bs), three tf32 mmas
-__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ab)[4], const uint32_t (&as)[4],
-                                     uint32_t bb0, uint32_t bb1, uint32_t bs0, uint32_t bs1) {
-    mma_tf32(c, as[0], as[1], as[2], as[3], bb0, bb1);
-    mma_tf32(c, ab[0], ab[1], ab[2], ab[3], bs0, bs1);
-    mma_tf32(c, ab[0], ab[1], ab[2], ab[3], bb0, bb1);
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d_f(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tm_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tm_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void umma_tma(uint32_t dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
 }
 
-// Float index of (row r, dim d) in a tile of four 64 x 32 boxes loaded with
-// 128-byte swizzle: box d / 32, row r, 16-byte chunk ((d / 4) % 8) XOR
-// (r % 8).  The K and V fragment reads below hit 32 distinct banks.
-__device__ __forceinline__ int swz_f(int r, int d) {
-    return (d >> 5) * (kTcKeys * 32) + r * 32 + ((((d >> 2) & 7) ^ (r & 7)) << 2) + (d & 3);
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+
+// 2^x on the special-function unit (ex2.approx.ftz: 2^-inf = +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-constexpr int kTcStagesD = 3;
-constexpr int kTcThreadsD = (kTcWarpsD + 1) * 32;  // 8 consumer warps + the producer
-constexpr int kTcSmem = 1024 /* alignment */ + (2 * kTcStagesD * kTcTileFloats + kTcQWords) * 4 +
-                       2 * kTcWarpsD * kTcRows * 4 + 2 * kTcRows * 4 + 2 * kTcStagesD * 8 + 16;
+// Tiled bulk tensor store shared -> global (completion through bulk groups).
+__device__ __forceinline__ void umma_tma_store(const CUtensorMap *tm, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreadsD, 1)
-attention_tc128_kernel(const float *__restrict__ Q, float *__restrict__ out, int seq_q, int seq_k,
-                        float scale_log2, const __grid_constant__ CUtensorMap tmk,
-                        const __grid_constant__ CUtensorMap tmv) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ __align__(16) float dsm_raw[];
-    float *dsm = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-    float *kt = dsm;                                  // [3][4 boxes][64][32]
-    float *vt = kt + kTcStagesD * kTcTileFloats;        // [3][4 boxes][64][32]
-    uint4 *qfb = reinterpret_cast<uint4 *>(vt + kTcStagesD * kTcTileFloats);  // [16][32]
-    uint4 *qfs = qfb + 16 * 32;                                              // [16][32]
-    float *wm = reinterpret_cast<float *>(qfs + 16 * 32);                    // [8][16] warp maxima
-    float *wl = wm + kTcWarpsD * kTcRows;                                     // [8][16] warp sums
-    uint64_t *full = reinterpret_cast<uint64_t *>(wl + kTcWarpsD * kTcRows + 2 * kTcRows);
-    uint64_t *empty = full + kTcStagesD;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int rank = (int)cluster.block_rank();
-    const int row0 = (blockIdx.x >> 1) * kTcRows;
-    const int half = ((seq_k + 1) / 2 + kTcKeys - 1) / kTcKeys * kTcKeys;
-    const int kbeg = rank * half, kend = min(seq_k, kbeg + half);
-    const int ntiles = kend > kbeg ? (kend - kbeg + kTcKeys - 1) / kTcKeys : 0;
+__global__ void __launch_bounds__(256, 1)
+attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
+                      float scale_log2, const __grid_constant__ UmmaMaps maps) {
+    extern __shared__ __align__(16) uint8_t usm_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(usm_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t base = smem_addr(sm);
+    const uint32_t q_big = base, q_small = base + 64 * 1024, k_big = base + 128 * 1024, k_small = base + 160 * 1024;
+    const uint32_t v_raw = base + 192 * 1024;
+    const uint32_t v_big = base, v_small = base + 32 * 1024;            // over Q big, once S is done
+    const uint32_t p_big = base + 64 * 1024, p_small = base + 96 * 1024;  // over Q small
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 224 * 1024);      // qk loads, v load, mma
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
+    float *red = reinterpret_cast<float *>(sm + 128 * 1024);  // over K, once S is done: max, sum per group
+    const int warp = threadIdx.x >> 5, wg = threadIdx.x >> 7, row = threadIdx.x & 127;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's tensor-memory lanes
+    const int row0 = blockIdx.x * kURows, key0 = blockIdx.y * kUKeys;
+    // the combine (a dependent launch) may start its CTAs now; it waits for
+    // this grid's completion before reading a partial
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
-        for (int b = 0; b < kTcStagesD; ++b) {
-            mbar_init(&full[b], 1);
-            mbar_init(&empty[b], kTcWarpsD);
-        }
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
         fence_barrier_init();
+        mbar_arrive_expect_tx(&bars[0], 4 * kUQBox + 4 * kUKBox);
+        mbar_arrive_expect_tx(&bars[1], 4 * kUKBox);
+        for (int x = 0; x < 4; ++x) {
+            umma_tma(q_big + x * kUQBox, &maps.q, 32 * x, row0, &bars[0]);
+            umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, key0, &bars[0]);
+        }
+        for (int x = 0; x < 4; ++x) umma_tma(v_raw + x * kUKBox, &maps.v, 32 * x, key0, &bars[1]);
     }
-    // Q as ready A fragments (all threads): lane ln's {a0..a3} of k-step ks
-    for (int i = threadIdx.x; i < 16 * 32; i += blockDim.x) {
-        const int ks = i >> 5, ln = i & 31, gg = ln >> 2, tt = ln & 3;
-        uint32_t b[4], sm[4];
-        const int rr[4] = {gg, gg + 8, gg, gg + 8}, dd[4] = {8 * ks + tt, 8 * ks + tt, 8 * ks + tt + 4, 8 * ks + tt + 4};
+    if (warp == 0) {  // 256 tensor-memory columns: S at 0-63, O at 64-191
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot, t_s = tmem, t_o = tmem + 64;
+
+    // Q small and K small at the raw copies' offsets in their own regions
+    (void)mbar_wait_bounded(&bars[0], 0, nullptr);
+    auto split16 = [](uint32_t raw, uint32_t dst_small) {
+        float4 v;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(raw));
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst_small), "f"(v.x - tf32_trunc(v.x)),
+                     "f"(v.y - tf32_trunc(v.y)), "f"(v.z - tf32_trunc(v.z)), "f"(v.w - tf32_trunc(v.w))
+                     : "memory");
+    };
+#pragma unroll 4
+    for (int i = threadIdx.x; i < 4 * kUQBox / 16; i += 256) split16(q_big + 16 * i, q_small + 16 * i);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < 4 * kUKBox / 16; i += 256) split16(k_big + 16 * i, k_small + 16 * i);
+    fence_proxy_async_smem();  // the split's generic stores before the tensor core's reads
+    tc_fence_before();
+    __syncthreads();
+
+    if (threadIdx.x == 0) {
+        tc_fence_after();
+        // S = Q K^T: k-step k reads 8 dims = 32 bytes of box k / 4
+        constexpr uint32_t idesc = umma_idesc(kUKeys, false);
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, bo = (k >> 2) * kUKBox + (k & 3) * 32;
+            const uint64_t ab = umma_desc(q_big + ao, 16, 1024), as = umma_desc(q_small + ao, 16, 1024);
+            const uint64_t bb = umma_desc(k_big + bo, 16, 1024), bs = umma_desc(k_small + bo, 16, 1024);
+            umma_tf32(t_s, ab, bb, idesc, k > 0);
+            umma_tf32(t_s, ab, bs, idesc, 1);
+            umma_tf32(t_s, as, bb, idesc, 1);
+        }
+        umma_commit(&bars[2]);
+    }
+    (void)mbar_wait_bounded(&bars[2], 0, nullptr);  // S complete, Q and K free
+    __syncwarp();  // warp 0's thread 0 issued the MMAs: reconverge before the aligned loads
+    tc_fence_after();
+
+    // V^T big / small, this thread's dim d = row, keys 32 wg .. 32 wg + 31:
+    // key j of raw V sits in box d / 32, row j, 16-byte chunk
+    // ((d % 32) / 4) ^ (j % 8); the transposed element (d, j) in box j / 32,
+    // row d, chunk ((j % 32) / 4) ^ (d % 8).
+    (void)mbar_wait_bounded(&bars[1], 0, nullptr);
+    {
+        const int d = row;
+        const uint32_t src = v_raw + (d >> 5) * kUKBox + (d & 3) * 4;
+#pragma unroll 4
+        for (int c = 8 * wg; c < 8 * wg + 8; ++c) {  // keys 4c .. 4c+3
+            float x[4], b[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * c + e;
+                asm volatile("ld.shared.f32 %0, [%1];"
+                             : "=f"(x[e])
+                             : "r"(src + j * 128 + ((((d & 31) >> 2) ^ (j & 7)) << 4)));
+                b[e] = tf32_trunc(x[e]);
+            }
+            const uint32_t off = (c >> 3) * kUVtBox + d * 128 + (((c & 7) ^ (d & 7)) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_big + off), "f"(x[0]), "f"(x[1]),
+                         "f"(x[2]), "f"(x[3])
+                         : "memory");
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_small + off), "f"(x[0] - b[0]),
+                         "f"(x[1] - b[1]), "f"(x[2] - b[2]), "f"(x[3] - b[3])
+                         : "memory");
+        }
+    }
+    // this warpgroup's 32 keys of the thread's row of S
+    uint32_t r[32];
+    tm_ld32(t_s + 32 * wg + lane_base, r);
+    tm_wait_ld();
+    const int nk = min(kUKeys, seq_k - key0) - 32 * wg;
+    float m = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float s = j < nk ? __uint_as_float(r[j]) * scale_log2 : -CUDART_INF_F;
+        r[j] = __float_as_uint(s);
+        m = fmaxf(m, s);
+    }
+    red[wg * 128 + row] = m;
+    __syncthreads();
+    m = fmaxf(red[row], red[128 + row]);  // finite: key key0 is valid
+    float l = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {  // keys 32 wg + 4cc .. +3: box wg, 16-byte chunk cc
+        float p4[4], b4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float x = row0 + rr[e] < seq_q ? Q[(size_t)(row0 + rr[e]) * 128 + dd[e]] : 0.f;
-            split_tf32(x, b[e], sm[e]);
+            const float s = __uint_as_float(r[4 * cc + e]);
+            p4[e] = ex2_approx(s - m);  // masked keys: s - m = -inf
+            l += p4[e];
+            b4[e] = tf32_trunc(p4[e]);
         }
-        qfb[i] = make_uint4(b[0], b[1], b[2], b[3]);
-        qfs[i] = make_uint4(sm[0], sm[1], sm[2], sm[3]);
+        const uint32_t off = wg * kUQBox + row * 128 + (((cc ^ (row & 7))) << 4);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_big + off), "f"(p4[0]), "f"(p4[1]),
+                     "f"(p4[2]), "f"(p4[3])
+                     : "memory");
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_small + off), "f"(p4[0] - b4[0]),
+                     "f"(p4[1] - b4[1]), "f"(p4[2] - b4[2]), "f"(p4[3] - b4[3])
+                     : "memory");
     }
-    __syncthreads();  // barriers initialised, Q fragments visible
-
-    float o[16][4];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;  // rows g, g + 8
-
-    if (warp == kTcWarpsD) {  // ---- producer (the whole warp waits, lane 0 issues: it stays converged)
-        for (int it = 0; it < ntiles; ++it) {
-            const int b = it % kTcStagesD;
-            if (it >= kTcStagesD)  // the consumers released tile it - 3
-                (void)mbar_wait_bounded(&empty[b], ((it / kTcStagesD) - 1) & 1, nullptr);
-            if (lane == 0) {
-                const int key0 = kbeg + it * kTcKeys;
-                float *kd = kt + b * kTcTileFloats, *vd = vt + b * kTcTileFloats;
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&full[b], 2u * kTcTileFloats * 4u);
-#pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    tma_load_2d_f(kd + x * kTcKeys * 32, &tmk, 32 * x, key0, &full[b]);
-                    tma_load_2d_f(vd + x * kTcKeys * 32, &tmv, 32 * x, key0, &full[b]);
-                }
-            }
-            __syncwarp();
-        }
-    } else if (ntiles > 0) {  // ---- consumer warp: keys 8w .. 8w+7 of every tile
-        const int kr = 8 * warp;
-        // S = Q K^T over this warp's 8 keys of one tile: six independent
-        // accumulator chains (product kind x k-step parity)
-        auto qk = [&](const float *kd, float (&sacc)[4]) {
-            float acc[6][4];
-#pragma unroll
-            for (int c = 0; c < 6; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < 16; ++ks) {
-                const int d0 = 8 * ks + t;
-                const uint4 fb = qfb[ks * 32 + lane], fs = qfs[ks * 32 + lane];
-                uint32_t bb0, bs0, bb1, bs1;
-                split_tf32(kd[swz_f(kr + g, d0)], bb0, bs0);
-                split_tf32(kd[swz_f(kr + g, d0 + 4)], bb1, bs1);
-                const int p = ks & 1;
-                mma_tf32(acc[p], fs.x, fs.y, fs.z, fs.w, bb0, bb1);
-                mma_tf32(acc[2 + p], fb.x, fb.y, fb.z, fb.w, bs0, bs1);
-                mma_tf32(acc[4 + p], fb.x, fb.y, fb.z, fb.w, bb0, bb1);
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                sacc[e] = ((acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e])) + (acc[4][e] + acc[5][e]);
-        };
-        float scur[4], snext[4] = {0.f, 0.f, 0.f, 0.f};
-        (void)mbar_wait_bounded(&full[0], 0, nullptr);
-        qk(kt, scur);
-        for (int it = 0; it < ntiles; ++it) {
-            const int b = it % kTcStagesD;
-            if (it + 1 < ntiles) {  // the next tile's scores first: independent of this tile's softmax
-                const int nb = (it + 1) % kTcStagesD;
-                (void)mbar_wait_bounded(&full[nb], ((it + 1) / kTcStagesD) & 1, nullptr);
-                qk(kt + nb * kTcTileFloats, snext);
-            }
-            const float *vd = vt + b * kTcTileFloats;
-            // online softmax (log2 domain) of rows g (keys 2t, 2t+1) and g + 8
-            const int kidx = kbeg + it * kTcKeys + 8 * warp + 2 * t;
-            const float s00 = kidx < kend ? scur[0] * scale_log2 : -CUDART_INF_F;
-            const float s01 = kidx + 1 < kend ? scur[1] * scale_log2 : -CUDART_INF_F;
-            const float s10 = kidx < kend ? scur[2] * scale_log2 : -CUDART_INF_F;
-            const float s11 = kidx + 1 < kend ? scur[3] * scale_log2 : -CUDART_INF_F;
-            float mx0 = fmaxf(s00, s01), mx1 = fmaxf(s10, s11);
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-            const float a0 = n0 == -CUDART_INF_F ? 1.f : exp2f(m0 - n0);
-            const float a1 = n1 == -CUDART_INF_F ? 1.f : exp2f(m1 - n1);
-            const float p00 = n0 == -CUDART_INF_F ? 0.f : exp2f(s00 - n0);
-            const float p01 = n0 == -CUDART_INF_F ? 0.f : exp2f(s01 - n0);
-            const float p10 = n1 == -CUDART_INF_F ? 0.f : exp2f(s10 - n1);
-            const float p11 = n1 == -CUDART_INF_F ? 0.f : exp2f(s11 - n1);
-            m0 = n0;
-            m1 = n1;
-            l0 = l0 * a0 + (p00 + p01);
-            l1 = l1 * a1 + (p10 + p11);
-            uint32_t pb[4], ps[4];
-            split_tf32(p00, pb[0], ps[0]);
-            split_tf32(p10, pb[1], ps[1]);
-            split_tf32(p01, pb[2], ps[2]);
-            split_tf32(p11, pb[3], ps[3]);
-            // O = O * alpha + P V (alpha is 1 unless a running max moved;
-            // scaling unconditionally keeps the loop body one basic block)
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                o[j][0] *= a0;
-                o[j][1] *= a0;
-                o[j][2] *= a1;
-                o[j][3] *= a1;
-                uint32_t bb0, bs0, bb1, bs1;
-                split_tf32(vd[swz_f(kr + 2 * t, 8 * j + g)], bb0, bs0);
-                split_tf32(vd[swz_f(kr + 2 * t + 1, 8 * j + g)], bb1, bs1);
-                mma3(o[j], pb, ps, bb0, bb1, bs0, bs1);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with tile it's buffer
-#pragma unroll
-            for (int e = 0; e < 4; ++e) scur[e] = snext[e];
-        }
-    }
-    __syncthreads();  // every warp is done with the ring: it holds the partials now
-
-    // ---- merge the 8 consumer warps, then the cluster's two CTAs
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    if (warp < kTcWarpsD) {
-        if (t == 0) {
-            wm[warp * kTcRows + g] = m0;
-            wm[warp * kTcRows + g + 8] = m1;
-            wl[warp * kTcRows + g] = l0;
-            wl[warp * kTcRows + g + 8] = l1;
-        }
-        float *po = dsm + warp * kTcRows * kTcOPad;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            *reinterpret_cast<float2 *>(po + g * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
-            *reinterpret_cast<float2 *>(po + (g + 8) * kTcOPad + 8 * j + 2 * t) = make_float2(o[j][2], o[j][3]);
-        }
-    }
+    red[256 + wg * 128 + row] = l;
+    fence_proxy_async_smem();  // P's generic stores before the tensor core's reads
+    tc_fence_before();
     __syncthreads();
-    float *co = dsm + kTcWarpsD * kTcRows * kTcOPad;  // [16][128]
-    float *cml = co + kTcRows * 128;                  // [16][2]
-    if (threadIdx.x < kTcRows) {
-        const int r = threadIdx.x;
-        float M = -CUDART_INF_F;
-#pragma unroll
-        for (int w = 0; w < kTcWarpsD; ++w) M = fmaxf(M, wm[w * kTcRows + r]);
-        float L = 0.f;
-#pragma unroll
-        for (int w = 0; w < kTcWarpsD; ++w) {
-            const float mw = wm[w * kTcRows + r];
-            const float sw = mw == -CUDART_INF_F ? 0.f : exp2f(mw - M);
-            L += sw * wl[w * kTcRows + r];
-            wm[w * kTcRows + r] = sw;
+    if (threadIdx.x == 0) {
+        tc_fence_after();
+        // O = P V: k-step k reads 8 keys (32 bytes of box k / 4) of P and of
+        // the transposed V
+        constexpr uint32_t idesc = umma_idesc(128, false);
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, vo = (k >> 2) * kUVtBox + (k & 3) * 32;
+            const uint64_t ab = umma_desc(p_big + ao, 16, 1024), as = umma_desc(p_small + ao, 16, 1024);
+            const uint64_t bb = umma_desc(v_big + vo, 16, 1024), bs = umma_desc(v_small + vo, 16, 1024);
+            umma_tf32(t_o, ab, bb, idesc, k > 0);
+            umma_tf32(t_o, ab, bs, idesc, 1);
+            umma_tf32(t_o, as, bb, idesc, 1);
         }
-        cml[2 * r] = M;
-        cml[2 * r + 1] = L;
+        umma_commit(&bars[2]);
     }
+    (void)mbar_wait_bounded(&bars[2], 1, nullptr);
+    __syncwarp();
+    tc_fence_after();
+    // this warpgroup's 64 columns of the row into staging boxes 2 wg, 2 wg + 1
+    // (32 columns x 128 rows each, 128-byte swizzle) over V
+    {
+        uint32_t o[64];
+        tm_ld64(t_o + 64 * wg + lane_base, o);
+        tm_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const uint32_t off = (2 * wg + (c >> 3)) * kUVtBox + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + off), "r"(o[4 * c]),
+                         "r"(o[4 * c + 1]), "r"(o[4 * c + 2]), "r"(o[4 * c + 3])
+                         : "memory");
+        }
+    }
+    const int prow0 = blockIdx.y * rows_pad + row0;
+    if (wg == 0) part_ml[(size_t)prow0 + row] = make_float2(m, red[256 + row] + red[384 + row]);
+    fence_proxy_async_smem();  // the staging stores before the bulk copy's reads
+    tc_fence_before();
     __syncthreads();
-    for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
-        const int r = i >> 7, d = i & 127;
-        float acc = 0.f;
+    if (threadIdx.x == 0) {
+        for (int x = 0; x < 4; ++x) umma_tma_store(&maps.part_o, 32 * x, prow0, base + x * kUVtBox);
+        bulk_commit();
+        bulk_wait_read_all();  // the staging tile stays until the copy has read it
+    }
+    __syncwarp();  // thread 0 rejoins its warp before the aligned dealloc
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+}
+
+// out[row] = sum_t exp2(m_t - M) O_t / sum_t exp2(m_t - M) L_t over the key
+// tiles t; one warp per row, a float4 of dims per lane.  Tiles go in
+// batches of 16 with a running max: a batch's (max, sum) pairs (lane j holds
+// tile j's) and its 16 partial rows are all loaded before any is used, so a
+// batch costs one memory round trip.  Launched as a programmatic dependent
+// of the attention grid: it waits for that grid's completion first.
+__global__ void combine_splits_kernel(const float *__restrict__ part_o, const float2 *__restrict__ part_ml,
+                                      float *__restrict__ out, int seq_q, int rows_pad, int nsplit) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row >= seq_q) return;
+    float M = -CUDART_INF_F, L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t0 = 0; t0 < nsplit; t0 += 16) {
+        const int cnt = min(16, nsplit - t0);
+        float2 ml = make_float2(-CUDART_INF_F, 0.f);
+        if (lane < cnt) ml = part_ml[(size_t)(t0 + lane) * rows_pad + row];
+        // all 16 loads issued here (volatile: not sunk to their uses); tiles
+        // past the batch re-read its first tile and get weight 0
+        float4 v[16];
 #pragma unroll
-        for (int w = 0; w < kTcWarpsD; ++w) acc += wm[w * kTcRows + r] * dsm[(w * kTcRows + r) * kTcOPad + d];
-        co[i] = acc;
-    }
-    cluster.sync();
-    if (rank == 0) {
-        const float *ro = cluster.map_shared_rank(co, 1);
-        const float *rml = cluster.map_shared_rank(cml, 1);
-        for (int i = threadIdx.x; i < kTcRows * 128; i += blockDim.x) {
-            const int r = i >> 7;
-            if (row0 + r >= seq_q) continue;
-            const float Ma = cml[2 * r], La = cml[2 * r + 1], Mb = rml[2 * r], Lb = rml[2 * r + 1];
-            const float M = fmaxf(Ma, Mb);
-            const float wa = Ma == -CUDART_INF_F ? 0.f : exp2f(Ma - M);
-            const float wb = Mb == -CUDART_INF_F ? 0.f : exp2f(Mb - M);
-            float L = wa * La + wb * Lb;
-            if (L == 0.f) L = 1e-6f;  // TensorOps::softmax's guard
-            out[(size_t)(row0 + r) * 128 + (i & 127)] = (wa * co[i] + wb * ro[i]) / L;
+        for (int u = 0; u < 16; ++u) {
+            const float *src = part_o + ((size_t)(t0 + (u < cnt ? u : 0)) * rows_pad + row) * 128 + 4 * lane;
+            asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(v[u].x), "=f"(v[u].y), "=f"(v[u].z), "=f"(v[u].w)
+                         : "l"(src));
         }
+        float mb = ml.x;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float Mn = fmaxf(M, mb);  // finite: every tile has a valid key
+        const float a = M == -CUDART_INF_F ? 0.f : exp2f(M - Mn);
+        const float w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - Mn);
+        float lb = w * ml.y;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, o);
+        L = L * a + lb;
+        acc = make_float4(acc.x * a, acc.y * a, acc.z * a, acc.w * a);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const float wu = __shfl_sync(0xffffffffu, w, u);
+            acc.x += wu * v[u].x, acc.y += wu * v[u].y, acc.z += wu * v[u].z, acc.w += wu * v[u].w;
+        }
+        M = Mn;
     }
-    cluster.sync();
+    if (L == 0.f) L = 1e-6f;  // TensorOps::softmax's guard
+    reinterpret_cast<float4 *>(out + (size_t)row * 128)[lane] =
+        make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// against libcuda): rows of 128 fp32, boxes of 64 rows x 32 floats, 128-byte
-// swizzle, zero fill past the last row.
+// against libcuda).
 using EncodeTiledFnD = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-bool make_rows_map(CUtensorMap *tm, const float *base, long long rows) {
+// fp32 rows of `cols` floats (a multiple of 32), boxes of box_rows rows x 32
+// floats, 128-byte swizzle, zero fill past the last row.
+bool make_map_f32(CUtensorMap *tm, const float *base, long long rows, int box_rows, long long cols = 128) {
     static EncodeTiledFnD fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -512,14 +569,72 @@ bool make_rows_map(CUtensorMap *tm, const float *base, long long rows) {
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<EncodeTiledFnD>(f);
     });
-    if (!fn || rows <= 0 || rows > (1ll << 31)) return false;
-    cuuint64_t gdim[2] = {128, (cuuint64_t)rows};
-    cuuint64_t gstride[1] = {128 * 4};
-    cuuint32_t box[2] = {32, (cuuint32_t)kTcKeys};
+    if (!fn || rows <= 0 || rows > (1ll << 31) || cols <= 0 || cols % 32 || cols > (1ll << 31)) return false;
+    cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
     cuuint32_t estride[2] = {1, 1};
     return fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), gdim, gstride, box, estride,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tcgen05 path: the key tiles' partials in stream-ordered scratch (the
+// device's default pool, which keeps its memory between calls), their
+// combine, the scratch released in stream order.
+int attention_umma(const float *Q, const float *K, const float *V, float *out, int seq_q, int seq_k, float s,
+                   cudaStream_t st) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVX_ECUDA;
+    static std::atomic<bool> pool_set[kMaxDevices];
+    if (!pool_set[dev].load(std::memory_order_acquire)) {
+        cudaMemPool_t pool;
+        uint64_t keep = ~0ull;
+        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess)
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        pool_set[dev].store(true, std::memory_order_release);
+    }
+    static std::atomic<bool> attr_done[kMaxDevices];
+    if (ensure_smem_attr(attr_done, attention_umma_kernel, kUSmem) != KVX_OK) return KVX_ECUDA;
+    const long long rows_pad = ((long long)seq_q + kURows - 1) / kURows * kURows;
+    const long long nsplit = ((long long)seq_k + kUKeys - 1) / kUKeys;
+    if (nsplit * rows_pad > 0x7fffffffLL) return KVX_EUNSUPPORTED;
+    const size_t pb = (size_t)nsplit * rows_pad * 512, mb = (size_t)nsplit * rows_pad * 8;
+    uint8_t *w = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void **>(&w), pb + mb, st) != cudaSuccess) {
+        cudaGetLastError();
+        return KVX_ENOSPC;
+    }
+    float *po = reinterpret_cast<float *>(w);
+    float2 *pml = reinterpret_cast<float2 *>(w + pb);
+    UmmaMaps maps;
+    int rc = KVX_OK;
+    if (!(make_map_f32(&maps.q, Q, seq_q, kURows) && make_map_f32(&maps.k, K, seq_k, kUKeys) &&
+          make_map_f32(&maps.v, V, seq_k, kUKeys) && make_map_f32(&maps.part_o, po, nsplit * rows_pad, kURows)))
+        rc = KVX_ECUDA;
+    if (rc == KVX_OK) {
+        attention_umma_kernel<<<dim3((unsigned)(rows_pad / kURows), (unsigned)nsplit), 256, kUSmem, st>>>(
+            pml, (int)rows_pad, seq_k, s * 1.4426950408889634f, maps);
+        rc = launch_status();
+    }
+    if (rc == KVX_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((seq_q * 32LL + 255) / 256));
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, combine_splits_kernel, (const float *)po, (const float2 *)pml, out, seq_q,
+                               (int)rows_pad, (int)nsplit) != cudaSuccess) {
+            cudaGetLastError();
+            rc = KVX_ECUDA;
+        }
+    }
+    if (cudaFreeAsync(w, st) != cudaSuccess && rc == KVX_OK) rc = KVX_ECUDA;
+    return rc;
 }
 
 }  // namespace
@@ -545,15 +660,7 @@ extern "C" KVX_API int kvx_attention_dense(const float *Q, const float *K, const
     const bool aligned = !((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15);
     if (dim == kDD && aligned && !((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(out)) & 15) &&
         seq_q <= (int64_t)0x3fffffff) {
-        static std::atomic<bool> attr_done[kMaxDevices];
-        CUtensorMap tmk, tmv;
-        if (make_rows_map(&tmk, K, seq_k) && make_rows_map(&tmv, V, seq_k)) {
-            const unsigned tiles = (unsigned)((seq_q + kTcRows - 1) / kTcRows);
-            if (ensure_smem_attr(attr_done, attention_tc128_kernel, kTcSmem) != KVX_OK) return KVX_ECUDA;
-            attention_tc128_kernel<<<2 * tiles, kTcThreadsD, kTcSmem, static_cast<cudaStream_t>(stream)>>>(
-                Q, out, (int)seq_q, (int)seq_k, s * 1.4426950408889634f, tmk, tmv);
-            return launch_status();
-        }
+        return attention_umma(Q, K, V, out, (int)seq_q, (int)seq_k, s, static_cast<cudaStream_t>(stream));
     }
     if (dim == kDD && aligned) {
         attention_dense128_kernel<<<(unsigned)((seq_q + kDQ - 1) / kDQ), 256, 0, static_cast<cudaStream_t>(stream)>>>(
