@@ -6,6 +6,8 @@
 // One thread per 16-byte vector of a (sequence, K|V, head) row: consecutive
 // threads write consecutive bytes of a row (coalesced), rows land wherever
 // the block table points.  Pure copy, bit-exact.
+#include <algorithm>
+
 #include "kvx_common.cuh"
 
 namespace kvx {
@@ -45,65 +47,95 @@ append_kernel(uint8_t *pool, const uint8_t *new_k, const uint8_t *new_v,
     }
 }
 
-// Chunked append: each sequence appends n_new consecutive tokens.  A warp
-// owns one run (sequence, page slice, K|V, head): the chunk's tokens that
-// fall into one physical page, at most 16 rows that are contiguous in the
-// page (one 4 KiB block at fp16) and head-strided in the source.  Lanes
-// cover a row in 16-byte vectors (two rows per instruction at fp16); all of
-// a run's loads are issued before its stores, so a warp keeps up to 8 rows
-// in flight.  All index arithmetic is per warp, not per vector.
+// Chunked append: each sequence appends n_new consecutive tokens.  The
+// launch's rows are numbered r = ((s * 2 + kv) * n_new + t) * hkv + h, so
+// consecutive rows are consecutive in the source (new_k / new_v are
+// [s][t][h][row]); the warps of the launch take equal contiguous ranges of
+// them (balanced to one warp instruction, whatever the chunks' page
+// alignment), and a warp instruction moves kRowsPerOp whole rows in 16-byte
+// vectors (two rows at fp16).  A lane walks its rows incrementally (no
+// division per row); the source address needs no table lookup, so a
+// batch's source loads (up to 8 per lane) are all in flight before its
+// stores, which go to slot pos % 16 of page block_table[s][pos / 16].
 template <int kRowVecs>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 append_chunk_kernel(uint8_t *pool, const uint8_t *new_k, const uint8_t *new_v,
                     const int32_t *block_table, const int32_t *positions, int32_t *error_flag,
-                    int batch, int n_new, int hkv, int max_pages, int num_pages, int slices) {
+                    int n_new, int hkv, int max_pages, int num_pages, uint32_t rows_total, uint32_t units_per_warp) {
     constexpr int kRowBytes = kRowVecs * 16;
-    constexpr int kRowsPerOp = 32 / kRowVecs;          // rows one warp instruction covers
-    constexpr int kOps = (kPageTokens + kRowsPerOp - 1) / kRowsPerOp;
+    constexpr int kRowsPerOp = 32 / kRowVecs;  // rows one warp instruction covers
+    constexpr int kBatch = 8;                  // loads in flight per lane
     // Dependent launch: the next launch on the stream may be scheduled now,
     // and this grid touches memory only once the previous one has finished
     // (it may have written the rows or the pool), so back-to-back appends
     // keep their order and lose only the launch gap.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int lane = threadIdx.x & 31;
-    const long long run = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const long long runs = (long long)batch * slices * 2 * hkv;
-    if (run >= runs) return;
-    const int h = (int)(run % hkv);
-    const int kv = (int)((run / hkv) % 2);
-    const int j = (int)((run / (2 * hkv)) % slices);
-    const int s = (int)(run / (2LL * hkv * slices));
-    const int start = positions[s];
-    if (start < 0) {
-        if (error_flag && lane == 0 && j == 0 && kv == 0 && h == 0) atomicOr(error_flag, 2);
-        return;
-    }
-    const int lp = start / kPageTokens + j;
-    const int t0 = max(start, lp * kPageTokens), t1 = min(start + n_new, (lp + 1) * kPageTokens);
-    if (t0 >= t1) return;  // the chunk ends before this slice
-    const int phys = lp < max_pages ? block_table[(size_t)s * max_pages + lp] : -1;
-    if (phys < 0 || phys >= num_pages) {
-        if (error_flag && lane == 0 && kv == 0 && h == 0) atomicOr(error_flag, 2);
-        return;
-    }
-    const int r_lane = lane / kRowVecs, v = lane % kRowVecs;
-    const uint8_t *src = (kv ? new_v : new_k) +
-                         (((size_t)s * n_new + (t0 - start)) * hkv + h) * kRowBytes + v * 16;
-    uint8_t *dst = pool + ((((size_t)phys * 2 + kv) * hkv + h) * kPageTokens + (t0 - lp * kPageTokens)) * kRowBytes +
-                   v * 16;
-    const int rows = t1 - t0;
-    uint4 val[kOps];
+    const int lane = threadIdx.x & 31, r_lane = lane / kRowVecs, v = lane % kRowVecs;
+    const uint32_t warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint64_t u0 = (uint64_t)warp * units_per_warp;
+    const uint64_t units = ((uint64_t)rows_total + kRowsPerOp - 1) / kRowsPerOp;
+    if (u0 >= units) return;
+    const uint32_t n_units = (uint32_t)(units - u0 < units_per_warp ? units - u0 : units_per_warp);
+    // this lane's first row, decomposed once
+    uint32_t r = (uint32_t)(u0 * kRowsPerOp) + r_lane;
+    uint32_t h = r % hkv, q = r / hkv;
+    uint32_t t = q % n_new, q2 = q / n_new;
+    uint32_t kv = q2 & 1, sq = q2 >> 1;
+    for (uint32_t b0 = 0; b0 < n_units; b0 += kBatch) {
+        uint4 val[kBatch];
+        uint8_t *dst[kBatch];
 #pragma unroll
-    for (int o = 0; o < kOps; ++o) {
-        const int r = o * kRowsPerOp + r_lane;
-        if (r < rows) val[o] = __ldcs(reinterpret_cast<const uint4 *>(src + (size_t)r * hkv * kRowBytes));
-    }
+        for (int o = 0; o < kBatch; ++o) {
+            dst[o] = nullptr;
+            if (b0 + o < n_units && r < rows_total) {
+                const uint8_t *src = (kv ? new_v : new_k) + (((size_t)sq * n_new + t) * hkv + h) * kRowBytes + v * 16;
+                val[o] = __ldcs(reinterpret_cast<const uint4 *>(src));
+                const int start = positions[sq];
+                const long long pos = (long long)start + t;
+                const long long lp = pos >> 4;
+                const int phys = start >= 0 && lp < max_pages ? block_table[(size_t)sq * max_pages + lp] : -1;
+                if (phys >= 0 && phys < num_pages)
+                    dst[o] = pool + ((((size_t)phys * 2 + kv) * hkv + h) * kPageTokens + (pos & 15)) * kRowBytes + v * 16;
+                else if (error_flag && v == 0)
+                    atomicOr(error_flag, 2);
+            }
+            // next row of this lane: kRowsPerOp further
+            r += kRowsPerOp;
+            h += kRowsPerOp;
+            while (h >= (uint32_t)hkv) {
+                h -= hkv;
+                if (++t == (uint32_t)n_new) {
+                    t = 0;
+                    if (++kv == 2) kv = 0, ++sq;
+                }
+            }
+        }
 #pragma unroll
-    for (int o = 0; o < kOps; ++o) {
-        const int r = o * kRowsPerOp + r_lane;
-        if (r < rows) *reinterpret_cast<uint4 *>(dst + (size_t)r * kRowBytes) = val[o];
+        for (int o = 0; o < kBatch; ++o)
+            if (dst[o]) *reinterpret_cast<uint4 *>(dst[o]) = val[o];
     }
+}
+
+// Resident append_chunk_kernel blocks per SM of the current device, looked
+// up once per device.
+int append_resident_blocks(bool f16) {
+    static std::atomic<int> cache[2][kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    int n = cached ? cache[f16][dev].load(std::memory_order_relaxed) : 0;
+    if (n <= 0) {
+        const cudaError_t e =
+            f16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, append_chunk_kernel<16>, 256, 0)
+                : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, append_chunk_kernel<32>, 256, 0);
+        if (e != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 4;
+        }
+        if (cached) cache[f16][dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
 }
 
 }  // namespace
@@ -124,11 +156,16 @@ extern "C" KVX_API int kvx_append_chunk(const kvx_paged *kv, const int32_t *bloc
          reinterpret_cast<uintptr_t>(new_v)) & 15)
         return KVX_EINVAL;
     if (batch == 0 || n_new == 0) return KVX_OK;
-    // page slices a chunk can touch: it may start anywhere inside a page
-    const int slices = (n_new + kPageTokens - 1) / kPageTokens + 1;
-    const long long runs = (long long)batch * slices * 2 * kv->num_kv_heads;
-    const long long blocks = (runs + 7) / 8;
-    if (blocks > 0x7fffffffLL) return KVX_EINVAL;
+    const uint64_t rows_total = (uint64_t)batch * 2 * n_new * kv->num_kv_heads;
+    if (rows_total > 0x7fffffffULL) return KVX_EUNSUPPORTED;
+    // warps: enough to fill every SM (resident blocks x SMs), at least one
+    // warp instruction of rows each; then an equal share of the rows each
+    const int rows_per_op = kv->dtype == KVX_F16 ? 2 : 1;
+    const uint64_t units = (rows_total + rows_per_op - 1) / rows_per_op;
+    const uint64_t warp_cap = (uint64_t)append_resident_blocks(kv->dtype == KVX_F16) * sm_count() * 8;
+    const uint64_t warps = std::min<uint64_t>(units, warp_cap);
+    const uint32_t per = (uint32_t)((units + warps - 1) / warps);
+    const uint64_t blocks = ((units + per - 1) / per + 7) / 8;
     auto *pool = static_cast<uint8_t *>(kv->pool);
     auto *k = static_cast<const uint8_t *>(new_k), *v = static_cast<const uint8_t *>(new_v);
     cudaLaunchConfig_t cfg{};
@@ -142,10 +179,10 @@ extern "C" KVX_API int kvx_append_chunk(const kvx_paged *kv, const int32_t *bloc
     cfg.numAttrs = 1;
     const cudaError_t e =
         kv->dtype == KVX_F16
-            ? cudaLaunchKernelEx(&cfg, append_chunk_kernel<16>, pool, k, v, block_table, positions, error_flag, batch,
-                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages, slices)
-            : cudaLaunchKernelEx(&cfg, append_chunk_kernel<32>, pool, k, v, block_table, positions, error_flag, batch,
-                                 n_new, kv->num_kv_heads, max_pages, kv->num_pages, slices);
+            ? cudaLaunchKernelEx(&cfg, append_chunk_kernel<16>, pool, k, v, block_table, positions, error_flag, n_new,
+                                 kv->num_kv_heads, max_pages, kv->num_pages, (uint32_t)rows_total, per)
+            : cudaLaunchKernelEx(&cfg, append_chunk_kernel<32>, pool, k, v, block_table, positions, error_flag, n_new,
+                                 kv->num_kv_heads, max_pages, kv->num_pages, (uint32_t)rows_total, per);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return KVX_ECUDA;

@@ -47,6 +47,20 @@ inline int ensure_smem_attr(std::atomic<bool> (&done)[kMaxDevices], Kernel kern,
     return KVX_OK;
 }
 
+// SM count of the current device, looked up once per device.
+inline int sm_count() {
+    static std::atomic<int> cache[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    int n = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        if (cached) cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -528,20 +528,6 @@ paged_decode_kernel(const DecodeParams p) {
 
 constexpr int kMinChunk = 4;
 
-// SM count of the current device, looked up once per device.
-int sm_count() {
-    static std::atomic<int> cache[kMaxDevices];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const bool cached = dev >= 0 && dev < kMaxDevices;
-    int n = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
-    if (n <= 0) {
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        if (cached) cache[dev].store(n, std::memory_order_relaxed);
-    }
-    return n;
-}
-
 int choose_chunk(int batch, int hkv, int nhg, int max_pages) {
     if (const char *e = getenv("KVX_DECODE_CHUNK")) {
         int c = atoi(e);
