@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 // as big = x itself, of which the tensor core reads the top 19 bits (x with
 // the low 13 mantissa bits cleared), and small = x - that truncation
 // (exact); a.b ~ big.big + big.small + small.big.  A CTA owns 128 query
-// rows (the MMA's M, one tensor-memory lane per row) and one tile of 64
-// keys:
+// rows (the MMA's M, one tensor-memory lane per row) and a range of 64-key
+// tiles; per tile:
 //  * TMA brings the raw fp32 Q (4 boxes of 128 rows x 32 floats), K and V
 //    (4 boxes of 64 keys x 32 floats each), 128-byte swizzle: the K-major
 //    canonical layout of the MMA's shared-memory descriptors.  Rows past
@@ -230,10 +230,12 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 //    layout that kind::tf32 MMA wrote zeros on B200 whatever its leading /
 //    stride offsets.)
 //  * O = P V: 8 k-steps x 3 MMAs (M 128, N 128, K 8) into columns 64-191;
-//    each warpgroup loads 64 columns of its row of O into a swizzled
-//    staging tile (over V), which leaves as 4 TMA tensor stores; the first
-//    warpgroup writes (max, sum): the key tile's partial.
-// combine_splits_kernel folds the key tiles' partials of every row.
+//    each warpgroup loads 64 columns of its rows of O and folds them into
+//    registers (running max and sum of the row over the CTA's tiles).
+// At the end the registers go through a swizzled staging tile (over V) and
+// leave as 4 TMA tensor stores: the output rows when the CTA has all the
+// keys, else the CTA's partial with (max, sum) per row beside it.
+// combine_splits_kernel folds the splits' partials of every row.
 constexpr int kURows = 128, kUKeys = 64;
 constexpr int kUQBox = kURows * 128, kUKBox = kUKeys * 128;  // bytes of one Q / K (V) box
 constexpr int kUVtBox = 128 * 128;                             // 128 dims x 32 keys of the transposed V
@@ -311,7 +313,7 @@ __device__ __forceinline__ void umma_tma_store(const CUtensorMap *tm, int x, int
 }
 
 __global__ void __launch_bounds__(256, 1)
-attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
+attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int tiles_per_split,
                       float scale_log2, const __grid_constant__ UmmaMaps maps) {
     extern __shared__ __align__(16) uint8_t usm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(usm_raw) + 1023) & ~uintptr_t(1023));
@@ -325,21 +327,27 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
     float *red = reinterpret_cast<float *>(sm + 128 * 1024);  // over K, once S is done: max, sum per group
     const int warp = threadIdx.x >> 5, wg = threadIdx.x >> 7, row = threadIdx.x & 127;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's tensor-memory lanes
-    const int row0 = blockIdx.x * kURows, key0 = blockIdx.y * kUKeys;
+    const int row0 = blockIdx.x * kURows;
+    const int tiles = (seq_k + kUKeys - 1) / kUKeys;
+    const int t_begin = blockIdx.y * tiles_per_split, t_end = min(tiles, t_begin + tiles_per_split);
     // the combine (a dependent launch) may start its CTAs now; it waits for
     // this grid's completion before reading a partial
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
-        fence_barrier_init();
+    // raw Q, K (bars[0]) and V (bars[1]) of key tile t
+    auto load_tile = [&](int t) {
         mbar_arrive_expect_tx(&bars[0], 4 * kUQBox + 4 * kUKBox);
         mbar_arrive_expect_tx(&bars[1], 4 * kUKBox);
         for (int x = 0; x < 4; ++x) {
             umma_tma(q_big + x * kUQBox, &maps.q, 32 * x, row0, &bars[0]);
-            umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, key0, &bars[0]);
+            umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, t * kUKeys, &bars[0]);
         }
-        for (int x = 0; x < 4; ++x) umma_tma(v_raw + x * kUKBox, &maps.v, 32 * x, key0, &bars[1]);
+        for (int x = 0; x < 4; ++x) umma_tma(v_raw + x * kUKBox, &maps.v, 32 * x, t * kUKeys, &bars[1]);
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+        if (t_begin < t_end) load_tile(t_begin);  // in flight during the tensor-memory allocation
     }
     if (warp == 0) {  // 256 tensor-memory columns: S at 0-63, O at 64-191
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot))
@@ -351,8 +359,6 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
     tc_fence_after();
     const uint32_t tmem = *tmem_slot, t_s = tmem, t_o = tmem + 64;
 
-    // Q small and K small at the raw copies' offsets in their own regions
-    (void)mbar_wait_bounded(&bars[0], 0, nullptr);
     auto split16 = [](uint32_t raw, uint32_t dst_small) {
         float4 v;
         asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -362,136 +368,168 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
                      "f"(v.y - tf32_trunc(v.y)), "f"(v.z - tf32_trunc(v.z)), "f"(v.w - tf32_trunc(v.w))
                      : "memory");
     };
-#pragma unroll 4
-    for (int i = threadIdx.x; i < 4 * kUQBox / 16; i += 256) split16(q_big + 16 * i, q_small + 16 * i);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < 4 * kUKBox / 16; i += 256) split16(k_big + 16 * i, k_small + 16 * i);
-    fence_proxy_async_smem();  // the split's generic stores before the tensor core's reads
-    tc_fence_before();
-    __syncthreads();
 
-    if (threadIdx.x == 0) {
-        tc_fence_after();
-        // S = Q K^T: k-step k reads 8 dims = 32 bytes of box k / 4
-        constexpr uint32_t idesc = umma_idesc(kUKeys, false);
-        for (int k = 0; k < 16; ++k) {
-            const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, bo = (k >> 2) * kUKBox + (k & 3) * 32;
-            const uint64_t ab = umma_desc(q_big + ao, 16, 1024), as = umma_desc(q_small + ao, 16, 1024);
-            const uint64_t bb = umma_desc(k_big + bo, 16, 1024), bs = umma_desc(k_small + bo, 16, 1024);
-            umma_tf32(t_s, ab, bb, idesc, k > 0);
-            umma_tf32(t_s, ab, bs, idesc, 1);
-            umma_tf32(t_s, as, bb, idesc, 1);
+    // this thread's 64 columns (64 wg ..) of its row of the split's O, with
+    // the running max and sum over the split's key tiles
+    float acc[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    float M = -CUDART_INF_F, L = 0.f;
+
+    for (int t = t_begin, it = 0; t < t_end; ++t, ++it) {
+        const int key0 = t * kUKeys;
+        const uint32_t ph = it & 1;  // bars[0], bars[1]: one phase per tile; bars[2]: two (S, then O)
+
+        // Q small and K small at the raw copies' offsets in their own regions
+        (void)mbar_wait_bounded(&bars[0], ph, nullptr);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < 4 * kUQBox / 16; i += 256) split16(q_big + 16 * i, q_small + 16 * i);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < 4 * kUKBox / 16; i += 256) split16(k_big + 16 * i, k_small + 16 * i);
+        fence_proxy_async_smem();  // the split's generic stores before the tensor core's reads
+        tc_fence_before();
+        __syncthreads();
+
+        if (threadIdx.x == 0) {
+            tc_fence_after();
+            // S = Q K^T: k-step k reads 8 dims = 32 bytes of box k / 4
+            constexpr uint32_t idesc = umma_idesc(kUKeys, false);
+            for (int k = 0; k < 16; ++k) {
+                const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, bo = (k >> 2) * kUKBox + (k & 3) * 32;
+                const uint64_t ab = umma_desc(q_big + ao, 16, 1024), as = umma_desc(q_small + ao, 16, 1024);
+                const uint64_t bb = umma_desc(k_big + bo, 16, 1024), bs = umma_desc(k_small + bo, 16, 1024);
+                umma_tf32(t_s, ab, bb, idesc, k > 0);
+                umma_tf32(t_s, ab, bs, idesc, 1);
+                umma_tf32(t_s, as, bb, idesc, 1);
+            }
+            umma_commit(&bars[2]);
         }
-        umma_commit(&bars[2]);
-    }
-    (void)mbar_wait_bounded(&bars[2], 0, nullptr);  // S complete, Q and K free
-    __syncwarp();  // warp 0's thread 0 issued the MMAs: reconverge before the aligned loads
-    tc_fence_after();
+        (void)mbar_wait_bounded(&bars[2], 0, nullptr);  // S complete, Q and K free
+        __syncwarp();  // warp 0's thread 0 issued the MMAs: reconverge before the aligned loads
+        tc_fence_after();
 
-    // V^T big / small, this thread's dim d = row, keys 32 wg .. 32 wg + 31:
-    // key j of raw V sits in box d / 32, row j, 16-byte chunk
-    // ((d % 32) / 4) ^ (j % 8); the transposed element (d, j) in box j / 32,
-    // row d, chunk ((j % 32) / 4) ^ (d % 8).
-    (void)mbar_wait_bounded(&bars[1], 0, nullptr);
-    {
-        const int d = row;
-        const uint32_t src = v_raw + (d >> 5) * kUKBox + (d & 3) * 4;
+        // V^T big / small, this thread's dim d = row, keys 32 wg .. 32 wg + 31:
+        // key j of raw V sits in box d / 32, row j, 16-byte chunk
+        // ((d % 32) / 4) ^ (j % 8); the transposed element (d, j) in box j / 32,
+        // row d, chunk ((j % 32) / 4) ^ (d % 8).
+        (void)mbar_wait_bounded(&bars[1], ph, nullptr);
+        {
+            const int d = row;
+            const uint32_t src = v_raw + (d >> 5) * kUKBox + (d & 3) * 4;
 #pragma unroll 4
-        for (int c = 8 * wg; c < 8 * wg + 8; ++c) {  // keys 4c .. 4c+3
-            float x[4], b[4];
+            for (int c = 8 * wg; c < 8 * wg + 8; ++c) {  // keys 4c .. 4c+3
+                float x[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * c + e;
+                    asm volatile("ld.shared.f32 %0, [%1];"
+                                 : "=f"(x[e])
+                                 : "r"(src + j * 128 + ((((d & 31) >> 2) ^ (j & 7)) << 4)));
+                }
+                const uint32_t off = (c >> 3) * kUVtBox + d * 128 + (((c & 7) ^ (d & 7)) << 4);
+                asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_big + off), "f"(x[0]), "f"(x[1]),
+                             "f"(x[2]), "f"(x[3])
+                             : "memory");
+                asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_small + off),
+                             "f"(x[0] - tf32_trunc(x[0])), "f"(x[1] - tf32_trunc(x[1])), "f"(x[2] - tf32_trunc(x[2])),
+                             "f"(x[3] - tf32_trunc(x[3]))
+                             : "memory");
+            }
+        }
+        // this warpgroup's 32 keys of the thread's row of S
+        uint32_t r[32];
+        tm_ld32(t_s + 32 * wg + lane_base, r);
+        tm_wait_ld();
+        const int nk = min(kUKeys, seq_k - key0) - 32 * wg;
+        float m = -CUDART_INF_F;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float s = j < nk ? __uint_as_float(r[j]) * scale_log2 : -CUDART_INF_F;
+            r[j] = __float_as_uint(s);
+            m = fmaxf(m, s);
+        }
+        red[wg * 128 + row] = m;
+        __syncthreads();
+        m = fmaxf(red[row], red[128 + row]);  // finite: key key0 is valid
+        float l = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {  // keys 32 wg + 4cc .. +3: box wg, 16-byte chunk cc
+            float p4[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int j = 4 * c + e;
-                asm volatile("ld.shared.f32 %0, [%1];"
-                             : "=f"(x[e])
-                             : "r"(src + j * 128 + ((((d & 31) >> 2) ^ (j & 7)) << 4)));
-                b[e] = tf32_trunc(x[e]);
+                p4[e] = ex2_approx(__uint_as_float(r[4 * cc + e]) - m);  // masked keys: -inf - m
+                l += p4[e];
             }
-            const uint32_t off = (c >> 3) * kUVtBox + d * 128 + (((c & 7) ^ (d & 7)) << 4);
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_big + off), "f"(x[0]), "f"(x[1]),
-                         "f"(x[2]), "f"(x[3])
+            const uint32_t off = wg * kUQBox + row * 128 + (((cc ^ (row & 7))) << 4);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_big + off), "f"(p4[0]), "f"(p4[1]),
+                         "f"(p4[2]), "f"(p4[3])
                          : "memory");
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(v_small + off), "f"(x[0] - b[0]),
-                         "f"(x[1] - b[1]), "f"(x[2] - b[2]), "f"(x[3] - b[3])
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_small + off),
+                         "f"(p4[0] - tf32_trunc(p4[0])), "f"(p4[1] - tf32_trunc(p4[1])),
+                         "f"(p4[2] - tf32_trunc(p4[2])), "f"(p4[3] - tf32_trunc(p4[3]))
                          : "memory");
         }
-    }
-    // this warpgroup's 32 keys of the thread's row of S
-    uint32_t r[32];
-    tm_ld32(t_s + 32 * wg + lane_base, r);
-    tm_wait_ld();
-    const int nk = min(kUKeys, seq_k - key0) - 32 * wg;
-    float m = -CUDART_INF_F;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const float s = j < nk ? __uint_as_float(r[j]) * scale_log2 : -CUDART_INF_F;
-        r[j] = __float_as_uint(s);
-        m = fmaxf(m, s);
-    }
-    red[wg * 128 + row] = m;
-    __syncthreads();
-    m = fmaxf(red[row], red[128 + row]);  // finite: key key0 is valid
-    float l = 0.f;
-#pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {  // keys 32 wg + 4cc .. +3: box wg, 16-byte chunk cc
-        float p4[4], b4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float s = __uint_as_float(r[4 * cc + e]);
-            p4[e] = ex2_approx(s - m);  // masked keys: s - m = -inf
-            l += p4[e];
-            b4[e] = tf32_trunc(p4[e]);
+        red[256 + wg * 128 + row] = l;
+        fence_proxy_async_smem();  // P's generic stores before the tensor core's reads
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            tc_fence_after();
+            // O = P V: k-step k reads 8 keys (32 bytes of box k / 4) of P and of
+            // the transposed V
+            constexpr uint32_t idesc = umma_idesc(128, false);
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, vo = (k >> 2) * kUVtBox + (k & 3) * 32;
+                const uint64_t ab = umma_desc(p_big + ao, 16, 1024), as = umma_desc(p_small + ao, 16, 1024);
+                const uint64_t bb = umma_desc(v_big + vo, 16, 1024), bs = umma_desc(v_small + vo, 16, 1024);
+                umma_tf32(t_o, ab, bb, idesc, k > 0);
+                umma_tf32(t_o, ab, bs, idesc, 1);
+                umma_tf32(t_o, as, bb, idesc, 1);
+            }
+            umma_commit(&bars[2]);
         }
-        const uint32_t off = wg * kUQBox + row * 128 + (((cc ^ (row & 7))) << 4);
-        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_big + off), "f"(p4[0]), "f"(p4[1]),
-                     "f"(p4[2]), "f"(p4[3])
-                     : "memory");
-        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(p_small + off), "f"(p4[0] - b4[0]),
-                     "f"(p4[1] - b4[1]), "f"(p4[2] - b4[2]), "f"(p4[3] - b4[3])
-                     : "memory");
-    }
-    red[256 + wg * 128 + row] = l;
-    fence_proxy_async_smem();  // P's generic stores before the tensor core's reads
-    tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x == 0) {
+        (void)mbar_wait_bounded(&bars[2], 1, nullptr);
+        __syncwarp();
         tc_fence_after();
-        // O = P V: k-step k reads 8 keys (32 bytes of box k / 4) of P and of
-        // the transposed V
-        constexpr uint32_t idesc = umma_idesc(128, false);
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, vo = (k >> 2) * kUVtBox + (k & 3) * 32;
-            const uint64_t ab = umma_desc(p_big + ao, 16, 1024), as = umma_desc(p_small + ao, 16, 1024);
-            const uint64_t bb = umma_desc(v_big + vo, 16, 1024), bs = umma_desc(v_small + vo, 16, 1024);
-            umma_tf32(t_o, ab, bb, idesc, k > 0);
-            umma_tf32(t_o, ab, bs, idesc, 1);
-            umma_tf32(t_o, as, bb, idesc, 1);
-        }
-        umma_commit(&bars[2]);
-    }
-    (void)mbar_wait_bounded(&bars[2], 1, nullptr);
-    __syncwarp();
-    tc_fence_after();
-    // this warpgroup's 64 columns of the row into staging boxes 2 wg, 2 wg + 1
-    // (32 columns x 128 rows each, 128-byte swizzle) over V
-    {
-        uint32_t o[64];
-        tm_ld64(t_o + 64 * wg + lane_base, o);
-        tm_wait_ld();
+        // fold the tile into the running (M, L, acc) of the thread's row
+        {
+            const float mn = fmaxf(M, m);
+            const float a = ex2_approx(M - mn), w = ex2_approx(m - mn);  // M = -inf on the first tile: a = 0
+            L = L * a + (red[256 + row] + red[384 + row]) * w;
+            M = mn;
+            uint32_t o[64];
+            tm_ld64(t_o + 64 * wg + lane_base, o);
+            tm_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const uint32_t off = (2 * wg + (c >> 3)) * kUVtBox + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + off), "r"(o[4 * c]),
-                         "r"(o[4 * c + 1]), "r"(o[4 * c + 2]), "r"(o[4 * c + 3])
-                         : "memory");
+            for (int j = 0; j < 64; ++j) acc[j] = acc[j] * a + __uint_as_float(o[j]) * w;
         }
+        // every thread's reads of this tile's shared memory (raw V, red) and
+        // tensor memory are done before the next tile's loads and MMAs
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && t + 1 < t_end) load_tile(t + 1);
     }
-    const int prow0 = blockIdx.y * rows_pad + row0;
-    if (wg == 0) part_ml[(size_t)prow0 + row] = make_float2(m, red[256 + row] + red[384 + row]);
+
+    // the split's result into staging boxes 2 wg, 2 wg + 1 (32 columns x 128
+    // rows each, 128-byte swizzle) over V: O itself with (M, L) beside it
+    // when the keys are split over several CTAs, else O / L, the output rows
+    const bool direct = gridDim.y == 1;
+    const float inv = direct ? 1.f / L : 1.f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const uint32_t off = (2 * wg + (c >> 3)) * kUVtBox + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(base + off), "f"(acc[4 * c] * inv),
+                     "f"(acc[4 * c + 1] * inv), "f"(acc[4 * c + 2] * inv), "f"(acc[4 * c + 3] * inv)
+                     : "memory");
+    }
+    const int prow0 = direct ? row0 : blockIdx.y * rows_pad + row0;
+    if (!direct && wg == 0) part_ml[(size_t)prow0 + row] = make_float2(M, L);
     fence_proxy_async_smem();  // the staging stores before the bulk copy's reads
     tc_fence_before();
     __syncthreads();
     if (threadIdx.x == 0) {
+        // rows past the output's end (direct) are not written by the copy
         for (int x = 0; x < 4; ++x) umma_tma_store(&maps.part_o, 32 * x, prow0, base + x * kUVtBox);
         bulk_commit();
         bulk_wait_read_all();  // the staging tile stays until the copy has read it
@@ -502,9 +540,9 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k,
 }
 
 // out[row] = sum_t exp2(m_t - M) O_t / sum_t exp2(m_t - M) L_t over the key
-// tiles t; one warp per row, a float4 of dims per lane.  Tiles go in
+// splits t; one warp per row, a float4 of dims per lane.  Splits go in
 // batches of 16 with a running max: a batch's (max, sum) pairs (lane j holds
-// tile j's) and its 16 partial rows are all loaded before any is used, so a
+// split j's) and its 16 partial rows are all loaded before any is used, so a
 // batch costs one memory round trip.  Launched as a programmatic dependent
 // of the attention grid: it waits for that grid's completion first.
 __global__ void combine_splits_kernel(const float *__restrict__ part_o, const float2 *__restrict__ part_ml,
@@ -579,13 +617,37 @@ bool make_map_f32(CUtensorMap *tm, const float *base, long long rows, int box_ro
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// The tcgen05 path: the key tiles' partials in stream-ordered scratch (the
-// device's default pool, which keeps its memory between calls), their
-// combine, the scratch released in stream order.
+// The tcgen05 path.  Key tiles split over CTAs only as far as the row tiles
+// leave SMs idle (one CTA per SM: floor(SMs / row tiles) splits, at most one
+// per tile); each CTA folds its tiles in registers.  One split: the CTAs
+// write the output rows themselves.  Several: their partials go to
+// stream-ordered scratch (the device's default pool, which keeps its memory
+// between calls; at most about SMs x 128 rows of partials, whatever the
+// sequence lengths), the combine folds them, the scratch is released in
+// stream order.
 int attention_umma(const float *Q, const float *K, const float *V, float *out, int seq_q, int seq_k, float s,
                    cudaStream_t st) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVX_ECUDA;
+    static std::atomic<bool> attr_done[kMaxDevices];
+    if (ensure_smem_attr(attr_done, attention_umma_kernel, kUSmem) != KVX_OK) return KVX_ECUDA;
+    const long long row_tiles = ((long long)seq_q + kURows - 1) / kURows, rows_pad = row_tiles * kURows;
+    const long long tiles = ((long long)seq_k + kUKeys - 1) / kUKeys;
+    if (row_tiles > 0x7fffffffLL) return KVX_EUNSUPPORTED;
+    long long nsplit = std::min<long long>(tiles, std::max<long long>(1, sm_count() / row_tiles));
+    const long long per = (tiles + nsplit - 1) / nsplit;
+    nsplit = (tiles + per - 1) / per;
+    const float scale_log2 = s * 1.4426950408889634f;
+    UmmaMaps maps;
+    if (!(make_map_f32(&maps.q, Q, seq_q, kURows) && make_map_f32(&maps.k, K, seq_k, kUKeys) &&
+          make_map_f32(&maps.v, V, seq_k, kUKeys)))
+        return KVX_ECUDA;
+    const dim3 grid((unsigned)row_tiles, (unsigned)nsplit);
+    if (nsplit == 1) {
+        if (!make_map_f32(&maps.part_o, out, seq_q, kURows)) return KVX_ECUDA;
+        attention_umma_kernel<<<grid, 256, kUSmem, st>>>(nullptr, (int)rows_pad, seq_k, (int)per, scale_log2, maps);
+        return launch_status();
+    }
     static std::atomic<bool> pool_set[kMaxDevices];
     if (!pool_set[dev].load(std::memory_order_acquire)) {
         cudaMemPool_t pool;
@@ -594,11 +656,6 @@ int attention_umma(const float *Q, const float *K, const float *V, float *out, i
             cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
         pool_set[dev].store(true, std::memory_order_release);
     }
-    static std::atomic<bool> attr_done[kMaxDevices];
-    if (ensure_smem_attr(attr_done, attention_umma_kernel, kUSmem) != KVX_OK) return KVX_ECUDA;
-    const long long rows_pad = ((long long)seq_q + kURows - 1) / kURows * kURows;
-    const long long nsplit = ((long long)seq_k + kUKeys - 1) / kUKeys;
-    if (nsplit * rows_pad > 0x7fffffffLL) return KVX_EUNSUPPORTED;
     const size_t pb = (size_t)nsplit * rows_pad * 512, mb = (size_t)nsplit * rows_pad * 8;
     uint8_t *w = nullptr;
     if (cudaMallocAsync(reinterpret_cast<void **>(&w), pb + mb, st) != cudaSuccess) {
@@ -607,14 +664,9 @@ int attention_umma(const float *Q, const float *K, const float *V, float *out, i
     }
     float *po = reinterpret_cast<float *>(w);
     float2 *pml = reinterpret_cast<float2 *>(w + pb);
-    UmmaMaps maps;
-    int rc = KVX_OK;
-    if (!(make_map_f32(&maps.q, Q, seq_q, kURows) && make_map_f32(&maps.k, K, seq_k, kUKeys) &&
-          make_map_f32(&maps.v, V, seq_k, kUKeys) && make_map_f32(&maps.part_o, po, nsplit * rows_pad, kURows)))
-        rc = KVX_ECUDA;
+    int rc = make_map_f32(&maps.part_o, po, nsplit * rows_pad, kURows) ? KVX_OK : KVX_ECUDA;
     if (rc == KVX_OK) {
-        attention_umma_kernel<<<dim3((unsigned)(rows_pad / kURows), (unsigned)nsplit), 256, kUSmem, st>>>(
-            pml, (int)rows_pad, seq_k, s * 1.4426950408889634f, maps);
+        attention_umma_kernel<<<grid, 256, kUSmem, st>>>(pml, (int)rows_pad, seq_k, (int)per, scale_log2, maps);
         rc = launch_status();
     }
     if (rc == KVX_OK) {
