@@ -617,14 +617,38 @@ bool make_map_f32(CUtensorMap *tm, const float *base, long long rows, int box_ro
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The library's stream-ordered scratch pool on device `dev` (made once, kept
+// for the process): freed blocks stay in the pool (release threshold at its
+// maximum), so a call after the first allocates no device memory.  A pool
+// of its own leaves the device's default pool as the application set it.
+cudaMemPool_t scratch_pool(int dev) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lk(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t p = nullptr;
+        if (cudaMemPoolCreate(&p, &props) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+        pools[dev] = p;
+    }
+    return pools[dev];
+}
+
 // The tcgen05 path.  Key tiles split over CTAs only as far as the row tiles
 // leave SMs idle (one CTA per SM: floor(SMs / row tiles) splits, at most one
 // per tile); each CTA folds its tiles in registers.  One split: the CTAs
 // write the output rows themselves.  Several: their partials go to
-// stream-ordered scratch (the device's default pool, which keeps its memory
-// between calls; at most about SMs x 128 rows of partials, whatever the
-// sequence lengths), the combine folds them, the scratch is released in
-// stream order.
+// stream-ordered scratch (scratch_pool; at most about SMs x 128 rows of
+// partials, whatever the sequence lengths), the combine folds them, the
+// scratch is released in stream order.
 int attention_umma(const float *Q, const float *K, const float *V, float *out, int seq_q, int seq_k, float s,
                    cudaStream_t st) {
     int dev = 0;
@@ -648,17 +672,11 @@ int attention_umma(const float *Q, const float *K, const float *V, float *out, i
         attention_umma_kernel<<<grid, 256, kUSmem, st>>>(nullptr, (int)rows_pad, seq_k, (int)per, scale_log2, maps);
         return launch_status();
     }
-    static std::atomic<bool> pool_set[kMaxDevices];
-    if (!pool_set[dev].load(std::memory_order_acquire)) {
-        cudaMemPool_t pool;
-        uint64_t keep = ~0ull;
-        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess)
-            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-        pool_set[dev].store(true, std::memory_order_release);
-    }
+    cudaMemPool_t pool = scratch_pool(dev);
+    if (!pool) return KVX_ECUDA;
     const size_t pb = (size_t)nsplit * rows_pad * 512, mb = (size_t)nsplit * rows_pad * 8;
     uint8_t *w = nullptr;
-    if (cudaMallocAsync(reinterpret_cast<void **>(&w), pb + mb, st) != cudaSuccess) {
+    if (cudaMallocFromPoolAsync(reinterpret_cast<void **>(&w), pb + mb, pool, st) != cudaSuccess) {
         cudaGetLastError();
         return KVX_ENOSPC;
     }
