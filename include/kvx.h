@@ -244,7 +244,12 @@ KVX_API int kvx_softmax_rows(const float *in, float *out, int64_t rows, int64_t 
  * rows over seq_k keys, fp32 [rows][dim] device arrays, dim <= 1024,
  * scale <= 0 -> 1/sqrt(dim).  Replaces the reference's cuda_attention
  * (runtime/gpu/cuda_executor.cu:246-311) with the semantics of
- * TensorOps::attention (runtime/tensor_ops.cpp:179-219). */
+ * TensorOps::attention (runtime/tensor_ops.cpp:179-219).  dim 128 with all
+ * four arrays 16-byte aligned runs on the tensor cores; when it splits the
+ * keys over CTAs it takes stream-ordered scratch (at most about
+ * 148 x 128 rows x 520 bytes) from a memory pool of the library's own,
+ * which keeps its memory between calls, and returns KVX_ENOSPC if that
+ * allocation fails. */
 KVX_API int kvx_attention_dense(const float *Q, const float *K, const float *V, float *out,
                                 int64_t seq_q, int64_t seq_k, int32_t dim, float scale,
                                 void *stream);
