@@ -574,14 +574,15 @@ def test_attention_dense_and_softmax_match_reference_rows(kvx, oracle):
 
 @pytest.mark.parametrize("seq_q,seq_k,mag", [(1024, 1024, 1.0), (1000, 777, 1.0), (1, 1, 1.0), (17, 65, 1.0),
                                              (300, 2049, 1.0), (64, 500, 1e5), (128, 300, 1e-3),
-                                             (4096, 4096, 1.0), (20000, 300, 1.0), (128, 40000, 1.0)])
+                                             (4096, 4096, 1.0), (20000, 300, 1.0), (128, 40001, 1.0)])
 def test_attention_dense_tensor_core_matches_fp64(kvx, seq_q, seq_k, mag):
     """The head-dim-128 dense attention (tensor cores, 3xTF32 products)
     over ragged query / key counts (partial key tiles, rows past the last
     query), key tiles split over CTAs one each (1024 x 1024), several per
-    CTA (4096 x 4096: 4 splits of 16 tiles; 128 x 40000: 125 splits of 5)
-    or all in one CTA that writes the output itself (20000 x 300: more row
-    tiles than SMs), and magnitudes far outside fp16's range, against
+    CTA (4096 x 4096: 4 splits of 16 tiles; 128 x 40001: 126 splits of 5,
+    the last with one tile of one key) or all in one CTA that writes the
+    output itself (20000 x 300: more row tiles than SMs), and magnitudes
+    far outside fp16's range, against
     softmax(Q K^T / sqrt(128)) V in float64 (TensorOps::attention,
     runtime/tensor_ops.cpp:179-219)."""
     g = torch.Generator(device="cuda")
