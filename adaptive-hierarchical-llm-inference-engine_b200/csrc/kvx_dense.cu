@@ -240,7 +240,7 @@ constexpr int kURows = 128, kUKeys = 64;
 constexpr int kUQBox = kURows * 128, kUKBox = kUKeys * 128;  // bytes of one Q / K (V) box
 constexpr int kUVtBox = 128 * 128;                             // 128 dims x 32 keys of the transposed V
 // Q big, Q small (64 KB each), K big, K small, raw V (32 KB each), barriers
-constexpr int kUSmem = 1024 + 224 * 1024 + 64;
+constexpr int kUSmem = 1024 + 224 * 1024 + 64;  // 4 mbarriers + the tensor-memory address
 static_assert(kUSmem <= 227 * 1024, "tcgen05 attention exceeds the shared memory of a CTA");
 
 struct UmmaMaps {
@@ -322,9 +322,9 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
     const uint32_t v_raw = base + 192 * 1024;
     const uint32_t v_big = base, v_small = base + 32 * 1024;            // over Q big, once S is done
     const uint32_t p_big = base + 64 * 1024, p_small = base + 96 * 1024;  // over Q small
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 224 * 1024);      // qk loads, v load, mma
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
-    float *red = reinterpret_cast<float *>(sm + 128 * 1024);  // over K, once S is done: max, sum per group
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 224 * 1024);      // K load, V load, MMAs, Q load
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4);
+    float *red = reinterpret_cast<float *>(sm + 160 * 1024);  // over K small, once S is done: max, sum per group
     const int warp = threadIdx.x >> 5, wg = threadIdx.x >> 7, row = threadIdx.x & 127;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's tensor-memory lanes
     const int row0 = blockIdx.x * kURows;
@@ -334,20 +334,29 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
     // this grid's completion before reading a partial
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // raw Q, K (bars[0]) and V (bars[1]) of key tile t
-    auto load_tile = [&](int t) {
-        mbar_arrive_expect_tx(&bars[0], 4 * kUQBox + 4 * kUKBox);
+    // raw K (bars[0]) and V (bars[1]) of key tile t, raw Q (bars[3]): each
+    // issued as soon as its region is free (the next tile's K once S is
+    // done, its V once the transposed V and P are written, Q once O is done)
+    auto load_k = [&](int t) {
+        mbar_arrive_expect_tx(&bars[0], 4 * kUKBox);
+        for (int x = 0; x < 4; ++x) umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, t * kUKeys, &bars[0]);
+    };
+    auto load_v = [&](int t) {
         mbar_arrive_expect_tx(&bars[1], 4 * kUKBox);
-        for (int x = 0; x < 4; ++x) {
-            umma_tma(q_big + x * kUQBox, &maps.q, 32 * x, row0, &bars[0]);
-            umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, t * kUKeys, &bars[0]);
-        }
         for (int x = 0; x < 4; ++x) umma_tma(v_raw + x * kUKBox, &maps.v, 32 * x, t * kUKeys, &bars[1]);
     };
+    auto load_q = [&]() {
+        mbar_arrive_expect_tx(&bars[3], 4 * kUQBox);
+        for (int x = 0; x < 4; ++x) umma_tma(q_big + x * kUQBox, &maps.q, 32 * x, row0, &bars[3]);
+    };
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
         fence_barrier_init();
-        if (t_begin < t_end) load_tile(t_begin);  // in flight during the tensor-memory allocation
+        if (t_begin < t_end) {  // in flight during the tensor-memory allocation
+            load_q();
+            load_k(t_begin);
+            load_v(t_begin);
+        }
     }
     if (warp == 0) {  // 256 tensor-memory columns: S at 0-63, O at 64-191
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot))
@@ -378,9 +387,11 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
 
     for (int t = t_begin, it = 0; t < t_end; ++t, ++it) {
         const int key0 = t * kUKeys;
-        const uint32_t ph = it & 1;  // bars[0], bars[1]: one phase per tile; bars[2]: two (S, then O)
+        const uint32_t ph = it & 1;  // bars[0, 1, 3]: one phase per tile; bars[2]: two (S, then O)
+        const bool more = t + 1 < t_end;
 
         // Q small and K small at the raw copies' offsets in their own regions
+        (void)mbar_wait_bounded(&bars[3], ph, nullptr);
         (void)mbar_wait_bounded(&bars[0], ph, nullptr);
 #pragma unroll 4
         for (int i = threadIdx.x; i < 4 * kUQBox / 16; i += 256) split16(q_big + 16 * i, q_small + 16 * i);
@@ -405,6 +416,7 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
             umma_commit(&bars[2]);
         }
         (void)mbar_wait_bounded(&bars[2], 0, nullptr);  // S complete, Q and K free
+        if (threadIdx.x == 0 && more) load_k(t + 1);
         __syncwarp();  // warp 0's thread 0 issued the MMAs: reconverge before the aligned loads
         tc_fence_after();
 
@@ -487,8 +499,10 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
                 umma_tf32(t_o, as, bb, idesc, 1);
             }
             umma_commit(&bars[2]);
+            if (more) load_v(t + 1);  // every thread is past its reads of the raw V
         }
         (void)mbar_wait_bounded(&bars[2], 1, nullptr);
+        if (threadIdx.x == 0 && more) load_q();  // the MMAs are done with Q's space (transposed V, P)
         __syncwarp();
         tc_fence_after();
         // fold the tile into the running (M, L, acc) of the thread's row
@@ -503,12 +517,10 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
 #pragma unroll
             for (int j = 0; j < 64; ++j) acc[j] = acc[j] * a + __uint_as_float(o[j]) * w;
         }
-        // every thread's reads of this tile's shared memory (raw V, red) and
-        // tensor memory are done before the next tile's loads and MMAs
-        fence_proxy_async_smem();
+        // every thread's reads of this tile's red and tensor memory are done
+        // before the next tile's split and MMAs
         tc_fence_before();
         __syncthreads();
-        if (threadIdx.x == 0 && t + 1 < t_end) load_tile(t + 1);
     }
 
     // the split's result into staging boxes 2 wg, 2 wg + 1 (32 columns x 128
