@@ -1691,17 +1691,18 @@ def run_kernel_profiles(args):
          fb * nf, lambda: kvx.migrate_frames(dev, nf, hp, nf, perm_d, perm_h, fb, 0, 16), "host link",
          link["d2h"])
     del host, dev
-    # dense attention (cuda_attention drop-in): 1024 x 1024 x 128 fp32
-    T = 1024
-    qd, kd, vd = (torch.randn((T, DIM), generator=g, device="cuda") for _ in range(3))
-    od = torch.empty_like(qd)
-    ms = _timed_events(lambda: kvx.attention_dense(qd, kd, vd, out=od), iters, warm=1)
-    flops = 4 * T * T * DIM
-    rows.append({"kernels": "attention_dense", "kernel": "attention_umma_kernel + combine_splits_kernel",
-                 "size": "1024 x 1024 x 128 fp32",
-                 "us": round(ms * 1e3, 2), "TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
-                 "note": "3 tcgen05 tf32 MMAs per product (3xTF32): the tensor pipe runs 3x the algorithmic flops"})
-    print(json.dumps(rows[-1]), flush=True)
+    # dense attention (cuda_attention drop-in), fp32: one key tile per CTA
+    # (1024 x 1024) and 16 tiles per CTA (4096 x 4096)
+    for T in (1024, 4096):
+        qd, kd, vd = (torch.randn((T, DIM), generator=g, device="cuda") for _ in range(3))
+        od = torch.empty_like(qd)
+        ms = _timed_events(lambda: kvx.attention_dense(qd, kd, vd, out=od), iters, warm=1)
+        flops = 4 * T * T * DIM
+        rows.append({"kernels": "attention_dense", "kernel": "attention_umma_kernel + combine_splits_kernel",
+                     "size": f"{T} x {T} x 128 fp32",
+                     "us": round(ms * 1e3, 2), "TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
+                     "note": "3 tcgen05 tf32 MMAs per product (3xTF32): the tensor pipe runs 3x the algorithmic flops"})
+        print(json.dumps(rows[-1]), flush=True)
 
 
 def main():
