@@ -218,8 +218,10 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 //    the ends read as zero.  The raw Q and K are the big operands;
 //  * the CTA's 256 threads write Q small and K small at the same swizzled
 //    offsets of their own regions;
-//  * S = Q K^T: 16 k-steps x 3 MMAs (M 128, N 64, K 8) into tensor-memory
-//    columns 0-63;
+//  * S = Q K^T: 16 k-steps x 2 MMAs (M 128, K 8): Q big against K big over
+//    K small (N 128, the two boxes adjacent in shared memory) into
+//    tensor-memory columns 0-127, Q small against K big (N 64) into 0-63;
+//    S = columns 0-63 + columns 64-127;
 //  * once S is complete each thread writes 32 keys of one dim of V, big and
 //    small, into the transposed (128 dims x 64 keys, K-major) V tiles over
 //    Q big; the two warpgroups load 32 columns each of their row of S
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 //    small.  (V as stored is an MN-major B operand; in the 128-byte swizzle
 //    layout that kind::tf32 MMA wrote zeros on B200 whatever its leading /
 //    stride offsets.)
-//  * O = P V: 8 k-steps x 3 MMAs (M 128, N 128, K 8) into columns 64-191;
+//  * O = P V: 8 k-steps x 3 MMAs (M 128, N 128, K 8) into columns 128-255;
 //    each warpgroup loads 64 columns of its rows of O and folds them into
 //    registers (running max and sum of the row over the CTA's tiles).
 // At the end the registers go through a swizzled staging tile (over V) and
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(256) attention_dense128_kernel(const float *__
 constexpr int kURows = 128, kUKeys = 64;
 constexpr int kUQBox = kURows * 128, kUKBox = kUKeys * 128;  // bytes of one Q / K (V) box
 constexpr int kUVtBox = 128 * 128;                             // 128 dims x 32 keys of the transposed V
-// Q big, Q small (64 KB each), K big, K small, raw V (32 KB each), barriers
+// Q big, Q small (64 KB each), K big / small (boxes interleaved) and raw V (32 KB each), barriers
 constexpr int kUSmem = 1024 + 224 * 1024 + 64;  // 4 mbarriers + the tensor-memory address
 static_assert(kUSmem <= 227 * 1024, "tcgen05 attention exceeds the shared memory of a CTA");
 
@@ -318,13 +320,15 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
     extern __shared__ __align__(16) uint8_t usm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(usm_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_addr(sm);
-    const uint32_t q_big = base, q_small = base + 64 * 1024, k_big = base + 128 * 1024, k_small = base + 160 * 1024;
+    // K: box x (32 dims) of K big at k_base + 16 KB x, of K small 8 KB further:
+    // one 128-row B operand of K big over K small per box
+    const uint32_t q_big = base, q_small = base + 64 * 1024, k_base = base + 128 * 1024;
     const uint32_t v_raw = base + 192 * 1024;
     const uint32_t v_big = base, v_small = base + 32 * 1024;            // over Q big, once S is done
     const uint32_t p_big = base + 64 * 1024, p_small = base + 96 * 1024;  // over Q small
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 224 * 1024);      // K load, V load, MMAs, Q load
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4);
-    float *red = reinterpret_cast<float *>(sm + 160 * 1024);  // over K small, once S is done: max, sum per group
+    float *red = reinterpret_cast<float *>(sm + 136 * 1024);  // over K small's box 0, once S is done: max, sum
     const int warp = threadIdx.x >> 5, wg = threadIdx.x >> 7, row = threadIdx.x & 127;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's tensor-memory lanes
     const int row0 = blockIdx.x * kURows;
@@ -339,7 +343,7 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
     // done, its V once the transposed V and P are written, Q once O is done)
     auto load_k = [&](int t) {
         mbar_arrive_expect_tx(&bars[0], 4 * kUKBox);
-        for (int x = 0; x < 4; ++x) umma_tma(k_big + x * kUKBox, &maps.k, 32 * x, t * kUKeys, &bars[0]);
+        for (int x = 0; x < 4; ++x) umma_tma(k_base + x * 2 * kUKBox, &maps.k, 32 * x, t * kUKeys, &bars[0]);
     };
     auto load_v = [&](int t) {
         mbar_arrive_expect_tx(&bars[1], 4 * kUKBox);
@@ -358,7 +362,7 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
             load_v(t_begin);
         }
     }
-    if (warp == 0) {  // 256 tensor-memory columns: S at 0-63, O at 64-191
+    if (warp == 0) {  // 256 tensor-memory columns: S in two halves at 0-127, O at 128-255
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -366,7 +370,7 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot, t_s = tmem, t_o = tmem + 64;
+    const uint32_t tmem = *tmem_slot, t_s = tmem, t_o = tmem + 128;
 
     auto split16 = [](uint32_t raw, uint32_t dst_small) {
         float4 v;
@@ -396,22 +400,27 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
 #pragma unroll 4
         for (int i = threadIdx.x; i < 4 * kUQBox / 16; i += 256) split16(q_big + 16 * i, q_small + 16 * i);
 #pragma unroll 4
-        for (int i = threadIdx.x; i < 4 * kUKBox / 16; i += 256) split16(k_big + 16 * i, k_small + 16 * i);
+        for (int i = threadIdx.x; i < 4 * kUKBox / 16; i += 256) {  // box i / 512, 16-byte chunk i % 512
+            const uint32_t src = k_base + (i >> 9) * 2 * kUKBox + (i & 511) * 16;
+            split16(src, src + kUKBox);
+        }
         fence_proxy_async_smem();  // the split's generic stores before the tensor core's reads
         tc_fence_before();
         __syncthreads();
 
         if (threadIdx.x == 0) {
             tc_fence_after();
-            // S = Q K^T: k-step k reads 8 dims = 32 bytes of box k / 4
-            constexpr uint32_t idesc = umma_idesc(kUKeys, false);
+            // S = Q K^T: k-step k reads 8 dims = 32 bytes of box k / 4.  Q big
+            // against K big over K small (N 128: Qb.Kb into columns 0-63,
+            // Qb.Ks into 64-127), then Q small against K big into 0-63; S is
+            // the sum of the two column halves.
+            constexpr uint32_t idesc128 = umma_idesc(2 * kUKeys, false), idesc64 = umma_idesc(kUKeys, false);
             for (int k = 0; k < 16; ++k) {
-                const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, bo = (k >> 2) * kUKBox + (k & 3) * 32;
+                const uint32_t ao = (k >> 2) * kUQBox + (k & 3) * 32, bo = (k >> 2) * 2 * kUKBox + (k & 3) * 32;
                 const uint64_t ab = umma_desc(q_big + ao, 16, 1024), as = umma_desc(q_small + ao, 16, 1024);
-                const uint64_t bb = umma_desc(k_big + bo, 16, 1024), bs = umma_desc(k_small + bo, 16, 1024);
-                umma_tf32(t_s, ab, bb, idesc, k > 0);
-                umma_tf32(t_s, ab, bs, idesc, 1);
-                umma_tf32(t_s, as, bb, idesc, 1);
+                const uint64_t bk = umma_desc(k_base + bo, 16, 1024);
+                umma_tf32(t_s, ab, bk, idesc128, k > 0);
+                umma_tf32(t_s, as, bk, idesc64, 1);
             }
             umma_commit(&bars[2]);
         }
@@ -448,10 +457,13 @@ attention_umma_kernel(float2 *__restrict__ part_ml, int rows_pad, int seq_k, int
                              : "memory");
             }
         }
-        // this warpgroup's 32 keys of the thread's row of S
-        uint32_t r[32];
+        // this warpgroup's 32 keys of the thread's row of S (sum of the halves)
+        uint32_t r[32], r2[32];
         tm_ld32(t_s + 32 * wg + lane_base, r);
+        tm_ld32(t_s + 64 + 32 * wg + lane_base, r2);
         tm_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(r2[j]));
         const int nk = min(kUKeys, seq_k - key0) - 32 * wg;
         float m = -CUDART_INF_F;
 #pragma unroll
