@@ -57,6 +57,26 @@ def test_append_bitexact(kvx, oracle, np_dtype):
 
 
 @pytest.mark.parametrize("np_dtype", [np.float32, np.float16])
+@pytest.mark.parametrize("page_tokens,dim", [(8, 64), (32, 256)])
+def test_append_other_page_geometry_bitexact(kvx, oracle, np_dtype, page_tokens, dim):
+    """Page sizes and head dims other than 16 x 128 (the element-wise
+    kernel) against the oracle's KVManager::save_page per token."""
+    lens = np.array([0, 5, 7, 8, 9, 63, 64, 100], np.int64)
+    bt, num_pages = kvgen.paged_layout(lens, page_tokens, 1, seed=81)
+    hkv = 4
+    pool = kvgen.normal(82, (num_pages, 2, hkv, page_tokens, dim)).astype(np_dtype)
+    nk = kvgen.normal(83, (lens.size, hkv, dim)).astype(np_dtype)
+    nv = kvgen.normal(84, (lens.size, hkv, dim)).astype(np_dtype)
+    pos = lens.astype(np.int32)
+    g_pool = dev(pool)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kvx.append(g_pool, dev(bt), dev(pos), dev(nk), dev(nv), error_flag=err)
+    oracle.append(pool, bt, pos, nk, nv, page_tokens)
+    assert np.array_equal(g_pool.cpu().numpy().view(np.uint8), pool.view(np.uint8))
+    assert err.item() == 0
+
+
+@pytest.mark.parametrize("np_dtype", [np.float32, np.float16])
 @pytest.mark.parametrize("n_new", [1, 5, 16, 17, 100, 256])
 def test_append_chunk_bitexact(kvx, oracle, np_dtype, n_new):
     """A chunk of n_new tokens per sequence from ragged start positions
