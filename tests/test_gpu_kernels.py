@@ -592,6 +592,27 @@ def test_attention_dense_and_softmax_match_reference_rows(kvx, oracle):
     assert np.abs(sm - e / e.sum(axis=1, keepdims=True)).max() < 1e-6
 
 
+@pytest.mark.parametrize("dim,offset", [(128, 1), (64, 0), (96, 0), (256, 0), (1000, 0)])
+def test_attention_dense_cuda_core_paths_match_fp64(kvx, dim, offset):
+    """The CUDA-core kernels of the dense attention: head dim 128 whose Q /
+    out rows are not 16-byte aligned (attention_dense128_kernel) and other
+    head dims up to 1024 (attention_dense_kernel), against float64."""
+    seq_q, seq_k = 37, 300
+    g = torch.Generator(device="cuda")
+    g.manual_seed(dim * 13 + offset)
+    qbuf = torch.randn(seq_q * dim + offset, generator=g, device="cuda")
+    q = qbuf[offset:].view(seq_q, dim)  # offset 1: rows start 4 bytes past a 16-byte boundary
+    k = torch.randn((seq_k, dim), generator=g, device="cuda")
+    v = torch.randn((seq_k, dim), generator=g, device="cuda")
+    obuf = torch.zeros(seq_q * dim + offset, device="cuda")
+    out = obuf[offset:].view(seq_q, dim)
+    kvx.attention_dense(q, k, v, out=out)
+    s = (q.double() @ k.double().T) / np.sqrt(float(dim))
+    ref = torch.softmax(s, dim=1) @ v.double()
+    assert_close(out.cpu().numpy(), ref.cpu().numpy())
+    assert obuf[:offset].abs().sum().item() == 0
+
+
 @pytest.mark.parametrize("seq_q,seq_k,mag", [(1024, 1024, 1.0), (1000, 777, 1.0), (1, 1, 1.0), (17, 65, 1.0),
                                              (300, 2049, 1.0), (64, 500, 1e5), (128, 300, 1e-3),
                                              (4096, 4096, 1.0), (20000, 300, 1.0), (128, 40001, 1.0)])
